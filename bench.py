@@ -1,0 +1,340 @@
+#!/usr/bin/env python3
+"""Decode benchmark: 7B-shape fp16 batch-1 decode tok/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decode token of the 7B Llama shape (32 layers, d 4096, 32 heads x 128, FFN
+11008, vocab 32000, fp16 weights, fp16 KV) at batch 1, after a 128-token prompt. With N > 1
+(launched under torchrun) the model is split tensor-parallel over N GPUs (strong scaling:
+the same model and batch, time per token shrinks). Weights are random-init from the seeded
+generator, filled directly in HBM (identical to the GGUF the fixture writer would produce);
+they total 13.5 GB, far above the 126 MB L2, so every step streams them from HBM.
+
+Printed (rank 0, one JSON line): whole-job tok/s from CUDA events on the engine's stream
+(max over ranks), the end-to-end tok/s through the host API (pinned host id in, host id
+out, every step), the HBM roofline of the dominant kernel (the fused RMSNorm + gate/up +
+SwiGLU projection, timed live with CUDA events on its own launches), the CPU oracle timed
+on this host's cores, and the SM clocks sampled during the timed region.
+`--impl reference` times the CPU restatement of the reference's decode path (oracle/) on
+the same workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vulkan-symbiote-loader_b200"))
+
+CONFIG_7B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
+                 rope_theta=10000.0, rms_eps=1e-5, wdtype=1)
+PROMPT = 128
+SEED = 1
+SIGMA = 0.02
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Polls SM clock, power and clock-event reasons through NVML while running."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
+               "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index: int, period: float = 0.02):
+        self.idx, self.period = device_index, period
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for k, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(k)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return ws, rank, local
+
+
+def init_dist(ws):
+    if ws == 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return dist
+
+
+def max_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline(cfg, seconds: float, threads: int | None = None):
+    """Oracle decode steps of the same model on the host cores (bounded sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle as O
+    from vsl import synth
+    L = O.lib()
+    if threads:
+        L.orc_set_num_threads(threads)
+    t0 = time.perf_counter()
+    m = O.Model.synthetic(n_layers=cfg["n_layers"], d=cfg["d_model"], n_heads=cfg["n_heads"], n_kv=cfg["n_kv_heads"],
+                          ffn=cfg["ffn"], vocab=cfg["vocab"], rope_theta=cfg["rope_theta"], eps=cfg["rms_eps"],
+                          wdtype=cfg["wdtype"], kvdtype=O.F16, max_seq=PROMPT + 256, max_batch=1, seed=SEED,
+                          sigma=SIGMA)
+    m.fill_kv_synthetic(SEED + 100, 1.0, PROMPT, 1)  # stands in for the prompt's keys/values
+    setup = time.perf_counter() - t0
+    ids = synth.synth_ids(SEED, 0, 256, cfg["vocab"])
+    n, t_total = 0, 0.0
+    m.step(ids[:1], np.array([PROMPT], np.int32), want_logits=False)  # warm-up (page-in)
+    while t_total < seconds and n < 255:
+        t1 = time.perf_counter()
+        m.step(ids[n + 1:n + 2], np.array([PROMPT + 1 + n], np.int32), want_logits=False)
+        t_total += time.perf_counter() - t1
+        n += 1
+    cores = int(L.orc_num_threads())
+    m.close()
+    return {"value": n / t_total, "unit": "tok/s", "cores": cores, "kind": "port",
+            "sample": f"{n} decode tokens of the full {cfg['n_layers']}-layer model at positions "
+                      f"{PROMPT + 1}..{PROMPT + n}, fp16 weights upcast exactly, fp32 math, {cores} OpenMP threads "
+                      f"(setup {setup:.1f}s excluded)"}
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    cfg = dict(CONFIG_7B)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    threads = os.cpu_count()
+    # a bounded sample: each step is one decode token; total CPU time kept to about 2 minutes
+    sec = min(120.0, max(10.0, 0.5 * (args.steps + args.warmup)))
+    cb = cpu_baseline(cfg, sec, threads)
+    line = {"metric": "decode tok/s (7B fp16, bs1)", "value": round(cb["value"], 4), "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random-init weights)",
+            "config": {"workload": "7B Llama shape fp16, batch 1, 128-token prompt then decode",
+                       "model": "llama-7b-shape", "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": round(cb["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
+    """Time the fused RMSNorm + gate/up + SwiGLU projection (the largest per-step byte share)
+    on 7B-shape weights, rotating 8 copies (1.4 GB, far above L2) with CUDA events."""
+    d, F = cfg["d_model"], cfg["ffn"] // tp
+    N, K = 2 * F, d
+    copies = 8
+    W = torch.empty((copies, N, K), dtype=torch.float16, device="cuda")
+    for c in range(copies):
+        vsl.synth_fill(W[c], vsl.F16, 99, 1000 + c, 0, N * K, 0.02)
+    x = torch.randn((1, K), device="cuda")
+    nw = torch.ones(K, device="cuda")
+    y = torch.empty((1, F), device="cuda")
+    s = torch.cuda.Stream()
+    st = s.cuda_stream
+    with torch.cuda.stream(s):
+        for i in range(3 * copies):
+            vsl.gemv(vsl.F16, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
+        reps = 20 * copies
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(reps):
+            vsl.gemv(vsl.F16, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    bytes_per_launch = N * K * 2 + K * 4 * 2 + F * 4  # weights + x + norm weights + output
+    achieved = bytes_per_launch / (ms * 1e-3) / 1e9
+    del W
+    torch.cuda.empty_cache()
+    return {"bound": "hbm", "kernel": "gemv_kernel<__half,1,EK_SWIGLU,NORM> (gate/up + SwiGLU, fused RMSNorm)",
+            "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+            "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms * 1e3, 3),
+            "traffic": None}
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import vsl
+    from vsl import synth
+    ws, rank, local = dist_env()
+    dist = init_dist(ws)
+    torch.cuda.set_device(local)
+    cfg = dict(CONFIG_7B)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    max_seq = PROMPT + args.warmup + 2 * args.steps + 8
+    max_seq = (max_seq + 63) // 64 * 64
+    nccl_id = None
+    if ws > 1:
+        buf = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            buf = torch.tensor(list(vsl.nccl_unique_id()), dtype=torch.uint8)
+        dist.broadcast(buf, 0)
+        nccl_id = bytes(buf.tolist())
+    t0 = time.perf_counter()
+    eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=1, max_seq=max_seq,
+                               tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
+    load_s = time.perf_counter() - t0
+    prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
+    eng.set_forced(prompt)
+    eng.run(PROMPT)  # prompt positions 0..127 (token-by-token prefill through the decode graph)
+    eng.run(args.warmup)
+    stream = eng.stream
+    s = torch.cuda.ExternalStream(stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernels, bytes_start = eng.step_stats(1)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e0.record(s)
+        eng.run(args.steps)
+        e1.record(s)
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ms = max_over_ranks(dist, ms)
+    _, bytes_end = eng.step_stats(1)
+    status = eng.device_status()
+    # end to end through the host API: pinned host id in, sampled id back, every step
+    toks = eng.read_tokens(PROMPT + args.warmup + args.steps)[-1:, 0]
+    nxt = np.array([int(toks[-1])], np.int32)
+    for _ in range(2):
+        nxt, _ = eng.step_host(nxt)
+    if dist:
+        dist.barrier()
+    n_e2e = args.steps
+    t1 = time.perf_counter()
+    for _ in range(n_e2e):
+        nxt, _ = eng.step_host(nxt)
+    e2e_s = time.perf_counter() - t1
+    e2e_s = max_over_ranks(dist, e2e_s)
+    if status != 0 or eng.device_status() != 0:
+        raise SystemExit(f"device status {status}")
+    hbm_peak, peak_kind = peaks()
+    roof = dominant_kernel_roofline(torch, vsl, cfg, ws, hbm_peak, peak_kind)
+    eng.close()
+    tok_s = args.steps / (ms / 1e3)
+    step_bytes = 0.5 * (bytes_start + bytes_end)  # per GPU; KV grows by one position per step
+    step_gbs = step_bytes / (ms / 1e3 / args.steps) / 1e9
+    cb = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline(cfg, args.cpu_seconds)
+    if rank == 0:
+        line = {
+            "metric": "decode tok/s (7B fp16, bs1)", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random-init weights filled in HBM)",
+            "config": {"workload": "7B Llama shape fp16 (BASELINE configs[1]), batch 1, 128-token prompt, "
+                                   f"decode positions {PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
+                       "model": "llama-7b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
+                       "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps,
+                       "parallelism": f"tp{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (13.5 GB of weights streamed per step)"},
+            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "api": "vsl_engine_step_host"},
+            "roofline": roof,
+            "step_roofline": {"bytes_per_step_per_gpu": round(step_bytes), "achieved": round(step_gbs, 1),
+                              "peak": hbm_peak, "unit": "GB/s", "frac": round(step_gbs / hbm_peak, 4),
+                              "tok_s_at_peak": round(hbm_peak * 1e9 / step_bytes, 1)},
+            "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
+            "clocks": clk.summary(), "load_seconds": round(load_s, 2),
+        }
+        if cb:
+            line["cpu_baseline"] = cb
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

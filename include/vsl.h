@@ -1,0 +1,248 @@
+/*
+ * vsl.h -- C ABI of the B200-native Vulkan-Symbiote decode engine (libvsl.so).
+ *
+ * The reference exposes its decode path only as C++ classes; its "kernel runtime"
+ * (vk_symbiote/src/ShaderRuntime.cpp) binds GLSL pipelines and dispatches them with
+ * ShaderRuntime::dispatch_compute (ShaderRuntime.cpp:1484-1542). This header replaces that
+ * role with plain C entry points: device pointers are caller-owned, every call takes an
+ * explicit cudaStream_t (passed as void*), never synchronises, and returns a status code
+ * (VSL_OK or a negative VSL_ERR_*); vsl_last_error_string() describes the last failure
+ * on the calling thread. No C++ exception crosses this boundary.
+ *
+ * Layout conventions
+ *   - Weights are GGUF row-major [N][K] (GGUF ne = [K, N]); a projection computes
+ *     y[b][n] = sum_k W[n][k] * x[b][k] with fp32 accumulation. Rows are 16-byte aligned
+ *     (K * sizeof(elem) % 16 == 0).
+ *   - Activations and the residual stream are fp32 [B][dim].
+ *   - Paged KV cache: k_cache / v_cache are [n_pages][n_kv][page_size][head_dim] in the
+ *     KV dtype; page_table is int32 [B][max_pages] mapping a sequence's logical page to a
+ *     physical page. Position p of sequence b lives in page page_table[b][p / page_size],
+ *     slot p % page_size.
+ *   - pos[b] is the absolute position of the token being decoded; the attention length
+ *     is pos[b] + 1.
+ *   - RoPE tables rope_cos / rope_sin are fp32 [max_pos][head_dim/2]: cos/sin of
+ *     pos * theta^(-2i/head_dim), adjacent-pair rotation (vk_symbiote/src/Utils.cpp:101-110).
+ */
+#ifndef VSL_H
+#define VSL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VSL_API __attribute__((visibility("default")))
+#else
+#define VSL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (the reference returns negative ints through Expected<T>,
+ *      vk_symbiote/include/vk_symbiote/Common.h:88-193) ---- */
+#define VSL_OK 0
+#define VSL_ERR_INVALID (-1)
+#define VSL_ERR_CUDA (-2)
+#define VSL_ERR_NCCL (-3)
+#define VSL_ERR_TIMEOUT (-4)
+#define VSL_ERR_BOUNDS (-5)
+#define VSL_ERR_IO (-6)
+#define VSL_ERR_FORMAT (-7)
+#define VSL_ERR_OOM (-8)
+#define VSL_ERR_UNSUPPORTED (-9)
+#define VSL_ERR_STATE (-10)
+
+/* ---- element types: ggml / GGUF tensor type ids ---- */
+#define VSL_F32 0
+#define VSL_F16 1
+#define VSL_BF16 30
+
+/* ---- projection epilogues ---- */
+#define VSL_EPI_STORE 0  /* y[b][n]  = acc                                             */
+#define VSL_EPI_ADD 1    /* y[b][n] += acc  (residual add)                             */
+#define VSL_EPI_SWIGLU 2 /* rows interleaved (gate_i, up_i): y[b][i] = silu(g) * up    */
+
+VSL_API const char* vsl_last_error_string(void);
+VSL_API int vsl_version(void);
+
+/* ======================================================================================
+ * Kernels
+ * ====================================================================================== */
+
+/* Embedding gather with id clamp to V-1 (replaces embed_tokens_with_weights,
+ * vk_symbiote/src/VulkanSymbioteEngine.cpp:2886-3026, and embedding_lookup.comp:21-41).
+ * table [V][d] in dtype; ids int32 [B]; x fp32 [B][d]. */
+VSL_API int vsl_embed_gather(int dtype, const void* table, int V, int d, const int32_t* ids, int B, float* x,
+                     void* stream);
+
+/* RMSNorm y = x / sqrt(mean(x^2) + eps) * w (replaces rms_norm_with_weights,
+ * VulkanSymbioteEngine.cpp:2809-2884, and rms_norm.comp:17-35). x, y fp32 [B][d]; w fp32 [d]. */
+VSL_API int vsl_rmsnorm(const float* x, const float* w, int B, int d, float eps, float* y, void* stream);
+
+/* Decode projection y = x W^T for B <= 16 rows of activations (replaces the projection
+ * parts of attention_with_weights :2440-2584, feed_forward_with_weights :2726-2807 and
+ * final_projection_with_weights :3028-3130). If norm_w is non-NULL the activations are
+ * RMS-normalised with norm_w (fp32 [K], epsilon eps) first, fusing rms_norm_with_weights.
+ * epilogue: VSL_EPI_STORE / VSL_EPI_ADD (y is the fp32 residual) / VSL_EPI_SWIGLU (N even,
+ * y has N/2 columns; feed_forward.comp:21,49-61). */
+VSL_API int vsl_gemv(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
+             const float* norm_w, float eps, void* stream);
+
+/* Fused QKV projection + RoPE + KV-cache append (replaces attention.comp:63-108 and the CPU
+ * append KVCacheEntry::append_kv, VulkanSymbioteEngine.cpp:41-54). Wqkv rows are
+ * [Wq (n_heads*hd); Wk (n_kv*hd); Wv (n_kv*hd)] over K = d_model inputs. x is the fp32
+ * residual, normalised with norm_w. Writes q_out fp32 [B][n_heads*hd] (rotated) and the
+ * rotated K and plain V of position pos[b] into the paged caches. */
+VSL_API int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
+                        const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
+                        const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
+                        void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
+                        void* stream);
+
+/* Bytes of scratch vsl_flash_decode needs for B sequences of up to max_len positions. */
+VSL_API int vsl_flash_decode_workspace_size(int B, int n_heads, int n_kv, int head_dim, int max_len, int split_len,
+                                    size_t* bytes);
+
+/* Split-K flash-decode attention over the paged cache, GQA-aware (query head h reads KV
+ * group h*n_kv/n_heads, attention.comp:92; softmax of q.K/sqrt(hd), attention.comp:116-189).
+ * q fp32 [B][n_heads*hd]; out fp32 [B][n_heads*hd]. split_len (a multiple of page_size)
+ * is the number of positions one CTA covers; the grid covers max_len. workspace must hold
+ * vsl_flash_decode_workspace_size() bytes and be zero-filled before its first use (the
+ * kernel leaves its split counters at zero when it returns). */
+VSL_API int vsl_flash_decode(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                     const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                     int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* lm_head projection fused with the sampler (replaces final_projection_with_weights
+ * :3028-3130 and sample_token :1540-1553). Computes logits[b][n] for the local vocab slice
+ * (global index = vocab_offset + n) and folds each row into argmax_slots[b] (uint64,
+ * must be zero before the call) with a 64-bit max of (value key, ~index): the largest
+ * value wins and ties go to the lowest index, like greedy_sampling's strict '>' scan
+ * (:1794-1804). With temperature > 0 the folded value is logit/temperature + Gumbel noise
+ * drawn from (seed, *step_counter, b, index), which samples the softmax distribution. */
+VSL_API int vsl_lm_head_sample(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w,
+                       float eps, int B, float* logits, unsigned long long* argmax_slots, int vocab_offset,
+                       float temperature, uint64_t seed, const int32_t* step_counter, void* stream);
+
+/* Greedy argmax of fp32 logits [B][V] (first maximum). */
+VSL_API int vsl_argmax(const float* logits, int B, int V, int32_t* out_ids, void* stream);
+
+/* Fill n elements [start, start+n) of seeded synthetic tensor `tensor_id` on the device
+ * (Irwin-Hall(4) of splitmix64 lanes scaled to standard deviation sigma, rounded to dtype).
+ * Bit-identical to the host generator used to write GGUF fixtures. */
+VSL_API int vsl_synth_fill(void* dst, int dtype, uint64_t seed, uint64_t tensor_id, uint64_t start, uint64_t n,
+                   double sigma, void* stream);
+
+/* ======================================================================================
+ * Engine (replaces VulkanSymbioteEngine's decode loop, VulkanSymbioteEngine.cpp:678-765)
+ * ====================================================================================== */
+
+typedef struct vsl_engine vsl_engine;
+
+typedef struct {
+    int n_layers;
+    int d_model;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int ffn;
+    int vocab;
+    float rope_theta;
+    float rms_eps;
+    int wdtype; /* VSL_F32 / VSL_F16 / VSL_BF16 */
+} vsl_model_config;
+
+typedef struct {
+    int device;        /* CUDA device ordinal                                          */
+    int max_batch;     /* sequences decoded together (B)                               */
+    int max_seq;       /* KV positions per sequence                                    */
+    int kv_dtype;      /* VSL_F32 / VSL_F16; -1 = F32 for F32 models, else F16         */
+    int page_size;     /* KV page size in positions (0 = 64)                           */
+    int split_len;     /* flash-decode positions per CTA (0 = automatic)               */
+    int tp_rank;       /* tensor-parallel rank                                         */
+    int tp_size;       /* tensor-parallel world size (1 = no NCCL)                     */
+    const void* nccl_id; /* 128-byte ncclUniqueId from vsl_nccl_unique_id (tp_size > 1)  */
+    double vram_budget_gb; /* 0 = no cap; above the cap layers stream from pinned host */
+    int use_graph;     /* capture the decode step in a CUDA graph (default 1)          */
+    int use_pdl;       /* programmatic dependent launch between kernels (default 1)    */
+} vsl_engine_options;
+
+VSL_API void vsl_engine_default_options(vsl_engine_options* opt);
+
+/* ======================================================================================
+ * GGUF inspection (host only, no GPU needed)
+ * ====================================================================================== */
+
+/* Model configuration of a GGUF file as the engine would load it (GGUFLoader::load +
+ * get_model_config, vk_symbiote/src/GGUFLoader.cpp:625-663, 673-728). */
+VSL_API int vsl_gguf_model_config(const char* path, vsl_model_config* out);
+
+/* Tensor lookup: ggml type id, dimensions (ne[0] innermost; unused entries 0) and absolute
+ * file offset of the data (GGUFLoader::get_tensor, GGUFLoader.h:280). */
+VSL_API int vsl_gguf_tensor_info(const char* path, const char* name, int* ggml_type, uint64_t ne[4], uint64_t* file_offset);
+
+
+/* ncclUniqueId bytes for tensor-parallel engines (call on rank 0, broadcast to the rest). */
+VSL_API int vsl_nccl_unique_id(void* out128);
+
+/* Load a GGUF model (GGUFLoader::load + load_all_weights, VulkanSymbioteEngine.cpp:1114-1175,
+ * 2189-2213): pinned-host staging and cudaMemcpyAsync into one HBM arena, native dtype. */
+VSL_API int vsl_engine_create_gguf(const char* path, const vsl_engine_options* opt, vsl_engine** out);
+
+/* Create an engine whose weights are filled on the device by the seeded generator
+ * (identical tensors to a GGUF written by vsl/synth.py with the same seed). */
+VSL_API int vsl_engine_create_synthetic(const vsl_model_config* cfg, uint64_t seed, double sigma,
+                                const vsl_engine_options* opt, vsl_engine** out);
+
+VSL_API int vsl_engine_destroy(vsl_engine* e);
+VSL_API int vsl_engine_get_config(const vsl_engine* e, vsl_model_config* out);
+
+/* Clear all sequences (clear_kv_cache, VulkanSymbioteEngine.h:116). */
+VSL_API int vsl_engine_reset(vsl_engine* e);
+
+/* Fill KV positions [0, n_pos) of the first B sequences with seeded values and set their
+ * next position to n_pos (the 8B long-context workload's prefilled cache). */
+VSL_API int vsl_engine_fill_kv_synthetic(vsl_engine* e, uint64_t seed, double sigma, int n_pos, int B);
+
+/* Queue token ids to feed: ids [n_steps][B] (host). Step s consumes forced[s][b] when s is
+ * below the forced count, otherwise the id sampled at step s-1. */
+VSL_API int vsl_engine_set_forced(vsl_engine* e, const int32_t* ids, int n_steps, int B);
+
+/* Run n_steps decode steps for B active sequences entirely on the device (graph replays);
+ * sampled ids accumulate in the engine's token log. temperature <= 0 is greedy. */
+VSL_API int vsl_engine_run(vsl_engine* e, int n_steps, int B, float temperature, uint64_t seed);
+
+/* One host-driven step: copy ids (host, [B]) in, decode, copy sampled ids (host, [B]) out,
+ * and optionally the logits (host, [B][vocab], gathered across TP ranks on every rank). */
+VSL_API int vsl_engine_step_host(vsl_engine* e, const int32_t* ids, int B, int32_t* out_ids, float* out_logits);
+
+/* Copy the token log (ids sampled at steps [0, n)) to host memory [n][B]. */
+VSL_API int vsl_engine_read_tokens(vsl_engine* e, int n, int B, int32_t* out);
+
+/* Positions of the B sequences (host copy). */
+VSL_API int vsl_engine_positions(vsl_engine* e, int B, int32_t* out);
+
+/* Greedy / temperature generation from a host prompt: prompt (n_prompt ids) for sequence 0,
+ * up to max_new tokens into out_ids; stops early at any id in stop_ids (the reference stops
+ * on 0 or 2, VulkanSymbioteEngine.cpp:747-749). *n_out receives the count. */
+VSL_API int vsl_engine_generate(vsl_engine* e, const int32_t* prompt, int n_prompt, int max_new, float temperature,
+                        uint64_t seed, const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out);
+
+/* The stream the engine launches its work on (cudaStream_t as void*). */
+VSL_API void* vsl_engine_stream(vsl_engine* e);
+
+/* Kernels launched per decode step and bytes of weights + KV read per step at the
+ * current positions (algorithmic bytes for the roofline). */
+VSL_API int vsl_engine_step_stats(vsl_engine* e, int B, int* kernels_per_step, double* bytes_per_step);
+
+/* Sticky device status word of the engine (0 = OK; VSL_ERR_TIMEOUT / VSL_ERR_BOUNDS set by
+ * kernels that gave up on a bounded wait or rejected an index). */
+VSL_API int vsl_engine_device_status(vsl_engine* e, int* status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VSL_H */

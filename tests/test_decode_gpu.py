@@ -1,0 +1,162 @@
+"""End-to-end decode parity of the engine (C ABI) against the CPU oracle and the goldens.
+
+Bars: fp32 models -> identical greedy ids; fp16/bf16 models -> per-step
+logits max-abs <= 2e-2 and top-1 agreement on >= 99% of steps, teacher-forced (both sides
+consume the same ids).
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+import vsl
+from vsl import synth
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL_F16 = 2e-2
+
+
+def test_tiny_fp32_greedy_ids_match_golden(golden, fixture_gguf):
+    g = golden("tiny_fp32")
+    with vsl.Engine.from_gguf(fixture_gguf("tiny_fp32"), max_seq=128) as e:
+        assert e.config["wdtype"] == vsl.F32 and e.config["n_layers"] == 4
+        ids = e.generate(g["prompt"], g["n_new"])
+        assert ids == g["ids"]
+        assert e.device_status() == 0
+
+
+def test_tiny_fp32_teacher_forced_logits(golden, fixture_gguf):
+    g = golden("tiny_fp32")
+    path = fixture_gguf("tiny_fp32")
+    seq = g["prompt"] + g["ids"][:-1]
+    orc = O.Model.from_gguf(path, kvdtype=O.F32, max_seq=128)
+    with vsl.Engine.from_gguf(path, max_seq=128) as e:
+        worst = 0.0
+        for p, tok in enumerate(seq):
+            ids, lg = e.step_host([tok], want_logits=True)
+            oid, olg = orc.step([tok], [p])
+            worst = max(worst, float(np.abs(lg - olg).max()))
+            assert ids[0] == oid[0]
+        assert worst < 1e-4
+
+
+def test_gqa_fp16_golden(golden, fixture_gguf):
+    g = golden("gqa_fp16")
+    with vsl.Engine.from_gguf(fixture_gguf("gqa_fp16"), max_seq=64) as e:
+        assert e.generate(g["prompt"], g["n_new"]) == g["ids"]
+        # same through the teacher-forced host path, with logits against the golden top-5
+        e.reset()
+        seq = g["prompt"] + g["ids"][:-1]
+        worst = 0.0
+        for p, tok in enumerate(seq):
+            _, lg = e.step_host([tok], want_logits=True)
+            k = p - (len(g["prompt"]) - 1)
+            if k >= 0:
+                for j, v in g["top5"][k]:
+                    worst = max(worst, abs(float(lg[0, j]) - v))
+        assert worst < 1e-3
+
+
+def _teacher_forced(cfg, seed, n_steps, batch=1, prefill=0, kv_seed=7, max_seq=None, **opts):
+    """Run engine and oracle on the same seeded model and ids; return per-step logits."""
+    max_seq = max_seq or (prefill + n_steps + 64)
+    e = vsl.Engine.synthetic(cfg, seed=seed, max_batch=batch, max_seq=max_seq, **opts)
+    orc = O.Model.synthetic(n_layers=cfg["n_layers"], d=cfg["d_model"], n_heads=cfg["n_heads"],
+                            n_kv=cfg["n_kv_heads"], ffn=cfg["ffn"], vocab=cfg["vocab"], rope_theta=cfg["rope_theta"],
+                            eps=cfg["rms_eps"], wdtype=cfg["wdtype"], kvdtype=O.F16 if cfg["wdtype"] != O.F32 else O.F32,
+                            max_seq=max_seq, max_batch=batch, seed=seed)
+    if prefill:
+        e.fill_kv_synthetic(kv_seed, 1.0, prefill, batch)
+        orc.fill_kv_synthetic(kv_seed, 1.0, prefill, batch)
+    ids = synth.synth_ids(seed, 1, n_steps * batch, cfg["vocab"]).reshape(n_steps, batch)
+    out = []
+    for s in range(n_steps):
+        gid, glg = e.step_host(ids[s], want_logits=True)
+        oid, olg = orc.step(ids[s], np.full(batch, prefill + s, np.int32))
+        out.append((gid, glg, oid, olg))
+    assert e.device_status() == 0
+    e.close()
+    return out
+
+
+def _check_half(res):
+    worst = max(float(np.abs(glg - olg).max()) for _, glg, _, olg in res)
+    agree = np.mean([np.mean(gid == oid) for gid, _, oid, _ in res])
+    assert worst <= LOGIT_TOL_F16, worst
+    assert agree >= 0.99, agree
+    return worst
+
+
+def test_7b_shape_fp16_reduced_depth():
+    cfg = dict(n_layers=2, d_model=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    _check_half(_teacher_forced(cfg, seed=21, n_steps=12))
+
+
+def test_8b_shape_bf16_gqa_batch_prefilled_kv():
+    cfg = dict(n_layers=2, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+               rope_theta=500000.0, rms_eps=1e-5, wdtype=vsl.BF16)
+    _check_half(_teacher_forced(cfg, seed=33, n_steps=4, batch=4, prefill=700))
+
+
+def test_graph_pdl_and_eager_agree_bitwise():
+    cfg = dict(n_layers=3, d_model=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1376, vocab=4000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    outs = []
+    for opts in (dict(use_graph=1, use_pdl=1), dict(use_graph=0, use_pdl=0), dict(use_graph=1, use_pdl=0)):
+        with vsl.Engine.synthetic(cfg, seed=4, max_seq=256, **opts) as e:
+            prompt = synth.synth_ids(4, 0, 20, cfg["vocab"])
+            ids = e.generate(prompt, 40)
+            _, lg = e.step_host([ids[-1]], want_logits=True)
+            outs.append((ids, lg))
+    assert outs[0][0] == outs[1][0] == outs[2][0]
+    assert np.array_equal(outs[0][1], outs[1][1]) and np.array_equal(outs[0][1], outs[2][1])
+
+
+def test_device_loop_matches_host_loop():
+    cfg = dict(n_layers=2, d_model=256, n_heads=4, n_kv_heads=4, head_dim=64, ffn=688, vocab=3000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.BF16)
+    prompt = synth.synth_ids(8, 0, 10, cfg["vocab"])
+    with vsl.Engine.synthetic(cfg, seed=8, max_seq=128) as e:
+        dev_ids = e.generate(prompt, 30)
+        e.reset()
+        host = []
+        nxt = None
+        for t in prompt:
+            nxt, _ = e.step_host([t])
+        for _ in range(30):
+            host.append(int(nxt[0]))
+            nxt, _ = e.step_host([host[-1]])
+        assert dev_ids == host
+        assert list(e.positions(1)) == [10 + 30]
+
+
+def test_temperature_sampling_is_seeded():
+    cfg = dict(n_layers=1, d_model=256, n_heads=4, n_kv_heads=2, head_dim=64, ffn=512, vocab=2000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    prompt = [1, 2, 3, 4]
+    with vsl.Engine.synthetic(cfg, seed=2, max_seq=128) as e:
+        greedy = e.generate(prompt, 30)
+        a = e.generate(prompt, 30, temperature=1.0, seed=5)
+        b = e.generate(prompt, 30, temperature=1.0, seed=5)
+        c = e.generate(prompt, 30, temperature=1.0, seed=6)
+        assert a == b and a != c and a != greedy
+        assert all(0 <= t < cfg["vocab"] for t in a + c)
+
+
+def test_stop_ids_and_bounds():
+    cfg = dict(n_layers=1, d_model=256, n_heads=4, n_kv_heads=4, head_dim=64, ffn=512, vocab=1000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    with vsl.Engine.synthetic(cfg, seed=3, max_seq=64) as e:
+        full = e.generate([5, 6, 7], 40)
+        stop = full[10]
+        cut = e.generate([5, 6, 7], 40, stop_ids=[stop])
+        assert cut == full[:full.index(stop) + 1]
+        with pytest.raises(vsl.VslError) as err:
+            e.generate([5, 6, 7], 62)
+        assert err.value.code == -5
+        e.reset()
+        e.run(64)
+        with pytest.raises(vsl.VslError):
+            e.run(1)
+        assert e.device_status() == 0

@@ -1,0 +1,152 @@
+// DecodeEngine: the B200 decode token loop behind vsl_engine_* and VulkanSymbioteEngine.
+//
+// One engine per GPU (tensor-parallel rank). All weights live in one HBM arena, laid out
+// per layer as one contiguous block [Wqkv | Wo | Wgate/up interleaved | Wdown | norms], so
+// a layer can also be streamed as a single copy when the model exceeds the HBM budget.
+// A decode step is one CUDA graph (captured once per batch size / sampler mode): the ids,
+// positions, step counter and token log are device-resident, so consecutive steps run
+// with no host round trip.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../../include/vk_symbiote/GGUFLoader.h"
+#include "../../../include/vk_symbiote/NomadPack.h"
+#include "../../../include/vsl.h"
+
+namespace vsl {
+
+struct LayerPtrs {
+    void* wqkv = nullptr;   // [(nh_l + 2 nkv_l) hd][d]
+    void* wo = nullptr;     // [d][nh_l hd]
+    void* wgu = nullptr;    // [2 F_l][d], rows (gate_i, up_i) interleaved
+    void* wd = nullptr;     // [d][F_l]
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    void* k_cache = nullptr;  // [n_pages][nkv_l][page][hd]
+    void* v_cache = nullptr;
+};
+
+class DecodeEngine {
+public:
+    static int create(const vsl_model_config& cfg, const vsl_engine_options& opt, std::unique_ptr<DecodeEngine>& out);
+    ~DecodeEngine();
+
+    int load_gguf(vk_symbiote::GGUFLoader& loader);
+    int init_synthetic(uint64_t seed, double sigma);
+
+    int reset();
+    int fill_kv_synthetic(uint64_t seed, double sigma, int n_pos, int B);
+    int set_forced(const int32_t* ids, int n_steps, int B);
+    int run(int n_steps, int B, float temperature, uint64_t seed);
+    int step_host(const int32_t* ids, int B, int32_t* out_ids, float* out_logits);
+    int read_tokens(int n, int B, int32_t* out);
+    int positions(int B, int32_t* out);
+    int generate(const int32_t* prompt, int n_prompt, int max_new, float temperature, uint64_t seed,
+                 const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out);
+    int device_status(int* status);
+    int step_stats(int B, int* kernels, double* bytes);
+
+    const vsl_model_config& config() const { return cfg_; }
+    cudaStream_t stream() const { return stream_; }
+    int max_batch() const { return opt_.max_batch; }
+    int max_seq() const { return opt_.max_seq; }
+    size_t arena_bytes() const { return arena_bytes_; }
+    size_t kv_bytes() const { return kv_bytes_; }
+    vk_symbiote::PackResidency residency() const { return residency_; }
+
+private:
+    DecodeEngine() = default;
+    int init(const vsl_model_config& cfg, const vsl_engine_options& opt);
+    int alloc_buffers();
+    int enqueue_step(int B, float temperature, uint64_t seed);
+    int get_graph(int B, float temperature, uint64_t seed, cudaGraphExec_t* exec);
+    int allreduce_x(int B);
+    int check_cuda(cudaError_t e, const char* what);
+    int device_of_layer(int l) const;
+
+    // weight upload helpers: a "source" is full-tensor rows in host (pinned or mapped) or
+    // device memory; `copy_rows` / `copy_cols` place the rank's slice into the arena.
+    int upload_tensor(const void* src, bool src_host, int dtype_src, size_t rows, size_t cols, void* dst,
+                      size_t dst_ld, size_t row0, size_t nrows, size_t col0, size_t ncols);
+    int upload_norm(const vk_symbiote::GGUFLoader& loader, const std::string& name, float* dst);
+
+    vsl_model_config cfg_{};
+    vsl_engine_options opt_{};
+    int nh_l_ = 0, nkv_l_ = 0, ff_l_ = 0, v_l_ = 0, v_off_ = 0;
+    int kvdtype_ = VSL_F16;
+    int page_size_ = 64, max_pages_ = 0, n_pages_ = 0, split_len_ = 64;
+    size_t es_ = 2;
+
+    cudaStream_t stream_ = nullptr;
+    cudaStream_t copy_stream_ = nullptr;
+    void* arena_ = nullptr;
+    size_t arena_bytes_ = 0;
+    void* kv_ = nullptr;
+    size_t kv_bytes_ = 0;
+    void* act_ = nullptr;  // activations and bookkeeping
+    void* fd_ws_ = nullptr;
+    size_t fd_ws_bytes_ = 0;
+
+    void* tok_embd_ = nullptr;
+    void* lm_head_ = nullptr;
+    float* out_norm_ = nullptr;
+    std::vector<LayerPtrs> layers_;
+    size_t layer_bytes_ = 0;
+
+    float* rope_cos_ = nullptr;
+    float* rope_sin_ = nullptr;
+    int32_t* page_table_ = nullptr;
+
+    float* x_ = nullptr;
+    float* q_ = nullptr;
+    float* attn_ = nullptr;
+    float* act_ffn_ = nullptr;
+    float* logits_ = nullptr;
+    float* logits_full_ = nullptr;
+    unsigned long long* slots_ = nullptr;
+    int32_t* ids_ = nullptr;
+    int32_t* pos_ = nullptr;
+    int32_t* step_ = nullptr;
+    int32_t* n_forced_ = nullptr;
+    int32_t* forced_ = nullptr;
+    int32_t* log_ = nullptr;
+    int32_t* sampled_ = nullptr;
+    int* status_ = nullptr;
+    int log_cap_ = 0;
+
+    // pinned host staging for step_host
+    int32_t* h_ids_ = nullptr;
+    int32_t* h_out_ = nullptr;
+    float* h_logits_ = nullptr;
+
+    std::vector<int32_t> pos_host_;
+    int steps_host_ = 0;
+
+    // one captured step per (batch, temperature, seed): the sampler parameters are baked
+    // into the lm_head launch
+    struct GraphKey {
+        int B;
+        float temperature;
+        uint64_t seed;
+        bool operator<(const GraphKey& o) const {
+            if (B != o.B) return B < o.B;
+            if (temperature != o.temperature) return temperature < o.temperature;
+            return seed < o.seed;
+        }
+    };
+    std::map<GraphKey, cudaGraphExec_t> graphs_;
+
+    void* nccl_ = nullptr;  // ncclComm_t
+    vk_symbiote::PackResidency residency_{};
+};
+
+int make_model_config_from_gguf(const vk_symbiote::GGUFLoader& loader, vsl_model_config* out);
+
+}  // namespace vsl

@@ -1,0 +1,28 @@
+// Host-side declarations of the engine-internal kernel launchers (defined in csrc/kernels).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace vsl {
+
+int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, int B, float* x,
+               unsigned long long* slots, cudaStream_t st);
+int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
+                           const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
+                           const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
+                           void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
+                           int* status, cudaStream_t stream);
+int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                      const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                      int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
+                      size_t workspace_bytes, cudaStream_t stream);
+int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start, uint64_t n, double sigma,
+               cudaStream_t st);
+int finalize_impl(const unsigned long long* slots, int B, int32_t* ids, int32_t* pos, int32_t* step_counter,
+                  const int32_t* forced, const int32_t* n_forced, int32_t* log, int log_cap, int32_t* sampled_out,
+                  int max_pos, int* status, cudaStream_t st);
+int sm_count();
+bool pdl_enabled();
+void set_pdl_enabled(bool on);
+
+}  // namespace vsl

@@ -1,0 +1,318 @@
+// Split-K flash-decode attention over the paged KV cache (GQA-aware).
+//
+// Replaces the dense attention of the reference (vk_symbiote/shaders/attention.comp:84-189,
+// dispatched from attention_with_weights, VulkanSymbioteEngine.cpp:2440-2584), which makes
+// three passes over K per (head, position). Semantics kept: query head h reads KV group
+// h*n_kv/n_heads (attention.comp:92), scores are q.k / sqrt(head_dim), softmax with max
+// subtraction over positions [0, pos], output = probabilities times V.
+//
+// Design: one CTA per (split, kv group, sequence). A split covers split_len positions; a
+// CTA stages 64-position chunks of K and V (one page-contiguous block each) in padded
+// shared memory, computes the scores of all G = n_heads/n_kv query heads of its group from
+// the same staged K (so a KV page is read from HBM once per group, not once per head), and
+// keeps an online softmax (running max / sum, fp32). Splits write (max, sum, partial
+// output) to the workspace; the last CTA of a (sequence, group) to finish -- found with an
+// atomic counter that it resets to zero -- combines them, so one launch does both phases.
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace vsl {
+
+constexpr int FD_THREADS = 128;
+constexpr int FD_CHUNK = 64;  // positions staged per iteration
+constexpr int FD_GMAX = 8;    // query heads per KV group supported
+
+struct FdParams {
+    const float* q;
+    const void* k_cache;
+    const void* v_cache;
+    const int32_t* page_table;
+    int max_pages, page_size;
+    const int32_t* pos;
+    int B, n_heads, n_kv, split_len, n_splits;
+    float scale;
+    float* out;
+    float* ws_o;   // [B][n_heads][n_splits][HD]
+    float* ws_ml;  // [B][n_heads][n_splits][2]
+    int* counters; // [B][n_kv]
+};
+
+template <typename KT> struct KvVec;
+template <> struct KvVec<float> {
+    static constexpr int VEC = 4;
+    __device__ __forceinline__ static void widen(const uint4& v, float* f) { WTraits<float>::widen(v, f); }
+};
+template <> struct KvVec<__half> {
+    static constexpr int VEC = 8;
+    __device__ __forceinline__ static void widen(const uint4& v, float* f) { WTraits<__half>::widen(v, f); }
+};
+
+template <int HD, typename KT>
+__host__ __device__ constexpr int fd_row_elems() {
+    return HD + 16 / (int)sizeof(KT);  // one 16-byte pad per row: conflict-free 16-byte reads
+}
+
+template <int HD, typename KT>
+__host__ __device__ constexpr size_t fd_smem_bytes() {
+    return (size_t)2 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunks
+           + (size_t)FD_GMAX * HD * sizeof(float)                      // q
+           + (size_t)2 * FD_GMAX * FD_CHUNK * sizeof(float)             // score partials
+           + (size_t)FD_GMAX * FD_CHUNK * sizeof(float)                 // probabilities
+           + (size_t)4 * FD_GMAX * sizeof(float);                       // m, l, alpha, misc
+}
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int RE = fd_row_elems<HD, KT>();
+    constexpr int VEC = KvVec<KT>::VEC;
+    KT* k_s = reinterpret_cast<KT*>(smem_raw);
+    KT* v_s = k_s + FD_CHUNK * RE;
+    float* q_s = reinterpret_cast<float*>(v_s + FD_CHUNK * RE);
+    float* part_s = q_s + FD_GMAX * HD;           // [2][GMAX][CHUNK]
+    float* p_s = part_s + 2 * FD_GMAX * FD_CHUNK;  // [GMAX][CHUNK]
+    float* m_s = p_s + FD_GMAX * FD_CHUNK;         // [GMAX]
+    float* l_s = m_s + FD_GMAX;
+    float* a_s = l_s + FD_GMAX;
+    __shared__ int is_last;
+
+    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.n_heads / p.n_kv;
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const int len = p.pos[b] + 1;
+    const int t_begin = split * p.split_len;
+    if (t_begin >= len) return;  // empty split: not counted by the combiner
+    const int t_end = min(len, t_begin + p.split_len);
+    const int n_active = (len + p.split_len - 1) / p.split_len;
+
+    // q of the G heads of this group
+    const int h0 = g * G;
+    for (int i = tid; i < G * HD; i += FD_THREADS)
+        q_s[i] = p.q[((size_t)b * p.n_heads + h0) * HD + i];
+    if (tid < FD_GMAX) { m_s[tid] = -CUDART_INF_F; l_s[tid] = 0.0f; }
+
+    constexpr int EPT = (HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
+    float o_acc[FD_GMAX][EPT];
+#pragma unroll
+    for (int j = 0; j < FD_GMAX; j++)
+#pragma unroll
+        for (int i = 0; i < EPT; i++) o_acc[j][i] = 0.0f;
+
+    for (int t0 = t_begin; t0 < t_end; t0 += FD_CHUNK) {
+        const int n = min(FD_CHUNK, t_end - t0);
+        __syncthreads();  // previous chunk fully consumed (and q / m / l initialised)
+        // stage K and V rows [t0, t0+n): within one page because t0 % 64 == 0 and
+        // page_size % 64 == 0
+        const int page = p.page_table[(size_t)b * p.max_pages + t0 / p.page_size];
+        const size_t base = (((size_t)page * p.n_kv + g) * p.page_size + (t0 % p.page_size)) * HD;
+        const KT* kg = reinterpret_cast<const KT*>(p.k_cache) + base;
+        const KT* vg = reinterpret_cast<const KT*>(p.v_cache) + base;
+        constexpr int VPR = HD / VEC;  // vectors per row
+        for (int i = tid; i < n * VPR; i += FD_THREADS) {
+            const int r = i / VPR, c = (i % VPR) * VEC;
+            *reinterpret_cast<uint4*>(k_s + r * RE + c) =
+                __ldcg(reinterpret_cast<const uint4*>(kg + (size_t)r * HD + c));
+            *reinterpret_cast<uint4*>(v_s + r * RE + c) =
+                __ldcg(reinterpret_cast<const uint4*>(vg + (size_t)r * HD + c));
+        }
+        __syncthreads();
+        // partial scores: thread (tt, half) covers half of the head dimension of position tt
+        {
+            const int tt = tid & (FD_CHUNK - 1), half = tid / FD_CHUNK;
+            if (tt < n) {
+                float acc[FD_GMAX];
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+                const KT* kr = k_s + tt * RE;
+#pragma unroll
+                for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += VEC) {
+                    float kf[VEC];
+                    KvVec<KT>::widen(*reinterpret_cast<const uint4*>(kr + c), kf);
+#pragma unroll
+                    for (int j = 0; j < FD_GMAX; j++) {
+                        if (j < G) {
+#pragma unroll
+                            for (int e = 0; e < VEC; e++) acc[j] = fmaf(q_s[j * HD + c + e], kf[e], acc[j]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++)
+                    if (j < G) part_s[(half * FD_GMAX + j) * FD_CHUNK + tt] = acc[j];
+            }
+        }
+        __syncthreads();
+        // online softmax per head: warp w handles heads w, w+4
+        for (int j = warp; j < G; j += FD_THREADS / 32) {
+            float s0 = -CUDART_INF_F, s1 = -CUDART_INF_F;
+            if (lane < n) s0 = (part_s[j * FD_CHUNK + lane] + part_s[(FD_GMAX + j) * FD_CHUNK + lane]) * p.scale;
+            if (lane + 32 < n)
+                s1 = (part_s[j * FD_CHUNK + lane + 32] + part_s[(FD_GMAX + j) * FD_CHUNK + lane + 32]) * p.scale;
+            const float cmax = warp_max(fmaxf(s0, s1));
+            const float m_old = m_s[j];
+            const float m_new = fmaxf(m_old, cmax);
+            const float e0 = lane < n ? expf(s0 - m_new) : 0.0f;
+            const float e1 = lane + 32 < n ? expf(s1 - m_new) : 0.0f;
+            p_s[j * FD_CHUNK + lane] = e0;
+            p_s[j * FD_CHUNK + lane + 32] = e1;
+            const float csum = warp_sum(e0 + e1);
+            if (lane == 0) {
+                const float alpha = expf(m_old - m_new);  // 0 on the first chunk (m_old = -inf)
+                a_s[j] = alpha;
+                l_s[j] = l_s[j] * alpha + csum;
+                m_s[j] = m_new;
+            }
+        }
+        __syncthreads();
+        // P V: thread owns output elements e = tid + i*128
+#pragma unroll
+        for (int i = 0; i < EPT; i++) {
+            const int e = tid + i * FD_THREADS;
+            if (e < HD) {
+                float acc[FD_GMAX];
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+                for (int tt = 0; tt < n; tt++) {
+                    const float vv = (float)v_s[tt * RE + e];
+#pragma unroll
+                    for (int j = 0; j < FD_GMAX; j++)
+                        if (j < G) acc[j] = fmaf(p_s[j * FD_CHUNK + tt], vv, acc[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++)
+                    if (j < G) o_acc[j][i] = o_acc[j][i] * a_s[j] + acc[j];
+            }
+        }
+    }
+
+    // ---- write this split's partial result ----
+#pragma unroll
+    for (int j = 0; j < FD_GMAX; j++) {
+        if (j >= G) continue;
+        const size_t row = ((size_t)b * p.n_heads + h0 + j) * p.n_splits + split;
+#pragma unroll
+        for (int i = 0; i < EPT; i++) {
+            const int e = tid + i * FD_THREADS;
+            if (e < HD) p.ws_o[row * HD + e] = o_acc[j][i];
+        }
+        if (tid == 0) {
+            p.ws_ml[row * 2 + 0] = m_s[j];
+            p.ws_ml[row * 2 + 1] = l_s[j];
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const int prev = atomicAdd(p.counters + (size_t)b * p.n_kv + g, 1);
+        is_last = prev == n_active - 1;
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // ---- combine the active splits of every head in this group ----
+    for (int j = 0; j < G; j++) {
+        const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits;
+        float M = -CUDART_INF_F;
+        for (int s = 0; s < n_active; s++) M = fmaxf(M, __ldcg(p.ws_ml + (row0 + s) * 2));
+        float L = 0.0f;
+        for (int s = 0; s < n_active; s++)
+            L += __ldcg(p.ws_ml + (row0 + s) * 2 + 1) * expf(__ldcg(p.ws_ml + (row0 + s) * 2) - M);
+        for (int e = tid; e < HD; e += FD_THREADS) {
+            float acc = 0.0f;
+            for (int s = 0; s < n_active; s++)
+                acc += __ldcg(p.ws_o + (row0 + s) * HD + e) * expf(__ldcg(p.ws_ml + (row0 + s) * 2) - M);
+            p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = acc / L;
+        }
+    }
+    if (tid == 0) p.counters[(size_t)b * p.n_kv + g] = 0;
+}
+
+static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+static int fd_splits(int max_len, int split_len) { return (max_len + split_len - 1) / split_len; }
+
+static size_t fd_workspace(int B, int n_heads, int n_kv, int head_dim, int n_splits) {
+    return align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float)) +
+           align256((size_t)B * n_heads * n_splits * 2 * sizeof(float)) +
+           align256((size_t)B * n_kv * sizeof(int));
+}
+
+template <int HD, typename KT>
+static int launch_fd(const FdParams& p, cudaStream_t st) {
+    auto kern = flash_decode_kernel<HD, KT>;
+    constexpr size_t smem = fd_smem_bytes<HD, KT>();
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return launch_status(e, "flash_decode smem attribute");
+        configured_dev = dev;
+    }
+    dim3 grid(p.n_splits, p.n_kv, p.B);
+    return launch_status(launch_k(kern, grid, dim3(FD_THREADS), smem, st, p), "flash_decode launch");
+}
+
+int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                      const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                      int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
+                      size_t workspace_bytes, cudaStream_t stream) {
+    if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
+        return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
+    if (B <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > FD_GMAX)
+        return set_error(VSL_ERR_UNSUPPORTED, "flash_decode: heads %d / kv %d (group size <= %d)", n_heads, n_kv,
+                         FD_GMAX);
+    if (page_size <= 0 || page_size % FD_CHUNK || split_len <= 0 || split_len % FD_CHUNK)
+        return set_error(VSL_ERR_INVALID, "flash_decode: page_size (%d) and split_len (%d) must be multiples of %d",
+                         page_size, split_len, FD_CHUNK);
+    if (max_len <= 0 || max_len > max_pages * page_size)
+        return set_error(VSL_ERR_INVALID, "flash_decode: max_len %d outside the page table", max_len);
+    const int n_splits = fd_splits(max_len, split_len);
+    const size_t need = fd_workspace(B, n_heads, n_kv, head_dim, n_splits);
+    if (workspace_bytes < need)
+        return set_error(VSL_ERR_INVALID, "flash_decode: workspace %zu bytes < %zu", workspace_bytes, need);
+    FdParams p = {};
+    p.q = q; p.k_cache = k_cache; p.v_cache = v_cache; p.page_table = page_table; p.max_pages = max_pages;
+    p.page_size = page_size; p.pos = pos; p.B = B; p.n_heads = n_heads; p.n_kv = n_kv; p.split_len = split_len;
+    p.n_splits = n_splits; p.scale = 1.0f / sqrtf((float)head_dim); p.out = out;
+    char* w = reinterpret_cast<char*>(workspace);
+    p.ws_o = reinterpret_cast<float*>(w);
+    w += align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float));
+    p.ws_ml = reinterpret_cast<float*>(w);
+    w += align256((size_t)B * n_heads * n_splits * 2 * sizeof(float));
+    p.counters = reinterpret_cast<int*>(w);
+    if (kvdtype == VSL_F16) {
+        if (head_dim == 128) return launch_fd<128, __half>(p, stream);
+        if (head_dim == 64) return launch_fd<64, __half>(p, stream);
+    } else if (kvdtype == VSL_F32) {
+        if (head_dim == 128) return launch_fd<128, float>(p, stream);
+        if (head_dim == 64) return launch_fd<64, float>(p, stream);
+    }
+    return set_error(VSL_ERR_UNSUPPORTED, "flash_decode: head_dim %d / kv dtype %d", head_dim, kvdtype);
+}
+
+}  // namespace vsl
+
+extern "C" int vsl_flash_decode_workspace_size(int B, int n_heads, int n_kv, int head_dim, int max_len,
+                                               int split_len, size_t* bytes) {
+    if (!bytes || B <= 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_len <= 0 || split_len <= 0)
+        return vsl::set_error(VSL_ERR_INVALID, "flash_decode_workspace_size: bad arguments");
+    *bytes = vsl::fd_workspace(B, n_heads, n_kv, head_dim, vsl::fd_splits(max_len, split_len));
+    return VSL_OK;
+}
+
+extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                                int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
+                                  n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
+                                  (cudaStream_t)stream);
+}

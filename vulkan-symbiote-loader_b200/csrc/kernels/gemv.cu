@@ -1,0 +1,458 @@
+// Decode projections: y = x W^T for a handful of activation rows, HBM-bound weight streaming.
+//
+// Replaces the projection math of the reference's attention.comp:63-99 (QKV), :191-199 (O),
+// feed_forward.comp:36-61 (gate/up/down) and final_linear.comp:38-86 (lm_head), which the
+// engine dispatches from attention_with_weights / feed_forward_with_weights /
+// final_projection_with_weights (vk_symbiote/src/VulkanSymbioteEngine.cpp:2440-2584,
+// 2726-2807, 3028-3130).
+//
+// Design (B200): weights are read exactly once per decode step, so the kernel is a pure
+// HBM stream. Each CTA owns a contiguous, balanced range of row pairs; a warp streams two
+// rows at a time with 16-byte L1-bypassing loads, U vectors per row in flight per lane,
+// and reduces with warp shuffles. The (optionally RMS-normalised) activations are staged
+// once per CTA in shared memory as fp32. Launched with programmatic dependent launch: the
+// first weight vectors are requested before griddepcontrol.wait, so the weight stream of
+// projection n+1 overlaps the tail of kernel n. Epilogues fuse the residual add, SwiGLU,
+// RoPE + paged KV append, and the lm_head argmax / Gumbel sampler.
+#include <cstdio>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace vsl {
+
+enum EpiKind { EK_STORE = 0, EK_ADD = 1, EK_SWIGLU = 2, EK_QKV = 3, EK_LMHEAD = 4 };
+
+struct GemvParams {
+    const void* W;
+    int N, K;
+    const float* x;
+    int B;
+    float* y;
+    const float* norm_w;
+    float eps;
+    // QKV + RoPE + KV append
+    int n_heads, n_kv, head_dim;
+    const int32_t* pos;
+    const float* rope_cos;
+    const float* rope_sin;
+    float* q_out;
+    void* k_cache;
+    void* v_cache;
+    int kvdtype;
+    const int32_t* page_table;
+    int max_pages, page_size;
+    // lm_head sampler
+    unsigned long long* slots;
+    int vocab_offset;
+    float inv_temp;
+    unsigned long long seed;
+    const int32_t* step_counter;
+    int* status;
+};
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_U = 4;  // 16-byte vectors per row in flight per lane
+
+__device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }
+
+__device__ __forceinline__ unsigned long long smix64(unsigned long long z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Gumbel(0,1) noise for (seed, step, b, index): -log(-log(u)), u in (0,1).
+__device__ __forceinline__ float gumbel(unsigned long long seed, int step, int b, uint32_t idx) {
+    unsigned long long h = smix64(smix64(seed ^ ((unsigned long long)step * 0x9E3779B97F4A7C15ull)) +
+                                  (((unsigned long long)b << 32) | idx));
+    float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    return -logf(-logf(u));
+}
+
+template <typename WT, int NB, int EK, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvParams p) {
+    extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations
+    __shared__ float red[NB][GEMV_THREADS / 32];
+    constexpr int VEC = WTraits<WT>::VEC;
+    const int K = p.K, N = p.N;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NW = GEMV_THREADS / 32;
+    const int nvec = K / VEC;
+    const int n_units = (N + 1) >> 1;
+    // balanced contiguous range of row pairs for this CTA
+    const int u_begin = (int)(((long long)n_units * blockIdx.x) / gridDim.x);
+    const int u_end = (int)(((long long)n_units * (blockIdx.x + 1)) / gridDim.x);
+    const WT* W = reinterpret_cast<const WT*>(p.W);
+
+    // Request the first weight vectors of this warp's first unit before waiting on the
+    // predecessor kernel: weights are never produced by it.
+    int unit = u_begin + warp;
+    uint4 pre0[GEMV_U], pre1[GEMV_U];
+    bool have_pre = false;
+    if (unit < u_end && (GEMV_U - 1) * 32 + lane < nvec) {
+        const int r0 = 2 * unit, r1 = min(2 * unit + 1, N - 1);
+        const WT* w0 = W + (size_t)r0 * K;
+        const WT* w1 = W + (size_t)r1 * K;
+#pragma unroll
+        for (int u = 0; u < GEMV_U; u++) {
+            pre0[u] = ldg_stream(w0 + (size_t)(lane + 32 * u) * VEC);
+            pre1[u] = ldg_stream(w1 + (size_t)(lane + 32 * u) * VEC);
+        }
+        have_pre = true;
+    }
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    // ---- stage activations (RMS-normalised if requested) ----
+    const int B = p.B;
+    if (NORM) {
+        float ss[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) ss[b] = 0.0f;
+        for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float v = b < B ? p.x[(size_t)b * K + k] : 0.0f;
+                ss[b] += v * v;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float s = warp_sum(ss[b]);
+            if (lane == 0) red[b][warp] = s;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) s += red[b][w];
+            ss[b] = sqrtf(s / (float)K + p.eps);  // rms_norm.comp:32-34: x / sqrt(var) * w
+        }
+        for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
+            float w = p.norm_w[k];
+#pragma unroll
+            for (int b = 0; b < NB; b++)
+                xs[b * K + k] = b < B ? p.x[(size_t)b * K + k] / ss[b] * w : 0.0f;
+        }
+    } else {
+        for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
+#pragma unroll
+            for (int b = 0; b < NB; b++) xs[b * K + k] = b < B ? p.x[(size_t)b * K + k] : 0.0f;
+        }
+    }
+    __syncthreads();
+
+    unsigned long long best[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) best[b] = 0ull;
+    int step = 0;
+    if (EK == EK_LMHEAD && p.inv_temp > 0.0f) step = *p.step_counter;
+
+    for (; unit < u_end; unit += NW) {
+        const int r0 = 2 * unit;
+        const bool has1 = r0 + 1 < N;
+        const int r1 = has1 ? r0 + 1 : r0;
+        const WT* w0 = W + (size_t)r0 * K;
+        const WT* w1 = W + (size_t)r1 * K;
+        float acc0[NB], acc1[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
+        int v = lane;
+        for (; v + 32 * (GEMV_U - 1) < nvec; v += 32 * GEMV_U) {
+            uint4 a[GEMV_U], c[GEMV_U];
+            if (have_pre) {
+#pragma unroll
+                for (int u = 0; u < GEMV_U; u++) { a[u] = pre0[u]; c[u] = pre1[u]; }
+                have_pre = false;
+            } else {
+#pragma unroll
+                for (int u = 0; u < GEMV_U; u++) {
+                    a[u] = ldg_stream(w0 + (size_t)(v + 32 * u) * VEC);
+                    c[u] = ldg_stream(w1 + (size_t)(v + 32 * u) * VEC);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < GEMV_U; u++) {
+                float fa[VEC], fc[VEC];
+                WTraits<WT>::widen(a[u], fa);
+                WTraits<WT>::widen(c[u], fc);
+                const int k = (v + 32 * u) * VEC;
+#pragma unroll
+                for (int b = 0; b < NB; b++) {
+                    const float4* xv = reinterpret_cast<const float4*>(xs + b * K + k);
+#pragma unroll
+                    for (int i = 0; i < VEC / 4; i++) {
+                        float4 xx = xv[i];
+                        acc0[b] = fmaf(fa[4 * i + 0], xx.x, acc0[b]);
+                        acc0[b] = fmaf(fa[4 * i + 1], xx.y, acc0[b]);
+                        acc0[b] = fmaf(fa[4 * i + 2], xx.z, acc0[b]);
+                        acc0[b] = fmaf(fa[4 * i + 3], xx.w, acc0[b]);
+                        acc1[b] = fmaf(fc[4 * i + 0], xx.x, acc1[b]);
+                        acc1[b] = fmaf(fc[4 * i + 1], xx.y, acc1[b]);
+                        acc1[b] = fmaf(fc[4 * i + 2], xx.z, acc1[b]);
+                        acc1[b] = fmaf(fc[4 * i + 3], xx.w, acc1[b]);
+                    }
+                }
+            }
+        }
+        for (; v < nvec; v += 32) {
+            uint4 a = ldg_stream(w0 + (size_t)v * VEC);
+            uint4 c = ldg_stream(w1 + (size_t)v * VEC);
+            float fa[VEC], fc[VEC];
+            WTraits<WT>::widen(a, fa);
+            WTraits<WT>::widen(c, fc);
+            const int k = v * VEC;
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+#pragma unroll
+                for (int i = 0; i < VEC; i++) {
+                    acc0[b] = fmaf(fa[i], xs[b * K + k + i], acc0[b]);
+                    acc1[b] = fmaf(fc[i], xs[b * K + k + i], acc1[b]);
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            acc0[b] = warp_sum(acc0[b]);
+            acc1[b] = warp_sum(acc1[b]);
+        }
+        // epilogue: lane b handles activation row b
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            if (lane != b || b >= B) continue;
+            const float s0 = acc0[b], s1 = acc1[b];
+            if (EK == EK_STORE) {
+                p.y[(size_t)b * N + r0] = s0;
+                if (has1) p.y[(size_t)b * N + r0 + 1] = s1;
+            } else if (EK == EK_ADD) {
+                p.y[(size_t)b * N + r0] += s0;
+                if (has1) p.y[(size_t)b * N + r0 + 1] += s1;
+            } else if (EK == EK_SWIGLU) {
+                p.y[(size_t)b * (N >> 1) + unit] = silu_f(s0) * s1;
+            } else if (EK == EK_QKV) {
+                const int hd = p.head_dim;
+                const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
+                const int pos = p.pos[b];
+                if (pos < 0 || pos >= p.max_pages * p.page_size) {
+                    if (p.status) atomicCAS(p.status, 0, VSL_ERR_BOUNDS);
+                    continue;
+                }
+                const int e = r0 % hd;  // even
+                float o0 = s0, o1 = s1;
+                if (r0 < qd + kvd) {  // rotate q and k: adjacent pair (e, e+1)
+                    const int half = hd >> 1;
+                    const float cs = p.rope_cos[(size_t)pos * half + (e >> 1)];
+                    const float sn = p.rope_sin[(size_t)pos * half + (e >> 1)];
+                    o0 = __fsub_rn(__fmul_rn(s0, cs), __fmul_rn(s1, sn));
+                    o1 = __fadd_rn(__fmul_rn(s0, sn), __fmul_rn(s1, cs));
+                }
+                if (r0 < qd) {
+                    p.q_out[(size_t)b * qd + r0] = o0;
+                    p.q_out[(size_t)b * qd + r0 + 1] = o1;
+                } else {
+                    const bool is_v = r0 >= qd + kvd;
+                    const int rr = is_v ? r0 - qd - kvd : r0 - qd;
+                    const int g = rr / hd;
+                    const int page = p.page_table[(size_t)b * p.max_pages + pos / p.page_size];
+                    const size_t idx =
+                        (((size_t)page * p.n_kv + g) * p.page_size + (pos % p.page_size)) * hd + e;
+                    void* cache = is_v ? p.v_cache : p.k_cache;
+                    kv_put(cache, idx, o0, p.kvdtype);
+                    kv_put(cache, idx + 1, o1, p.kvdtype);
+                }
+            } else if (EK == EK_LMHEAD) {
+                p.y[(size_t)b * N + r0] = s0;
+                if (has1) p.y[(size_t)b * N + r0 + 1] = s1;
+                float c0 = s0, c1 = s1;
+                const uint32_t g0 = (uint32_t)(p.vocab_offset + r0);
+                if (p.inv_temp > 0.0f) {
+                    c0 = s0 * p.inv_temp + gumbel(p.seed, step, b, g0);
+                    c1 = s1 * p.inv_temp + gumbel(p.seed, step, b, g0 + 1);
+                }
+                if (c0 == c0) best[b] = max(best[b], pack_argmax(c0, g0));
+                if (has1 && c1 == c1) best[b] = max(best[b], pack_argmax(c1, g0 + 1));
+            }
+        }
+    }
+    if (EK == EK_LMHEAD) {
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+            if (lane == b && b < B && best[b] != 0ull) atomicMax(p.slots + b, best[b]);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host dispatch
+// ---------------------------------------------------------------------------------------
+
+template <typename WT, int NB, int EK, bool NORM>
+static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
+    auto kern = gemv_kernel<WT, NB, EK, NORM>;
+    const size_t smem = (size_t)NB * p.K * sizeof(float);
+    static thread_local int configured_dev = -1;
+    static thread_local int occ = 1;
+    static thread_local size_t occ_smem = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev || occ_smem != smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return launch_status(e, "gemv smem attribute");
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMV_THREADS, smem);
+        if (e != cudaSuccess) return launch_status(e, "gemv occupancy");
+        if (occ < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d does not fit in shared memory", p.K);
+        configured_dev = dev;
+        occ_smem = smem;
+    }
+    const int n_units = (p.N + 1) / 2;
+    const int nw = GEMV_THREADS / 32;
+    int grid = sm_count() * occ;
+    const int max_grid = (n_units + nw - 1) / nw;
+    if (grid > max_grid) grid = max_grid;
+    if (grid < 1) grid = 1;
+    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
+}
+
+template <typename WT, int EK, bool NORM>
+static int launch_gemv_nb(const GemvParams& p, cudaStream_t st) {
+    if (p.B <= 1) return launch_gemv_t<WT, 1, EK, NORM>(p, st);
+    if (p.B <= 2) return launch_gemv_t<WT, 2, EK, NORM>(p, st);
+    return launch_gemv_t<WT, 4, EK, NORM>(p, st);
+}
+
+template <int EK, bool NORM>
+static int launch_gemv_w(int wdtype, const GemvParams& p, cudaStream_t st) {
+    switch (wdtype) {
+        case VSL_F32: return launch_gemv_nb<float, EK, NORM>(p, st);
+        case VSL_F16: return launch_gemv_nb<__half, EK, NORM>(p, st);
+        case VSL_BF16: return launch_gemv_nb<__nv_bfloat16, EK, NORM>(p, st);
+        default: return set_error(VSL_ERR_UNSUPPORTED, "gemv: weight dtype %d", wdtype);
+    }
+}
+
+template <int EK>
+static int launch_gemv_norm(int wdtype, const GemvParams& p, cudaStream_t st) {
+    return p.norm_w ? launch_gemv_w<EK, true>(wdtype, p, st) : launch_gemv_w<EK, false>(wdtype, p, st);
+}
+
+static size_t elem_size(int dtype) { return dtype == VSL_F32 ? 4 : 2; }
+
+static int check_common(int wdtype, const void* W, int N, int K, const float* x, int B) {
+    if (wdtype != VSL_F32 && wdtype != VSL_F16 && wdtype != VSL_BF16)
+        return set_error(VSL_ERR_UNSUPPORTED, "weight dtype %d", wdtype);
+    if (!W || !x || N <= 0 || K <= 0 || B <= 0)
+        return set_error(VSL_ERR_INVALID, "gemv: null pointer or empty shape (N=%d K=%d B=%d)", N, K, B);
+    if (((uintptr_t)W & 15) || ((size_t)K * elem_size(wdtype)) % 16)
+        return set_error(VSL_ERR_INVALID, "gemv: weight rows must be 16-byte aligned (K=%d)", K);
+    if ((uintptr_t)x & 15) return set_error(VSL_ERR_INVALID, "gemv: activations must be 16-byte aligned");
+    return VSL_OK;
+}
+
+// Large batches are processed in chunks of 4 activation rows (each chunk re-streams W).
+static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y_cols) {
+    const int B = p.B;
+    // activation rows per launch: at most 4, and at most what fits in ~200 KB of shared memory
+    int cmax = (int)((200 * 1024) / ((size_t)p.K * sizeof(float)));
+    if (cmax > 4) cmax = 4;
+    if (cmax < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d exceeds the shared-memory staging limit", p.K);
+    for (int b0 = 0; b0 < B; b0 += cmax) {
+        GemvParams q = p;
+        q.B = B - b0 < cmax ? B - b0 : cmax;
+        q.x = p.x + (size_t)b0 * p.K;
+        if (p.y) q.y = p.y + (size_t)b0 * y_cols;
+        if (p.pos) q.pos = p.pos + b0;
+        if (p.q_out) q.q_out = p.q_out + (size_t)b0 * p.n_heads * p.head_dim;
+        if (p.page_table) q.page_table = p.page_table + (size_t)b0 * p.max_pages;
+        if (p.slots) q.slots = p.slots + b0;
+        int rc;
+        switch (kind) {
+            case EK_STORE: rc = launch_gemv_norm<EK_STORE>(wdtype, q, st); break;
+            case EK_ADD: rc = launch_gemv_norm<EK_ADD>(wdtype, q, st); break;
+            case EK_SWIGLU: rc = launch_gemv_norm<EK_SWIGLU>(wdtype, q, st); break;
+            case EK_QKV: rc = launch_gemv_norm<EK_QKV>(wdtype, q, st); break;
+            default: rc = launch_gemv_norm<EK_LMHEAD>(wdtype, q, st); break;
+        }
+        if (rc) return rc;
+    }
+    return VSL_OK;
+}
+
+}  // namespace vsl
+
+using namespace vsl;
+
+extern "C" int vsl_gemv(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
+                        const float* norm_w, float eps, void* stream) {
+    int rc = check_common(wdtype, W, N, K, x, B);
+    if (rc) return rc;
+    if (!y) return set_error(VSL_ERR_INVALID, "gemv: null output");
+    if (epilogue == VSL_EPI_SWIGLU && (N & 1))
+        return set_error(VSL_ERR_INVALID, "gemv: SwiGLU needs interleaved gate/up rows (N even), N=%d", N);
+    GemvParams p = {};
+    p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
+    int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
+    if (epilogue != VSL_EPI_STORE && epilogue != VSL_EPI_ADD && epilogue != VSL_EPI_SWIGLU)
+        return set_error(VSL_ERR_INVALID, "gemv: unknown epilogue %d", epilogue);
+    return run_chunks(wdtype, kind, p, (cudaStream_t)stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N);
+}
+
+extern "C" int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
+                                   const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
+                                   const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
+                                   void* v_cache, int kvdtype, const int32_t* page_table, int max_pages,
+                                   int page_size, void* stream) {
+    if (n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || (head_dim & 1) || n_heads % n_kv)
+        return set_error(VSL_ERR_INVALID, "qkv: bad head geometry (%d/%d x %d)", n_heads, n_kv, head_dim);
+    const int N = (n_heads + 2 * n_kv) * head_dim;
+    int rc = check_common(wdtype, Wqkv, N, K, x, B);
+    if (rc) return rc;
+    if (!pos || !rope_cos || !rope_sin || !q_out || !k_cache || !v_cache || !page_table || max_pages <= 0 ||
+        page_size <= 0)
+        return set_error(VSL_ERR_INVALID, "qkv: null pointer or empty cache geometry");
+    if (kvdtype != VSL_F32 && kvdtype != VSL_F16 && kvdtype != VSL_BF16)
+        return set_error(VSL_ERR_UNSUPPORTED, "qkv: kv dtype %d", kvdtype);
+    GemvParams p = {};
+    p.W = Wqkv; p.N = N; p.K = K; p.x = x; p.B = B; p.norm_w = norm_w; p.eps = eps;
+    p.n_heads = n_heads; p.n_kv = n_kv; p.head_dim = head_dim; p.pos = pos;
+    p.rope_cos = rope_cos; p.rope_sin = rope_sin; p.q_out = q_out; p.k_cache = k_cache; p.v_cache = v_cache;
+    p.kvdtype = kvdtype; p.page_table = page_table; p.max_pages = max_pages; p.page_size = page_size;
+    return run_chunks(wdtype, EK_QKV, p, (cudaStream_t)stream, 0);
+}
+
+// Engine-internal variant with a device status word for out-of-range positions.
+namespace vsl {
+int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
+                           const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
+                           const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
+                           void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
+                           int* status, cudaStream_t stream) {
+    GemvParams p = {};
+    p.W = Wqkv; p.N = (n_heads + 2 * n_kv) * head_dim; p.K = K; p.x = x; p.B = B; p.norm_w = norm_w; p.eps = eps;
+    p.n_heads = n_heads; p.n_kv = n_kv; p.head_dim = head_dim; p.pos = pos;
+    p.rope_cos = rope_cos; p.rope_sin = rope_sin; p.q_out = q_out; p.k_cache = k_cache; p.v_cache = v_cache;
+    p.kvdtype = kvdtype; p.page_table = page_table; p.max_pages = max_pages; p.page_size = page_size;
+    p.status = status;
+    return run_chunks(wdtype, EK_QKV, p, stream, 0);
+}
+}  // namespace vsl
+
+extern "C" int vsl_lm_head_sample(int wdtype, const void* W, int V_local, int K, const float* x,
+                                  const float* norm_w, float eps, int B, float* logits,
+                                  unsigned long long* argmax_slots, int vocab_offset, float temperature,
+                                  uint64_t seed, const int32_t* step_counter, void* stream) {
+    int rc = check_common(wdtype, W, V_local, K, x, B);
+    if (rc) return rc;
+    if (!logits || !argmax_slots) return set_error(VSL_ERR_INVALID, "lm_head: null logits or slots");
+    if (temperature > 0.0f && !step_counter)
+        return set_error(VSL_ERR_INVALID, "lm_head: sampling needs a device step counter");
+    GemvParams p = {};
+    p.W = W; p.N = V_local; p.K = K; p.x = x; p.B = B; p.y = logits; p.norm_w = norm_w; p.eps = eps;
+    p.slots = argmax_slots; p.vocab_offset = vocab_offset;
+    p.inv_temp = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+    p.seed = seed; p.step_counter = step_counter;
+    return run_chunks(wdtype, EK_LMHEAD, p, (cudaStream_t)stream, V_local);
+}
