@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--sweep", action="store_true",
+                    help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     return ap.parse_args()
 
 
@@ -329,8 +331,51 @@ def run_ours(args):
     return 0
 
 
+SWEEP_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+
+
+def run_sweep(args):
+    """y = x W^T with fp16 W [N][K] N(0, 0.02) and fp16-valued x [B][K] N(0, 1) (held as fp32 activations),
+    fp32 accumulation. Rotates copies of W so that each pass reads more than the 126 MB L2."""
+    import torch
+
+    import vsl
+    hbm_peak, peak_kind = peaks()
+    for N, K in SWEEP_SHAPES:
+        copies = max(2, -(-400_000_000 // (N * K * 2)))
+        W = torch.empty((copies, N, K), dtype=torch.float16, device="cuda")
+        for c in range(copies):
+            vsl.synth_fill(W[c], vsl.F16, 1, 5000 + c, 0, N * K, 0.02)
+        for B in (1, 4, 16, 64):
+            x = torch.randn((B, K), device="cuda").half().float()
+            y = torch.empty((B, N), device="cuda")
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for i in range(2 * copies):
+                    vsl.gemv(vsl.F16, W[i % copies], N, K, x, B, y, stream=s.cuda_stream)
+                reps = max(20, 4 * copies)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(s)
+                for i in range(reps):
+                    vsl.gemv(vsl.F16, W[i % copies], N, K, x, B, y, stream=s.cuda_stream)
+                e1.record(s)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            algo = 2 * N * K + 2 * B * K + 2 * B * N
+            gbs = algo / (us * 1e-6) / 1e9
+            print(json.dumps({"sweep": "projection", "N": N, "K": K, "B": B, "us": round(us, 3),
+                              "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 4), "peak": hbm_peak,
+                              "peak_kind": peak_kind, "TFLOP/s": round(2 * B * N * K / (us * 1e-6) / 1e12, 2),
+                              "launches_per_call": -(-B // 4)}), flush=True)
+        del W
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     args = parse()
+    if args.sweep:
+        return run_sweep(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -504,22 +504,33 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     const int d = c.d_model, hd = c.head_dim;
     const int res_epi = opt_.tp_rank == 0 ? VSL_EPI_ADD : VSL_EPI_STORE;  // partial sums reduced into x
     cudaStream_t st = stream_;
+    // L2 prefetch hints: each kernel requests the head of the next projection's weights so
+    // that the weight stream does not stall at kernel boundaries; the attention kernel
+    // (which reads little from HBM) prefetches the whole output projection.
+    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * d * es_, wo_b = (size_t)d * nh_l_ * hd * es_;
+    const size_t wgu_b = 2 * (size_t)ff_l_ * d * es_, wd_b = (size_t)d * ff_l_ * es_;
+    const size_t head = 16ull << 20;
+    auto H = [&](size_t bytes) { return std::min(bytes, head); };
     RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
+        const bool last = l + 1 == c.n_layers;
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, x_, L.attn_norm, c.rms_eps, B, pos_,
                                   rope_cos_, rope_sin_, q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_,
-                                  page_size_, status_, st));
+                                  page_size_, status_, st, L.wo, H(wo_b)));
         RC(flash_decode_impl(q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_, page_size_, pos_, B, nh_l_,
-                             nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st));
-        RC(vsl_gemv(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, st));
+                             nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st, L.wo,
+                             head ? wo_b : 0));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st));
         RC(allreduce_x(B));
-        RC(vsl_gemv(c.wdtype, L.wgu, 2 * ff_l_, d, x_, B, act_ffn_, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, st));
-        RC(vsl_gemv(c.wdtype, L.wd, d, ff_l_, act_ffn_, B, x_, res_epi, nullptr, 0.0f, st));
+        RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, x_, B, act_ffn_, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
+                     H(wd_b), st));
+        RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, act_ffn_, B, x_, res_epi, nullptr, 0.0f,
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st));
         RC(allreduce_x(B));
     }
-    RC(vsl_lm_head_sample(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_,
-                          temperature, seed, step_, st));
+    RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
+                    seed, step_, layers_[0].wqkv, H(qkv_b), st));
     if (nccl_) {
         ncclResult_t r = ncclAllReduce(slots_, slots_, (size_t)B, ncclUint64, ncclMax, (ncclComm_t)nccl_, st);
         if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));

@@ -38,6 +38,8 @@ struct FdParams {
     float* ws_o;   // [B][n_heads][n_splits][HD]
     float* ws_ml;  // [B][n_heads][n_splits][2]
     int* counters; // [B][n_kv]
+    const void* pf_ptr;  // weights of the projection that follows (prefetched into L2)
+    size_t pf_bytes;
 };
 
 template <typename KT> struct KvVec;
@@ -57,21 +59,28 @@ __host__ __device__ constexpr int fd_row_elems() {
 
 template <int HD, typename KT>
 __host__ __device__ constexpr size_t fd_smem_bytes() {
-    return (size_t)2 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunks
+    return (size_t)4 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunks, double-buffered
            + (size_t)FD_GMAX * HD * sizeof(float)                      // q
            + (size_t)2 * FD_GMAX * FD_CHUNK * sizeof(float)             // score partials
            + (size_t)FD_GMAX * FD_CHUNK * sizeof(float)                 // probabilities
            + (size_t)4 * FD_GMAX * sizeof(float);                       // m, l, alpha, misc
 }
 
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <int HD, typename KT>
 __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int RE = fd_row_elems<HD, KT>();
     constexpr int VEC = KvVec<KT>::VEC;
-    KT* k_s = reinterpret_cast<KT*>(smem_raw);
-    KT* v_s = k_s + FD_CHUNK * RE;
-    float* q_s = reinterpret_cast<float*>(v_s + FD_CHUNK * RE);
+    constexpr int VPR = HD / VEC;  // 16-byte vectors per row
+    KT* kv_s = reinterpret_cast<KT*>(smem_raw);  // [2 buffers][K, V][CHUNK][RE]
+    float* q_s = reinterpret_cast<float*>(kv_s + 4 * FD_CHUNK * RE);
     float* part_s = q_s + FD_GMAX * HD;           // [2][GMAX][CHUNK]
     float* p_s = part_s + 2 * FD_GMAX * FD_CHUNK;  // [GMAX][CHUNK]
     float* m_s = p_s + FD_GMAX * FD_CHUNK;         // [GMAX]
@@ -83,19 +92,77 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.n_heads / p.n_kv;
 
+    // pos[] and the cache below position pos were written by kernels that finished before the
+    // immediate predecessor started, so they are read before griddepcontrol.wait; the
+    // predecessor (the QKV projection) writes q and the key/value row at pos.
+    // Positions past the page table or the grid's coverage are never read (the QKV kernel
+    // has already flagged such a position in the engine's status word).
+    const int pos = p.pos[b];
+    const int len = min(pos + 1, min(p.max_pages * p.page_size, p.n_splits * p.split_len));
+    const int t_begin = split * p.split_len;
+    if (t_begin >= len) {  // empty split: not counted by the combiner; it only prefetches
+        if (p.pf_ptr && tid < 32) {
+            const int nblk = gridDim.x * gridDim.y * gridDim.z;
+            const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+            prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
+        }
+        return;
+    }
+    const int t_end = min(len, t_begin + p.split_len);
+    const int n_active = (len + p.split_len - 1) / p.split_len;
+    const int n_chunks = (t_end - t_begin + FD_CHUNK - 1) / FD_CHUNK;
+    const int new_row = pos - t_begin;  // row of the freshly appended position, if in this split
+
+    auto chunk_ptrs = [&](int ci, const KT*& kg, const KT*& vg) {
+        const int t0 = t_begin + ci * FD_CHUNK;  // t0 % 64 == 0 and page_size % 64 == 0: one page
+        const int page = p.page_table[(size_t)b * p.max_pages + t0 / p.page_size];
+        const size_t base = (((size_t)page * p.n_kv + g) * p.page_size + (t0 % p.page_size)) * HD;
+        kg = reinterpret_cast<const KT*>(p.k_cache) + base;
+        vg = reinterpret_cast<const KT*>(p.v_cache) + base;
+    };
+    // stage chunk ci into buffer buf with cp.async; rows equal to `skip` are left for later
+    auto issue = [&](int ci, int buf, int skip) {
+        const KT* kg;
+        const KT* vg;
+        chunk_ptrs(ci, kg, vg);
+        const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
+        KT* ks = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
+        KT* vs = ks + FD_CHUNK * RE;
+        for (int i = tid; i < n * VPR; i += FD_THREADS) {
+            const int r = i / VPR, c = (i % VPR) * VEC;
+            if (ci * FD_CHUNK + r == skip) continue;
+            cp_async16(ks + r * RE + c, kg + (size_t)r * HD + c);
+            cp_async16(vs + r * RE + c, vg + (size_t)r * HD + c);
+        }
+        cp_async_commit();
+    };
+
+    issue(0, 0, new_row);
+    if (n_chunks > 1) issue(1, 1, new_row);
+    if (p.pf_ptr && tid < 32) {
+        const int nblk = gridDim.x * gridDim.y * gridDim.z;
+        const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
+    }
+
     pdl_wait();
     pdl_launch_dependents();
 
-    const int len = p.pos[b] + 1;
-    const int t_begin = split * p.split_len;
-    if (t_begin >= len) return;  // empty split: not counted by the combiner
-    const int t_end = min(len, t_begin + p.split_len);
-    const int n_active = (len + p.split_len - 1) / p.split_len;
-
-    // q of the G heads of this group
+    // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done
+    if (new_row >= 0 && new_row < min(n_chunks, 2) * FD_CHUNK) {
+        const int ci = new_row / FD_CHUNK, r = new_row % FD_CHUNK;
+        const KT* kg;
+        const KT* vg;
+        chunk_ptrs(ci, kg, vg);
+        KT* ks = kv_s + (size_t)(2 * ci) * FD_CHUNK * RE;
+        KT* vs = ks + FD_CHUNK * RE;
+        for (int i = tid; i < VPR; i += FD_THREADS) {
+            *reinterpret_cast<uint4*>(ks + r * RE + i * VEC) = __ldcg(reinterpret_cast<const uint4*>(kg + (size_t)r * HD + i * VEC));
+            *reinterpret_cast<uint4*>(vs + r * RE + i * VEC) = __ldcg(reinterpret_cast<const uint4*>(vg + (size_t)r * HD + i * VEC));
+        }
+    }
     const int h0 = g * G;
-    for (int i = tid; i < G * HD; i += FD_THREADS)
-        q_s[i] = p.q[((size_t)b * p.n_heads + h0) * HD + i];
+    for (int i = tid; i < G * HD; i += FD_THREADS) q_s[i] = __ldcg(p.q + ((size_t)b * p.n_heads + h0) * HD + i);
     if (tid < FD_GMAX) { m_s[tid] = -CUDART_INF_F; l_s[tid] = 0.0f; }
 
     constexpr int EPT = (HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
@@ -105,24 +172,14 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
 #pragma unroll
         for (int i = 0; i < EPT; i++) o_acc[j][i] = 0.0f;
 
-    for (int t0 = t_begin; t0 < t_end; t0 += FD_CHUNK) {
-        const int n = min(FD_CHUNK, t_end - t0);
-        __syncthreads();  // previous chunk fully consumed (and q / m / l initialised)
-        // stage K and V rows [t0, t0+n): within one page because t0 % 64 == 0 and
-        // page_size % 64 == 0
-        const int page = p.page_table[(size_t)b * p.max_pages + t0 / p.page_size];
-        const size_t base = (((size_t)page * p.n_kv + g) * p.page_size + (t0 % p.page_size)) * HD;
-        const KT* kg = reinterpret_cast<const KT*>(p.k_cache) + base;
-        const KT* vg = reinterpret_cast<const KT*>(p.v_cache) + base;
-        constexpr int VPR = HD / VEC;  // vectors per row
-        for (int i = tid; i < n * VPR; i += FD_THREADS) {
-            const int r = i / VPR, c = (i % VPR) * VEC;
-            *reinterpret_cast<uint4*>(k_s + r * RE + c) =
-                __ldcg(reinterpret_cast<const uint4*>(kg + (size_t)r * HD + c));
-            *reinterpret_cast<uint4*>(v_s + r * RE + c) =
-                __ldcg(reinterpret_cast<const uint4*>(vg + (size_t)r * HD + c));
-        }
+    for (int ci = 0; ci < n_chunks; ci++) {
+        const int buf = ci & 1;
+        const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
+        if (ci + 1 < n_chunks) cp_async_wait<1>();  // the next chunk may still be in flight
+        else cp_async_wait<0>();
         __syncthreads();
+        const KT* k_s = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
+        const KT* v_s = k_s + FD_CHUNK * RE;
         // partial scores: thread (tt, half) covers half of the head dimension of position tt
         {
             const int tt = tid & (FD_CHUNK - 1), half = tid / FD_CHUNK;
@@ -190,6 +247,8 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
                     if (j < G) o_acc[j][i] = o_acc[j][i] * a_s[j] + acc[j];
             }
         }
+        __syncthreads();  // buffer `buf` is free again
+        if (ci + 2 < n_chunks) issue(ci + 2, buf, -1);
     }
 
     // ---- write this split's partial result ----
@@ -206,6 +265,18 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
             p.ws_ml[row * 2 + 0] = m_s[j];
             p.ws_ml[row * 2 + 1] = l_s[j];
         }
+    }
+    if (n_active == 1) {  // a single split: its partial is the answer
+#pragma unroll
+        for (int j = 0; j < FD_GMAX; j++) {
+            if (j >= G) continue;
+#pragma unroll
+            for (int i = 0; i < EPT; i++) {
+                const int e = tid + i * FD_THREADS;
+                if (e < HD) p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = o_acc[j][i] / l_s[j];
+            }
+        }
+        return;
     }
     __threadfence();
     __syncthreads();
@@ -263,7 +334,7 @@ static int launch_fd(const FdParams& p, cudaStream_t st) {
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
-                      size_t workspace_bytes, cudaStream_t stream) {
+                      size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes) {
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
         return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
     if (B <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > FD_GMAX)
@@ -288,6 +359,8 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
     p.ws_ml = reinterpret_cast<float*>(w);
     w += align256((size_t)B * n_heads * n_splits * 2 * sizeof(float));
     p.counters = reinterpret_cast<int*>(w);
+    p.pf_ptr = pf_ptr;
+    p.pf_bytes = pf_bytes;
     if (kvdtype == VSL_F16) {
         if (head_dim == 128) return launch_fd<128, __half>(p, stream);
         if (head_dim == 64) return launch_fd<64, __half>(p, stream);
@@ -314,5 +387,5 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream);
+                                  (cudaStream_t)stream, nullptr, 0);
 }

@@ -29,6 +29,86 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     return r;
 }
 
+// ---------------------------------------------------------------------------------------
+// Bulk asynchronous copies (TMA, non-tensor form) and mbarriers.
+// Every wait is bounded by wall time (%globaltimer): on expiry the caller records
+// VSL_ERR_TIMEOUT in a status word and stops, instead of spinning forever.
+// ---------------------------------------------------------------------------------------
+constexpr unsigned long long WAIT_LIMIT_NS = 1000000000ull;  // one second
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase with the given parity to complete; false after WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 64; i++)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > WAIT_LIMIT_NS) return false;
+    }
+}
+// global -> shared bulk copy completing on `bar` (bytes % 16 == 0, both addresses 16-aligned)
+__device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// bring [src, src+bytes) into L2 without waiting (bytes % 16 == 0)
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+// Request share `part` of `nparts` of [base, base+bytes) into L2, split among `nlanes`
+// callers (caller `lane_id` issues every nlanes-th 16 KB piece).
+__device__ __forceinline__ void prefetch_share(const void* base, size_t bytes, int part, int nparts, int lane_id,
+                                               int nlanes) {
+    const size_t lo = (bytes * (size_t)part / (size_t)nparts) & ~(size_t)15;
+    const size_t hi = (bytes * (size_t)(part + 1) / (size_t)nparts) & ~(size_t)15;
+    const char* b = reinterpret_cast<const char*>(base);
+    for (size_t off = lo + (size_t)lane_id * 16384; off < hi; off += (size_t)nlanes * 16384)
+        prefetch_l2(b + off, (uint32_t)(hi - off < 16384 ? hi - off : 16384));
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void set_status(int* status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -50,10 +50,11 @@ struct GemvParams {
     unsigned long long seed;
     const int32_t* step_counter;
     int* status;
+    // L2 prefetch hint: weights of the kernel that follows; each CTA requests its share
+    // once its own rows are done, filling the tail of this launch
+    const void* pf_ptr;
+    size_t pf_bytes;
 };
-
-constexpr int GEMV_THREADS = 256;
-constexpr int GEMV_U = 4;  // 16-byte vectors per row in flight per lane
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }
 
@@ -72,8 +73,12 @@ __device__ __forceinline__ float gumbel(unsigned long long seed, int step, int b
     return -logf(-logf(u));
 }
 
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_U = 8;
+constexpr int GEMV_L2_HEAD = 96 * 1024;
+
 template <typename WT, int NB, int EK, bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = WTraits<WT>::VEC;
@@ -87,21 +92,17 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvParams p) {
     const int u_end = (int)(((long long)n_units * (blockIdx.x + 1)) / gridDim.x);
     const WT* W = reinterpret_cast<const WT*>(p.W);
 
-    // Request the first weight vectors of this warp's first unit before waiting on the
-    // predecessor kernel: weights are never produced by it.
     int unit = u_begin + warp;
-    uint4 pre0[GEMV_U], pre1[GEMV_U];
-    bool have_pre = false;
-    if (unit < u_end && (GEMV_U - 1) * 32 + lane < nvec) {
-        const int r0 = 2 * unit, r1 = min(2 * unit + 1, N - 1);
-        const WT* w0 = W + (size_t)r0 * K;
-        const WT* w1 = W + (size_t)r1 * K;
-#pragma unroll
-        for (int u = 0; u < GEMV_U; u++) {
-            pre0[u] = ldg_stream(w0 + (size_t)(lane + 32 * u) * VEC);
-            pre1[u] = ldg_stream(w1 + (size_t)(lane + 32 * u) * VEC);
-        }
-        have_pre = true;
+
+    // L2 window: the CTA's rows are one contiguous byte range; request its head now
+    {
+        const size_t row_bytes = (size_t)K * sizeof(WT);
+        const size_t r_lo = 2 * (size_t)u_begin, r_hi = min((size_t)N, 2 * (size_t)u_end);
+        const char* base = reinterpret_cast<const char*>(W) + r_lo * row_bytes;
+        const size_t total = (r_hi - r_lo) * row_bytes;
+        const size_t head = min(total, (size_t)GEMV_L2_HEAD);
+        for (size_t off = (size_t)threadIdx.x * 16384; off < head; off += (size_t)GEMV_THREADS * 16384)
+            prefetch_l2(base + off, (uint32_t)min((size_t)16384, head - off));
     }
 
     pdl_wait();
@@ -159,22 +160,22 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvParams p) {
         const int r1 = has1 ? r0 + 1 : r0;
         const WT* w0 = W + (size_t)r0 * K;
         const WT* w1 = W + (size_t)r1 * K;
+        // keep the L2 window moving: this warp's next pair
+        if (lane == 0 && unit + NW < u_end) {
+            const int rn = 2 * (unit + NW);
+            const int rows = min(2, N - rn);
+            prefetch_l2(W + (size_t)rn * K, (uint32_t)((size_t)rows * K * sizeof(WT)));
+        }
         float acc0[NB], acc1[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
         int v = lane;
         for (; v + 32 * (GEMV_U - 1) < nvec; v += 32 * GEMV_U) {
             uint4 a[GEMV_U], c[GEMV_U];
-            if (have_pre) {
 #pragma unroll
-                for (int u = 0; u < GEMV_U; u++) { a[u] = pre0[u]; c[u] = pre1[u]; }
-                have_pre = false;
-            } else {
-#pragma unroll
-                for (int u = 0; u < GEMV_U; u++) {
-                    a[u] = ldg_stream(w0 + (size_t)(v + 32 * u) * VEC);
-                    c[u] = ldg_stream(w1 + (size_t)(v + 32 * u) * VEC);
-                }
+            for (int u = 0; u < GEMV_U; u++) {
+                a[u] = ldg_stream(w0 + (size_t)(v + 32 * u) * VEC);
+                c[u] = ldg_stream(w1 + (size_t)(v + 32 * u) * VEC);
             }
 #pragma unroll
             for (int u = 0; u < GEMV_U; u++) {
@@ -284,30 +285,41 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvParams p) {
         for (int b = 0; b < NB; b++)
             if (lane == b && b < B && best[b] != 0ull) atomicMax(p.slots + b, best[b]);
     }
+    if (p.pf_ptr && lane == 0) prefetch_share(p.pf_ptr, p.pf_bytes, blockIdx.x, gridDim.x, warp, NW);
 }
 
 // ---------------------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------------------
 
+// activation rows one launch stages in shared memory (fp32 [rows][K]); the compiled row
+// counts are 1, 2 and 4
+static int max_rows_per_launch(int K) {
+    const size_t room = 200 * 1024;
+    const int c = (int)(room / ((size_t)K * sizeof(float)));
+    return c >= 4 ? 4 : c >= 2 ? 2 : c;
+}
+
 template <typename WT, int NB, int EK, bool NORM>
 static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
     auto kern = gemv_kernel<WT, NB, EK, NORM>;
     const size_t smem = (size_t)NB * p.K * sizeof(float);
     static thread_local int configured_dev = -1;
+    static thread_local size_t configured_smem = 0;
     static thread_local int occ = 1;
-    static thread_local size_t occ_smem = 0;
     int dev = 0;
     cudaGetDevice(&dev);
-    if (configured_dev != dev || occ_smem != smem) {
+    if (configured_dev != dev || configured_smem != smem) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return launch_status(e, "gemv smem attribute");
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMV_THREADS, smem);
         if (e != cudaSuccess) return launch_status(e, "gemv occupancy");
         if (occ < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d does not fit in shared memory", p.K);
+        if (occ > 2) occ = 2;
         configured_dev = dev;
-        occ_smem = smem;
+        configured_smem = smem;
     }
+    // grid = whole waves of resident CTAs; each CTA owns a contiguous, balanced range of row pairs
     const int n_units = (p.N + 1) / 2;
     const int nw = GEMV_THREADS / 32;
     int grid = sm_count() * occ;
@@ -355,9 +367,8 @@ static int check_common(int wdtype, const void* W, int N, int K, const float* x,
 // Large batches are processed in chunks of 4 activation rows (each chunk re-streams W).
 static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y_cols) {
     const int B = p.B;
-    // activation rows per launch: at most 4, and at most what fits in ~200 KB of shared memory
-    int cmax = (int)((200 * 1024) / ((size_t)p.K * sizeof(float)));
-    if (cmax > 4) cmax = 4;
+    // activation rows per launch: at most 4, and at most what fits beside the weight ring
+    const int cmax = max_rows_per_launch(p.K);
     if (cmax < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d exceeds the shared-memory staging limit", p.K);
     for (int b0 = 0; b0 < B; b0 += cmax) {
         GemvParams q = p;
@@ -423,19 +434,44 @@ extern "C" int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, in
     return run_chunks(wdtype, EK_QKV, p, (cudaStream_t)stream, 0);
 }
 
-// Engine-internal variant with a device status word for out-of-range positions.
+// Engine-internal entry points: a device status word for out-of-range positions and the
+// L2 prefetch hint for the weights of the next kernel in the decode step.
 namespace vsl {
+int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
+              const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream) {
+    int rc = check_common(wdtype, W, N, K, x, B);
+    if (rc) return rc;
+    GemvParams p = {};
+    p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
+    p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
+    int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
+    return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N);
+}
+
+int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
+                 float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
+                 const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream) {
+    GemvParams p = {};
+    p.W = W; p.N = V_local; p.K = K; p.x = x; p.B = B; p.y = logits; p.norm_w = norm_w; p.eps = eps;
+    p.slots = slots; p.vocab_offset = vocab_offset;
+    p.inv_temp = temperature > 0.0f ? 1.0f / temperature : 0.0f;
+    p.seed = seed; p.step_counter = step_counter;
+    p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
+    return run_chunks(wdtype, EK_LMHEAD, p, stream, V_local);
+}
+
 int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
                            const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
                            const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
-                           int* status, cudaStream_t stream) {
+                           int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes) {
     GemvParams p = {};
     p.W = Wqkv; p.N = (n_heads + 2 * n_kv) * head_dim; p.K = K; p.x = x; p.B = B; p.norm_w = norm_w; p.eps = eps;
     p.n_heads = n_heads; p.n_kv = n_kv; p.head_dim = head_dim; p.pos = pos;
     p.rope_cos = rope_cos; p.rope_sin = rope_sin; p.q_out = q_out; p.k_cache = k_cache; p.v_cache = v_cache;
     p.kvdtype = kvdtype; p.page_table = page_table; p.max_pages = max_pages; p.page_size = page_size;
     p.status = status;
+    p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
     return run_chunks(wdtype, EK_QKV, p, stream, 0);
 }
 }  // namespace vsl
