@@ -115,6 +115,22 @@ VSL_API int vsl_flash_decode(const float* q, const void* k_cache, const void* v_
                      int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of vsl_flash_decode (no counterpart in the reference). For callers
+ * that must not have the library allocate device memory -- hosts that own every device
+ * byte through their own pool or budget, or loops that cannot take an allocation's implicit
+ * synchronisation -- the split-K scratch comes from a fixed 4 MiB device array inside
+ * libvsl.so (one per GPU that loads the library, held until the process exits). Shapes
+ * whose scratch (vsl_flash_decode_workspace_size) exceeds 4 MiB are rejected with
+ * VSL_ERR_UNSUPPORTED. The first call on a device looks up the array's device address
+ * with that device current, so make that first call before any stream capture. Every
+ * call shares the one array: calls that can overlap on the GPU (different streams, or
+ * different host threads on the same device) race and must be serialised by the caller.
+ * Each call clears the split counters it needs before launching. */
+VSL_API int vsl_flash_decode_noalloc(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                     const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                     int B, int n_heads, int n_kv, int head_dim, int max_len, int split_len,
+                                     float* out, void* stream);
+
 /* lm_head projection fused with the sampler (replaces final_projection_with_weights
  * :3028-3130 and sample_token :1540-1553). Computes logits[b][n] for the local vocab slice
  * (global index = vocab_offset + n) and folds each row into argmax_slots[b] (uint64,

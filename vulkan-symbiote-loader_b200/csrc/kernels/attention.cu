@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.cuh"
 
@@ -387,5 +389,73 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
+                                  (cudaStream_t)stream, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant.
+//
+// Some callers cannot let a library call cudaMalloc: hosts whose device memory is owned by
+// their own pool or budget (every byte must come from them or be fixed up front), and
+// latency-critical loops that cannot afford an allocation's implicit device
+// synchronisation or its failure modes mid-run. vsl_flash_decode_noalloc gives them the
+// split-K attention without a workspace argument: its scratch is this file-scope device
+// array, which exists once per GPU that loads the library and lives until the process exits.
+// ---------------------------------------------------------------------------------------
+static constexpr size_t FD_STATIC_SCRATCH_BYTES = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_fd_static_scratch[FD_STATIC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_fd_scratch_mu;
+void* g_fd_scratch_addr[kMaxDevices] = {};
+
+// Device address of the static scratch on the current device. In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device with that
+// device current, and cached.
+int fd_static_scratch(void** out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices)
+        return vsl::set_error(VSL_ERR_UNSUPPORTED, "flash_decode_noalloc: device ordinal %d", dev);
+    std::lock_guard<std::mutex> lock(g_fd_scratch_mu);
+    if (!g_fd_scratch_addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_fd_static_scratch);
+        if (e != cudaSuccess || !p)
+            return vsl::set_error(VSL_ERR_CUDA, "flash_decode_noalloc: cudaGetSymbolAddress failed: %s",
+                                  cudaGetErrorString(e));
+        g_fd_scratch_addr[dev] = p;
+    }
+    *out = g_fd_scratch_addr[dev];
+    return VSL_OK;
+}
+}  // namespace
+
+extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                        const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                        int B, int n_heads, int n_kv, int head_dim, int max_len, int split_len,
+                                        float* out, void* stream) {
+    if (B <= 0 || n_heads <= 0 || n_kv <= 0 || head_dim <= 0 || max_len <= 0 || split_len <= 0)
+        return vsl::set_error(VSL_ERR_INVALID, "flash_decode_noalloc: bad arguments");
+    const int n_splits = vsl::fd_splits(max_len, split_len);
+    const size_t need = vsl::fd_workspace(B, n_heads, n_kv, head_dim, n_splits);
+    if (need > FD_STATIC_SCRATCH_BYTES)
+        return vsl::set_error(VSL_ERR_UNSUPPORTED,
+                              "flash_decode_noalloc: this shape needs %zu bytes of scratch but the static scratch "
+                              "holds %zu; use vsl_flash_decode with a caller-owned workspace",
+                              need, FD_STATIC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    int rc = fd_static_scratch(&ws);
+    if (rc) return rc;
+    // The array keeps whatever the previous call left; the split counters must start at zero.
+    const size_t counters_off = vsl::align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float)) +
+                                vsl::align256((size_t)B * n_heads * n_splits * 2 * sizeof(float));
+    cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(ws) + counters_off, 0, (size_t)B * n_kv * sizeof(int),
+                                    (cudaStream_t)stream);
+    if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");
+    return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
+                                  n_kv, head_dim, max_len, split_len, out, ws, FD_STATIC_SCRATCH_BYTES,
                                   (cudaStream_t)stream, nullptr, 0);
 }
