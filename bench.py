@@ -194,6 +194,19 @@ def run_reference(args):
     return 0
 
 
+def profiled_traffic():
+    """DRAM read+write bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gemv_gateup_7b_fp16_bs1.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.startswith("| traffic per launch"):
+                    return int(float(line.split("|")[2].split()[0]) * 1e6)
+    except (OSError, ValueError, IndexError):
+        pass
+    return None
+
+
 def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     """Time the fused RMSNorm + gate/up + SwiGLU projection (the largest per-step byte share)
     on 7B-shape weights, rotating 8 copies (1.4 GB, far above L2) with CUDA events."""
@@ -226,7 +239,9 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     return {"bound": "hbm", "kernel": "gemv_kernel<__half,1,EK_SWIGLU,NORM> (gate/up + SwiGLU, fused RMSNorm)",
             "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms * 1e3, 3),
-            "traffic": None}
+            "traffic": profiled_traffic() if tp == 1 else None,
+            "traffic_source": "profiles/gemv_gateup_7b_fp16_bs1.md (ncu, engine launch: includes the 16.8 MB "
+                              "L2 prefetch of the next projection)"}
 
 
 def run_ours(args):
