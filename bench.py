@@ -111,33 +111,6 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def dist_env():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", str(rank)))
-    return ws, rank, local
-
-
-def init_dist(ws):
-    if ws == 1:
-        return None
-    import datetime
-
-    import torch.distributed as dist
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
-    return dist
-
-
-def max_over_ranks(dist, v: float) -> float:
-    if dist is None:
-        return v
-    import torch
-    t = torch.tensor([v], dtype=torch.float64)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
-
-
 def cpu_baseline(cfg, seconds: float, threads: int | None = None):
     """Oracle decode steps of the same model on the host cores (bounded sample)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -172,7 +145,8 @@ def cpu_baseline(cfg, seconds: float, threads: int | None = None):
 
 
 def run_reference(args):
-    ws, rank, _ = dist_env()
+    from vsl import dist as vdist
+    ws, rank, _ = vdist.env()
     if rank != 0:
         return 0
     cfg = dict(CONFIG_7B)
@@ -249,22 +223,17 @@ def run_ours(args):
     import torch
 
     import vsl
+    from vsl import dist as vdist
     from vsl import synth
-    ws, rank, local = dist_env()
-    dist = init_dist(ws)
+    ws, rank, local = vdist.env()
+    dist = vdist.init(ws)
     torch.cuda.set_device(local)
     cfg = dict(CONFIG_7B)
     if args.layers:
         cfg["n_layers"] = args.layers
     max_seq = PROMPT + args.warmup + 2 * args.steps + 8
     max_seq = (max_seq + 63) // 64 * 64
-    nccl_id = None
-    if ws > 1:
-        buf = torch.zeros(128, dtype=torch.uint8)
-        if rank == 0:
-            buf = torch.tensor(list(vsl.nccl_unique_id()), dtype=torch.uint8)
-        dist.broadcast(buf, 0)
-        nccl_id = bytes(buf.tolist())
+    nccl_id = vdist.nccl_id(dist)
     t0 = time.perf_counter()
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=1, max_seq=max_seq,
                                tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
@@ -289,7 +258,7 @@ def run_ours(args):
     if dist:
         dist.barrier()
     ms = e0.elapsed_time(e1)
-    ms = max_over_ranks(dist, ms)
+    ms = vdist.max_over_ranks(dist, ms)
     _, bytes_end = eng.step_stats(1)
     status = eng.device_status()
     # end to end through the host API: pinned host id in, sampled id back, every step
@@ -304,7 +273,7 @@ def run_ours(args):
     for _ in range(n_e2e):
         nxt, _ = eng.step_host(nxt)
     e2e_s = time.perf_counter() - t1
-    e2e_s = max_over_ranks(dist, e2e_s)
+    e2e_s = vdist.max_over_ranks(dist, e2e_s)
     if status != 0 or eng.device_status() != 0:
         raise SystemExit(f"device status {status}")
     hbm_peak, peak_kind = peaks()

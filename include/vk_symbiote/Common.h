@@ -16,6 +16,13 @@
 #include <utility>
 #include <vector>
 
+// Symbols of the C++ API exported from libvsl.so (built with hidden visibility).
+#if defined(__GNUC__)
+#define VSL_CPP_API __attribute__((visibility("default")))
+#else
+#define VSL_CPP_API
+#endif
+
 namespace vk_symbiote {
 
 using uint8 = uint8_t;

@@ -39,7 +39,7 @@ struct GGUFHeader {
     uint64 metadata_kv_count = 0;
 };
 
-struct GGUFTensorInfo {
+struct VSL_CPP_API GGUFTensorInfo {
     std::string name;
     uint32 n_dimensions = 0;
     std::vector<uint64> dimensions;  // ne[0] is the contiguous dimension
@@ -52,7 +52,7 @@ struct GGUFTensorInfo {
     uint64 element_count() const;
 };
 
-struct GGUFMetadataKV {
+struct VSL_CPP_API GGUFMetadataKV {
     std::string key;
     GGUFValueType value_type = GGUFValueType::UINT8;
     std::vector<uint8_t> raw_value;  // scalar bytes; string bytes; array: element bytes
@@ -100,7 +100,7 @@ struct TensorCacheConfig {
     bool enable_compression = false;
 };
 
-class GGUFLoader {
+class VSL_CPP_API GGUFLoader {
 public:
     explicit GGUFLoader(const Path& file_path);
     ~GGUFLoader();

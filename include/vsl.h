@@ -200,7 +200,8 @@ VSL_API int vsl_gguf_model_config(const char* path, vsl_model_config* out);
 VSL_API int vsl_gguf_tensor_info(const char* path, const char* name, int* ggml_type, uint64_t ne[4], uint64_t* file_offset);
 
 
-/* ncclUniqueId bytes for tensor-parallel engines (call on rank 0, broadcast to the rest). */
+/* ncclUniqueId bytes for tensor-parallel engines (call on rank 0, broadcast to the rest).
+ * An id forms exactly one communicator: every tensor-parallel engine group needs a fresh id. */
 VSL_API int vsl_nccl_unique_id(void* out128);
 
 /* Load a GGUF model (GGUFLoader::load + load_all_weights, VulkanSymbioteEngine.cpp:1114-1175,
@@ -252,6 +253,10 @@ VSL_API void* vsl_engine_stream(vsl_engine* e);
 /* Kernels launched per decode step and bytes of weights + KV read per step at the
  * current positions (algorithmic bytes for the roofline). */
 VSL_API int vsl_engine_step_stats(vsl_engine* e, int B, int* kernels_per_step, double* bytes_per_step);
+
+/* Device bytes held by the engine: weights (HBM arena), paged KV cache, and everything
+ * else (activations, token log, attention workspace). Feeds get_vram_stats(). */
+VSL_API int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t* kv_bytes, size_t* other_bytes);
 
 /* Sticky device status word of the engine (0 = OK; VSL_ERR_TIMEOUT / VSL_ERR_BOUNDS set by
  * kernels that gave up on a bounded wait or rejected an index). */

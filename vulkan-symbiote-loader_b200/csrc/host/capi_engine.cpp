@@ -217,3 +217,11 @@ extern "C" int vsl_gguf_tensor_info(const char* path, const char* name, int* ggm
     return VSL_OK;
     GUARD_END
 }
+
+extern "C" int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t* kv_bytes, size_t* other_bytes) {
+    if (int rc = check_engine(e)) return rc;
+    if (weight_bytes) *weight_bytes = e->impl->arena_bytes();
+    if (kv_bytes) *kv_bytes = e->impl->kv_bytes();
+    if (other_bytes) *other_bytes = e->impl->other_bytes();
+    return VSL_OK;
+}

@@ -209,6 +209,7 @@ int DecodeEngine::alloc_buffers() {
     };
     size_t total = 0;
     for (auto& it : items) total += align_up(it.bytes, A);
+    act_bytes_ = total;
     CK(cudaMalloc(&act_, total));
     CK(cudaMemset(act_, 0, total));
     char* a = (char*)act_;

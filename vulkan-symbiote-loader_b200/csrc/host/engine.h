@@ -59,6 +59,7 @@ public:
     int max_seq() const { return opt_.max_seq; }
     size_t arena_bytes() const { return arena_bytes_; }
     size_t kv_bytes() const { return kv_bytes_; }
+    size_t other_bytes() const { return act_bytes_ + fd_ws_bytes_; }
     vk_symbiote::PackResidency residency() const { return residency_; }
 
 private:
@@ -91,6 +92,7 @@ private:
     void* kv_ = nullptr;
     size_t kv_bytes_ = 0;
     void* act_ = nullptr;  // activations and bookkeeping
+    size_t act_bytes_ = 0;
     void* fd_ws_ = nullptr;
     size_t fd_ws_bytes_ = 0;
 
