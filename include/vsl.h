@@ -183,6 +183,9 @@ typedef struct {
     double vram_budget_gb; /* 0 = no cap; above the cap layers stream from pinned host */
     int use_graph;     /* capture the decode step in a CUDA graph (default 1)          */
     int use_pdl;       /* programmatic dependent launch between kernels (default 1)    */
+    int use_fused;     /* 1 = run each decode step as one persistent cooperative kernel
+                          when the shape allows it; 0 (default) = one kernel per operation,
+                          replayed as a CUDA graph with programmatic dependent launch  */
 } vsl_engine_options;
 
 VSL_API void vsl_engine_default_options(vsl_engine_options* opt);
@@ -257,6 +260,13 @@ VSL_API int vsl_engine_step_stats(vsl_engine* e, int B, int* kernels_per_step, d
 /* Device bytes held by the engine: weights (HBM arena), paged KV cache, and everything
  * else (activations, token log, attention workspace). Feeds get_vram_stats(). */
 VSL_API int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t* kv_bytes, size_t* other_bytes);
+
+/* Per-phase trace of the fused decode step (one persistent kernel per token): when on, CTA 0
+ * records %globaltimer (ns) at kernel start and after each phase barrier of every step;
+ * vsl_engine_read_trace copies the last step's stamps (embedding, then per layer QKV,
+ * attention, combine, O, gate/up, down, then lm_head). */
+VSL_API int vsl_engine_set_trace(vsl_engine* e, int enable);
+VSL_API int vsl_engine_read_trace(vsl_engine* e, int cap, uint64_t* out_ns, int* n_out);
 
 /* Sticky device status word of the engine (0 = OK; VSL_ERR_TIMEOUT / VSL_ERR_BOUNDS set by
  * kernels that gave up on a bounded wait or rejected an index). */

@@ -37,6 +37,7 @@ extern "C" void vsl_engine_default_options(vsl_engine_options* o) {
     o->vram_budget_gb = 0.0;
     o->use_graph = 1;
     o->use_pdl = 1;
+    o->use_fused = 0;
 }
 
 extern "C" int vsl_nccl_unique_id(void* out128) {
@@ -224,4 +225,18 @@ extern "C" int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size
     if (kv_bytes) *kv_bytes = e->impl->kv_bytes();
     if (other_bytes) *other_bytes = e->impl->other_bytes();
     return VSL_OK;
+}
+
+extern "C" int vsl_engine_set_trace(vsl_engine* e, int enable) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    return e->impl->set_trace(enable != 0);
+    GUARD_END
+}
+
+extern "C" int vsl_engine_read_trace(vsl_engine* e, int cap, uint64_t* out_ns, int* n_out) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    return e->impl->read_trace(cap, reinterpret_cast<unsigned long long*>(out_ns), n_out);
+    GUARD_END
 }

@@ -19,6 +19,7 @@
 #include "../../../include/vk_symbiote/GGUFLoader.h"
 #include "../../../include/vk_symbiote/NomadPack.h"
 #include "../../../include/vsl.h"
+#include "../kernels/fused_step.h"
 
 namespace vsl {
 
@@ -52,6 +53,8 @@ public:
                  const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out);
     int device_status(int* status);
     int step_stats(int B, int* kernels, double* bytes);
+    int set_trace(bool on);
+    int read_trace(int cap, unsigned long long* out, int* n);
 
     const vsl_model_config& config() const { return cfg_; }
     cudaStream_t stream() const { return stream_; }
@@ -67,6 +70,9 @@ private:
     int init(const vsl_model_config& cfg, const vsl_engine_options& opt);
     int alloc_buffers();
     int enqueue_step(int B, float temperature, uint64_t seed);
+    int build_fused_program();
+    bool fused_supported(int B) const;
+    int enqueue_fused_step(int B, float temperature, uint64_t seed);
     int get_graph(int B, float temperature, uint64_t seed, cudaGraphExec_t* exec);
     int allreduce_x(int B);
     int check_cuda(cudaError_t e, const char* what);
@@ -144,6 +150,18 @@ private:
         }
     };
     std::map<GraphKey, cudaGraphExec_t> graphs_;
+
+    // fused decode step
+    FsPhase* fs_phases_ = nullptr;  // device
+    FsKV* fs_kv_ = nullptr;         // device
+    int fs_n_phases_ = 0;
+    int fs_max_chunks_ = 0;
+    float* fs_att_ws_ = nullptr;
+    unsigned long long* fs_bar_ = nullptr;  // [counter, epoch]
+    int* fs_abort_ = nullptr;
+    unsigned long long* fs_trace_ = nullptr;
+    bool fs_trace_on_ = false;
+    bool fs_ready_ = false;
 
     void* nccl_ = nullptr;  // ncclComm_t
     vk_symbiote::PackResidency residency_{};

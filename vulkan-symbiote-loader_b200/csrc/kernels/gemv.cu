@@ -18,60 +18,10 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 #include "launch.cuh"
 
 namespace vsl {
-
-enum EpiKind { EK_STORE = 0, EK_ADD = 1, EK_SWIGLU = 2, EK_QKV = 3, EK_LMHEAD = 4 };
-
-struct GemvParams {
-    const void* W;
-    int N, K;
-    const float* x;
-    int B;
-    float* y;
-    const float* norm_w;
-    float eps;
-    // QKV + RoPE + KV append
-    int n_heads, n_kv, head_dim;
-    const int32_t* pos;
-    const float* rope_cos;
-    const float* rope_sin;
-    float* q_out;
-    void* k_cache;
-    void* v_cache;
-    int kvdtype;
-    const int32_t* page_table;
-    int max_pages, page_size;
-    // lm_head sampler
-    unsigned long long* slots;
-    int vocab_offset;
-    float inv_temp;
-    unsigned long long seed;
-    const int32_t* step_counter;
-    int* status;
-    // L2 prefetch hint: weights of the kernel that follows; each CTA requests its share
-    // once its own rows are done, filling the tail of this launch
-    const void* pf_ptr;
-    size_t pf_bytes;
-};
-
-__device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }
-
-__device__ __forceinline__ unsigned long long smix64(unsigned long long z) {
-    z += 0x9E3779B97F4A7C15ull;
-    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-    return z ^ (z >> 31);
-}
-
-// Gumbel(0,1) noise for (seed, step, b, index): -log(-log(u)), u in (0,1).
-__device__ __forceinline__ float gumbel(unsigned long long seed, int step, int b, uint32_t idx) {
-    unsigned long long h = smix64(smix64(seed ^ ((unsigned long long)step * 0x9E3779B97F4A7C15ull)) +
-                                  (((unsigned long long)b << 32) | idx));
-    float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
-    return -logf(-logf(u));
-}
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_U = 8;
@@ -227,57 +177,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams 
         for (int b = 0; b < NB; b++) {
             if (lane != b || b >= B) continue;
             const float s0 = acc0[b], s1 = acc1[b];
-            if (EK == EK_STORE) {
-                p.y[(size_t)b * N + r0] = s0;
-                if (has1) p.y[(size_t)b * N + r0 + 1] = s1;
-            } else if (EK == EK_ADD) {
-                p.y[(size_t)b * N + r0] += s0;
-                if (has1) p.y[(size_t)b * N + r0 + 1] += s1;
-            } else if (EK == EK_SWIGLU) {
-                p.y[(size_t)b * (N >> 1) + unit] = silu_f(s0) * s1;
-            } else if (EK == EK_QKV) {
-                const int hd = p.head_dim;
-                const int qd = p.n_heads * hd, kvd = p.n_kv * hd;
-                const int pos = p.pos[b];
-                if (pos < 0 || pos >= p.max_pages * p.page_size) {
-                    if (p.status) atomicCAS(p.status, 0, VSL_ERR_BOUNDS);
-                    continue;
-                }
-                const int e = r0 % hd;  // even
-                float o0 = s0, o1 = s1;
-                if (r0 < qd + kvd) {  // rotate q and k: adjacent pair (e, e+1)
-                    const int half = hd >> 1;
-                    const float cs = p.rope_cos[(size_t)pos * half + (e >> 1)];
-                    const float sn = p.rope_sin[(size_t)pos * half + (e >> 1)];
-                    o0 = __fsub_rn(__fmul_rn(s0, cs), __fmul_rn(s1, sn));
-                    o1 = __fadd_rn(__fmul_rn(s0, sn), __fmul_rn(s1, cs));
-                }
-                if (r0 < qd) {
-                    p.q_out[(size_t)b * qd + r0] = o0;
-                    p.q_out[(size_t)b * qd + r0 + 1] = o1;
-                } else {
-                    const bool is_v = r0 >= qd + kvd;
-                    const int rr = is_v ? r0 - qd - kvd : r0 - qd;
-                    const int g = rr / hd;
-                    const int page = p.page_table[(size_t)b * p.max_pages + pos / p.page_size];
-                    const size_t idx =
-                        (((size_t)page * p.n_kv + g) * p.page_size + (pos % p.page_size)) * hd + e;
-                    void* cache = is_v ? p.v_cache : p.k_cache;
-                    kv_put(cache, idx, o0, p.kvdtype);
-                    kv_put(cache, idx + 1, o1, p.kvdtype);
-                }
-            } else if (EK == EK_LMHEAD) {
-                p.y[(size_t)b * N + r0] = s0;
-                if (has1) p.y[(size_t)b * N + r0 + 1] = s1;
-                float c0 = s0, c1 = s1;
-                const uint32_t g0 = (uint32_t)(p.vocab_offset + r0);
-                if (p.inv_temp > 0.0f) {
-                    c0 = s0 * p.inv_temp + gumbel(p.seed, step, b, g0);
-                    c1 = s1 * p.inv_temp + gumbel(p.seed, step, b, g0 + 1);
-                }
-                if (c0 == c0) best[b] = max(best[b], pack_argmax(c0, g0));
-                if (has1 && c1 == c1) best[b] = max(best[b], pack_argmax(c1, g0 + 1));
-            }
+            gemv_pair_epilogue<EK>(p, b, r0, unit, has1, s0, s1, best[b], step);
         }
     }
     if (EK == EK_LMHEAD) {

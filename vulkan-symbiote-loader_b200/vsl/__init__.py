@@ -41,7 +41,7 @@ class EngineOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("max_batch", C.c_int), ("max_seq", C.c_int), ("kv_dtype", C.c_int),
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
-                ("use_pdl", C.c_int)]
+                ("use_pdl", C.c_int), ("use_fused", C.c_int)]
 
 
 _lib = None
@@ -89,6 +89,9 @@ def lib() -> C.CDLL:
         "vsl_engine_stream": (vp, [vp]),
         "vsl_engine_step_stats": (i32, [vp, i32, C.POINTER(i32), C.POINTER(f64)]),
         "vsl_engine_device_status": (i32, [vp, C.POINTER(i32)]),
+        "vsl_engine_set_trace": (i32, [vp, i32]),
+        "vsl_engine_read_trace": (i32, [vp, i32, C.POINTER(C.c_uint64), C.POINTER(i32)]),
+        "vsl_engine_memory_stats": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -311,6 +314,22 @@ class Engine:
         b = C.c_double()
         check(lib().vsl_engine_step_stats(self.h, batch, C.byref(k), C.byref(b)))
         return k.value, b.value
+
+    def set_trace(self, on: bool = True):
+        check(lib().vsl_engine_set_trace(self.h, 1 if on else 0))
+
+    def read_trace(self):
+        """Nanosecond stamps of the last fused step: start, then one per phase barrier."""
+        cap = 4096
+        buf = (C.c_uint64 * cap)()
+        n = C.c_int()
+        check(lib().vsl_engine_read_trace(self.h, cap, buf, C.byref(n)))
+        return [int(buf[i]) for i in range(n.value)]
+
+    def memory_stats(self):
+        w, kv, o = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        check(lib().vsl_engine_memory_stats(self.h, C.byref(w), C.byref(kv), C.byref(o)))
+        return dict(weights=w.value, kv=kv.value, other=o.value)
 
     def device_status(self) -> int:
         s = C.c_int()
