@@ -89,6 +89,22 @@ VSL_API int vsl_rmsnorm(const float* x, const float* w, int B, int d, float eps,
 VSL_API int vsl_gemv(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
              const float* norm_w, float eps, void* stream);
 
+/* Batched projection on the tcgen05 tensor cores for 1 <= B <= 64 activation rows (the
+ * skinny-GEMM form of vsl_gemv for batched decode: every weight tile is read from HBM once
+ * for all B rows; same projection sites as vsl_gemv). W is fp16 or bf16 with N >= 128,
+ * K >= 64 and K % 8 == 0; x, y, norm_w, eps and epilogue mean what they mean for vsl_gemv.
+ * The fp32 activations enter the tensor cores as a hi + lo pair of 16-bit values, so results
+ * match the fp32-activation GEMV to ~1e-6 relative (fp16) / ~2e-5 (bf16).
+ * workspace: caller-owned device memory of vsl_skinny_gemm_tc_workspace_size bytes, 1 KB
+ * aligned, zero-filled before its first use (the kernel leaves its arrival counters, kept at
+ * the tail of the workspace, zero again). Calls of different shapes may share a workspace
+ * sized with the largest N, K and B together; calls that share one must be ordered on one
+ * stream. Two launches on `stream`. */
+VSL_API int vsl_skinny_gemm_tc_workspace_size(int N, int K, int B, size_t* bytes);
+VSL_API int vsl_skinny_gemm_tc(int wdtype, const void* W, int N, int K, const float* x, int B, float* y,
+                               int epilogue, const float* norm_w, float eps, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Fused QKV projection + RoPE + KV-cache append (replaces attention.comp:63-108 and the CPU
  * append KVCacheEntry::append_kv, VulkanSymbioteEngine.cpp:41-54). Wqkv rows are
  * [Wq (n_heads*hd); Wk (n_kv*hd); Wv (n_kv*hd)] over K = d_model inputs. x is the fp32

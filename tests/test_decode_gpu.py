@@ -99,6 +99,22 @@ def test_8b_shape_bf16_gqa_batch_prefilled_kv():
     _check_half(_teacher_forced(cfg, seed=33, n_steps=4, batch=4, prefill=700))
 
 
+def test_8b_shape_bf16_batch16_tensor_cores():
+    """Batch 16 takes the tcgen05 route for every projection (two launches each)."""
+    cfg = dict(n_layers=2, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+               rope_theta=500000.0, rms_eps=1e-5, wdtype=vsl.BF16)
+    with vsl.Engine.synthetic(cfg, seed=2, max_batch=16, max_seq=64) as e:
+        kernels, _ = e.step_stats(16)
+        assert kernels == 1 + 2 * (2 + 1 + 2 + 2 + 2) + 2 + 1
+    _check_half(_teacher_forced(cfg, seed=35, n_steps=3, batch=16, prefill=300))
+
+
+def test_fp16_batch8_tensor_cores_generate():
+    cfg = dict(n_layers=3, d_model=1024, n_heads=8, n_kv_heads=8, head_dim=128, ffn=2816, vocab=6000,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    _check_half(_teacher_forced(cfg, seed=36, n_steps=10, batch=8))
+
+
 def test_graph_pdl_and_eager_agree_bitwise():
     cfg = dict(n_layers=3, d_model=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1376, vocab=4000,
                rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)

@@ -130,6 +130,7 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(kv_);
     cudaFree(act_);
     cudaFree(fd_ws_);
+    cudaFree(tc_ws_);
     cudaFreeHost(h_ids_);
     cudaFreeHost(h_out_);
     cudaFreeHost(h_logits_);
@@ -225,6 +226,19 @@ int DecodeEngine::alloc_buffers() {
                                        &fd_ws_bytes_));
     CK(cudaMalloc(&fd_ws_, fd_ws_bytes_));
     CK(cudaMemset(fd_ws_, 0, fd_ws_bytes_));
+
+    // batched projections (5..64 rows, 16-bit weights) run on the tensor cores: one workspace
+    // sized for the largest projection of the model
+    if (es_ == 2 && opt_.max_batch >= TC_MIN_BATCH) {
+        const int tb = std::min(opt_.max_batch, 64);
+        const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
+        const int k_max = std::max({c.d_model, nh_l_ * c.head_dim, ff_l_});
+        tc_ws_bytes_ = tc_workspace_bytes(n_max, k_max, tb) + 1024;
+        CK(cudaMalloc(&tc_ws_, tc_ws_bytes_));
+        CK(cudaMemset(tc_ws_, 0, tc_ws_bytes_));
+        char* base = reinterpret_cast<char*>(((uintptr_t)tc_ws_ + 1023) & ~(uintptr_t)1023);
+        tc_route_ = TcRoute{base, tc_ws_bytes_ - 1024, TC_MIN_BATCH, status_};
+    }
 
     CK(cudaMallocHost((void**)&h_ids_, mb * 4));
     CK(cudaMallocHost((void**)&h_out_, mb * 4));
@@ -562,6 +576,7 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(status_, 0, 4, stream_));
     CK(cudaMemsetAsync(fs_bar_, 0, 16, stream_));
     CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
+    if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     CK(cudaStreamSynchronize(stream_));
     std::fill(pos_host_.begin(), pos_host_.end(), 0);
     steps_host_ = 0;
@@ -631,6 +646,7 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     const int d = c.d_model, hd = c.head_dim;
     const int res_epi = opt_.tp_rank == 0 ? VSL_EPI_ADD : VSL_EPI_STORE;  // partial sums reduced into x
     cudaStream_t st = stream_;
+    const TcRoute* tcr = tc_ws_ ? &tc_route_ : nullptr;
     // L2 prefetch hints: each kernel requests the head of the next projection's weights so
     // that the weight stream does not stall at kernel boundaries; the attention kernel
     // (which reads little from HBM) prefetches the whole output projection.
@@ -644,20 +660,20 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
         const bool last = l + 1 == c.n_layers;
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, x_, L.attn_norm, c.rms_eps, B, pos_,
                                   rope_cos_, rope_sin_, q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_,
-                                  page_size_, status_, st, L.wo, H(wo_b)));
+                                  page_size_, status_, st, L.wo, H(wo_b), tcr));
         RC(flash_decode_impl(q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_, page_size_, pos_, B, nh_l_,
                              nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st, L.wo,
                              head ? wo_b : 0));
-        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
         RC(allreduce_x(B));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, x_, B, act_ffn_, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
-                     H(wd_b), st));
+                     H(wd_b), st, tcr));
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, act_ffn_, B, x_, res_epi, nullptr, 0.0f,
-                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st));
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st, tcr));
         RC(allreduce_x(B));
     }
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
-                    seed, step_, layers_[0].wqkv, H(qkv_b), st));
+                    seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr));
     if (nccl_) {
         ncclResult_t r = ncclAllReduce(slots_, slots_, (size_t)B, ncclUint64, ncclMax, (ncclComm_t)nccl_, st);
         if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));
@@ -828,8 +844,11 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
     if (kernels && fused_supported(B)) {
         *kernels = 1;
     } else if (kernels) {
-        // GEMV launches cover at most 4 activation rows (fewer when K is large), see gemv.cu
+        // GEMV launches cover at most 4 activation rows (fewer when K is large), see gemv.cu;
+        // batches on the tensor-core route take two launches per projection (split + GEMM)
+        const bool tc = tc_ws_ && B >= TC_MIN_BATCH && B <= 64;
         auto chunks = [&](int K) {
+            if (tc) return 2;
             int cmax = (int)std::min<size_t>(4, (200 * 1024) / ((size_t)K * 4));
             return (B + cmax - 1) / cmax;
         };

@@ -18,6 +18,7 @@
 
 #include "../../../include/vk_symbiote/GGUFLoader.h"
 #include "../../../include/vk_symbiote/NomadPack.h"
+#include "kernels.h"
 #include "../../../include/vsl.h"
 #include "../kernels/fused_step.h"
 
@@ -62,7 +63,7 @@ public:
     int max_seq() const { return opt_.max_seq; }
     size_t arena_bytes() const { return arena_bytes_; }
     size_t kv_bytes() const { return kv_bytes_; }
-    size_t other_bytes() const { return act_bytes_ + fd_ws_bytes_; }
+    size_t other_bytes() const { return act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_; }
     vk_symbiote::PackResidency residency() const { return residency_; }
 
 private:
@@ -101,6 +102,9 @@ private:
     size_t act_bytes_ = 0;
     void* fd_ws_ = nullptr;
     size_t fd_ws_bytes_ = 0;
+    void* tc_ws_ = nullptr;  // tensor-core route of batched projections (batch >= 5, 16-bit weights)
+    size_t tc_ws_bytes_ = 0;
+    TcRoute tc_route_ = {};
 
     void* tok_embd_ = nullptr;
     void* lm_head_ = nullptr;

@@ -5,18 +5,32 @@
 
 namespace vsl {
 
+// Engine-owned route of batched projections onto the tensor cores (kernels/tc_gemm.cu):
+// a workspace of tc_workspace_bytes for the largest projection and batch, zero-filled once.
+struct TcRoute {
+    void* ws;
+    size_t bytes;
+    int min_batch;  // projections with at least this many activation rows use the tensor cores
+    int* status;    // device status word for expired waits
+};
+size_t tc_workspace_bytes(int N, int K, int B);
+constexpr int TC_MIN_BATCH = 5;  // below this the GEMV streams the weights once per launch anyway
+
 int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, int B, float* x,
                unsigned long long* slots, cudaStream_t st);
 int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
                            const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
                            const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
-                           int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes);
+                           int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
+                           const TcRoute* tc = nullptr);
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
-              const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream);
+              const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
+              const TcRoute* tc = nullptr);
 int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
                  float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
-                 const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream);
+                 const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
+                 const TcRoute* tc = nullptr);
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,

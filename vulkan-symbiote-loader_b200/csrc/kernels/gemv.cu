@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "tc_gemm.h"
 #include "launch.cuh"
 
 namespace vsl {
@@ -264,9 +265,14 @@ static int check_common(int wdtype, const void* W, int N, int K, const float* x,
     return VSL_OK;
 }
 
-// Large batches are processed in chunks of 4 activation rows (each chunk re-streams W).
-static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y_cols) {
+// Large batches go to the tensor cores when the caller provides a route (every weight tile
+// read once for all rows); otherwise they are processed in chunks of 4 activation rows, each
+// chunk re-streaming W.
+static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y_cols,
+                      const TcRoute* tc = nullptr) {
     const int B = p.B;
+    if (tc && tc->ws && B >= tc->min_batch && tc_supported(wdtype, p.N, p.K, B))
+        return tc_project(wdtype, kind, p, tc->ws, tc->bytes, tc->status ? tc->status : p.status, st);
     // activation rows per launch: at most 4, and at most what fits beside the weight ring
     const int cmax = max_rows_per_launch(p.K);
     if (cmax < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d exceeds the shared-memory staging limit", p.K);
@@ -338,33 +344,36 @@ extern "C" int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, in
 // L2 prefetch hint for the weights of the next kernel in the decode step.
 namespace vsl {
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
-              const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream) {
+              const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
+              const TcRoute* tc) {
     int rc = check_common(wdtype, W, N, K, x, B);
     if (rc) return rc;
     GemvParams p = {};
     p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
     int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
-    return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N);
+    return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N, tc);
 }
 
 int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
                  float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
-                 const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream) {
+                 const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
+                 const TcRoute* tc) {
     GemvParams p = {};
     p.W = W; p.N = V_local; p.K = K; p.x = x; p.B = B; p.y = logits; p.norm_w = norm_w; p.eps = eps;
     p.slots = slots; p.vocab_offset = vocab_offset;
     p.inv_temp = temperature > 0.0f ? 1.0f / temperature : 0.0f;
     p.seed = seed; p.step_counter = step_counter;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
-    return run_chunks(wdtype, EK_LMHEAD, p, stream, V_local);
+    return run_chunks(wdtype, EK_LMHEAD, p, stream, V_local, tc);
 }
 
 int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, int head_dim, int K,
                            const float* x, const float* norm_w, float eps, int B, const int32_t* pos,
                            const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
-                           int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes) {
+                           int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
+                           const TcRoute* tc) {
     GemvParams p = {};
     p.W = Wqkv; p.N = (n_heads + 2 * n_kv) * head_dim; p.K = K; p.x = x; p.B = B; p.norm_w = norm_w; p.eps = eps;
     p.n_heads = n_heads; p.n_kv = n_kv; p.head_dim = head_dim; p.pos = pos;
@@ -372,7 +381,7 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
     p.kvdtype = kvdtype; p.page_table = page_table; p.max_pages = max_pages; p.page_size = page_size;
     p.status = status;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
-    return run_chunks(wdtype, EK_QKV, p, stream, 0);
+    return run_chunks(wdtype, EK_QKV, p, stream, 0, tc);
 }
 }  // namespace vsl
 

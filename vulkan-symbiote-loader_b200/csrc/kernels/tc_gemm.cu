@@ -1,0 +1,651 @@
+// Batched decode projections on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// For batch sizes where a projection y = x·Wᵀ stops being a pure weight stream (B > 4 rows
+// of activations), the GEMV kernels would re-stream W once per 4 rows. Here every weight
+// tile is read from HBM once and multiplied against all B rows on the tensor cores:
+//   D[128 rows of W][2·Bp] = W_tile[128][K] · X2[2·Bp][K]ᵀ        (kind::f16, fp32 accumulate)
+// tcgen05 wants both operands in the same 16-bit type, so the fp32 activations are split
+// once per projection into x = hi + lo with hi = rn(x), lo = rn(x - hi) in the weight's type
+// (X2 = [hi rows; lo rows]); the epilogue adds the two accumulator columns of each row. The
+// products of 16-bit values are exact in fp32, so the result matches an fp32-activation GEMV
+// to within the ~2^-22 (fp16) / 2^-16 (bf16) relative size of the dropped remainder.
+//
+// CTA roles (192 threads, one CTA per SM, persistent over a stream-K share of the work):
+//   warp 0     TMA producer: W tile (128 x 64, 128-byte swizzle) and X2 tile (2Bp x 64) per
+//              k-block into a ring of shared-memory stages (mbarrier complete_tx);
+//   warp 1     allocates the TMEM accumulator (2Bp fp32 columns x 128 lanes) and one lane
+//              issues tcgen05.mma (M=128, N=2Bp, K=16; 4 per k-block), committing each stage
+//              back to the producer and each finished segment to the epilogue;
+//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (= rows), hi + lo, then either the
+//              projection epilogue directly (a segment that covers all of K) or a partial to
+//              the workspace; the last CTA to finish a split row tile sums the partials in a
+//              fixed order (deterministic) and runs the epilogue.
+// Work split (stream-K): the flattened sequence of (row tile, k-block) pairs is cut into
+// gridDim.x equal ranges, one per CTA, so every SM streams the same number of weight bytes.
+// Every wait is bounded (one second); on expiry the kernel records VSL_ERR_TIMEOUT, lets its
+// copies and MMAs drain (bounded again), frees its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "epilogue.cuh"
+#include "launch.cuh"
+#include "tc_gemm.h"
+
+namespace vsl {
+
+constexpr int TC_THREADS = 192;
+constexpr int TC_BM = 128;            // rows of W per tile (MMA M)
+constexpr int TC_ATOM = 64;           // k per 128-byte swizzle atom of 16-bit values
+constexpr int TC_KA = 2;              // atoms per stage
+constexpr int TC_BK = TC_ATOM * TC_KA;           // k per stage (one k-block)
+constexpr int TC_A_ATOM = TC_BM * TC_ATOM * 2;   // 16 KB
+constexpr int TC_A_BYTES = TC_A_ATOM * TC_KA;    // 32 KB of weights per stage
+constexpr int TC_MAX_STAGES = 12;
+constexpr int TC_SMEM_BUDGET = 200 * 1024;     // ring bytes (+1 KB alignment slack)
+
+struct TcArgs {
+    int N, K, B, Bp;     // rows, inner dimension, batch, batch padded to a multiple of 8
+    int n_rt, nkb;       // row tiles, k-blocks
+    long long T;         // n_rt * nkb
+    int stages, stage_bytes, b_atom, b_bytes;  // X2 bytes per atom and per stage
+    uint32_t idesc;      // tcgen05 instruction descriptor
+    int tmem_cols;
+    float* ws;           // [gridDim.x][2][Bp][128] split-tile partials
+    int* counters;       // [n_rt] arrivals per split row tile (zero between launches)
+    int* status;         // VSL_ERR_TIMEOUT on an expired wait (nullable)
+    GemvParams ep;       // epilogue parameters (y, residual, RoPE/KV, sampler)
+};
+
+// ---------------------------------------------------------------------------------------
+// PTX wrappers (tcgen05, tensor TMA)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tmap_prefetch(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ int ld_abort(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major tile in the canonical 128-byte-swizzle layout
+// (8-row x 128-byte atoms, 1024 bytes apart): start address >> 4 in bits 0-13, leading byte
+// offset (unused for this layout, 16) in 16-29, stride byte offset 1024 in 32-45, descriptor
+// version 1 in 46-47, swizzle mode 2 (128 B) in 61-63. The tile base is 1024-byte aligned.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(16 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on `bar` once every tcgen05.mma issued so far by this thread has completed
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 16 consecutive fp32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ---------------------------------------------------------------------------------------
+// stream-K partition: CTA c owns flat k-blocks [lo(c), lo(c+1)), lo(c) = c*T/G
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ long long sk_lo(long long T, int G, int c) { return T * c / G; }
+// CTA whose range holds flat k-block f
+__device__ __forceinline__ int sk_owner(long long T, int G, long long f) { return (int)(((f + 1) * G - 1) / T); }
+
+struct Segment {
+    int rt, kb0, kb1;
+    bool full;   // covers all k-blocks of the row tile
+    int slot;    // workspace slot of a split segment: 0 = first of this CTA, 1 = last
+};
+
+__device__ __forceinline__ bool next_segment(const TcArgs& a, long long& f, long long f1, long long f0, Segment& s) {
+    if (f >= f1) return false;
+    s.rt = (int)(f / a.nkb);
+    s.kb0 = (int)(f - (long long)s.rt * a.nkb);
+    const long long rem = f1 - f;
+    s.kb1 = (long long)(a.nkb - s.kb0) < rem ? a.nkb : s.kb0 + (int)rem;
+    s.full = s.kb0 == 0 && s.kb1 == a.nkb;
+    s.slot = f == f0 ? 0 : 1;
+    f += s.kb1 - s.kb0;
+    return true;
+}
+
+// ---------------------------------------------------------------------------------------
+// activation split: X2[b] = rn(xn), X2[Bp + b] = rn(xn - X2[b]), xn = RMSNorm(x[b]) or x[b]
+// ---------------------------------------------------------------------------------------
+template <typename WT>
+__global__ void __launch_bounds__(256) xsplit_kernel(const float* __restrict__ x, int K, const float* __restrict__ nw,
+                                                     float eps, int Bp, WT* __restrict__ x2) {
+    __shared__ float red[8];
+    const int b = blockIdx.x;
+    pdl_wait();
+    pdl_launch_dependents();
+    const float* xr = x + (size_t)b * K;
+    float den = 1.0f;
+    if (nw) {
+        float ss = 0.0f;
+        for (int k = threadIdx.x; k < K; k += 256) ss += xr[k] * xr[k];
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) s += red[w];
+        den = sqrtf(s / (float)K + eps);  // rms_norm.comp:32-34: x / sqrt(var) * w
+    }
+    WT* hi = x2 + (size_t)b * K;
+    WT* lo = x2 + (size_t)(Bp + b) * K;
+    for (int k = threadIdx.x; k < K; k += 256) {
+        const float v = nw ? xr[k] / den * nw[k] : xr[k];
+        WT h, l;
+        if constexpr (std::is_same<WT, __half>::value) {
+            h = __float2half_rn(v);
+            l = __float2half_rn(v - __half2float(h));
+        } else {
+            h = __float2bfloat16_rn(v);
+            l = __float2bfloat16_rn(v - __bfloat162float(h));
+        }
+        hi[k] = h;
+        lo[k] = l;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// the GEMM
+// ---------------------------------------------------------------------------------------
+// Epilogue of up to TC_EB activation rows b0.. for this thread's weight row: v[j] is the
+// finished sum for row `row`, sequence b0 + j. Rows pair up within a warp (lane parity = row
+// parity) and the even lane runs the pair. All global inputs of the chunk (residuals, positions,
+// RoPE terms) are requested before any is used, so the chunk costs one memory round trip.
+constexpr int TC_EB = 16;
+
+template <int EK>
+__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int row, const float* v, int step) {
+    const int lane = threadIdx.x & 31;
+    float v1[TC_EB];
+#pragma unroll
+    for (int j = 0; j < TC_EB; j++) v1[j] = __shfl_down_sync(0xffffffffu, v[j], 1);
+    const bool act = !(lane & 1) && row < a.N;
+    const bool has1 = row + 1 < a.N;
+    const int nb = a.B - b0 < TC_EB ? a.B - b0 : TC_EB;
+    unsigned long long best[EK == EK_LMHEAD ? TC_EB : 1];
+#pragma unroll
+    for (int j = 0; j < (EK == EK_LMHEAD ? TC_EB : 1); j++) best[j] = 0ull;
+    if (act) {
+        EpiPre pre[TC_EB];
+#pragma unroll
+        for (int j = 0; j < TC_EB; j++) {
+            if (j < nb) {
+                int pos = 0, page = 0;
+                if (EK == EK_QKV) epi_pos_page(a.ep, b0 + j, pos, page);
+                pre[j] = epi_fetch<EK>(a.ep, b0 + j, row, has1, pos, page);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < TC_EB; j++) {
+            if (j < nb) {
+                unsigned long long bb = 0ull;
+                epi_apply<EK>(a.ep, pre[j], b0 + j, row, row >> 1, has1, v[j], v1[j], bb, step);
+                if (EK == EK_LMHEAD) best[EK == EK_LMHEAD ? j : 0] = bb;
+            }
+        }
+    }
+    if (EK == EK_LMHEAD) {
+#pragma unroll
+        for (int j = 0; j < TC_EB; j++) {
+            unsigned long long bb = best[EK == EK_LMHEAD ? j : 0];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, bb, o);
+                bb = t > bb ? t : bb;
+            }
+            if (lane == 0 && bb && j < nb) atomicMax(a.ep.slots + b0 + j, bb);
+        }
+    }
+}
+
+template <int EK>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                   const __grid_constant__ TcArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t full[TC_MAX_STAGES], empty[TC_MAX_STAGES];
+    __shared__ __align__(8) uint64_t tmem_full, tmem_empty;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+    __shared__ int last_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t ring = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long f0 = sk_lo(a.T, G, c), f1 = sk_lo(a.T, G, c + 1);
+    const int S = a.stages;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&tmem_full, 1);
+        mbar_init(&tmem_empty, 4);
+        mbar_fence_init();
+        abort_s = 0;
+        tmap_prefetch(&map_w);
+        tmap_prefetch(&map_x);
+    }
+    if (warp == 1) {  // TMEM accumulator: 128 lanes x tmem_cols fp32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                     "r"(a.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 0) {
+        // ================= producer =================
+        if (lane == 0) {
+            const uint32_t tx = (uint32_t)(TC_A_BYTES + a.b_bytes);
+            long long it = 0;
+            // weights do not depend on the previous kernel: the first stages' W tiles are
+            // requested before griddepcontrol.wait, their X2 tiles after it
+            long long f = f0;
+            Segment sg;
+            int pre = 0;
+            {
+                long long g = f0;
+                Segment s2;
+                while (pre < S && next_segment(a, g, f1, f0, s2))
+                    for (int kb = s2.kb0; kb < s2.kb1 && pre < S; kb++, pre++) {
+                        mbar_arrive_expect_tx(&full[pre], tx);
+#pragma unroll
+                        for (int at = 0; at < TC_KA; at++)
+                            tma_load_2d(ring + pre * a.stage_bytes + at * TC_A_ATOM, &map_w, kb * TC_BK + at * TC_ATOM,
+                                        s2.rt * TC_BM, &full[pre]);
+                    }
+            }
+            pdl_wait();
+            pdl_launch_dependents();
+            bool ok = true;
+            // stage index and the parity of its empty-barrier phase advance incrementally (a
+            // 64-bit division per k-block costs more issue slots than the rest of the loop)
+            int s = 0;
+            uint32_t epar = 1u;  // the first lap finds every stage free
+            while (ok && next_segment(a, f, f1, f0, sg)) {
+                for (int kb = sg.kb0; kb < sg.kb1; kb++, it++) {
+                    if (it >= pre) {
+                        if (it >= S && !mbar_wait(&empty[s], epar)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], tx);
+#pragma unroll
+                        for (int at = 0; at < TC_KA; at++)
+                            tma_load_2d(ring + s * a.stage_bytes + at * TC_A_ATOM, &map_w, kb * TC_BK + at * TC_ATOM,
+                                        sg.rt * TC_BM, &full[s]);
+                    }
+#pragma unroll
+                    for (int at = 0; at < TC_KA; at++)
+                        tma_load_2d(ring + s * a.stage_bytes + TC_A_BYTES + at * a.b_atom, &map_x,
+                                    kb * TC_BK + at * TC_ATOM, 0, &full[s]);
+                    if (++s == S) {
+                        s = 0;
+                        epar ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+            }
+            // every copy issued must land before the CTA may exit
+            const long long issued = it > pre ? it : pre;
+            for (long long u = issued > S ? issued - S : 0; u < issued; u++) mbar_wait(&full[u % S], (uint32_t)((u / S) & 1));
+        }
+    } else if (warp == 1) {
+        // ================= MMA issuer =================
+        if (lane == 0) {
+            pdl_wait();
+            pdl_launch_dependents();
+            long long f = f0, it = 0;
+            int si = 0, s = 0;
+            uint32_t fpar = 0u;
+            Segment sg;
+            bool ok = true;
+            bool committed = false;
+            while (ok && next_segment(a, f, f1, f0, sg)) {
+                if (si > 0 && !mbar_wait(&tmem_empty, (uint32_t)((si - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = sg.kb0; kb < sg.kb1; kb++, it++) {
+                    if (!mbar_wait(&full[s], fpar) || (((int)it & 15) == 0 && ld_abort(&abort_s))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = ring + s * a.stage_bytes, sb = sa + TC_A_BYTES;
+#pragma unroll
+                    for (int at = 0; at < TC_KA; at++) {
+                        const uint64_t ad = sw128_desc(sa + at * TC_A_ATOM), bd = sw128_desc(sb + at * a.b_atom);
+#pragma unroll
+                        for (int k = 0; k < TC_ATOM / 16; k++)  // +32 bytes per 16 values inside the atom
+                            tc_mma(tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), a.idesc,
+                                   (kb > sg.kb0 || at > 0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
+                    if (++s == S) {
+                        s = 0;
+                        fpar ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tmem_full);
+                committed = true;
+                si++;
+            }
+            if (!ok) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+            }
+            // the accumulator must not be freed under a running MMA
+            if (committed) mbar_wait(&tmem_full, (uint32_t)((si - 1) & 1));
+        }
+        __syncwarp();
+    } else {
+        // ================= epilogue warps =================
+        pdl_wait();
+        pdl_launch_dependents();
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int rloc = q * 32 + lane;
+        const int et = threadIdx.x - 64;  // 0..127
+        int step = 0;
+        if (EK == EK_LMHEAD && a.ep.inv_temp > 0.0f) step = *a.ep.step_counter;
+        long long f = f0;
+        int si = 0;
+        Segment sg;
+        while (next_segment(a, f, f1, f0, sg)) {
+            if (!mbar_wait(&tmem_full, (uint32_t)(si & 1)) || ld_abort(&abort_s)) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+                break;
+            }
+            tc_fence_after();
+            const int row = sg.rt * TC_BM + rloc;
+            float* wsp = a.ws + ((size_t)c * 2 + sg.slot) * a.Bp * TC_BM;
+            for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
+                float hi[TC_EB], lo[TC_EB];
+                const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
+                tmem_ld16(tl + (uint32_t)b0, hi);
+                tmem_ld16(tl + (uint32_t)(a.Bp + b0), lo);
+#pragma unroll
+                for (int i = 0; i < TC_EB; i++) hi[i] += lo[i];
+                if (sg.full) {
+                    tc_epilogue_chunk<EK>(a, b0, row, hi, step);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < TC_EB; i++)
+                        if (b0 + i < a.B) wsp[(size_t)(b0 + i) * TC_BM + rloc] = hi[i];
+                }
+            }
+            // accumulator read: hand TMEM back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tmem_empty);
+            si++;
+            if (!sg.full) {
+                // split row tile: the last of its CTAs to arrive reduces, in CTA order
+                __threadfence();
+                named_barrier_sync(1, 128);
+                if (et == 0) {
+                    const int first = sk_owner(a.T, G, (long long)sg.rt * a.nkb);
+                    const int lastc = sk_owner(a.T, G, (long long)sg.rt * a.nkb + a.nkb - 1);
+                    const int prev = atomicAdd(a.counters + sg.rt, 1);
+                    last_s = prev == lastc - first ? 1 : 0;
+                }
+                named_barrier_sync(1, 128);
+                if (last_s) {
+                    __threadfence();
+                    const int first = sk_owner(a.T, G, (long long)sg.rt * a.nkb);
+                    const int lastc = sk_owner(a.T, G, (long long)sg.rt * a.nkb + a.nkb - 1);
+                    // partials of CTAs first..lastc, summed in CTA order; TC_EB rows x 4 CTAs
+                    // of loads are in flight at a time
+                    for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
+                        float v[TC_EB];
+#pragma unroll
+                        for (int j = 0; j < TC_EB; j++) v[j] = 0.0f;
+                        for (int c0 = first; c0 <= lastc; c0 += 4) {
+                            float t[4][TC_EB];
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int cc = c0 + u;
+                                if (cc <= lastc) {
+                                    const int slot = sk_lo(a.T, G, cc) >= (long long)sg.rt * a.nkb ? 0 : 1;
+                                    const float* src = a.ws + (((size_t)cc * 2 + slot) * a.Bp + b0) * TC_BM + rloc;
+#pragma unroll
+                                    for (int j = 0; j < TC_EB; j++) t[u][j] = b0 + j < a.B ? __ldcg(src + (size_t)j * TC_BM) : 0.0f;
+                                }
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; u++)
+                                if (c0 + u <= lastc)
+#pragma unroll
+                                    for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
+                        }
+                        tc_epilogue_chunk<EK>(a, b0, row, v, step);
+                    }
+                    if (et == 0) a.counters[sg.rt] = 0;
+                }
+            }
+        }
+    }
+
+    // ---- teardown: the allocating warp frees TMEM once every role is done with it ----
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols)
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D tensor map over a row-major [rows][cols] 16-bit matrix, box = box_rows x 64 columns,
+// 128-byte swizzle (the canonical K-major tcgen05 operand layout), zero fill out of bounds.
+static int make_map(CUtensorMap* m, const void* base, int wdtype, int rows, int cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return set_error(VSL_ERR_CUDA, "tensor-map encoder unavailable from the driver");
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_ATOM, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(m, wdtype == VSL_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(VSL_ERR_INVALID, "tensor map encode failed (%d) rows=%d cols=%d", (int)r, rows, cols);
+    return VSL_OK;
+}
+
+static int pad_batch(int B) { return (B + 7) / 8 * 8; }
+
+size_t tc_workspace_bytes(int N, int K, int B) {
+    const int Bp = pad_batch(B);
+    const int G = sm_count();
+    const size_t x2 = (size_t)2 * Bp * K * 2;
+    const size_t ws = (size_t)G * 2 * Bp * TC_BM * sizeof(float);
+    const size_t cnt = (size_t)((N + TC_BM - 1) / TC_BM) * sizeof(int);
+    auto up = [](size_t v) { return (v + 1023) / 1024 * 1024; };
+    return up(x2) + up(ws) + up(cnt);
+}
+
+bool tc_supported(int wdtype, int N, int K, int B) {
+    // shapes at least one tile in each direction (TMA boxes are 128 rows x 64 columns) and
+    // 16-byte row pitches (tensor-map strides)
+    return (wdtype == VSL_F16 || wdtype == VSL_BF16) && B >= 1 && B <= TC_MAX_BATCH && N >= TC_BM && K >= TC_ATOM &&
+           (K % 8) == 0;
+}
+
+template <int EK>
+static int launch_tc(const TcArgs& a, const CUtensorMap& mw, const CUtensorMap& mx, int grid, size_t smem,
+                     cudaStream_t st) {
+    auto kern = tc_gemm_kernel<EK>;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             TC_SMEM_BUDGET + 1024);
+        if (e != cudaSuccess) return launch_status(e, "tc gemm smem attribute");
+        configured_dev = dev;
+    }
+    return launch_status(launch_k(kern, dim3(grid), dim3(TC_THREADS), smem, st, mw, mx, a), "tc gemm launch");
+}
+
+int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_t ws_bytes, int* status,
+               cudaStream_t st) {
+    if (!tc_supported(wdtype, p.N, p.K, p.B))
+        return set_error(VSL_ERR_UNSUPPORTED, "tc gemm: dtype %d N=%d K=%d B=%d", wdtype, p.N, p.K, p.B);
+    if (((uintptr_t)p.W & 15) || ((uintptr_t)p.x & 15))
+        return set_error(VSL_ERR_INVALID, "tc gemm: weights and activations must be 16-byte aligned");
+    const size_t need = tc_workspace_bytes(p.N, p.K, p.B);
+    if (!workspace || ws_bytes < need || ((uintptr_t)workspace & 1023))
+        return set_error(VSL_ERR_INVALID, "tc gemm: workspace of %zu bytes (1 KB aligned) needed", need);
+
+    TcArgs a = {};
+    a.N = p.N;
+    a.K = p.K;
+    a.B = p.B;
+    a.Bp = pad_batch(p.B);
+    a.n_rt = (p.N + TC_BM - 1) / TC_BM;
+    a.nkb = (p.K + TC_BK - 1) / TC_BK;
+    a.T = (long long)a.n_rt * a.nkb;
+    const int n = 2 * a.Bp;  // MMA N (multiple of 16)
+    a.b_atom = n * TC_ATOM * 2;  // n % 16 == 0: a multiple of 2 KB, so every atom stays 1 KB aligned
+    a.b_bytes = a.b_atom * TC_KA;
+    a.stage_bytes = TC_A_BYTES + a.b_bytes;
+    a.stages = TC_SMEM_BUDGET / a.stage_bytes;
+    if (a.stages > TC_MAX_STAGES) a.stages = TC_MAX_STAGES;
+    a.tmem_cols = 32;
+    while (a.tmem_cols < n) a.tmem_cols <<= 1;
+    const uint32_t fmt = wdtype == VSL_BF16 ? 1u : 0u;
+    // instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A/B format (bits 7-9, 10-12),
+    // both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28
+    a.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+
+    unsigned char* w8 = static_cast<unsigned char*>(workspace);
+    auto up = [](size_t v) { return (v + 1023) / 1024 * 1024; };
+    void* x2 = w8;
+    const size_t x2b = up((size_t)2 * a.Bp * p.K * 2);
+    const int G0 = sm_count();
+    a.ws = reinterpret_cast<float*>(w8 + x2b);
+    // the arrival counters sit at the tail of the workspace whatever the shape of the call, so
+    // calls of different shapes sharing one workspace (sized for the largest N and K together)
+    // never write split activations or partials over another shape's counters
+    const size_t cnt_bytes = (size_t)a.n_rt * sizeof(int);
+    a.counters = reinterpret_cast<int*>(w8 + ((ws_bytes - cnt_bytes) & ~(size_t)1023));
+    a.status = status;
+    a.ep = p;
+    a.ep.status = status;
+
+    int grid = G0;
+    if ((long long)grid > a.T) grid = (int)a.T;
+
+    CUtensorMap mw, mx;
+    int rc = make_map(&mw, p.W, wdtype, p.N, p.K, TC_BM);
+    if (rc) return rc;
+    rc = make_map(&mx, x2, wdtype, n, p.K, n);
+    if (rc) return rc;
+
+    // activation split (+ RMSNorm)
+    cudaError_t e;
+    if (wdtype == VSL_BF16)
+        e = launch_k(xsplit_kernel<__nv_bfloat16>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
+                     static_cast<__nv_bfloat16*>(x2));
+    else
+        e = launch_k(xsplit_kernel<__half>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
+                     static_cast<__half*>(x2));
+    rc = launch_status(e, "tc activation split");
+    if (rc) return rc;
+
+    const size_t smem = (size_t)a.stages * a.stage_bytes + 1024;
+    switch (kind) {
+        case EK_STORE: return launch_tc<EK_STORE>(a, mw, mx, grid, smem, st);
+        case EK_ADD: return launch_tc<EK_ADD>(a, mw, mx, grid, smem, st);
+        case EK_SWIGLU: return launch_tc<EK_SWIGLU>(a, mw, mx, grid, smem, st);
+        case EK_QKV: return launch_tc<EK_QKV>(a, mw, mx, grid, smem, st);
+        default: return launch_tc<EK_LMHEAD>(a, mw, mx, grid, smem, st);
+    }
+}
+
+}  // namespace vsl
+
+using namespace vsl;
+
+extern "C" int vsl_skinny_gemm_tc_workspace_size(int N, int K, int B, size_t* bytes) {
+    if (!bytes || N <= 0 || K <= 0 || B <= 0 || B > TC_MAX_BATCH)
+        return set_error(VSL_ERR_INVALID, "tc workspace: bad shape N=%d K=%d B=%d", N, K, B);
+    *bytes = tc_workspace_bytes(N, K, B);
+    return VSL_OK;
+}
+
+extern "C" int vsl_skinny_gemm_tc(int wdtype, const void* W, int N, int K, const float* x, int B, float* y,
+                                  int epilogue, const float* norm_w, float eps, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+    if (!W || !x || !y) return set_error(VSL_ERR_INVALID, "tc gemm: null pointer");
+    if (epilogue != VSL_EPI_STORE && epilogue != VSL_EPI_ADD && epilogue != VSL_EPI_SWIGLU)
+        return set_error(VSL_ERR_INVALID, "tc gemm: unknown epilogue %d", epilogue);
+    if (epilogue == VSL_EPI_SWIGLU && (N & 1))
+        return set_error(VSL_ERR_INVALID, "tc gemm: SwiGLU needs interleaved gate/up rows (N even), N=%d", N);
+    GemvParams p = {};
+    p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
+    const int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
+    return tc_project(wdtype, kind, p, workspace, workspace_bytes, nullptr, (cudaStream_t)stream);
+}

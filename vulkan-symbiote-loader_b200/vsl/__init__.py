@@ -62,6 +62,8 @@ def lib() -> C.CDLL:
         "vsl_embed_gather": (i32, [i32, vp, i32, i32, vp, i32, vp, vp]),
         "vsl_rmsnorm": (i32, [vp, vp, i32, i32, f32, vp, vp]),
         "vsl_gemv": (i32, [i32, vp, i32, i32, vp, i32, vp, i32, vp, f32, vp]),
+        "vsl_skinny_gemm_tc_workspace_size": (i32, [i32, i32, i32, C.POINTER(sz)]),
+        "vsl_skinny_gemm_tc": (i32, [i32, vp, i32, i32, vp, i32, vp, i32, vp, f32, vp, sz, vp]),
         "vsl_qkv_rope_append": (i32, [i32, vp, i32, i32, i32, i32, vp, vp, f32, i32, vp, vp, vp, vp, vp, vp, i32, vp,
                                       i32, i32, vp]),
         "vsl_flash_decode_workspace_size": (i32, [i32, i32, i32, i32, i32, i32, C.POINTER(sz)]),
@@ -140,6 +142,18 @@ def rmsnorm(x, w, B, d, eps, y, stream=0):
 
 def gemv(wdtype, W, N, K, x, B, y, epilogue=EPI_STORE, norm_w=None, eps=0.0, stream=0):
     check(lib().vsl_gemv(wdtype, _ptr(W), N, K, _ptr(x), B, _ptr(y), epilogue, _ptr(norm_w), eps, stream))
+
+
+def skinny_gemm_tc_workspace_size(N, K, B) -> int:
+    out = C.c_size_t()
+    check(lib().vsl_skinny_gemm_tc_workspace_size(N, K, B, C.byref(out)))
+    return out.value
+
+
+def skinny_gemm_tc(wdtype, W, N, K, x, B, y, epilogue=EPI_STORE, norm_w=None, eps=0.0, workspace=None,
+                   workspace_bytes=0, stream=0):
+    check(lib().vsl_skinny_gemm_tc(wdtype, _ptr(W), N, K, _ptr(x), B, _ptr(y), epilogue, _ptr(norm_w), eps,
+                                   _ptr(workspace), workspace_bytes, stream))
 
 
 def qkv_rope_append(wdtype, Wqkv, n_heads, n_kv, head_dim, K, x, norm_w, eps, B, pos, rope_cos, rope_sin, q_out,
