@@ -33,6 +33,9 @@ sys.path.insert(0, os.path.join(ROOT, "vulkan-symbiote-loader_b200"))
 
 CONFIG_7B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
                  rope_theta=10000.0, rms_eps=1e-5, wdtype=1)
+CONFIG_8B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+                 rope_theta=500000.0, rms_eps=1e-5, wdtype=30)  # GGUF type 30 = bf16
+PREFILL_8B, BATCH_8B = 8192, 16
 PROMPT = 128
 SEED = 1
 SIGMA = 0.02
@@ -47,6 +50,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--workload", default="7b", choices=["7b", "8b"],
+                    help="7b: the headline (BASELINE configs[1]); 8b: BASELINE configs[3], batch 16 over "
+                         "8192 prefilled KV positions each (bf16, GQA, tensor-core projections)")
     ap.add_argument("--sweep", action="store_true",
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     return ap.parse_args()
@@ -228,42 +234,52 @@ def run_ours(args):
     ws, rank, local = vdist.env()
     dist = vdist.init(ws)
     torch.cuda.set_device(local)
-    cfg = dict(CONFIG_7B)
+    big = args.workload == "8b"
+    cfg = dict(CONFIG_8B if big else CONFIG_7B)
     if args.layers:
         cfg["n_layers"] = args.layers
-    max_seq = PROMPT + args.warmup + 2 * args.steps + 8
+    B = BATCH_8B if big else 1
+    start = PREFILL_8B if big else PROMPT
+    max_seq = start + args.warmup + 2 * args.steps + 8
     max_seq = (max_seq + 63) // 64 * 64
     nccl_id = vdist.nccl_id(dist)
     t0 = time.perf_counter()
-    eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=1, max_seq=max_seq,
+    eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=B, max_seq=max_seq,
                                tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
     load_s = time.perf_counter() - t0
-    prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
-    eng.set_forced(prompt)
-    eng.run(PROMPT)  # prompt positions 0..127 (token-by-token prefill through the decode graph)
-    eng.run(args.warmup)
+    if big:
+        # 8192 positions of seeded N(0, 1) keys/values per sequence written straight into the
+        # paged cache (no prefill pass), then greedy decode from one seeded id per sequence
+        eng.fill_kv_synthetic(SEED + 100, 1.0, PREFILL_8B, B)
+        eng.set_forced(synth.synth_ids(SEED, 0, B, cfg["vocab"]).reshape(1, B))
+        eng.run(1, batch=B)
+    else:
+        prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
+        eng.set_forced(prompt)
+        eng.run(PROMPT)  # prompt positions 0..127 (token-by-token prefill through the decode graph)
+    eng.run(args.warmup, batch=B)
     stream = eng.stream
     s = torch.cuda.ExternalStream(stream)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    kernels, bytes_start = eng.step_stats(1)
+    kernels, bytes_start = eng.step_stats(B)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         e0.record(s)
-        eng.run(args.steps)
+        eng.run(args.steps, batch=B)
         e1.record(s)
         torch.cuda.synchronize()
     if dist:
         dist.barrier()
     ms = e0.elapsed_time(e1)
     ms = vdist.max_over_ranks(dist, ms)
-    _, bytes_end = eng.step_stats(1)
+    _, bytes_end = eng.step_stats(B)
     status = eng.device_status()
-    # end to end through the host API: pinned host id in, sampled id back, every step
-    toks = eng.read_tokens(PROMPT + args.warmup + args.steps)[-1:, 0]
-    nxt = np.array([int(toks[-1])], np.int32)
+    # end to end through the host API: pinned host ids in, sampled ids back, every step
+    n_log = (1 if big else PROMPT) + args.warmup + args.steps
+    nxt = np.asarray(eng.read_tokens(n_log, batch=B)[-1], np.int32).reshape(B)
     for _ in range(2):
         nxt, _ = eng.step_host(nxt)
     if dist:
@@ -277,15 +293,38 @@ def run_ours(args):
     if status != 0 or eng.device_status() != 0:
         raise SystemExit(f"device status {status}")
     hbm_peak, peak_kind = peaks()
-    roof = dominant_kernel_roofline(torch, vsl, cfg, ws, hbm_peak, peak_kind)
+    roof = None if big else dominant_kernel_roofline(torch, vsl, cfg, ws, hbm_peak, peak_kind)
     eng.close()
-    tok_s = args.steps / (ms / 1e3)
+    tok_s = args.steps * B / (ms / 1e3)
     step_bytes = 0.5 * (bytes_start + bytes_end)  # per GPU; KV grows by one position per step
     step_gbs = step_bytes / (ms / 1e3 / args.steps) / 1e9
     cb = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not big:
         cb = cpu_baseline(cfg, args.cpu_seconds)
-    if rank == 0:
+    if rank == 0 and big:
+        step_roof = {"bound": "hbm", "kernel": "whole decode step (weights + 16 x 8192-position KV)",
+                     "achieved": round(step_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(step_gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                     "bytes_per_step_per_gpu": round(step_bytes), "traffic": None}
+        line = {
+            "metric": "decode tok/s (8B bf16 GQA, bs16, 8192-position KV)", "value": round(tok_s, 3),
+            "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights and KV in HBM)",
+            "config": {"workload": "8B Llama-3 shape bf16 (BASELINE configs[3]), 16 sequences x 8192 prefilled "
+                                   "fp16 KV positions, greedy decode",
+                       "model": "llama-3-8b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
+                       "global_batch": B, "seq_len": start + args.warmup + args.steps,
+                       "parallelism": f"tp{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (15 GB weights + 17 GB KV per step)"},
+            "e2e": {"value": round(n_e2e * B / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
+                    "d2h_bytes_per_step": 4 * B, "api": "vsl_engine_step_host"},
+            "roofline": step_roof,
+            "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
+            "clocks": clk.summary(), "load_seconds": round(load_s, 2),
+        }
+        print(json.dumps(line), flush=True)
+    elif rank == 0:
         line = {
             "metric": "decode tok/s (7B fp16, bs1)", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
@@ -333,24 +372,46 @@ def run_sweep(args):
         for B in (1, 4, 16, 64):
             x = torch.randn((B, K), device="cuda").half().float()
             y = torch.empty((B, N), device="cuda")
+            tc = B >= 5  # the engine's route: GEMV up to 4 rows, tcgen05 tensor cores above
+            if tc:
+                nws = vsl.skinny_gemm_tc_workspace_size(N, K, B)
+                wst = torch.zeros(nws // 4 + 512, dtype=torch.int32, device="cuda")
+                wsp = (wst.data_ptr() + 1023) // 1024 * 1024
             s = torch.cuda.Stream()
+
+            def call(i):
+                if tc:
+                    vsl.skinny_gemm_tc(vsl.F16, W[i % copies], N, K, x, B, y, vsl.EPI_STORE, None, 0.0, wsp, nws,
+                                       s.cuda_stream)
+                else:
+                    vsl.gemv(vsl.F16, W[i % copies], N, K, x, B, y, stream=s.cuda_stream)
+            # captured in a CUDA graph (as in the engine), so host launch cost is not timed
+            reps = max(20, 4 * copies)
+            g = torch.cuda.CUDAGraph()
             with torch.cuda.stream(s):
                 for i in range(2 * copies):
-                    vsl.gemv(vsl.F16, W[i % copies], N, K, x, B, y, stream=s.cuda_stream)
-                reps = max(20, 4 * copies)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(s)
-                for i in range(reps):
-                    vsl.gemv(vsl.F16, W[i % copies], N, K, x, B, y, stream=s.cuda_stream)
-                e1.record(s)
+                    call(i)
+                s.synchronize()
+                with torch.cuda.graph(g, stream=s):
+                    for i in range(reps):
+                        call(i)
+            g.replay()
             torch.cuda.synchronize()
+            cur = torch.cuda.current_stream()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            g.replay()
+            e1.record(cur)
+            torch.cuda.synchronize()
+            del g
             us = e0.elapsed_time(e1) * 1e3 / reps
             algo = 2 * N * K + 2 * B * K + 2 * B * N
             gbs = algo / (us * 1e-6) / 1e9
             print(json.dumps({"sweep": "projection", "N": N, "K": K, "B": B, "us": round(us, 3),
                               "GB/s": round(gbs, 1), "frac_of_hbm": round(gbs / hbm_peak, 4), "peak": hbm_peak,
                               "peak_kind": peak_kind, "TFLOP/s": round(2 * B * N * K / (us * 1e-6) / 1e12, 2),
-                              "launches_per_call": -(-B // 4)}), flush=True)
+                              "path": "tcgen05" if tc else "gemv",
+                              "launches_per_call": 2 if tc else -(-B // 4)}), flush=True)
         del W
         torch.cuda.empty_cache()
     return 0
