@@ -39,11 +39,26 @@ struct PackMetadata {
 
 // Residency plan of the engine's weights (what NomadPackManager decided at load time).
 struct PackResidency {
-    uint32 resident_layers = 0;   // layers kept in HBM
+    uint32 resident_layers = 0;   // layers kept in HBM (layers 0 .. resident_layers-1)
     uint32 streamed_layers = 0;   // layers copied from pinned host memory every step
-    uint64 resident_bytes = 0;
+    uint64 resident_bytes = 0;    // HBM for weights: resident layers, embeddings, lm_head, slots
     uint64 streamed_bytes_per_step = 0;
-    uint64 slot_bytes = 0;        // size of one streaming slot (the largest layer)
+    uint64 slot_bytes = 0;        // size of one streaming slot (one layer), 0 when nothing streams
+    bool feasible = true;         // false: the budget cannot hold the fixed part and two slots
+};
+
+// Decides which decoder layers stay in HBM (replaces the prefetch/evict policy of the
+// reference's PackManager, NomadPack.cpp:1190-1249, and the engine's schedule_prefetch /
+// evict_low_priority, VulkanSymbioteEngine.cpp:1555-1599). Decode visits every layer once per
+// token in order, so recency/frequency scores carry no information here: the plan keeps the
+// first layers resident, and the others stream through two rotating HBM slots, each copy
+// overlapping the compute of the layer before it.
+class VSL_CPP_API NomadPackManager {
+public:
+    // layer_bytes: one decoder layer's weights; fixed_bytes: everything else that must live in
+    // HBM (KV cache, activations, workspaces, embeddings, lm_head, final norm); budget_bytes:
+    // the cap (0 = none). Streaming engages only when the whole model does not fit.
+    static PackResidency plan(uint64 layer_bytes, uint32 n_layers, uint64 fixed_bytes, uint64 budget_bytes);
 };
 
 }  // namespace vk_symbiote

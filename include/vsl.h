@@ -277,6 +277,21 @@ VSL_API int vsl_engine_step_stats(vsl_engine* e, int B, int* kernels_per_step, d
  * else (activations, token log, attention workspace). Feeds get_vram_stats(). */
 VSL_API int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t* kv_bytes, size_t* other_bytes);
 
+/* Weight residency under vram_budget_gb (replaces PackManager::get_vram_stats and the pack
+ * scheduler's state, NomadPack.cpp:1190-1249, 1323-1326; VulkanSymbioteEngine.cpp:1555-1599):
+ * layers 0..resident_layers-1 stay in HBM, the other streamed_layers live in pinned host memory
+ * and are copied into two rotating HBM slots every step (streamed_bytes_per_step over the host
+ * link). Without a budget, or when the model fits, streamed_layers is 0. */
+VSL_API int vsl_engine_residency(vsl_engine* e, uint32_t* resident_layers, uint32_t* streamed_layers,
+                                 uint64_t* streamed_bytes_per_step, uint64_t* host_bytes);
+
+/* The residency plan itself (pure host arithmetic, what the engine applies at creation):
+ * layer_bytes per decoder layer, n_layers, fixed_bytes that must stay in HBM (KV cache,
+ * activations, workspaces, embeddings, lm_head), budget_gb (0 = no cap). Returns
+ * VSL_ERR_OOM when the budget cannot hold the fixed part plus two layer slots. */
+VSL_API int vsl_pack_plan(uint64_t layer_bytes, uint32_t n_layers, uint64_t fixed_bytes, double budget_gb,
+                          uint32_t* resident_layers, uint32_t* streamed_layers);
+
 /* Per-phase trace of the fused decode step (one persistent kernel per token): when on, CTA 0
  * records %globaltimer (ns) at kernel start and after each phase barrier of every step;
  * vsl_engine_read_trace copies the last step's stamps (embedding, then per layer QKV,

@@ -227,6 +227,29 @@ extern "C" int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size
     return VSL_OK;
 }
 
+extern "C" int vsl_engine_residency(vsl_engine* e, uint32_t* resident_layers, uint32_t* streamed_layers,
+                                    uint64_t* streamed_bytes_per_step, uint64_t* host_bytes) {
+    if (int rc = check_engine(e)) return rc;
+    const vk_symbiote::PackResidency r = e->impl->residency();
+    if (resident_layers) *resident_layers = r.resident_layers;
+    if (streamed_layers) *streamed_layers = r.streamed_layers;
+    if (streamed_bytes_per_step) *streamed_bytes_per_step = r.streamed_bytes_per_step;
+    if (host_bytes) *host_bytes = r.streamed_bytes_per_step;  // one pinned copy of every streamed layer
+    return VSL_OK;
+}
+
+extern "C" int vsl_pack_plan(uint64_t layer_bytes, uint32_t n_layers, uint64_t fixed_bytes, double budget_gb,
+                             uint32_t* resident_layers, uint32_t* streamed_layers) {
+    if (!resident_layers || !streamed_layers || budget_gb < 0)
+        return set_error(VSL_ERR_INVALID, "pack_plan: null output or negative budget");
+    const vk_symbiote::PackResidency r = vk_symbiote::NomadPackManager::plan(
+        layer_bytes, n_layers, fixed_bytes, (uint64_t)(budget_gb > 0 ? budget_gb * 1e9 : 0));
+    if (!r.feasible) return set_error(VSL_ERR_OOM, "pack_plan: budget below the fixed part plus two layer slots");
+    *resident_layers = r.resident_layers;
+    *streamed_layers = r.streamed_layers;
+    return VSL_OK;
+}
+
 extern "C" int vsl_engine_set_trace(vsl_engine* e, int enable) {
     GUARD_BEGIN
     if (int rc = check_engine(e)) return rc;

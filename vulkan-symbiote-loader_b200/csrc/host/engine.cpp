@@ -8,6 +8,8 @@
 // a decode step is a single graph launch with device-resident ids and positions.
 #include "engine.h"
 
+#include <type_traits>
+
 #include <nccl.h>
 
 #include <algorithm>
@@ -131,6 +133,9 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(act_);
     cudaFree(fd_ws_);
     cudaFree(tc_ws_);
+    if (host_layers_) cudaFreeHost(host_layers_);
+    for (cudaEvent_t ev : {ev_fork_, ev_copied_[0], ev_copied_[1], ev_done_[0], ev_done_[1]})
+        if (ev) cudaEventDestroy(ev);
     cudaFreeHost(h_ids_);
     cudaFreeHost(h_out_);
     cudaFreeHost(h_logits_);
@@ -149,30 +154,7 @@ int DecodeEngine::alloc_buffers() {
     const size_t b_norm = align_up(d * 4, A);
     layer_bytes_ = b_qkv + b_wo + b_wgu + b_wd + 2 * b_norm;
     const size_t b_emb = align_up((size_t)c.vocab * d * es_, A), b_head = align_up((size_t)v_l_ * d * es_, A);
-    arena_bytes_ = layer_bytes_ * c.n_layers + b_emb + b_head + b_norm;
-    if (opt_.vram_budget_gb > 0 && (double)arena_bytes_ > opt_.vram_budget_gb * 1e9)
-        return set_error(VSL_ERR_UNSUPPORTED,
-                         "engine: weights (%.2f GB) exceed the %.2f GB budget; pack streaming is not enabled in this "
-                         "build",
-                         arena_bytes_ / 1e9, opt_.vram_budget_gb);
-    CK(cudaMalloc(&arena_, arena_bytes_));
-    char* p = (char*)arena_;
     layers_.resize(c.n_layers);
-    for (int l = 0; l < c.n_layers; l++) {
-        LayerPtrs& L = layers_[l];
-        L.wqkv = p; p += b_qkv;
-        L.wo = p; p += b_wo;
-        L.wgu = p; p += b_wgu;
-        L.wd = p; p += b_wd;
-        L.attn_norm = (float*)p; p += b_norm;
-        L.ffn_norm = (float*)p; p += b_norm;
-    }
-    tok_embd_ = p; p += b_emb;
-    lm_head_ = p; p += b_head;
-    out_norm_ = (float*)p; p += b_norm;
-    residency_.resident_layers = c.n_layers;
-    residency_.resident_bytes = arena_bytes_;
-
     // paged KV cache: per layer K then V, each [n_pages][nkv_l][page][hd]
     const size_t kv_es = dtype_bytes(kvdtype_);
     const size_t b_kv_one = align_up((size_t)n_pages_ * nkv_l_ * page_size_ * hd * kv_es, A);
@@ -240,6 +222,63 @@ int DecodeEngine::alloc_buffers() {
         tc_route_ = TcRoute{base, tc_ws_bytes_ - 1024, TC_MIN_BATCH, status_};
     }
 
+
+    // ---- weights: resident layers + embeddings + lm_head in one HBM arena; when the model
+    // exceeds the HBM budget, the layers that do not fit live in pinned host memory and
+    // stream through two rotating HBM slots (NomadPackManager plan) ----
+    const size_t emb_bytes = b_emb + b_head + b_norm;
+    const size_t fixed = kv_bytes_ + act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_ + emb_bytes;
+    residency_ = vk_symbiote::NomadPackManager::plan(layer_bytes_, (uint32_t)c.n_layers, fixed,
+                                                     (uint64_t)(opt_.vram_budget_gb > 0 ? opt_.vram_budget_gb * 1e9 : 0));
+    if (!residency_.feasible)
+        return set_error(VSL_ERR_OOM,
+                         "engine: a %.2f GB budget cannot hold the KV cache, activations and embeddings (%.2f GB) "
+                         "plus two %.2f GB layer slots",
+                         opt_.vram_budget_gb, fixed / 1e9, layer_bytes_ / 1e9);
+    const int R = (int)residency_.resident_layers;
+    const int n_slots = residency_.streamed_layers ? 2 : 0;
+    arena_bytes_ = layer_bytes_ * (size_t)(R + n_slots) + emb_bytes;
+    CK(cudaMalloc(&arena_, arena_bytes_));
+    if (residency_.streamed_layers) {
+        host_layers_bytes_ = layer_bytes_ * residency_.streamed_layers;
+        CK(cudaHostAlloc(&host_layers_, host_layers_bytes_, cudaHostAllocMapped | cudaHostAllocPortable));
+        for (int i = 0; i < 2; i++) {
+            CK(cudaEventCreateWithFlags(&ev_copied_[i], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&ev_done_[i], cudaEventDisableTiming));
+        }
+        CK(cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming));
+    }
+    char* p = (char*)arena_;
+    auto place = [&](LayerPtrs& L, char* base) {
+        char* q = base;
+        L.wqkv = q; q += b_qkv;
+        L.wo = q; q += b_wo;
+        L.wgu = q; q += b_wgu;
+        L.wd = q; q += b_wd;
+        L.attn_norm = (float*)q; q += b_norm;
+        L.ffn_norm = (float*)q;
+    };
+    for (int l = 0; l < R; l++) {
+        place(layers_[l], p);
+        p += layer_bytes_;
+    }
+    for (int i = 0; i < n_slots; i++) {
+        slot_[i] = p;
+        p += layer_bytes_;
+    }
+    // streamed layers are loaded straight into pinned host memory (mapped, so the synthetic
+    // fill kernels and the upload copies write there); activate_streaming() then points them
+    // at their slot
+    for (int l = R; l < c.n_layers; l++) {
+        char* h = (char*)host_layers_ + (size_t)(l - R) * layer_bytes_;
+        place(layers_[l], h);
+        layers_[l].host = h;
+        layers_[l].slot = (l - R) & 1;
+    }
+    tok_embd_ = p; p += b_emb;
+    lm_head_ = p; p += b_head;
+    out_norm_ = (float*)p;
+
     CK(cudaMallocHost((void**)&h_ids_, mb * 4));
     CK(cudaMallocHost((void**)&h_out_, mb * 4));
     CK(cudaMallocHost((void**)&h_logits_, mb * (size_t)c.vocab * 4));
@@ -269,7 +308,7 @@ int DecodeEngine::alloc_buffers() {
 // gate/up (+SwiGLU) -> down (+residual), then lm_head (+argmax) and the token bookkeeping.
 int DecodeEngine::build_fused_program() {
     fs_ready_ = false;
-    if (!opt_.use_fused || opt_.tp_size != 1) return VSL_OK;
+    if (!opt_.use_fused || opt_.tp_size != 1 || residency_.streamed_layers) return VSL_OK;
     const vsl_model_config& c = cfg_;
     const int hd = c.head_dim, d = c.d_model;
     const int vec = (int)(16 / es_);
@@ -319,7 +358,7 @@ int DecodeEngine::build_fused_program() {
 }
 
 bool DecodeEngine::fused_supported(int B) const {
-    if (!fs_ready_ || B < 1 || B > 4) return false;
+    if (!fs_ready_ || B < 1 || B > 4 || residency_.streamed_layers) return false;
     const vsl_model_config& c = cfg_;
     if (c.head_dim != 64 && c.head_dim != 128) return false;
     if (c.head_dim == 128 && kvdtype_ != VSL_F16) return false;
@@ -394,7 +433,7 @@ int DecodeEngine::upload_tensor(const void* src, bool src_host, int dtype_src, s
     const size_t row_bytes = ncols * es;
     if (!src_host) {
         CK(cudaMemcpy2DAsync(dst, dst_ld, (const char*)src + (row0 * cols + col0) * es, cols * es, row_bytes, nrows,
-                             cudaMemcpyDeviceToDevice, copy_stream_));
+                             cudaMemcpyDefault, copy_stream_));
         CK(cudaStreamSynchronize(copy_stream_));
         return VSL_OK;
     }
@@ -421,7 +460,7 @@ int DecodeEngine::upload_tensor(const void* src, bool src_host, int dtype_src, s
             for (size_t i = 0; i < n; i++) memcpy(t + i * row_bytes, s + i * cols * es, row_bytes);
         }
         rc = check_cuda(cudaMemcpy2DAsync((char*)dst + r * dst_ld, dst_ld, t, row_bytes, row_bytes, n,
-                                          cudaMemcpyHostToDevice, copy_stream_),
+                                          cudaMemcpyDefault, copy_stream_),
                         "upload copy");
         if (!rc) rc = check_cuda(cudaEventRecord(done[buf], copy_stream_), "staging record");
     }
@@ -439,7 +478,7 @@ int DecodeEngine::upload_norm(const vk_symbiote::GGUFLoader& loader, const std::
         return set_error(VSL_ERR_FORMAT, "gguf: missing or mis-sized norm tensor %s", name.c_str());
     auto v = const_cast<vk_symbiote::GGUFLoader&>(loader).read_tensor_data(*t, true);
     if (!v) return set_error(VSL_ERR_FORMAT, "gguf: cannot read %s (%d)", name.c_str(), v.error());
-    CK(cudaMemcpy(dst, v.value().data(), (size_t)cfg_.d_model * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dst, v.value().data(), (size_t)cfg_.d_model * 4, cudaMemcpyDefault));
     return VSL_OK;
 }
 
@@ -524,6 +563,26 @@ int DecodeEngine::load_gguf(vk_symbiote::GGUFLoader& loader) {
         RC(upload_norm(loader, p + "ffn_norm.weight", L.ffn_norm));
     }
     CK(cudaDeviceSynchronize());
+    return activate_streaming();
+}
+
+// After loading: streamed layers switch their weight pointers from the pinned host copy to
+// their HBM slot (same offsets inside the layer block); the step copies host -> slot.
+int DecodeEngine::activate_streaming() {
+    if (streaming_active_) return VSL_OK;
+    for (LayerPtrs& L : layers_) {
+        if (L.slot < 0) continue;
+        char* h = L.host;
+        char* sl = slot_[L.slot];
+        auto mv = [&](auto*& ptr) { ptr = reinterpret_cast<std::remove_reference_t<decltype(ptr)>>(sl + ((char*)ptr - h)); };
+        mv(L.wqkv);
+        mv(L.wo);
+        mv(L.wgu);
+        mv(L.wd);
+        mv(L.attn_norm);
+        mv(L.ffn_norm);
+    }
+    streaming_active_ = true;
     return VSL_OK;
 }
 
@@ -553,12 +612,12 @@ int DecodeEngine::init_synthetic(uint64_t seed, double sigma) {
         RC(synth2d_impl((char*)L.wgu + d * es_, dt, 2 * d, seed, tid_layer(l, K_UP), (size_t)r * ff_l_, ff_l_, d, 0, d,
                         sigma, st));
         RC(synth2d_impl(L.wd, dt, ff_l_, seed, tid_layer(l, K_DOWN), 0, d, c.ffn, (size_t)r * ff_l_, ff_l_, sigma, st));
-        CK(cudaMemcpyAsync(L.attn_norm, ones.data(), d * 4, cudaMemcpyHostToDevice, st));
-        CK(cudaMemcpyAsync(L.ffn_norm, ones.data(), d * 4, cudaMemcpyHostToDevice, st));
+        CK(cudaMemcpyAsync(L.attn_norm, ones.data(), d * 4, cudaMemcpyDefault, st));
+        CK(cudaMemcpyAsync(L.ffn_norm, ones.data(), d * 4, cudaMemcpyDefault, st));
         CK(cudaStreamSynchronize(st));  // `ones` is pageable; keep it alive across the copies
     }
     CK(cudaStreamSynchronize(st));
-    return VSL_OK;
+    return activate_streaming();
 }
 
 // ---------------------------------------------------------------------------------------
@@ -655,9 +714,23 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     const size_t head = 16ull << 20;
     auto H = [&](size_t bytes) { return std::min(bytes, head); };
     RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
+    const bool streamed = residency_.streamed_layers > 0;
+    if (streamed) {  // bring the copy stream into this step (and into a graph being captured)
+        CK(cudaEventRecord(ev_fork_, st));
+        CK(cudaStreamWaitEvent(copy_stream_, ev_fork_, 0));
+    }
+    const int R = (int)residency_.resident_layers;
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
         const bool last = l + 1 == c.n_layers;
+        if (L.slot >= 0) {
+            // host -> slot copy of this layer on the side stream, after the slot's previous
+            // user (layer l - 2) has finished; it overlaps the compute of layer l - 1
+            if (l - 2 >= R) CK(cudaStreamWaitEvent(copy_stream_, ev_done_[L.slot], 0));
+            CK(cudaMemcpyAsync(slot_[L.slot], L.host, layer_bytes_, cudaMemcpyHostToDevice, copy_stream_));
+            CK(cudaEventRecord(ev_copied_[L.slot], copy_stream_));
+            CK(cudaStreamWaitEvent(st, ev_copied_[L.slot], 0));
+        }
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, x_, L.attn_norm, c.rms_eps, B, pos_,
                                   rope_cos_, rope_sin_, q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_,
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
@@ -671,6 +744,7 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, act_ffn_, B, x_, res_epi, nullptr, 0.0f,
                      last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st, tcr));
         RC(allreduce_x(B));
+        if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
                     seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr));

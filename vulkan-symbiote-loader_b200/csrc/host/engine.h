@@ -33,6 +33,10 @@ struct LayerPtrs {
     float* ffn_norm = nullptr;
     void* k_cache = nullptr;  // [n_pages][nkv_l][page][hd]
     void* v_cache = nullptr;
+    // streamed layers (over the HBM budget): weights live at `host` (pinned) and are copied
+    // into HBM slot `slot` each step; the pointers above then address the slot
+    char* host = nullptr;
+    int slot = -1;
 };
 
 class DecodeEngine {
@@ -102,6 +106,12 @@ private:
     size_t act_bytes_ = 0;
     void* fd_ws_ = nullptr;
     size_t fd_ws_bytes_ = 0;
+    void* host_layers_ = nullptr;  // pinned host copies of the streamed layers
+    size_t host_layers_bytes_ = 0;
+    char* slot_[2] = {nullptr, nullptr};
+    cudaEvent_t ev_fork_ = nullptr, ev_copied_[2] = {nullptr, nullptr}, ev_done_[2] = {nullptr, nullptr};
+    bool streaming_active_ = false;
+    int activate_streaming();
     void* tc_ws_ = nullptr;  // tensor-core route of batched projections (batch >= 5, 16-bit weights)
     size_t tc_ws_bytes_ = 0;
     TcRoute tc_route_ = {};

@@ -94,6 +94,9 @@ def lib() -> C.CDLL:
         "vsl_engine_set_trace": (i32, [vp, i32]),
         "vsl_engine_read_trace": (i32, [vp, i32, C.POINTER(C.c_uint64), C.POINTER(i32)]),
         "vsl_engine_memory_stats": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+        "vsl_engine_residency": (i32, [vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(u64),
+                                       C.POINTER(u64)]),
+        "vsl_pack_plan": (i32, [u64, C.c_uint32, u64, f64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -202,6 +205,13 @@ def gguf_tensor_info(path: str, name: str):
     off = C.c_uint64()
     check(lib().vsl_gguf_tensor_info(path.encode(), name.encode(), C.byref(t), ne, C.byref(off)))
     return t.value, [int(v) for v in ne if v], off.value
+
+
+def pack_plan(layer_bytes: int, n_layers: int, fixed_bytes: int, budget_gb: float) -> tuple[int, int]:
+    """(resident_layers, streamed_layers) the engine would choose under `budget_gb`."""
+    r, st = C.c_uint32(), C.c_uint32()
+    check(lib().vsl_pack_plan(layer_bytes, n_layers, fixed_bytes, budget_gb, C.byref(r), C.byref(st)))
+    return r.value, st.value
 
 
 def nccl_unique_id() -> bytes:
@@ -344,6 +354,14 @@ class Engine:
         w, kv, o = C.c_size_t(), C.c_size_t(), C.c_size_t()
         check(lib().vsl_engine_memory_stats(self.h, C.byref(w), C.byref(kv), C.byref(o)))
         return dict(weights=w.value, kv=kv.value, other=o.value)
+
+    def residency(self) -> dict:
+        """Weight residency under the HBM budget (layers kept in HBM / streamed each step)."""
+        r, st = C.c_uint32(), C.c_uint32()
+        sb, hb = C.c_uint64(), C.c_uint64()
+        check(lib().vsl_engine_residency(self.h, C.byref(r), C.byref(st), C.byref(sb), C.byref(hb)))
+        return {"resident_layers": r.value, "streamed_layers": st.value, "streamed_bytes_per_step": sb.value,
+                "host_bytes": hb.value}
 
     def device_status(self) -> int:
         s = C.c_int()
