@@ -131,6 +131,19 @@ VSL_API int vsl_flash_decode(const float* q, const void* k_cache, const void* v_
                      int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Long-context decode attention with the score product on the tcgen05 tensor cores (same
+ * semantics and cache layout as vsl_flash_decode; fp16 KV, head_dim 128, up to 8 query heads
+ * per KV group, B <= 64, page_size a multiple of 64). n_pages is the size of the physical page
+ * pool the page table indexes. Work is split evenly over persistent CTAs whatever the
+ * per-sequence lengths; sequences shared by several CTAs are merged deterministically.
+ * workspace: vsl_flash_decode_tc_workspace_size bytes, zero-filled before first use (its
+ * counters are left zero by every call). */
+VSL_API int vsl_flash_decode_tc_workspace_size(int B, int n_kv, size_t* bytes);
+VSL_API int vsl_flash_decode_tc(const float* q, const void* k_cache, const void* v_cache, int n_pages,
+                                const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                                int n_heads, int n_kv, int head_dim, int max_len, float* out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* Allocation-free form of vsl_flash_decode (no counterpart in the reference). For callers
  * that must not have the library allocate device memory -- hosts that own every device
  * byte through their own pool or budget, or loops that cannot take an allocation's implicit

@@ -109,6 +109,13 @@ def test_8b_shape_bf16_batch16_tensor_cores():
     _check_half(_teacher_forced(cfg, seed=35, n_steps=3, batch=16, prefill=300))
 
 
+def test_8b_shape_long_context_tensor_core_attention():
+    """max_seq >= 2048 selects the tcgen05-score attention; batch 8 the tcgen05 projections."""
+    cfg = dict(n_layers=2, d_model=4096, n_heads=32, n_kv_heads=8, head_dim=128, ffn=14336, vocab=128256,
+               rope_theta=500000.0, rms_eps=1e-5, wdtype=vsl.BF16)
+    _check_half(_teacher_forced(cfg, seed=37, n_steps=3, batch=8, prefill=2500, max_seq=2688))
+
+
 def test_fp16_batch8_tensor_cores_generate():
     cfg = dict(n_layers=3, d_model=1024, n_heads=8, n_kv_heads=8, head_dim=128, ffn=2816, vocab=6000,
                rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)

@@ -133,6 +133,7 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(act_);
     cudaFree(fd_ws_);
     cudaFree(tc_ws_);
+    cudaFree(fdtc_ws_);
     if (host_layers_) cudaFreeHost(host_layers_);
     for (cudaEvent_t ev : {ev_fork_, ev_copied_[0], ev_copied_[1], ev_done_[0], ev_done_[1]})
         if (ev) cudaEventDestroy(ev);
@@ -209,6 +210,13 @@ int DecodeEngine::alloc_buffers() {
     CK(cudaMalloc(&fd_ws_, fd_ws_bytes_));
     CK(cudaMemset(fd_ws_, 0, fd_ws_bytes_));
 
+    // long caches: attention with tcgen05 scores and an even split of the KV over the SMs
+    if (opt_.max_seq >= FDTC_MIN_SEQ &&
+        flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, opt_.max_batch, page_size_)) {
+        fdtc_ws_bytes_ = flash_decode_tc_workspace_bytes(opt_.max_batch, nkv_l_);
+        CK(cudaMalloc(&fdtc_ws_, fdtc_ws_bytes_));
+        CK(cudaMemset(fdtc_ws_, 0, fdtc_ws_bytes_));
+    }
     // batched projections (5..64 rows, 16-bit weights) run on the tensor cores: one workspace
     // sized for the largest projection of the model
     if (es_ == 2 && opt_.max_batch >= TC_MIN_BATCH) {
@@ -227,7 +235,7 @@ int DecodeEngine::alloc_buffers() {
     // exceeds the HBM budget, the layers that do not fit live in pinned host memory and
     // stream through two rotating HBM slots (NomadPackManager plan) ----
     const size_t emb_bytes = b_emb + b_head + b_norm;
-    const size_t fixed = kv_bytes_ + act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_ + emb_bytes;
+    const size_t fixed = kv_bytes_ + act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_ + fdtc_ws_bytes_ + emb_bytes;
     residency_ = vk_symbiote::NomadPackManager::plan(layer_bytes_, (uint32_t)c.n_layers, fixed,
                                                      (uint64_t)(opt_.vram_budget_gb > 0 ? opt_.vram_budget_gb * 1e9 : 0));
     if (!residency_.feasible)
@@ -636,6 +644,7 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(fs_bar_, 0, 16, stream_));
     CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
+    if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
     CK(cudaStreamSynchronize(stream_));
     std::fill(pos_host_.begin(), pos_host_.end(), 0);
     steps_host_ = 0;
@@ -734,9 +743,13 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, x_, L.attn_norm, c.rms_eps, B, pos_,
                                   rope_cos_, rope_sin_, q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_,
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
-        RC(flash_decode_impl(q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_, page_size_, pos_, B, nh_l_,
-                             nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st, L.wo,
-                             head ? wo_b : 0));
+        if (fdtc_ws_)
+            RC(flash_decode_tc_impl(q_, L.k_cache, L.v_cache, n_pages_, page_table_, max_pages_, page_size_, pos_, B,
+                                    nh_l_, nkv_l_, opt_.max_seq, attn_, fdtc_ws_, fdtc_ws_bytes_, status_, st));
+        else
+            RC(flash_decode_impl(q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_, page_size_, pos_, B,
+                                 nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st, L.wo,
+                                 head ? wo_b : 0));
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
         RC(allreduce_x(B));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, x_, B, act_ffn_, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,

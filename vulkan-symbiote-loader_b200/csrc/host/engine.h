@@ -67,7 +67,7 @@ public:
     int max_seq() const { return opt_.max_seq; }
     size_t arena_bytes() const { return arena_bytes_; }
     size_t kv_bytes() const { return kv_bytes_; }
-    size_t other_bytes() const { return act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_; }
+    size_t other_bytes() const { return act_bytes_ + fd_ws_bytes_ + tc_ws_bytes_ + fdtc_ws_bytes_; }
     vk_symbiote::PackResidency residency() const { return residency_; }
 
 private:
@@ -112,6 +112,8 @@ private:
     cudaEvent_t ev_fork_ = nullptr, ev_copied_[2] = {nullptr, nullptr}, ev_done_[2] = {nullptr, nullptr};
     bool streaming_active_ = false;
     int activate_streaming();
+    void* fdtc_ws_ = nullptr;  // long-context attention (tcgen05 scores) workspace; null = split-K kernel
+    size_t fdtc_ws_bytes_ = 0;
     void* tc_ws_ = nullptr;  // tensor-core route of batched projections (batch >= 5, 16-bit weights)
     size_t tc_ws_bytes_ = 0;
     TcRoute tc_route_ = {};

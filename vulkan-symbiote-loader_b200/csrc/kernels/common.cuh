@@ -115,6 +115,19 @@ __device__ __forceinline__ void prefetch_share(const void* base, size_t bytes, i
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// Named barrier that also ORs a predicate over the participating threads: every thread gets
+// true if any of them passed true. Threads that must leave a loop together (for example after
+// a timed-out wait) decide with this, so none is left waiting at a later bar.sync.
+__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
 __device__ __forceinline__ void set_status(int* status, int code) {
     if (status) atomicCAS(status, 0, code);
 }

@@ -500,7 +500,10 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(const __grid_
             if (B == 1) tiles_ok = tiles(std::integral_constant<int, 1>{});
             else if (B == 2) tiles_ok = tiles(std::integral_constant<int, 2>{});
             else tiles_ok = tiles(std::integral_constant<int, 4>{});
-            if (!tiles_ok) return;
+            // a warp whose wait expired has raised the abort flag and skipped its remaining
+            // tiles; it still takes part in the barriers below, and the grid barrier then
+            // returns false for every consumer warp together
+            (void)tiles_ok;
             if (f.epi == EK_LMHEAD) {
 #pragma unroll
                 for (int b = 0; b < FS_BMAX; b++)

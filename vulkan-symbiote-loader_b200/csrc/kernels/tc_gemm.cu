@@ -396,10 +396,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int si = 0;
         Segment sg;
         while (next_segment(a, f, f1, f0, sg)) {
-            if (!mbar_wait(&tmem_full, (uint32_t)(si & 1)) || ld_abort(&abort_s)) {
-                set_status(a.status, VSL_ERR_TIMEOUT);
-                atomicExch(&abort_s, 1);
-                break;
+            {
+                // the four epilogue warps leave together (they meet at named barriers below)
+                const bool bad = !mbar_wait(&tmem_full, (uint32_t)(si & 1)) || ld_abort(&abort_s);
+                if (named_barrier_or(1, 128, bad)) {
+                    set_status(a.status, VSL_ERR_TIMEOUT);
+                    atomicExch(&abort_s, 1);
+                    break;
+                }
             }
             tc_fence_after();
             const int row = sg.rt * TC_BM + rloc;

@@ -68,6 +68,8 @@ def lib() -> C.CDLL:
                                       i32, i32, vp]),
         "vsl_flash_decode_workspace_size": (i32, [i32, i32, i32, i32, i32, i32, C.POINTER(sz)]),
         "vsl_flash_decode": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, sz, vp]),
+        "vsl_flash_decode_tc_workspace_size": (i32, [i32, i32, C.POINTER(sz)]),
+        "vsl_flash_decode_tc": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp, vp, sz, vp]),
         "vsl_lm_head_sample": (i32, [i32, vp, i32, i32, vp, vp, f32, i32, vp, vp, i32, f32, u64, vp, vp]),
         "vsl_argmax": (i32, [vp, i32, i32, vp, vp]),
         "vsl_synth_fill": (i32, [vp, i32, u64, u64, u64, u64, f64, vp]),
@@ -177,6 +179,19 @@ def flash_decode(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size,
     check(lib().vsl_flash_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), kvdtype, _ptr(page_table), max_pages,
                                  page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, split_len, _ptr(out),
                                  _ptr(workspace), workspace_bytes, stream))
+
+
+def flash_decode_tc_workspace_size(B, n_kv) -> int:
+    out = C.c_size_t()
+    check(lib().vsl_flash_decode_tc_workspace_size(B, n_kv, C.byref(out)))
+    return out.value
+
+
+def flash_decode_tc(q, k_cache, v_cache, n_pages, page_table, max_pages, page_size, pos, B, n_heads, n_kv, head_dim,
+                    max_len, out, workspace, workspace_bytes, stream=0):
+    check(lib().vsl_flash_decode_tc(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table), max_pages,
+                                    page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, _ptr(out),
+                                    _ptr(workspace), workspace_bytes, stream))
 
 
 def lm_head_sample(wdtype, W, V_local, K, x, norm_w, eps, B, logits, slots, vocab_offset=0, temperature=0.0,
