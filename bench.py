@@ -57,6 +57,9 @@ def parse():
                     help="7b: the headline (BASELINE configs[1]); 8b: BASELINE configs[3], batch 16 over "
                          "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b-stream: "
                          "BASELINE configs[4] on one GPU under a 64 GB HBM cap (layers streamed from host)")
+    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc"],
+                    help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
+                         "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads")
     ap.add_argument("--sweep", action="store_true",
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     return ap.parse_args()
@@ -506,8 +509,43 @@ def run_sweep(args):
     return 0
 
 
+def run_profile_case(args):
+    """A single kernel case, launched three times, sized for an ncu capture (about 1-2 GB)."""
+    import torch
+
+    import vsl
+    if args.profile_case == "tc_gemm":
+        N, K, B = 32000, 4096, 16
+        Ws = [torch.randn(N, K, device="cuda").mul_(0.02).half() for _ in range(2)]
+        x = torch.randn(B, K, device="cuda")
+        y = torch.zeros(B, N, device="cuda")
+        n = vsl.skinny_gemm_tc_workspace_size(N, K, B)
+        wst = torch.zeros(n // 4 + 512, dtype=torch.int32, device="cuda")
+        ws = (wst.data_ptr() + 1023) // 1024 * 1024
+        for i in range(3):
+            vsl.skinny_gemm_tc(vsl.F16, Ws[i % 2], N, K, x, B, y, vsl.EPI_STORE, None, 0.0, ws, n)
+    else:
+        B, nh, nkv, L, page = 16, 32, 8, 8192, 64
+        mp = L // page
+        k = torch.randn(B * mp, nkv, page, 128, device="cuda").half()
+        v = torch.randn(B * mp, nkv, page, 128, device="cuda").half()
+        pt = torch.arange(B * mp, dtype=torch.int32, device="cuda").reshape(B, mp)
+        pos = torch.full((B,), L - 1, dtype=torch.int32, device="cuda")
+        q = torch.randn(B, nh, 128, device="cuda")
+        out = torch.zeros(B, nh, 128, device="cuda")
+        n = vsl.flash_decode_tc_workspace_size(B, nkv)
+        w = torch.zeros(n // 4 + 64, dtype=torch.int32, device="cuda")
+        for _ in range(3):
+            vsl.flash_decode_tc(q, k, v, B * mp, pt, mp, page, pos, B, nh, nkv, 128, L, out, w, n)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "launches": 3}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_case:
+        return run_profile_case(args)
     if args.sweep:
         return run_sweep(args)
     if args.impl == "reference":
