@@ -1,27 +1,29 @@
-// Long-context decode attention with the score product on tcgen05 tensor cores.
+// Long-context decode attention on tcgen05 tensor cores.
 //
 // Same semantics as flash_decode_kernel (attention.cu; reference attention.comp:84-189): query
 // head h reads KV group h*n_kv/n_heads, scores q.k / sqrt(head_dim), max-subtracted softmax over
 // positions [0, pos], output = probabilities times V. Built for caches of thousands of positions
-// (fp16 KV, head_dim 128, up to 8 query heads per KV group):
-//   * S^T[128 positions][16] = K_chunk[128][128] . Q2[16][128]^T on the tensor cores
-//     (tcgen05.mma kind::f16, M = 128, N = 16, K = 16 x 8, fp32 accumulate in TMEM). Q2 holds
-//     the group's query heads as hi/lo fp16 pairs (rows 0..G-1 hi, 8..8+G-1 lo, rest zero), so
-//     the scores keep ~22 bits of the fp32 query; a thread reads the row of its position with
-//     tcgen05.ld and adds the two columns. Positions sit on M because tcgen05 needs M >= 64 and a
-//     group has only 4-8 query heads.
-//   * softmax (online, fp32) and P.V on the CUDA cores: P.V costs one multiply-add per V byte
-//     per head, well under the FMA rate needed at HBM speed; V is read straight from the
-//     swizzled stage.
+// (fp16 KV, head_dim 128, up to 8 query heads per KV group). Per 128-position chunk:
+//   * S^T[128 positions][16] = K[128][128] . Q2[16][128]^T (tcgen05.mma kind::f16, M = 128,
+//     N = 16, fp32 in TMEM). Q2 holds the group's query heads as hi/lo fp16 pairs (rows 0..G-1
+//     hi, 8..8+G-1 lo, the rest zero), so scores keep ~22 bits of the fp32 query. Positions sit
+//     on M because tcgen05 needs M >= 64 and a group has only 4-8 query heads.
+//   * online softmax (fp32) by 4 warps, one position per thread (tcgen05.ld of its TMEM row);
+//     the probabilities go back to shared memory as hi/lo fp16 rows P2[16][128].
+//   * O^T[128 dims][16] = V^T . P2^T on the tensor cores, with the V tile used in place as the
+//     MN-major A operand (the TMA layout: positions as rows of 64 dims); a thread (= head dim)
+//     folds O into its accumulators one chunk later, so the next chunk's scores and softmax
+//     overlap this product.
 //   * K and V chunks (two 64-position pages each, 2 x 64-column 128-byte-swizzle atoms) arrive by
-//     tensor TMA into a 3-stage mbarrier ring (192 KB in flight per SM).
+//     tensor TMA into a 3-stage mbarrier ring (192 KB in flight per SM); rows past the end of a
+//     sequence are zeroed in shared memory before the product reads them (0 x garbage).
 //   * work split (stream-K): the flattened list of (sequence, KV group, 128-position chunk) is cut
-//     into gridDim.x equal ranges, one per persistent CTA, whatever the per-sequence lengths; a
-//     (sequence, group) shared by several CTAs is merged by the last to finish, in CTA order
+//     into equal ranges over persistent CTAs, whatever the per-sequence lengths; a (sequence,
+//     group) shared by several CTAs is merged by the last to finish, in CTA order
 //     (deterministic), with an atomic counter it resets to zero.
-// Roles: warps 0-3 softmax (TMEM lane quarter = warp), warps 0-7 P.V, warp 8 TMA producer,
-// warp 9 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second) and records
-// VSL_ERR_TIMEOUT; the kernel then drains its copies and MMAs and frees its TMEM.
+// Roles: warps 0-3 softmax and accumulation (TMEM lane quarter = warp), warp 4 TMA producer,
+// warp 5 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second) and
+// records VSL_ERR_TIMEOUT; the kernel then drains its copies and MMAs and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -34,7 +36,7 @@
 
 namespace vsl {
 
-constexpr int FT_THREADS = 320;  // 8 softmax/P.V warps, TMA producer, MMA issuer
+constexpr int FT_THREADS = 192;  // 4 softmax warps, TMA producer, MMA issuer
 constexpr int FT_CHUNK = 128;                 // positions per chunk (MMA M)
 constexpr int FT_HD = 128;
 constexpr int FT_GMAX = 8;
@@ -44,8 +46,8 @@ constexpr int FT_ATOM = 128 * 64 * 2;         // one 64-column swizzle atom of a
 constexpr int FT_STAGE = 4 * FT_ATOM;         // K (2 atoms) + V (2 atoms) = 64 KB
 constexpr int FT_Q2 = 2 * FT_N * 128;         // 2 atoms of 16 rows x 128 bytes
 constexpr int FT_BMAX = 64;
-constexpr size_t FT_RED = (size_t)3 * FT_GMAX * FT_HD * 4;  // partial outputs of position quarters 1-3
-constexpr size_t FT_SMEM = 1024 + (size_t)FT_STAGES * FT_STAGE + FT_Q2 + (size_t)FT_CHUNK * FT_GMAX * 4 + FT_RED;
+constexpr int FT_P2 = 2 * FT_N * 128;         // P as hi/lo fp16 rows: 2 atoms of 16 rows x 128 bytes
+constexpr size_t FT_SMEM = 1024 + (size_t)FT_STAGES * FT_STAGE + FT_Q2 + 2 * (size_t)FT_P2;
 
 struct FtArgs {
     const float* q;          // [B][n_heads][128]
@@ -58,7 +60,8 @@ struct FtArgs {
     float* ws_ml;            // [grid][2][8][2]
     int* counters;           // [B][n_kv], zero between launches
     int* status;
-    uint32_t idesc;
+    uint32_t idesc;     // S MMA: K (A, K-major) . Q2 (B, K-major)
+    uint32_t idesc_pv;  // PV MMA: V (A, MN-major) . P2 (B, K-major)
 };
 
 __device__ __forceinline__ void ft_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -76,6 +79,32 @@ __device__ __forceinline__ uint64_t ft_desc(uint32_t saddr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 __device__ __forceinline__ int ft_abort(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+// MN-major 128-byte-swizzle operand (the V tile as it lands from TMA: rows = positions = K,
+// 64 head dims = M per 128-byte row): atoms of 64 M x 8 K; the next 64 dims sit one 16 KB atom
+// further (leading byte offset), the next 8 positions 1024 bytes further (stride byte offset)
+__device__ __forceinline__ uint64_t ft_desc_mn(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(FT_ATOM >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void ft_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void ft_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void ft_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 // Flattened work list: for sequence b, n_kv groups x nch[b] chunks, starting at off[b].
 struct FtWork {
@@ -114,6 +143,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                            const __grid_constant__ FtArgs a) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[FT_STAGES], empty[FT_STAGES], s_full[2], s_free[2], q_ready;
+    __shared__ __align__(8) uint64_t p_ready[2], o_full[2], o_free[2];
     __shared__ uint32_t tmem_s;
     __shared__ int abort_s, last_s;
     __shared__ float red_max[4][FT_GMAX], red_sum[4][FT_GMAX];
@@ -123,18 +153,20 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const uint32_t ring = base;
     const uint32_t q2 = base + FT_STAGES * FT_STAGE;
-    float* Ps = reinterpret_cast<float*>(smem_raw + (q2 + FT_Q2 - smem_u32(smem_raw)));  // [128][8]
-    float* red_o = Ps + FT_CHUNK * FT_GMAX;                                                // [3][8][128]
+    const uint32_t p2 = q2 + FT_Q2;  // two P2 tiles [16 rows][128 positions], K-major, 128-byte swizzle
     const int c = blockIdx.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < FT_STAGES; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 8);
+            mbar_init(&empty[s], 1);  // tcgen05.commit after the chunk's P.V
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], 4);
+            mbar_init(&p_ready[i], 4);
+            mbar_init(&o_full[i], 1);
+            mbar_init(&o_free[i], 4);
         }
         mbar_init(&q_ready, 4);
         mbar_fence_init();
@@ -142,8 +174,8 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
     }
-    if (warp == 9) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_s)), "r"(32)
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_s)), "r"(64)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -176,7 +208,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     const int Gc = (long long)gridDim.x < T ? (int)gridDim.x : (int)T;
     const long long f0 = c < Gc ? ft_lo(T, Gc, c) : 0, f1 = c < Gc ? ft_lo(T, Gc, c + 1) : 0;
 
-    if (warp == 8) {
+    if (warp == 4) {
         // ================= TMA producer =================
         if (lane == 0) {
             FtCur cu;
@@ -218,284 +250,292 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             for (long long u = issued > FT_STAGES ? issued - FT_STAGES : 0; u < issued; u++)
                 mbar_wait(&full[u % FT_STAGES], (uint32_t)((u / FT_STAGES) & 1));
         }
-    } else if (warp == 9) {
+    } else if (warp == 5) {
         // ================= MMA issue =================
+        // per chunk i: S(i) = K . Q2^T into TMEM S[i&1]; PV(i) = V^T . P2(i)^T into TMEM O[i&1]
+        // once the softmax warps have written P2(i). S(i+1) is issued before PV(i) when chunk i+1
+        // belongs to the same (sequence, group), so scores and products overlap the softmax.
         if (lane == 0) {
-            FtCur cu;
-            if (f0 < f1) ft_seek(wk, a.B, a.n_kv, f0, cu);
-            int s = 0, buf = 0, seg = 0;
-            uint32_t fpar = 0u;
-            long long it = 0;
-            bool ok = true;
+            FtCur cs;  // cursor of the next S to issue
+            if (f0 < f1) ft_seek(wk, a.B, a.n_kv, f0, cs);
+            const long long n = f1 - f0;
+            int ss = 0;           // stage of the next S
+            uint32_t fpar = 0u;   // its full-barrier parity
+            int seg = 0;
             int pb = -1, pg = -1;
-            for (long long f = f0; f < f1 && ok; f++, it++) {
-                if (cu.b != pb || cu.g != pg) {  // new (sequence, group): its query rows must be staged
-                    if (!mbar_wait(&q_ready, (uint32_t)(seg & 1))) {
-                        ok = false;
-                        break;
-                    }
+            bool ok = true;
+            long long s_issued = 0;
+            int st_of[2] = {0, 0};      // stage of chunk i (kept for PV(i) and the stage release)
+            int segpos[2] = {0, 0};     // (b * n_kv + g) of chunk i
+            auto issue_s = [&](long long i) -> bool {
+                const int key = cs.b * a.n_kv + cs.g;
+                if (cs.b != pb || cs.g != pg) {  // new (sequence, group): its query rows must be staged
+                    if (!mbar_wait(&q_ready, (uint32_t)(seg & 1))) return false;
                     seg++;
-                    pb = cu.b;
-                    pg = cu.g;
+                    pb = cs.b;
+                    pg = cs.g;
                 }
-                if (!mbar_wait(&full[s], fpar) || (it >= 2 && !mbar_wait(&s_free[buf], (uint32_t)(((it >> 1) - 1) & 1))) ||
-                    ft_abort(&abort_s)) {
-                    ok = false;
-                    break;
-                }
+                if (!mbar_wait(&full[ss], fpar)) return false;
+                if (i >= 2 && !mbar_wait(&s_free[i & 1], (uint32_t)(((i >> 1) - 1) & 1))) return false;
                 ft_fence_after();
-                const uint32_t st = ring + s * FT_STAGE;
+                const uint32_t st = ring + ss * FT_STAGE;
 #pragma unroll
                 for (int at = 0; at < 2; at++) {
                     const uint64_t ad = ft_desc(st + at * FT_ATOM), bd = ft_desc(q2 + at * (FT_Q2 / 2));
 #pragma unroll
                     for (int k = 0; k < 4; k++)
-                        asm volatile(
-                            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem + buf * FT_N),
-                            "l"(ad + (uint64_t)(2 * k)), "l"(bd + (uint64_t)(2 * k)), "r"(a.idesc),
-                            "r"((at > 0 || k > 0) ? 1u : 0u)
-                            : "memory");
+                        ft_mma(tmem + (uint32_t)((i & 1) * FT_N), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k),
+                               a.idesc, (at > 0 || k > 0) ? 1u : 0u);
                 }
-                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 smem_u32(&s_full[buf]))
-                             : "memory");
-                ft_next(wk, a.n_kv, cu);
-                buf ^= 1;
-                if (++s == FT_STAGES) {
-                    s = 0;
+                ft_commit(&s_full[i & 1]);
+                st_of[i & 1] = ss;
+                segpos[i & 1] = key;
+                if (++ss == FT_STAGES) {
+                    ss = 0;
                     fpar ^= 1u;
+                }
+                ft_next(wk, a.n_kv, cs);
+                return true;
+            };
+            auto issue_pv = [&](long long i) -> bool {
+                if (!mbar_wait(&p_ready[i & 1], (uint32_t)((i >> 1) & 1))) return false;
+                if (i >= 2 && !mbar_wait(&o_free[i & 1], (uint32_t)(((i >> 1) - 1) & 1))) return false;
+                ft_fence_after();
+                const uint32_t vt = ring + st_of[i & 1] * FT_STAGE + 2 * FT_ATOM;
+                const uint32_t pt = p2 + (uint32_t)(i & 1) * FT_P2;
+#pragma unroll
+                for (int k = 0; k < FT_CHUNK / 16; k++) {
+                    // V as the MN-major A operand: 16 positions (rows) per step = 2048 bytes
+                    const uint64_t ad = ft_desc_mn(vt + (uint32_t)(k * 2048));
+                    const uint64_t bd = ft_desc(pt + (uint32_t)((k >> 2) * (FT_P2 / 2))) + (uint64_t)(2 * (k & 3));
+                    ft_mma(tmem + (uint32_t)(2 * FT_N + (i & 1) * FT_N), ad, bd, a.idesc_pv, k > 0 ? 1u : 0u);
+                }
+                ft_commit(&o_full[i & 1]);
+                ft_commit(&empty[st_of[i & 1]]);  // K and V of this chunk are no longer read
+                return true;
+            };
+            if (n > 0) ok = issue_s(0);
+            s_issued = ok ? 1 : 0;
+            for (long long i = 0; i < n && ok; i++) {
+                if (ft_abort(&abort_s)) {
+                    ok = false;
+                    break;
+                }
+                // look ahead one S only inside the same (sequence, group): a new one needs the
+                // softmax warps to have finished this one first (they stage its query rows)
+                if (s_issued == i + 1 && i + 1 < n && cs.b * a.n_kv + cs.g == segpos[i & 1]) {
+                    ok = issue_s(i + 1);
+                    if (!ok) break;
+                    s_issued++;
+                }
+                ok = issue_pv(i);
+                if (!ok) break;
+                if (s_issued == i + 1 && i + 1 < n) {
+                    ok = issue_s(i + 1);
+                    if (!ok) break;
+                    s_issued++;
                 }
             }
             if (!ok) {
                 set_status(a.status, VSL_ERR_TIMEOUT);
                 atomicExch(&abort_s, 1);
             }
-            if (it > 0) mbar_wait(&s_full[(it - 1) & 1], (uint32_t)(((it - 1) >> 1) & 1));  // last MMAs done
+            // the accumulators must not be freed under a running MMA
+            if (n > 0) {
+                const long long last = (s_issued > 0 ? s_issued : 1) - 1;
+                mbar_wait(&s_full[last & 1], (uint32_t)((last >> 1) & 1));
+                mbar_wait(&o_full[last & 1], (uint32_t)((last >> 1) & 1));
+            }
         }
         __syncwarp();
     } else {
-        // ================= softmax (warps 0-3) + P.V (warps 0-7) =================
-        // warps 0-3: thread t reads TMEM row t (its position in the chunk) and runs the online
-        // softmax; all 8 warps then share P.V: thread t owns output dims 2*(t&63), +1 over the
-        // position quarter t>>6 of the chunk, with its own partial accumulator (the four quarters
-        // are summed in order at the end of a segment)
+        // ================= softmax + accumulation (warps 0-3; thread t = position t, dim t) =================
         const int t = threadIdx.x;
-        const bool sm_warp = warp < 4;
-        const int dp = t & 63, pq = t >> 6;
         const int G = a.G;
-        float m[FT_GMAX], l[FT_GMAX], o0[FT_GMAX], o1[FT_GMAX];
+        float m[FT_GMAX], lt[FT_GMAX], o[FT_GMAX], alpha_prev[FT_GMAX];
+        unsigned char* smem_g = smem_raw - smem_u32(smem_raw);  // generic pointer of shared address 0
+        // P2 rows beyond the group's heads stay zero in both buffers
+        for (int i = t; i < 2 * FT_P2 / 16; i += 128)
+            *reinterpret_cast<uint4*>(smem_g + p2 + i * 16) = make_uint4(0, 0, 0, 0);
         FtCur cu;
         if (f0 < f1) ft_seek(wk, a.B, a.n_kv, f0, cu);
-        int s = 0, buf = 0;
-        long long it = 0;
+        long long i = 0;
         int pb = -1, pg = -1;
-        // V element (position p, dims 2dp..2dp+1) inside a stage: atom dp/32, row p, 16-byte chunk
-        // ((2dp mod 64)/8) ^ (p mod 8), byte (2dp mod 8)*2
-        const int v_atom = dp >> 5, v_chunk = (dp & 31) >> 2, v_byte = (dp & 3) * 4;
-        for (long long f = f0; f < f1; f++, it++) {
+        int sst = 0;
+        uint32_t fpar = 0u;
+        for (long long f = f0; f < f1; f++, i++) {
             const int b = cu.b, g = cu.g, ch = cu.ch;
             const int len = wk.len[b];
-            if (b != pb || g != pg) {
+            const bool seg_start = b != pb || g != pg;
+            if (seg_start) {
                 // ---- new (sequence, group): reset the softmax state, stage Q2 for the tensor cores ----
 #pragma unroll
                 for (int j = 0; j < FT_GMAX; j++) {
                     m[j] = -CUDART_INF_F;
-                    l[j] = 0.0f;
-                    o0[j] = 0.0f;
-                    o1[j] = 0.0f;
+                    lt[j] = 0.0f;
+                    o[j] = 0.0f;
+                    alpha_prev[j] = 1.0f;
                 }
-                if (sm_warp) {
-                    const int r = t >> 4, at = (t >> 3) & 1, cc = t & 7;  // query row r, atom, 16-byte chunk
-                    uint4 hv = make_uint4(0, 0, 0, 0), lv = make_uint4(0, 0, 0, 0);
-                    if (r < G) {
-                        const float* qr = a.q + ((size_t)b * a.n_heads + (size_t)g * G + r) * FT_HD + at * 64 + cc * 8;
-                        const float4 x0 = __ldcg(reinterpret_cast<const float4*>(qr));
-                        const float4 x1 = __ldcg(reinterpret_cast<const float4*>(qr) + 1);
-                        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-                        __half hh[8], ll[8];
+                const int r = t >> 4, at = (t >> 3) & 1, cc = t & 7;  // query row r, atom, 16-byte chunk
+                uint4 hv = make_uint4(0, 0, 0, 0), lv = make_uint4(0, 0, 0, 0);
+                if (r < G) {
+                    const float* qr = a.q + ((size_t)b * a.n_heads + (size_t)g * G + r) * FT_HD + at * 64 + cc * 8;
+                    const float4 x0 = __ldcg(reinterpret_cast<const float4*>(qr));
+                    const float4 x1 = __ldcg(reinterpret_cast<const float4*>(qr) + 1);
+                    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+                    __half hh[8], ll[8];
 #pragma unroll
-                        for (int e = 0; e < 8; e++) {
-                            hh[e] = __float2half_rn(xs[e]);
-                            ll[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
-                        }
-                        hv = *reinterpret_cast<const uint4*>(hh);
-                        lv = *reinterpret_cast<const uint4*>(ll);
+                    for (int e = 0; e < 8; e++) {
+                        hh[e] = __float2half_rn(xs[e]);
+                        ll[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
                     }
-                    unsigned char* q2p = smem_raw + (q2 - smem_u32(smem_raw)) + at * (FT_Q2 / 2);
-                    const int rh = r, rl = r + 8;
-                    *reinterpret_cast<uint4*>(q2p + rh * 128 + ((cc ^ (rh & 7)) << 4)) = hv;
-                    *reinterpret_cast<uint4*>(q2p + rl * 128 + ((cc ^ (rl & 7)) << 4)) = lv;
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&q_ready);
+                    hv = *reinterpret_cast<const uint4*>(hh);
+                    lv = *reinterpret_cast<const uint4*>(ll);
                 }
+                unsigned char* q2p = smem_g + q2 + at * (FT_Q2 / 2);
+                *reinterpret_cast<uint4*>(q2p + r * 128 + ((cc ^ (r & 7)) << 4)) = hv;
+                *reinterpret_cast<uint4*>(q2p + (r + 8) * 128 + ((cc ^ ((r + 8) & 7)) << 4)) = lv;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&q_ready);
                 pb = b;
                 pg = g;
             }
-            // ---- scores of this chunk (TMEM row t, warps 0-3) ----
-            const int n_valid = min(FT_CHUNK, len - ch * FT_CHUNK);
-            const bool valid = t < n_valid;
-            float sc[FT_GMAX];
+            // ---- scores of chunk i (TMEM row t) ----
             {
-                bool bad = false;
-                if (sm_warp) bad = !mbar_wait(&s_full[buf], (uint32_t)((it >> 1) & 1));
-                bad = bad || ft_abort(&abort_s);
-                // the eight warps leave together (they meet at named barriers further down)
-                if (named_barrier_or(1, 256, bad)) {
+                const bool bad = !mbar_wait(&s_full[i & 1], (uint32_t)((i >> 1) & 1)) || ft_abort(&abort_s);
+                if (named_barrier_or(1, 128, bad)) {  // the four warps leave together
                     set_status(a.status, VSL_ERR_TIMEOUT);
                     atomicExch(&abort_s, 1);
                     break;
                 }
             }
-            if (sm_warp) {
-                ft_fence_after();
-                uint32_t r[16];
-                asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                    "[%16];"
-                    : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-                      "=r"(r[15])
-                    : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * FT_N)));
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                ft_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[buf]);
+            ft_fence_after();
+            uint32_t r[16];
+            ft_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)((i & 1) * FT_N), r);
+            ft_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[i & 1]);
+            const int n_valid = min(FT_CHUNK, len - ch * FT_CHUNK);
+            const bool valid = t < n_valid;
+            float sc[FT_GMAX];
 #pragma unroll
-                for (int j = 0; j < FT_GMAX; j++)
-                    sc[j] = (j < G && valid) ? (__uint_as_float(r[j]) + __uint_as_float(r[8 + j])) * a.scale
-                                             : -CUDART_INF_F;
-#pragma unroll
-                for (int j = 0; j < FT_GMAX; j++) {
-                    if (j >= G) break;
+            for (int j = 0; j < FT_GMAX; j++) {
+                sc[j] = (j < G && valid) ? (__uint_as_float(r[j]) + __uint_as_float(r[8 + j])) * a.scale : -CUDART_INF_F;
+                if (j < G) {
                     const float mx = warp_max(sc[j]);
                     if (lane == 0) red_max[warp][j] = mx;
                 }
             }
-            named_barrier_sync(1, 256);
-            // ---- online softmax: every thread keeps the same running max / sum ----
+            named_barrier_sync(1, 128);
             float alpha[FT_GMAX];
+            const int pc = t >> 6, pcol = t & 63;  // P2 atom and column of position t
+            unsigned char* p2p = smem_g + p2 + (uint32_t)(i & 1) * FT_P2 + pc * (FT_P2 / 2) + ((pcol & 7) << 1);
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++) {
                 if (j >= G) break;
                 const float cm = fmaxf(fmaxf(red_max[0][j], red_max[1][j]), fmaxf(red_max[2][j], red_max[3][j]));
                 const float mn = fmaxf(m[j], cm);
                 alpha[j] = expf(m[j] - mn);
-                if (sm_warp) {
-                    const float pj = valid ? expf(sc[j] - mn) : 0.0f;
-                    sc[j] = pj;
-                    const float sm = warp_sum(pj);
-                    if (lane == 0) red_sum[warp][j] = sm;
-                }
+                const float pj = valid ? expf(sc[j] - mn) : 0.0f;
                 m[j] = mn;
+                lt[j] = lt[j] * alpha[j] + pj;
+                const __half ph = __float2half_rn(pj);
+                const __half pl = __float2half_rn(pj - __half2float(ph));
+                const int rh = j, rl = j + 8;
+                *reinterpret_cast<__half*>(p2p + rh * 128 + ((((pcol >> 3) ^ (rh & 7))) << 4)) = ph;
+                *reinterpret_cast<__half*>(p2p + rl * 128 + ((((pcol >> 3) ^ (rl & 7))) << 4)) = pl;
             }
-            if (sm_warp) {
-                float4* pr = reinterpret_cast<float4*>(Ps + t * FT_GMAX);
-                pr[0] = make_float4(sc[0], G > 1 ? sc[1] : 0.f, G > 2 ? sc[2] : 0.f, G > 3 ? sc[3] : 0.f);
-                if (G > 4) pr[1] = make_float4(sc[4], G > 5 ? sc[5] : 0.f, G > 6 ? sc[6] : 0.f, G > 7 ? sc[7] : 0.f);
+            if (n_valid < FT_CHUNK && !valid) {
+                // rows past the sequence end hold whatever the cache had (possibly NaN bit patterns):
+                // zero them so that 0 x garbage cannot reach the product
+                mbar_wait(&full[sst], fpar);  // order after the TMA's writes to this stage
+                unsigned char* vrow = smem_g + ring + sst * FT_STAGE + 2 * FT_ATOM + t * 128;
+#pragma unroll
+                for (int at2 = 0; at2 < 2; at2++)
+#pragma unroll
+                    for (int c16 = 0; c16 < 8; c16++)
+                        *reinterpret_cast<uint4*>(vrow + at2 * FT_ATOM + c16 * 16) = make_uint4(0, 0, 0, 0);
             }
-            named_barrier_sync(1, 256);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_ready[i & 1]);
+            if (++sst == FT_STAGES) {
+                sst = 0;
+                fpar ^= 1u;
+            }
+            // ---- fold PV(i-1) into the output (lagged one chunk: PV(i) overlaps the next softmax) ----
+            ft_next(wk, a.n_kv, cu);
+            const bool seg_end = f + 1 == f1 || cu.b != b || cu.g != g;
+            auto fold = [&](long long k, const float* al) -> bool {
+                const bool bad = !mbar_wait(&o_full[k & 1], (uint32_t)((k >> 1) & 1)) || ft_abort(&abort_s);
+                if (named_barrier_or(1, 128, bad)) return false;
+                ft_fence_after();
+                uint32_t ov[16];
+                ft_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(2 * FT_N + (k & 1) * FT_N), ov);
+                ft_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&o_free[k & 1]);
+#pragma unroll
+                for (int j = 0; j < FT_GMAX; j++)
+                    if (j < G) o[j] = o[j] * al[j] + (__uint_as_float(ov[j]) + __uint_as_float(ov[8 + j]));
+                return true;
+            };
+            bool fold_ok = true;
+            if (!seg_start) fold_ok = fold(i - 1, alpha_prev);
+            if (fold_ok && seg_end) fold_ok = fold(i, alpha);
+            if (!fold_ok) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < FT_GMAX; j++) alpha_prev[j] = alpha[j];
+            if (!seg_end) continue;
+            // ---- end of this CTA's part of (b, g): softmax denominators over the 128 positions ----
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++) {
                 if (j >= G) break;
-                l[j] = l[j] * alpha[j] + (red_sum[0][j] + red_sum[1][j] + red_sum[2][j] + red_sum[3][j]);
+                const float sm = warp_sum(lt[j]);
+                if (lane == 0) red_sum[warp][j] = sm;
             }
-            // ---- P.V: dims 2dp, 2dp+1 over positions [32 pq, 32 pq + 32) of the valid ones ----
-            {
-                const unsigned char* vb = smem_raw + (ring + s * FT_STAGE + 2 * FT_ATOM - smem_u32(smem_raw)) +
-                                          v_atom * FT_ATOM + v_byte;
-                float a0[FT_GMAX], a1[FT_GMAX];
+            named_barrier_sync(1, 128);
+            float l[FT_GMAX];
 #pragma unroll
-                for (int j = 0; j < FT_GMAX; j++) a0[j] = a1[j] = 0.0f;
-                const int pe = min(32 * pq + 32, n_valid);
-#pragma unroll 4
-                for (int pp = 32 * pq; pp < pe; pp++) {
-                    const __half2 vh = *reinterpret_cast<const __half2*>(vb + pp * 128 + ((v_chunk ^ (pp & 7)) << 4));
-                    const float2 v = __half22float2(vh);
-                    const float4 w0 = *reinterpret_cast<const float4*>(Ps + pp * FT_GMAX);
-                    a0[0] = fmaf(w0.x, v.x, a0[0]); a1[0] = fmaf(w0.x, v.y, a1[0]);
-                    a0[1] = fmaf(w0.y, v.x, a0[1]); a1[1] = fmaf(w0.y, v.y, a1[1]);
-                    a0[2] = fmaf(w0.z, v.x, a0[2]); a1[2] = fmaf(w0.z, v.y, a1[2]);
-                    a0[3] = fmaf(w0.w, v.x, a0[3]); a1[3] = fmaf(w0.w, v.y, a1[3]);
-                    if (G > 4) {
-                        const float4 w1 = *reinterpret_cast<const float4*>(Ps + pp * FT_GMAX + 4);
-                        a0[4] = fmaf(w1.x, v.x, a0[4]); a1[4] = fmaf(w1.x, v.y, a1[4]);
-                        a0[5] = fmaf(w1.y, v.x, a0[5]); a1[5] = fmaf(w1.y, v.y, a1[5]);
-                        a0[6] = fmaf(w1.z, v.x, a0[6]); a1[6] = fmaf(w1.z, v.y, a1[6]);
-                        a0[7] = fmaf(w1.w, v.x, a0[7]); a1[7] = fmaf(w1.w, v.y, a1[7]);
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < FT_GMAX; j++) {
-                    if (j >= G) break;
-                    o0[j] = o0[j] * alpha[j] + a0[j];
-                    o1[j] = o1[j] * alpha[j] + a1[j];
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-            if (++s == FT_STAGES) s = 0;
-            buf ^= 1;
-            // ---- end of this CTA's part of (b, g)? ----
-            ft_next(wk, a.n_kv, cu);
-            const bool seg_end = f + 1 == f1 || cu.b != b || cu.g != g;
-            if (!seg_end) continue;
-            // sum the four position quarters in order: quarters 1-3 stage their partials
-            if (pq > 0) {
-                float* ro = red_o + ((size_t)(pq - 1) * FT_GMAX) * FT_HD + 2 * dp;
-#pragma unroll
-                for (int j = 0; j < FT_GMAX; j++)
-                    if (j < G) *reinterpret_cast<float2*>(ro + (size_t)j * FT_HD) = make_float2(o0[j], o1[j]);
-            }
-            named_barrier_sync(1, 256);
+            for (int j = 0; j < FT_GMAX; j++)
+                l[j] = j < G ? (red_sum[0][j] + red_sum[1][j]) + (red_sum[2][j] + red_sum[3][j]) : 1.0f;
             const long long p0 = wk.off[b] + (long long)g * wk.nch[b];
             const int first = ft_owner(T, Gc, p0), lastc = ft_owner(T, Gc, p0 + wk.nch[b] - 1);
-            float* out = a.out + ((size_t)b * a.n_heads + (size_t)g * G) * FT_HD + 2 * dp;
-            const int slot = ft_lo(T, Gc, c) >= p0 ? 0 : 1;
-            if (pq == 0) {
-#pragma unroll
-                for (int j = 0; j < FT_GMAX; j++) {
-                    if (j >= G) break;
-#pragma unroll
-                    for (int q3 = 0; q3 < 3; q3++) {
-                        const float2 v = *reinterpret_cast<const float2*>(red_o + ((size_t)q3 * FT_GMAX + j) * FT_HD + 2 * dp);
-                        o0[j] += v.x;
-                        o1[j] += v.y;
-                    }
-                }
-                if (first == lastc) {
-#pragma unroll
-                    for (int j = 0; j < FT_GMAX; j++)
-                        if (j < G) *reinterpret_cast<float2*>(out + (size_t)j * FT_HD) = make_float2(o0[j] / l[j], o1[j] / l[j]);
-                } else {
-                    float* wo = a.ws_o + (((size_t)c * 2 + slot) * FT_GMAX) * FT_HD + 2 * dp;
-#pragma unroll
-                    for (int j = 0; j < FT_GMAX; j++)
-                        if (j < G) *reinterpret_cast<float2*>(wo + (size_t)j * FT_HD) = make_float2(o0[j], o1[j]);
-                    if (dp < G) {
-                        float* wml = a.ws_ml + (((size_t)c * 2 + slot) * FT_GMAX + dp) * 2;
-                        float mt = m[0], lt = l[0];
-#pragma unroll
-                        for (int j = 1; j < FT_GMAX; j++)
-                            if (j == dp) {
-                                mt = m[j];
-                                lt = l[j];
-                            }
-                        wml[0] = mt;
-                        wml[1] = lt;
-                    }
-                }
-            }
+            float* out = a.out + ((size_t)b * a.n_heads + (size_t)g * G) * FT_HD + t;
             if (first == lastc) {
-                named_barrier_sync(1, 256);  // red_o is reused by the next segment
+#pragma unroll
+                for (int j = 0; j < FT_GMAX; j++)
+                    if (j < G) out[(size_t)j * FT_HD] = o[j] / l[j];
+                named_barrier_sync(1, 128);  // red_sum is reused by the next segment
                 continue;
             }
+            const int slot = ft_lo(T, Gc, c) >= p0 ? 0 : 1;
+            float* wo = a.ws_o + (((size_t)c * 2 + slot) * FT_GMAX) * FT_HD + t;
+#pragma unroll
+            for (int j = 0; j < FT_GMAX; j++)
+                if (j < G) wo[(size_t)j * FT_HD] = o[j];
+            if (t < G) {
+                float* wml = a.ws_ml + (((size_t)c * 2 + slot) * FT_GMAX + t) * 2;
+                float mt = m[0], ltt = l[0];
+#pragma unroll
+                for (int j = 1; j < FT_GMAX; j++)
+                    if (j == t) {
+                        mt = m[j];
+                        ltt = l[j];
+                    }
+                wml[0] = mt;
+                wml[1] = ltt;
+            }
             __threadfence();
-            named_barrier_sync(1, 256);
+            named_barrier_sync(1, 128);
             if (t == 0) last_s = atomicAdd(a.counters + (size_t)b * a.n_kv + g, 1) == lastc - first;
-            named_barrier_sync(1, 256);
-            if (last_s && pq == 0) {
+            named_barrier_sync(1, 128);
+            if (last_s) {
                 __threadfence();
 #pragma unroll
                 for (int j = 0; j < FT_GMAX; j++) {
@@ -505,29 +545,27 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                         const int sl = ft_lo(T, Gc, cc2) >= p0 ? 0 : 1;
                         M = fmaxf(M, __ldcg(a.ws_ml + (((size_t)cc2 * 2 + sl) * FT_GMAX + j) * 2));
                     }
-                    float L = 0.0f, O0 = 0.0f, O1 = 0.0f;
+                    float L = 0.0f, O = 0.0f;
                     for (int cc2 = first; cc2 <= lastc; cc2++) {
                         const int sl = ft_lo(T, Gc, cc2) >= p0 ? 0 : 1;
                         const float* ml = a.ws_ml + (((size_t)cc2 * 2 + sl) * FT_GMAX + j) * 2;
                         const float w = expf(__ldcg(ml) - M);
                         L += __ldcg(ml + 1) * w;
-                        const float2 ov =
-                            __ldcg(reinterpret_cast<const float2*>(a.ws_o + (((size_t)cc2 * 2 + sl) * FT_GMAX + j) * FT_HD + 2 * dp));
-                        O0 += ov.x * w;
-                        O1 += ov.y * w;
+                        O += __ldcg(a.ws_o + (((size_t)cc2 * 2 + sl) * FT_GMAX + j) * FT_HD + t) * w;
                     }
-                    *reinterpret_cast<float2*>(out + (size_t)j * FT_HD) = make_float2(O0 / L, O1 / L);
+                    out[(size_t)j * FT_HD] = O / L;
                 }
                 if (t == 0) a.counters[(size_t)b * a.n_kv + g] = 0;
             }
+            named_barrier_sync(1, 128);  // last_s and red_sum are reused by the next segment
         }
     }
 
     ft_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == 5) {
         ft_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(32) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64) : "memory");
     }
 }
 
@@ -610,6 +648,7 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
     // instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A/B f16 (0), both K-major,
     // N >> 3 in bits 17-22, M >> 4 in bits 24-28
     a.idesc = (1u << 4) | ((uint32_t)(FT_N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    a.idesc_pv = a.idesc | (1u << 15);  // A (V) MN-major
     const long long rows = (long long)n_pages * n_kv * page_size;
     CUtensorMap mk, mv;
     int rc = ft_map(&mk, k_cache, rows);
