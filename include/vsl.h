@@ -215,6 +215,8 @@ typedef struct {
     int use_fused;     /* 1 = run each decode step as one persistent cooperative kernel
                           when the shape allows it; 0 (default) = one kernel per operation,
                           replayed as a CUDA graph with programmatic dependent launch  */
+    int use_p2p;       /* tensor parallel: 1 (default) = one-shot NVLink peer-memory all-reduces
+                          (CUDA IPC buffers, one kernel per reduction); 0 = NCCL            */
 } vsl_engine_options;
 
 VSL_API void vsl_engine_default_options(vsl_engine_options* opt);

@@ -1,6 +1,7 @@
-"""Tensor parallelism on 2 GPUs (NCCL): TP=2 logits and greedy ids against a single-GPU
-engine on the same seeded model, fp32 (tight) and bf16 GQA with batch 3 and a prefilled
-cache (logit tolerance 2e-2). Skipped when fewer than 2 GPUs are visible."""
+"""Tensor parallelism on 2 GPUs: TP=2 logits and greedy ids against a single-GPU engine on the
+same seeded model, fp32 (tight) and bf16 GQA with batch 3 and a prefilled cache (logit
+tolerance 2e-2), with the peer-memory all-reduce (which must also reproduce bit for bit) and
+with NCCL. Skipped when fewer than 2 GPUs are visible."""
 import json
 import os
 import socket
@@ -33,6 +34,9 @@ def test_tp2_matches_single_gpu(tmp_path):
         logs = "".join(f"\n--- {p}\n" + p.read_text()[-4000:] for p in sorted(log_dir.rglob("*.log")))
         raise AssertionError(f"tp worker failed ({r.returncode}):{logs}\n{r.stderr[-2000:]}")
     res = json.loads(out.read_text())
-    assert res["fp32_gqa"]["status"] == 0 and res["fp32_gqa"]["ids_equal"] and res["fp32_gqa"]["gen_equal"]
-    assert res["fp32_gqa"]["max_abs"] < 1e-4
-    assert res["bf16_8b_like"]["status"] == 0 and res["bf16_8b_like"]["max_abs"] < 2e-2
+    for tag in ("p2p", "nccl"):  # peer-memory all-reduce and NCCL
+        f = res[f"fp32_gqa_{tag}"]
+        assert f["status"] == 0 and f["ids_equal"] and f["gen_equal"] and f["max_abs"] < 1e-4, (tag, f)
+        b = res[f"bf16_8b_like_{tag}"]
+        assert b["status"] == 0 and b["max_abs"] < 2e-2, (tag, b)
+    assert res["fp32_gqa_p2p_repeat_equal"] and res["bf16_8b_like_p2p_repeat_equal"]

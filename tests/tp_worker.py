@@ -40,16 +40,18 @@ def main():
     result = {}
     for name, c in cases.items():
         kw = dict(device=local, max_batch=c["batch"], max_seq=256)
-        nid = vdist.nccl_id(d)  # a unique id forms exactly one communicator: one per engine
-        e = vsl.Engine.synthetic(c["cfg"], seed=11, tp_rank=rank, tp_size=ws, nccl_id=nid, **kw)
-        if c["prefill"]:
-            e.fill_kv_synthetic(3, 1.0, c["prefill"], c["batch"])
-        lg_tp, ids_tp = run(e, c["cfg"], 6, c["batch"])
-        gen_tp = None
-        if c["batch"] == 1:
-            gen_tp = e.generate([5, 9, 13, 200], 24)
-        status = e.device_status()
-        e.close()
+        runs = {}
+        # peer-memory all-reduce (twice: it must reproduce bit for bit) and NCCL
+        for tag, p2p in (("p2p", 1), ("p2p_again", 1), ("nccl", 0)):
+            nid = vdist.nccl_id(d)  # a unique id forms exactly one communicator: one per engine
+            e = vsl.Engine.synthetic(c["cfg"], seed=11, tp_rank=rank, tp_size=ws, nccl_id=nid, use_p2p=p2p, **kw)
+            if c["prefill"]:
+                e.fill_kv_synthetic(3, 1.0, c["prefill"], c["batch"])
+            lg_tp, ids_tp = run(e, c["cfg"], 6, c["batch"])
+            gen_tp = e.generate([5, 9, 13, 200], 24) if c["batch"] == 1 else None
+            runs[tag] = (lg_tp, ids_tp, gen_tp, e.device_status())
+            e.close()
+            d.barrier()
         if rank == 0:
             e1 = vsl.Engine.synthetic(c["cfg"], seed=11, **kw)
             if c["prefill"]:
@@ -57,8 +59,12 @@ def main():
             lg_1, ids_1 = run(e1, c["cfg"], 6, c["batch"])
             gen_1 = e1.generate([5, 9, 13, 200], 24) if c["batch"] == 1 else None
             e1.close()
-            result[name] = dict(max_abs=float(np.abs(lg_tp - lg_1).max()), ids_equal=bool((ids_tp == ids_1).all()),
-                                gen_equal=gen_tp == gen_1, status=status)
+            for tag in ("p2p", "nccl"):
+                lg_tp, ids_tp, gen_tp, status = runs[tag]
+                result[f"{name}_{tag}"] = dict(max_abs=float(np.abs(lg_tp - lg_1).max()),
+                                               ids_equal=bool((ids_tp == ids_1).all()), gen_equal=gen_tp == gen_1,
+                                               status=status)
+            result[f"{name}_p2p_repeat_equal"] = bool(np.array_equal(runs["p2p"][0], runs["p2p_again"][0]))
         d.barrier()
     if rank == 0:
         with open(sys.argv[1], "w") as f:

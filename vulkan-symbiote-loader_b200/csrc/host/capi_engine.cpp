@@ -38,6 +38,7 @@ extern "C" void vsl_engine_default_options(vsl_engine_options* o) {
     o->use_graph = 1;
     o->use_pdl = 1;
     o->use_fused = 0;
+    o->use_p2p = 1;
 }
 
 extern "C" int vsl_nccl_unique_id(void* out128) {

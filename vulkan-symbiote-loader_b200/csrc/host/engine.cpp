@@ -119,7 +119,19 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
         if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
         nccl_ = comm;
     }
-    return alloc_buffers();
+    RC(alloc_buffers());
+    if (nccl_ && opt_.use_p2p && tp <= P2P_MAX_RANKS) RC(setup_p2p());
+    return VSL_OK;
+}
+
+// Receive buffers of the peer-memory all-reduces, exchanged with the other ranks by CUDA IPC.
+int DecodeEngine::setup_p2p() {
+    RC(p2p_setup(&p2p_x_, &p2p_x_local_, p2p_x_opened_, opt_.tp_rank, opt_.tp_size, opt_.max_batch * cfg_.d_model, 4,
+                 nccl_, ar_epochs_, status_, stream_));
+    RC(p2p_setup(&p2p_s_, &p2p_s_local_, p2p_s_opened_, opt_.tp_rank, opt_.tp_size, opt_.max_batch, 8, nccl_,
+                 ar_epochs_ + 1, status_, stream_));
+    p2p_ready_ = true;
+    return VSL_OK;
 }
 
 DecodeEngine::~DecodeEngine() {
@@ -127,6 +139,8 @@ DecodeEngine::~DecodeEngine() {
     if (stream_) cudaStreamSynchronize(stream_);
     for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
     graphs_.clear();
+    p2p_teardown(p2p_x_local_, p2p_x_opened_, opt_.tp_size);
+    p2p_teardown(p2p_s_local_, p2p_s_opened_, opt_.tp_size);
     if (nccl_) ncclCommDestroy((ncclComm_t)nccl_);
     cudaFree(arena_);
     cudaFree(kv_);
@@ -190,6 +204,7 @@ int DecodeEngine::alloc_buffers() {
         {(void**)&rope_cos_, (size_t)opt_.max_seq * half * 4},
         {(void**)&rope_sin_, (size_t)opt_.max_seq * half * 4},
         {(void**)&page_table_, mb * (size_t)max_pages_ * 4},
+        {(void**)&ar_epochs_, 16},
         {(void**)&fs_bar_, 16},
         {(void**)&fs_abort_, 4},
         {(void**)&fs_att_ws_, mb * (size_t)nh_l_ * (size_t)((opt_.max_seq + 63) / 64) * (hd + 2) * 4},
@@ -703,6 +718,7 @@ int DecodeEngine::set_forced(const int32_t* ids, int n_steps, int B) {
 
 int DecodeEngine::allreduce_x(int B) {
     if (!nccl_) return VSL_OK;
+    if (p2p_ready_ && B * cfg_.d_model <= p2p_x_.cap) return p2p_allreduce(p2p_x_, x_, B * cfg_.d_model, 0, stream_);
     ncclResult_t r = ncclAllReduce(x_, x_, (size_t)B * cfg_.d_model, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_);
     if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
     return VSL_OK;
@@ -761,7 +777,9 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     }
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
                     seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr));
-    if (nccl_) {
+    if (p2p_ready_) {
+        RC(p2p_allreduce(p2p_s_, slots_, B, 1, st));
+    } else if (nccl_) {
         ncclResult_t r = ncclAllReduce(slots_, slots_, (size_t)B, ncclUint64, ncclMax, (ncclComm_t)nccl_, st);
         if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));
     }

@@ -19,6 +19,7 @@
 #include "../../../include/vk_symbiote/GGUFLoader.h"
 #include "../../../include/vk_symbiote/NomadPack.h"
 #include "kernels.h"
+#include "../kernels/p2p_allreduce.h"
 #include "../../../include/vsl.h"
 #include "../kernels/fused_step.h"
 
@@ -112,6 +113,15 @@ private:
     cudaEvent_t ev_fork_ = nullptr, ev_copied_[2] = {nullptr, nullptr}, ev_done_[2] = {nullptr, nullptr};
     bool streaming_active_ = false;
     int activate_streaming();
+    // tensor parallel: one-shot NVLink peer-memory all-reduces (residual sums, argmax keys)
+    P2pPeers p2p_x_{}, p2p_s_{};
+    void* p2p_x_local_ = nullptr;
+    void* p2p_s_local_ = nullptr;
+    void* p2p_x_opened_[P2P_MAX_RANKS] = {};
+    void* p2p_s_opened_[P2P_MAX_RANKS] = {};
+    bool p2p_ready_ = false;
+    unsigned long long* ar_epochs_ = nullptr;  // device call counters of the two all-reduces
+    int setup_p2p();
     void* fdtc_ws_ = nullptr;  // long-context attention (tcgen05 scores) workspace; null = split-K kernel
     size_t fdtc_ws_bytes_ = 0;
     void* tc_ws_ = nullptr;  // tensor-core route of batched projections (batch >= 5, 16-bit weights)

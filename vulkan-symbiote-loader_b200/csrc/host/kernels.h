@@ -5,6 +5,11 @@
 
 namespace vsl {
 
+struct P2pPeers;
+int p2p_setup(P2pPeers* out, void** local, void** opened, int rank, int n, int cap, int elem_bytes, void* comm,
+              unsigned long long* epoch, int* status, cudaStream_t st);
+void p2p_teardown(void* local, void** opened, int n);
+
 // Engine-owned route of batched projections onto the tensor cores (kernels/tc_gemm.cu):
 // a workspace of tc_workspace_bytes for the largest projection and batch, zero-filled once.
 struct TcRoute {

@@ -41,7 +41,8 @@ class EngineOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("max_batch", C.c_int), ("max_seq", C.c_int), ("kv_dtype", C.c_int),
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
-                ("use_pdl", C.c_int), ("use_fused", C.c_int)]
+                ("use_pdl", C.c_int), ("use_fused", C.c_int),
+                ("use_p2p", C.c_int)]
 
 
 _lib = None
