@@ -292,6 +292,15 @@ VSL_API int vsl_engine_step_stats(vsl_engine* e, int B, int* kernels_per_step, d
  * else (activations, token log, attention workspace). Feeds get_vram_stats(). */
 VSL_API int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t* kv_bytes, size_t* other_bytes);
 
+/* Prompt pass (the batched prompt processing the reference's generate lacks: it re-runs the whole
+ * sequence per token, VulkanSymbioteEngine.cpp:678-765): ids[0..n) are positions pos..pos+n-1 of
+ * sequence `seq`, processed up to 64 at a time as rows of one batch (tensor-core projections; each
+ * row attends causally through its own position over the sequence's pages). Their KV is written,
+ * pos advances by n, and the sequence's next input becomes the greedy argmax of the last prompt
+ * token's logits, returned in *next_id (logits: optional [vocab] of that token). Decoding then
+ * continues with vsl_engine_run / vsl_engine_step_host. */
+VSL_API int vsl_engine_prefill(vsl_engine* e, const int32_t* ids, int n, int seq, int32_t* next_id, float* logits);
+
 /* Weight residency under vram_budget_gb (replaces PackManager::get_vram_stats and the pack
  * scheduler's state, NomadPack.cpp:1190-1249, 1323-1326; VulkanSymbioteEngine.cpp:1555-1599):
  * layers 0..resident_layers-1 stay in HBM, the other streamed_layers live in pinned host memory

@@ -1,7 +1,7 @@
 """Tensor parallelism on 2 GPUs: TP=2 logits and greedy ids against a single-GPU engine on the
 same seeded model, fp32 (tight) and bf16 GQA with batch 3 and a prefilled cache (logit
 tolerance 2e-2), with the peer-memory all-reduce (which must also reproduce bit for bit) and
-with NCCL. Skipped when fewer than 2 GPUs are visible."""
+with NCCL, and the chunked prompt pass (prefill). Skipped when fewer than 2 GPUs are visible."""
 import json
 import os
 import socket
@@ -37,6 +37,7 @@ def test_tp2_matches_single_gpu(tmp_path):
     for tag in ("p2p", "nccl"):  # peer-memory all-reduce and NCCL
         f = res[f"fp32_gqa_{tag}"]
         assert f["status"] == 0 and f["ids_equal"] and f["gen_equal"] and f["max_abs"] < 1e-4, (tag, f)
+        assert f["pf_next_equal"] and f["pf_max_abs"] < 1e-4, (tag, f)  # prompt pass (prefill)
         b = res[f"bf16_8b_like_{tag}"]
-        assert b["status"] == 0 and b["max_abs"] < 2e-2, (tag, b)
+        assert b["status"] == 0 and b["max_abs"] < 2e-2 and b["pf_max_abs"] < 2e-2, (tag, b)
     assert res["fp32_gqa_p2p_repeat_equal"] and res["bf16_8b_like_p2p_repeat_equal"]

@@ -38,6 +38,7 @@ def main():
                              prefill=130),
     }
     result = {}
+    prompt = synth.synth_ids(7, 9, 90, 4096).tolist()  # two prefill chunks (64 + 26 rows)
     for name, c in cases.items():
         kw = dict(device=local, max_batch=c["batch"], max_seq=256)
         runs = {}
@@ -49,7 +50,9 @@ def main():
                 e.fill_kv_synthetic(3, 1.0, c["prefill"], c["batch"])
             lg_tp, ids_tp = run(e, c["cfg"], 6, c["batch"])
             gen_tp = e.generate([5, 9, 13, 200], 24) if c["batch"] == 1 else None
-            runs[tag] = (lg_tp, ids_tp, gen_tp, e.device_status())
+            e.reset()
+            pf_tp = e.prefill(prompt, seq=c["batch"] - 1, want_logits=True)
+            runs[tag] = (lg_tp, ids_tp, gen_tp, e.device_status(), pf_tp)
             e.close()
             d.barrier()
         if rank == 0:
@@ -58,12 +61,15 @@ def main():
                 e1.fill_kv_synthetic(3, 1.0, c["prefill"], c["batch"])
             lg_1, ids_1 = run(e1, c["cfg"], 6, c["batch"])
             gen_1 = e1.generate([5, 9, 13, 200], 24) if c["batch"] == 1 else None
+            e1.reset()
+            pf_1 = e1.prefill(prompt, seq=c["batch"] - 1, want_logits=True)
             e1.close()
             for tag in ("p2p", "nccl"):
-                lg_tp, ids_tp, gen_tp, status = runs[tag]
+                lg_tp, ids_tp, gen_tp, status, pf_tp = runs[tag]
                 result[f"{name}_{tag}"] = dict(max_abs=float(np.abs(lg_tp - lg_1).max()),
                                                ids_equal=bool((ids_tp == ids_1).all()), gen_equal=gen_tp == gen_1,
-                                               status=status)
+                                               status=status, pf_max_abs=float(np.abs(pf_tp[1] - pf_1[1]).max()),
+                                               pf_next_equal=pf_tp[0] == pf_1[0])
             result[f"{name}_p2p_repeat_equal"] = bool(np.array_equal(runs["p2p"][0], runs["p2p_again"][0]))
         d.barrier()
     if rank == 0:

@@ -228,6 +228,14 @@ extern "C" int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size
     return VSL_OK;
 }
 
+extern "C" int vsl_engine_prefill(vsl_engine* e, const int32_t* ids, int n, int seq, int32_t* next_id,
+                                  float* logits) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    return e->impl->prefill(ids, n, seq, next_id, logits);
+    GUARD_END
+}
+
 extern "C" int vsl_engine_residency(vsl_engine* e, uint32_t* resident_layers, uint32_t* streamed_layers,
                                     uint64_t* streamed_bytes_per_step, uint64_t* host_bytes) {
     if (int rc = check_engine(e)) return rc;

@@ -147,6 +147,11 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(act_);
     cudaFree(fd_ws_);
     cudaFree(tc_ws_);
+    cudaFree(pf_mem_);
+    cudaFree(pf_fd_ws_);
+    cudaFree(pf_fdtc_ws_);
+    cudaFree(pf_tc_ws_);
+    if (pf_h_) cudaFreeHost(pf_h_);
     cudaFree(fdtc_ws_);
     if (host_layers_) cudaFreeHost(host_layers_);
     for (cudaEvent_t ev : {ev_fork_, ev_copied_[0], ev_copied_[1], ev_done_[0], ev_done_[1]})
@@ -322,6 +327,7 @@ int DecodeEngine::alloc_buffers() {
     for (size_t b = 0; b < mb; b++)
         for (int i = 0; i < max_pages_; i++) pt[b * max_pages_ + i] = (int32_t)(b * max_pages_ + i);
     CK(cudaMemcpy(page_table_, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+    pt_host_ = pt;
     pos_host_.assign(mb, 0);
     return build_fused_program();
 }
@@ -660,6 +666,8 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
+    if (pf_tc_ws_) CK(cudaMemsetAsync(pf_tc_route_.ws, 0, pf_tc_route_.bytes, stream_));
+    if (pf_fdtc_ws_) CK(cudaMemsetAsync(pf_fdtc_ws_, 0, pf_fdtc_bytes_, stream_));
     CK(cudaStreamSynchronize(stream_));
     std::fill(pos_host_.begin(), pos_host_.end(), 0);
     steps_host_ = 0;
@@ -716,21 +724,22 @@ int DecodeEngine::set_forced(const int32_t* ids, int n_steps, int B) {
 // the decode step
 // ---------------------------------------------------------------------------------------
 
-int DecodeEngine::allreduce_x(int B) {
+int DecodeEngine::allreduce_sum(float* buf, int count) {
     if (!nccl_) return VSL_OK;
-    if (p2p_ready_ && B * cfg_.d_model <= p2p_x_.cap) return p2p_allreduce(p2p_x_, x_, B * cfg_.d_model, 0, stream_);
-    ncclResult_t r = ncclAllReduce(x_, x_, (size_t)B * cfg_.d_model, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_);
+    if (p2p_ready_ && count <= p2p_x_.cap) return p2p_allreduce(p2p_x_, buf, count, 0, stream_);
+    ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_);
     if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
     return VSL_OK;
 }
 
-int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
-    if (fused_supported(B)) return enqueue_fused_step(B, temperature, seed);
+// The decoder layers for B activation rows held in `sb` (the decode step's buffers, or a
+// prefill chunk's, where the rows are consecutive prompt positions of one sequence).
+int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
     const vsl_model_config& c = cfg_;
     const int d = c.d_model, hd = c.head_dim;
     const int res_epi = opt_.tp_rank == 0 ? VSL_EPI_ADD : VSL_EPI_STORE;  // partial sums reduced into x
     cudaStream_t st = stream_;
-    const TcRoute* tcr = tc_ws_ ? &tc_route_ : nullptr;
+    const TcRoute* tcr = sb.tc;
     // L2 prefetch hints: each kernel requests the head of the next projection's weights so
     // that the weight stream does not stall at kernel boundaries; the attention kernel
     // (which reads little from HBM) prefetches the whole output projection.
@@ -738,7 +747,6 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     const size_t wgu_b = 2 * (size_t)ff_l_ * d * es_, wd_b = (size_t)d * ff_l_ * es_;
     const size_t head = 16ull << 20;
     auto H = [&](size_t bytes) { return std::min(bytes, head); };
-    RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
     const bool streamed = residency_.streamed_layers > 0;
     if (streamed) {  // bring the copy stream into this step (and into a graph being captured)
         CK(cudaEventRecord(ev_fork_, st));
@@ -756,25 +764,40 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
             CK(cudaEventRecord(ev_copied_[L.slot], copy_stream_));
             CK(cudaStreamWaitEvent(st, ev_copied_[L.slot], 0));
         }
-        RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, x_, L.attn_norm, c.rms_eps, B, pos_,
-                                  rope_cos_, rope_sin_, q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_,
+        RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, sb.x, L.attn_norm, c.rms_eps, B, sb.pos,
+                                  rope_cos_, rope_sin_, sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_,
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
-        if (fdtc_ws_)
-            RC(flash_decode_tc_impl(q_, L.k_cache, L.v_cache, n_pages_, page_table_, max_pages_, page_size_, pos_, B,
-                                    nh_l_, nkv_l_, opt_.max_seq, attn_, fdtc_ws_, fdtc_ws_bytes_, status_, st));
+        if (sb.fdtc_ws)
+            RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
+                                    nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st));
         else
-            RC(flash_decode_impl(q_, L.k_cache, L.v_cache, kvdtype_, page_table_, max_pages_, page_size_, pos_, B,
-                                 nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, attn_, fd_ws_, fd_ws_bytes_, st, L.wo,
-                                 head ? wo_b : 0));
-        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, attn_, B, x_, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
-        RC(allreduce_x(B));
-        RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, x_, B, act_ffn_, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
+            RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
+                                 nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
+                                 head ? wo_b : 0, sb.shared_pages));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
+        RC(allreduce_sum(sb.x, B * d));
+        RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
                      H(wd_b), st, tcr));
-        RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, act_ffn_, B, x_, res_epi, nullptr, 0.0f,
+        RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, sb.act, B, sb.x, res_epi, nullptr, 0.0f,
                      last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st, tcr));
-        RC(allreduce_x(B));
+        RC(allreduce_sum(sb.x, B * d));
         if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
+    return VSL_OK;
+}
+
+int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
+    if (fused_supported(B)) return enqueue_fused_step(B, temperature, seed);
+    const vsl_model_config& c = cfg_;
+    const int d = c.d_model, hd = c.head_dim;
+    cudaStream_t st = stream_;
+    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * d * es_;
+    auto H = [&](size_t bytes) { return std::min(bytes, (size_t)16 << 20); };
+    RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
+    StepBufs sb{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
+                tc_ws_ ? &tc_route_ : nullptr, false};
+    RC(enqueue_layers(sb, B));
+    const TcRoute* tcr = sb.tc;
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
                     seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr));
     if (p2p_ready_) {
@@ -831,6 +854,109 @@ int DecodeEngine::run(int n_steps, int B, float temperature, uint64_t seed) {
     }
     for (int b = 0; b < B; b++) pos_host_[b] += n_steps;
     steps_host_ += n_steps;
+    return VSL_OK;
+}
+
+// Buffers of the prompt pass, allocated on first use.
+int DecodeEngine::alloc_prefill() {
+    if (pf_mem_) return VSL_OK;
+    const vsl_model_config& c = cfg_;
+    const size_t P = PF_ROWS, d = c.d_model, qd = (size_t)nh_l_ * c.head_dim, A = 256;
+    const size_t n_int = 2 * P + P * (size_t)max_pages_;
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += align_up(bytes, A);
+        return o;
+    };
+    const size_t o_ids = take(n_int * 4), o_x = take(P * d * 4), o_q = take(P * qd * 4), o_attn = take(P * qd * 4),
+                 o_act = take(P * ff_l_ * 4), o_lg = take((size_t)v_l_ * 4), o_slot = take(16), o_next = take(4);
+    CK(cudaMalloc(&pf_mem_, off));
+    CK(cudaMemset(pf_mem_, 0, off));
+    char* m = static_cast<char*>(pf_mem_);
+    pf_ids_ = reinterpret_cast<int32_t*>(m + o_ids);
+    pf_pos_ = pf_ids_ + P;
+    pf_pages_ = pf_ids_ + 2 * P;
+    pf_x_ = reinterpret_cast<float*>(m + o_x);
+    pf_q_ = reinterpret_cast<float*>(m + o_q);
+    pf_attn_ = reinterpret_cast<float*>(m + o_attn);
+    pf_act_ = reinterpret_cast<float*>(m + o_act);
+    pf_logits_ = reinterpret_cast<float*>(m + o_lg);
+    pf_slot_ = reinterpret_cast<unsigned long long*>(m + o_slot);
+    pf_next_ = reinterpret_cast<int32_t*>(m + o_next);
+    CK(cudaMallocHost((void**)&pf_h_, n_int * 4 + 64));
+    RC(vsl_flash_decode_workspace_size(PF_ROWS, nh_l_, nkv_l_, c.head_dim, opt_.max_seq, split_len_, &pf_fd_bytes_));
+    CK(cudaMalloc(&pf_fd_ws_, pf_fd_bytes_));
+    CK(cudaMemset(pf_fd_ws_, 0, pf_fd_bytes_));
+    if (fdtc_ws_ && flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, PF_ROWS, page_size_)) {
+        pf_fdtc_bytes_ = flash_decode_tc_workspace_bytes(PF_ROWS, nkv_l_);
+        CK(cudaMalloc(&pf_fdtc_ws_, pf_fdtc_bytes_));
+        CK(cudaMemset(pf_fdtc_ws_, 0, pf_fdtc_bytes_));
+    }
+    if (es_ == 2) {
+        const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
+        const int k_max = std::max({c.d_model, nh_l_ * c.head_dim, ff_l_});
+        const size_t bytes = tc_workspace_bytes(n_max, k_max, PF_ROWS) + 1024;
+        CK(cudaMalloc(&pf_tc_ws_, bytes));
+        CK(cudaMemset(pf_tc_ws_, 0, bytes));
+        char* base = reinterpret_cast<char*>(((uintptr_t)pf_tc_ws_ + 1023) & ~(uintptr_t)1023);
+        pf_tc_route_ = TcRoute{base, bytes - 1024, TC_MIN_BATCH, status_};
+    }
+    return VSL_OK;
+}
+
+int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits) {
+    if (!ids || n <= 0 || seq < 0 || seq >= opt_.max_batch)
+        return set_error(VSL_ERR_INVALID, "prefill: %d ids for sequence %d", n, seq);
+    if (pos_host_[seq] + n > opt_.max_seq)
+        return set_error(VSL_ERR_BOUNDS, "prefill: sequence %d at %d + %d positions exceeds max_seq %d", seq,
+                         pos_host_[seq], n, opt_.max_seq);
+    const vsl_model_config& c = cfg_;
+    CK(cudaSetDevice(opt_.device));
+    CK(cudaStreamSynchronize(stream_));
+    RC(alloc_prefill());
+    const int d = c.d_model, P = PF_ROWS;
+    const int p0 = pos_host_[seq];
+    for (int c0 = 0; c0 < n; c0 += P) {
+        const int nc = std::min(P, n - c0);
+        CK(cudaStreamSynchronize(stream_));  // the staging buffer is reused
+        for (int i = 0; i < nc; i++) {
+            pf_h_[i] = ids[c0 + i];
+            pf_h_[P + i] = p0 + c0 + i;
+            memcpy(pf_h_ + 2 * P + (size_t)i * max_pages_, pt_host_.data() + (size_t)seq * max_pages_,
+                   (size_t)max_pages_ * 4);
+        }
+        CK(cudaMemcpyAsync(pf_ids_, pf_h_, (2 * (size_t)P + (size_t)P * max_pages_) * 4, cudaMemcpyHostToDevice,
+                           stream_));
+        RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, pf_ids_, nc, pf_x_, nullptr, stream_));
+        StepBufs sb{pf_x_, pf_q_, pf_attn_, pf_act_, pf_pos_, pf_pages_, pf_fd_ws_, pf_fd_bytes_, pf_fdtc_ws_,
+                    pf_fdtc_bytes_, pf_tc_ws_ ? &pf_tc_route_ : nullptr, true};
+        RC(enqueue_layers(sb, nc));
+        if (c0 + nc == n) {  // the last prompt token: logits, greedy next token
+            CK(cudaMemsetAsync(pf_slot_, 0, 16, stream_));
+            RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, pf_x_ + (size_t)(nc - 1) * d, out_norm_, c.rms_eps, 1,
+                            pf_logits_, pf_slot_, v_off_, 0.0f, 0, step_, nullptr, 0, stream_));
+            if (p2p_ready_) {
+                RC(p2p_allreduce(p2p_s_, pf_slot_, 1, 1, stream_));
+            } else if (nccl_) {
+                ncclResult_t r = ncclAllReduce(pf_slot_, pf_slot_, 1, ncclUint64, ncclMax, (ncclComm_t)nccl_, stream_);
+                if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));
+            }
+            RC(prefill_finish_impl(pf_slot_, ids_, pos_, seq, p0 + n, pf_next_, stream_));
+        }
+    }
+    const float* lsrc = pf_logits_;
+    if (out_logits && nccl_) {
+        ncclResult_t r = ncclAllGather(pf_logits_, logits_full_, (size_t)v_l_, ncclFloat, (ncclComm_t)nccl_, stream_);
+        if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllGather(logits): %s", ncclGetErrorString(r));
+        lsrc = logits_full_;  // [rank][v_l] = [vocab]
+    }
+    if (out_logits) CK(cudaMemcpyAsync(h_logits_, lsrc, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaMemcpyAsync(h_out_, pf_next_, 4, cudaMemcpyDeviceToHost, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    if (next_id) *next_id = h_out_[0];
+    if (out_logits) memcpy(out_logits, h_logits_, (size_t)c.vocab * 4);
+    pos_host_[seq] = p0 + n;
     return VSL_OK;
 }
 

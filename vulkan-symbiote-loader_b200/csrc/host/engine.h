@@ -53,6 +53,11 @@ public:
     int set_forced(const int32_t* ids, int n_steps, int B);
     int run(int n_steps, int B, float temperature, uint64_t seed);
     int step_host(const int32_t* ids, int B, int32_t* out_ids, float* out_logits);
+    // Prompt pass: positions pos..pos+n-1 of sequence `seq` run as up to 64 rows at a time
+    // (tensor-core projections, causal attention through per-row positions over the sequence's
+    // pages); writes their KV and leaves `seq` ready to decode the token sampled greedily from
+    // the last prompt token's logits.
+    int prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits);
     int read_tokens(int n, int B, int32_t* out);
     int positions(int B, int32_t* out);
     int generate(const int32_t* prompt, int n_prompt, int max_new, float temperature, uint64_t seed,
@@ -80,7 +85,44 @@ private:
     bool fused_supported(int B) const;
     int enqueue_fused_step(int B, float temperature, uint64_t seed);
     int get_graph(int B, float temperature, uint64_t seed, cudaGraphExec_t* exec);
-    int allreduce_x(int B);
+    // buffers of one pass over the decoder layers (decode step or prefill chunk)
+    struct StepBufs {
+        float* x;
+        float* q;
+        float* attn;
+        float* act;
+        int32_t* pos;
+        int32_t* pages;
+        void* fd_ws;
+        size_t fd_bytes;
+        void* fdtc_ws;
+        size_t fdtc_bytes;
+        const TcRoute* tc;
+        bool shared_pages;  // rows are consecutive positions of one sequence (prompt chunk)
+    };
+    int enqueue_layers(const StepBufs& sb, int B);
+    static constexpr int PF_ROWS = 64;  // prompt rows per prefill chunk
+    int alloc_prefill();
+    void* pf_mem_ = nullptr;
+    int32_t* pf_ids_ = nullptr;   // [PF] ids, then [PF] positions, then [PF][max_pages] page rows
+    int32_t* pf_pos_ = nullptr;
+    int32_t* pf_pages_ = nullptr;
+    float* pf_x_ = nullptr;
+    float* pf_q_ = nullptr;
+    float* pf_attn_ = nullptr;
+    float* pf_act_ = nullptr;
+    float* pf_logits_ = nullptr;
+    unsigned long long* pf_slot_ = nullptr;
+    int32_t* pf_next_ = nullptr;
+    int32_t* pf_h_ = nullptr;     // pinned staging of ids / positions / page rows
+    void* pf_fd_ws_ = nullptr;
+    size_t pf_fd_bytes_ = 0;
+    void* pf_fdtc_ws_ = nullptr;
+    size_t pf_fdtc_bytes_ = 0;
+    void* pf_tc_ws_ = nullptr;
+    TcRoute pf_tc_route_ = {};
+    std::vector<int32_t> pt_host_;  // host copy of the page table
+    int allreduce_sum(float* buf, int count);
     int check_cuda(cudaError_t e, const char* what);
     int device_of_layer(int l) const;
 

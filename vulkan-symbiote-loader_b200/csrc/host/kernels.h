@@ -39,7 +39,8 @@ int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, 
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
-                      size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes);
+                      size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
+                      bool shared_pages = false);
 size_t flash_decode_tc_workspace_bytes(int B, int n_kv);
 bool flash_decode_tc_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int B, int page_size);
 int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages,
@@ -52,6 +53,8 @@ int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start
 int finalize_impl(const unsigned long long* slots, int B, int32_t* ids, int32_t* pos, int32_t* step_counter,
                   const int32_t* forced, const int32_t* n_forced, int32_t* log, int log_cap, int32_t* sampled_out,
                   int max_pos, int* status, cudaStream_t st);
+int prefill_finish_impl(const unsigned long long* slot, int32_t* ids, int32_t* pos, int seq, int new_pos,
+                        int32_t* next_out, cudaStream_t st);
 int sm_count();
 bool pdl_enabled();
 void set_pdl_enabled(bool on);

@@ -42,6 +42,7 @@ struct FdParams {
     int* counters; // [B][n_kv]
     const void* pf_ptr;  // weights of the projection that follows (prefetched into L2)
     size_t pf_bytes;
+    int wait_first;      // rows share one sequence's pages (prompt chunk): no cache read before the wait
 };
 
 template <typename KT> struct KvVec;
@@ -94,9 +95,11 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int G = p.n_heads / p.n_kv;
 
-    // pos[] and the cache below position pos were written by kernels that finished before the
-    // immediate predecessor started, so they are read before griddepcontrol.wait; the
-    // predecessor (the QKV projection) writes q and the key/value row at pos.
+    // In decode, pos[] and the cache below position pos were written by kernels that finished
+    // before the immediate predecessor started, so they are read before griddepcontrol.wait; the
+    // predecessor (the QKV projection) writes q and the key/value row at pos. When the rows are
+    // consecutive positions of one sequence (a prompt chunk), the predecessor also wrote the
+    // rows below pos, so the kernel waits first (wait_first).
     // Positions past the page table or the grid's coverage are never read (the QKV kernel
     // has already flagged such a position in the engine's status word).
     const int pos = p.pos[b];
@@ -114,6 +117,7 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
     const int n_active = (len + p.split_len - 1) / p.split_len;
     const int n_chunks = (t_end - t_begin + FD_CHUNK - 1) / FD_CHUNK;
     const int new_row = pos - t_begin;  // row of the freshly appended position, if in this split
+    if (p.wait_first) pdl_wait();
 
     auto chunk_ptrs = [&](int ci, const KT*& kg, const KT*& vg) {
         const int t0 = t_begin + ci * FD_CHUNK;  // t0 % 64 == 0 and page_size % 64 == 0: one page
@@ -336,7 +340,8 @@ static int launch_fd(const FdParams& p, cudaStream_t st) {
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
-                      size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes) {
+                      size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
+                      bool shared_pages) {
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
         return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
     if (B <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > FD_GMAX)
@@ -363,6 +368,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
     p.counters = reinterpret_cast<int*>(w);
     p.pf_ptr = pf_ptr;
     p.pf_bytes = pf_bytes;
+    p.wait_first = shared_pages ? 1 : 0;
     if (kvdtype == VSL_F16) {
         if (head_dim == 128) return launch_fd<128, __half>(p, stream);
         if (head_dim == 64) return launch_fd<64, __half>(p, stream);
@@ -389,7 +395,7 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0);
+                                  (cudaStream_t)stream, nullptr, 0, true);  // the caller's rows may share pages
 }
 
 // ---------------------------------------------------------------------------------------
@@ -457,5 +463,5 @@ extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, con
     if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, ws, FD_STATIC_SCRATCH_BYTES,
-                                  (cudaStream_t)stream, nullptr, 0);
+                                  (cudaStream_t)stream, nullptr, 0, true);  // the caller's rows may share pages
 }

@@ -247,6 +247,27 @@ int finalize_impl(const unsigned long long* slots, int B, int32_t* ids, int32_t*
                          "finalize");
 }
 
+// End of a prefill: sequence `seq` continues from position new_pos with the token sampled from
+// the prompt's last logits (the argmax key in `slot`).
+__global__ void prefill_finish_kernel(const unsigned long long* __restrict__ slot, int32_t* ids, int32_t* pos, int seq,
+                                      int new_pos, int32_t* next_out) {
+    pdl_wait();
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        const unsigned long long s = *slot;
+        const int32_t id = s ? (int32_t)unpack_argmax_idx(s) : 0;
+        ids[seq] = id;
+        pos[seq] = new_pos;
+        *next_out = id;
+    }
+}
+
+int prefill_finish_impl(const unsigned long long* slot, int32_t* ids, int32_t* pos, int seq, int new_pos,
+                        int32_t* next_out, cudaStream_t st) {
+    return launch_status(launch_k(prefill_finish_kernel, dim3(1), dim3(32), 0, st, slot, ids, pos, seq, new_pos, next_out),
+                         "prefill finish");
+}
+
 }  // namespace vsl
 
 using namespace vsl;

@@ -97,6 +97,7 @@ def lib() -> C.CDLL:
         "vsl_engine_set_trace": (i32, [vp, i32]),
         "vsl_engine_read_trace": (i32, [vp, i32, C.POINTER(C.c_uint64), C.POINTER(i32)]),
         "vsl_engine_memory_stats": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+        "vsl_engine_prefill": (i32, [vp, vp, i32, i32, C.POINTER(i32), vp]),
         "vsl_engine_residency": (i32, [vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(u64),
                                        C.POINTER(u64)]),
         "vsl_pack_plan": (i32, [u64, C.c_uint32, u64, f64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
@@ -370,6 +371,16 @@ class Engine:
         w, kv, o = C.c_size_t(), C.c_size_t(), C.c_size_t()
         check(lib().vsl_engine_memory_stats(self.h, C.byref(w), C.byref(kv), C.byref(o)))
         return dict(weights=w.value, kv=kv.value, other=o.value)
+
+    def prefill(self, ids, seq: int = 0, want_logits: bool = False):
+        """Prompt pass for sequence `seq`; returns (next id, logits of the last prompt token or None)."""
+        import numpy as np
+        a = np.ascontiguousarray(ids, dtype=np.int32).reshape(-1)
+        nxt = C.c_int()
+        lg = np.empty(self.config["vocab"], np.float32) if want_logits else None
+        check(lib().vsl_engine_prefill(self.h, a.ctypes.data, a.size, seq, C.byref(nxt),
+                                       lg.ctypes.data if lg is not None else None))
+        return nxt.value, lg
 
     def residency(self) -> dict:
         """Weight residency under the HBM budget (layers kept in HBM / streamed each step)."""
