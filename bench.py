@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
                          "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads")
+    ap.add_argument("--profile-shape", default="32000,4096,16",
+                    help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     return ap.parse_args()
@@ -263,9 +265,19 @@ def run_ours(args):
         eng.set_forced(synth.synth_ids(SEED, 0, B, cfg["vocab"]).reshape(1, B))
         eng.run(1, batch=B)
     else:
+        # prompt positions 0..127 through the prompt pass (two chunks of 64 rows); time to first
+        # token through the host API (ids in, first sampled id out), the median of 3 after one
+        # untimed call, each from an empty cache
         prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
-        eng.set_forced(prompt)
-        eng.run(PROMPT)  # prompt positions 0..127 (token-by-token prefill through the decode graph)
+        ttft = []
+        for i in range(4):
+            eng.reset()
+            if dist:
+                dist.barrier()
+            t_p = time.perf_counter()
+            eng.prefill(prompt)
+            ttft.append(time.perf_counter() - t_p)
+        ttft_s = vdist.max_over_ranks(dist, sorted(ttft[1:])[1])
     eng.run(args.warmup, batch=B)
     stream = eng.stream
     s = torch.cuda.ExternalStream(stream)
@@ -287,7 +299,7 @@ def run_ours(args):
     _, bytes_end = eng.step_stats(B)
     status = eng.device_status()
     # end to end through the host API: pinned host ids in, sampled ids back, every step
-    n_log = (1 if big else PROMPT) + args.warmup + args.steps
+    n_log = (1 if big else 0) + args.warmup + args.steps
     nxt = np.asarray(eng.read_tokens(n_log, batch=B)[-1], np.int32).reshape(B)
     for _ in range(2):
         nxt, _ = eng.step_host(nxt)
@@ -339,7 +351,7 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init weights filled in HBM)",
-            "config": {"workload": "7B Llama shape fp16 (BASELINE configs[1]), batch 1, 128-token prompt, "
+            "config": {"workload": "7B Llama shape fp16 (BASELINE configs[1]), batch 1, 128-token prompt (prefill), "
                                    f"decode positions {PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
                        "model": "llama-7b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
                        "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps,
@@ -353,6 +365,9 @@ def run_ours(args):
                               "tok_s_at_peak": round(hbm_peak * 1e9 / step_bytes, 1)},
             "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
             "clocks": clk.summary(), "load_seconds": round(load_s, 2),
+            "prefill": {"prompt_tokens": PROMPT, "ttft_ms": round(ttft_s * 1e3, 3),
+                        "tok_s": round(PROMPT / ttft_s, 1), "api": "vsl_engine_prefill",
+                        "timing": "host wall clock, median of 3 warm calls, max over ranks"},
         }
         if cb:
             line["cpu_baseline"] = cb
@@ -515,15 +530,16 @@ def run_profile_case(args):
 
     import vsl
     if args.profile_case == "tc_gemm":
-        N, K, B = 32000, 4096, 16
-        Ws = [torch.randn(N, K, device="cuda").mul_(0.02).half() for _ in range(2)]
+        N, K, B = (int(v) for v in args.profile_shape.split(","))
+        # enough weight copies that every launch reads its weights from HBM (more than L2)
+        Ws = [torch.randn(N, K, device="cuda").mul_(0.02).half() for _ in range(max(2, -(-300_000_000 // (N * K * 2))))]
         x = torch.randn(B, K, device="cuda")
         y = torch.zeros(B, N, device="cuda")
         n = vsl.skinny_gemm_tc_workspace_size(N, K, B)
         wst = torch.zeros(n // 4 + 512, dtype=torch.int32, device="cuda")
         ws = (wst.data_ptr() + 1023) // 1024 * 1024
         for i in range(3):
-            vsl.skinny_gemm_tc(vsl.F16, Ws[i % 2], N, K, x, B, y, vsl.EPI_STORE, None, 0.0, ws, n)
+            vsl.skinny_gemm_tc(vsl.F16, Ws[i % len(Ws)], N, K, x, B, y, vsl.EPI_STORE, None, 0.0, ws, n)
     else:
         B, nh, nkv, L, page = 16, 32, 8, 8192, 64
         mp = L // page

@@ -141,12 +141,11 @@ def test_device_loop_matches_host_loop():
                rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.BF16)
     prompt = synth.synth_ids(8, 0, 10, cfg["vocab"])
     with vsl.Engine.synthetic(cfg, seed=8, max_seq=128) as e:
-        dev_ids = e.generate(prompt, 30)
+        dev_ids = e.generate(prompt, 30)  # prompt pass, then graph-launched steps
         e.reset()
         host = []
-        nxt = None
-        for t in prompt:
-            nxt, _ = e.step_host([t])
+        first, _ = e.prefill(prompt)
+        nxt = [first]
         for _ in range(30):
             host.append(int(nxt[0]))
             nxt, _ = e.step_host([host[-1]])

@@ -905,7 +905,8 @@ int DecodeEngine::alloc_prefill() {
     return VSL_OK;
 }
 
-int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits) {
+int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits, float temperature,
+                          uint64_t seed) {
     if (!ids || n <= 0 || seq < 0 || seq >= opt_.max_batch)
         return set_error(VSL_ERR_INVALID, "prefill: %d ids for sequence %d", n, seq);
     if (pos_host_[seq] + n > opt_.max_seq)
@@ -935,7 +936,7 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
         if (c0 + nc == n) {  // the last prompt token: logits, greedy next token
             CK(cudaMemsetAsync(pf_slot_, 0, 16, stream_));
             RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, pf_x_ + (size_t)(nc - 1) * d, out_norm_, c.rms_eps, 1,
-                            pf_logits_, pf_slot_, v_off_, 0.0f, 0, step_, nullptr, 0, stream_));
+                            pf_logits_, pf_slot_, v_off_, temperature, seed, step_, nullptr, 0, stream_));
             if (p2p_ready_) {
                 RC(p2p_allreduce(p2p_s_, pf_slot_, 1, 1, stream_));
             } else if (nccl_) {
@@ -1030,34 +1031,33 @@ int DecodeEngine::generate(const int32_t* prompt, int n_prompt, int max_new, flo
     *n_out = 0;
     if (max_new == 0) return VSL_OK;
     RC(reset());
-    RC(set_forced(prompt, n_prompt, 1));
-    const int total = n_prompt + max_new - 1;
-    int done = 0, emitted = 0;
-    // prompt steps, then decode in chunks so stop ids can end the loop early
-    const int chunk = n_stop > 0 ? 16 : total;
+    // the prompt in one prompt pass (chunks of 64 rows), which also samples the first new
+    // token; then one graph-launched decode step per token, in chunks of 16 when stop ids can
+    // end the loop early
+    auto is_stop = [&](int32_t t) {
+        for (int s = 0; s < n_stop; s++)
+            if (t == stop_ids[s]) return true;
+        return false;
+    };
+    RC(prefill(prompt, n_prompt, 0, &out_ids[0], nullptr, temperature, seed));
+    *n_out = 1;
+    if (is_stop(out_ids[0])) return VSL_OK;
+    const int total = max_new - 1;
+    const int chunk = n_stop > 0 ? 16 : std::max(total, 1);
     std::vector<int32_t> log;
+    int done = 0;
     while (done < total) {
         const int n = std::min(chunk, total - done);
         RC(run(n, 1, temperature, seed));
-        done += n;
-        if (done < n_prompt) continue;
-        log.resize(done);
-        RC(read_tokens(done, 1, log.data()));
-        emitted = done - (n_prompt - 1);
-        for (int i = 0; i < emitted && n_stop > 0; i++) {
-            const int32_t t = log[n_prompt - 1 + i];
-            for (int s = 0; s < n_stop; s++)
-                if (t == stop_ids[s]) {
-                    for (int k = 0; k <= i; k++) out_ids[k] = log[n_prompt - 1 + k];
-                    *n_out = i + 1;
-                    return VSL_OK;
-                }
+        log.resize(done + n);
+        RC(read_tokens(done + n, 1, log.data()));
+        for (int i = done; i < done + n; i++) {
+            out_ids[1 + i] = log[i];
+            *n_out = 2 + i;
+            if (is_stop(log[i])) return VSL_OK;
         }
+        done += n;
     }
-    log.resize(total);
-    RC(read_tokens(total, 1, log.data()));
-    for (int k = 0; k < max_new; k++) out_ids[k] = log[n_prompt - 1 + k];
-    *n_out = max_new;
     return VSL_OK;
 }
 

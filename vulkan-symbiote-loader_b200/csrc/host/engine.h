@@ -57,7 +57,8 @@ public:
     // (tensor-core projections, causal attention through per-row positions over the sequence's
     // pages); writes their KV and leaves `seq` ready to decode the token sampled greedily from
     // the last prompt token's logits.
-    int prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits);
+    int prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits, float temperature = 0.0f,
+                uint64_t seed = 0);
     int read_tokens(int n, int B, int32_t* out);
     int positions(int B, int32_t* out);
     int generate(const int32_t* prompt, int n_prompt, int max_new, float temperature, uint64_t seed,

@@ -13,13 +13,20 @@
 // CTA roles (192 threads, one CTA per SM, persistent over a stream-K share of the work):
 //   warp 0     TMA producer: W tile (128 x 64, 128-byte swizzle) and X2 tile (2Bp x 64) per
 //              k-block into a ring of shared-memory stages (mbarrier complete_tx);
-//   warp 1     allocates the TMEM accumulator (2Bp fp32 columns x 128 lanes) and one lane
-//              issues tcgen05.mma (M=128, N=2Bp, K=16; 4 per k-block), committing each stage
+//   warp 1     allocates two TMEM accumulators (2Bp fp32 columns x 128 lanes each, so the
+//              MMAs of one segment overlap the epilogue of the previous one) and one lane
+//              issues tcgen05.mma (M=128, N=2Bp, K=16; 8 per k-block), committing each stage
 //              back to the producer and each finished segment to the epilogue;
 //   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (= rows), hi + lo, then either the
 //              projection epilogue directly (a segment that covers all of K) or a partial to
-//              the workspace; the last CTA to finish a split row tile sums the partials in a
-//              fixed order (deterministic) and runs the epilogue.
+//              the workspace plus an arrival on the row tile's counter.
+// Split row tiles: at 32 or more activation rows, when each row tile is shared by two or
+// more CTAs, they are finished by all of their CTAs together: after its own stream, each contributing CTA waits (bounded) until every
+// contributor of the tile has arrived, then sums the partials of its own 1/s share of the
+// batch rows in CTA order (deterministic) and runs the epilogue for them. The grid never
+// exceeds the SM count and a CTA fills an SM, so all contributors are resident together; a
+// CTA waits only after all of its own MMAs are done. Otherwise the sum is short, and the last
+// CTA to arrive sums all rows (same order) while the others leave.
 // Work split (stream-K): the flattened sequence of (row tile, k-block) pairs is cut into
 // gridDim.x equal ranges, one per CTA, so every SM streams the same number of weight bytes.
 // Every wait is bounded (one second); on expiry the kernel records VSL_ERR_TIMEOUT, lets its
@@ -54,9 +61,10 @@ struct TcArgs {
     long long T;         // n_rt * nkb
     int stages, stage_bytes, b_atom, b_bytes;  // X2 bytes per atom and per stage
     uint32_t idesc;      // tcgen05 instruction descriptor
-    int tmem_cols;
+    int tmem_cols;       // columns of one accumulator (two are allocated)
+    int dist_fixup;      // split tiles finished by all contributors (else by the last to arrive)
     float* ws;           // [gridDim.x][2][Bp][128] split-tile partials
-    int* counters;       // [n_rt] arrivals per split row tile (zero between launches)
+    int* counters;       // [2][n_rt] arrivals and finished fixups per split row tile (zero between launches)
     int* status;         // VSL_ERR_TIMEOUT on an expired wait (nullable)
     GemvParams ep;       // epilogue parameters (y, residual, RoPE/KV, sampler)
 };
@@ -188,14 +196,15 @@ __global__ void __launch_bounds__(256) xsplit_kernel(const float* __restrict__ x
 constexpr int TC_EB = 16;
 
 template <int EK>
-__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int row, const float* v, int step) {
+__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int b_end, int row, const float* v,
+                                                  int step) {
     const int lane = threadIdx.x & 31;
     float v1[TC_EB];
 #pragma unroll
     for (int j = 0; j < TC_EB; j++) v1[j] = __shfl_down_sync(0xffffffffu, v[j], 1);
     const bool act = !(lane & 1) && row < a.N;
     const bool has1 = row + 1 < a.N;
-    const int nb = a.B - b0 < TC_EB ? a.B - b0 : TC_EB;
+    const int nb = b_end - b0 < TC_EB ? b_end - b0 : TC_EB;
     unsigned long long best[EK == EK_LMHEAD ? TC_EB : 1];
 #pragma unroll
     for (int j = 0; j < (EK == EK_LMHEAD ? TC_EB : 1); j++) best[j] = 0ull;
@@ -232,13 +241,45 @@ __device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int r
     }
 }
 
+// Sum of the partials of split row tile rt from CTAs first..lastc (in CTA order: the result
+// does not depend on arrival order) for activation rows [bs0, bs1), then the epilogue.
+template <int EK>
+__device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, int G, int rt, int first, int lastc, int bs0, int bs1,
+                                              int row, int rloc, int step) {
+    for (int b0 = bs0; b0 < bs1; b0 += TC_EB) {
+        // TC_EB rows x 4 CTAs of loads are in flight at a time
+        float v[TC_EB];
+#pragma unroll
+        for (int j = 0; j < TC_EB; j++) v[j] = 0.0f;
+        for (int c0 = first; c0 <= lastc; c0 += 4) {
+            float t[4][TC_EB];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int cc = c0 + u;
+                if (cc <= lastc) {
+                    const int slot = sk_lo(a.T, G, cc) >= (long long)rt * a.nkb ? 0 : 1;
+                    const float* src = a.ws + (((size_t)cc * 2 + slot) * a.Bp + b0) * TC_BM + rloc;
+#pragma unroll
+                    for (int j = 0; j < TC_EB; j++) t[u][j] = b0 + j < bs1 ? __ldcg(src + (size_t)j * TC_BM) : 0.0f;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (c0 + u <= lastc)
+#pragma unroll
+                    for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
+        }
+        tc_epilogue_chunk<EK>(a, b0, bs1, row, v, step);
+    }
+}
+
 template <int EK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ TcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[TC_MAX_STAGES], empty[TC_MAX_STAGES];
-    __shared__ __align__(8) uint64_t tmem_full, tmem_empty;
+    __shared__ __align__(8) uint64_t tmem_full[2], tmem_empty[2];
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
     __shared__ int last_s;
@@ -254,16 +295,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(&tmem_full, 1);
-        mbar_init(&tmem_empty, 4);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tmem_full[i], 1);
+            mbar_init(&tmem_empty[i], 4);
+        }
         mbar_fence_init();
         abort_s = 0;
         tmap_prefetch(&map_w);
         tmap_prefetch(&map_x);
     }
-    if (warp == 1) {  // TMEM accumulator: 128 lanes x tmem_cols fp32 columns
+    if (warp == 1) {  // two TMEM accumulators: 128 lanes x tmem_cols fp32 columns each
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
-                     "r"(a.tmem_cols)
+                     "r"(2 * a.tmem_cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -344,11 +387,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             bool ok = true;
             bool committed = false;
             while (ok && next_segment(a, f, f1, f0, sg)) {
-                if (si > 0 && !mbar_wait(&tmem_empty, (uint32_t)((si - 1) & 1))) {
+                const int buf = si & 1;
+                // accumulator buf was last used by segment si - 2
+                if (si >= 2 && !mbar_wait(&tmem_empty[buf], (uint32_t)(((si >> 1) - 1) & 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(buf * a.tmem_cols);
                 for (int kb = sg.kb0; kb < sg.kb1; kb++, it++) {
                     if (!mbar_wait(&full[s], fpar) || (((int)it & 15) == 0 && ld_abort(&abort_s))) {
                         ok = false;
@@ -361,7 +407,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         const uint64_t ad = sw128_desc(sa + at * TC_A_ATOM), bd = sw128_desc(sb + at * a.b_atom);
 #pragma unroll
                         for (int k = 0; k < TC_ATOM / 16; k++)  // +32 bytes per 16 values inside the atom
-                            tc_mma(tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), a.idesc,
+                            tc_mma(acc, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), a.idesc,
                                    (kb > sg.kb0 || at > 0 || k > 0) ? 1u : 0u);
                     }
                     tc_commit(&empty[s]);  // frees the stage once these MMAs have read it
@@ -371,7 +417,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     }
                 }
                 if (!ok) break;
-                tc_commit(&tmem_full);
+                tc_commit(&tmem_full[buf]);
                 committed = true;
                 si++;
             }
@@ -380,7 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 atomicExch(&abort_s, 1);
             }
             // the accumulator must not be freed under a running MMA
-            if (committed) mbar_wait(&tmem_full, (uint32_t)((si - 1) & 1));
+            if (committed) mbar_wait(&tmem_full[(si - 1) & 1], (uint32_t)(((si - 1) >> 1) & 1));
         }
         __syncwarp();
     } else {
@@ -395,28 +441,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         long long f = f0;
         int si = 0;
         Segment sg;
+        int n_split = 0, split_rt[2] = {0, 0};  // split tiles of this CTA: only its first and last segment
+        bool aborted = false;
         while (next_segment(a, f, f1, f0, sg)) {
+            const int buf = si & 1;
             {
                 // the four epilogue warps leave together (they meet at named barriers below)
-                const bool bad = !mbar_wait(&tmem_full, (uint32_t)(si & 1)) || ld_abort(&abort_s);
+                const bool bad = !mbar_wait(&tmem_full[buf], (uint32_t)((si >> 1) & 1)) || ld_abort(&abort_s);
                 if (named_barrier_or(1, 128, bad)) {
                     set_status(a.status, VSL_ERR_TIMEOUT);
                     atomicExch(&abort_s, 1);
+                    aborted = true;
                     break;
                 }
             }
             tc_fence_after();
             const int row = sg.rt * TC_BM + rloc;
             float* wsp = a.ws + ((size_t)c * 2 + sg.slot) * a.Bp * TC_BM;
+            const uint32_t tl = tmem + (uint32_t)(buf * a.tmem_cols) + ((uint32_t)(q * 32) << 16);
             for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
                 float hi[TC_EB], lo[TC_EB];
-                const uint32_t tl = tmem + ((uint32_t)(q * 32) << 16);
                 tmem_ld16(tl + (uint32_t)b0, hi);
                 tmem_ld16(tl + (uint32_t)(a.Bp + b0), lo);
 #pragma unroll
                 for (int i = 0; i < TC_EB; i++) hi[i] += lo[i];
                 if (sg.full) {
-                    tc_epilogue_chunk<EK>(a, b0, row, hi, step);
+                    tc_epilogue_chunk<EK>(a, b0, a.B, row, hi, step);
                 } else {
 #pragma unroll
                     for (int i = 0; i < TC_EB; i++)
@@ -426,50 +476,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // accumulator read: hand TMEM back to the MMA warp
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tmem_empty);
+            if (lane == 0) mbar_arrive(&tmem_empty[buf]);
             si++;
             if (!sg.full) {
-                // split row tile: the last of its CTAs to arrive reduces, in CTA order
+                // partial written: arrive on the row tile (release after the CTA's stores)
                 __threadfence();
                 named_barrier_sync(1, 128);
-                if (et == 0) {
+                if (a.dist_fixup) {
+                    if (et == 0) atomicAdd(a.counters + sg.rt, 1);
+                    split_rt[n_split++] = sg.rt;
+                } else {
                     const int first = sk_owner(a.T, G, (long long)sg.rt * a.nkb);
                     const int lastc = sk_owner(a.T, G, (long long)sg.rt * a.nkb + a.nkb - 1);
-                    const int prev = atomicAdd(a.counters + sg.rt, 1);
-                    last_s = prev == lastc - first ? 1 : 0;
-                }
-                named_barrier_sync(1, 128);
-                if (last_s) {
-                    __threadfence();
-                    const int first = sk_owner(a.T, G, (long long)sg.rt * a.nkb);
-                    const int lastc = sk_owner(a.T, G, (long long)sg.rt * a.nkb + a.nkb - 1);
-                    // partials of CTAs first..lastc, summed in CTA order; TC_EB rows x 4 CTAs
-                    // of loads are in flight at a time
-                    for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
-                        float v[TC_EB];
-#pragma unroll
-                        for (int j = 0; j < TC_EB; j++) v[j] = 0.0f;
-                        for (int c0 = first; c0 <= lastc; c0 += 4) {
-                            float t[4][TC_EB];
-#pragma unroll
-                            for (int u = 0; u < 4; u++) {
-                                const int cc = c0 + u;
-                                if (cc <= lastc) {
-                                    const int slot = sk_lo(a.T, G, cc) >= (long long)sg.rt * a.nkb ? 0 : 1;
-                                    const float* src = a.ws + (((size_t)cc * 2 + slot) * a.Bp + b0) * TC_BM + rloc;
-#pragma unroll
-                                    for (int j = 0; j < TC_EB; j++) t[u][j] = b0 + j < a.B ? __ldcg(src + (size_t)j * TC_BM) : 0.0f;
-                                }
-                            }
-#pragma unroll
-                            for (int u = 0; u < 4; u++)
-                                if (c0 + u <= lastc)
-#pragma unroll
-                                    for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
-                        }
-                        tc_epilogue_chunk<EK>(a, b0, row, v, step);
+                    if (et == 0) last_s = atomicAdd(a.counters + sg.rt, 1) == lastc - first ? 1 : 0;
+                    named_barrier_sync(1, 128);
+                    if (last_s) {
+                        __threadfence();
+                        tc_fixup_rows<EK>(a, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
+                        if (et == 0) a.counters[sg.rt] = 0;
                     }
-                    if (et == 0) a.counters[sg.rt] = 0;
+                }
+            }
+        }
+        // fixup of the split tiles: contributor k of s sums batch rows [B k / s, B (k + 1) / s)
+        for (int i = 0; i < n_split && !aborted; i++) {
+            const int rt = split_rt[i];
+            const int first = sk_owner(a.T, G, (long long)rt * a.nkb);
+            const int lastc = sk_owner(a.T, G, (long long)rt * a.nkb + a.nkb - 1);
+            const int ns = lastc - first + 1, k = c - first;
+            bool bad = false;
+            if (et == 0) {
+                const volatile int* cnt = a.counters + rt;
+                bool ok = *cnt >= ns;
+                if (!ok) {
+                    const unsigned long long t0 = globaltimer_ns();
+                    while (!ok) {
+                        for (int r = 0; r < 32 && !ok; r++) ok = *cnt >= ns;
+                        if (!ok && (globaltimer_ns() - t0 > WAIT_LIMIT_NS || ld_abort(&abort_s))) break;
+                    }
+                }
+                bad = !ok;
+            }
+            if (named_barrier_or(1, 128, bad)) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+                break;
+            }
+            __threadfence();
+            tc_fixup_rows<EK>(a, G, rt, first, lastc, (int)((long long)a.B * k / ns),
+                              (int)((long long)a.B * (k + 1) / ns), rt * TC_BM + rloc, rloc, step);
+            // the last contributor through here clears the tile's counters for the next launch
+            // (every contributor has seen all arrivals by now)
+            if (et == 0) {
+                const int prev = atomicAdd(a.counters + a.n_rt + rt, 1);
+                if (prev == ns - 1) {
+                    a.counters[rt] = 0;
+                    a.counters[a.n_rt + rt] = 0;
                 }
             }
         }
@@ -480,7 +542,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * a.tmem_cols)
                      : "memory");
     }
 }
@@ -525,7 +587,7 @@ size_t tc_workspace_bytes(int N, int K, int B) {
     const int G = sm_count();
     const size_t x2 = (size_t)2 * Bp * K * 2;
     const size_t ws = (size_t)G * 2 * Bp * TC_BM * sizeof(float);
-    const size_t cnt = (size_t)((N + TC_BM - 1) / TC_BM) * sizeof(int);
+    const size_t cnt = (size_t)2 * ((N + TC_BM - 1) / TC_BM) * sizeof(int);
     auto up = [](size_t v) { return (v + 1023) / 1024 * 1024; };
     return up(x2) + up(ws) + up(cnt);
 }
@@ -593,7 +655,7 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     // the arrival counters sit at the tail of the workspace whatever the shape of the call, so
     // calls of different shapes sharing one workspace (sized for the largest N and K together)
     // never write split activations or partials over another shape's counters
-    const size_t cnt_bytes = (size_t)a.n_rt * sizeof(int);
+    const size_t cnt_bytes = (size_t)2 * a.n_rt * sizeof(int);
     a.counters = reinterpret_cast<int*>(w8 + ((ws_bytes - cnt_bytes) & ~(size_t)1023));
     a.status = status;
     a.ep = p;
@@ -601,6 +663,8 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
 
     int grid = G0;
     if ((long long)grid > a.T) grid = (int)a.T;
+    // many contributors per split tile (at least two CTAs per row tile) and a long sum
+    a.dist_fixup = a.B >= 32 && 2 * a.n_rt <= grid ? 1 : 0;
 
     CUtensorMap mw, mx;
     int rc = make_map(&mw, p.W, wdtype, p.N, p.K, TC_BM);
