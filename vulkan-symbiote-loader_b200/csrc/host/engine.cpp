@@ -888,7 +888,9 @@ int DecodeEngine::alloc_prefill() {
     RC(vsl_flash_decode_workspace_size(PF_ROWS, nh_l_, nkv_l_, c.head_dim, opt_.max_seq, split_len_, &pf_fd_bytes_));
     CK(cudaMalloc(&pf_fd_ws_, pf_fd_bytes_));
     CK(cudaMemset(pf_fd_ws_, 0, pf_fd_bytes_));
-    if (fdtc_ws_ && flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, PF_ROWS, page_size_)) {
+    // prompt chunks: 64 rows of one sequence over the same pages, so the tcgen05-score attention
+    // (one KV pass per row and KV head on the tensor cores) at every cache length
+    if (flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, PF_ROWS, page_size_)) {
         pf_fdtc_bytes_ = flash_decode_tc_workspace_bytes(PF_ROWS, nkv_l_);
         CK(cudaMalloc(&pf_fdtc_ws_, pf_fdtc_bytes_));
         CK(cudaMemset(pf_fdtc_ws_, 0, pf_fdtc_bytes_));
