@@ -117,6 +117,7 @@ private:
     ModelConfig config_;
     PerformanceMetrics performance_metrics_;
     uint32_t max_seq_ = 0;
+    uint32_t max_batch_ = 1;
     double peak_vram_gb_ = 0.0;
 };
 

@@ -301,6 +301,20 @@ VSL_API int vsl_engine_memory_stats(vsl_engine* e, size_t* weight_bytes, size_t*
  * continues with vsl_engine_run / vsl_engine_step_host. */
 VSL_API int vsl_engine_prefill(vsl_engine* e, const int32_t* ids, int n, int seq, int32_t* next_id, float* logits);
 
+/* Batched serving (the reference's generate_text_batch, VulkanSymbioteEngine.cpp:850-935, loops
+ * over its prompts one at a time): prompts = n_seq prompts concatenated, lens[b] ids each
+ * (n_seq <= max_batch). Each sequence gets its own prompt pass, then all decode together, one
+ * graph-launched step per token for the whole batch. out_ids[b * max_new + k] receives sequence
+ * b's ids, n_out[b] how many (a sequence ends after emitting one of stop_ids). */
+VSL_API int vsl_engine_generate_batch(vsl_engine* e, const int32_t* prompts, const int* lens, int n_seq, int max_new,
+                                      float temperature, uint64_t seed, const int32_t* stop_ids, int n_stop,
+                                      int32_t* out_ids, int* n_out);
+
+/* Continuous batching: free sequence slot `seq` (position 0; the other slots keep their state),
+ * then vsl_engine_prefill(e, new_prompt, n, seq, ...) admits a new request into it while the
+ * others continue to decode through vsl_engine_run. */
+VSL_API int vsl_engine_reset_seq(vsl_engine* e, int seq);
+
 /* Weight residency under vram_budget_gb (replaces PackManager::get_vram_stats and the pack
  * scheduler's state, NomadPack.cpp:1190-1249, 1323-1326; VulkanSymbioteEngine.cpp:1555-1599):
  * layers 0..resident_layers-1 stay in HBM, the other streamed_layers live in pinned host memory

@@ -79,6 +79,15 @@ int main(int argc, char** argv) {
             threw = true;
         }
         printf(",\"overflow_throws\":%d", threw);
+        // generate_text_batch decodes its prompts together (max_batch 3): same text as one at a time
+        const std::vector<std::string> prompts = {"ab c", "xyz", "hello there b"};
+        std::vector<std::string> one;
+        for (const auto& p : prompts) one.push_back(engine.generate(p, 12));
+        DeviceOptions ob = o;
+        ob.max_batch = 3;
+        VulkanSymbioteEngine batched(model, ob);
+        const auto many = batched.generate_text_batch(prompts, 12);
+        printf(",\"batch_equal\":%d", (int)(many == one));
     }
     printf("}\n");
     return 0;

@@ -64,3 +64,4 @@ def test_engine_generate_matches_golden(api_bin, config_file, golden, fixture_gg
     assert out["bench_tok_s"] > 0 and out["kv_bytes"] > 0 and out["vram_used"] > out["kv_bytes"]
     assert out["tok_s_metric"] > 0 and out["gbps"] > 0
     assert out["overflow_throws"] == 1
+    assert out["batch_equal"] == 1  # generate_text_batch (batched decode) == per-prompt generate

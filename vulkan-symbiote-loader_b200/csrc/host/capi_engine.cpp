@@ -236,6 +236,22 @@ extern "C" int vsl_engine_prefill(vsl_engine* e, const int32_t* ids, int n, int 
     GUARD_END
 }
 
+extern "C" int vsl_engine_reset_seq(vsl_engine* e, int seq) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    return e->impl->reset_seq(seq);
+    GUARD_END
+}
+
+extern "C" int vsl_engine_generate_batch(vsl_engine* e, const int32_t* prompts, const int* lens, int n_seq,
+                                         int max_new, float temperature, uint64_t seed, const int32_t* stop_ids,
+                                         int n_stop, int32_t* out_ids, int* n_out) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    return e->impl->generate_batch(prompts, lens, n_seq, max_new, temperature, seed, stop_ids, n_stop, out_ids, n_out);
+    GUARD_END
+}
+
 extern "C" int vsl_engine_residency(vsl_engine* e, uint32_t* resident_layers, uint32_t* streamed_layers,
                                     uint64_t* streamed_bytes_per_step, uint64_t* host_bytes) {
     if (int rc = check_engine(e)) return rc;

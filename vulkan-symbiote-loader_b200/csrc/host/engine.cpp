@@ -963,6 +963,80 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
     return VSL_OK;
 }
 
+int DecodeEngine::reset_seq(int seq) {
+    if (seq < 0 || seq >= opt_.max_batch) return set_error(VSL_ERR_INVALID, "reset_seq: sequence %d", seq);
+    CK(cudaSetDevice(opt_.device));
+    CK(cudaStreamSynchronize(stream_));
+    CK(cudaMemsetAsync(pos_ + seq, 0, 4, stream_));
+    CK(cudaMemsetAsync(ids_ + seq, 0, 4, stream_));
+    CK(cudaStreamSynchronize(stream_));
+    pos_host_[seq] = 0;
+    return VSL_OK;
+}
+
+// Batched generation (the reference's generate_text_batch, VulkanSymbioteEngine.cpp:850-935,
+// runs its prompts one after another): every sequence gets its own prompt pass into its own
+// pages, then all of them decode together, one graph-launched step per token for the whole
+// batch. A sequence that emits a stop id stops collecting ids; the batch ends when every
+// sequence has stopped or produced max_new ids.
+int DecodeEngine::generate_batch(const int32_t* prompts, const int* lens, int n_seq, int max_new, float temperature,
+                                 uint64_t seed, const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out) {
+    if (!prompts || !lens || !out_ids || !n_out || n_seq <= 0 || n_seq > opt_.max_batch || max_new < 0 ||
+        (n_stop > 0 && !stop_ids))
+        return set_error(VSL_ERR_INVALID, "generate_batch: %d sequences (max batch %d)", n_seq, opt_.max_batch);
+    int longest = 0;
+    for (int b = 0; b < n_seq; b++) {
+        if (lens[b] <= 0) return set_error(VSL_ERR_INVALID, "generate_batch: empty prompt %d", b);
+        longest = std::max(longest, lens[b]);
+    }
+    if (longest + max_new - 1 > opt_.max_seq)
+        return set_error(VSL_ERR_BOUNDS, "generate_batch: prompt %d + %d new tokens exceed max_seq %d", longest,
+                         max_new, opt_.max_seq);
+    for (int b = 0; b < n_seq; b++) n_out[b] = 0;
+    if (max_new == 0) return VSL_OK;
+    auto is_stop = [&](int32_t t) {
+        for (int s = 0; s < n_stop; s++)
+            if (t == stop_ids[s]) return true;
+        return false;
+    };
+    RC(reset());
+    std::vector<char> done(n_seq, 0);
+    int live = n_seq;
+    size_t off = 0;
+    for (int b = 0; b < n_seq; b++) {
+        RC(prefill(prompts + off, lens[b], b, &out_ids[(size_t)b * max_new], nullptr, temperature, seed));
+        off += lens[b];
+        n_out[b] = 1;
+        if (is_stop(out_ids[(size_t)b * max_new])) {
+            done[b] = 1;
+            live--;
+        }
+    }
+    const int total = max_new - 1;
+    const int chunk = n_stop > 0 ? 16 : std::max(total, 1);
+    std::vector<int32_t> log;
+    int steps = 0;
+    while (steps < total && live > 0) {
+        const int n = std::min(chunk, total - steps);
+        RC(run(n, n_seq, temperature, seed));
+        log.resize((size_t)(steps + n) * n_seq);
+        RC(read_tokens(steps + n, n_seq, log.data()));
+        for (int t = steps; t < steps + n; t++)
+            for (int b = 0; b < n_seq; b++) {
+                if (done[b]) continue;
+                const int32_t id = log[(size_t)t * n_seq + b];
+                out_ids[(size_t)b * max_new + 1 + t] = id;
+                n_out[b] = 2 + t;
+                if (is_stop(id)) {
+                    done[b] = 1;
+                    live--;
+                }
+            }
+        steps += n;
+    }
+    return VSL_OK;
+}
+
 int DecodeEngine::step_host(const int32_t* ids, int B, int32_t* out_ids, float* out_logits) {
     if (!ids || B <= 0 || B > opt_.max_batch) return set_error(VSL_ERR_INVALID, "step_host: bad batch %d", B);
     for (int b = 0; b < B; b++)

@@ -59,6 +59,12 @@ public:
     // the last prompt token's logits.
     int prefill(const int32_t* ids, int n, int seq, int32_t* next_id, float* out_logits, float temperature = 0.0f,
                 uint64_t seed = 0);
+    // Free one sequence slot (position 0) while the others keep their state.
+    int reset_seq(int seq);
+    // n_seq prompts (concatenated, lens[b] ids each): one prompt pass per sequence, then batched
+    // decode steps; out_ids[b * max_new + k], n_out[b] ids per sequence (stop ids end a sequence).
+    int generate_batch(const int32_t* prompts, const int* lens, int n_seq, int max_new, float temperature,
+                       uint64_t seed, const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out);
     int read_tokens(int n, int B, int32_t* out);
     int positions(int B, int32_t* out);
     int generate(const int32_t* prompt, int n_prompt, int max_new, float temperature, uint64_t seed,

@@ -79,6 +79,7 @@ void VulkanSymbioteEngine::open(const Path& model_path, const DeviceOptions& opt
         o.nccl_id = opt.nccl_id.data();
     }
     o.max_batch = (int)std::max<uint32_t>(1, opt.max_batch);
+    max_batch_ = (uint32_t)o.max_batch;
     max_seq_ = opt.max_seq ? opt.max_seq : std::min<uint32_t>(std::max<uint32_t>(config_.max_position_embeddings, 64), 4096);
     o.max_seq = (int)max_seq_;
     o.vram_budget_gb =
@@ -131,9 +132,40 @@ std::string VulkanSymbioteEngine::generate(const std::string& prompt, uint32_t m
 
 std::vector<std::string> VulkanSymbioteEngine::generate_text_batch(const std::vector<std::string>& prompts,
                                                                    uint32_t max_tokens_per_prompt, float temperature) {
+    // up to max_batch prompts decode together (one prompt pass each, then batched steps);
+    // greedy and stop ids 0/2 as in generate()
     std::vector<std::string> out;
     out.reserve(prompts.size());
-    for (const auto& p : prompts) out.push_back(generate(p, max_tokens_per_prompt, temperature));
+    for (size_t p0 = 0; p0 < prompts.size(); p0 += max_batch_) {
+        const size_t nb = std::min<size_t>(max_batch_, prompts.size() - p0);
+        std::vector<int32_t> flat;
+        std::vector<int> lens(nb);
+        uint32_t longest = 0;
+        for (size_t b = 0; b < nb; b++) {
+            std::vector<uint32_t> ids = encode(prompts[p0 + b]);
+            if (ids.size() >= max_seq_) ids.resize(max_seq_ - 1);
+            lens[b] = (int)ids.size();
+            longest = std::max<uint32_t>(longest, (uint32_t)ids.size());
+            flat.insert(flat.end(), ids.begin(), ids.end());
+        }
+        const uint32_t n = std::min<uint32_t>(max_tokens_per_prompt, max_seq_ - longest);
+        std::vector<int32_t> ids_out(nb * std::max<uint32_t>(n, 1));
+        std::vector<int> n_out(nb, 0);
+        const int32_t stops[2] = {0, 2};
+        const uint64_t t0 = get_current_time_ns();
+        if (n > 0 && vsl_engine_generate_batch(engine_, flat.data(), lens.data(), (int)nb, (int)n, 0.0f, 0, stops, 2,
+                                               ids_out.data(), n_out.data()) != VSL_OK)
+            throw_vsl("generate_text_batch");
+        uint32_t produced = 0;
+        for (size_t b = 0; b < nb; b++) {
+            std::string r = prompts[p0 + b];
+            for (int k = 0; k < n_out[b]; k++) r += decode({(uint32_t)ids_out[b * n + k]});
+            produced += (uint32_t)n_out[b];
+            out.push_back(std::move(r));
+        }
+        performance_metrics_.update(get_current_time_ns() - t0, produced);
+    }
+    (void)temperature;
     return out;
 }
 

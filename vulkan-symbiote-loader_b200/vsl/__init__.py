@@ -98,6 +98,8 @@ def lib() -> C.CDLL:
         "vsl_engine_read_trace": (i32, [vp, i32, C.POINTER(C.c_uint64), C.POINTER(i32)]),
         "vsl_engine_memory_stats": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
         "vsl_engine_prefill": (i32, [vp, vp, i32, i32, C.POINTER(i32), vp]),
+        "vsl_engine_reset_seq": (i32, [vp, i32]),
+        "vsl_engine_generate_batch": (i32, [vp, vp, vp, i32, i32, C.c_float, C.c_uint64, vp, i32, vp, vp]),
         "vsl_engine_residency": (i32, [vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(u64),
                                        C.POINTER(u64)]),
         "vsl_pack_plan": (i32, [u64, C.c_uint32, u64, f64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
@@ -381,6 +383,22 @@ class Engine:
         check(lib().vsl_engine_prefill(self.h, a.ctypes.data, a.size, seq, C.byref(nxt),
                                        lg.ctypes.data if lg is not None else None))
         return nxt.value, lg
+
+    def reset_seq(self, seq: int):
+        check(lib().vsl_engine_reset_seq(self.h, seq))
+
+    def generate_batch(self, prompts, max_new: int, temperature: float = 0.0, seed: int = 0, stop_ids=()):
+        """One prompt pass per sequence, then batched decode; returns one id list per prompt."""
+        import numpy as np
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, np.int32).reshape(-1) for p in prompts]), np.int32)
+        lens = np.ascontiguousarray([len(p) for p in prompts], np.int32)
+        st = np.ascontiguousarray(list(stop_ids), np.int32) if len(stop_ids) else None
+        out = np.zeros((len(prompts), max(max_new, 1)), np.int32)
+        n = np.zeros(len(prompts), np.int32)
+        check(lib().vsl_engine_generate_batch(self.h, flat.ctypes.data, lens.ctypes.data, len(prompts), max_new,
+                                              temperature, seed, st.ctypes.data if st is not None else None,
+                                              0 if st is None else st.size, out.ctypes.data, n.ctypes.data))
+        return [out[b, :n[b]].tolist() for b in range(len(prompts))]
 
     def residency(self) -> dict:
         """Weight residency under the HBM budget (layers kept in HBM / streamed each step)."""
