@@ -18,6 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
 F32, F16, BF16 = 0, 1, 30
+Q4_0, Q8_0 = 2, 8
 
 
 class OrcConfig(C.Structure):
@@ -60,6 +61,9 @@ def lib():
         L.orc_argmax.argtypes = [vp, i32]
         L.orc_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]
         L.orc_model_load_gguf.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp)]
+        L.orc_model_load_gguf_ex.argtypes = [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)]
+        L.orc_dequant_blocks.argtypes = [i32, vp, C.c_size_t, i32, vp]
+        L.orc_synthq_dequant.argtypes = [C.c_uint64, C.c_uint64, C.c_size_t, C.c_size_t, C.c_double, i32, vp]
         L.orc_model_synthetic.argtypes = [C.POINTER(OrcConfig), C.c_uint64, C.c_double, C.POINTER(vp)]
         L.orc_model_free.argtypes = [vp]
         L.orc_model_get_config.argtypes = [vp, C.POINTER(OrcConfig)]
@@ -74,6 +78,21 @@ def lib():
 
 def _p(a: np.ndarray):
     return a.ctypes.data_as(C.c_void_p)
+
+
+def dequant_blocks(dtype, blocks: np.ndarray, n_elems: int, legacy_q4: int = 0) -> np.ndarray:
+    """GGUF Q8_0 / Q4_0 block bytes -> fp32 values (the reference loader's dequantisation)."""
+    out = np.empty(n_elems, np.float32)
+    b = np.ascontiguousarray(blocks, np.uint8)
+    lib().orc_dequant_blocks(dtype, _p(b), n_elems, legacy_q4, _p(out))
+    return out
+
+
+def synthq_dequant(seed, tid, rows, cols, dtype, sigma=0.02) -> np.ndarray:
+    """Seeded block-quantized tensor, dequantized to fp32 [rows][cols]."""
+    out = np.empty((rows, cols), np.float32)
+    lib().orc_synthq_dequant(seed, tid, rows, cols, sigma, dtype, _p(out))
+    return out
 
 
 def synth_fill(seed, tid, n, sigma=0.02, dtype=F32, start=0):
@@ -151,9 +170,9 @@ class Model:
         self.cfg = cfg
 
     @classmethod
-    def from_gguf(cls, path, kvdtype=F32, max_seq=512, max_batch=1):
+    def from_gguf(cls, path, kvdtype=F32, max_seq=512, max_batch=1, legacy_q4=0):
         h = C.c_void_p()
-        rc = lib().orc_model_load_gguf(path.encode(), kvdtype, max_seq, max_batch, C.byref(h))
+        rc = lib().orc_model_load_gguf_ex(path.encode(), kvdtype, max_seq, max_batch, legacy_q4, C.byref(h))
         if rc != 0:
             raise RuntimeError(f"oracle GGUF load failed: {rc}")
         return cls(h)

@@ -52,7 +52,8 @@
 #endif
 
 /* ggml tensor type ids (standard GGUF), used for weights and the KV cache */
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_BF16 = 30 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_BF16 = 30 };
+static inline int orc_is_quant(int dt) { return dt == ORC_Q4_0 || dt == ORC_Q8_0; }
 
 /* ------------------------------------------------------------------------- */
 /* number formats                                                            */
@@ -166,6 +167,60 @@ void orc_synth_fill(uint64_t seed, uint64_t tensor_id, uint64_t start, uint64_t 
         else if (dtype == ORC_BF16) ((uint16_t*)out)[j] = orc_f2bf(v);
         else ((float*)out)[j] = v;
     }
+}
+
+/* ------------------------------------------------------------------------- */
+/* block-quantized weights (GGUF Q8_0 / Q4_0, 32 elements per block)         */
+/* ------------------------------------------------------------------------- */
+
+/* GGUFLoader.cpp dequantize_tensor: per block, d = fp16_to_fp32(first two bytes) (:1131-1147,
+ * exact IEEE half), then value = q * d in fp32: Q8_0 q = int8 qs[i] (:1185-1200); Q4_0
+ * q = nibble - 8 (:1150-1162). The reference reads the nibbles of byte i as elements 2i (low)
+ * and 2i + 1 (high) (:1154-1159); ggml's format defines them as elements i and i + 16. Both
+ * orders are restated: legacy_q4 = 1 follows the reference loader, 0 the format. */
+void orc_dequant_blocks(int dtype, const void* blocks, size_t n_elems, int legacy_q4, float* out) {
+    const uint8_t* p = (const uint8_t*)blocks;
+    const size_t bb = dtype == ORC_Q8_0 ? 34 : 18;
+    for (size_t b = 0; b * 32 < n_elems; b++, p += bb) {
+        const float d = orc_h2f((uint16_t)(p[0] | (p[1] << 8)));
+        float* o = out + b * 32;
+        if (dtype == ORC_Q8_0) {
+            for (int i = 0; i < 32; i++) o[i] = (float)(int8_t)p[2 + i] * d;
+        } else {
+            for (int i = 0; i < 16; i++) {
+                const int lo = (p[2 + i] & 0x0F) - 8, hi = ((p[2 + i] >> 4) & 0x0F) - 8;
+                if (legacy_q4) { o[2 * i] = (float)lo * d; o[2 * i + 1] = (float)hi * d; }
+                else { o[i] = (float)lo * d; o[i + 16] = (float)hi * d; }
+            }
+        }
+    }
+}
+
+/* Seeded block-quantized tensor [rows][cols], dequantized (the device initialiser writes the
+ * same quants and scales in its packed layout): element gi = r * cols + c has quant
+ * h(gi) % 255 - 127 (Q8_0) or (1 + h(gi) % 15) - 8 (Q4_0); block gb = r * (cols / 32) + c / 32 has
+ * scale fp16(m * k), m = 49152 + (h'(gb) & 0x7fff), h' the tensor's second stream and
+ * k = sigma / std(quant) / 65536 in fp32. */
+void orc_synthq_dequant(uint64_t seed, uint64_t tensor_id, size_t rows, size_t cols, double sigma, int dtype,
+                        float* out) {
+    const uint64_t base = smix(seed ^ (tensor_id * 0xD1B54A32D192ED03ull));
+    const uint64_t sbase = smix(seed ^ ((tensor_id ^ 0x5CA1E5ull) * 0xD1B54A32D192ED03ull));
+    const double sq = dtype == ORC_Q8_0 ? 73.6115932 : 4.3204938;
+    const float k = (float)(sigma / sq / 65536.0);
+    const size_t nb = cols / 32;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < (int64_t)rows; r++)
+        for (size_t b = 0; b < nb; b++) {
+            const uint64_t hs = smix(sbase + (uint64_t)r * nb + b);
+            const float m = (float)(49152u + (unsigned)(hs & 0x7fffull));
+            const float d = orc_h2f(orc_f2h(m * k));
+            for (int i = 0; i < 32; i++) {
+                const size_t gi = (size_t)r * cols + b * 32 + (size_t)i;
+                const uint64_t h = smix(base + gi);
+                const int q = dtype == ORC_Q8_0 ? (int)(h % 255ull) - 127 : (int)(1ull + h % 15ull) - 8;
+                out[gi] = (float)q * d;
+            }
+        }
 }
 
 /* prompt ids: uniform in [0, V) (modulo mapping of a 64-bit draw) */
@@ -360,6 +415,8 @@ typedef struct {
     void* map;
     size_t map_len;
     void* owned; /* synthetic weights */
+    float** qbufs; /* dequantized copies of block-quantized GGUF tensors */
+    int n_qbufs;
     /* KV cache [l][b][kv][max_seq][hd] in kvdtype */
     void* kcache;
     void* vcache;
@@ -428,6 +485,8 @@ static double rd_num(rd_t* r, uint32_t t) {
 static void model_free_storage(orc_model* m) {
     if (m->map) munmap(m->map, m->map_len);
     free(m->owned);
+    for (int i = 0; i < m->n_qbufs; i++) free(m->qbufs[i]);
+    free(m->qbufs);
     free(m->layers);
     free(m->kcache);
     free(m->vcache);
@@ -454,7 +513,8 @@ static const char* layer_suffix[9] = {"attn_norm", "attn_q", "attn_k", "attn_v",
 
 /* Load a standard GGUF (ggml tensor type ids, general.alignment respected).
  * Metadata keys follow GGUFLoader.cpp:673-728; head_dim = d / heads (:725). */
-int orc_model_load_gguf(const char* path, int kvdtype, int max_seq, int max_batch, orc_model** out) {
+int orc_model_load_gguf_ex(const char* path, int kvdtype, int max_seq, int max_batch, int legacy_q4,
+                           orc_model** out) {
     int fd = open(path, O_RDONLY);
     if (fd < 0) return -6;
     struct stat st;
@@ -514,12 +574,26 @@ int orc_model_load_gguf(const char* path, int kvdtype, int max_seq, int max_batc
     int found = 0;
     for (uint64_t i = 0; i < n_tensors; i++) {
         orc_w w = {(const uint8_t*)map + data0 + ts[i].offset, ts[i].dtype};
-        if (ts[i].dtype != ORC_F32 && ts[i].dtype != ORC_F16 && ts[i].dtype != ORC_BF16) continue;
+        if (ts[i].dtype != ORC_F32 && ts[i].dtype != ORC_F16 && ts[i].dtype != ORC_BF16 && !orc_is_quant(ts[i].dtype))
+            continue;
+        if (orc_is_quant(ts[i].dtype)) {
+            /* the reference dequantises quantized tensors to fp32 when it reads them
+             * (read_tensor_data -> dequantize_tensor, GGUFLoader.cpp:776-778) */
+            size_t n = 1;
+            for (int j = 0; j < ts[i].n_dims && j < 4; j++) n *= (size_t)ts[i].ne[j];
+            float* f = (float*)malloc(n * sizeof(float));
+            if (!f) { free(ts); model_free_storage(m); free(m); return -8; }
+            orc_dequant_blocks(ts[i].dtype, w.p, n, legacy_q4, f);
+            m->qbufs = (float**)realloc(m->qbufs, sizeof(float*) * (size_t)(m->n_qbufs + 1));
+            m->qbufs[m->n_qbufs++] = f;
+            w.p = f;
+            w.dtype = ORC_F32;
+        }
         const char* nm = ts[i].name;
         if (!strcmp(nm, "token_embd.weight")) {
             m->tok_embd = w; found++;
             if (c->vocab == 0) c->vocab = (int)ts[i].ne[1];
-            c->wdtype = ts[i].dtype;
+            c->wdtype = ts[i].dtype; /* the file's type (quantized tensors are held as fp32) */
         } else if (!strcmp(nm, "output.weight")) { m->output = w; found++; }
         else if (!strcmp(nm, "output_norm.weight")) { m->out_norm = w; found++; }
         else if (!strncmp(nm, "blk.", 4)) {
@@ -548,13 +622,18 @@ int orc_model_load_gguf(const char* path, int kvdtype, int max_seq, int max_batc
     return 0;
 }
 
+int orc_model_load_gguf(const char* path, int kvdtype, int max_seq, int max_batch, orc_model** out) {
+    return orc_model_load_gguf_ex(path, kvdtype, max_seq, max_batch, 0, out);
+}
+
 /* Build a model whose weights come from the seeded generator (norms = 1.0),
  * exactly the tensors vsl/synth.py writes into a GGUF and the device initialiser fills. */
 int orc_model_synthetic(const orc_config* cfg, uint64_t seed, double sigma, orc_model** out) {
     orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
     m->c = *cfg;
     orc_config* c = &m->c;
-    size_t es = dtype_size(c->wdtype);
+    const int quant = orc_is_quant(c->wdtype);
+    size_t es = quant ? 4 : dtype_size(c->wdtype); /* quantized weights are held dequantized */
     size_t qd = (size_t)c->n_heads * c->head_dim, kvd = (size_t)c->n_kv * c->head_dim;
     size_t per_layer = qd * c->d + 2 * kvd * c->d + c->d * qd + 3 * (size_t)c->ffn * c->d;
     size_t mats = per_layer * c->n_layers + 2 * (size_t)c->vocab * c->d;
@@ -567,8 +646,9 @@ int orc_model_synthetic(const orc_config* cfg, uint64_t seed, double sigma, orc_
     for (size_t i = 0; i < norms; i++) nrm[i] = 1.0f;
 #define TAKE(dst, tid, rows, cols)                                                   \
     do {                                                                             \
-        orc_synth_fill(seed, (tid), 0, (uint64_t)(rows) * (cols), sigma, c->wdtype, p); \
-        (dst).p = p; (dst).dtype = c->wdtype; p += (size_t)(rows) * (cols) * es;    \
+        if (quant) orc_synthq_dequant(seed, (tid), (rows), (cols), sigma, c->wdtype, (float*)p); \
+        else orc_synth_fill(seed, (tid), 0, (uint64_t)(rows) * (cols), sigma, c->wdtype, p); \
+        (dst).p = p; (dst).dtype = quant ? ORC_F32 : c->wdtype; p += (size_t)(rows) * (cols) * es; \
     } while (0)
     TAKE(m->tok_embd, TID_TOK_EMBD, c->vocab, c->d);
     TAKE(m->output, TID_OUTPUT, c->vocab, c->d);

@@ -69,8 +69,6 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     if (cfg.n_layers <= 0 || cfg.d_model <= 0 || cfg.n_heads <= 0 || cfg.n_kv_heads <= 0 || cfg.ffn <= 0 ||
         cfg.vocab <= 0 || cfg.head_dim <= 0)
         return set_error(VSL_ERR_INVALID, "engine: empty model dimension");
-    if (cfg.wdtype != VSL_F32 && cfg.wdtype != VSL_F16 && cfg.wdtype != VSL_BF16)
-        return set_error(VSL_ERR_UNSUPPORTED, "engine: weight dtype %d", cfg.wdtype);
     if (cfg.head_dim != 64 && cfg.head_dim != 128)
         return set_error(VSL_ERR_UNSUPPORTED, "engine: head_dim %d (64 or 128 supported)", cfg.head_dim);
     if (cfg.n_heads % cfg.n_kv_heads || cfg.n_heads / cfg.n_kv_heads > 8)
@@ -81,10 +79,14 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
                          cfg.n_heads, cfg.n_kv_heads, cfg.ffn, cfg.vocab, tp);
     if (opt.max_batch <= 0 || opt.max_batch > 1024 || opt.max_seq <= 0)
         return set_error(VSL_ERR_INVALID, "engine: max_batch %d / max_seq %d", opt.max_batch, opt.max_seq);
-    es_ = dtype_bytes(cfg.wdtype);
-    if (((size_t)cfg.d_model * es_) % 16 || ((size_t)cfg.ffn / tp * es_) % 16 ||
-        ((size_t)cfg.n_heads / tp * cfg.head_dim * es_) % 16)
-        return set_error(VSL_ERR_UNSUPPORTED, "engine: projection inner dimensions must be 16-byte multiples");
+    if (cfg.wdtype != VSL_F32 && cfg.wdtype != VSL_F16 && cfg.wdtype != VSL_BF16 && !is_quant(cfg.wdtype))
+        return set_error(VSL_ERR_UNSUPPORTED, "engine: weight dtype %d", cfg.wdtype);
+    es_ = is_quant(cfg.wdtype) ? 1 : dtype_bytes(cfg.wdtype);  // 16-bit paths test es_ == 2
+    if (is_quant(cfg.wdtype) && (cfg.d_model % QBLK || (cfg.ffn / tp) % QBLK || (cfg.n_heads / tp * cfg.head_dim) % QBLK))
+        return set_error(VSL_ERR_UNSUPPORTED, "engine: quantized projections need inner dimensions divisible by 32");
+    for (size_t k : {(size_t)cfg.d_model, (size_t)cfg.ffn / tp, (size_t)cfg.n_heads / tp * cfg.head_dim})
+        if (weight_row_bytes(cfg.wdtype, k) % 16)
+            return set_error(VSL_ERR_UNSUPPORTED, "engine: projection inner dimensions must be 16-byte multiples");
     nh_l_ = cfg.n_heads / tp;
     nkv_l_ = cfg.n_kv_heads / tp;
     ff_l_ = cfg.ffn / tp;
@@ -169,11 +171,11 @@ int DecodeEngine::alloc_buffers() {
     const size_t qkv_rows = (size_t)(nh_l_ + 2 * nkv_l_) * hd;
     const size_t qd_l = (size_t)nh_l_ * hd;
     const size_t A = 256;
-    const size_t b_qkv = align_up(qkv_rows * d * es_, A), b_wo = align_up(d * qd_l * es_, A);
-    const size_t b_wgu = align_up(2 * (size_t)ff_l_ * d * es_, A), b_wd = align_up(d * ff_l_ * es_, A);
+    const size_t b_qkv = align_up(qkv_rows * wrow(d), A), b_wo = align_up(d * wrow(qd_l), A);
+    const size_t b_wgu = align_up(2 * (size_t)ff_l_ * wrow(d), A), b_wd = align_up(d * wrow(ff_l_), A);
     const size_t b_norm = align_up(d * 4, A);
     layer_bytes_ = b_qkv + b_wo + b_wgu + b_wd + 2 * b_norm;
-    const size_t b_emb = align_up((size_t)c.vocab * d * es_, A), b_head = align_up((size_t)v_l_ * d * es_, A);
+    const size_t b_emb = align_up((size_t)c.vocab * wrow(d), A), b_head = align_up((size_t)v_l_ * wrow(d), A);
     layers_.resize(c.n_layers);
     // paged KV cache: per layer K then V, each [n_pages][nkv_l][page][hd]
     const size_t kv_es = dtype_bytes(kvdtype_);
@@ -239,7 +241,7 @@ int DecodeEngine::alloc_buffers() {
     }
     // batched projections (5..64 rows, 16-bit weights) run on the tensor cores: one workspace
     // sized for the largest projection of the model
-    if (es_ == 2 && opt_.max_batch >= TC_MIN_BATCH) {
+    if (es_ == 2 && !is_quant(c.wdtype) && opt_.max_batch >= TC_MIN_BATCH) {
         const int tb = std::min(opt_.max_batch, 64);
         const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
         const int k_max = std::max({c.d_model, nh_l_ * c.head_dim, ff_l_});
@@ -337,7 +339,7 @@ int DecodeEngine::alloc_buffers() {
 // gate/up (+SwiGLU) -> down (+residual), then lm_head (+argmax) and the token bookkeeping.
 int DecodeEngine::build_fused_program() {
     fs_ready_ = false;
-    if (!opt_.use_fused || opt_.tp_size != 1 || residency_.streamed_layers) return VSL_OK;
+    if (!opt_.use_fused || opt_.tp_size != 1 || residency_.streamed_layers || is_quant(cfg_.wdtype)) return VSL_OK;
     const vsl_model_config& c = cfg_;
     const int hd = c.head_dim, d = c.d_model;
     const int vec = (int)(16 / es_);
@@ -459,7 +461,10 @@ int DecodeEngine::upload_tensor(const void* src, bool src_host, int dtype_src, s
                                 size_t dst_ld, size_t row0, size_t nrows, size_t col0, size_t ncols) {
     const size_t es = dtype_bytes(dtype_src);
     if (row0 + nrows > rows || col0 + ncols > cols) return set_error(VSL_ERR_BOUNDS, "upload: slice out of range");
-    const size_t row_bytes = ncols * es;
+    const bool q = is_quant(dtype_src);
+    if (q && (!src_host || cols % QBLK || col0 % QBLK || ncols % QBLK))
+        return set_error(VSL_ERR_INVALID, "upload: quantized slices are host-side and block aligned");
+    const size_t row_bytes = q ? weight_row_bytes(dtype_src, ncols) : ncols * es;
     if (!src_host) {
         CK(cudaMemcpy2DAsync(dst, dst_ld, (const char*)src + (row0 * cols + col0) * es, cols * es, row_bytes, nrows,
                              cudaMemcpyDefault, copy_stream_));
@@ -483,7 +488,10 @@ int DecodeEngine::upload_tensor(const void* src, bool src_host, int dtype_src, s
         if (rc) break;
         const char* s = (const char*)src + ((row0 + r) * cols + col0) * es;
         char* t = (char*)stage[buf];
-        if (ncols == cols) {
+        if (q) {  // GGUF blocks -> device row layout
+            rc = repack_gguf_rows(dtype_src, src, cols, row0 + r, n, col0, ncols, t, row_bytes, opt_.legacy_q4);
+            if (rc) break;
+        } else if (ncols == cols) {
             memcpy(t, s, n * row_bytes);
         } else {
             for (size_t i = 0; i < n; i++) memcpy(t + i * row_bytes, s + i * cols * es, row_bytes);
@@ -520,6 +528,8 @@ int make_model_config_from_gguf(const vk_symbiote::GGUFLoader& loader, vsl_model
         case vk_symbiote::GGMLType::F32: dt = VSL_F32; break;
         case vk_symbiote::GGMLType::F16: dt = VSL_F16; break;
         case vk_symbiote::GGMLType::BF16: dt = VSL_BF16; break;
+        case vk_symbiote::GGMLType::Q8_0: dt = VSL_Q8_0; break;
+        case vk_symbiote::GGMLType::Q4_0: dt = VSL_Q4_0; break;
         default: return set_error(VSL_ERR_UNSUPPORTED, "gguf: token_embd dtype %u", (unsigned)emb->data_type);
     }
     vsl_model_config c = {};
@@ -550,7 +560,7 @@ int DecodeEngine::load_gguf(vk_symbiote::GGUFLoader& loader) {
             return set_error(VSL_ERR_FORMAT, "gguf: %s has shape [%llu,%llu], expected ne=[%zu,%zu]", name.c_str(),
                              (unsigned long long)t->dimensions[0],
                              (unsigned long long)(t->dimensions.size() > 1 ? t->dimensions[1] : 0), K, N);
-        const int want = c.wdtype == VSL_F32 ? 0 : c.wdtype == VSL_F16 ? 1 : 30;
+        const int want = c.wdtype;  // VSL dtype ids are the ggml tensor type ids
         if ((int)t->data_type != want)
             return set_error(VSL_ERR_UNSUPPORTED, "gguf: %s dtype %u differs from the model dtype %d", name.c_str(),
                              (unsigned)t->data_type, want);
@@ -559,35 +569,35 @@ int DecodeEngine::load_gguf(vk_symbiote::GGUFLoader& loader) {
     };
     const void* src = nullptr;
     RC(matrix("token_embd.weight", c.vocab, d, &src));
-    RC(upload_tensor(src, true, c.wdtype, c.vocab, d, tok_embd_, d * es_, 0, c.vocab, 0, d));
+    RC(upload_tensor(src, true, c.wdtype, c.vocab, d, tok_embd_, wrow(d), 0, c.vocab, 0, d));
     const char* head_name = loader.get_tensor("output.weight") ? "output.weight" : "token_embd.weight";  // tied
     RC(matrix(head_name, c.vocab, d, &src));
-    RC(upload_tensor(src, true, c.wdtype, c.vocab, d, lm_head_, d * es_, (size_t)v_off_, v_l_, 0, d));
+    RC(upload_tensor(src, true, c.wdtype, c.vocab, d, lm_head_, wrow(d), (size_t)v_off_, v_l_, 0, d));
     RC(upload_norm(loader, "output_norm.weight", out_norm_));
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
         const std::string p = "blk." + std::to_string(l) + ".";
         char* qkv = (char*)L.wqkv;
         RC(matrix(p + "attn_q.weight", qd, d, &src));
-        RC(upload_tensor(src, true, c.wdtype, qd, d, qkv, d * es_, (size_t)r * nh_l_ * hd, (size_t)nh_l_ * hd, 0, d));
-        qkv += (size_t)nh_l_ * hd * d * es_;
+        RC(upload_tensor(src, true, c.wdtype, qd, d, qkv, wrow(d), (size_t)r * nh_l_ * hd, (size_t)nh_l_ * hd, 0, d));
+        qkv += (size_t)nh_l_ * hd * wrow(d);
         RC(matrix(p + "attn_k.weight", kvd, d, &src));
-        RC(upload_tensor(src, true, c.wdtype, kvd, d, qkv, d * es_, (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, 0, d));
-        qkv += (size_t)nkv_l_ * hd * d * es_;
+        RC(upload_tensor(src, true, c.wdtype, kvd, d, qkv, wrow(d), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, 0, d));
+        qkv += (size_t)nkv_l_ * hd * wrow(d);
         RC(matrix(p + "attn_v.weight", kvd, d, &src));
-        RC(upload_tensor(src, true, c.wdtype, kvd, d, qkv, d * es_, (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, 0, d));
+        RC(upload_tensor(src, true, c.wdtype, kvd, d, qkv, wrow(d), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, 0, d));
         // attn_output (llama.cpp name) or attn_o (the reference's name, VulkanSymbioteEngine.cpp:2037)
         const std::string o_name = loader.get_tensor(p + "attn_output.weight") ? p + "attn_output.weight" : p + "attn_o.weight";
         RC(matrix(o_name, d, qd, &src));
-        RC(upload_tensor(src, true, c.wdtype, d, qd, L.wo, (size_t)nh_l_ * hd * es_, 0, d, (size_t)r * nh_l_ * hd,
+        RC(upload_tensor(src, true, c.wdtype, d, qd, L.wo, wrow((size_t)nh_l_ * hd), 0, d, (size_t)r * nh_l_ * hd,
                          (size_t)nh_l_ * hd));
         RC(matrix(p + "ffn_gate.weight", c.ffn, d, &src));
-        RC(upload_tensor(src, true, c.wdtype, c.ffn, d, L.wgu, 2 * d * es_, (size_t)r * ff_l_, ff_l_, 0, d));
+        RC(upload_tensor(src, true, c.wdtype, c.ffn, d, L.wgu, 2 * wrow(d), (size_t)r * ff_l_, ff_l_, 0, d));
         RC(matrix(p + "ffn_up.weight", c.ffn, d, &src));
-        RC(upload_tensor(src, true, c.wdtype, c.ffn, d, (char*)L.wgu + d * es_, 2 * d * es_, (size_t)r * ff_l_, ff_l_,
+        RC(upload_tensor(src, true, c.wdtype, c.ffn, d, (char*)L.wgu + wrow(d), 2 * wrow(d), (size_t)r * ff_l_, ff_l_,
                          0, d));
         RC(matrix(p + "ffn_down.weight", d, c.ffn, &src));
-        RC(upload_tensor(src, true, c.wdtype, d, c.ffn, L.wd, (size_t)ff_l_ * es_, 0, d, (size_t)r * ff_l_, ff_l_));
+        RC(upload_tensor(src, true, c.wdtype, d, c.ffn, L.wd, wrow(ff_l_), 0, d, (size_t)r * ff_l_, ff_l_));
         RC(upload_norm(loader, p + "attn_norm.weight", L.attn_norm));
         RC(upload_norm(loader, p + "ffn_norm.weight", L.ffn_norm));
     }
@@ -621,26 +631,28 @@ int DecodeEngine::init_synthetic(uint64_t seed, double sigma) {
     const size_t d = c.d_model, hd = c.head_dim, qd = (size_t)c.n_heads * hd;
     const int dt = c.wdtype;
     cudaStream_t st = copy_stream_;
-    RC(synth2d_impl(tok_embd_, dt, d, seed, TID_TOK_EMBD, 0, c.vocab, d, 0, d, sigma, st));
-    RC(synth2d_impl(lm_head_, dt, d, seed, TID_OUTPUT, (size_t)v_off_, v_l_, d, 0, d, sigma, st));
+    // slice [row0, +nrows) x [col0, +ncols) of tensor tid ([*][src_cols]) into rows of ld bytes
+    auto S = [&](void* dst, size_t ld, uint64_t tid, size_t row0, size_t nrows, size_t src_cols, size_t col0,
+                 size_t ncols) {
+        return is_quant(dt) ? synthq2d_impl(dst, dt, ld, seed, tid, row0, nrows, src_cols, col0, ncols, sigma, st)
+                            : synth2d_impl(dst, dt, ld / es_, seed, tid, row0, nrows, src_cols, col0, ncols, sigma, st);
+    };
+    RC(S(tok_embd_, wrow(d), TID_TOK_EMBD, 0, c.vocab, d, 0, d));
+    RC(S(lm_head_, wrow(d), TID_OUTPUT, (size_t)v_off_, v_l_, d, 0, d));
     std::vector<float> ones(d, 1.0f);
     CK(cudaMemcpy(out_norm_, ones.data(), d * 4, cudaMemcpyHostToDevice));
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
         char* qkv = (char*)L.wqkv;
-        RC(synth2d_impl(qkv, dt, d, seed, tid_layer(l, K_Q), (size_t)r * nh_l_ * hd, (size_t)nh_l_ * hd, d, 0, d, sigma, st));
-        qkv += (size_t)nh_l_ * hd * d * es_;
-        RC(synth2d_impl(qkv, dt, d, seed, tid_layer(l, K_K), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, d, 0, d, sigma,
-                        st));
-        qkv += (size_t)nkv_l_ * hd * d * es_;
-        RC(synth2d_impl(qkv, dt, d, seed, tid_layer(l, K_V), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, d, 0, d, sigma,
-                        st));
-        RC(synth2d_impl(L.wo, dt, (size_t)nh_l_ * hd, seed, tid_layer(l, K_O), 0, d, qd, (size_t)r * nh_l_ * hd,
-                        (size_t)nh_l_ * hd, sigma, st));
-        RC(synth2d_impl(L.wgu, dt, 2 * d, seed, tid_layer(l, K_GATE), (size_t)r * ff_l_, ff_l_, d, 0, d, sigma, st));
-        RC(synth2d_impl((char*)L.wgu + d * es_, dt, 2 * d, seed, tid_layer(l, K_UP), (size_t)r * ff_l_, ff_l_, d, 0, d,
-                        sigma, st));
-        RC(synth2d_impl(L.wd, dt, ff_l_, seed, tid_layer(l, K_DOWN), 0, d, c.ffn, (size_t)r * ff_l_, ff_l_, sigma, st));
+        RC(S(qkv, wrow(d), tid_layer(l, K_Q), (size_t)r * nh_l_ * hd, (size_t)nh_l_ * hd, d, 0, d));
+        qkv += (size_t)nh_l_ * hd * wrow(d);
+        RC(S(qkv, wrow(d), tid_layer(l, K_K), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, d, 0, d));
+        qkv += (size_t)nkv_l_ * hd * wrow(d);
+        RC(S(qkv, wrow(d), tid_layer(l, K_V), (size_t)r * nkv_l_ * hd, (size_t)nkv_l_ * hd, d, 0, d));
+        RC(S(L.wo, wrow((size_t)nh_l_ * hd), tid_layer(l, K_O), 0, d, qd, (size_t)r * nh_l_ * hd, (size_t)nh_l_ * hd));
+        RC(S(L.wgu, 2 * wrow(d), tid_layer(l, K_GATE), (size_t)r * ff_l_, ff_l_, d, 0, d));
+        RC(S((char*)L.wgu + wrow(d), 2 * wrow(d), tid_layer(l, K_UP), (size_t)r * ff_l_, ff_l_, d, 0, d));
+        RC(S(L.wd, wrow(ff_l_), tid_layer(l, K_DOWN), 0, d, c.ffn, (size_t)r * ff_l_, ff_l_));
         CK(cudaMemcpyAsync(L.attn_norm, ones.data(), d * 4, cudaMemcpyDefault, st));
         CK(cudaMemcpyAsync(L.ffn_norm, ones.data(), d * 4, cudaMemcpyDefault, st));
         CK(cudaStreamSynchronize(st));  // `ones` is pageable; keep it alive across the copies
@@ -743,8 +755,8 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
     // L2 prefetch hints: each kernel requests the head of the next projection's weights so
     // that the weight stream does not stall at kernel boundaries; the attention kernel
     // (which reads little from HBM) prefetches the whole output projection.
-    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * d * es_, wo_b = (size_t)d * nh_l_ * hd * es_;
-    const size_t wgu_b = 2 * (size_t)ff_l_ * d * es_, wd_b = (size_t)d * ff_l_ * es_;
+    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * wrow(d), wo_b = (size_t)d * wrow((size_t)nh_l_ * hd);
+    const size_t wgu_b = 2 * (size_t)ff_l_ * wrow(d), wd_b = (size_t)d * wrow(ff_l_);
     const size_t head = 16ull << 20;
     auto H = [&](size_t bytes) { return std::min(bytes, head); };
     const bool streamed = residency_.streamed_layers > 0;
@@ -779,7 +791,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
                      H(wd_b), st, tcr));
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, sb.act, B, sb.x, res_epi, nullptr, 0.0f,
-                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * d * es_) : H(qkv_b), st, tcr));
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr));
         RC(allreduce_sum(sb.x, B * d));
         if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
@@ -791,7 +803,7 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     const vsl_model_config& c = cfg_;
     const int d = c.d_model, hd = c.head_dim;
     cudaStream_t st = stream_;
-    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * d * es_;
+    const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * wrow(d);
     auto H = [&](size_t bytes) { return std::min(bytes, (size_t)16 << 20); };
     RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
     StepBufs sb{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
@@ -895,7 +907,7 @@ int DecodeEngine::alloc_prefill() {
         CK(cudaMalloc(&pf_fdtc_ws_, pf_fdtc_bytes_));
         CK(cudaMemset(pf_fdtc_ws_, 0, pf_fdtc_bytes_));
     }
-    if (es_ == 2) {
+    if (es_ == 2 && !is_quant(c.wdtype)) {
         const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
         const int k_max = std::max({c.d_model, nh_l_ * c.head_dim, ff_l_});
         const size_t bytes = tc_workspace_bytes(n_max, k_max, PF_ROWS) + 1024;
@@ -1141,10 +1153,11 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
     if (B <= 0 || B > opt_.max_batch) return set_error(VSL_ERR_INVALID, "step_stats: bad batch");
     const vsl_model_config& c = cfg_;
     const double d = c.d_model, hd = c.head_dim;
-    const double es = (double)es_;
-    const double qkv = (double)(nh_l_ + 2 * nkv_l_) * hd * d, wo = d * nh_l_ * hd, wgu = 2.0 * ff_l_ * d,
-                 wd = d * ff_l_;
-    double w = c.n_layers * ((qkv + wo + wgu + wd) * es + 2 * d * 4) + (double)v_l_ * d * es + d * 4 + B * d * es;
+    // weight bytes per step (quantized rows include their scales), norms, the embedding rows
+    const double rd = (double)wrow(c.d_model);
+    const double qkv = (double)(nh_l_ + 2 * nkv_l_) * hd * rd, wo = d * (double)wrow((size_t)nh_l_ * c.head_dim),
+                 wgu = 2.0 * ff_l_ * rd, wd = d * (double)wrow(ff_l_);
+    double w = c.n_layers * (qkv + wo + wgu + wd + 2 * d * 4) + (double)v_l_ * rd + d * 4 + B * rd;
     double kv = 0;
     const double kv_es = (double)dtype_bytes(kvdtype_);
     for (int b = 0; b < B; b++) kv += 2.0 * c.n_layers * nkv_l_ * hd * kv_es * (pos_host_[b] + 1);

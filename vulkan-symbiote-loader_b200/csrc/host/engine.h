@@ -144,7 +144,9 @@ private:
     int nh_l_ = 0, nkv_l_ = 0, ff_l_ = 0, v_l_ = 0, v_off_ = 0;
     int kvdtype_ = VSL_F16;
     int page_size_ = 64, max_pages_ = 0, n_pages_ = 0, split_len_ = 64;
-    size_t es_ = 2;
+    size_t es_ = 2;  // bytes per weight element of the 16/32-bit types (1 for block-quantized)
+    // bytes of a weight row of K elements in device layout (quantized rows include their scales)
+    size_t wrow(size_t K) const { return weight_row_bytes(cfg_.wdtype, K); }
 
     cudaStream_t stream_ = nullptr;
     cudaStream_t copy_stream_ = nullptr;

@@ -3,7 +3,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../kernels/quant_layout.h"
+
 namespace vsl {
+
+int synthq2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t tid, size_t row0, size_t nrows,
+                  size_t src_cols, size_t col0, size_t ncols, double sigma, cudaStream_t st);
+// GGUF Q8_0 / Q4_0 rows -> device row layout (host memory on both sides). `blocks` is the
+// tensor's data ([rows][cols / 32] GGUF blocks); rows [row0, row0 + nrows) x columns
+// [col0, col0 + ncols) (multiples of 32) go to out (row pitch out_ld bytes). legacy_q4: read
+// Q4_0 nibbles in the reference loader's order (element 2i low nibble, 2i + 1 high nibble of
+// byte i, GGUFLoader.cpp:1146-1160) instead of ggml's.
+int repack_gguf_rows(int dtype, const void* blocks, size_t cols, size_t row0, size_t nrows, size_t col0, size_t ncols,
+                     void* out, size_t out_ld, int legacy_q4);
 
 struct P2pPeers;
 int p2p_setup(P2pPeers* out, void** local, void** opened, int rank, int n, int cap, int elem_bytes, void* comm,

@@ -19,6 +19,7 @@
 
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "quant_layout.h"
 #include "tc_gemm.h"
 #include "launch.cuh"
 
@@ -190,14 +191,228 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams 
 }
 
 // ---------------------------------------------------------------------------------------
+// Block-quantized weights (Q8_0 / Q4_0 in the repacked row layout of quant_layout.h)
+// ---------------------------------------------------------------------------------------
+// One 16-byte vector of quants is 16 (Q8_0) or 32 (Q4_0) weights of one block. Quants become
+// exact fp32 integers without a conversion instruction: a byte (or nibble) placed under the
+// exponent pattern 0x4B000000 is the float 2^23 + value, and subtracting 2^23 (plus the
+// format's zero point) leaves the integer. Each vector contributes d * sum(q * x) to the row.
+template <int QT> struct QTraits;
+template <> struct QTraits<VSL_Q8_0> {
+    static constexpr int VEC = 16;  // weights per 16-byte vector (half a block)
+    __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+        // int8 -> biased byte (q + 128) -> float 2^23 + q + 128
+        const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                f[4 * j + i] = __uint_as_float(__byte_perm(w[j], 0x4B000000u, 0x7540u + i)) - 8388736.0f;
+    }
+};
+template <> struct QTraits<VSL_Q4_0> {
+    static constexpr int VEC = 32;  // weights per 16-byte vector (one block)
+    __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                // element 4j + i from the low nibbles, 16 + 4j + i from the high ones; zero point 8
+                f[4 * j + i] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + i)) - 8388616.0f;
+                f[16 + 4 * j + i] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + i)) - 8388616.0f;
+            }
+        }
+    }
+};
+
+// Activations are staged as fp32 with 4 floats of padding after every VEC values, so the
+// 16-byte shared-memory reads of a warp (lane l reads chunk l) fall in distinct banks.
+template <int QT>
+__host__ __device__ constexpr int q_xpitch(int K) {
+    return K + (K / QTraits<QT>::VEC) * 4;
+}
+
+template <int QT, int NB, int EK, bool NORM>
+__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParams p) {
+    extern __shared__ __align__(16) float xs[];  // [NB][q_xpitch(K)] fp32 activations, padded
+    __shared__ float red[NB][GEMV_THREADS / 32];
+    constexpr int VEC = QTraits<QT>::VEC;
+    constexpr int CH = VEC + 4;  // padded chunk
+    const int K = p.K, N = p.N;
+    const int XP = q_xpitch<QT>(K);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int NW = GEMV_THREADS / 32;
+    const int nvec = K / VEC;
+    const size_t RB = weight_row_bytes(QT, K), QB = quant_bytes(QT, K);
+    const int n_units = (N + 1) >> 1;
+    const int u_begin = (int)(((long long)n_units * blockIdx.x) / gridDim.x);
+    const int u_end = (int)(((long long)n_units * (blockIdx.x + 1)) / gridDim.x);
+    const char* W = reinterpret_cast<const char*>(p.W);
+
+    int unit = u_begin + warp;
+    {
+        const size_t r_lo = 2 * (size_t)u_begin, r_hi = min((size_t)N, 2 * (size_t)u_end);
+        const char* base = W + r_lo * RB;
+        const size_t total = (r_hi - r_lo) * RB;
+        const size_t head = min(total, (size_t)GEMV_L2_HEAD);
+        for (size_t off = (size_t)threadIdx.x * 16384; off < head; off += (size_t)GEMV_THREADS * 16384)
+            prefetch_l2(base + off, (uint32_t)min((size_t)16384, head - off));
+    }
+
+    pdl_wait();
+    pdl_launch_dependents();
+
+    const int B = p.B;
+    float den[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) den[b] = 1.0f;
+    if (NORM) {
+#pragma unroll
+        for (int b = 0; b < NB; b++) den[b] = 0.0f;
+        for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                float v = b < B ? p.x[(size_t)b * K + k] : 0.0f;
+                den[b] += v * v;
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float s = warp_sum(den[b]);
+            if (lane == 0) red[b][warp] = s;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float s = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NW; w++) s += red[b][w];
+            den[b] = sqrtf(s / (float)K + p.eps);  // rms_norm.comp:32-34: x / sqrt(var) * w
+        }
+    }
+    for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
+        const float w = NORM ? p.norm_w[k] : 1.0f;
+        const int xi = k + (k / VEC) * 4;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            const float v = b < B ? p.x[(size_t)b * K + k] : 0.0f;
+            xs[b * XP + xi] = NORM ? v / den[b] * w : v;
+        }
+    }
+    __syncthreads();
+
+    unsigned long long best[NB];
+#pragma unroll
+    for (int b = 0; b < NB; b++) best[b] = 0ull;
+    int step = 0;
+    if (EK == EK_LMHEAD && p.inv_temp > 0.0f) step = *p.step_counter;
+
+    constexpr int U = (QT == VSL_Q4_0 && NB >= 4) ? 2 : 4;  // vectors in flight per row and lane
+    for (; unit < u_end; unit += NW) {
+        const int r0 = 2 * unit;
+        const bool has1 = r0 + 1 < N;
+        const int r1 = has1 ? r0 + 1 : r0;
+        const char* row0 = W + (size_t)r0 * RB;
+        const char* row1 = W + (size_t)r1 * RB;
+        const __half* sc0 = reinterpret_cast<const __half*>(row0 + QB);
+        const __half* sc1 = reinterpret_cast<const __half*>(row1 + QB);
+        if (lane == 0 && unit + NW < u_end) {
+            const int rn = 2 * (unit + NW);
+            const int rows = min(2, N - rn);
+            prefetch_l2(W + (size_t)rn * RB, (uint32_t)(rows * RB));
+        }
+        float acc0[NB], acc1[NB];
+#pragma unroll
+        for (int b = 0; b < NB; b++) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
+        auto consume = [&](const uint4& a, const uint4& c, float d0, float d1, int v) {
+            float f[VEC];
+            float t0[NB], t1[NB];
+#pragma unroll
+            for (int b = 0; b < NB; b++) { t0[b] = 0.0f; t1[b] = 0.0f; }
+            QTraits<QT>::unpack(a, f);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float4* xv = reinterpret_cast<const float4*>(xs + b * XP + v * CH);
+#pragma unroll
+                for (int i = 0; i < VEC / 4; i++) {
+                    const float4 xx = xv[i];
+                    t0[b] = fmaf(f[4 * i + 0], xx.x, t0[b]);
+                    t0[b] = fmaf(f[4 * i + 1], xx.y, t0[b]);
+                    t0[b] = fmaf(f[4 * i + 2], xx.z, t0[b]);
+                    t0[b] = fmaf(f[4 * i + 3], xx.w, t0[b]);
+                }
+            }
+            QTraits<QT>::unpack(c, f);
+#pragma unroll
+            for (int b = 0; b < NB; b++) {
+                const float4* xv = reinterpret_cast<const float4*>(xs + b * XP + v * CH);
+#pragma unroll
+                for (int i = 0; i < VEC / 4; i++) {
+                    const float4 xx = xv[i];
+                    t1[b] = fmaf(f[4 * i + 0], xx.x, t1[b]);
+                    t1[b] = fmaf(f[4 * i + 1], xx.y, t1[b]);
+                    t1[b] = fmaf(f[4 * i + 2], xx.z, t1[b]);
+                    t1[b] = fmaf(f[4 * i + 3], xx.w, t1[b]);
+                }
+                acc0[b] = fmaf(d0, t0[b], acc0[b]);
+                acc1[b] = fmaf(d1, t1[b], acc1[b]);
+            }
+        };
+        int v = lane;
+        for (; v + 32 * (U - 1) < nvec; v += 32 * U) {
+            uint4 a[U], c[U];
+            unsigned short s0[U], s1[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int vv = v + 32 * u;
+                a[u] = ldg_stream(row0 + (size_t)vv * 16);
+                c[u] = ldg_stream(row1 + (size_t)vv * 16);
+                s0[u] = __ldcs(reinterpret_cast<const unsigned short*>(sc0) + (vv * VEC) / QBLK);
+                s1[u] = __ldcs(reinterpret_cast<const unsigned short*>(sc1) + (vv * VEC) / QBLK);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++)
+                consume(a[u], c[u], __half2float(__ushort_as_half(s0[u])), __half2float(__ushort_as_half(s1[u])),
+                        v + 32 * u);
+        }
+        for (; v < nvec; v += 32) {
+            const uint4 a = ldg_stream(row0 + (size_t)v * 16);
+            const uint4 c = ldg_stream(row1 + (size_t)v * 16);
+            const float d0 = __half2float(sc0[(v * VEC) / QBLK]), d1 = __half2float(sc1[(v * VEC) / QBLK]);
+            consume(a, c, d0, d1, v);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            acc0[b] = warp_sum(acc0[b]);
+            acc1[b] = warp_sum(acc1[b]);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            if (lane != b || b >= B) continue;
+            gemv_pair_epilogue<EK>(p, b, r0, unit, has1, acc0[b], acc1[b], best[b], step);
+        }
+    }
+    if (EK == EK_LMHEAD) {
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+            if (lane == b && b < B && best[b] != 0ull) atomicMax(p.slots + b, best[b]);
+    }
+    if (p.pf_ptr && lane == 0) prefetch_share(p.pf_ptr, p.pf_bytes, blockIdx.x, gridDim.x, warp, NW);
+}
+
+// ---------------------------------------------------------------------------------------
 // host dispatch
 // ---------------------------------------------------------------------------------------
 
 // activation rows one launch stages in shared memory (fp32 [rows][K]); the compiled row
 // counts are 1, 2 and 4
-static int max_rows_per_launch(int K) {
+static int max_rows_per_launch(int wdtype, int K) {
     const size_t room = 200 * 1024;
-    const int c = (int)(room / ((size_t)K * sizeof(float)));
+    const size_t pitch = wdtype == VSL_Q8_0 ? (size_t)q_xpitch<VSL_Q8_0>(K)
+                         : wdtype == VSL_Q4_0 ? (size_t)q_xpitch<VSL_Q4_0>(K) : (size_t)K;
+    const int c = (int)(room / (pitch * sizeof(float)));
     return c >= 4 ? 4 : c >= 2 ? 2 : c;
 }
 
@@ -230,6 +445,41 @@ static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
     return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
 }
 
+template <int QT, int NB, int EK, bool NORM>
+static int launch_gemv_q_t(const GemvParams& p, cudaStream_t st) {
+    auto kern = gemv_q_kernel<QT, NB, EK, NORM>;
+    const size_t smem = (size_t)NB * q_xpitch<QT>(p.K) * sizeof(float);
+    static thread_local int configured_dev = -1;
+    static thread_local size_t configured_smem = 0;
+    static thread_local int occ = 1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev || configured_smem != smem) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return launch_status(e, "gemv smem attribute");
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, GEMV_THREADS, smem);
+        if (e != cudaSuccess) return launch_status(e, "gemv occupancy");
+        if (occ < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d does not fit in shared memory", p.K);
+        if (occ > 2) occ = 2;
+        configured_dev = dev;
+        configured_smem = smem;
+    }
+    const int n_units = (p.N + 1) / 2;
+    const int nw = GEMV_THREADS / 32;
+    int grid = sm_count() * occ;
+    const int max_grid = (n_units + nw - 1) / nw;
+    if (grid > max_grid) grid = max_grid;
+    if (grid < 1) grid = 1;
+    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
+}
+
+template <int QT, int EK, bool NORM>
+static int launch_gemv_q_nb(const GemvParams& p, cudaStream_t st) {
+    if (p.B <= 1) return launch_gemv_q_t<QT, 1, EK, NORM>(p, st);
+    if (p.B <= 2) return launch_gemv_q_t<QT, 2, EK, NORM>(p, st);
+    return launch_gemv_q_t<QT, 4, EK, NORM>(p, st);
+}
+
 template <typename WT, int EK, bool NORM>
 static int launch_gemv_nb(const GemvParams& p, cudaStream_t st) {
     if (p.B <= 1) return launch_gemv_t<WT, 1, EK, NORM>(p, st);
@@ -243,6 +493,8 @@ static int launch_gemv_w(int wdtype, const GemvParams& p, cudaStream_t st) {
         case VSL_F32: return launch_gemv_nb<float, EK, NORM>(p, st);
         case VSL_F16: return launch_gemv_nb<__half, EK, NORM>(p, st);
         case VSL_BF16: return launch_gemv_nb<__nv_bfloat16, EK, NORM>(p, st);
+        case VSL_Q8_0: return launch_gemv_q_nb<VSL_Q8_0, EK, NORM>(p, st);
+        case VSL_Q4_0: return launch_gemv_q_nb<VSL_Q4_0, EK, NORM>(p, st);
         default: return set_error(VSL_ERR_UNSUPPORTED, "gemv: weight dtype %d", wdtype);
     }
 }
@@ -252,14 +504,14 @@ static int launch_gemv_norm(int wdtype, const GemvParams& p, cudaStream_t st) {
     return p.norm_w ? launch_gemv_w<EK, true>(wdtype, p, st) : launch_gemv_w<EK, false>(wdtype, p, st);
 }
 
-static size_t elem_size(int dtype) { return dtype == VSL_F32 ? 4 : 2; }
-
 static int check_common(int wdtype, const void* W, int N, int K, const float* x, int B) {
-    if (wdtype != VSL_F32 && wdtype != VSL_F16 && wdtype != VSL_BF16)
+    if (wdtype != VSL_F32 && wdtype != VSL_F16 && wdtype != VSL_BF16 && !is_quant(wdtype))
         return set_error(VSL_ERR_UNSUPPORTED, "weight dtype %d", wdtype);
     if (!W || !x || N <= 0 || K <= 0 || B <= 0)
         return set_error(VSL_ERR_INVALID, "gemv: null pointer or empty shape (N=%d K=%d B=%d)", N, K, B);
-    if (((uintptr_t)W & 15) || ((size_t)K * elem_size(wdtype)) % 16)
+    if (is_quant(wdtype) && K % QBLK)
+        return set_error(VSL_ERR_INVALID, "gemv: quantized rows need K a multiple of %d (K=%d)", QBLK, K);
+    if (((uintptr_t)W & 15) || weight_row_bytes(wdtype, (size_t)K) % 16)
         return set_error(VSL_ERR_INVALID, "gemv: weight rows must be 16-byte aligned (K=%d)", K);
     if ((uintptr_t)x & 15) return set_error(VSL_ERR_INVALID, "gemv: activations must be 16-byte aligned");
     return VSL_OK;
@@ -274,7 +526,7 @@ static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y
     if (tc && tc->ws && B >= tc->min_batch && tc_supported(wdtype, p.N, p.K, B))
         return tc_project(wdtype, kind, p, tc->ws, tc->bytes, tc->status ? tc->status : p.status, st);
     // activation rows per launch: at most 4, and at most what fits beside the weight ring
-    const int cmax = max_rows_per_launch(p.K);
+    const int cmax = max_rows_per_launch(wdtype, p.K);
     if (cmax < 1) return set_error(VSL_ERR_UNSUPPORTED, "gemv: K=%d exceeds the shared-memory staging limit", p.K);
     for (int b0 = 0; b0 < B; b0 += cmax) {
         GemvParams q = p;

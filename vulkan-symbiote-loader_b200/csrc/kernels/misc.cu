@@ -6,6 +6,7 @@
 #include <math_constants.h>
 
 #include "common.cuh"
+#include "quant_layout.h"
 #include "launch.cuh"
 
 namespace vsl {
@@ -46,11 +47,48 @@ __global__ void embed_kernel(const WT* __restrict__ table, int V, int d, const i
     if (slots && threadIdx.x == 0) slots[b] = 0ull;  // argmax slot of this step's sampler
 }
 
+// Block-quantized table (device row layout of quant_layout.h): element j of the row is
+// quant(j) * d(j / 32) in fp32, the reference's dequantisation (GGUFLoader.cpp:1141-1181).
+template <int QT>
+__global__ void embed_q_kernel(const unsigned char* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
+                               float* __restrict__ x, unsigned long long* slots) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int b = blockIdx.x;
+    int id = ids[b];
+    if (id < 0) id = 0;
+    if (id > V - 1) id = V - 1;
+    const unsigned char* row = table + (size_t)id * weight_row_bytes(QT, d);
+    const __half* sc = reinterpret_cast<const __half*>(row + quant_bytes(QT, d));
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+        const float s = __half2float(sc[j / QBLK]);
+        int q;
+        if (QT == VSL_Q8_0) {
+            q = (int)(signed char)row[j];
+        } else {
+            const int blk = j / QBLK, i = j % QBLK;
+            const unsigned char byte = row[blk * 16 + (i & 15)];
+            q = (int)(i < 16 ? (byte & 15) : (byte >> 4)) - 8;
+        }
+        x[(size_t)b * d + j] = (float)q * s;
+    }
+    if (slots && threadIdx.x == 0) slots[b] = 0ull;
+}
+
 int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, int B, float* x,
                unsigned long long* slots, cudaStream_t st) {
     if (!table || !ids || !x || V <= 0 || d <= 0 || B <= 0) return set_error(VSL_ERR_INVALID, "embed: bad arguments");
     dim3 grid(B), block(256);
+    if (is_quant(dtype) && d % QBLK) return set_error(VSL_ERR_INVALID, "embed: quantized rows need d %% 32 == 0");
     switch (dtype) {
+        case VSL_Q8_0:
+            return launch_status(launch_k(embed_q_kernel<VSL_Q8_0>, grid, block, 0, st, (const unsigned char*)table, V,
+                                          d, ids, x, slots),
+                                 "embed");
+        case VSL_Q4_0:
+            return launch_status(launch_k(embed_q_kernel<VSL_Q4_0>, grid, block, 0, st, (const unsigned char*)table, V,
+                                          d, ids, x, slots),
+                                 "embed");
         case VSL_F32:
             return launch_status(launch_k(embed_kernel<float>, grid, block, 0, st, (const float*)table, V, d, ids, x, slots),
                                  "embed");
@@ -182,6 +220,73 @@ __global__ void synth2d_kernel(T* __restrict__ dst, size_t dst_ld, unsigned long
         else if constexpr (std::is_same<T, __nv_bfloat16>::value) *o = __float2bfloat16_rn(v);
         else *o = v;
     }
+}
+
+// Seeded block-quantized tensor, written in the device row layout (row pitch dst_ld bytes):
+// global element gi = row * src_cols + col has quant h(gi) (Q8_0: h % 255 - 127; Q4_0: nibble
+// 1 + h % 15, value nibble - 8, symmetric like Q8_0) and global block gb = row * (src_cols / 32) + col / 32 the scale
+// fp16(m * c), m = 49152 + (h'(gb) & 0x7fff), h' from a second stream of the same tensor.
+template <int QT>
+__global__ void synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, unsigned long long base,
+                              unsigned long long sbase, size_t row0, size_t nrows, size_t src_cols, size_t col0,
+                              size_t ncols, float c) {
+    const size_t qb = quant_bytes(QT, ncols), nblk = ncols / QBLK;
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t t0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (size_t j = t0; j < nrows * qb; j += stride) {  // one quant byte per iteration
+        const size_t r = j / qb, cb = j - r * qb;
+        const size_t grow = (row0 + r) * src_cols + col0;
+        unsigned char out;
+        if (QT == VSL_Q8_0) {
+            const unsigned long long h = smix(base + grow + cb);
+            out = (unsigned char)(signed char)((int)(h % 255ull) - 127);
+        } else {
+            const size_t blk = cb / 16, i = cb % 16;  // byte i holds elements i and i + 16 of the block
+            const unsigned long long h0 = smix(base + grow + blk * QBLK + i);
+            const unsigned long long h1 = smix(base + grow + blk * QBLK + i + 16);
+            out = (unsigned char)((1ull + h0 % 15ull) | ((1ull + h1 % 15ull) << 4));
+        }
+        dst[r * dst_ld + cb] = out;
+    }
+    const size_t sb = scale_bytes(ncols) / 2;  // scale slots, padding included
+    for (size_t j = t0; j < nrows * sb; j += stride) {
+        const size_t r = j / sb, k = j - r * sb;
+        __half v = __float2half_rn(0.0f);
+        if (k < nblk) {
+            const unsigned long long gb = (row0 + r) * (src_cols / QBLK) + col0 / QBLK + k;
+            const unsigned long long h = smix(sbase + gb);
+            v = __float2half_rn(__fmul_rn((float)(49152u + (unsigned)(h & 0x7fffull)), c));
+        }
+        reinterpret_cast<__half*>(dst + r * dst_ld + qb)[k] = v;
+    }
+}
+
+// scale-stream seed of a quantized synthetic tensor
+static unsigned long long synthq_scale_base(uint64_t seed, uint64_t tid) {
+    return host_smix(seed ^ ((tid ^ 0x5CA1E5ull) * 0xD1B54A32D192ED03ull));
+}
+// fp32 factor of the block scales: d = m * c has mean ~ sigma / std(quant)
+static float synthq_scale_c(int dtype, double sigma) {
+    const double sq = dtype == VSL_Q8_0 ? 73.6115932 : 4.3204938;  // std of U{-127..127}, U{-7..7}
+    return (float)(sigma / sq / 65536.0);
+}
+
+int synthq2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t tid, size_t row0, size_t nrows,
+                  size_t src_cols, size_t col0, size_t ncols, double sigma, cudaStream_t st) {
+    if (!dst || !is_quant(dtype) || col0 % QBLK || ncols % QBLK || src_cols % QBLK || col0 + ncols > src_cols ||
+        dst_ld < weight_row_bytes(dtype, ncols))
+        return set_error(VSL_ERR_INVALID, "synthq2d: bad slice");
+    if (nrows == 0 || ncols == 0) return VSL_OK;
+    const unsigned long long base = host_smix(seed ^ (tid * 0xD1B54A32D192ED03ull));
+    const unsigned long long sbase = synthq_scale_base(seed, tid);
+    const float c = synthq_scale_c(dtype, sigma);
+    dim3 grid((unsigned)(sm_count() * 16)), block(256);
+    cudaError_t e = dtype == VSL_Q8_0
+                        ? launch_k(synthq_kernel<VSL_Q8_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                                   row0, nrows, src_cols, col0, ncols, c)
+                        : launch_k(synthq_kernel<VSL_Q4_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                                   row0, nrows, src_cols, col0, ncols, c);
+    return launch_status(e, "synthq2d");
 }
 
 int synth2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t tid, size_t row0, size_t nrows,

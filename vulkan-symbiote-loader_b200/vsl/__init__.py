@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(PKG, "lib", "libvsl.so")
 HEADER = os.path.join(os.path.dirname(PKG), "include", "vsl.h")
 
 F32, F16, BF16 = 0, 1, 30
+Q4_0, Q8_0 = 2, 8  # weights only (block-quantized device layout)
 EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
 ERR = {0: "OK", -1: "INVALID", -2: "CUDA", -3: "NCCL", -4: "TIMEOUT", -5: "BOUNDS", -6: "IO", -7: "FORMAT",
        -8: "OOM", -9: "UNSUPPORTED", -10: "STATE"}
@@ -42,7 +43,7 @@ class EngineOptions(C.Structure):
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
-                ("use_p2p", C.c_int)]
+                ("use_p2p", C.c_int), ("legacy_q4", C.c_int)]
 
 
 _lib = None
@@ -77,6 +78,8 @@ def lib() -> C.CDLL:
         "vsl_engine_default_options": (None, [C.POINTER(EngineOptions)]),
         "vsl_nccl_unique_id": (i32, [vp]),
         "vsl_gguf_model_config": (i32, [C.c_char_p, C.POINTER(ModelConfig)]),
+        "vsl_weight_row_bytes": (i32, [i32, i32, C.POINTER(sz)]),
+        "vsl_repack_gguf_rows": (i32, [i32, vp, sz, sz, sz, sz, sz, vp, sz, i32]),
         "vsl_gguf_tensor_info": (i32, [C.c_char_p, C.c_char_p, C.POINTER(i32), C.POINTER(u64), C.POINTER(u64)]),
         "vsl_engine_create_gguf": (i32, [C.c_char_p, C.POINTER(EngineOptions), C.POINTER(vp)]),
         "vsl_engine_create_synthetic": (i32, [C.POINTER(ModelConfig), u64, f64, C.POINTER(EngineOptions),
@@ -151,6 +154,28 @@ def rmsnorm(x, w, B, d, eps, y, stream=0):
 
 def gemv(wdtype, W, N, K, x, B, y, epilogue=EPI_STORE, norm_w=None, eps=0.0, stream=0):
     check(lib().vsl_gemv(wdtype, _ptr(W), N, K, _ptr(x), B, _ptr(y), epilogue, _ptr(norm_w), eps, stream))
+
+
+def weight_row_bytes(dtype: int, K: int) -> int:
+    """Bytes of one weight row of K elements in device layout (quantized rows include scales)."""
+    out = C.c_size_t()
+    check(lib().vsl_weight_row_bytes(dtype, K, C.byref(out)))
+    return out.value
+
+
+def repack_gguf_rows(dtype: int, blocks, rows: int, cols: int, legacy_q4: bool = False, row0: int = 0,
+                     nrows: int | None = None, col0: int = 0, ncols: int | None = None):
+    """GGUF Q8_0 / Q4_0 block bytes ([rows][cols / 32 blocks], host) -> device row layout (uint8
+    numpy array [nrows][weight_row_bytes(dtype, ncols)])."""
+    import numpy as np
+    nrows = rows - row0 if nrows is None else nrows
+    ncols = cols - col0 if ncols is None else ncols
+    b = np.ascontiguousarray(blocks, np.uint8)
+    pitch = weight_row_bytes(dtype, ncols)
+    out = np.zeros((nrows, pitch), np.uint8)
+    check(lib().vsl_repack_gguf_rows(dtype, b.ctypes.data, cols, row0, nrows, col0, ncols, out.ctypes.data, pitch,
+                                     1 if legacy_q4 else 0))
+    return out
 
 
 def skinny_gemm_tc_workspace_size(N, K, B) -> int:

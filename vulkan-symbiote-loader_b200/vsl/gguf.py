@@ -69,7 +69,8 @@ def _align(n: int, a: int) -> int:
 
 def write_gguf(path: str, metadata: list[tuple[str, int, object]], tensors: list[tuple[str, np.ndarray, int]],
                alignment: int = 32):
-    """tensors: (name, array in storage form with shape [rows, cols] or [n], ggml type)."""
+    """tensors: (name, array in storage form with shape [rows, cols] or [n], ggml type[, ne]);
+    block-quantized tensors pass their GGUF block bytes and the element dimensions ne."""
     head = bytearray()
     head += b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(metadata) + 1)
     _kv(head, "general.alignment", T_U32, alignment)
@@ -77,8 +78,8 @@ def write_gguf(path: str, metadata: list[tuple[str, int, object]], tensors: list
         _kv(head, key, vtype, value)
     offset = 0
     infos = []
-    for name, arr, gtype in tensors:
-        ne = list(reversed(arr.shape))  # ne[0] is the contiguous (innermost) dimension
+    for name, arr, gtype, *dims in tensors:
+        ne = list(dims[0]) if dims else list(reversed(arr.shape))  # ne[0]: the contiguous dimension
         _s(head, name)
         head += struct.pack("<I", len(ne))
         for n in ne:
@@ -120,21 +121,27 @@ def write_synthetic_llama(path: str, shape: LlamaShape, dtype: int, seed: int, s
     d, hd, F, V = shape.d_model, shape.head_dim, shape.ffn, shape.vocab
     qd, kvd = shape.n_heads * hd, shape.n_kv_heads * hd
     ones = np.ones(d, dtype=np.float32)
-    t = [("token_embd.weight", synth.synth_tensor(seed, synth.TID_TOK_EMBD, (V, d), dtype, sigma), dtype),
+
+    def mat(tid, rows, cols):
+        if dtype in synth.Q_STD:  # block-quantized: GGUF blocks + element dims
+            return (synth.synth_q_blocks(seed, tid, rows, cols, dtype, sigma), dtype, (cols, rows))
+        return (synth.synth_tensor(seed, tid, (rows, cols), dtype, sigma), dtype)
+
+    t = [("token_embd.weight", *mat(synth.TID_TOK_EMBD, V, d)),
          ("output_norm.weight", ones, synth.GGML_F32),
-         ("output.weight", synth.synth_tensor(seed, synth.TID_OUTPUT, (V, d), dtype, sigma), dtype)]
+         ("output.weight", *mat(synth.TID_OUTPUT, V, d))]
     for l in range(shape.n_layers):
         def m(kind, rows, cols):
-            return synth.synth_tensor(seed, synth.tid_layer(l, kind), (rows, cols), dtype, sigma)
+            return mat(synth.tid_layer(l, kind), rows, cols)
         t += [(f"blk.{l}.attn_norm.weight", ones, synth.GGML_F32),
-              (f"blk.{l}.attn_q.weight", m(synth.K_Q, qd, d), dtype),
-              (f"blk.{l}.attn_k.weight", m(synth.K_K, kvd, d), dtype),
-              (f"blk.{l}.attn_v.weight", m(synth.K_V, kvd, d), dtype),
-              (f"blk.{l}.attn_output.weight", m(synth.K_O, d, qd), dtype),
+              (f"blk.{l}.attn_q.weight", *m(synth.K_Q, qd, d)),
+              (f"blk.{l}.attn_k.weight", *m(synth.K_K, kvd, d)),
+              (f"blk.{l}.attn_v.weight", *m(synth.K_V, kvd, d)),
+              (f"blk.{l}.attn_output.weight", *m(synth.K_O, d, qd)),
               (f"blk.{l}.ffn_norm.weight", ones, synth.GGML_F32),
-              (f"blk.{l}.ffn_gate.weight", m(synth.K_GATE, F, d), dtype),
-              (f"blk.{l}.ffn_up.weight", m(synth.K_UP, F, d), dtype),
-              (f"blk.{l}.ffn_down.weight", m(synth.K_DOWN, d, F), dtype)]
+              (f"blk.{l}.ffn_gate.weight", *m(synth.K_GATE, F, d)),
+              (f"blk.{l}.ffn_up.weight", *m(synth.K_UP, F, d)),
+              (f"blk.{l}.ffn_down.weight", *m(synth.K_DOWN, d, F))]
     write_gguf(path, llama_metadata(shape), t)
 
 
