@@ -53,13 +53,15 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="7b", choices=["7b", "8b", "70b-stream"],
-                    help="7b: the headline (BASELINE configs[1]); 8b: BASELINE configs[3], batch 16 over "
+    ap.add_argument("--workload", default="7b", choices=["7b", "7b-q8", "7b-q4", "8b", "70b-stream"],
+                    help="7b: the headline (BASELINE configs[1]); 7b-q8 / 7b-q4: the same model with GGUF "
+                         "Q8_0 / Q4_0 block-quantized weights; 8b: BASELINE configs[3], batch 16 over "
                          "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b-stream: "
                          "BASELINE configs[4] on one GPU under a 64 GB HBM cap (layers streamed from host)")
-    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc"],
+    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
-                         "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads")
+                         "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 = "
+                         "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 weights at batch 1")
     ap.add_argument("--profile-shape", default="32000,4096,16",
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
@@ -198,13 +200,19 @@ def profiled_traffic():
 
 def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     """Time the fused RMSNorm + gate/up + SwiGLU projection (the largest per-step byte share)
-    on 7B-shape weights, rotating 8 copies (1.4 GB, far above L2) with CUDA events."""
+    on 7B-shape weights, rotating 8 copies (far above L2) with CUDA events."""
     d, F = cfg["d_model"], cfg["ffn"] // tp
     N, K = 2 * F, d
     copies = 8
-    W = torch.empty((copies, N, K), dtype=torch.float16, device="cuda")
+    dt = cfg.get("wdtype", vsl.F16)
+    quant = dt in (vsl.Q8_0, vsl.Q4_0)
+    rb = vsl.weight_row_bytes(dt, K)
+    W = torch.empty((copies, N, rb), dtype=torch.uint8, device="cuda")
     for c in range(copies):
-        vsl.synth_fill(W[c], vsl.F16, 99, 1000 + c, 0, N * K, 0.02)
+        if quant:
+            vsl.synth_fill_q(W[c], dt, 99, 1000 + c, N, K, 0.02)
+        else:
+            vsl.synth_fill(W[c], vsl.F16, 99, 1000 + c, 0, N * K, 0.02)
     x = torch.randn((1, K), device="cuda")
     nw = torch.ones(K, device="cuda")
     y = torch.empty((1, F), device="cuda")
@@ -212,19 +220,25 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     st = s.cuda_stream
     with torch.cuda.stream(s):
         for i in range(3 * copies):
-            vsl.gemv(vsl.F16, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
+            vsl.gemv(dt, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
         reps = 20 * copies
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
         for i in range(reps):
-            vsl.gemv(vsl.F16, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
+            vsl.gemv(dt, W[i % copies], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5, stream=st)
         e1.record(s)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    bytes_per_launch = N * K * 2 + K * 4 * 2 + F * 4  # weights + x + norm weights + output
+    bytes_per_launch = N * rb + K * 4 * 2 + F * 4  # weights (with block scales) + x + norm weights + output
     achieved = bytes_per_launch / (ms * 1e-3) / 1e9
     del W
     torch.cuda.empty_cache()
+    if quant:
+        return {"bound": "hbm", "kernel": f"gemv_q_kernel<{'Q8_0' if dt == vsl.Q8_0 else 'Q4_0'},1,EK_SWIGLU,NORM> "
+                                          "(gate/up + SwiGLU, fused RMSNorm)",
+                "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch,
+                "us_per_launch": round(ms * 1e3, 3), "traffic": None}
     return {"bound": "hbm", "kernel": "gemv_kernel<__half,1,EK_SWIGLU,NORM> (gate/up + SwiGLU, fused RMSNorm)",
             "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms * 1e3, 3),
@@ -247,6 +261,9 @@ def run_ours(args):
         return run_stream70(args)
     big = args.workload == "8b"
     cfg = dict(CONFIG_8B if big else CONFIG_7B)
+    qname = {"7b-q8": "Q8_0", "7b-q4": "Q4_0"}.get(args.workload)
+    if qname:
+        cfg["wdtype"] = vsl.Q8_0 if qname == "Q8_0" else vsl.Q4_0
     if args.layers:
         cfg["n_layers"] = args.layers
     B = BATCH_8B if big else 1
@@ -320,7 +337,7 @@ def run_ours(args):
     step_bytes = 0.5 * (bytes_start + bytes_end)  # per GPU; KV grows by one position per step
     step_gbs = step_bytes / (ms / 1e3 / args.steps) / 1e9
     cb = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not big:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not big and not qname:
         cb = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0 and big:
         step_roof = {"bound": "hbm", "kernel": "whole decode step (weights + 16 x 8192-position KV)",
@@ -347,11 +364,14 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     elif rank == 0:
         line = {
-            "metric": "decode tok/s (7B fp16, bs1)", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "metric": f"decode tok/s (7B {qname or 'fp16'}, bs1)", "value": round(tok_s, 3), "unit": "tok/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": qname.lower() + " weights, f32 math" if qname else "f16",
             "data": "synthetic (seeded random-init weights filled in HBM)",
-            "config": {"workload": "7B Llama shape fp16 (BASELINE configs[1]), batch 1, 128-token prompt (prefill), "
+            "config": {"workload": f"7B Llama shape {qname or 'fp16'} (BASELINE configs[1]"
+                                   f"{' with block-quantized weights' if qname else ''}), batch 1, "
+                                   "128-token prompt (prefill), "
                                    f"decode positions {PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
                        "model": "llama-7b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
                        "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps,
@@ -529,7 +549,19 @@ def run_profile_case(args):
     import torch
 
     import vsl
-    if args.profile_case == "tc_gemm":
+    if args.profile_case in ("gemv_q8", "gemv_q4"):
+        dt = vsl.Q8_0 if args.profile_case == "gemv_q8" else vsl.Q4_0
+        N, K = 2 * CONFIG_7B["ffn"], CONFIG_7B["d_model"]
+        rb = vsl.weight_row_bytes(dt, K)
+        Ws = [torch.empty(N, rb, dtype=torch.uint8, device="cuda") for _ in range(4)]  # > L2 in total
+        for i, w in enumerate(Ws):
+            vsl.synth_fill_q(w, dt, 7, 500 + i, N, K)
+        x = torch.randn(1, K, device="cuda")
+        nw = torch.ones(K, device="cuda")
+        y = torch.zeros(1, N // 2, device="cuda")
+        for i in range(3):
+            vsl.gemv(dt, Ws[i % 4], N, K, x, 1, y, vsl.EPI_SWIGLU, nw, 1e-5)
+    elif args.profile_case == "tc_gemm":
         N, K, B = (int(v) for v in args.profile_shape.split(","))
         # enough weight copies that every launch reads its weights from HBM (more than L2)
         Ws = [torch.randn(N, K, device="cuda").mul_(0.02).half() for _ in range(max(2, -(-300_000_000 // (N * K * 2))))]

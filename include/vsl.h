@@ -235,6 +235,10 @@ VSL_API void vsl_engine_default_options(vsl_engine_options* opt);
  * tensor's block data (host) into that layout (host, row pitch out_ld bytes). The projection
  * kernels (vsl_gemv, vsl_qkv_rope_append, vsl_lm_head_sample) accept these dtypes. */
 VSL_API int vsl_weight_row_bytes(int dtype, int K, size_t* bytes);
+/* Seeded block-quantized tensor [rows][cols] (the engine's synthetic weights) written in the
+ * device layout with row pitch row_pitch bytes (>= vsl_weight_row_bytes). */
+VSL_API int vsl_synth_fill_q(void* dst, int dtype, size_t row_pitch, uint64_t seed, uint64_t tensor_id, size_t rows,
+                             size_t cols, double sigma, void* stream);
 VSL_API int vsl_repack_gguf_rows(int dtype, const void* blocks, size_t cols, size_t row0, size_t nrows, size_t col0,
                                  size_t ncols, void* out, size_t out_ld, int legacy_q4);
 

@@ -193,55 +193,91 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams 
 // ---------------------------------------------------------------------------------------
 // Block-quantized weights (Q8_0 / Q4_0 in the repacked row layout of quant_layout.h)
 // ---------------------------------------------------------------------------------------
-// One 16-byte vector of quants is 16 (Q8_0) or 32 (Q4_0) weights of one block. Quants become
-// exact fp32 integers without a conversion instruction: a byte (or nibble) placed under the
-// exponent pattern 0x4B000000 is the float 2^23 + value, and subtracting 2^23 (plus the
-// format's zero point) leaves the integer. Each vector contributes d * sum(q * x) to the row.
+// One 16-byte vector of quants is 16 (Q8_0, half a block) or 32 (Q4_0, one block) weights.
+// Quants become floats without conversion instructions: a 32-bit pattern u < 2^23 read as an
+// fp32 value is exactly u * 2^-149 (a subnormal, or the first normal binade), so one byte
+// permute that drops the biased quant (q + 128 for Q8_0, the stored nibble for Q4_0) into the
+// low byte of a zero word gives the exact float u * 2^-149. The activations are staged
+// multiplied by 2^64, so each product u * x * 2^-85 stays a normal fp32 number, and the
+// products are accumulated two at a time with the packed fp32 FMA (fma.rn.f32x2) of sm_100.
+// Per vector the zero point comes out once: sum(q * x) = 2^85 * sum(u * x') - z * sum(x), with
+// z = 128 (Q8_0) or 8 (Q4_0) and the per-vector activation sums staged beside the activations;
+// the row accumulates d * that (one fp32 FMA per vector and row).
 template <int QT> struct QTraits;
 template <> struct QTraits<VSL_Q8_0> {
-    static constexpr int VEC = 16;  // weights per 16-byte vector (half a block)
-    __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
-        // int8 -> biased byte (q + 128) -> float 2^23 + q + 128
+    static constexpr int VEC = 16;     // weights per 16-byte vector
+    static constexpr float ZP = 128.0f;  // bias of the stored byte
+    // u[i] = biased quant of element i (as fp32 bit pattern)
+    __device__ __forceinline__ static void unpack(const uint4& v, uint32_t* u) {
         const uint32_t w[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
 #pragma unroll
         for (int j = 0; j < 4; j++)
 #pragma unroll
-            for (int i = 0; i < 4; i++)
-                f[4 * j + i] = __uint_as_float(__byte_perm(w[j], 0x4B000000u, 0x7540u + i)) - 8388736.0f;
+            for (int i = 0; i < 4; i++) u[4 * j + i] = __byte_perm(w[j], 0u, 0x4440u + i);
     }
 };
 template <> struct QTraits<VSL_Q4_0> {
-    static constexpr int VEC = 32;  // weights per 16-byte vector (one block)
-    __device__ __forceinline__ static void unpack(const uint4& v, float* f) {
+    static constexpr int VEC = 32;
+    static constexpr float ZP = 8.0f;
+    __device__ __forceinline__ static void unpack(const uint4& v, uint32_t* u) {
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const uint32_t lo = w[j] & 0x0F0F0F0Fu, hi = (w[j] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                // element 4j + i from the low nibbles, 16 + 4j + i from the high ones; zero point 8
-                f[4 * j + i] = __uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7540u + i)) - 8388616.0f;
-                f[16 + 4 * j + i] = __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7540u + i)) - 8388616.0f;
+                u[4 * j + i] = __byte_perm(lo, 0u, 0x4440u + i);       // element 4j + i
+                u[16 + 4 * j + i] = __byte_perm(hi, 0u, 0x4440u + i);  // element 16 + 4j + i
             }
         }
     }
 };
 
-// Activations are staged as fp32 with 4 floats of padding after every VEC values, so the
-// 16-byte shared-memory reads of a warp (lane l reads chunk l) fall in distinct banks.
+__device__ __forceinline__ unsigned long long pack2(uint32_t lo, uint32_t hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ unsigned long long pack2f(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+// acc.{x,y} += a.{x,y} * b.{x,y}, each lane one fp32 FMA (round to nearest, subnormals kept)
+__device__ __forceinline__ void ffma2(unsigned long long& acc, unsigned long long a, unsigned long long b) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(a), "l"(b));
+}
+__device__ __forceinline__ float sum2(unsigned long long v) {
+    float lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+    return lo + hi;
+}
+
+constexpr float Q_XSCALE = 18446744073709551616.0f;  // 2^64, activation pre-scale
+constexpr float Q_UNSCALE = 38685626227668133590597632.0f;  // 2^85 = 2^149 / 2^64
+
+// Activations are staged as fp32 (times 2^64) with 4 floats of padding after every VEC
+// values, so the 16-byte shared-memory reads of a warp (lane l reads chunk l) fall in
+// distinct banks; the per-vector sums (times the zero point) follow the activations.
 template <int QT>
 __host__ __device__ constexpr int q_xpitch(int K) {
     return K + (K / QTraits<QT>::VEC) * 4;
 }
+// per activation row: the padded activations, then the vector sums, rounded up to 4 floats so
+// that every row starts 16-byte aligned (the float4 reads)
+template <int QT>
+__host__ __device__ constexpr int q_stage_floats(int K) {
+    return q_xpitch<QT>(K) + (K / QTraits<QT>::VEC + 3) / 4 * 4;
+}
 
 template <int QT, int NB, int EK, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParams p) {
-    extern __shared__ __align__(16) float xs[];  // [NB][q_xpitch(K)] fp32 activations, padded
+    extern __shared__ __align__(16) float xs[];  // [NB][q_stage_floats(K)]
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = QTraits<QT>::VEC;
     constexpr int CH = VEC + 4;  // padded chunk
     const int K = p.K, N = p.N;
-    const int XP = q_xpitch<QT>(K);
+    const int XP = q_xpitch<QT>(K), SP = q_stage_floats<QT>(K);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int NW = GEMV_THREADS / 32;
     const int nvec = K / VEC;
@@ -298,8 +334,18 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             const float v = b < B ? p.x[(size_t)b * K + k] : 0.0f;
-            xs[b * XP + xi] = NORM ? v / den[b] * w : v;
+            xs[b * SP + xi] = (NORM ? v / den[b] * w : v) * Q_XSCALE;
         }
+    }
+    __syncthreads();
+    // zero-point term of every vector: z * sum of its activations (fixed order)
+    for (int i = threadIdx.x; i < NB * nvec; i += GEMV_THREADS) {
+        const int b = i / nvec, v = i - b * nvec;
+        const float* c = xs + b * SP + v * CH;
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VEC; j++) s += c[j];
+        xs[b * SP + XP + v] = s * (QTraits<QT>::ZP / Q_XSCALE);
     }
     __syncthreads();
 
@@ -316,48 +362,35 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
         const int r1 = has1 ? r0 + 1 : r0;
         const char* row0 = W + (size_t)r0 * RB;
         const char* row1 = W + (size_t)r1 * RB;
-        const __half* sc0 = reinterpret_cast<const __half*>(row0 + QB);
-        const __half* sc1 = reinterpret_cast<const __half*>(row1 + QB);
-        if (lane == 0 && unit + NW < u_end) {
+        const unsigned short* sc0 = reinterpret_cast<const unsigned short*>(row0 + QB);
+        const unsigned short* sc1 = reinterpret_cast<const unsigned short*>(row1 + QB);
+        if (lane == 0 && unit + NW < u_end) {  // keep the L2 window moving: this warp's next pair
             const int rn = 2 * (unit + NW);
-            const int rows = min(2, N - rn);
-            prefetch_l2(W + (size_t)rn * RB, (uint32_t)(rows * RB));
+            prefetch_l2(W + (size_t)rn * RB, (uint32_t)(min(2, N - rn) * RB));
         }
         float acc0[NB], acc1[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
         auto consume = [&](const uint4& a, const uint4& c, float d0, float d1, int v) {
-            float f[VEC];
-            float t0[NB], t1[NB];
-#pragma unroll
-            for (int b = 0; b < NB; b++) { t0[b] = 0.0f; t1[b] = 0.0f; }
-            QTraits<QT>::unpack(a, f);
+            uint32_t ua[VEC], uc[VEC];
+            QTraits<QT>::unpack(a, ua);
+            QTraits<QT>::unpack(c, uc);
 #pragma unroll
             for (int b = 0; b < NB; b++) {
-                const float4* xv = reinterpret_cast<const float4*>(xs + b * XP + v * CH);
+                unsigned long long t0 = 0ull, t1 = 0ull;
+                const float4* xv = reinterpret_cast<const float4*>(xs + b * SP + v * CH);
 #pragma unroll
                 for (int i = 0; i < VEC / 4; i++) {
                     const float4 xx = xv[i];
-                    t0[b] = fmaf(f[4 * i + 0], xx.x, t0[b]);
-                    t0[b] = fmaf(f[4 * i + 1], xx.y, t0[b]);
-                    t0[b] = fmaf(f[4 * i + 2], xx.z, t0[b]);
-                    t0[b] = fmaf(f[4 * i + 3], xx.w, t0[b]);
+                    const unsigned long long x01 = pack2f(xx.x, xx.y), x23 = pack2f(xx.z, xx.w);
+                    ffma2(t0, pack2(ua[4 * i + 0], ua[4 * i + 1]), x01);
+                    ffma2(t0, pack2(ua[4 * i + 2], ua[4 * i + 3]), x23);
+                    ffma2(t1, pack2(uc[4 * i + 0], uc[4 * i + 1]), x01);
+                    ffma2(t1, pack2(uc[4 * i + 2], uc[4 * i + 3]), x23);
                 }
-            }
-            QTraits<QT>::unpack(c, f);
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                const float4* xv = reinterpret_cast<const float4*>(xs + b * XP + v * CH);
-#pragma unroll
-                for (int i = 0; i < VEC / 4; i++) {
-                    const float4 xx = xv[i];
-                    t1[b] = fmaf(f[4 * i + 0], xx.x, t1[b]);
-                    t1[b] = fmaf(f[4 * i + 1], xx.y, t1[b]);
-                    t1[b] = fmaf(f[4 * i + 2], xx.z, t1[b]);
-                    t1[b] = fmaf(f[4 * i + 3], xx.w, t1[b]);
-                }
-                acc0[b] = fmaf(d0, t0[b], acc0[b]);
-                acc1[b] = fmaf(d1, t1[b], acc1[b]);
+                const float zx = xs[b * SP + XP + v];
+                acc0[b] = fmaf(d0, fmaf(Q_UNSCALE, sum2(t0), -zx), acc0[b]);
+                acc1[b] = fmaf(d1, fmaf(Q_UNSCALE, sum2(t1), -zx), acc1[b]);
             }
         };
         int v = lane;
@@ -369,8 +402,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
                 const int vv = v + 32 * u;
                 a[u] = ldg_stream(row0 + (size_t)vv * 16);
                 c[u] = ldg_stream(row1 + (size_t)vv * 16);
-                s0[u] = __ldcs(reinterpret_cast<const unsigned short*>(sc0) + (vv * VEC) / QBLK);
-                s1[u] = __ldcs(reinterpret_cast<const unsigned short*>(sc1) + (vv * VEC) / QBLK);
+                s0[u] = __ldcs(sc0 + (vv * VEC) / QBLK);
+                s1[u] = __ldcs(sc1 + (vv * VEC) / QBLK);
             }
 #pragma unroll
             for (int u = 0; u < U; u++)
@@ -380,7 +413,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
         for (; v < nvec; v += 32) {
             const uint4 a = ldg_stream(row0 + (size_t)v * 16);
             const uint4 c = ldg_stream(row1 + (size_t)v * 16);
-            const float d0 = __half2float(sc0[(v * VEC) / QBLK]), d1 = __half2float(sc1[(v * VEC) / QBLK]);
+            const float d0 = __half2float(__ushort_as_half(__ldcs(sc0 + (v * VEC) / QBLK)));
+            const float d1 = __half2float(__ushort_as_half(__ldcs(sc1 + (v * VEC) / QBLK)));
             consume(a, c, d0, d1, v);
         }
 #pragma unroll
@@ -410,8 +444,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
 // counts are 1, 2 and 4
 static int max_rows_per_launch(int wdtype, int K) {
     const size_t room = 200 * 1024;
-    const size_t pitch = wdtype == VSL_Q8_0 ? (size_t)q_xpitch<VSL_Q8_0>(K)
-                         : wdtype == VSL_Q4_0 ? (size_t)q_xpitch<VSL_Q4_0>(K) : (size_t)K;
+    const size_t pitch = wdtype == VSL_Q8_0 ? (size_t)q_stage_floats<VSL_Q8_0>(K)
+                         : wdtype == VSL_Q4_0 ? (size_t)q_stage_floats<VSL_Q4_0>(K) : (size_t)K;
     const int c = (int)(room / (pitch * sizeof(float)));
     return c >= 4 ? 4 : c >= 2 ? 2 : c;
 }
@@ -448,7 +482,7 @@ static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
 template <int QT, int NB, int EK, bool NORM>
 static int launch_gemv_q_t(const GemvParams& p, cudaStream_t st) {
     auto kern = gemv_q_kernel<QT, NB, EK, NORM>;
-    const size_t smem = (size_t)NB * q_xpitch<QT>(p.K) * sizeof(float);
+    const size_t smem = (size_t)NB * q_stage_floats<QT>(p.K) * sizeof(float);
     static thread_local int configured_dev = -1;
     static thread_local size_t configured_smem = 0;
     static thread_local int occ = 1;

@@ -394,6 +394,12 @@ extern "C" int vsl_argmax(const float* logits, int B, int V, int32_t* out_ids, v
                          "argmax");
 }
 
+extern "C" int vsl_synth_fill_q(void* dst, int dtype, size_t row_pitch, uint64_t seed, uint64_t tensor_id,
+                                size_t rows, size_t cols, double sigma, void* stream) {
+    return vsl::synthq2d_impl(dst, dtype, row_pitch, seed, tensor_id, 0, rows, cols, 0, cols, sigma,
+                              (cudaStream_t)stream);
+}
+
 extern "C" int vsl_synth_fill(void* dst, int dtype, uint64_t seed, uint64_t tensor_id, uint64_t start, uint64_t n,
                               double sigma, void* stream) {
     return synth_impl(dst, dtype, seed, tensor_id, start, n, sigma, (cudaStream_t)stream);

@@ -79,6 +79,7 @@ def lib() -> C.CDLL:
         "vsl_nccl_unique_id": (i32, [vp]),
         "vsl_gguf_model_config": (i32, [C.c_char_p, C.POINTER(ModelConfig)]),
         "vsl_weight_row_bytes": (i32, [i32, i32, C.POINTER(sz)]),
+        "vsl_synth_fill_q": (i32, [vp, i32, sz, u64, u64, sz, sz, f64, vp]),
         "vsl_repack_gguf_rows": (i32, [i32, vp, sz, sz, sz, sz, sz, vp, sz, i32]),
         "vsl_gguf_tensor_info": (i32, [C.c_char_p, C.c_char_p, C.POINTER(i32), C.POINTER(u64), C.POINTER(u64)]),
         "vsl_engine_create_gguf": (i32, [C.c_char_p, C.POINTER(EngineOptions), C.POINTER(vp)]),
@@ -161,6 +162,12 @@ def weight_row_bytes(dtype: int, K: int) -> int:
     out = C.c_size_t()
     check(lib().vsl_weight_row_bytes(dtype, K, C.byref(out)))
     return out.value
+
+
+def synth_fill_q(dst, dtype: int, seed: int, tid: int, rows: int, cols: int, sigma: float = 0.02, stream=0):
+    """Seeded Q8_0 / Q4_0 tensor [rows][cols] into device memory in the device row layout."""
+    check(lib().vsl_synth_fill_q(_ptr(dst), dtype, weight_row_bytes(dtype, cols), seed, tid, rows, cols, sigma,
+                                 stream))
 
 
 def repack_gguf_rows(dtype: int, blocks, rows: int, cols: int, legacy_q4: bool = False, row0: int = 0,
