@@ -294,19 +294,59 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
     if (!is_last) return;
     __threadfence();
     // ---- combine the active splits of every head in this group ----
+    // The split statistics and weights are staged in shared memory by all threads at once (one
+    // L2 round trip each), so the combine costs a few round trips rather than one per split.
+    // Sums run in split order, as a sequential combine would.
+    float* cw = part_s;                       // exp(m_s - M) of a tile of splits
+    float* cl = part_s + FD_GMAX * FD_CHUNK;  // l_s of the same tile
+    constexpr int TILE = FD_GMAX * FD_CHUNK;
+    float* red = m_s;                         // FD_THREADS / 32 partial maxima (own stats are written)
     for (int j = 0; j < G; j++) {
         const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits;
-        float M = -CUDART_INF_F;
-        for (int s = 0; s < n_active; s++) M = fmaxf(M, __ldcg(p.ws_ml + (row0 + s) * 2));
+        float mx = -CUDART_INF_F;
+        for (int s = tid; s < n_active; s += FD_THREADS) mx = fmaxf(mx, __ldcg(p.ws_ml + (row0 + s) * 2));
+        mx = warp_max(mx);
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+        float M = red[0];
+#pragma unroll
+        for (int w = 1; w < FD_THREADS / 32; w++) M = fmaxf(M, red[w]);
         float L = 0.0f;
-        for (int s = 0; s < n_active; s++)
-            L += __ldcg(p.ws_ml + (row0 + s) * 2 + 1) * expf(__ldcg(p.ws_ml + (row0 + s) * 2) - M);
-        for (int e = tid; e < HD; e += FD_THREADS) {
-            float acc = 0.0f;
-            for (int s = 0; s < n_active; s++)
-                acc += __ldcg(p.ws_o + (row0 + s) * HD + e) * expf(__ldcg(p.ws_ml + (row0 + s) * 2) - M);
-            p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = acc / L;
+        float acc[EPT];
+#pragma unroll
+        for (int i = 0; i < EPT; i++) acc[i] = 0.0f;
+        for (int t0 = 0; t0 < n_active; t0 += TILE) {
+            const int nt = min(TILE, n_active - t0);
+            __syncthreads();  // previous tile (and red) consumed
+            for (int s = tid; s < nt; s += FD_THREADS) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (row0 + t0 + s) * 2));
+                cw[s] = expf(ml.x - M);
+                cl[s] = ml.y;
+            }
+            __syncthreads();
+            for (int s = 0; s < nt; s++) L += cl[s] * cw[s];
+#pragma unroll
+            for (int i = 0; i < EPT; i++) {
+                const int e = tid + i * FD_THREADS;
+                if (e >= HD) continue;
+                const float* src = p.ws_o + (row0 + t0) * HD + e;
+                int s = 0;
+                for (; s + 8 <= nt; s += 8) {  // eight independent loads in flight
+                    float o[8];
+#pragma unroll
+                    for (int u = 0; u < 8; u++) o[u] = __ldcg(src + (size_t)(s + u) * HD);
+#pragma unroll
+                    for (int u = 0; u < 8; u++) acc[i] += o[u] * cw[s + u];
+                }
+                for (; s < nt; s++) acc[i] += __ldcg(src + (size_t)s * HD) * cw[s];
+            }
         }
+#pragma unroll
+        for (int i = 0; i < EPT; i++) {
+            const int e = tid + i * FD_THREADS;
+            if (e < HD) p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = acc[i] / L;
+        }
+        __syncthreads();  // red / cw reused by the next head
     }
     if (tid == 0) p.counters[(size_t)b * p.n_kv + g] = 0;
 }
