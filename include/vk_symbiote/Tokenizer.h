@@ -1,10 +1,19 @@
-// Text <-> token id conversion with the behaviour the reference actually exhibits
-// (vk_symbiote/src/Tokenizer.cpp). Its GGUF vocabulary reader reads key, type and
-// length in the wrong order (:41-46), so on standard GGUF files it always falls back to the
-// 256-entry byte vocabulary (:113-129): encode() maps every non-whitespace byte of the text
-// to its value (words are split on whitespace, :131-178) and returns {0} for empty text;
-// decode() maps each id to the byte id % 256 and joins them with single spaces (:180-198).
-// This class reproduces that contract; a real subword tokenizer is outside the decode path.
+// Text <-> token ids.
+//
+// From a GGUF file with a SentencePiece vocabulary (tokenizer.ggml.model "llama", tokens,
+// scores and token types) the tokenizer is the SentencePiece BPE of that vocabulary: spaces
+// become U+2581, a dummy prefix space is added, UTF-8 characters are merged pairwise in order
+// of the merged piece's score (ties: the leftmost pair), pieces missing from the vocabulary
+// fall back to <0xXX> byte tokens, and BOS is prepended (tokenizer.ggml.add_bos_token,
+// default true). decode() reverses it (control tokens render as nothing, byte tokens as their
+// byte, U+2581 as a space, the dummy prefix removed).
+//
+// Without such a vocabulary it keeps the behaviour the reference actually exhibits
+// (vk_symbiote/src/Tokenizer.cpp): its GGUF reader reads key, type and length in the wrong
+// order (:41-46), so it always falls back to the 256-entry byte vocabulary (:113-129):
+// encode() maps every non-whitespace byte of the text to its value (words are split on
+// whitespace, :131-178) and returns {0} for empty text; decode() maps each id to the byte
+// id % 256 and joins them with single spaces (:180-198).
 #pragma once
 
 #include <cstdint>
@@ -21,10 +30,25 @@ class VSL_CPP_API Tokenizer {
 public:
     static std::unique_ptr<Tokenizer> from_gguf(const Path& gguf_path);
     static std::unique_ptr<Tokenizer> byte_level();
+    // SentencePiece BPE over an explicit vocabulary (token types: 1 normal, 2 unknown,
+    // 3 control, 6 byte; GGUF's tokenizer.ggml.token_type)
+    static std::unique_ptr<Tokenizer> sentencepiece(const std::vector<std::string>& tokens,
+                                                    const std::vector<float>& scores,
+                                                    const std::vector<int32_t>& types, uint32_t bos_id,
+                                                    uint32_t eos_id, uint32_t unk_id, bool add_bos,
+                                                    bool add_space_prefix);
+    ~Tokenizer();
 
     std::vector<uint32_t> encode(const std::string& text) const;
     std::string decode(const std::vector<uint32_t>& tokens) const;
-    uint32_t vocab_size() const { return 256; }
+    uint32_t vocab_size() const;
+    bool is_subword() const { return spm_ != nullptr; }
+    uint32_t bos_id() const;
+    uint32_t eos_id() const;
+
+private:
+    struct Spm;
+    Spm* spm_ = nullptr;  // null: the byte-level contract
 };
 
 }  // namespace vk_symbiote

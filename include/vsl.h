@@ -336,6 +336,19 @@ VSL_API int vsl_engine_generate_batch(vsl_engine* e, const int32_t* prompts, con
  * others continue to decode through vsl_engine_run. */
 VSL_API int vsl_engine_reset_seq(vsl_engine* e, int seq);
 
+/* ======================================================================================
+ * Tokenizer (host only): SentencePiece BPE from a GGUF vocabulary (tokenizer.ggml.model
+ * "llama"), else the reference's byte-level behaviour (Tokenizer.cpp:113-198).
+ * vsl_tokenize writes the ids (BOS first when the vocabulary asks for it) and their count
+ * in *n (VSL_ERR_BOUNDS if cap is smaller); vsl_detokenize the UTF-8 text and its length.
+ * ====================================================================================== */
+typedef struct vsl_tokenizer vsl_tokenizer;
+VSL_API int vsl_tokenizer_create_gguf(const char* path, vsl_tokenizer** out);
+VSL_API void vsl_tokenizer_destroy(vsl_tokenizer* t);
+VSL_API int vsl_tokenizer_info(vsl_tokenizer* t, int* vocab_size, int* is_subword, int32_t* bos_id, int32_t* eos_id);
+VSL_API int vsl_tokenize(vsl_tokenizer* t, const char* text, size_t len, int32_t* out, int cap, int* n);
+VSL_API int vsl_detokenize(vsl_tokenizer* t, const int32_t* ids, int n, char* out, size_t cap, size_t* len);
+
 /* Weight residency under vram_budget_gb (replaces PackManager::get_vram_stats and the pack
  * scheduler's state, NomadPack.cpp:1190-1249, 1323-1326; VulkanSymbioteEngine.cpp:1555-1599):
  * layers 0..resident_layers-1 stay in HBM, the other streamed_layers live in pinned host memory

@@ -17,31 +17,6 @@
 namespace vk_symbiote {
 
 // ---------------------------------------------------------------------------------------
-// Tokenizer (byte-level contract of the reference, Tokenizer.cpp:113-198)
-// ---------------------------------------------------------------------------------------
-std::unique_ptr<Tokenizer> Tokenizer::from_gguf(const Path&) { return byte_level(); }
-std::unique_ptr<Tokenizer> Tokenizer::byte_level() { return std::unique_ptr<Tokenizer>(new Tokenizer()); }
-
-std::vector<uint32_t> Tokenizer::encode(const std::string& text) const {
-    std::vector<uint32_t> ids;
-    std::istringstream in(text);
-    std::string word;
-    while (in >> word)
-        for (unsigned char c : word) ids.push_back(c);
-    if (ids.empty()) ids.push_back(0);
-    return ids;
-}
-
-std::string Tokenizer::decode(const std::vector<uint32_t>& tokens) const {
-    std::string out;
-    for (size_t i = 0; i < tokens.size(); i++) {
-        out += (char)(unsigned char)(tokens[i] % 256u);
-        if (i + 1 < tokens.size()) out += ' ';
-    }
-    return out;
-}
-
-// ---------------------------------------------------------------------------------------
 // VulkanSymbioteEngine
 // ---------------------------------------------------------------------------------------
 static void throw_vsl(const char* what) {

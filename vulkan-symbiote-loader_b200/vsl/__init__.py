@@ -79,6 +79,11 @@ def lib() -> C.CDLL:
         "vsl_nccl_unique_id": (i32, [vp]),
         "vsl_gguf_model_config": (i32, [C.c_char_p, C.POINTER(ModelConfig)]),
         "vsl_weight_row_bytes": (i32, [i32, i32, C.POINTER(sz)]),
+        "vsl_tokenizer_create_gguf": (i32, [C.c_char_p, C.POINTER(vp)]),
+        "vsl_tokenizer_destroy": (None, [vp]),
+        "vsl_tokenizer_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i32), C.POINTER(i32)]),
+        "vsl_tokenize": (i32, [vp, C.c_char_p, sz, vp, i32, C.POINTER(i32)]),
+        "vsl_detokenize": (i32, [vp, vp, i32, C.c_char_p, sz, C.POINTER(sz)]),
         "vsl_synth_fill_q": (i32, [vp, i32, sz, u64, u64, sz, sz, f64, vp]),
         "vsl_repack_gguf_rows": (i32, [i32, vp, sz, sz, sz, sz, sz, vp, sz, i32]),
         "vsl_gguf_tensor_info": (i32, [C.c_char_p, C.c_char_p, C.POINTER(i32), C.POINTER(u64), C.POINTER(u64)]),
@@ -155,6 +160,47 @@ def rmsnorm(x, w, B, d, eps, y, stream=0):
 
 def gemv(wdtype, W, N, K, x, B, y, epilogue=EPI_STORE, norm_w=None, eps=0.0, stream=0):
     check(lib().vsl_gemv(wdtype, _ptr(W), N, K, _ptr(x), B, _ptr(y), epilogue, _ptr(norm_w), eps, stream))
+
+
+class Tokenizer:
+    """SentencePiece BPE of a GGUF vocabulary (tokenizer.ggml.model "llama"), else the
+    reference's byte-level behaviour."""
+
+    def __init__(self, path: str):
+        self.h = C.c_void_p()
+        check(lib().vsl_tokenizer_create_gguf(path.encode(), C.byref(self.h)))
+        v, sw, bos, eos = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        check(lib().vsl_tokenizer_info(self.h, C.byref(v), C.byref(sw), C.byref(bos), C.byref(eos)))
+        self.vocab_size, self.is_subword, self.bos_id, self.eos_id = v.value, bool(sw.value), bos.value, eos.value
+
+    def encode(self, text: str) -> list[int]:
+        import numpy as np
+        b = text.encode("utf-8")
+        n = C.c_int()
+        cap = 2 * len(b) + 8
+        out = np.empty(cap, np.int32)
+        check(lib().vsl_tokenize(self.h, b, len(b), out.ctypes.data, cap, C.byref(n)))
+        return out[:n.value].tolist()
+
+    def decode(self, ids) -> str:
+        import numpy as np
+        a = np.ascontiguousarray(ids, np.int32)
+        n = C.c_size_t()
+        lib().vsl_detokenize(self.h, a.ctypes.data, a.size, None, 0, C.byref(n))  # size query
+        buf = C.create_string_buffer(max(n.value, 1))
+        check(lib().vsl_detokenize(self.h, a.ctypes.data, a.size, buf, n.value, C.byref(n)))
+        return buf.raw[:n.value].decode("utf-8", errors="replace")
+
+    def close(self):
+        if self.h:
+            lib().vsl_tokenizer_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def weight_row_bytes(dtype: int, K: int) -> int:
