@@ -58,10 +58,11 @@ def parse():
                          "Q8_0 / Q4_0 block-quantized weights; 8b: BASELINE configs[3], batch 16 over "
                          "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b-stream: "
                          "BASELINE configs[4] on one GPU under a 64 GB HBM cap (layers streamed from host)")
-    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4"],
+    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "prefill"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
                          "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 = "
-                         "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 weights at batch 1")
+                         "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 weights at batch 1; prefill = "
+                         "three 128-token prompt passes on the 7B shape (--layers, default 4)")
     ap.add_argument("--profile-shape", default="32000,4096,16",
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
@@ -549,7 +550,18 @@ def run_profile_case(args):
     import torch
 
     import vsl
-    if args.profile_case in ("gemv_q8", "gemv_q4"):
+    if args.profile_case == "prefill":
+        from vsl import synth
+        cfg = dict(CONFIG_7B)
+        cfg["n_layers"] = args.layers or 4
+        with vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, max_batch=1, max_seq=512) as e:
+            prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
+            for _ in range(3):
+                e.reset()
+                e.prefill(prompt)
+            if e.device_status() != 0:
+                raise SystemExit("device status")
+    elif args.profile_case in ("gemv_q8", "gemv_q4"):
         dt = vsl.Q8_0 if args.profile_case == "gemv_q8" else vsl.Q4_0
         N, K = 2 * CONFIG_7B["ffn"], CONFIG_7B["d_model"]
         rb = vsl.weight_row_bytes(dt, K)
