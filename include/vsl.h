@@ -220,6 +220,9 @@ typedef struct {
                           replayed as a CUDA graph with programmatic dependent launch  */
     int use_p2p;       /* tensor parallel: 1 (default) = one-shot NVLink peer-memory all-reduces
                           (CUDA IPC buffers, one kernel per reduction); 0 = NCCL            */
+    int fuse_allreduce; /* tensor parallel with use_p2p: 1 (default) = the residual sums ride on the
+                          projections (row-parallel GEMV pushes its rows to every rank, the next
+                          projection sums them while staging); 0 = separate all-reduce kernel */
     int legacy_q4;     /* 1 = read GGUF Q4_0 nibbles in the reference loader's order
                           (GGUFLoader.cpp:1146-1160: element 2i low, 2i+1 high nibble of
                           byte i); 0 (default) = ggml's order (element i low, i+16 high)  */

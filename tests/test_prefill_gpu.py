@@ -62,13 +62,15 @@ def test_tiny_fp32_prefill_logits_match_oracle(golden, fixture_gguf):
         assert nxt2 == nxt and float(np.abs(lg2 - olg).max()) < 1e-4
 
 
-@pytest.mark.parametrize("wdtype,n_prompt,max_seq", [(vsl.F16, 100, 256), (vsl.BF16, 64, 256),
-                                                     (vsl.BF16, 200, 2048)])
-def test_half_prefill_chunks_match_oracle(wdtype, n_prompt, max_seq):
-    """100 tokens = chunks of 64 + 36 rows (tcgen05 projections); max_seq 2048 routes attention
-    through the tcgen05-score kernel. Then 6 teacher-forced decode steps."""
-    cfg = dict(n_layers=2, d_model=1024, n_heads=8, n_kv_heads=2, head_dim=128, ffn=2816, vocab=6000,
-               rope_theta=10000.0, rms_eps=1e-5, wdtype=wdtype)
+@pytest.mark.parametrize("wdtype,n_prompt,max_seq,hd", [(vsl.F16, 100, 256, 128), (vsl.BF16, 64, 256, 128),
+                                                        (vsl.BF16, 200, 2048, 128), (vsl.BF16, 90, 256, 64),
+                                                        (vsl.F16, 150, 256, 64)])
+def test_half_prefill_chunks_match_oracle(wdtype, n_prompt, max_seq, hd):
+    """100 tokens = chunks of 64 + 36 rows (tcgen05 projections); head_dim 128 takes the
+    tcgen05-score attention, head_dim 64 the split-K kernel, whose split counters must stay
+    valid when the last chunk has fewer rows than the first. Then 6 teacher-forced decode steps."""
+    cfg = dict(n_layers=2, d_model=1024, n_heads=1024 // hd, n_kv_heads=256 // hd, head_dim=hd, ffn=2816,
+               vocab=6000, rope_theta=10000.0, rms_eps=1e-5, wdtype=wdtype)
     seed = 41
     prompt = synth.synth_ids(seed, 5, n_prompt, cfg["vocab"]).tolist()
     follow = synth.synth_ids(seed, 6, 6, cfg["vocab"]).tolist()

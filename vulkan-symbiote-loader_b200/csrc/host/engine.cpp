@@ -212,6 +212,7 @@ int DecodeEngine::alloc_buffers() {
         {(void**)&rope_sin_, (size_t)opt_.max_seq * half * 4},
         {(void**)&page_table_, mb * (size_t)max_pages_ * 4},
         {(void**)&ar_epochs_, 16},
+        {(void**)&ar_done_, 16},
         {(void**)&fs_bar_, 16},
         {(void**)&fs_abort_, 4},
         {(void**)&fs_att_ws_, mb * (size_t)nh_l_ * (size_t)((opt_.max_seq + 63) / 64) * (hd + 2) * 4},
@@ -676,6 +677,7 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(status_, 0, 4, stream_));
     CK(cudaMemsetAsync(fs_bar_, 0, 16, stream_));
     CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
+    CK(cudaMemsetAsync(ar_done_, 0, 16, stream_));
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
     if (pf_tc_ws_) CK(cudaMemsetAsync(pf_tc_route_.ws, 0, pf_tc_route_.bytes, stream_));
@@ -746,7 +748,18 @@ int DecodeEngine::allreduce_sum(float* buf, int count) {
 
 // The decoder layers for B activation rows held in `sb` (the decode step's buffers, or a
 // prefill chunk's, where the rows are consecutive prompt positions of one sequence).
-int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
+// The tensor-parallel residual sums ride on the projections (reduce on read): the row-parallel
+// O and down projections push their rows into every rank's receive slot, and the next
+// projection (gate/up, the next layer's QKV, lm_head) sums the ranks' rows while it stages its
+// normalised input. One GEMV launch over all rows (16/32-bit weights, B <= 4) is needed for
+// that; other shapes use the separate all-reduce kernel.
+bool DecodeEngine::fuse_allreduce(const StepBufs& sb, int B) const {
+    return p2p_ready_ && nccl_ && opt_.fuse_allreduce && !is_quant(cfg_.wdtype) && !sb.shared_pages && B <= 4 &&
+           !(sb.tc && B >= sb.tc->min_batch) && (cfg_.d_model & 1) == 0 &&
+           (size_t)B * cfg_.d_model * sizeof(float) <= p2p_x_.slot_bytes;
+}
+
+int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
     const vsl_model_config& c = cfg_;
     const int d = c.d_model, hd = c.head_dim;
     const int res_epi = opt_.tp_rank == 0 ? VSL_EPI_ADD : VSL_EPI_STORE;  // partial sums reduced into x
@@ -765,6 +778,8 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         CK(cudaStreamWaitEvent(copy_stream_, ev_fork_, 0));
     }
     const int R = (int)residency_.resident_layers;
+    const bool fuse = fuse_allreduce(sb, B);
+    const ArFuse prod{1, &p2p_x_, ar_done_, sb.x}, cons{2, &p2p_x_, ar_done_, sb.x};
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
         const bool last = l + 1 == c.n_layers;
@@ -778,7 +793,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         }
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, sb.x, L.attn_norm, c.rms_eps, B, sb.pos,
                                   rope_cos_, rope_sin_, sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_,
-                                  page_size_, status_, st, L.wo, H(wo_b), tcr));
+                                  page_size_, status_, st, L.wo, H(wo_b), tcr, fuse && l > 0 ? &cons : nullptr));
         if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                     nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st));
@@ -786,15 +801,19 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
                                  head ? wo_b : 0, sb.shared_pages));
-        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
-        RC(allreduce_sum(sb.x, B * d));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr,
+                     fuse ? &prod : nullptr));
+        if (!fuse) RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
-                     H(wd_b), st, tcr));
+                     H(wd_b), st, tcr, fuse ? &cons : nullptr));
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, sb.act, B, sb.x, res_epi, nullptr, 0.0f,
-                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr));
-        RC(allreduce_sum(sb.x, B * d));
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr,
+                     fuse ? &prod : nullptr));
+        if (!fuse) RC(allreduce_sum(sb.x, B * d));
         if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
+    if (x_pending) *x_pending = fuse;
+    else if (fuse) return set_error(VSL_ERR_STATE, "enqueue_layers: fused sums need a consumer");
     return VSL_OK;
 }
 
@@ -808,10 +827,12 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
     StepBufs sb{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
                 tc_ws_ ? &tc_route_ : nullptr, false};
-    RC(enqueue_layers(sb, B));
+    bool pending = false;
+    RC(enqueue_layers(sb, B, &pending));
     const TcRoute* tcr = sb.tc;
+    const ArFuse cons{2, &p2p_x_, ar_done_, x_};
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
-                    seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr));
+                    seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr, pending ? &cons : nullptr));
     if (p2p_ready_) {
         RC(p2p_allreduce(p2p_s_, slots_, B, 1, st));
     } else if (nccl_) {

@@ -107,7 +107,10 @@ private:
         const TcRoute* tc;
         bool shared_pages;  // rows are consecutive positions of one sequence (prompt chunk)
     };
-    int enqueue_layers(const StepBufs& sb, int B);
+    // *x_pending: the last layer's down projection left its rows in the peers' buffers (fused
+    // tensor-parallel sum); the next projection reading x must consume them
+    int enqueue_layers(const StepBufs& sb, int B, bool* x_pending = nullptr);
+    bool fuse_allreduce(const StepBufs& sb, int B) const;
     static constexpr int PF_ROWS = 64;  // prompt rows per prefill chunk
     int alloc_prefill();
     void* pf_mem_ = nullptr;
@@ -172,6 +175,7 @@ private:
     void* p2p_s_opened_[P2P_MAX_RANKS] = {};
     bool p2p_ready_ = false;
     unsigned long long* ar_epochs_ = nullptr;  // device call counters of the two all-reduces
+    unsigned int* ar_done_ = nullptr;          // arrival counters of the fused exchanges (producer, consumer)
     int setup_p2p();
     void* fdtc_ws_ = nullptr;  // long-context attention (tcgen05 scores) workspace; null = split-K kernel
     size_t fdtc_ws_bytes_ = 0;

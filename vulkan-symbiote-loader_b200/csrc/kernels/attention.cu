@@ -355,10 +355,16 @@ static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 static int fd_splits(int max_len, int split_len) { return (max_len + split_len - 1) / split_len; }
 
+// Workspace: split partials from the front, split counters at the tail (+256 bytes of slack), so
+// calls with fewer rows on the same workspace (a prompt pass's last chunk) find their counters
+// inside the range every call leaves at zero, never under another call's partials.
 static size_t fd_workspace(int B, int n_heads, int n_kv, int head_dim, int n_splits) {
     return align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float)) +
            align256((size_t)B * n_heads * n_splits * 2 * sizeof(float)) +
-           align256((size_t)B * n_kv * sizeof(int));
+           align256((size_t)B * n_kv * sizeof(int)) + 256;
+}
+static size_t fd_counters_offset(int B, int n_kv, size_t workspace_bytes) {
+    return (workspace_bytes - (size_t)B * n_kv * sizeof(int)) & ~(size_t)255;
 }
 
 template <int HD, typename KT>
@@ -404,8 +410,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
     p.ws_o = reinterpret_cast<float*>(w);
     w += align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float));
     p.ws_ml = reinterpret_cast<float*>(w);
-    w += align256((size_t)B * n_heads * n_splits * 2 * sizeof(float));
-    p.counters = reinterpret_cast<int*>(w);
+    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + fd_counters_offset(B, n_kv, workspace_bytes));
     p.pf_ptr = pf_ptr;
     p.pf_bytes = pf_bytes;
     p.wait_first = shared_pages ? 1 : 0;
@@ -496,8 +501,7 @@ extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, con
     int rc = fd_static_scratch(&ws);
     if (rc) return rc;
     // The array keeps whatever the previous call left; the split counters must start at zero.
-    const size_t counters_off = vsl::align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float)) +
-                                vsl::align256((size_t)B * n_heads * n_splits * 2 * sizeof(float));
+    const size_t counters_off = vsl::fd_counters_offset(B, n_kv, FD_STATIC_SCRATCH_BYTES);
     cudaError_t e = cudaMemsetAsync(static_cast<unsigned char*>(ws) + counters_off, 0, (size_t)B * n_kv * sizeof(int),
                                     (cudaStream_t)stream);
     if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");

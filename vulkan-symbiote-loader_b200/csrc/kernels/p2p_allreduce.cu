@@ -24,15 +24,6 @@ namespace vsl {
 
 constexpr int AR_THREADS = 1024;
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 template <int OP>  // 0: fp32 sum, 1: u64 max
 __global__ void __launch_bounds__(AR_THREADS, 1) p2p_allreduce_kernel(void* data, int n, const P2pPeers peers) {
     __shared__ unsigned long long s_epoch;

@@ -20,6 +20,16 @@ struct P2pPeers {
     int* status;                 // VSL_ERR_TIMEOUT when a peer's message never arrives
 };
 
+// A projection's role in a fused tensor-parallel sum (reduce on read, see GemvParams): mode 1
+// = row-parallel producer, 2 = consumer whose input is the sum of the ranks' rows (written back
+// to x_out); done = this rank's two arrival counters (zero between calls).
+struct ArFuse {
+    int mode;
+    const P2pPeers* peers;
+    unsigned int* done;
+    float* x_out;
+};
+
 // op 0: in-place fp32 sum of n floats; op 1: in-place max of n u64 keys. One launch on `st`.
 int p2p_allreduce(const P2pPeers& peers, void* data, int n, int op, cudaStream_t st);
 

@@ -43,7 +43,7 @@ class EngineOptions(C.Structure):
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
-                ("use_p2p", C.c_int), ("legacy_q4", C.c_int)]
+                ("use_p2p", C.c_int), ("fuse_allreduce", C.c_int), ("legacy_q4", C.c_int)]
 
 
 _lib = None
