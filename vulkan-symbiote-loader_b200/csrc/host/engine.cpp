@@ -1197,6 +1197,13 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
                    c.n_layers * (chunks(c.d_model) /*qkv*/ + 1 /*attention*/ + chunks(nh_l_ * c.head_dim) /*o*/ +
                                  chunks(c.d_model) /*gate-up*/ + chunks(ff_l_) /*down*/) +
                    chunks(c.d_model) /*lm_head*/ + 1 /*finalize*/;
+        // tensor parallel over peer memory: the argmax exchange, and the residual all-reduce
+        // kernels unless the sums ride on the projections (NCCL's kernels are not counted)
+        if (p2p_ready_) {
+            StepBufs probe{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
+                           tc_ws_ ? &tc_route_ : nullptr, false};
+            *kernels += 1 + (fuse_allreduce(probe, B) ? 0 : 2 * c.n_layers);
+        }
     }
     if (bytes) *bytes = w + kv;
     return VSL_OK;
