@@ -53,9 +53,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="7b", choices=["7b", "7b-q8", "7b-q4", "8b", "70b-stream"],
-                    help="7b: the headline (BASELINE configs[1]); 7b-q8 / 7b-q4: the same model with GGUF "
-                         "Q8_0 / Q4_0 block-quantized weights; 8b: BASELINE configs[3], batch 16 over "
+    ap.add_argument("--workload", default="7b", choices=["7b", "7b-q8", "7b-q4", "7b-q41", "8b", "70b-stream"],
+                    help="7b: the headline (BASELINE configs[1]); 7b-q8 / 7b-q4 / 7b-q41: the same model with GGUF "
+                         "Q8_0 / Q4_0 / Q4_1 block-quantized weights; 8b: BASELINE configs[3], batch 16 over "
                          "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b-stream: "
                          "BASELINE configs[4] on one GPU under a 64 GB HBM cap (layers streamed from host)")
     ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "prefill"],
@@ -206,7 +206,7 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     N, K = 2 * F, d
     copies = 8
     dt = cfg.get("wdtype", vsl.F16)
-    quant = dt in (vsl.Q8_0, vsl.Q4_0)
+    quant = dt in (vsl.Q8_0, vsl.Q4_0, vsl.Q4_1)
     rb = vsl.weight_row_bytes(dt, K)
     W = torch.empty((copies, N, rb), dtype=torch.uint8, device="cuda")
     for c in range(copies):
@@ -235,7 +235,8 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     del W
     torch.cuda.empty_cache()
     if quant:
-        return {"bound": "hbm", "kernel": f"gemv_q_kernel<{'Q8_0' if dt == vsl.Q8_0 else 'Q4_0'},1,EK_SWIGLU,NORM> "
+        qn = {vsl.Q8_0: "Q8_0", vsl.Q4_0: "Q4_0", vsl.Q4_1: "Q4_1"}[dt]
+        return {"bound": "hbm", "kernel": f"gemv_q_kernel<{qn},1,EK_SWIGLU,NORM> "
                                           "(gate/up + SwiGLU, fused RMSNorm)",
                 "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch,
@@ -262,9 +263,9 @@ def run_ours(args):
         return run_stream70(args)
     big = args.workload == "8b"
     cfg = dict(CONFIG_8B if big else CONFIG_7B)
-    qname = {"7b-q8": "Q8_0", "7b-q4": "Q4_0"}.get(args.workload)
+    qname = {"7b-q8": "Q8_0", "7b-q4": "Q4_0", "7b-q41": "Q4_1"}.get(args.workload)
     if qname:
-        cfg["wdtype"] = vsl.Q8_0 if qname == "Q8_0" else vsl.Q4_0
+        cfg["wdtype"] = {"Q8_0": vsl.Q8_0, "Q4_0": vsl.Q4_0, "Q4_1": vsl.Q4_1}[qname]
     if args.layers:
         cfg["n_layers"] = args.layers
     B = BATCH_8B if big else 1

@@ -58,6 +58,7 @@ extern "C" {
 #define VSL_F16 1
 #define VSL_BF16 30
 #define VSL_Q4_0 2  /* weights only, device layout: see vsl_weight_row_bytes / vsl_repack_gguf_rows */
+#define VSL_Q4_1 3  /* weights only, same device layout plus a per-block fp16 minimum */
 #define VSL_Q8_0 8
 
 /* ---- projection epilogues ---- */
@@ -198,7 +199,7 @@ typedef struct {
     int vocab;
     float rope_theta;
     float rms_eps;
-    int wdtype; /* VSL_F32 / VSL_F16 / VSL_BF16 / VSL_Q8_0 / VSL_Q4_0 (every projection,
+    int wdtype; /* VSL_F32 / VSL_F16 / VSL_BF16 / VSL_Q8_0 / VSL_Q4_0 / VSL_Q4_1 (every projection,
                    the embedding table and lm_head share it)                    */
 } vsl_model_config;
 
@@ -223,17 +224,18 @@ typedef struct {
     int fuse_allreduce; /* tensor parallel with use_p2p: 1 (default) = the residual sums ride on the
                           projections (row-parallel GEMV pushes its rows to every rank, the next
                           projection sums them while staging); 0 = separate all-reduce kernel */
-    int legacy_q4;     /* 1 = read GGUF Q4_0 nibbles in the reference loader's order
+    int legacy_q4;     /* 1 = read GGUF Q4_0 / Q4_1 nibbles in the reference loader's order
                           (GGUFLoader.cpp:1146-1160: element 2i low, 2i+1 high nibble of
                           byte i); 0 (default) = ggml's order (element i low, i+16 high)  */
 } vsl_engine_options;
 
 VSL_API void vsl_engine_default_options(vsl_engine_options* opt);
 
-/* Block-quantized weights (VSL_Q8_0 / VSL_Q4_0) on the device: each row of K elements (K a
- * multiple of 32) is [quants: K bytes (Q8_0) or K/2 bytes (Q4_0)][K/32 fp16 scales, padded to
- * 16 bytes]; Q4_0 byte i of a block holds element i (low nibble) and i+16 (high nibble), value
- * (nibble - 8) * d; Q8_0 value int8 * d. vsl_weight_row_bytes gives the row pitch (any dtype);
+/* Block-quantized weights (VSL_Q8_0 / VSL_Q4_0 / VSL_Q4_1) on the device: each row of K elements
+ * (K a multiple of 32) is [quants: K bytes (Q8_0) or K/2 bytes (Q4_x)][K/32 fp16 scales, padded
+ * to 16 bytes] and, for Q4_1 only, [K/32 fp16 minimums, padded to 16 bytes]; Q4_x byte i of a
+ * block holds element i (low nibble) and i+16 (high nibble), value (nibble - 8) * d (Q4_0) or
+ * nibble * d + m (Q4_1); Q8_0 value int8 * d. vsl_weight_row_bytes gives the row pitch (any dtype);
  * vsl_repack_gguf_rows converts rows [row0, row0+nrows) x columns [col0, col0+ncols) of a GGUF
  * tensor's block data (host) into that layout (host, row pitch out_ld bytes). The projection
  * kernels (vsl_gemv, vsl_qkv_rope_append, vsl_lm_head_sample) accept these dtypes. */

@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
 
 F32, F16, BF16 = 0, 1, 30
-Q4_0, Q8_0 = 2, 8
+Q4_0, Q4_1, Q8_0 = 2, 3, 8
 
 
 class OrcConfig(C.Structure):
@@ -81,7 +81,7 @@ def _p(a: np.ndarray):
 
 
 def dequant_blocks(dtype, blocks: np.ndarray, n_elems: int, legacy_q4: int = 0) -> np.ndarray:
-    """GGUF Q8_0 / Q4_0 block bytes -> fp32 values (the reference loader's dequantisation)."""
+    """GGUF Q8_0 / Q4_0 / Q4_1 block bytes -> fp32 values (the reference loader's dequantisation)."""
     out = np.empty(n_elems, np.float32)
     b = np.ascontiguousarray(blocks, np.uint8)
     lib().orc_dequant_blocks(dtype, _p(b), n_elems, legacy_q4, _p(out))

@@ -52,8 +52,8 @@
 #endif
 
 /* ggml tensor type ids (standard GGUF), used for weights and the KV cache */
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_BF16 = 30 };
-static inline int orc_is_quant(int dt) { return dt == ORC_Q4_0 || dt == ORC_Q8_0; }
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q4_1 = 3, ORC_Q8_0 = 8, ORC_BF16 = 30 };
+static inline int orc_is_quant(int dt) { return dt == ORC_Q4_0 || dt == ORC_Q4_1 || dt == ORC_Q8_0; }
 
 /* ------------------------------------------------------------------------- */
 /* number formats                                                            */
@@ -170,22 +170,32 @@ void orc_synth_fill(uint64_t seed, uint64_t tensor_id, uint64_t start, uint64_t 
 }
 
 /* ------------------------------------------------------------------------- */
-/* block-quantized weights (GGUF Q8_0 / Q4_0, 32 elements per block)         */
+/* block-quantized weights (GGUF Q8_0 / Q4_0 / Q4_1, 32 elements per block)  */
 /* ------------------------------------------------------------------------- */
 
 /* GGUFLoader.cpp dequantize_tensor: per block, d = fp16_to_fp32(first two bytes) (:1131-1147,
  * exact IEEE half), then value = q * d in fp32: Q8_0 q = int8 qs[i] (:1185-1200); Q4_0
- * q = nibble - 8 (:1150-1162). The reference reads the nibbles of byte i as elements 2i (low)
- * and 2i + 1 (high) (:1154-1159); ggml's format defines them as elements i and i + 16. Both
- * orders are restated: legacy_q4 = 1 follows the reference loader, 0 the format. */
+ * q = nibble - 8 (:1150-1162); Q4_1 (:1173-1196) blocks carry a second fp16, the minimum m,
+ * after d, and value = (float)nibble * d + m (an fp32 multiply, then an fp32 add). The reference
+ * reads the nibbles of byte i as elements 2i (low) and 2i + 1 (high) (:1154-1159, :1187-1191);
+ * ggml's format defines them as elements i and i + 16. Both orders are restated: legacy_q4 = 1
+ * follows the reference loader, 0 the format. */
 void orc_dequant_blocks(int dtype, const void* blocks, size_t n_elems, int legacy_q4, float* out) {
     const uint8_t* p = (const uint8_t*)blocks;
-    const size_t bb = dtype == ORC_Q8_0 ? 34 : 18;
+    const size_t bb = dtype == ORC_Q8_0 ? 34 : dtype == ORC_Q4_1 ? 20 : 18;
     for (size_t b = 0; b * 32 < n_elems; b++, p += bb) {
         const float d = orc_h2f((uint16_t)(p[0] | (p[1] << 8)));
         float* o = out + b * 32;
         if (dtype == ORC_Q8_0) {
             for (int i = 0; i < 32; i++) o[i] = (float)(int8_t)p[2 + i] * d;
+        } else if (dtype == ORC_Q4_1) {
+            const float m = orc_h2f((uint16_t)(p[2] | (p[3] << 8)));
+            for (int i = 0; i < 16; i++) {
+                const int lo = p[4 + i] & 0x0F, hi = (p[4 + i] >> 4) & 0x0F;
+                const float vlo = (float)lo * d, vhi = (float)hi * d;
+                if (legacy_q4) { o[2 * i] = vlo + m; o[2 * i + 1] = vhi + m; }
+                else { o[i] = vlo + m; o[i + 16] = vhi + m; }
+            }
         } else {
             for (int i = 0; i < 16; i++) {
                 const int lo = (p[2 + i] & 0x0F) - 8, hi = ((p[2 + i] >> 4) & 0x0F) - 8;
@@ -198,14 +208,15 @@ void orc_dequant_blocks(int dtype, const void* blocks, size_t n_elems, int legac
 
 /* Seeded block-quantized tensor [rows][cols], dequantized (the device initialiser writes the
  * same quants and scales in its packed layout): element gi = r * cols + c has quant
- * h(gi) % 255 - 127 (Q8_0) or (1 + h(gi) % 15) - 8 (Q4_0); block gb = r * (cols / 32) + c / 32 has
- * scale fp16(m * k), m = 49152 + (h'(gb) & 0x7fff), h' the tensor's second stream and
- * k = sigma / std(quant) / 65536 in fp32. */
+ * h(gi) % 255 - 127 (Q8_0), (1 + h(gi) % 15) - 8 (Q4_0) or h(gi) % 16 (Q4_1); block
+ * gb = r * (cols / 32) + c / 32 has scale d = fp16(m * k), m = 49152 + (h'(gb) & 0x7fff), h' the
+ * tensor's second stream and k = sigma / std(quant) / 65536 in fp32; a Q4_1 block's minimum is
+ * fp16(-7.5 * d) (so its values are centred), value = quant * d + minimum. */
 void orc_synthq_dequant(uint64_t seed, uint64_t tensor_id, size_t rows, size_t cols, double sigma, int dtype,
                         float* out) {
     const uint64_t base = smix(seed ^ (tensor_id * 0xD1B54A32D192ED03ull));
     const uint64_t sbase = smix(seed ^ ((tensor_id ^ 0x5CA1E5ull) * 0xD1B54A32D192ED03ull));
-    const double sq = dtype == ORC_Q8_0 ? 73.6115932 : 4.3204938;
+    const double sq = dtype == ORC_Q8_0 ? 73.6115932 : dtype == ORC_Q4_1 ? 4.6097722 : 4.3204938;
     const float k = (float)(sigma / sq / 65536.0);
     const size_t nb = cols / 32;
 #pragma omp parallel for schedule(static)
@@ -214,9 +225,15 @@ void orc_synthq_dequant(uint64_t seed, uint64_t tensor_id, size_t rows, size_t c
             const uint64_t hs = smix(sbase + (uint64_t)r * nb + b);
             const float m = (float)(49152u + (unsigned)(hs & 0x7fffull));
             const float d = orc_h2f(orc_f2h(m * k));
+            const float mn = orc_h2f(orc_f2h(-7.5f * d));
             for (int i = 0; i < 32; i++) {
                 const size_t gi = (size_t)r * cols + b * 32 + (size_t)i;
                 const uint64_t h = smix(base + gi);
+                if (dtype == ORC_Q4_1) {
+                    const float v = (float)(int)(h % 16ull) * d;
+                    out[gi] = v + mn;
+                    continue;
+                }
                 const int q = dtype == ORC_Q8_0 ? (int)(h % 255ull) - 127 : (int)(1ull + h % 15ull) - 8;
                 out[gi] = (float)q * d;
             }

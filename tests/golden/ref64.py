@@ -91,7 +91,7 @@ class Ref64:
 
 
 def load_tensors_f64(path: str) -> dict[str, np.ndarray]:
-    """Read every F32/F16/BF16/Q8_0/Q4_0 tensor of a GGUF as float64 (rows = ne[1], cols = ne[0])."""
+    """Read every F32/F16/BF16/Q8_0/Q4_0/Q4_1 tensor of a GGUF as float64 (rows = ne[1], cols = ne[0])."""
     import os
     import sys
     sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "..", "vulkan-symbiote-loader_b200"))
@@ -107,7 +107,7 @@ def load_tensors_f64(path: str) -> dict[str, np.ndarray]:
             a = np.frombuffer(mm, dtype=np.float16, count=n, offset=off).astype(np.float64)
         elif gt == synth.GGML_BF16:
             a = synth.bf16_bits_to_f32(np.frombuffer(mm, dtype=np.uint16, count=n, offset=off)).astype(np.float64)
-        elif gt in synth.Q_STD:  # Q8_0 / Q4_0 blocks, dequantized as the reference loader does
+        elif gt in synth.Q_STD:  # Q8_0 / Q4_0 / Q4_1 blocks, dequantized as the reference loader does
             nbytes = n // 32 * synth.Q_BLOCK_BYTES[gt]
             a = synth.dequant_q_blocks(np.frombuffer(mm, dtype=np.uint8, count=nbytes, offset=off), gt,
                                        int(ne[0])).astype(np.float64).reshape(-1)

@@ -1,4 +1,4 @@
-"""Block-quantized weights (Q8_0 / Q4_0) on the B200: the quantized GEMV against a torch fp32
+"""Block-quantized weights (Q8_0 / Q4_0 / Q4_1) on the B200: the quantized GEMV against a torch fp32
 reference of the same dequantized weights (every epilogue and row count), and the engine
 against the goldens (GGUF fixtures, greedy ids) and the oracle (seeded 7B/8B-shaped models,
 teacher-forced logits within 2e-2, top-1 agreement >= 99%)."""
@@ -22,7 +22,7 @@ def _qweights(dtype, N, K, seed=1, tid=300):
     return torch.from_numpy(packed).cuda(), torch.from_numpy(deq).cuda()
 
 
-@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0])
+@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0, vsl.Q4_1])
 @pytest.mark.parametrize("N,K", [(4096, 4096), (333, 1376), (1024, 11008)])
 @pytest.mark.parametrize("B", [1, 2, 4, 6])
 def test_gemv_quantized_store(dtype, N, K, B):
@@ -36,7 +36,19 @@ def test_gemv_quantized_store(dtype, N, K, B):
     assert err <= 1e-4 * max(1.0, ref.abs().max().item()), err
 
 
-@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0])
+@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0, vsl.Q4_1])
+def test_device_synthesis_equals_repacked_numpy_blocks(dtype):
+    """The engine's seeded quantized weights (generated on the device) are, byte for byte, the
+    NumPy GGUF blocks of the same seed repacked into the device row layout."""
+    rows, cols, seed, tid = 37, 1376, 9, synth.tid_layer(0, synth.K_DOWN)
+    want = vsl.repack_gguf_rows(dtype, synth.synth_q_blocks(seed, tid, rows, cols, dtype), rows, cols)
+    dev = torch.zeros(want.size, dtype=torch.uint8, device="cuda")
+    vsl.synth_fill_q(dev, dtype, seed, tid, rows, cols)
+    torch.cuda.synchronize()
+    assert np.array_equal(dev.cpu().numpy().reshape(want.shape), want)
+
+
+@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0, vsl.Q4_1])
 def test_gemv_quantized_epilogues(dtype):
     N, K, B = 2 * 704, 512, 3  # interleaved gate/up rows for SwiGLU
     W, Wd = _qweights(dtype, N, K, tid=301)
@@ -58,7 +70,7 @@ def test_gemv_quantized_epilogues(dtype):
     assert (a - torch.nn.functional.silu(g) * u).abs().max().item() < 1e-4
 
 
-@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4"])
+@pytest.mark.parametrize("name", ["tiny_q8", "tiny_q4", "tiny_q41"])
 def test_quantized_gguf_greedy_matches_golden(golden, fixture_gguf, name):
     g = golden(name)
     with vsl.Engine.from_gguf(fixture_gguf(name), max_seq=128) as e:
@@ -78,10 +90,11 @@ def test_quantized_gguf_greedy_matches_golden(golden, fixture_gguf, name):
         assert e.device_status() == 0
 
 
-def test_legacy_q4_nibble_order_matches_oracle(fixture_gguf, golden):
+@pytest.mark.parametrize("name", ["tiny_q4", "tiny_q41"])
+def test_legacy_q4_nibble_order_matches_oracle(fixture_gguf, golden, name):
     """legacy_q4 = 1 reads the file the way the reference's loader does (different weights)."""
-    g = golden("tiny_q4")
-    path = fixture_gguf("tiny_q4")
+    g = golden(name)
+    path = fixture_gguf(name)
     orc = O.Model.from_gguf(path, kvdtype=O.F16, max_seq=128, legacy_q4=1)
     want, _ = orc.greedy(g["prompt"], 16)
     with vsl.Engine.from_gguf(path, max_seq=128, legacy_q4=1) as e:
@@ -108,7 +121,7 @@ def _teacher_forced(cfg, seed, n_steps, batch=1):
     return worst, float(np.mean(agree))
 
 
-@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0])
+@pytest.mark.parametrize("dtype", [vsl.Q8_0, vsl.Q4_0, vsl.Q4_1])
 def test_7b_shape_quantized_reduced_depth(dtype):
     cfg = dict(n_layers=2, d_model=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
                rope_theta=10000.0, rms_eps=1e-5, wdtype=dtype)

@@ -531,6 +531,7 @@ int make_model_config_from_gguf(const vk_symbiote::GGUFLoader& loader, vsl_model
         case vk_symbiote::GGMLType::BF16: dt = VSL_BF16; break;
         case vk_symbiote::GGMLType::Q8_0: dt = VSL_Q8_0; break;
         case vk_symbiote::GGMLType::Q4_0: dt = VSL_Q4_0; break;
+        case vk_symbiote::GGMLType::Q4_1: dt = VSL_Q4_1; break;
         default: return set_error(VSL_ERR_UNSUPPORTED, "gguf: token_embd dtype %u", (unsigned)emb->data_type);
     }
     vsl_model_config c = {};

@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams 
 }
 
 // ---------------------------------------------------------------------------------------
-// Block-quantized weights (Q8_0 / Q4_0 in the repacked row layout of quant_layout.h)
+// Block-quantized weights (Q8_0 / Q4_0 / Q4_1 in the repacked row layout of quant_layout.h)
 // ---------------------------------------------------------------------------------------
 // One 16-byte vector of quants is 16 (Q8_0, half a block) or 32 (Q4_0, one block) weights.
 // Quants become floats without conversion instructions: a 32-bit pattern u < 2^23 read as an
@@ -326,6 +326,14 @@ template <> struct QTraits<VSL_Q4_0> {
             }
         }
     }
+};
+
+// Q4_1: the same nibbles, unsigned; value = nibble * d + m, so a vector contributes
+// d * sum(u * x) + m * sum(x), and the staged per-vector sums are the plain sums (ZP = 1).
+template <> struct QTraits<VSL_Q4_1> {
+    static constexpr int VEC = 32;
+    static constexpr float ZP = 1.0f;
+    __device__ __forceinline__ static void unpack(const uint4& v, uint32_t* u) { QTraits<VSL_Q4_0>::unpack(v, u); }
 };
 
 __device__ __forceinline__ unsigned long long pack2(uint32_t lo, uint32_t hi) {
@@ -377,6 +385,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
     constexpr int NW = GEMV_THREADS / 32;
     const int nvec = K / VEC;
     const size_t RB = weight_row_bytes(QT, K), QB = quant_bytes(QT, K);
+    const int MO = (int)(scale_bytes(K) / 2);  // Q4_1: minimums follow the scales (fp16 elements)
     const int n_units = (N + 1) >> 1;
     const int u_begin = (int)(((long long)n_units * blockIdx.x) / gridDim.x);
     const int u_end = (int)(((long long)n_units * (blockIdx.x + 1)) / gridDim.x);
@@ -450,7 +459,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
     int step = 0;
     if (EK == EK_LMHEAD && p.inv_temp > 0.0f) step = *p.step_counter;
 
-    constexpr int U = (QT == VSL_Q4_0 && NB >= 4) ? 2 : 4;  // vectors in flight per row and lane
+    constexpr int U = (QT != VSL_Q8_0 && NB >= 4) ? 2 : 4;  // vectors in flight per row and lane
+    constexpr bool MIN = QT == VSL_Q4_1;
     for (; unit < u_end; unit += NW) {
         const int r0 = 2 * unit;
         const bool has1 = r0 + 1 < N;
@@ -466,7 +476,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
         float acc0[NB], acc1[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) { acc0[b] = 0.0f; acc1[b] = 0.0f; }
-        auto consume = [&](const uint4& a, const uint4& c, float d0, float d1, int v) {
+        auto consume = [&](const uint4& a, const uint4& c, float d0, float d1, float m0, float m1, int v) {
             uint32_t ua[VEC], uc[VEC];
             QTraits<QT>::unpack(a, ua);
             QTraits<QT>::unpack(c, uc);
@@ -484,14 +494,19 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
                     ffma2(t1, pack2(uc[4 * i + 2], uc[4 * i + 3]), x23);
                 }
                 const float zx = xs[b * SP + XP + v];
-                acc0[b] = fmaf(d0, fmaf(Q_UNSCALE, sum2(t0), -zx), acc0[b]);
-                acc1[b] = fmaf(d1, fmaf(Q_UNSCALE, sum2(t1), -zx), acc1[b]);
+                if (MIN) {  // d * sum(u x) + m * sum(x)
+                    acc0[b] = fmaf(d0, Q_UNSCALE * sum2(t0), fmaf(m0, zx, acc0[b]));
+                    acc1[b] = fmaf(d1, Q_UNSCALE * sum2(t1), fmaf(m1, zx, acc1[b]));
+                } else {    // d * (sum(u x) - z sum(x))
+                    acc0[b] = fmaf(d0, fmaf(Q_UNSCALE, sum2(t0), -zx), acc0[b]);
+                    acc1[b] = fmaf(d1, fmaf(Q_UNSCALE, sum2(t1), -zx), acc1[b]);
+                }
             }
         };
         int v = lane;
         for (; v + 32 * (U - 1) < nvec; v += 32 * U) {
             uint4 a[U], c[U];
-            unsigned short s0[U], s1[U];
+            unsigned short s0[U], s1[U], n0[U], n1[U];
 #pragma unroll
             for (int u = 0; u < U; u++) {
                 const int vv = v + 32 * u;
@@ -499,18 +514,25 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
                 c[u] = ldg_stream(row1 + (size_t)vv * 16);
                 s0[u] = __ldcs(sc0 + (vv * VEC) / QBLK);
                 s1[u] = __ldcs(sc1 + (vv * VEC) / QBLK);
+                if (MIN) {
+                    n0[u] = __ldcs(sc0 + MO + (vv * VEC) / QBLK);
+                    n1[u] = __ldcs(sc1 + MO + (vv * VEC) / QBLK);
+                }
             }
 #pragma unroll
             for (int u = 0; u < U; u++)
                 consume(a[u], c[u], __half2float(__ushort_as_half(s0[u])), __half2float(__ushort_as_half(s1[u])),
-                        v + 32 * u);
+                        MIN ? __half2float(__ushort_as_half(n0[u])) : 0.0f,
+                        MIN ? __half2float(__ushort_as_half(n1[u])) : 0.0f, v + 32 * u);
         }
         for (; v < nvec; v += 32) {
             const uint4 a = ldg_stream(row0 + (size_t)v * 16);
             const uint4 c = ldg_stream(row1 + (size_t)v * 16);
             const float d0 = __half2float(__ushort_as_half(__ldcs(sc0 + (v * VEC) / QBLK)));
             const float d1 = __half2float(__ushort_as_half(__ldcs(sc1 + (v * VEC) / QBLK)));
-            consume(a, c, d0, d1, v);
+            const float m0 = MIN ? __half2float(__ushort_as_half(__ldcs(sc0 + MO + (v * VEC) / QBLK))) : 0.0f;
+            const float m1 = MIN ? __half2float(__ushort_as_half(__ldcs(sc1 + MO + (v * VEC) / QBLK))) : 0.0f;
+            consume(a, c, d0, d1, m0, m1, v);
         }
 #pragma unroll
         for (int b = 0; b < NB; b++) {
@@ -539,8 +561,10 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParam
 // counts are 1, 2 and 4
 static int max_rows_per_launch(int wdtype, int K) {
     const size_t room = 200 * 1024;
-    const size_t pitch = wdtype == VSL_Q8_0 ? (size_t)q_stage_floats<VSL_Q8_0>(K)
-                         : wdtype == VSL_Q4_0 ? (size_t)q_stage_floats<VSL_Q4_0>(K) : (size_t)K;
+    const size_t pitch = wdtype == VSL_Q8_0   ? (size_t)q_stage_floats<VSL_Q8_0>(K)
+                         : wdtype == VSL_Q4_0 ? (size_t)q_stage_floats<VSL_Q4_0>(K)
+                         : wdtype == VSL_Q4_1 ? (size_t)q_stage_floats<VSL_Q4_1>(K)
+                                              : (size_t)K;
     const int c = (int)(room / (pitch * sizeof(float)));
     return c >= 4 ? 4 : c >= 2 ? 2 : c;
 }
@@ -627,6 +651,7 @@ static int launch_gemv_w(int wdtype, const GemvParams& p, cudaStream_t st) {
         case VSL_BF16: return launch_gemv_nb<__nv_bfloat16, EK, NORM>(p, st);
         case VSL_Q8_0: return launch_gemv_q_nb<VSL_Q8_0, EK, NORM>(p, st);
         case VSL_Q4_0: return launch_gemv_q_nb<VSL_Q4_0, EK, NORM>(p, st);
+        case VSL_Q4_1: return launch_gemv_q_nb<VSL_Q4_1, EK, NORM>(p, st);
         default: return set_error(VSL_ERR_UNSUPPORTED, "gemv: weight dtype %d", wdtype);
     }
 }

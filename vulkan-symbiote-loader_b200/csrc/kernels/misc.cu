@@ -48,7 +48,8 @@ __global__ void embed_kernel(const WT* __restrict__ table, int V, int d, const i
 }
 
 // Block-quantized table (device row layout of quant_layout.h): element j of the row is
-// quant(j) * d(j / 32) in fp32, the reference's dequantisation (GGUFLoader.cpp:1141-1181).
+// quant(j) * d(j / 32) in fp32 (Q4_1: then + m(j / 32) in fp32), the reference's
+// dequantisation (GGUFLoader.cpp:1150-1207).
 template <int QT>
 __global__ void embed_q_kernel(const unsigned char* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
                                float* __restrict__ x, unsigned long long* slots) {
@@ -60,6 +61,7 @@ __global__ void embed_q_kernel(const unsigned char* __restrict__ table, int V, i
     if (id > V - 1) id = V - 1;
     const unsigned char* row = table + (size_t)id * weight_row_bytes(QT, d);
     const __half* sc = reinterpret_cast<const __half*>(row + quant_bytes(QT, d));
+    const __half* mn = sc + scale_bytes(d) / 2;  // Q4_1 minimums follow the scales
     for (int j = threadIdx.x; j < d; j += blockDim.x) {
         const float s = __half2float(sc[j / QBLK]);
         int q;
@@ -68,9 +70,10 @@ __global__ void embed_q_kernel(const unsigned char* __restrict__ table, int V, i
         } else {
             const int blk = j / QBLK, i = j % QBLK;
             const unsigned char byte = row[blk * 16 + (i & 15)];
-            q = (int)(i < 16 ? (byte & 15) : (byte >> 4)) - 8;
+            q = (int)(i < 16 ? (byte & 15) : (byte >> 4)) - (QT == VSL_Q4_1 ? 0 : 8);
         }
-        x[(size_t)b * d + j] = (float)q * s;
+        x[(size_t)b * d + j] = QT == VSL_Q4_1 ? __fadd_rn(__fmul_rn((float)q, s), __half2float(mn[j / QBLK]))
+                                              : (float)q * s;
     }
     if (slots && threadIdx.x == 0) slots[b] = 0ull;
 }
@@ -87,6 +90,10 @@ int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, i
                                  "embed");
         case VSL_Q4_0:
             return launch_status(launch_k(embed_q_kernel<VSL_Q4_0>, grid, block, 0, st, (const unsigned char*)table, V,
+                                          d, ids, x, slots),
+                                 "embed");
+        case VSL_Q4_1:
+            return launch_status(launch_k(embed_q_kernel<VSL_Q4_1>, grid, block, 0, st, (const unsigned char*)table, V,
                                           d, ids, x, slots),
                                  "embed");
         case VSL_F32:
@@ -224,8 +231,9 @@ __global__ void synth2d_kernel(T* __restrict__ dst, size_t dst_ld, unsigned long
 
 // Seeded block-quantized tensor, written in the device row layout (row pitch dst_ld bytes):
 // global element gi = row * src_cols + col has quant h(gi) (Q8_0: h % 255 - 127; Q4_0: nibble
-// 1 + h % 15, value nibble - 8, symmetric like Q8_0) and global block gb = row * (src_cols / 32) + col / 32 the scale
-// fp16(m * c), m = 49152 + (h'(gb) & 0x7fff), h' from a second stream of the same tensor.
+// 1 + h % 15, value nibble - 8, symmetric like Q8_0; Q4_1: nibble h % 16) and global block
+// gb = row * (src_cols / 32) + col / 32 the scale d = fp16(m * c), m = 49152 + (h'(gb) & 0x7fff),
+// h' from a second stream of the same tensor; a Q4_1 block's minimum is fp16(-7.5 * d).
 template <int QT>
 __global__ void synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, unsigned long long base,
                               unsigned long long sbase, size_t row0, size_t nrows, size_t src_cols, size_t col0,
@@ -244,7 +252,8 @@ __global__ void synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, un
             const size_t blk = cb / 16, i = cb % 16;  // byte i holds elements i and i + 16 of the block
             const unsigned long long h0 = smix(base + grow + blk * QBLK + i);
             const unsigned long long h1 = smix(base + grow + blk * QBLK + i + 16);
-            out = (unsigned char)((1ull + h0 % 15ull) | ((1ull + h1 % 15ull) << 4));
+            out = QT == VSL_Q4_1 ? (unsigned char)((h0 % 16ull) | ((h1 % 16ull) << 4))
+                                 : (unsigned char)((1ull + h0 % 15ull) | ((1ull + h1 % 15ull) << 4));
         }
         dst[r * dst_ld + cb] = out;
     }
@@ -258,6 +267,9 @@ __global__ void synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, un
             v = __float2half_rn(__fmul_rn((float)(49152u + (unsigned)(h & 0x7fffull)), c));
         }
         reinterpret_cast<__half*>(dst + r * dst_ld + qb)[k] = v;
+        if (QT == VSL_Q4_1)  // minimum: fp16(-7.5 * d), +0 in the padding
+            reinterpret_cast<__half*>(dst + r * dst_ld + qb + 2 * sb)[k] =
+                k < nblk ? __float2half_rn(__fmul_rn(-7.5f, __half2float(v))) : __float2half_rn(0.0f);
     }
 }
 
@@ -267,7 +279,8 @@ static unsigned long long synthq_scale_base(uint64_t seed, uint64_t tid) {
 }
 // fp32 factor of the block scales: d = m * c has mean ~ sigma / std(quant)
 static float synthq_scale_c(int dtype, double sigma) {
-    const double sq = dtype == VSL_Q8_0 ? 73.6115932 : 4.3204938;  // std of U{-127..127}, U{-7..7}
+    // std of U{-127..127}, U{-7..7}, U{0..15}
+    const double sq = dtype == VSL_Q8_0 ? 73.6115932 : dtype == VSL_Q4_1 ? 4.6097722 : 4.3204938;
     return (float)(sigma / sq / 65536.0);
 }
 
@@ -283,6 +296,9 @@ int synthq2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t t
     dim3 grid((unsigned)(sm_count() * 16)), block(256);
     cudaError_t e = dtype == VSL_Q8_0
                         ? launch_k(synthq_kernel<VSL_Q8_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                                   row0, nrows, src_cols, col0, ncols, c)
+                    : dtype == VSL_Q4_1
+                        ? launch_k(synthq_kernel<VSL_Q4_1>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
                                    row0, nrows, src_cols, col0, ncols, c)
                         : launch_k(synthq_kernel<VSL_Q4_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
                                    row0, nrows, src_cols, col0, ncols, c);

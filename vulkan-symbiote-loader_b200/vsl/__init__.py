@@ -17,7 +17,7 @@ LIB_PATH = os.path.join(PKG, "lib", "libvsl.so")
 HEADER = os.path.join(os.path.dirname(PKG), "include", "vsl.h")
 
 F32, F16, BF16 = 0, 1, 30
-Q4_0, Q8_0 = 2, 8  # weights only (block-quantized device layout)
+Q4_0, Q4_1, Q8_0 = 2, 3, 8  # weights only (block-quantized device layout)
 EPI_STORE, EPI_ADD, EPI_SWIGLU = 0, 1, 2
 ERR = {0: "OK", -1: "INVALID", -2: "CUDA", -3: "NCCL", -4: "TIMEOUT", -5: "BOUNDS", -6: "IO", -7: "FORMAT",
        -8: "OOM", -9: "UNSUPPORTED", -10: "STATE"}
@@ -211,14 +211,14 @@ def weight_row_bytes(dtype: int, K: int) -> int:
 
 
 def synth_fill_q(dst, dtype: int, seed: int, tid: int, rows: int, cols: int, sigma: float = 0.02, stream=0):
-    """Seeded Q8_0 / Q4_0 tensor [rows][cols] into device memory in the device row layout."""
+    """Seeded Q8_0 / Q4_0 / Q4_1 tensor [rows][cols] into device memory in the device row layout."""
     check(lib().vsl_synth_fill_q(_ptr(dst), dtype, weight_row_bytes(dtype, cols), seed, tid, rows, cols, sigma,
                                  stream))
 
 
 def repack_gguf_rows(dtype: int, blocks, rows: int, cols: int, legacy_q4: bool = False, row0: int = 0,
                      nrows: int | None = None, col0: int = 0, ncols: int | None = None):
-    """GGUF Q8_0 / Q4_0 block bytes ([rows][cols / 32 blocks], host) -> device row layout (uint8
+    """GGUF Q8_0 / Q4_0 / Q4_1 block bytes ([rows][cols / 32 blocks], host) -> device row layout (uint8
     numpy array [nrows][weight_row_bytes(dtype, ncols)])."""
     import numpy as np
     nrows = rows - row0 if nrows is None else nrows

@@ -16,11 +16,13 @@ Tensor ids: token_embd 1, output 2; per layer l and kind k (attn_norm 0, q 1, k 
 output 4, ffn_norm 5, gate 6, up 7, down 8): 256 + 16 l + k; KV prefill 0x40000000 + 2 l +
 (0 for K, 1 for V); prompt stream s: 0xFFFF0000 + s. Norm weights are 1.0.
 
-Block-quantized tensors (GGUF Q8_0 / Q4_0, blocks of 32 along a row of `cols`) are defined
-in quantized form: element gi = r * cols + c has quant h(gi) % 255 - 127 (Q8_0) or nibble
-1 + h(gi) % 15, value nibble - 8 (Q4_0; both symmetric around zero); block gb = r * (cols / 32) + c / 32 has the fp16 scale
-round(m * k), m = 49152 + (h'(gb) & 0x7fff) with h' the stream of tensor id (tid ^ 0x5CA1E5)
-and k = float32(sigma / std(quant) / 65536); value = quant * scale in fp32.
+Block-quantized tensors (GGUF Q8_0 / Q4_0 / Q4_1, blocks of 32 along a row of `cols`) are
+defined in quantized form: element gi = r * cols + c has quant h(gi) % 255 - 127 (Q8_0), nibble
+1 + h(gi) % 15 with value nibble - 8 (Q4_0; both symmetric around zero) or nibble h(gi) % 16
+(Q4_1); block gb = r * (cols / 32) + c / 32 has the fp16 scale d = round(m * k),
+m = 49152 + (h'(gb) & 0x7fff) with h' the stream of tensor id (tid ^ 0x5CA1E5) and
+k = float32(sigma / std(quant) / 65536); value = quant * d in fp32, and for Q4_1 the block's fp16
+minimum is round(-7.5 * d) and value = nibble * d + minimum (fp32 multiply, then fp32 add).
 """
 from __future__ import annotations
 
@@ -37,9 +39,10 @@ TID_TOK_EMBD, TID_OUTPUT, TID_OUTPUT_NORM = 1, 2, 3
 K_ATTN_NORM, K_Q, K_K, K_V, K_O, K_FFN_NORM, K_GATE, K_UP, K_DOWN = range(9)
 
 GGML_F32, GGML_F16, GGML_BF16 = 0, 1, 30
-GGML_Q4_0, GGML_Q8_0 = 2, 8
-Q_STD = {GGML_Q8_0: 73.6115932, GGML_Q4_0: 4.3204938}  # std of U{-127..127}, U{-7..7}
-Q_BLOCK_BYTES = {GGML_Q8_0: 34, GGML_Q4_0: 18}
+GGML_Q4_0, GGML_Q4_1, GGML_Q8_0 = 2, 3, 8
+# std of U{-127..127}, U{-7..7}, U{0..15}
+Q_STD = {GGML_Q8_0: 73.6115932, GGML_Q4_0: 4.3204938, GGML_Q4_1: 4.6097722}
+Q_BLOCK_BYTES = {GGML_Q8_0: 34, GGML_Q4_0: 18, GGML_Q4_1: 20}
 
 
 def tid_layer(layer: int, kind: int) -> int:
@@ -119,9 +122,9 @@ def synth_tensor(seed: int, tid: int, shape: tuple[int, ...], dtype: int, sigma:
 
 
 def synth_q_blocks(seed: int, tid: int, rows: int, cols: int, dtype: int, sigma: float = 0.02) -> np.ndarray:
-    """GGUF block bytes [rows][cols / 32 * block bytes] of a seeded Q8_0 / Q4_0 tensor (ggml
-    layout: fp16 scale, then 32 int8 quants or 16 bytes holding elements i (low nibble) and
-    i + 16 (high nibble))."""
+    """GGUF block bytes [rows][cols / 32 * block bytes] of a seeded Q8_0 / Q4_0 / Q4_1 tensor
+    (ggml layout: fp16 scale, for Q4_1 an fp16 minimum, then 32 int8 quants or 16 bytes holding
+    elements i (low nibble) and i + 16 (high nibble))."""
     assert cols % 32 == 0 and dtype in Q_STD
     nb = cols // 32
     base = np.uint64(tensor_base(seed, tid))
@@ -136,6 +139,11 @@ def synth_q_blocks(seed: int, tid: int, rows: int, cols: int, dtype: int, sigma:
     blk[..., :2] = d16.view(np.uint8).reshape(rows, nb, 2)
     if dtype == GGML_Q8_0:
         blk[..., 2:] = ((h % np.uint64(255)).astype(np.int16) - 127).astype(np.int8).view(np.uint8)
+    elif dtype == GGML_Q4_1:
+        m16 = (d16.astype(np.float32) * np.float32(-7.5)).astype(np.float16)
+        blk[..., 2:4] = m16.view(np.uint8).reshape(rows, nb, 2)
+        n = (h % np.uint64(16)).astype(np.uint8)
+        blk[..., 4:] = n[..., :16] | (n[..., 16:] << np.uint8(4))
     else:
         n = (np.uint64(1) + h % np.uint64(15)).astype(np.uint8)
         blk[..., 2:] = n[..., :16] | (n[..., 16:] << np.uint8(4))
@@ -143,20 +151,26 @@ def synth_q_blocks(seed: int, tid: int, rows: int, cols: int, dtype: int, sigma:
 
 
 def dequant_q_blocks(blocks: np.ndarray, dtype: int, cols: int, legacy_q4: bool = False) -> np.ndarray:
-    """fp32 values [rows][cols] of GGUF Q8_0 / Q4_0 rows: quant * fp16 scale, one fp32 multiply
-    (the reference's dequantize_tensor). legacy_q4 reads Q4_0 byte i as elements 2i (low
-    nibble) and 2i + 1 (high), the reference loader's order; otherwise ggml's i and i + 16."""
+    """fp32 values [rows][cols] of GGUF Q8_0 / Q4_0 / Q4_1 rows: quant * fp16 scale, one fp32
+    multiply (Q4_1: then + fp16 minimum, one fp32 add; the reference's dequantize_tensor).
+    legacy_q4 reads Q4_x byte i as elements 2i (low nibble) and 2i + 1 (high), the reference
+    loader's order; otherwise ggml's i and i + 16."""
     bb = Q_BLOCK_BYTES[dtype]
     b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, cols // 32, bb)
     d = b[..., :2].copy().view(np.float16).astype(np.float32)  # [rows][nb][1]
     if dtype == GGML_Q8_0:
         q = b[..., 2:].view(np.int8).astype(np.float32)
-    else:
-        lo = (b[..., 2:] & 15).astype(np.int16) - 8
-        hi = (b[..., 2:] >> 4).astype(np.int16) - 8
-        q = (np.stack([lo, hi], -1).reshape(lo.shape[:-1] + (32,)) if legacy_q4
-             else np.concatenate([lo, hi], -1)).astype(np.float32)
-    return (q * d).reshape(-1, cols)
+        return (q * d).reshape(-1, cols)
+    hb = 4 if dtype == GGML_Q4_1 else 2
+    zp = 0 if dtype == GGML_Q4_1 else 8
+    lo = (b[..., hb:] & 15).astype(np.int16) - zp
+    hi = (b[..., hb:] >> 4).astype(np.int16) - zp
+    q = (np.stack([lo, hi], -1).reshape(lo.shape[:-1] + (32,)) if legacy_q4
+         else np.concatenate([lo, hi], -1)).astype(np.float32)
+    v = (q * d).astype(np.float32)
+    if dtype == GGML_Q4_1:
+        v = v + b[..., 2:4].copy().view(np.float16).astype(np.float32)
+    return v.reshape(-1, cols)
 
 
 def synth_ids(seed: int, stream: int, n: int, vocab: int) -> np.ndarray:
