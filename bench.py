@@ -53,11 +53,13 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override depth (profiling captures only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
-    ap.add_argument("--workload", default="7b", choices=["7b", "7b-q8", "7b-q4", "7b-q41", "8b", "70b-stream"],
+    ap.add_argument("--workload", default="7b", choices=["7b", "7b-q8", "7b-q4", "7b-q41", "8b", "70b", "70b-stream"],
                     help="7b: the headline (BASELINE configs[1]); 7b-q8 / 7b-q4 / 7b-q41: the same model with GGUF "
                          "Q8_0 / Q4_0 / Q4_1 block-quantized weights; 8b: BASELINE configs[3], batch 16 over "
-                         "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b-stream: "
-                         "BASELINE configs[4] on one GPU under a 64 GB HBM cap (layers streamed from host)")
+                         "8192 prefilled KV positions each (bf16, GQA, tensor-core projections); 70b: BASELINE "
+                         "configs[4] at batch 1 after a 2048-token prompt pass, tensor-parallel over --gpus "
+                         "(run it under torchrun with 8 GPUs for the TP 8 figure); 70b-stream: BASELINE configs[4] "
+                         "on one GPU under a 64 GB HBM cap (layers streamed from host)")
     ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "prefill"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
                          "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 = "
@@ -262,14 +264,15 @@ def run_ours(args):
     if args.workload == "70b-stream":
         return run_stream70(args)
     big = args.workload == "8b"
-    cfg = dict(CONFIG_8B if big else CONFIG_7B)
+    w70 = args.workload == "70b"
+    cfg = dict(CONFIG_8B if big else CONFIG_70B if w70 else CONFIG_7B)
     qname = {"7b-q8": "Q8_0", "7b-q4": "Q4_0", "7b-q41": "Q4_1"}.get(args.workload)
     if qname:
         cfg["wdtype"] = {"Q8_0": vsl.Q8_0, "Q4_0": vsl.Q4_0, "Q4_1": vsl.Q4_1}[qname]
     if args.layers:
         cfg["n_layers"] = args.layers
     B = BATCH_8B if big else 1
-    start = PREFILL_8B if big else PROMPT
+    start = PREFILL_8B if big else PREFILL_70B if w70 else PROMPT
     max_seq = start + args.warmup + 2 * args.steps + 8
     max_seq = (max_seq + 63) // 64 * 64
     nccl_id = vdist.nccl_id(dist)
@@ -283,6 +286,15 @@ def run_ours(args):
         eng.fill_kv_synthetic(SEED + 100, 1.0, PREFILL_8B, B)
         eng.set_forced(synth.synth_ids(SEED, 0, B, cfg["vocab"]).reshape(1, B))
         eng.run(1, batch=B)
+    elif w70:
+        # the 2048-token prompt through the prompt pass once (time to first token, host call to
+        # sampled id, max over ranks)
+        prompt = synth.synth_ids(SEED, 0, PREFILL_70B, cfg["vocab"])
+        if dist:
+            dist.barrier()
+        t_p = time.perf_counter()
+        eng.prefill(prompt)
+        ttft_s = vdist.max_over_ranks(dist, time.perf_counter() - t_p)
     else:
         # prompt positions 0..127 through the prompt pass (two chunks of 64 rows); time to first
         # token through the host API (ids in, first sampled id out), the median of 3 after one
@@ -333,13 +345,13 @@ def run_ours(args):
     if status != 0 or eng.device_status() != 0:
         raise SystemExit(f"device status {status}")
     hbm_peak, peak_kind = peaks()
-    roof = None if big else dominant_kernel_roofline(torch, vsl, cfg, ws, hbm_peak, peak_kind)
+    roof = None if big or w70 else dominant_kernel_roofline(torch, vsl, cfg, ws, hbm_peak, peak_kind)
     eng.close()
     tok_s = args.steps * B / (ms / 1e3)
     step_bytes = 0.5 * (bytes_start + bytes_end)  # per GPU; KV grows by one position per step
     step_gbs = step_bytes / (ms / 1e3 / args.steps) / 1e9
     cb = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not big and not qname:
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline and not big and not w70 and not qname:
         cb = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0 and big:
         step_roof = {"bound": "hbm", "kernel": "whole decode step (weights + 16 x 8192-position KV)",
@@ -362,6 +374,31 @@ def run_ours(args):
             "roofline": step_roof,
             "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
             "clocks": clk.summary(), "load_seconds": round(load_s, 2),
+        }
+        print(json.dumps(line), flush=True)
+    elif rank == 0 and w70:
+        line = {
+            "metric": "decode tok/s (70B fp16, bs1)", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random-init weights filled in HBM)",
+            "config": {"workload": "70B Llama shape fp16 (BASELINE configs[4]), batch 1, 2048-token prompt (prefill), "
+                                   f"decode positions {PREFILL_70B + args.warmup}..{PREFILL_70B + args.warmup + args.steps - 1}",
+                       "model": "llama-70b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
+                       "global_batch": 1, "seq_len": PREFILL_70B + args.warmup + args.steps,
+                       "parallelism": f"tp{ws}" if ws > 1 else "single",
+                       "l2": "inputs larger than L2 (140 GB of weights over the ranks per step)"},
+            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
+                    "api": "vsl_engine_step_host"},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step (this rank's weights + KV)",
+                         "achieved": round(step_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(step_gbs / hbm_peak, 4), "peak_kind": peak_kind,
+                         "bytes_per_step_per_gpu": round(step_bytes), "traffic": None},
+            "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
+            "clocks": clk.summary(), "load_seconds": round(load_s, 2),
+            "prefill": {"prompt_tokens": PREFILL_70B, "ttft_ms": round(ttft_s * 1e3, 3),
+                        "tok_s": round(PREFILL_70B / ttft_s, 1), "api": "vsl_engine_prefill",
+                        "timing": "host wall clock, one call, max over ranks"},
         }
         print(json.dumps(line), flush=True)
     elif rank == 0:
