@@ -8,6 +8,15 @@
 // default true). decode() reverses it (control tokens render as nothing, byte tokens as their
 // byte, U+2581 as a space, the dummy prefix removed).
 //
+// From a GGUF file with a byte-level BPE vocabulary (tokenizer.ggml.model "gpt2": tokens,
+// token types, merges, tokenizer.ggml.pre) it is GPT-2-style byte-level BPE: the text is split
+// by the pre-tokenizer pattern of tokenizer.ggml.pre ("llama-bpe" / "llama3": the Llama 3
+// pattern; anything else: GPT-2's), each piece's bytes become the printable characters of
+// GPT-2's byte map, and adjacent symbols are merged in order of merge rank (ties: leftmost);
+// with the Llama 3 pattern a piece that is itself a token is not merged (ignore_merges). BOS
+// is prepended when tokenizer.ggml.add_bos_token is true (default false). decode() maps the
+// characters back to bytes (control tokens render as nothing).
+//
 // Without such a vocabulary it keeps the behaviour the reference actually exhibits
 // (vk_symbiote/src/Tokenizer.cpp): its GGUF reader reads key, type and length in the wrong
 // order (:41-46), so it always falls back to the 256-entry byte vocabulary (:113-129):
@@ -37,18 +46,27 @@ public:
                                                     const std::vector<int32_t>& types, uint32_t bos_id,
                                                     uint32_t eos_id, uint32_t unk_id, bool add_bos,
                                                     bool add_space_prefix);
+    // GPT-2-style byte-level BPE: tokens in byte-map form, token types (3 = control, never
+    // produced by encode), merges "left right" in rank order, pre-tokenizer name
+    static std::unique_ptr<Tokenizer> byte_bpe(const std::vector<std::string>& tokens, const std::vector<int32_t>& types,
+                                               const std::vector<std::string>& merges, const std::string& pre,
+                                               uint32_t bos_id, uint32_t eos_id, bool add_bos);
     ~Tokenizer();
 
     std::vector<uint32_t> encode(const std::string& text) const;
     std::string decode(const std::vector<uint32_t>& tokens) const;
     uint32_t vocab_size() const;
-    bool is_subword() const { return spm_ != nullptr; }
+    bool is_subword() const { return spm_ != nullptr || bpe_ != nullptr; }
     uint32_t bos_id() const;
     uint32_t eos_id() const;
 
 private:
     struct Spm;
-    Spm* spm_ = nullptr;  // null: the byte-level contract
+    struct Bpe;
+    Spm* spm_ = nullptr;  // SentencePiece vocabulary
+    Bpe* bpe_ = nullptr;  // byte-level BPE vocabulary (both null: the byte-level contract)
+    std::vector<uint32_t> bpe_encode(const std::string& text) const;
+    std::string bpe_decode(const std::vector<uint32_t>& tokens) const;
 };
 
 }  // namespace vk_symbiote

@@ -1,6 +1,6 @@
-// Tokenizer: SentencePiece BPE from a GGUF vocabulary, or the reference's byte-level contract
-// (vk_symbiote/src/Tokenizer.cpp:113-198) when the file has none. Host code, off the decode
-// path: the engine consumes ids.
+// Tokenizer: SentencePiece BPE or GPT-2-style byte-level BPE (tokenizer_bpe.cpp) from a GGUF
+// vocabulary, or the reference's byte-level contract (vk_symbiote/src/Tokenizer.cpp:113-198)
+// when the file has none. Host code, off the decode path: the engine consumes ids.
 #include "../../../include/vk_symbiote/Tokenizer.h"
 
 #include <cstring>
@@ -11,6 +11,7 @@
 #include "../../../include/vk_symbiote/GGUFLoader.h"
 #include "../../../include/vsl.h"
 #include "status.h"
+#include "tokenizer_bpe.h"
 
 namespace vk_symbiote {
 
@@ -27,7 +28,10 @@ struct Tokenizer::Spm {
     bool add_bos = true, add_space_prefix = true;
 };
 
-Tokenizer::~Tokenizer() { delete spm_; }
+Tokenizer::~Tokenizer() {
+    delete spm_;
+    delete bpe_;
+}
 
 std::unique_ptr<Tokenizer> Tokenizer::byte_level() { return std::unique_ptr<Tokenizer>(new Tokenizer()); }
 
@@ -72,7 +76,31 @@ std::unique_ptr<Tokenizer> Tokenizer::from_gguf(const Path& gguf_path) {
     if (!loader.load()) return byte_level();
     const GGUFMetadataKV* model = loader.get_metadata("tokenizer.ggml.model");
     const auto& vocab = loader.get_vocabulary();
-    if (!model || model->get_string() != "llama" || vocab.empty()) return byte_level();
+    if (!model || vocab.empty()) return byte_level();
+    auto u32 = [&](const char* key, uint32_t dflt) {
+        const GGUFMetadataKV* kv = loader.get_metadata(key);
+        return kv ? (uint32_t)kv->get_number() : dflt;
+    };
+    auto flag = [&](const char* key, bool dflt) {
+        const GGUFMetadataKV* kv = loader.get_metadata(key);
+        return kv ? kv->get_bool() : dflt;
+    };
+    if (model->get_string() == "gpt2") {  // byte-level BPE: tokens, types, merges, pre-tokenizer
+        const GGUFMetadataKV* merges = loader.get_metadata("tokenizer.ggml.merges");
+        if (!merges) return byte_level();
+        const GGUFMetadataKV* pre = loader.get_metadata("tokenizer.ggml.pre");
+        std::vector<std::string> toks;
+        std::vector<int32_t> types;
+        toks.reserve(vocab.size());
+        for (const auto& e : vocab) {
+            toks.push_back(e.token);
+            types.push_back((int32_t)e.token_type);
+        }
+        return byte_bpe(toks, types, merges->array_strings, pre ? pre->get_string() : std::string(),
+                        u32("tokenizer.ggml.bos_token_id", 0), u32("tokenizer.ggml.eos_token_id", 0),
+                        flag("tokenizer.ggml.add_bos_token", false));
+    }
+    if (model->get_string() != "llama") return byte_level();
     std::vector<std::string> toks;
     std::vector<float> scores;
     std::vector<int32_t> types;
@@ -82,22 +110,16 @@ std::unique_ptr<Tokenizer> Tokenizer::from_gguf(const Path& gguf_path) {
         scores.push_back(e.score);
         types.push_back(e.token_type);
     }
-    auto u32 = [&](const char* key, uint32_t dflt) {
-        const GGUFMetadataKV* kv = loader.get_metadata(key);
-        return kv ? (uint32_t)kv->get_number() : dflt;
-    };
-    auto flag = [&](const char* key, bool dflt) {
-        const GGUFMetadataKV* kv = loader.get_metadata(key);
-        return kv ? kv->get_bool() : dflt;
-    };
     return sentencepiece(toks, scores, types, u32("tokenizer.ggml.bos_token_id", 1), u32("tokenizer.ggml.eos_token_id", 2),
                          u32("tokenizer.ggml.unknown_token_id", 0), flag("tokenizer.ggml.add_bos_token", true),
                          flag("tokenizer.ggml.add_space_prefix", true));
 }
 
-uint32_t Tokenizer::vocab_size() const { return spm_ ? (uint32_t)spm_->pieces.size() : 256u; }
-uint32_t Tokenizer::bos_id() const { return spm_ ? spm_->bos : 0u; }
-uint32_t Tokenizer::eos_id() const { return spm_ ? spm_->eos : 0u; }
+uint32_t Tokenizer::vocab_size() const {
+    return spm_ ? (uint32_t)spm_->pieces.size() : bpe_ ? (uint32_t)bpe_->tokens.size() : 256u;
+}
+uint32_t Tokenizer::bos_id() const { return spm_ ? spm_->bos : bpe_ ? bpe_->bos : 0u; }
+uint32_t Tokenizer::eos_id() const { return spm_ ? spm_->eos : bpe_ ? bpe_->eos : 0u; }
 
 static size_t utf8_len(unsigned char c) {
     if (c < 0x80) return 1;
@@ -108,6 +130,7 @@ static size_t utf8_len(unsigned char c) {
 }
 
 std::vector<uint32_t> Tokenizer::encode(const std::string& text) const {
+    if (bpe_) return bpe_encode(text);
     if (!spm_) {  // byte-level contract of the reference
         std::vector<uint32_t> ids;
         std::istringstream in(text);
@@ -183,6 +206,7 @@ std::vector<uint32_t> Tokenizer::encode(const std::string& text) const {
 }
 
 std::string Tokenizer::decode(const std::vector<uint32_t>& tokens) const {
+    if (bpe_) return bpe_decode(tokens);
     if (!spm_) {
         std::string out;
         for (size_t i = 0; i < tokens.size(); i++) {
