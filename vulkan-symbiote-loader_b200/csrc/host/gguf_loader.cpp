@@ -261,6 +261,13 @@ ExpectedVoid GGUFLoader::load() {
     if (auto v = m.meta("tokenizer.ggml.model")) m.tok_cfg.model_type = v->get_string();
     if (auto v = m.meta("tokenizer.ggml.bos_token_id")) m.tok_cfg.bos_token_id = v->get_uint32();
     if (auto v = m.meta("tokenizer.ggml.eos_token_id")) m.tok_cfg.eos_token_id = v->get_uint32();
+    if (auto v = m.meta("tokenizer.ggml.unknown_token_id")) m.tok_cfg.unk_token_id = v->get_uint32();
+    if (auto v = m.meta("tokenizer.ggml.padding_token_id")) m.tok_cfg.pad_token_id = v->get_uint32();
+    if (auto v = m.meta("tokenizer.ggml.add_bos_token")) m.tok_cfg.add_bos_token = v->get_bool();
+    if (auto v = m.meta("tokenizer.ggml.add_eos_token")) m.tok_cfg.add_eos_token = v->get_bool();
+    if (auto v = m.meta("tokenizer.ggml.add_space_prefix")) m.tok_cfg.add_space_prefix = v->get_bool();
+    if (auto v = m.meta("tokenizer.ggml.pre")) m.tok_cfg.pre_tokenizer = v->get_string();
+    if (auto v = m.meta("tokenizer.chat_template")) m.tok_cfg.chat_template = v->get_string();
     m.loaded = true;
     return ExpectedVoid();
 }
