@@ -176,7 +176,8 @@ def run_reference(args):
     # a bounded sample: each step is one decode token; total CPU time kept to about 2 minutes
     sec = min(120.0, max(10.0, 0.5 * (args.steps + args.warmup)))
     cb = cpu_baseline(cfg, sec, threads)
-    line = {"metric": "decode tok/s (7B fp16, bs1)", "value": round(cb["value"], 4), "unit": "tok/s",
+    cb["value"] = round(cb["value"], 4)  # the line's value
+    line = {"metric": "decode tok/s (7B fp16, bs1)", "value": cb["value"], "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random-init weights)",
