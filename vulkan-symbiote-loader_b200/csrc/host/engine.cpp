@@ -110,6 +110,7 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     set_pdl_enabled(opt.use_pdl != 0);
 
     CK(cudaSetDevice(opt.device));
+    CK(cudaDeviceGetAttribute(&l2_bytes_, cudaDevAttrL2CacheSize, opt.device));
     CK(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     CK(cudaStreamCreateWithFlags(&copy_stream_, cudaStreamNonBlocking));
     if (tp > 1) {
@@ -768,11 +769,13 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
     const TcRoute* tcr = sb.tc;
     // L2 prefetch hints: each kernel requests the head of the next projection's weights so
     // that the weight stream does not stall at kernel boundaries; the attention kernel
-    // (which reads little from HBM) prefetches the whole output projection.
+    // (which reads little from HBM) prefetches the output projection, up to half the L2
+    // (a larger request would evict its own head before the projection reads it).
     const size_t qkv_b = (size_t)(nh_l_ + 2 * nkv_l_) * hd * wrow(d), wo_b = (size_t)d * wrow((size_t)nh_l_ * hd);
     const size_t wgu_b = 2 * (size_t)ff_l_ * wrow(d), wd_b = (size_t)d * wrow(ff_l_);
     const size_t head = 16ull << 20;
     auto H = [&](size_t bytes) { return std::min(bytes, head); };
+    const size_t att_pf = std::min(wo_b, (size_t)l2_bytes_ / 2);
     const bool streamed = residency_.streamed_layers > 0;
     if (streamed) {  // bring the copy stream into this step (and into a graph being captured)
         CK(cudaEventRecord(ev_fork_, st));
@@ -801,7 +804,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
         else
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
-                                 head ? wo_b : 0, sb.shared_pages));
+                                 att_pf, sb.shared_pages));
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr,
                      fuse ? &prod : nullptr));
         if (!fuse) RC(allreduce_sum(sb.x, B * d));

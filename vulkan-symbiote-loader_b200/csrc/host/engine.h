@@ -208,6 +208,7 @@ private:
     int32_t* log_ = nullptr;
     int32_t* sampled_ = nullptr;
     int* status_ = nullptr;
+    int l2_bytes_ = 0;  // the device's L2 capacity (caps the attention kernel's L2 prefetch)
     int log_cap_ = 0;
 
     // pinned host staging for step_host
