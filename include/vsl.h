@@ -221,9 +221,10 @@ typedef struct {
                           replayed as a CUDA graph with programmatic dependent launch  */
     int use_p2p;       /* tensor parallel: 1 (default) = one-shot NVLink peer-memory all-reduces
                           (CUDA IPC buffers, one kernel per reduction); 0 = NCCL            */
-    int fuse_allreduce; /* tensor parallel with use_p2p: 1 (default) = the residual sums ride on the
+    int fuse_allreduce; /* tensor parallel with use_p2p: 1 = the residual sums ride on the
                           projections (row-parallel GEMV pushes its rows to every rank, the next
-                          projection sums them while staging); 0 = separate all-reduce kernel */
+                          projection sums them while staging); 0 (default) = separate all-reduce
+                          kernel (the fused sums measured slower at TP 2, 7B fp16 batch 1) */
     int legacy_q4;     /* 1 = read GGUF Q4_0 / Q4_1 nibbles in the reference loader's order
                           (GGUFLoader.cpp:1146-1160: element 2i low, 2i+1 high nibble of
                           byte i); 0 (default) = ggml's order (element i low, i+16 high)  */
