@@ -224,3 +224,24 @@ def test_known_answers(tmp_path):
     assert tokens[ord("\n")] == chr(256 + 10) and tok.encode("\n") == [ord("\n")]
     assert tok.decode([258, 256, 259]) == " thehe"
     tok.close()
+
+
+def test_arbitrary_bytes_round_trip(bpe_case):
+    """Byte-level BPE loses nothing: any byte string, invalid UTF-8 included, comes back
+    byte for byte (through the C ABI, without a text decode in between)."""
+    import ctypes as C
+
+    import numpy as np
+    _, voc, tok = bpe_case
+    L = vsl.lib()
+    rng = random.Random(5)
+    for n in list(range(0, 8)) + [rng.randrange(8, 200) for _ in range(150)]:
+        raw = bytes(rng.randrange(256) for _ in range(n))
+        ids = np.empty(2 * n + 8, np.int32)
+        cnt = C.c_int()
+        vsl.check(L.vsl_tokenize(tok.h, raw, len(raw), ids.ctypes.data, ids.size, C.byref(cnt)))
+        assert cnt.value >= 1 and ids[0] == voc["bos"]
+        buf = C.create_string_buffer(n + 1)
+        out_len = C.c_size_t()
+        vsl.check(L.vsl_detokenize(tok.h, ids.ctypes.data, cnt.value, buf, n + 1, C.byref(out_len)))
+        assert buf.raw[:out_len.value] == raw
