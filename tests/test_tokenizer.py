@@ -129,3 +129,33 @@ def test_files_without_vocabulary_keep_the_byte_level_contract(tmp_path):
     assert tok.encode("ab c") == [97, 98, 99]
     assert tok.encode("   ") == [0]
     assert tok.decode([97, 98, 99]) == "a b c"
+
+
+def test_arbitrary_bytes_round_trip(tmp_path):
+    """Byte fallback covers every byte: any byte string (invalid UTF-8 included, without the
+    bytes of U+2581 itself) comes back byte for byte through the C ABI."""
+    import ctypes as C
+
+    import numpy as np
+    pieces, scores, types = base_vocab()
+    for p in ("a", "b", SP, SP + "a", "ab", "é"):
+        pieces.append(p)
+        scores.append(-1.0)
+        types.append(1)
+    path = tmp_path / "bytes.gguf"
+    write_vocab_gguf(path, pieces, scores, types)
+    tok = vsl.Tokenizer(str(path))
+    L = vsl.lib()
+    rng = random.Random(3)
+    for n in list(range(0, 6)) + [rng.randrange(6, 120) for _ in range(150)]:
+        raw = bytes(rng.choice([rng.randrange(256), ord("a"), ord("b"), ord(" ")]) for _ in range(n))
+        if "▁".encode() in raw:
+            continue
+        ids = np.empty(4 * n + 8, np.int32)
+        cnt = C.c_int()
+        vsl.check(L.vsl_tokenize(tok.h, raw, len(raw), ids.ctypes.data, ids.size, C.byref(cnt)))
+        buf = C.create_string_buffer(n + 8)
+        out_len = C.c_size_t()
+        vsl.check(L.vsl_detokenize(tok.h, ids.ctypes.data, cnt.value, buf, n + 8, C.byref(out_len)))
+        assert buf.raw[:out_len.value] == raw, raw
+    tok.close()

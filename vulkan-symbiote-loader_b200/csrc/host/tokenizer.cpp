@@ -129,6 +129,16 @@ static size_t utf8_len(unsigned char c) {
     return 1;  // stray continuation byte: its own symbol
 }
 
+// bytes of the character at t[i]: its UTF-8 length when all continuation bytes are present,
+// else 1 (a malformed lead byte is a symbol of its own and does not swallow what follows)
+static size_t char_len(const std::string& t, size_t i) {
+    const size_t n = utf8_len((unsigned char)t[i]);
+    if (i + n > t.size()) return 1;
+    for (size_t k = 1; k < n; k++)
+        if (((unsigned char)t[i + k] & 0xC0) != 0x80) return 1;
+    return n;
+}
+
 std::vector<uint32_t> Tokenizer::encode(const std::string& text) const {
     if (bpe_) return bpe_encode(text);
     if (!spm_) {  // byte-level contract of the reference
@@ -157,7 +167,7 @@ std::vector<uint32_t> Tokenizer::encode(const std::string& text) const {
     };
     std::vector<Sym> sym;
     for (size_t i = 0; i < t.size();) {
-        const size_t n = std::min(utf8_len((unsigned char)t[i]), t.size() - i);
+        const size_t n = char_len(t, i);
         sym.push_back({(int)sym.size() - 1, (int)sym.size() + 1, i, n});
         i += n;
     }
