@@ -11,7 +11,7 @@
 // From a GGUF file with a byte-level BPE vocabulary (tokenizer.ggml.model "gpt2": tokens,
 // token types, merges, tokenizer.ggml.pre) it is GPT-2-style byte-level BPE: the text is split
 // by the pre-tokenizer pattern of tokenizer.ggml.pre ("llama-bpe" / "llama3": the Llama 3
-// pattern; anything else: GPT-2's), each piece's bytes become the printable characters of
+// pattern; "qwen2": the same with one digit per number piece; anything else: GPT-2's), each piece's bytes become the printable characters of
 // GPT-2's byte map, and adjacent symbols are merged in order of merge rank (ties: leftmost);
 // with the Llama 3 pattern a piece that is itself a token is not merged (ignore_merges). BOS
 // is prepended when tokenizer.ggml.add_bos_token is true (default false). decode() maps the

@@ -16,7 +16,8 @@ regex = pytest.importorskip("regex")
 GPT2_PAT = r"""'s|'t|'re|'ve|'m|'ll|'d| ?\p{L}+| ?\p{N}+| ?[^\s\p{L}\p{N}]+|\s+(?!\S)|\s+"""
 LLAMA3_PAT = (r"""(?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}| ?[^\s\p{L}\p{N}]+[\r\n]*|"""
               r"""\s*[\r\n]+|\s+(?!\S)|\s+""")
-PATTERNS = {"gpt-2": GPT2_PAT, "llama-bpe": LLAMA3_PAT}
+QWEN2_PAT = LLAMA3_PAT.replace(r"\p{N}{1,3}", r"\p{N}")
+PATTERNS = {"gpt-2": GPT2_PAT, "llama-bpe": LLAMA3_PAT, "qwen2": QWEN2_PAT}
 SPECIAL = ["<|begin_of_text|>", "<|end_of_text|>"]
 
 
@@ -98,7 +99,7 @@ def ref_encode(text, voc, pre, add_bos=True):
     out = [bos] if add_bos else []
     for p in pieces(text, pre):
         chars = to_chars(p)
-        if pre == "llama-bpe" and "".join(chars) in index:  # ignore_merges
+        if pre in ("llama-bpe", "qwen2") and "".join(chars) in index:  # ignore_merges
             out.append(index["".join(chars)])
             continue
         out += [index[s] for s in ref_bpe(chars, ranks)]
@@ -164,7 +165,7 @@ def write_bpe_gguf(path, voc, pre, add_bos=True):
     gguf.write_gguf(str(path), meta, [])
 
 
-@pytest.fixture(scope="module", params=["gpt-2", "llama-bpe"])
+@pytest.fixture(scope="module", params=["gpt-2", "llama-bpe", "qwen2"])
 def bpe_case(request, tmp_path_factory):
     pre = request.param
     voc = build_vocab(pre)

@@ -147,7 +147,8 @@ size_t match_gpt2(const std::vector<Cp>& c, size_t i) {
 
 // Llama 3: (?i:'s|'t|'re|'ve|'m|'ll|'d)|[^\r\n\p{L}\p{N}]?\p{L}+|\p{N}{1,3}|
 //          ?[^\s\p{L}\p{N}]+[\r\n]*|\s*[\r\n]+|\s+(?!\S)|\s+
-size_t match_llama3(const std::vector<Cp>& c, size_t i) {
+// Qwen 2: the same with \p{N} (one digit per piece): max_digits 1.
+size_t match_llama3(const std::vector<Cp>& c, size_t i, size_t max_digits) {
     const size_t n = c.size();
     if (size_t k = contraction(c, i, true)) return k;
     const CpClass ci = c[i].cls;
@@ -156,7 +157,7 @@ size_t match_llama3(const std::vector<Cp>& c, size_t i) {
     if (ci == C_LETTER) return run(c, i, C_LETTER);
     if (ci == C_NUMBER) {
         const size_t r = run(c, i, C_NUMBER);
-        return r < 3 ? r : 3;
+        return r < max_digits ? r : max_digits;
     }
     size_t j = 0;
     if (c[i].cp == ' ' && i + 1 < n && c[i + 1].cls == C_OTHER) j = i + 1 + run(c, i + 1, C_OTHER);
@@ -187,7 +188,8 @@ std::unique_ptr<Tokenizer> Tokenizer::byte_bpe(const std::vector<std::string>& t
     b->bos = bos_id;
     b->eos = eos_id;
     b->add_bos = add_bos;
-    b->llama3 = pre == "llama-bpe" || pre == "llama3" || pre == "llama-v3";
+    b->llama3 = pre == "llama-bpe" || pre == "llama3" || pre == "llama-v3" || pre == "qwen2";
+    b->max_digits = pre == "qwen2" ? 1 : 3;
     for (uint32_t i = 0; i < (uint32_t)tokens.size(); i++)
         if (b->types[i] != 3) b->index.emplace(tokens[i], i);  // the first id of a duplicate wins
     for (int r = 0; r < (int)merges.size(); r++) b->ranks.emplace(merges[r], r);
@@ -216,7 +218,7 @@ std::vector<uint32_t> Tokenizer::bpe_encode(const std::string& text) const {
     };
     auto worse = [](const Pair& x, const Pair& y) { return x.rank > y.rank || (x.rank == y.rank && x.left > y.left); };
     for (size_t i = 0; i < c.size();) {
-        const size_t k = b.llama3 ? match_llama3(c, i) : match_gpt2(c, i);
+        const size_t k = b.llama3 ? match_llama3(c, i, b.max_digits) : match_gpt2(c, i);
         const size_t p0 = c[i].pos, p1 = c[i + k - 1].pos + c[i + k - 1].len;
         i += k;
         std::vector<Sym> sym;

@@ -17,7 +17,8 @@ struct Tokenizer::Bpe {
     std::unordered_map<std::string, int> ranks;       // "left right" -> merge rank
     std::string byte_char[256];                       // byte -> its printable character (UTF-8)
     std::unordered_map<unsigned, unsigned char> char_byte;
-    bool llama3 = false;
+    bool llama3 = false;      // the Llama 3 pattern family (with ignore_merges), else GPT-2's
+    size_t max_digits = 3;    // digits per number piece in that family (Qwen 2: 1)
     uint32_t bos = 0, eos = 0;
     bool add_bos = false;
 };
