@@ -60,10 +60,10 @@ def parse():
                          "configs[4] at batch 1 after a 2048-token prompt pass, tensor-parallel over --gpus "
                          "(run it under torchrun with 8 GPUs for the TP 8 figure); 70b-stream: BASELINE configs[4] "
                          "on one GPU under a 64 GB HBM cap (layers streamed from host)")
-    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "prefill"],
+    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "gemv_q41", "prefill"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
-                         "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 = "
-                         "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 weights at batch 1; prefill = "
+                         "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 / gemv_q41 = "
+                         "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 / Q4_1 weights at batch 1; prefill = "
                          "three 128-token prompt passes on the 7B shape (--layers, default 4)")
     ap.add_argument("--profile-shape", default="32000,4096,16",
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
@@ -600,8 +600,8 @@ def run_profile_case(args):
                 e.prefill(prompt)
             if e.device_status() != 0:
                 raise SystemExit("device status")
-    elif args.profile_case in ("gemv_q8", "gemv_q4"):
-        dt = vsl.Q8_0 if args.profile_case == "gemv_q8" else vsl.Q4_0
+    elif args.profile_case in ("gemv_q8", "gemv_q4", "gemv_q41"):
+        dt = {"gemv_q8": vsl.Q8_0, "gemv_q4": vsl.Q4_0, "gemv_q41": vsl.Q4_1}[args.profile_case]
         N, K = 2 * CONFIG_7B["ffn"], CONFIG_7B["d_model"]
         rb = vsl.weight_row_bytes(dt, K)
         Ws = [torch.empty(N, rb, dtype=torch.uint8, device="cuda") for _ in range(4)]  # > L2 in total
