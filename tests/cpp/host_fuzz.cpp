@@ -1,0 +1,91 @@
+// Host-code fuzz driver, built with AddressSanitizer and UndefinedBehaviorSanitizer by
+// tests/test_host_sanitizers.py (no GPU, no CUDA code): damaged copies of a GGUF file go through
+// GGUFLoader (parse, model config, tensor lookup, host fp32 reads, mapped tensors),
+// Tokenizer::from_gguf with random bytes to encode and random ids to decode, and random text
+// goes through ConfigManager's file parser. Prints "ok <files> <refused>" when every input
+// returned; any memory error or undefined behaviour aborts the process with a report.
+//
+//   host_fuzz <model.gguf> <scratch dir> <seed> <iterations>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <fstream>
+#include <iterator>
+#include <random>
+#include <string>
+#include <vector>
+
+#include "vk_symbiote/ConfigManager.h"
+#include "vk_symbiote/GGUFLoader.h"
+#include "vk_symbiote/Tokenizer.h"
+
+using namespace vk_symbiote;
+
+static void write_file(const std::string& path, const std::vector<unsigned char>& d) {
+    std::ofstream f(path, std::ios::binary | std::ios::trunc);
+    f.write(reinterpret_cast<const char*>(d.data()), (std::streamsize)d.size());
+}
+
+int main(int argc, char** argv) {
+    if (argc < 5) {
+        fprintf(stderr, "usage: host_fuzz <model.gguf> <scratch dir> <seed> <iterations>\n");
+        return 2;
+    }
+    std::ifstream in(argv[1], std::ios::binary);
+    const std::vector<unsigned char> base((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+    if (base.size() < 64) return 2;
+    const std::string dir = argv[2];
+    std::mt19937_64 rng(std::strtoull(argv[3], nullptr, 10));
+    const int iters = std::atoi(argv[4]);
+    const size_t head = std::min<size_t>(base.size(), 4096);  // header, metadata, tensor infos
+    auto uni = [&](size_t n) { return (size_t)(rng() % (n ? n : 1)); };
+    int refused = 0;
+    for (int it = 0; it < iters; it++) {
+        std::vector<unsigned char> d = base;
+        const size_t mode = uni(10);
+        if (mode < 7) {
+            for (size_t k = 0, n = 1 + uni(5); k < n; k++) d[8 + uni(head - 8)] = (unsigned char)uni(256);
+        } else if (mode < 9) {  // a count or length field set huge
+            const size_t p = 8 + uni(head - 16);
+            const uint64_t v[3] = {~0ull, 0x7fffffffull, 1ull << 40};
+            const uint64_t x = v[uni(3)];
+            for (int b = 0; b < 8; b++) d[p + b] = (unsigned char)(x >> (8 * b));
+        } else {
+            d.resize(uni(d.size()));
+        }
+        const std::string path = dir + "/fuzz.gguf";
+        write_file(path, d);
+        {
+            GGUFLoader g(path);
+            if (!g.load()) {
+                refused++;
+            } else {
+                (void)g.get_model_config();
+                for (const std::string& name : g.get_tensor_names()) {
+                    const GGUFTensorInfo* t = g.get_tensor(name);
+                    if (t && t->element_count() <= (1u << 20)) (void)g.read_tensor_data(*t);
+                    (void)g.map_tensor(name);
+                }
+                (void)g.get_vocabulary().size();
+            }
+        }
+        auto tok = Tokenizer::from_gguf(path);
+        std::string text;
+        for (size_t k = 0, n = uni(48); k < n; k++) text += (char)uni(256);
+        const std::vector<uint32_t> ids = tok->encode(text);
+        std::vector<uint32_t> rid;
+        for (size_t k = 0, n = uni(16); k < n; k++) rid.push_back((uint32_t)uni(2 * tok->vocab_size() + 3));
+        (void)tok->decode(ids);
+        (void)tok->decode(rid);
+        if (it % 4 == 0) {  // the config parser on random text (brackets, quotes, '=' and '#' likely)
+            const char alphabet[] = "[]=#\"'\n .-_0123456789abcdefgmrvtuxyzAB\t";
+            std::string cfg;
+            for (size_t k = 0, n = uni(300); k < n; k++) cfg += alphabet[uni(sizeof(alphabet) - 1)];
+            std::vector<unsigned char> c(cfg.begin(), cfg.end());
+            write_file(dir + "/fuzz.toml", c);
+            (void)ConfigManager::instance().load_from_file(dir + "/fuzz.toml");
+        }
+    }
+    printf("ok %d %d\n", iters, refused);
+    return 0;
+}

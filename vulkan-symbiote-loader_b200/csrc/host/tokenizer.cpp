@@ -28,6 +28,16 @@ struct Tokenizer::Spm {
     bool add_bos = true, add_space_prefix = true;
 };
 
+// The byte of a byte piece "<0xXX>" (exactly two hex digits), or -1 for any other piece.
+static int byte_piece(const std::string& p) {
+    if (p.size() != 6 || p.compare(0, 3, "<0x") != 0 || p[5] != '>') return -1;
+    auto hex = [](char c) {
+        return c >= '0' && c <= '9' ? c - '0' : c >= 'A' && c <= 'F' ? c - 'A' + 10 : c >= 'a' && c <= 'f' ? c - 'a' + 10 : -1;
+    };
+    const int hi = hex(p[3]), lo = hex(p[4]);
+    return hi < 0 || lo < 0 ? -1 : hi * 16 + lo;
+}
+
 Tokenizer::~Tokenizer() {
     delete spm_;
     delete bpe_;
@@ -57,8 +67,8 @@ std::unique_ptr<Tokenizer> Tokenizer::sentencepiece(const std::vector<std::strin
     for (uint32_t i = 0; i < (uint32_t)tokens.size(); i++) {
         const std::string& p = tokens[i];
         // byte pieces "<0xXX>" (type 6 in GGUF) are the fallback for characters without a piece
-        if (p.size() == 6 && p.compare(0, 3, "<0x") == 0 && p[5] == '>') {
-            const int b = (int)std::strtol(p.substr(3, 2).c_str(), nullptr, 16);
+        const int b = byte_piece(p);
+        if (b >= 0) {
             if (!s->has_byte[b]) {
                 s->has_byte[b] = true;
                 s->byte_id[b] = i;
@@ -231,8 +241,9 @@ std::string Tokenizer::decode(const std::vector<uint32_t>& tokens) const {
         if (id >= s.pieces.size()) continue;
         if (s.types[id] == 3) continue;  // control
         const std::string& p = s.pieces[id];
-        if (p.size() == 6 && p.compare(0, 3, "<0x") == 0 && p[5] == '>') {
-            out += (char)std::strtol(p.substr(3, 2).c_str(), nullptr, 16);
+        const int b = byte_piece(p);
+        if (b >= 0) {
+            out += (char)b;
             continue;
         }
         for (size_t i = 0; i < p.size();) {
