@@ -1,6 +1,7 @@
 """The host C++ code that parses untrusted input (GGUFLoader, Tokenizer, ConfigManager), built
 with AddressSanitizer and UndefinedBehaviorSanitizer and fuzzed with damaged GGUF files, random
-text and random ids (tests/cpp/host_fuzz.cpp). No GPU and no CUDA code are involved."""
+text and random ids (tests/cpp/host_fuzz.cpp); and the loader's threaded reads and tensor cache
+built with ThreadSanitizer (tests/cpp/loader_threads.cpp). No GPU and no CUDA code are involved."""
 import os
 import shutil
 import subprocess
@@ -69,3 +70,17 @@ def test_host_parsers_under_sanitizers(fuzz_bin, model_gguf, tmp_path, which, se
     assert "runtime error" not in r.stderr, r.stderr[-3000:]
     words = r.stdout.split()
     assert words[0] == "ok" and int(words[1]) == 1500 and int(words[2]) > 300  # most damaged files are refused
+
+
+def test_loader_threads_under_thread_sanitizer(model_gguf, tmp_path):
+    if not shutil.which("g++"):
+        pytest.skip("g++ not available")
+    out = str(tmp_path / "loader_threads")
+    subprocess.run(["g++", "-std=c++17", "-g", "-O1", "-fsanitize=thread", "-I" + os.path.join(ROOT, "include"),
+                    "-I" + HOST, "-I/usr/local/cuda/include", os.path.join(ROOT, "tests", "cpp", "loader_threads.cpp"),
+                    os.path.join(HOST, "gguf_loader.cpp"), os.path.join(HOST, "status.cpp"), "-o", out, "-lpthread"],
+                   check=True, capture_output=True, timeout=600)
+    r = subprocess.run([out, model_gguf[0]], capture_output=True, text=True, timeout=600,
+                       env=dict(os.environ, TSAN_OPTIONS="halt_on_error=1"))
+    assert r.returncode == 0 and "ThreadSanitizer" not in r.stderr, r.stderr[-3000:]
+    assert r.stdout.split() == ["ok", "6"]

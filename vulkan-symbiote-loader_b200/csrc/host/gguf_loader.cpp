@@ -442,7 +442,8 @@ Expected<std::vector<float>> GGUFLoader::read_tensor_cached(const std::string& n
     if (!r) return r;
     std::lock_guard<std::mutex> lk(m.cache_mu);
     const size_t bytes = r.value().size() * sizeof(float);
-    if (bytes <= m.cache_cfg.max_memory_bytes) {
+    // another thread may have read and cached the same tensor meanwhile: keep one copy
+    if (bytes <= m.cache_cfg.max_memory_bytes && m.lru_map.find(key) == m.lru_map.end()) {
         m.lru.emplace_front(key, r.value());
         m.lru_map[key] = m.lru.begin();
         m.cache_bytes += bytes;
@@ -481,8 +482,14 @@ void GGUFLoader::clear_tensor_cache() {
     pimpl_->lru_map.clear();
     pimpl_->cache_bytes = 0;
 }
-size_t GGUFLoader::get_tensor_cache_size() const { return pimpl_->lru.size(); }
-void GGUFLoader::configure_cache(const TensorCacheConfig& c) { pimpl_->cache_cfg = c; }
+size_t GGUFLoader::get_tensor_cache_size() const {
+    std::lock_guard<std::mutex> lk(pimpl_->cache_mu);
+    return pimpl_->lru.size();
+}
+void GGUFLoader::configure_cache(const TensorCacheConfig& c) {
+    std::lock_guard<std::mutex> lk(pimpl_->cache_mu);
+    pimpl_->cache_cfg = c;
+}
 
 std::vector<std::string> GGUFLoader::get_tensor_names() const {
     std::vector<std::string> v;
