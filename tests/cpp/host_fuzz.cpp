@@ -60,7 +60,7 @@ int main(int argc, char** argv) {
             if (!g.load()) {
                 refused++;
             } else {
-                (void)g.get_model_config();
+                (void)g.generate_packs(g.get_model_config());
                 for (const std::string& name : g.get_tensor_names()) {
                     const GGUFTensorInfo* t = g.get_tensor(name);
                     if (t && t->element_count() <= (1u << 20)) (void)g.read_tensor_data(*t);
@@ -84,6 +84,15 @@ int main(int argc, char** argv) {
             std::vector<unsigned char> c(cfg.begin(), cfg.end());
             write_file(dir + "/fuzz.toml", c);
             (void)ConfigManager::instance().load_from_file(dir + "/fuzz.toml");
+            // and the command line: flags of the reference, values that do not parse, missing values
+            static const char* const flags[] = {"--model", "--config", "--vram-gb", "--ram-gb", "-v", "--verbose",
+                                                "--power-profile", "--benchmark", "--tp", "--device", "--disable-gpu",
+                                                "1.5", "-3", "x", "", "99999999999999999999", "nan"};
+            std::vector<std::string> args = {"prog"};
+            for (size_t k = 0, n = uni(8); k < n; k++) args.push_back(flags[uni(sizeof(flags) / sizeof(flags[0]))]);
+            std::vector<char*> av;
+            for (auto& a : args) av.push_back(&a[0]);
+            (void)ConfigManager::instance().load_from_args((int)av.size(), av.data());
         }
     }
     printf("ok %d %d\n", iters, refused);
