@@ -159,3 +159,15 @@ def test_arbitrary_bytes_round_trip(tmp_path):
         vsl.check(L.vsl_detokenize(tok.h, ids.ctypes.data, cnt.value, buf, n + 8, C.byref(out_len)))
         assert buf.raw[:out_len.value] == raw, raw
     tok.close()
+
+
+def test_encode_grows_its_buffer(tmp_path):
+    """Without a U+2581 piece every space costs three byte tokens: more ids than bytes."""
+    pieces, scores, types = base_vocab()
+    path = tmp_path / "nospace.gguf"
+    write_vocab_gguf(path, pieces, scores, types)
+    tok = vsl.Tokenizer(str(path))
+    ids = tok.encode(" " * 40)
+    assert len(ids) == 1 + 3 * 41  # BOS, then the dummy prefix and 40 spaces as 3 bytes each
+    assert tok.decode(ids) == " " * 40
+    tok.close()

@@ -236,23 +236,24 @@ std::string Tokenizer::decode(const std::vector<uint32_t>& tokens) const {
         return out;
     }
     const Spm& s = *spm_;
-    std::string out;
+    // pieces and byte tokens first, then every U+2581 of the result is a space (also when the
+    // mark itself came as byte tokens), then the dummy prefix goes
+    std::string raw;
     for (uint32_t id : tokens) {
         if (id >= s.pieces.size()) continue;
         if (s.types[id] == 3) continue;  // control
         const std::string& p = s.pieces[id];
         const int b = byte_piece(p);
-        if (b >= 0) {
-            out += (char)b;
-            continue;
-        }
-        for (size_t i = 0; i < p.size();) {
-            if (p.compare(i, SPACE_MARK.size(), SPACE_MARK) == 0) {
-                out += ' ';
-                i += SPACE_MARK.size();
-            } else {
-                out += p[i++];
-            }
+        if (b >= 0) raw += (char)b;
+        else raw += p;
+    }
+    std::string out;
+    for (size_t i = 0; i < raw.size();) {
+        if (raw.compare(i, SPACE_MARK.size(), SPACE_MARK) == 0) {
+            out += ' ';
+            i += SPACE_MARK.size();
+        } else {
+            out += raw[i++];
         }
     }
     if (s.add_space_prefix && !out.empty() && out[0] == ' ') out.erase(0, 1);

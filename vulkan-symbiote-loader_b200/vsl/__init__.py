@@ -179,7 +179,11 @@ class Tokenizer:
         n = C.c_int()
         cap = 2 * len(b) + 8
         out = np.empty(cap, np.int32)
-        check(lib().vsl_tokenize(self.h, b, len(b), out.ctypes.data, cap, C.byref(n)))
+        rc = lib().vsl_tokenize(self.h, b, len(b), out.ctypes.data, cap, C.byref(n))
+        if rc == -5 and n.value > cap:  # VSL_ERR_BOUNDS: n holds the count needed
+            out = np.empty(n.value, np.int32)
+            rc = lib().vsl_tokenize(self.h, b, len(b), out.ctypes.data, n.value, C.byref(n))
+        check(rc)
         return out[:n.value].tolist()
 
     def decode(self, ids) -> str:
