@@ -2,7 +2,9 @@
 // tests/test_host_sanitizers.py (no GPU, no CUDA code): damaged copies of a GGUF file go through
 // GGUFLoader (parse, model config, tensor lookup, host fp32 reads, mapped tensors),
 // Tokenizer::from_gguf with random bytes to encode and random ids to decode, and random text
-// goes through ConfigManager's file parser. Prints "ok <files> <refused>" when every input
+// goes through ConfigManager's file parser; random slices of random GGUF blocks are repacked into
+// the device row layout (exactly sized buffers) and the pack planner gets random budgets. Prints
+// "ok <files> <refused>" when every input
 // returned; any memory error or undefined behaviour aborts the process with a report.
 //
 //   host_fuzz <model.gguf> <scratch dir> <seed> <iterations>
@@ -15,8 +17,10 @@
 #include <string>
 #include <vector>
 
+#include "kernels.h"
 #include "vk_symbiote/ConfigManager.h"
 #include "vk_symbiote/GGUFLoader.h"
+#include "vk_symbiote/NomadPack.h"
 #include "vk_symbiote/Tokenizer.h"
 
 using namespace vk_symbiote;
@@ -94,6 +98,24 @@ int main(int argc, char** argv) {
             for (auto& a : args) av.push_back(&a[0]);
             (void)ConfigManager::instance().load_from_args((int)av.size(), av.data());
         }
+    }
+    for (int it = 0; it < iters; it++) {  // repack and residency planning
+        const int dts[4] = {VSL_Q8_0, VSL_Q4_0, VSL_Q4_1, VSL_F16};
+        const int dt = dts[uni(4)];
+        const size_t cols = 32 * (1 + uni(16)), rows = 1 + uni(6);
+        const size_t bb = vsl::is_quant(dt) ? vsl::gguf_block_bytes(dt) : 2;
+        std::vector<unsigned char> blocks(rows * (cols / 32) * bb);
+        for (auto& x : blocks) x = (unsigned char)uni(256);
+        const size_t row0 = uni(rows), nrows = 1 + uni(rows - row0);
+        size_t col0 = 32 * uni(cols / 32 + 1), ncols = 32 * uni(cols / 32 + 1);
+        if (uni(8) == 0) col0 += 1 + uni(31);  // misaligned: refused
+        const size_t ld = vsl::is_quant(dt) ? vsl::weight_row_bytes(dt, ncols) + 16 * uni(2) : 64;
+        std::vector<unsigned char> out(nrows * ld + 1);
+        if (vsl::repack_gguf_rows(dt, blocks.data(), cols, row0, nrows, col0, ncols, out.data(), ld, (int)uni(2)))
+            refused++;
+        const uint64_t lb = rng() >> uni(64), fb = rng() >> uni(64), budget = rng() >> uni(64);
+        const PackResidency r = NomadPackManager::plan(lb >> 20, (uint32_t)uni(200), fb >> 20, budget >> 20);
+        if (r.feasible && r.resident_layers + r.streamed_layers > 200) return 3;
     }
     printf("ok %d %d\n", iters, refused);
     return 0;

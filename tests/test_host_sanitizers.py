@@ -13,7 +13,8 @@ from vsl import gguf, synth
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HOST = os.path.join(ROOT, "vulkan-symbiote-loader_b200", "csrc", "host")
-SOURCES = ["gguf_loader.cpp", "tokenizer.cpp", "tokenizer_bpe.cpp", "config_manager.cpp", "status.cpp"]
+SOURCES = ["gguf_loader.cpp", "tokenizer.cpp", "tokenizer_bpe.cpp", "config_manager.cpp", "quant_repack.cpp",
+           "nomad_pack.cpp", "status.cpp"]
 
 
 @pytest.fixture(scope="module")
