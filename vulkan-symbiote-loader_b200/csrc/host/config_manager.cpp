@@ -6,6 +6,7 @@
 #include <ctime>
 #include <fstream>
 #include <iomanip>
+#include <limits>
 #include <iostream>
 #include <sstream>
 
@@ -231,7 +232,9 @@ bool ConfigManager::save_to_toml(const Path& config_path) {
     std::ofstream f(config_path.string());
     if (!f.is_open()) return false;
     f << "# Vulkan-Symbiote B200 configuration\n";
-    f << "[memory]\nvram_budget_gb = " << std::fixed << std::setprecision(2) << memory_config_.vram_budget_gb
+    // floats with enough digits to read back the same value (a fixed 2 decimals did not)
+    f << std::setprecision(std::numeric_limits<float>::max_digits10);
+    f << "[memory]\nvram_budget_gb = " << memory_config_.vram_budget_gb
       << "\nram_budget_gb = " << memory_config_.ram_budget_gb
       << "\nprefetch_lookahead = " << memory_config_.prefetch_lookahead
       << "\neviction_aggression = " << memory_config_.eviction_aggression
