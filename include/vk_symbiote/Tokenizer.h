@@ -57,6 +57,7 @@ public:
     std::string decode(const std::vector<uint32_t>& tokens) const;
     uint32_t vocab_size() const;
     bool is_subword() const { return spm_ != nullptr || bpe_ != nullptr; }
+    bool is_byte_bpe() const { return bpe_ != nullptr; }  // a GPT-2-style ("gpt2") vocabulary
     uint32_t bos_id() const;
     uint32_t eos_id() const;
 

@@ -74,8 +74,9 @@ public:
     VulkanSymbioteEngine& operator=(const VulkanSymbioteEngine&) = delete;
 
     // generate (VulkanSymbioteEngine.cpp:678-765): returns prompt + decoded tokens; stops
-    // after emitting id 0 or 2. Any temperature gives the reference's result, the argmax
-    // (its top_k_sampling hands back the most probable token first, :1548-1552).
+    // after emitting id 0 or 2 (with a byte-level BPE vocabulary, where those are ordinary
+    // tokens: after its end-of-text id). Any temperature gives the reference's result, the
+    // argmax (its top_k_sampling hands back the most probable token first, :1548-1552).
     std::string generate(const std::string& prompt, uint32_t max_tokens = 256, float temperature = 0.7f);
 
     // Token-id generation: temperature > 0 samples with the seeded Gumbel-max sampler;
@@ -114,6 +115,9 @@ private:
 
     vsl_engine* engine_ = nullptr;
     std::unique_ptr<Tokenizer> tokenizer_;
+    // ids that end generate() / generate_text_batch(): 0 and 2 as in the reference, or the
+    // end-of-text id of a byte-level BPE vocabulary (where 0 and 2 are ordinary tokens)
+    std::vector<uint32_t> text_stop_ids() const;
     ModelConfig config_;
     PerformanceMetrics performance_metrics_;
     uint32_t max_seq_ = 0;

@@ -69,6 +69,11 @@ std::vector<uint32_t> VulkanSymbioteEngine::encode(const std::string& text) { re
 
 std::string VulkanSymbioteEngine::decode(const std::vector<uint32_t>& tokens) { return tokenizer_->decode(tokens); }
 
+std::vector<uint32_t> VulkanSymbioteEngine::text_stop_ids() const {
+    if (tokenizer_ && tokenizer_->is_byte_bpe()) return {tokenizer_->eos_id()};
+    return {0u, 2u};
+}
+
 std::vector<uint32_t> VulkanSymbioteEngine::generate_ids(const std::vector<uint32_t>& prompt, uint32_t max_new_tokens,
                                                          float temperature, const std::vector<uint32_t>& stop_ids,
                                                          uint64_t seed) {
@@ -99,8 +104,11 @@ std::string VulkanSymbioteEngine::generate(const std::string& prompt, uint32_t m
     const uint32_t n = std::min(max_tokens, room);
     std::string result = prompt;
     if (n == 0) return result;
-    // greedy for every temperature, and stop after emitting 0 or 2 (VulkanSymbioteEngine.cpp:747-749)
-    const std::vector<uint32_t> out = generate_ids(ids, n, 0.0f, {0u, 2u});
+    // greedy for every temperature, and stop after emitting 0 or 2 (VulkanSymbioteEngine.cpp:747-749),
+    // the unknown and end-of-sequence ids of the SentencePiece vocabularies the reference has in
+    // view; in a byte-level BPE vocabulary those ids are ordinary tokens ("!" and "#"), so there
+    // the vocabulary's own end-of-text id stops generation instead
+    const std::vector<uint32_t> out = generate_ids(ids, n, 0.0f, text_stop_ids());
     for (uint32_t t : out) result += decode({t});
     return result;
 }
@@ -126,10 +134,11 @@ std::vector<std::string> VulkanSymbioteEngine::generate_text_batch(const std::ve
         const uint32_t n = std::min<uint32_t>(max_tokens_per_prompt, max_seq_ - longest);
         std::vector<int32_t> ids_out(nb * std::max<uint32_t>(n, 1));
         std::vector<int> n_out(nb, 0);
-        const int32_t stops[2] = {0, 2};
+        const std::vector<uint32_t> sv = text_stop_ids();
+        const std::vector<int32_t> stops(sv.begin(), sv.end());
         const uint64_t t0 = get_current_time_ns();
-        if (n > 0 && vsl_engine_generate_batch(engine_, flat.data(), lens.data(), (int)nb, (int)n, 0.0f, 0, stops, 2,
-                                               ids_out.data(), n_out.data()) != VSL_OK)
+        if (n > 0 && vsl_engine_generate_batch(engine_, flat.data(), lens.data(), (int)nb, (int)n, 0.0f, 0, stops.data(),
+                                               (int)stops.size(), ids_out.data(), n_out.data()) != VSL_OK)
             throw_vsl("generate_text_batch");
         uint32_t produced = 0;
         for (size_t b = 0; b < nb; b++) {
