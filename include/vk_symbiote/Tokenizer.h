@@ -55,6 +55,11 @@ public:
 
     std::vector<uint32_t> encode(const std::string& text) const;
     std::string decode(const std::vector<uint32_t>& tokens) const;
+    // Text of `tokens` generated after `context`: for a vocabulary, decode(context + tokens)
+    // with decode(context) taken off the front, so each piece keeps its own spaces (decoding a
+    // piece alone would drop its leading space as the dummy prefix); for the byte-level
+    // contract, the tokens decoded one by one and concatenated, as the reference's generate does.
+    std::string decode_continuation(const std::vector<uint32_t>& context, const std::vector<uint32_t>& tokens) const;
     uint32_t vocab_size() const;
     bool is_subword() const { return spm_ != nullptr || bpe_ != nullptr; }
     bool is_byte_bpe() const { return bpe_ != nullptr; }  // a GPT-2-style ("gpt2") vocabulary

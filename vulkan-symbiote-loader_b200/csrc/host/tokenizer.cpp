@@ -260,6 +260,20 @@ std::string Tokenizer::decode(const std::vector<uint32_t>& tokens) const {
     return out;
 }
 
+std::string Tokenizer::decode_continuation(const std::vector<uint32_t>& context,
+                                           const std::vector<uint32_t>& tokens) const {
+    std::string per_token;
+    if (!is_subword()) {
+        for (uint32_t t : tokens) per_token += decode({t});
+        return per_token;
+    }
+    std::vector<uint32_t> all(context);
+    all.insert(all.end(), tokens.begin(), tokens.end());
+    const std::string head = decode(context), full = decode(all);
+    if (full.size() >= head.size() && full.compare(0, head.size(), head) == 0) return full.substr(head.size());
+    return decode(tokens);  // not reached for these decoders: the context's text is always a prefix
+}
+
 }  // namespace vk_symbiote
 
 // ---------------------------------------------------------------------------------------

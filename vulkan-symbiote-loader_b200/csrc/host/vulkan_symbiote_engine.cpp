@@ -109,7 +109,7 @@ std::string VulkanSymbioteEngine::generate(const std::string& prompt, uint32_t m
     // view; in a byte-level BPE vocabulary those ids are ordinary tokens ("!" and "#"), so there
     // the vocabulary's own end-of-text id stops generation instead
     const std::vector<uint32_t> out = generate_ids(ids, n, 0.0f, text_stop_ids());
-    for (uint32_t t : out) result += decode({t});
+    result += tokenizer_->decode_continuation(ids, out);
     return result;
 }
 
@@ -123,9 +123,11 @@ std::vector<std::string> VulkanSymbioteEngine::generate_text_batch(const std::ve
         const size_t nb = std::min<size_t>(max_batch_, prompts.size() - p0);
         std::vector<int32_t> flat;
         std::vector<int> lens(nb);
+        std::vector<std::vector<uint32_t>> prompt_ids(nb);
         uint32_t longest = 0;
         for (size_t b = 0; b < nb; b++) {
-            std::vector<uint32_t> ids = encode(prompts[p0 + b]);
+            std::vector<uint32_t>& ids = prompt_ids[b];
+            ids = encode(prompts[p0 + b]);
             if (ids.size() >= max_seq_) ids.resize(max_seq_ - 1);
             lens[b] = (int)ids.size();
             longest = std::max<uint32_t>(longest, (uint32_t)ids.size());
@@ -143,7 +145,8 @@ std::vector<std::string> VulkanSymbioteEngine::generate_text_batch(const std::ve
         uint32_t produced = 0;
         for (size_t b = 0; b < nb; b++) {
             std::string r = prompts[p0 + b];
-            for (int k = 0; k < n_out[b]; k++) r += decode({(uint32_t)ids_out[b * n + k]});
+            const std::vector<uint32_t> gen(ids_out.begin() + b * n, ids_out.begin() + b * n + n_out[b]);
+            r += tokenizer_->decode_continuation(prompt_ids[b], gen);
             produced += (uint32_t)n_out[b];
             out.push_back(std::move(r));
         }
