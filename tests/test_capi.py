@@ -65,3 +65,19 @@ def test_default_options():
     assert o.max_batch == 1 and o.tp_size == 1 and o.use_graph == 1 and o.kv_dtype == -1 and o.page_size == 64
     # tensor parallel: peer-memory all-reduce kernel by default, fused sums opt-in
     assert o.use_p2p == 1 and o.fuse_allreduce == 0 and o.use_pdl == 1 and o.use_fused == 0
+
+
+@pytest.mark.parametrize("change,code", [
+    (dict(n_kv_heads=3), -9),                  # query heads not a multiple of KV heads
+    (dict(n_layers=0), -1), (dict(vocab=-5), -1), (dict(d_model=0), -1),
+    (dict(head_dim=63), -9),                   # head_dim 64 or 128
+    (dict(wdtype=77), -9),                     # not a weight type
+    (dict(wdtype=vsl.Q8_0, ffn=1370), -9),     # quantized rows need K % 32 == 0
+])
+def test_invalid_model_configs_refused_before_device_work(change, code):
+    cfg = dict(n_layers=2, d_model=512, n_heads=8, n_kv_heads=2, head_dim=64, ffn=1376, vocab=4096,
+               rope_theta=10000.0, rms_eps=1e-5, wdtype=vsl.F16)
+    cfg.update(change)
+    with pytest.raises(vsl.VslError) as e:
+        vsl.Engine.synthetic(cfg, seed=0, device=0, max_seq=128)
+    assert e.value.code == code, str(e.value)
