@@ -239,12 +239,12 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
     torch.cuda.empty_cache()
     if quant:
         qn = {vsl.Q8_0: "Q8_0", vsl.Q4_0: "Q4_0", vsl.Q4_1: "Q4_1"}[dt]
-        return {"bound": "hbm", "kernel": f"gemv_q_kernel<{qn},1,EK_SWIGLU,NORM> "
+        return {"bound": "hbm", "kernel": f"vsl_gemv_q_kernel<{qn},1,EK_SWIGLU,NORM> "
                                           "(gate/up + SwiGLU, fused RMSNorm)",
                 "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch,
                 "us_per_launch": round(ms * 1e3, 3), "traffic": None}
-    return {"bound": "hbm", "kernel": "gemv_kernel<__half,1,EK_SWIGLU,NORM> (gate/up + SwiGLU, fused RMSNorm)",
+    return {"bound": "hbm", "kernel": "vsl_gemv_kernel<__half,1,EK_SWIGLU,NORM> (gate/up + SwiGLU, fused RMSNorm)",
             "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms * 1e3, 3),
             "traffic": profiled_traffic() if tp == 1 else None,

@@ -77,7 +77,7 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 template <int HD, typename KT>
-__global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(FdParams p) {
+__global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int RE = fd_row_elems<HD, KT>();
     constexpr int VEC = KvVec<KT>::VEC;
@@ -369,7 +369,7 @@ static size_t fd_counters_offset(int B, int n_kv, size_t workspace_bytes) {
 
 template <int HD, typename KT>
 static int launch_fd(const FdParams& p, cudaStream_t st) {
-    auto kern = flash_decode_kernel<HD, KT>;
+    auto kern = vsl_flash_decode_kernel<HD, KT>;
     constexpr size_t smem = fd_smem_bytes<HD, KT>();
     static thread_local int configured_dev = -1;
     int dev = 0;

@@ -1,6 +1,6 @@
 // Long-context decode attention on tcgen05 tensor cores.
 //
-// Same semantics as flash_decode_kernel (attention.cu; reference attention.comp:84-189): query
+// Same semantics as vsl_flash_decode_kernel (attention.cu; reference attention.comp:84-189): query
 // head h reads KV group h*n_kv/n_heads, scores q.k / sqrt(head_dim), max-subtracted softmax over
 // positions [0, pos], output = probabilities times V. Built for caches of thousands of positions
 // (fp16 KV, head_dim 128, up to 8 query heads per KV group). Per 128-position chunk:
@@ -139,7 +139,7 @@ __device__ __forceinline__ void ft_next(const FtWork& w, int n_kv, FtCur& c) {
 }
 
 __global__ void __launch_bounds__(FT_THREADS, 1)
-    flash_decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+    vsl_flash_decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                            const __grid_constant__ FtArgs a) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[FT_STAGES], empty[FT_STAGES], s_full[2], s_free[2], q_ready;
@@ -659,12 +659,12 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(flash_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(vsl_flash_decode_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)FT_SMEM);
         if (e != cudaSuccess) return launch_status(e, "flash_decode_tc smem attribute");
         configured_dev = dev;
     }
-    return launch_status(launch_k(flash_decode_tc_kernel, dim3(grid), dim3(FT_THREADS), FT_SMEM, st, mk, mv, a),
+    return launch_status(launch_k(vsl_flash_decode_tc_kernel, dim3(grid), dim3(FT_THREADS), FT_SMEM, st, mk, mv, a),
                          "flash_decode_tc launch");
 }
 

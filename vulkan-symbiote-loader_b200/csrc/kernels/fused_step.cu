@@ -115,7 +115,7 @@ __device__ __forceinline__ bool fs_wait(uint64_t* bar, uint32_t par, const int* 
 // the kernel
 // ---------------------------------------------------------------------------------------
 template <typename WT, typename KT, int HD>
-__global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(const __grid_constant__ FsProgram P) {
+__global__ void __launch_bounds__(FS_THREADS, 1) vsl_fused_step_kernel(const __grid_constant__ FsProgram P) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + FS_STAGES;
@@ -702,7 +702,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) fused_step_kernel(const __grid_
 // ---------------------------------------------------------------------------------------
 template <typename WT, typename KT, int HD>
 static int launch_fs(const FsProgram& prog, int grid, cudaStream_t st) {
-    auto kern = fused_step_kernel<WT, KT, HD>;
+    auto kern = vsl_fused_step_kernel<WT, KT, HD>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);

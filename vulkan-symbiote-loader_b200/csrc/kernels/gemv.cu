@@ -31,7 +31,7 @@ constexpr int GEMV_L2_HEAD = 96 * 1024;
 constexpr int AR_ROWS = 128;  // output rows a producer CTA stages for the peers (reduce on read)
 
 template <typename WT, int NB, int EK, bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvParams p) {
     extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations (+ [NB][AR_ROWS] producer rows)
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = WTraits<WT>::VEC;
@@ -374,7 +374,7 @@ __host__ __device__ constexpr int q_stage_floats(int K) {
 }
 
 template <int QT, int NB, int EK, bool NORM>
-__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_q_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_q_kernel(const GemvParams p) {
     extern __shared__ __align__(16) float xs[];  // [NB][q_stage_floats(K)]
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = QTraits<QT>::VEC;
@@ -571,7 +571,7 @@ static int max_rows_per_launch(int wdtype, int K) {
 
 template <typename WT, int NB, int EK, bool NORM>
 static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
-    auto kern = gemv_kernel<WT, NB, EK, NORM>;
+    auto kern = vsl_gemv_kernel<WT, NB, EK, NORM>;
     const size_t smem = (size_t)NB * (p.K + (p.ar_mode == 1 ? AR_ROWS : 0)) * sizeof(float);
     static thread_local int configured_dev = -1;
     static thread_local size_t configured_smem = 0;
@@ -603,7 +603,7 @@ static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
 
 template <int QT, int NB, int EK, bool NORM>
 static int launch_gemv_q_t(const GemvParams& p, cudaStream_t st) {
-    auto kern = gemv_q_kernel<QT, NB, EK, NORM>;
+    auto kern = vsl_gemv_q_kernel<QT, NB, EK, NORM>;
     const size_t smem = (size_t)NB * q_stage_floats<QT>(p.K) * sizeof(float);
     static thread_local int configured_dev = -1;
     static thread_local size_t configured_smem = 0;

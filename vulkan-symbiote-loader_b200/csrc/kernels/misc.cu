@@ -34,7 +34,7 @@ int sm_count() {
 // embedding gather: x[b][j] = E[min(id, V-1)][j] (embedding_lookup.comp:29-40)
 // ---------------------------------------------------------------------------------------
 template <typename WT>
-__global__ void embed_kernel(const WT* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
+__global__ void vsl_embed_kernel(const WT* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
                              float* __restrict__ x, unsigned long long* slots) {
     pdl_wait();
     pdl_launch_dependents();
@@ -51,7 +51,7 @@ __global__ void embed_kernel(const WT* __restrict__ table, int V, int d, const i
 // quant(j) * d(j / 32) in fp32 (Q4_1: then + m(j / 32) in fp32), the reference's
 // dequantisation (GGUFLoader.cpp:1150-1207).
 template <int QT>
-__global__ void embed_q_kernel(const unsigned char* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
+__global__ void vsl_embed_q_kernel(const unsigned char* __restrict__ table, int V, int d, const int32_t* __restrict__ ids,
                                float* __restrict__ x, unsigned long long* slots) {
     pdl_wait();
     pdl_launch_dependents();
@@ -85,25 +85,25 @@ int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, i
     if (is_quant(dtype) && d % QBLK) return set_error(VSL_ERR_INVALID, "embed: quantized rows need d %% 32 == 0");
     switch (dtype) {
         case VSL_Q8_0:
-            return launch_status(launch_k(embed_q_kernel<VSL_Q8_0>, grid, block, 0, st, (const unsigned char*)table, V,
+            return launch_status(launch_k(vsl_embed_q_kernel<VSL_Q8_0>, grid, block, 0, st, (const unsigned char*)table, V,
                                           d, ids, x, slots),
                                  "embed");
         case VSL_Q4_0:
-            return launch_status(launch_k(embed_q_kernel<VSL_Q4_0>, grid, block, 0, st, (const unsigned char*)table, V,
+            return launch_status(launch_k(vsl_embed_q_kernel<VSL_Q4_0>, grid, block, 0, st, (const unsigned char*)table, V,
                                           d, ids, x, slots),
                                  "embed");
         case VSL_Q4_1:
-            return launch_status(launch_k(embed_q_kernel<VSL_Q4_1>, grid, block, 0, st, (const unsigned char*)table, V,
+            return launch_status(launch_k(vsl_embed_q_kernel<VSL_Q4_1>, grid, block, 0, st, (const unsigned char*)table, V,
                                           d, ids, x, slots),
                                  "embed");
         case VSL_F32:
-            return launch_status(launch_k(embed_kernel<float>, grid, block, 0, st, (const float*)table, V, d, ids, x, slots),
+            return launch_status(launch_k(vsl_embed_kernel<float>, grid, block, 0, st, (const float*)table, V, d, ids, x, slots),
                                  "embed");
         case VSL_F16:
             return launch_status(
-                launch_k(embed_kernel<__half>, grid, block, 0, st, (const __half*)table, V, d, ids, x, slots), "embed");
+                launch_k(vsl_embed_kernel<__half>, grid, block, 0, st, (const __half*)table, V, d, ids, x, slots), "embed");
         case VSL_BF16:
-            return launch_status(launch_k(embed_kernel<__nv_bfloat16>, grid, block, 0, st,
+            return launch_status(launch_k(vsl_embed_kernel<__nv_bfloat16>, grid, block, 0, st,
                                           (const __nv_bfloat16*)table, V, d, ids, x, slots),
                                  "embed");
         default: return set_error(VSL_ERR_UNSUPPORTED, "embed: dtype %d", dtype);
@@ -113,7 +113,7 @@ int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, i
 // ---------------------------------------------------------------------------------------
 // RMSNorm (rms_norm.comp:24-34): one CTA per row
 // ---------------------------------------------------------------------------------------
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int d, float eps,
+__global__ void vsl_rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int d, float eps,
                                float* __restrict__ y) {
     __shared__ float red[32];
     pdl_wait();
@@ -134,7 +134,7 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // ---------------------------------------------------------------------------------------
 // argmax over fp32 rows (first maximum), one CTA per row
 // ---------------------------------------------------------------------------------------
-__global__ void argmax_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ out) {
+__global__ void vsl_argmax_kernel(const float* __restrict__ logits, int V, int32_t* __restrict__ out) {
     __shared__ unsigned long long red[32];
     pdl_wait();
     pdl_launch_dependents();
@@ -166,7 +166,7 @@ __device__ __forceinline__ unsigned long long smix(unsigned long long z) {
 }
 
 template <typename T>
-__global__ void synth_kernel(T* __restrict__ out, unsigned long long base, unsigned long long start,
+__global__ void vsl_synth_kernel(T* __restrict__ out, unsigned long long base, unsigned long long start,
                              unsigned long long n, float c) {
     for (unsigned long long j = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; j < n;
          j += (unsigned long long)gridDim.x * blockDim.x) {
@@ -198,10 +198,10 @@ int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start
     dim3 grid((unsigned)blocks), block(256);
     cudaError_t e;
     switch (dtype) {
-        case VSL_F32: e = launch_k(synth_kernel<float>, grid, block, 0, st, (float*)dst, base, start, n, c); break;
-        case VSL_F16: e = launch_k(synth_kernel<__half>, grid, block, 0, st, (__half*)dst, base, start, n, c); break;
+        case VSL_F32: e = launch_k(vsl_synth_kernel<float>, grid, block, 0, st, (float*)dst, base, start, n, c); break;
+        case VSL_F16: e = launch_k(vsl_synth_kernel<__half>, grid, block, 0, st, (__half*)dst, base, start, n, c); break;
         case VSL_BF16:
-            e = launch_k(synth_kernel<__nv_bfloat16>, grid, block, 0, st, (__nv_bfloat16*)dst, base, start, n, c);
+            e = launch_k(vsl_synth_kernel<__nv_bfloat16>, grid, block, 0, st, (__nv_bfloat16*)dst, base, start, n, c);
             break;
         default: return set_error(VSL_ERR_UNSUPPORTED, "synth_fill: dtype %d", dtype);
     }
@@ -212,7 +212,7 @@ int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start
 // (row0 + i) * src_cols + col0 + j, written to dst[i * dst_ld + j] (tensor-parallel shards
 // and the interleaved gate/up layout are generated in place).
 template <typename T>
-__global__ void synth2d_kernel(T* __restrict__ dst, size_t dst_ld, unsigned long long base, size_t row0,
+__global__ void vsl_synth2d_kernel(T* __restrict__ dst, size_t dst_ld, unsigned long long base, size_t row0,
                                size_t nrows, size_t src_cols, size_t col0, size_t ncols, float c) {
     const size_t total = nrows * ncols;
     for (size_t j = (size_t)blockIdx.x * blockDim.x + threadIdx.x; j < total; j += (size_t)gridDim.x * blockDim.x) {
@@ -235,7 +235,7 @@ __global__ void synth2d_kernel(T* __restrict__ dst, size_t dst_ld, unsigned long
 // gb = row * (src_cols / 32) + col / 32 the scale d = fp16(m * c), m = 49152 + (h'(gb) & 0x7fff),
 // h' from a second stream of the same tensor; a Q4_1 block's minimum is fp16(-7.5 * d).
 template <int QT>
-__global__ void synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, unsigned long long base,
+__global__ void vsl_synthq_kernel(unsigned char* __restrict__ dst, size_t dst_ld, unsigned long long base,
                               unsigned long long sbase, size_t row0, size_t nrows, size_t src_cols, size_t col0,
                               size_t ncols, float c) {
     const size_t qb = quant_bytes(QT, ncols), nblk = ncols / QBLK;
@@ -295,12 +295,12 @@ int synthq2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t t
     const float c = synthq_scale_c(dtype, sigma);
     dim3 grid((unsigned)(sm_count() * 16)), block(256);
     cudaError_t e = dtype == VSL_Q8_0
-                        ? launch_k(synthq_kernel<VSL_Q8_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                        ? launch_k(vsl_synthq_kernel<VSL_Q8_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
                                    row0, nrows, src_cols, col0, ncols, c)
                     : dtype == VSL_Q4_1
-                        ? launch_k(synthq_kernel<VSL_Q4_1>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                        ? launch_k(vsl_synthq_kernel<VSL_Q4_1>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
                                    row0, nrows, src_cols, col0, ncols, c)
-                        : launch_k(synthq_kernel<VSL_Q4_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
+                        : launch_k(vsl_synthq_kernel<VSL_Q4_0>, grid, block, 0, st, (unsigned char*)dst, dst_ld, base, sbase,
                                    row0, nrows, src_cols, col0, ncols, c);
     return launch_status(e, "synthq2d");
 }
@@ -316,15 +316,15 @@ int synth2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t ti
     cudaError_t e;
     switch (dtype) {
         case VSL_F32:
-            e = launch_k(synth2d_kernel<float>, grid, block, 0, st, (float*)dst, dst_ld, base, row0, nrows, src_cols,
+            e = launch_k(vsl_synth2d_kernel<float>, grid, block, 0, st, (float*)dst, dst_ld, base, row0, nrows, src_cols,
                          col0, ncols, c);
             break;
         case VSL_F16:
-            e = launch_k(synth2d_kernel<__half>, grid, block, 0, st, (__half*)dst, dst_ld, base, row0, nrows, src_cols,
+            e = launch_k(vsl_synth2d_kernel<__half>, grid, block, 0, st, (__half*)dst, dst_ld, base, row0, nrows, src_cols,
                          col0, ncols, c);
             break;
         case VSL_BF16:
-            e = launch_k(synth2d_kernel<__nv_bfloat16>, grid, block, 0, st, (__nv_bfloat16*)dst, dst_ld, base, row0,
+            e = launch_k(vsl_synth2d_kernel<__nv_bfloat16>, grid, block, 0, st, (__nv_bfloat16*)dst, dst_ld, base, row0,
                          nrows, src_cols, col0, ncols, c);
             break;
         default: return set_error(VSL_ERR_UNSUPPORTED, "synth2d: dtype %d", dtype);
@@ -336,7 +336,7 @@ int synth2d_impl(void* dst, int dtype, size_t dst_ld, uint64_t seed, uint64_t ti
 // end of a decode step: sampled id from the argmax slot, next input id (forced or
 // sampled), token log, position advance and step counter
 // ---------------------------------------------------------------------------------------
-__global__ void finalize_kernel(const unsigned long long* __restrict__ slots, int B, int32_t* ids, int32_t* pos,
+__global__ void vsl_finalize_kernel(const unsigned long long* __restrict__ slots, int B, int32_t* ids, int32_t* pos,
                                 int32_t* step_counter, const int32_t* __restrict__ forced, const int32_t* n_forced,
                                 int32_t* log, int log_cap, int32_t* sampled_out, int max_pos, int* status) {
     pdl_wait();
@@ -363,14 +363,14 @@ int finalize_impl(const unsigned long long* slots, int B, int32_t* ids, int32_t*
                   const int32_t* forced, const int32_t* n_forced, int32_t* log, int log_cap, int32_t* sampled_out,
                   int max_pos, int* status, cudaStream_t st) {
     if (B > 1024) return set_error(VSL_ERR_UNSUPPORTED, "finalize: batch %d > 1024", B);
-    return launch_status(launch_k(finalize_kernel, dim3(1), dim3(B < 32 ? 32 : ((B + 31) / 32) * 32), 0, st, slots, B,
+    return launch_status(launch_k(vsl_finalize_kernel, dim3(1), dim3(B < 32 ? 32 : ((B + 31) / 32) * 32), 0, st, slots, B,
                                   ids, pos, step_counter, forced, n_forced, log, log_cap, sampled_out, max_pos, status),
                          "finalize");
 }
 
 // End of a prefill: sequence `seq` continues from position new_pos with the token sampled from
 // the prompt's last logits (the argmax key in `slot`).
-__global__ void prefill_finish_kernel(const unsigned long long* __restrict__ slot, int32_t* ids, int32_t* pos, int seq,
+__global__ void vsl_prefill_finish_kernel(const unsigned long long* __restrict__ slot, int32_t* ids, int32_t* pos, int seq,
                                       int new_pos, int32_t* next_out) {
     pdl_wait();
     pdl_launch_dependents();
@@ -385,7 +385,7 @@ __global__ void prefill_finish_kernel(const unsigned long long* __restrict__ slo
 
 int prefill_finish_impl(const unsigned long long* slot, int32_t* ids, int32_t* pos, int seq, int new_pos,
                         int32_t* next_out, cudaStream_t st) {
-    return launch_status(launch_k(prefill_finish_kernel, dim3(1), dim3(32), 0, st, slot, ids, pos, seq, new_pos, next_out),
+    return launch_status(launch_k(vsl_prefill_finish_kernel, dim3(1), dim3(32), 0, st, slot, ids, pos, seq, new_pos, next_out),
                          "prefill finish");
 }
 
@@ -400,13 +400,13 @@ extern "C" int vsl_embed_gather(int dtype, const void* table, int V, int d, cons
 
 extern "C" int vsl_rmsnorm(const float* x, const float* w, int B, int d, float eps, float* y, void* stream) {
     if (!x || !w || !y || B <= 0 || d <= 0) return set_error(VSL_ERR_INVALID, "rmsnorm: bad arguments");
-    return launch_status(launch_k(rmsnorm_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, x, w, d, eps, y),
+    return launch_status(launch_k(vsl_rmsnorm_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, x, w, d, eps, y),
                          "rmsnorm");
 }
 
 extern "C" int vsl_argmax(const float* logits, int B, int V, int32_t* out_ids, void* stream) {
     if (!logits || !out_ids || B <= 0 || V <= 0) return set_error(VSL_ERR_INVALID, "argmax: bad arguments");
-    return launch_status(launch_k(argmax_kernel, dim3(B), dim3(512), 0, (cudaStream_t)stream, logits, V, out_ids),
+    return launch_status(launch_k(vsl_argmax_kernel, dim3(B), dim3(512), 0, (cudaStream_t)stream, logits, V, out_ids),
                          "argmax");
 }
 

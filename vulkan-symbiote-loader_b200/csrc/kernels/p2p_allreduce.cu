@@ -25,7 +25,7 @@ namespace vsl {
 constexpr int AR_THREADS = 1024;
 
 template <int OP>  // 0: fp32 sum, 1: u64 max
-__global__ void __launch_bounds__(AR_THREADS, 1) p2p_allreduce_kernel(void* data, int n, const P2pPeers peers) {
+__global__ void __launch_bounds__(AR_THREADS, 1) vsl_p2p_allreduce_kernel(void* data, int n, const P2pPeers peers) {
     __shared__ unsigned long long s_epoch;
     __shared__ int s_ok;
     pdl_wait();
@@ -121,8 +121,8 @@ int p2p_allreduce(const P2pPeers& peers, void* data, int n, int op, cudaStream_t
     if ((uintptr_t)data & 15) return set_error(VSL_ERR_INVALID, "p2p_allreduce: message must be 16-byte aligned");
     if (peers.slot_bytes % 256 || peers.slot_bytes < (size_t)n * (op == 0 ? 4 : 8))
         return set_error(VSL_ERR_INVALID, "p2p_allreduce: slot stride %zu", peers.slot_bytes);
-    cudaError_t e = op == 0 ? launch_k(p2p_allreduce_kernel<0>, dim3(1), dim3(AR_THREADS), 0, st, data, n, peers)
-                            : launch_k(p2p_allreduce_kernel<1>, dim3(1), dim3(AR_THREADS), 0, st, data, n, peers);
+    cudaError_t e = op == 0 ? launch_k(vsl_p2p_allreduce_kernel<0>, dim3(1), dim3(AR_THREADS), 0, st, data, n, peers)
+                            : launch_k(vsl_p2p_allreduce_kernel<1>, dim3(1), dim3(AR_THREADS), 0, st, data, n, peers);
     return launch_status(e, "p2p allreduce launch");
 }
 

@@ -150,7 +150,7 @@ __device__ __forceinline__ bool next_segment(const TcArgs& a, long long& f, long
 // activation split: X2[b] = rn(xn), X2[Bp + b] = rn(xn - X2[b]), xn = RMSNorm(x[b]) or x[b]
 // ---------------------------------------------------------------------------------------
 template <typename WT>
-__global__ void __launch_bounds__(256) xsplit_kernel(const float* __restrict__ x, int K, const float* __restrict__ nw,
+__global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict__ x, int K, const float* __restrict__ nw,
                                                      float eps, int Bp, WT* __restrict__ x2) {
     __shared__ float red[8];
     const int b = blockIdx.x;
@@ -275,7 +275,7 @@ __device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, int G, int rt, in
 
 template <int EK>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+    vsl_tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ TcArgs a) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[TC_MAX_STAGES], empty[TC_MAX_STAGES];
@@ -602,7 +602,7 @@ bool tc_supported(int wdtype, int N, int K, int B) {
 template <int EK>
 static int launch_tc(const TcArgs& a, const CUtensorMap& mw, const CUtensorMap& mx, int grid, size_t smem,
                      cudaStream_t st) {
-    auto kern = tc_gemm_kernel<EK>;
+    auto kern = vsl_tc_gemm_kernel<EK>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -680,10 +680,10 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     // activation split (+ RMSNorm)
     cudaError_t e;
     if (wdtype == VSL_BF16)
-        e = launch_k(xsplit_kernel<__nv_bfloat16>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
+        e = launch_k(vsl_xsplit_kernel<__nv_bfloat16>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
                      static_cast<__nv_bfloat16*>(x2));
     else
-        e = launch_k(xsplit_kernel<__half>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
+        e = launch_k(vsl_xsplit_kernel<__half>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
                      static_cast<__half*>(x2));
     rc = launch_status(e, "tc activation split");
     if (rc) return rc;
