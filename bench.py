@@ -164,6 +164,69 @@ def cpu_baseline(cfg, seconds: float, threads: int | None = None):
                       f"(setup {setup:.1f}s excluded)"}
 
 
+def config_7b(args, ws, qname=None):
+    """The `config` object of the 7B lines (our arm and the reference arm print the same one)."""
+    return {"workload": f"7B Llama shape {qname or 'fp16'} (BASELINE configs[1]"
+                        f"{' with block-quantized weights' if qname else ''}), batch 1, "
+                        "128-token prompt (prefill), "
+                        f"decode positions {PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
+            "model": "llama-7b-shape" + (f"-{args.layers}L" if args.layers else ""),
+            "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps,
+            "parallelism": f"tp{ws}" if ws > 1 else "single",
+            "l2": "inputs larger than L2 (13.5 GB of weights streamed per step)"}
+
+
+TP_CHECK = os.path.join(ROOT, "tests", "golden", "tp_check_7b_2l.json")
+
+
+def tp_parity(np, vsl, vdist, dist, rank, ws, local):
+    """Before the timed region: the engine under the timed run's tensor parallelism, on the
+    benchmark's 7B shape cut to 2 layers, fed 8 ids teacher-forced, against the committed oracle
+    fixture of that model (tests/golden/tp_check_7b_2l.json: argmax ids, top-8 and 64 probe
+    logits per step) and, on rank 0 of a multi-GPU run, against a single-GPU engine of the same
+    model (all logits). Bars: ids identical, logits within 2e-2."""
+    with open(TP_CHECK) as f:
+        g = json.load(f)
+    cfg = {k: g[k] for k in ("n_layers", "d_model", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab",
+                             "rope_theta", "rms_eps", "wdtype")}
+    probe = np.asarray(g["probe_index"])
+
+    def run(**kw):
+        e = vsl.Engine.synthetic(cfg, seed=g["seed"], sigma=g["sigma"], device=local, max_seq=g["max_seq"], **kw)
+        lgs, ids = [], []
+        for t in g["ids"]:
+            o, lg = e.step_host(np.array([t], np.int32), want_logits=True)
+            lgs.append(lg[0])
+            ids.append(int(o[0]))
+        status = e.device_status()
+        e.close()
+        return np.stack(lgs), ids, status
+
+    nid = vdist.nccl_id(dist)
+    lg, ids, status = run(tp_rank=rank, tp_size=ws, nccl_id=nid)
+    if dist:
+        dist.barrier()
+    if rank != 0:
+        return None
+    worst = 0.0
+    for k, st in enumerate(g["steps"]):
+        for i, v in st["top8"]:
+            worst = max(worst, abs(float(lg[k, i]) - v))
+        worst = max(worst, float(np.abs(lg[k, probe] - np.asarray(st["probe"])).max()))
+    want = [st["argmax"] for st in g["steps"]]
+    out = {"tp": ws, "layers": cfg["n_layers"], "steps": len(ids), "tol": 0.02,
+           "vs_oracle_fixture": {"max_abs": round(worst, 6), "ids_equal": ids == want},
+           "device_status": status}
+    ok = status == 0 and worst <= 0.02 and ids == want
+    if ws > 1:
+        lg1, ids1, st1 = run()
+        d1 = float(np.abs(lg - lg1).max())
+        out["vs_single_gpu"] = {"max_abs": round(d1, 6), "ids_equal": ids == ids1}
+        ok = ok and st1 == 0 and d1 <= 0.02 and ids == ids1
+    out["ok"] = bool(ok)
+    return out
+
+
 def run_reference(args):
     from vsl import dist as vdist
     ws, rank, _ = vdist.env()
@@ -181,8 +244,7 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / cb["value"], 3), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded random-init weights)",
-            "config": {"workload": "7B Llama shape fp16, batch 1, 128-token prompt then decode",
-                       "model": "llama-7b-shape", "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps},
+            "config": config_7b(args, args.gpus),
             "impl": "reference", "cpu_baseline": cb,
             "e2e": {"value": round(cb["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -276,6 +338,7 @@ def run_ours(args):
     start = PREFILL_8B if big else PREFILL_70B if w70 else PROMPT
     max_seq = start + args.warmup + 2 * args.steps + 8
     max_seq = (max_seq + 63) // 64 * 64
+    parity = tp_parity(np, vsl, vdist, dist, rank, ws, local) if not (big or w70 or qname) else None
     nccl_id = vdist.nccl_id(dist)
     t0 = time.perf_counter()
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=B, max_seq=max_seq,
@@ -371,7 +434,8 @@ def run_ours(args):
                        "parallelism": f"tp{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (15 GB weights + 17 GB KV per step)"},
             "e2e": {"value": round(n_e2e * B / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
-                    "d2h_bytes_per_step": 4 * B, "api": "vsl_engine_step_host"},
+                    "d2h_bytes_per_step": 4 * (B + 1), "api": "vsl_engine_step_host",
+                    "d2h": "sampled ids + device status word"},
             "roofline": step_roof,
             "gpu_launches": kernels * args.steps, "kernels_per_step": kernels,
             "clocks": clk.summary(), "load_seconds": round(load_s, 2),
@@ -389,8 +453,8 @@ def run_ours(args):
                        "global_batch": 1, "seq_len": PREFILL_70B + args.warmup + args.steps,
                        "parallelism": f"tp{ws}" if ws > 1 else "single",
                        "l2": "inputs larger than L2 (140 GB of weights over the ranks per step)"},
-            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "api": "vsl_engine_step_host"},
+            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8,
+                    "api": "vsl_engine_step_host", "d2h": "sampled id + device status word"},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (this rank's weights + KV)",
                          "achieved": round(step_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(step_gbs / hbm_peak, 4), "peak_kind": peak_kind,
@@ -409,16 +473,9 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": qname.lower() + " weights, f32 math" if qname else "f16",
             "data": "synthetic (seeded random-init weights filled in HBM)",
-            "config": {"workload": f"7B Llama shape {qname or 'fp16'} (BASELINE configs[1]"
-                                   f"{' with block-quantized weights' if qname else ''}), batch 1, "
-                                   "128-token prompt (prefill), "
-                                   f"decode positions {PROMPT + args.warmup}..{PROMPT + args.warmup + args.steps - 1}",
-                       "model": "llama-7b-shape" + (f"-{cfg['n_layers']}L" if args.layers else ""),
-                       "global_batch": 1, "seq_len": PROMPT + args.warmup + args.steps,
-                       "parallelism": f"tp{ws}" if ws > 1 else "single",
-                       "l2": "inputs larger than L2 (13.5 GB of weights streamed per step)"},
-            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4,
-                    "api": "vsl_engine_step_host"},
+            "config": config_7b(args, ws, qname),
+            "e2e": {"value": round(n_e2e / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 8,
+                    "api": "vsl_engine_step_host", "d2h": "sampled id + device status word"},
             "roofline": roof,
             "step_roofline": {"bytes_per_step_per_gpu": round(step_bytes), "achieved": round(step_gbs, 1),
                               "peak": hbm_peak, "unit": "GB/s", "frac": round(step_gbs / hbm_peak, 4),
@@ -431,6 +488,8 @@ def run_ours(args):
         }
         if cb:
             line["cpu_baseline"] = cb
+        if parity is not None:
+            line["tp_parity"] = parity
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
@@ -509,7 +568,7 @@ def run_stream70(args):
                    "model": "llama-70b-shape", "global_batch": 1, "seq_len": PREFILL_70B + args.warmup + args.steps,
                    "parallelism": "single", "l2": "inputs larger than L2"},
         "e2e": {"value": round(args.steps / e2e_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 4,
-                "d2h_bytes_per_step": 4, "api": "vsl_engine_step_host"},
+                "d2h_bytes_per_step": 8, "api": "vsl_engine_step_host", "d2h": "sampled id + device status word"},
         "roofline": {"bound": "host link", "kernel": "streamed layer copies (pinned host -> HBM slot)",
                      "achieved": round(streamed / step_s / 1e9, 1), "peak": round(link, 1), "unit": "GB/s",
                      "frac": round(streamed / step_s / 1e9 / link, 4), "peak_kind": "measured pinned H2D copy (1 GiB)",

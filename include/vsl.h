@@ -157,7 +157,9 @@ VSL_API int vsl_flash_decode_tc(const float* q, const void* k_cache, const void*
  * with that device current, so make that first call before any stream capture. Every
  * call shares the one array: calls that can overlap on the GPU (different streams, or
  * different host threads on the same device) race and must be serialised by the caller.
- * Each call clears the split counters it needs before launching. */
+ * Each call clears the split counters it needs before launching. The looked-up address is kept
+ * per device for the rest of the process: a cudaDeviceReset on that device ends the context the
+ * address belongs to, so after one this entry point must not be called again in that process. */
 VSL_API int vsl_flash_decode_noalloc(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                                      const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
                                      int B, int n_heads, int n_kv, int head_dim, int max_len, int split_len,
@@ -182,6 +184,23 @@ VSL_API int vsl_argmax(const float* logits, int B, int V, int32_t* out_ids, void
  * Bit-identical to the host generator used to write GGUF fixtures. */
 VSL_API int vsl_synth_fill(void* dst, int dtype, uint64_t seed, uint64_t tensor_id, uint64_t start, uint64_t n,
                    double sigma, void* stream);
+
+/* One-shot peer-memory all-reduce of the tensor-parallel engine (it stands where an NCCL
+ * all-reduce would follow each row-parallel projection; the reference has no multi-GPU path).
+ * Each rank owns a receive buffer of vsl_p2p_buffer_size(n_ranks, cap_bytes) bytes, 256-byte
+ * aligned and zero-filled once; bases[r] is rank r's buffer as this rank addresses it (its own
+ * buffer, or a CUDA IPC / peer mapping of another GPU's). op 0 sums n fp32 values, op 1 takes the
+ * maximum of n uint64 keys, in place on `data` (16-byte aligned, n * element size <= cap_bytes).
+ * The message is cut into chunks of at least 1 KB, one CTA each: a CTA stores its chunk into every
+ * rank's buffer, raises a flag there, waits up to wait_ns nanoseconds for every rank's flag in its
+ * own buffer and sums the chunk's slots in rank order, so all ranks get identical bits. epochs is
+ * a zero-filled device array of 64 uint64 call counters (one per chunk) that every call advances,
+ * also one that timed out; status (device int, may be NULL) receives VSL_ERR_TIMEOUT when a
+ * peer's flag never arrived, and the data are then left partly unreduced. Every rank makes the
+ * same sequence of calls with the same n; one launch on `stream`. */
+VSL_API int vsl_p2p_buffer_size(int n_ranks, size_t cap_bytes, size_t* bytes);
+VSL_API int vsl_p2p_allreduce(void* const* bases, int n_ranks, int rank, size_t cap_bytes, void* data, int n, int op,
+                              uint64_t* epochs, int* status, uint64_t wait_ns, void* stream);
 
 /* ======================================================================================
  * Engine (replaces VulkanSymbioteEngine's decode loop, VulkanSymbioteEngine.cpp:678-765)
@@ -221,13 +240,14 @@ typedef struct {
                           replayed as a CUDA graph with programmatic dependent launch  */
     int use_p2p;       /* tensor parallel: 1 (default) = one-shot NVLink peer-memory all-reduces
                           (CUDA IPC buffers, one kernel per reduction); 0 = NCCL            */
-    int fuse_allreduce; /* tensor parallel with use_p2p: 1 = the residual sums ride on the
-                          projections (row-parallel GEMV pushes its rows to every rank, the next
-                          projection sums them while staging); 0 (default) = separate all-reduce
-                          kernel (the fused sums measured slower at TP 2, 7B fp16 batch 1) */
     int legacy_q4;     /* 1 = read GGUF Q4_0 / Q4_1 nibbles in the reference loader's order
                           (GGUFLoader.cpp:1146-1160: element 2i low, 2i+1 high nibble of
                           byte i); 0 (default) = ggml's order (element i low, i+16 high)  */
+    int nccl_timeout_ms; /* tensor parallel: the longest the host waits for work that involves the
+                          other ranks (one call's stream work); past it, or when NCCL reports an
+                          asynchronous error, the communicator is aborted, the call returns
+                          VSL_ERR_TIMEOUT / VSL_ERR_NCCL and the engine refuses further work with
+                          VSL_ERR_STATE (recreate it). 0 = 120000 (two minutes)               */
 } vsl_engine_options;
 
 VSL_API void vsl_engine_default_options(vsl_engine_options* opt);
@@ -380,6 +400,13 @@ VSL_API int vsl_engine_read_trace(vsl_engine* e, int cap, uint64_t* out_ns, int*
 /* Sticky device status word of the engine (0 = OK; VSL_ERR_TIMEOUT / VSL_ERR_BOUNDS set by
  * kernels that gave up on a bounded wait or rejected an index). */
 VSL_API int vsl_engine_device_status(vsl_engine* e, int* status);
+
+/* Failure injection for tests (failures are made on the host, never by faulting a GPU): set
+ * the sticky device status word to `code` (VSL_OK or a VSL_ERR_*) as a kernel that gave up on a
+ * bounded wait or rejected an index would. The next host-facing call that reads the word
+ * (vsl_engine_step_host, vsl_engine_prefill, vsl_engine_generate, vsl_engine_generate_batch after
+ * their decode steps) returns it as its error; vsl_engine_reset clears it. */
+VSL_API int vsl_engine_inject_status(vsl_engine* e, int code);
 
 #ifdef __cplusplus
 }

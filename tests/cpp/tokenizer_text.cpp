@@ -37,6 +37,13 @@ int main() {
     report("spm_prompt", spm->decode(ctx), "the quick");
     report("spm_continuation", spm->decode_continuation(ctx, {fox, the}), " fox the");
     report("spm_no_context", spm->decode_continuation({}, {fox, the}), "fox the");
+    // the prompt ends with the first two byte tokens of a U+2581 mark (E2 96); the continuation
+    // brings its last byte (81) and 'x': the new text is the space and the x
+    report("spm_split_mark", spm->decode_continuation({1, the, 3 + 0xE2, 3 + 0x96}, {3 + 0x81, 3 + 'x'}), " x");
+    // the prompt ends inside a two-byte character (C3 of U+00E9): the prompt's text keeps the
+    // lead byte, so the continuation starts with the trailing byte (their concatenation is the
+    // full text)
+    report("spm_split_char", spm->decode_continuation({1, the, 3 + 0xC3}, {3 + 0xA9, fox}), "\xA9 fox");
     // byte-level BPE: the continuation is the bytes of its tokens
     std::vector<std::string> toks;
     std::vector<int32_t> btypes;

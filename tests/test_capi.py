@@ -63,8 +63,8 @@ def test_engine_config_validation_without_device():
 def test_default_options():
     o = vsl.default_options()
     assert o.max_batch == 1 and o.tp_size == 1 and o.use_graph == 1 and o.kv_dtype == -1 and o.page_size == 64
-    # tensor parallel: peer-memory all-reduce kernel by default, fused sums opt-in
-    assert o.use_p2p == 1 and o.fuse_allreduce == 0 and o.use_pdl == 1 and o.use_fused == 0
+    # tensor parallel: peer-memory all-reduce kernel by default; a bounded host wait on the ranks
+    assert o.use_p2p == 1 and o.use_pdl == 1 and o.use_fused == 0 and o.nccl_timeout_ms == 120000
 
 
 @pytest.mark.parametrize("change,code", [

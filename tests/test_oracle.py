@@ -170,3 +170,23 @@ def test_oracle_batch_rows_independent():
     _, l1 = m1.step(np.array([5], np.int32), np.array([10], np.int32))
     assert np.array_equal(l1[0], lg[0])
     assert not np.array_equal(lg[0], lg[1])
+
+
+def test_tp_check_fixture_is_the_oracles():
+    """tests/golden/tp_check_7b_2l.json (what bench.py checks tensor-parallel engines against)
+    holds the oracle's ids and logits of its model."""
+    import json
+    import os
+    with open(os.path.join(os.path.dirname(__file__), "golden", "tp_check_7b_2l.json")) as f:
+        g = json.load(f)
+    m = O.Model.synthetic(n_layers=g["n_layers"], d=g["d_model"], n_heads=g["n_heads"], n_kv=g["n_kv_heads"],
+                          ffn=g["ffn"], vocab=g["vocab"], rope_theta=g["rope_theta"], eps=g["rms_eps"],
+                          wdtype=g["wdtype"], kvdtype=O.F16, max_seq=g["max_seq"], max_batch=1, seed=g["seed"],
+                          sigma=g["sigma"])
+    assert g["ids"] == O.synth_ids(g["seed"], 2, g["n_steps"], g["vocab"]).tolist()
+    for p, (t, st) in enumerate(zip(g["ids"], g["steps"])):
+        oid, lg = m.step([t], [p])
+        assert int(oid[0]) == st["argmax"]
+        assert np.abs(lg[0][g["probe_index"]] - np.asarray(st["probe"])).max() == 0.0
+        assert all(lg[0][i] == v for i, v in st["top8"])
+    m.close()

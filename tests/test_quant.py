@@ -57,6 +57,27 @@ def test_dequant_known_answers():
     assert legacy[0] == 1.0 and legacy[1] == 29.0 and (legacy[2:] == -1.0).all()
 
 
+def test_dequant_negative_subnormal_scale_keeps_its_sign():
+    """Block scales are IEEE fp16, read with their sign also when subnormal. The reference loader's
+    dequantisation helper returns +mantissa * 2^-24 for every subnormal half, dropping the sign
+    (vk_symbiote/src/GGUFLoader.cpp:1136-1137), so a block whose scale is a negative subnormal would
+    come out negated there; the engine and this oracle follow the format (the two agree on every
+    scale that is normal, zero or positive)."""
+    b8 = np.zeros(34, np.uint8)
+    b8[0], b8[1] = 0x03, 0x80  # fp16 0x8003 = -3 * 2^-24
+    b8[2:5] = np.array([2, -5, 127], np.int8).view(np.uint8)
+    v = O.dequant_blocks(O.Q8_0, b8, 32)
+    d = -3.0 * 2.0 ** -24
+    assert v[:3].tolist() == [2 * d, -5 * d, 127 * d] and not v[3:].any()
+    reference_reading = 3.0 * 2.0 ** -24  # what GGUFLoader.cpp:1137 would use as the scale
+    assert v[0] == -2 * reference_reading
+    # Q4_0 with a negative subnormal scale: element 0 = (1 - 8) * d > 0
+    b4 = np.full(18, 0x88, np.uint8)
+    b4[0], b4[1], b4[2] = 0x01, 0x80, 0x81  # fp16 0x8001 = -2^-24; byte 0: low nibble 1, high 8
+    v4 = O.dequant_blocks(O.Q4_0, b4, 32, 0)
+    assert v4[0] == 7.0 * 2.0 ** -24 and np.count_nonzero(v4) == 1
+
+
 @pytest.mark.parametrize("dtype", [O.Q8_0, O.Q4_0, O.Q4_1])
 def test_seeded_quantized_tensor_numpy_equals_c(dtype):
     rows, cols, seed, tid = 7, 160, 11, synth.tid_layer(1, synth.K_GATE)

@@ -42,12 +42,10 @@ def main():
     for name, c in cases.items():
         kw = dict(device=local, max_batch=c["batch"], max_seq=256)
         runs = {}
-        # sums fused into the projections over peer memory (twice: bit for bit), the separate
-        # peer-memory all-reduce kernel, and NCCL
-        for tag, p2p, fuse in (("p2p", 1, 1), ("p2p_again", 1, 1), ("p2p_sep", 1, 0), ("nccl", 0, 0)):
+        # the peer-memory all-reduce kernel (twice: bit for bit) and NCCL
+        for tag, p2p in (("p2p", 1), ("p2p_again", 1), ("nccl", 0)):
             nid = vdist.nccl_id(d)  # a unique id forms exactly one communicator: one per engine
-            e = vsl.Engine.synthetic(c["cfg"], seed=11, tp_rank=rank, tp_size=ws, nccl_id=nid, use_p2p=p2p,
-                                     fuse_allreduce=fuse, **kw)
+            e = vsl.Engine.synthetic(c["cfg"], seed=11, tp_rank=rank, tp_size=ws, nccl_id=nid, use_p2p=p2p, **kw)
             if c["prefill"]:
                 e.fill_kv_synthetic(3, 1.0, c["prefill"], c["batch"])
             lg_tp, ids_tp = run(e, c["cfg"], 6, c["batch"])
@@ -66,14 +64,13 @@ def main():
             e1.reset()
             pf_1 = e1.prefill(prompt, seq=c["batch"] - 1, want_logits=True)
             e1.close()
-            for tag in ("p2p", "p2p_sep", "nccl"):
+            for tag in ("p2p", "nccl"):
                 lg_tp, ids_tp, gen_tp, status, pf_tp = runs[tag]
                 result[f"{name}_{tag}"] = dict(max_abs=float(np.abs(lg_tp - lg_1).max()),
                                                ids_equal=bool((ids_tp == ids_1).all()), gen_equal=gen_tp == gen_1,
                                                status=status, pf_max_abs=float(np.abs(pf_tp[1] - pf_1[1]).max()),
                                                pf_next_equal=pf_tp[0] == pf_1[0])
             result[f"{name}_p2p_repeat_equal"] = bool(np.array_equal(runs["p2p"][0], runs["p2p_again"][0]))
-            result[f"{name}_fused_equals_separate"] = bool(np.array_equal(runs["p2p"][0], runs["p2p_sep"][0]))
         d.barrier()
     if rank == 0:
         with open(sys.argv[1], "w") as f:

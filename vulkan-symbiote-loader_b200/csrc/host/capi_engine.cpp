@@ -40,7 +40,7 @@ extern "C" void vsl_engine_default_options(vsl_engine_options* o) {
     o->use_fused = 0;
     o->use_p2p = 1;
     o->legacy_q4 = 0;
-    o->fuse_allreduce = 0;  // opt-in: the fused sums measured slower at TP 2 than the separate kernel
+    o->nccl_timeout_ms = 120000;
 }
 
 extern "C" int vsl_nccl_unique_id(void* out128) {
@@ -190,6 +190,14 @@ extern "C" int vsl_engine_device_status(vsl_engine* e, int* status) {
     if (int rc = check_engine(e)) return rc;
     if (!status) return set_error(VSL_ERR_INVALID, "device_status: null output");
     return e->impl->device_status(status);
+    GUARD_END
+}
+
+extern "C" int vsl_engine_inject_status(vsl_engine* e, int code) {
+    GUARD_BEGIN
+    if (int rc = check_engine(e)) return rc;
+    if (code > 0 || code < VSL_ERR_STATE) return set_error(VSL_ERR_INVALID, "inject_status: %d is not a status", code);
+    return e->impl->inject_status(code);
     GUARD_END
 }
 

@@ -13,6 +13,7 @@
 #include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -20,6 +21,7 @@
 
 #include "kernels.h"
 #include "status.h"
+#include "watchdog.h"
 
 namespace vsl {
 
@@ -39,6 +41,101 @@ int DecodeEngine::check_cuda(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return VSL_OK;
     if (e == cudaErrorMemoryAllocation) return set_error(VSL_ERR_OOM, "%s: %s", what, cudaGetErrorString(e));
     return set_error(VSL_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+static double seconds_now() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+static double nccl_timeout_s(const vsl_engine_options& o) {
+    return (o.nccl_timeout_ms > 0 ? o.nccl_timeout_ms : 120000) * 1e-3;
+}
+
+void DecodeEngine::abort_comm() {
+    if (nccl_) ncclCommAbort((ncclComm_t)nccl_);
+    nccl_ = nullptr;
+}
+
+int DecodeEngine::check_usable() const {
+    if (!failed_) return VSL_OK;
+    return set_error(VSL_ERR_STATE,
+                     "engine: a tensor-parallel exchange failed (status %d); the ranks are out of step, destroy and "
+                     "recreate the engine on every rank",
+                     failed_code_);
+}
+
+int DecodeEngine::nccl_result(int r0, const char* what) {
+    ncclResult_t r = (ncclResult_t)r0;
+    if (r == ncclInProgress && nccl_) {
+        // non-blocking communicator: the call finishes in the background; bounded wait
+        const double t0 = seconds_now(), limit = nccl_timeout_s(opt_);
+        while (r == ncclInProgress) {
+            ncclResult_t q = ncclCommGetAsyncError((ncclComm_t)nccl_, &r);
+            if (q != ncclSuccess) r = q;
+            if (r == ncclInProgress && seconds_now() - t0 > limit) {
+                abort_comm();
+                failed_ = true;
+                failed_code_ = VSL_ERR_TIMEOUT;
+                return set_error(VSL_ERR_TIMEOUT, "%s: not finished after %.1f s; communicator aborted", what, limit);
+            }
+            if (r == ncclInProgress) std::this_thread::yield();
+        }
+    }
+    if (r == ncclSuccess) return VSL_OK;
+    abort_comm();
+    failed_ = true;
+    failed_code_ = VSL_ERR_NCCL;
+    return set_error(VSL_ERR_NCCL, "%s: %s; communicator aborted", what, ncclGetErrorString(r));
+}
+
+int DecodeEngine::sync() {
+    if (!nccl_) return check_cuda(cudaStreamSynchronize(stream_), "cudaStreamSynchronize");
+    cudaError_t qerr = cudaSuccess;
+    ncclComm_t comm = (ncclComm_t)nccl_;
+    const int rc = watched_wait(
+        [&] {
+            const cudaError_t e = cudaStreamQuery(stream_);
+            if (e == cudaSuccess) return StreamPoll::Done;
+            if (e == cudaErrorNotReady) return StreamPoll::Pending;
+            qerr = e;
+            return StreamPoll::Error;
+        },
+        [&] {
+            ncclResult_t ae = ncclSuccess;
+            if (ncclCommGetAsyncError(comm, &ae) != ncclSuccess) return true;
+            return ae != ncclSuccess && ae != ncclInProgress;
+        },
+        [&] { abort_comm(); }, nccl_timeout_s(opt_), seconds_now,
+        [](unsigned long long it) {
+            // spin first (a decode step's wait is tens of microseconds), then back off
+            if (it > 4096) std::this_thread::sleep_for(std::chrono::microseconds(50));
+        });
+    if (rc == VSL_OK) return VSL_OK;
+    if (rc == VSL_ERR_CUDA) return check_cuda(qerr, "stream");
+    failed_ = true;
+    failed_code_ = rc;
+    if (rc == VSL_ERR_TIMEOUT)
+        return set_error(rc, "tensor-parallel work not finished after %.1f s: a rank is missing; communicator aborted, "
+                             "recreate the engine", nccl_timeout_s(opt_));
+    return set_error(rc, "NCCL reported an asynchronous error; communicator aborted, recreate the engine");
+}
+
+static int status_error(int st, const char* what) {
+    const char* why = st == VSL_ERR_TIMEOUT  ? "a bounded wait expired (a peer rank or a co-operating CTA never arrived)"
+                      : st == VSL_ERR_BOUNDS ? "an index was out of range (a position beyond max_seq)"
+                                             : "a kernel reported an error";
+    return set_error(st, "%s: %s (device status %d)", what, why, st);
+}
+
+int DecodeEngine::check_device_status(const char* what) {
+    int st = 0;
+    if (int rc = check_cuda(cudaMemcpy(&st, status_, 4, cudaMemcpyDeviceToHost), "status read")) return rc;
+    if (st == 0) return VSL_OK;
+    if (st == VSL_ERR_TIMEOUT && opt_.tp_size > 1) {
+        failed_ = true;
+        failed_code_ = st;
+    }
+    return status_error(st, what);
 }
 
 #define CK(expr)                                   \
@@ -117,10 +214,13 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
         if (!opt.nccl_id) return set_error(VSL_ERR_INVALID, "engine: tp_size %d needs an NCCL unique id", tp);
         ncclUniqueId id;
         memcpy(&id, opt.nccl_id, sizeof(id));
-        ncclComm_t comm;
-        ncclResult_t r = ncclCommInitRank(&comm, tp, id, opt.tp_rank);
-        if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclCommInitRank: %s", ncclGetErrorString(r));
+        // non-blocking, so that no host call can wait on a peer without a bound (sync())
+        ncclConfig_t ncfg = NCCL_CONFIG_INITIALIZER;
+        ncfg.blocking = 0;
+        ncclComm_t comm = nullptr;
+        ncclResult_t r = ncclCommInitRankConfig(&comm, tp, id, opt.tp_rank, &ncfg);
         nccl_ = comm;
+        RC(nccl_result(r, "ncclCommInitRankConfig"));
     }
     RC(alloc_buffers());
     if (nccl_ && opt_.use_p2p && tp <= P2P_MAX_RANKS) RC(setup_p2p());
@@ -132,7 +232,7 @@ int DecodeEngine::setup_p2p() {
     RC(p2p_setup(&p2p_x_, &p2p_x_local_, p2p_x_opened_, opt_.tp_rank, opt_.tp_size, opt_.max_batch * cfg_.d_model, 4,
                  nccl_, ar_epochs_, status_, stream_));
     RC(p2p_setup(&p2p_s_, &p2p_s_local_, p2p_s_opened_, opt_.tp_rank, opt_.tp_size, opt_.max_batch, 8, nccl_,
-                 ar_epochs_ + 1, status_, stream_));
+                 ar_epochs_ + P2P_MAX_CHUNKS, status_, stream_));
     p2p_ready_ = true;
     return VSL_OK;
 }
@@ -144,7 +244,20 @@ DecodeEngine::~DecodeEngine() {
     graphs_.clear();
     p2p_teardown(p2p_x_local_, p2p_x_opened_, opt_.tp_size);
     p2p_teardown(p2p_s_local_, p2p_s_opened_, opt_.tp_size);
-    if (nccl_) ncclCommDestroy((ncclComm_t)nccl_);
+    if (nccl_) {
+        // non-blocking communicator: finalize (bounded), then free; abort if a peer is gone
+        ncclComm_t comm = (ncclComm_t)nccl_;
+        ncclResult_t r = ncclCommFinalize(comm);
+        const auto t0 = std::chrono::steady_clock::now();
+        while (r == ncclInProgress) {
+            if (ncclCommGetAsyncError(comm, &r) != ncclSuccess) break;
+            if (std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10)) break;
+            std::this_thread::yield();
+        }
+        if (r == ncclSuccess) ncclCommDestroy(comm);
+        else ncclCommAbort(comm);
+        nccl_ = nullptr;
+    }
     cudaFree(arena_);
     cudaFree(kv_);
     cudaFree(act_);
@@ -203,17 +316,15 @@ int DecodeEngine::alloc_buffers() {
         {(void**)&slots_, mb * 8},
         {(void**)&ids_, mb * 4},
         {(void**)&pos_, mb * 4},
-        {(void**)&sampled_, mb * 4},
+        {(void**)&sampled_, mb * 4 + 4},  // sampled ids [mb], then the status word
         {(void**)&step_, 4},
         {(void**)&n_forced_, 4},
-        {(void**)&status_, 4},
         {(void**)&forced_, (size_t)log_cap_ * mb * 4},
         {(void**)&log_, (size_t)log_cap_ * mb * 4},
         {(void**)&rope_cos_, (size_t)opt_.max_seq * half * 4},
         {(void**)&rope_sin_, (size_t)opt_.max_seq * half * 4},
         {(void**)&page_table_, mb * (size_t)max_pages_ * 4},
-        {(void**)&ar_epochs_, 16},
-        {(void**)&ar_done_, 16},
+        {(void**)&ar_epochs_, 2 * P2P_MAX_CHUNKS * 8},
         {(void**)&fs_bar_, 16},
         {(void**)&fs_abort_, 4},
         {(void**)&fs_att_ws_, mb * (size_t)nh_l_ * (size_t)((opt_.max_seq + 63) / 64) * (hd + 2) * 4},
@@ -228,6 +339,7 @@ int DecodeEngine::alloc_buffers() {
     CK(cudaMemset(act_, 0, total));
     char* a = (char*)act_;
     for (auto& it : items) { *it.dst = a; a += align_up(it.bytes, A); }
+    status_ = reinterpret_cast<int*>(sampled_ + mb);
 
     RC(vsl_flash_decode_workspace_size(opt_.max_batch, nh_l_, nkv_l_, c.head_dim, opt_.max_seq, split_len_,
                                        &fd_ws_bytes_));
@@ -312,7 +424,7 @@ int DecodeEngine::alloc_buffers() {
     out_norm_ = (float*)p;
 
     CK(cudaMallocHost((void**)&h_ids_, mb * 4));
-    CK(cudaMallocHost((void**)&h_out_, mb * 4));
+    CK(cudaMallocHost((void**)&h_out_, (mb + 1) * 4));
     CK(cudaMallocHost((void**)&h_logits_, mb * (size_t)c.vocab * 4));
 
     // RoPE tables: cos/sin(pos * theta^(-2i/hd)) evaluated in double (Utils.cpp:101-110)
@@ -669,8 +781,9 @@ int DecodeEngine::init_synthetic(uint64_t seed, double sigma) {
 // ---------------------------------------------------------------------------------------
 
 int DecodeEngine::reset() {
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     const size_t mb = opt_.max_batch;
     CK(cudaMemsetAsync(pos_, 0, mb * 4, stream_));
     CK(cudaMemsetAsync(ids_, 0, mb * 4, stream_));
@@ -679,12 +792,11 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(status_, 0, 4, stream_));
     CK(cudaMemsetAsync(fs_bar_, 0, 16, stream_));
     CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
-    CK(cudaMemsetAsync(ar_done_, 0, 16, stream_));
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
     if (pf_tc_ws_) CK(cudaMemsetAsync(pf_tc_route_.ws, 0, pf_tc_route_.bytes, stream_));
     if (pf_fdtc_ws_) CK(cudaMemsetAsync(pf_fdtc_ws_, 0, pf_fdtc_bytes_, stream_));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     std::fill(pos_host_.begin(), pos_host_.end(), 0);
     steps_host_ = 0;
     return VSL_OK;
@@ -693,6 +805,7 @@ int DecodeEngine::reset() {
 int DecodeEngine::fill_kv_synthetic(uint64_t seed, double sigma, int n_pos, int B) {
     if (n_pos < 0 || n_pos > opt_.max_seq || B <= 0 || B > opt_.max_batch)
         return set_error(VSL_ERR_INVALID, "fill_kv: n_pos %d / B %d out of range", n_pos, B);
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
     const vsl_model_config& c = cfg_;
     const size_t hd = c.head_dim;
@@ -718,7 +831,7 @@ int DecodeEngine::fill_kv_synthetic(uint64_t seed, double sigma, int n_pos, int 
     CK(cudaMemcpy(pos.data(), pos_, pos.size() * 4, cudaMemcpyDeviceToHost));
     for (int b = 0; b < B; b++) pos[b] = n_pos;
     CK(cudaMemcpyAsync(pos_, pos.data(), pos.size() * 4, cudaMemcpyHostToDevice, stream_));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     for (int b = 0; b < B; b++) pos_host_[b] = n_pos;
     return VSL_OK;
 }
@@ -726,8 +839,9 @@ int DecodeEngine::fill_kv_synthetic(uint64_t seed, double sigma, int n_pos, int 
 int DecodeEngine::set_forced(const int32_t* ids, int n_steps, int B) {
     if (!ids || n_steps <= 0 || n_steps > log_cap_ || B <= 0 || B > opt_.max_batch)
         return set_error(VSL_ERR_INVALID, "set_forced: %d steps x %d sequences out of range", n_steps, B);
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     CK(cudaMemcpy(forced_, ids, (size_t)n_steps * B * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(n_forced_, &n_steps, 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(ids_, ids, (size_t)B * 4, cudaMemcpyHostToDevice));
@@ -743,25 +857,15 @@ int DecodeEngine::set_forced(const int32_t* ids, int n_steps, int B) {
 int DecodeEngine::allreduce_sum(float* buf, int count) {
     if (!nccl_) return VSL_OK;
     if (p2p_ready_ && count <= p2p_x_.cap) return p2p_allreduce(p2p_x_, buf, count, 0, stream_);
-    ncclResult_t r = ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_);
-    if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
-    return VSL_OK;
+    return nccl_result(ncclAllReduce(buf, buf, (size_t)count, ncclFloat, ncclSum, (ncclComm_t)nccl_, stream_),
+                       "ncclAllReduce");
 }
 
 // The decoder layers for B activation rows held in `sb` (the decode step's buffers, or a
-// prefill chunk's, where the rows are consecutive prompt positions of one sequence).
-// The tensor-parallel residual sums ride on the projections (reduce on read): the row-parallel
-// O and down projections push their rows into every rank's receive slot, and the next
-// projection (gate/up, the next layer's QKV, lm_head) sums the ranks' rows while it stages its
-// normalised input. One GEMV launch over all rows (16/32-bit weights, B <= 4) is needed for
-// that; other shapes use the separate all-reduce kernel.
-bool DecodeEngine::fuse_allreduce(const StepBufs& sb, int B) const {
-    return p2p_ready_ && nccl_ && opt_.fuse_allreduce && !is_quant(cfg_.wdtype) && !sb.shared_pages && B <= 4 &&
-           !(sb.tc && B >= sb.tc->min_batch) && (cfg_.d_model & 1) == 0 &&
-           (size_t)B * cfg_.d_model * sizeof(float) <= p2p_x_.slot_bytes;
-}
-
-int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
+// prefill chunk's, where the rows are consecutive prompt positions of one sequence). Under
+// tensor parallelism the row-parallel O and down projections leave partial residuals that the
+// peer-memory all-reduce (or NCCL) sums on every rank.
+int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
     const vsl_model_config& c = cfg_;
     const int d = c.d_model, hd = c.head_dim;
     const int res_epi = opt_.tp_rank == 0 ? VSL_EPI_ADD : VSL_EPI_STORE;  // partial sums reduced into x
@@ -782,8 +886,6 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
         CK(cudaStreamWaitEvent(copy_stream_, ev_fork_, 0));
     }
     const int R = (int)residency_.resident_layers;
-    const bool fuse = fuse_allreduce(sb, B);
-    const ArFuse prod{1, &p2p_x_, ar_done_, sb.x}, cons{2, &p2p_x_, ar_done_, sb.x};
     for (int l = 0; l < c.n_layers; l++) {
         const LayerPtrs& L = layers_[l];
         const bool last = l + 1 == c.n_layers;
@@ -797,7 +899,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
         }
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, sb.x, L.attn_norm, c.rms_eps, B, sb.pos,
                                   rope_cos_, rope_sin_, sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_,
-                                  page_size_, status_, st, L.wo, H(wo_b), tcr, fuse && l > 0 ? &cons : nullptr));
+                                  page_size_, status_, st, L.wo, H(wo_b), tcr));
         if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                     nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st));
@@ -805,19 +907,15 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B, bool* x_pending) {
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
                                  att_pf, sb.shared_pages));
-        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr,
-                     fuse ? &prod : nullptr));
-        if (!fuse) RC(allreduce_sum(sb.x, B * d));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
+        RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
-                     H(wd_b), st, tcr, fuse ? &cons : nullptr));
+                     H(wd_b), st, tcr));
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, sb.act, B, sb.x, res_epi, nullptr, 0.0f,
-                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr,
-                     fuse ? &prod : nullptr));
-        if (!fuse) RC(allreduce_sum(sb.x, B * d));
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr));
+        RC(allreduce_sum(sb.x, B * d));
         if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
-    if (x_pending) *x_pending = fuse;
-    else if (fuse) return set_error(VSL_ERR_STATE, "enqueue_layers: fused sums need a consumer");
     return VSL_OK;
 }
 
@@ -831,17 +929,14 @@ int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
     RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, ids_, B, x_, slots_, st));
     StepBufs sb{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
                 tc_ws_ ? &tc_route_ : nullptr, false};
-    bool pending = false;
-    RC(enqueue_layers(sb, B, &pending));
-    const TcRoute* tcr = sb.tc;
-    const ArFuse cons{2, &p2p_x_, ar_done_, x_};
+    RC(enqueue_layers(sb, B));
     RC(lm_head_hint(c.wdtype, lm_head_, v_l_, d, x_, out_norm_, c.rms_eps, B, logits_, slots_, v_off_, temperature,
-                    seed, step_, layers_[0].wqkv, H(qkv_b), st, tcr, pending ? &cons : nullptr));
+                    seed, step_, layers_[0].wqkv, H(qkv_b), st, sb.tc));
     if (p2p_ready_) {
         RC(p2p_allreduce(p2p_s_, slots_, B, 1, st));
     } else if (nccl_) {
-        ncclResult_t r = ncclAllReduce(slots_, slots_, (size_t)B, ncclUint64, ncclMax, (ncclComm_t)nccl_, st);
-        if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));
+        RC(nccl_result(ncclAllReduce(slots_, slots_, (size_t)B, ncclUint64, ncclMax, (ncclComm_t)nccl_, st),
+                       "ncclAllReduce(argmax)"));
     }
     RC(finalize_impl(slots_, B, ids_, pos_, step_, forced_, n_forced_, log_, log_cap_, sampled_, opt_.max_seq, status_,
                      st));
@@ -880,6 +975,7 @@ int DecodeEngine::run(int n_steps, int B, float temperature, uint64_t seed) {
         if (pos_host_[b] + n_steps > opt_.max_seq)
             return set_error(VSL_ERR_BOUNDS, "run: sequence %d at position %d cannot take %d more steps (max_seq %d)", b,
                              pos_host_[b], n_steps, opt_.max_seq);
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
     if (n_steps == 0) return VSL_OK;
     if (opt_.use_graph) {
@@ -951,15 +1047,16 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
     if (pos_host_[seq] + n > opt_.max_seq)
         return set_error(VSL_ERR_BOUNDS, "prefill: sequence %d at %d + %d positions exceeds max_seq %d", seq,
                          pos_host_[seq], n, opt_.max_seq);
+    RC(check_usable());
     const vsl_model_config& c = cfg_;
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     RC(alloc_prefill());
     const int d = c.d_model, P = PF_ROWS;
     const int p0 = pos_host_[seq];
     for (int c0 = 0; c0 < n; c0 += P) {
         const int nc = std::min(P, n - c0);
-        CK(cudaStreamSynchronize(stream_));  // the staging buffer is reused
+        RC(sync());  // the staging buffer is reused
         for (int i = 0; i < nc; i++) {
             pf_h_[i] = ids[c0 + i];
             pf_h_[P + i] = p0 + c0 + i;
@@ -979,21 +1076,22 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
             if (p2p_ready_) {
                 RC(p2p_allreduce(p2p_s_, pf_slot_, 1, 1, stream_));
             } else if (nccl_) {
-                ncclResult_t r = ncclAllReduce(pf_slot_, pf_slot_, 1, ncclUint64, ncclMax, (ncclComm_t)nccl_, stream_);
-                if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllReduce(argmax): %s", ncclGetErrorString(r));
+                RC(nccl_result(ncclAllReduce(pf_slot_, pf_slot_, 1, ncclUint64, ncclMax, (ncclComm_t)nccl_, stream_),
+                               "ncclAllReduce(argmax)"));
             }
             RC(prefill_finish_impl(pf_slot_, ids_, pos_, seq, p0 + n, pf_next_, stream_));
         }
     }
     const float* lsrc = pf_logits_;
     if (out_logits && nccl_) {
-        ncclResult_t r = ncclAllGather(pf_logits_, logits_full_, (size_t)v_l_, ncclFloat, (ncclComm_t)nccl_, stream_);
-        if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllGather(logits): %s", ncclGetErrorString(r));
+        RC(nccl_result(ncclAllGather(pf_logits_, logits_full_, (size_t)v_l_, ncclFloat, (ncclComm_t)nccl_, stream_),
+                       "ncclAllGather(logits)"));
         lsrc = logits_full_;  // [rank][v_l] = [vocab]
     }
     if (out_logits) CK(cudaMemcpyAsync(h_logits_, lsrc, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, stream_));
     CK(cudaMemcpyAsync(h_out_, pf_next_, 4, cudaMemcpyDeviceToHost, stream_));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
+    RC(check_device_status("prefill"));
     if (next_id) *next_id = h_out_[0];
     if (out_logits) memcpy(out_logits, h_logits_, (size_t)c.vocab * 4);
     pos_host_[seq] = p0 + n;
@@ -1002,11 +1100,12 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
 
 int DecodeEngine::reset_seq(int seq) {
     if (seq < 0 || seq >= opt_.max_batch) return set_error(VSL_ERR_INVALID, "reset_seq: sequence %d", seq);
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     CK(cudaMemsetAsync(pos_ + seq, 0, 4, stream_));
     CK(cudaMemsetAsync(ids_ + seq, 0, 4, stream_));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     pos_host_[seq] = 0;
     return VSL_OK;
 }
@@ -1058,6 +1157,7 @@ int DecodeEngine::generate_batch(const int32_t* prompts, const int* lens, int n_
         RC(run(n, n_seq, temperature, seed));
         log.resize((size_t)(steps + n) * n_seq);
         RC(read_tokens(steps + n, n_seq, log.data()));
+        RC(check_device_status("generate_batch"));
         for (int t = steps; t < steps + n; t++)
             for (int b = 0; b < n_seq; b++) {
                 if (done[b]) continue;
@@ -1079,20 +1179,29 @@ int DecodeEngine::step_host(const int32_t* ids, int B, int32_t* out_ids, float* 
     for (int b = 0; b < B; b++)
         if (pos_host_[b] + 1 > opt_.max_seq)
             return set_error(VSL_ERR_BOUNDS, "step_host: sequence %d is at max_seq %d", b, opt_.max_seq);
+    RC(check_usable());
     CK(cudaSetDevice(opt_.device));
     memcpy(h_ids_, ids, (size_t)B * 4);
     CK(cudaMemcpyAsync(ids_, h_ids_, (size_t)B * 4, cudaMemcpyHostToDevice, stream_));
     RC(run(1, B, 0.0f, 0));
-    CK(cudaMemcpyAsync(h_out_, sampled_, (size_t)B * 4, cudaMemcpyDeviceToHost, stream_));
+    // the sampled ids and the status word behind them in one copy
+    CK(cudaMemcpyAsync(h_out_, sampled_, ((size_t)opt_.max_batch + 1) * 4, cudaMemcpyDeviceToHost, stream_));
     const float* lsrc = logits_;
     if (out_logits && nccl_) {
-        ncclResult_t r = ncclAllGather(logits_, logits_full_, (size_t)B * v_l_, ncclFloat, (ncclComm_t)nccl_, stream_);
-        if (r != ncclSuccess) return set_error(VSL_ERR_NCCL, "ncclAllGather(logits): %s", ncclGetErrorString(r));
+        RC(nccl_result(ncclAllGather(logits_, logits_full_, (size_t)B * v_l_, ncclFloat, (ncclComm_t)nccl_, stream_),
+                       "ncclAllGather(logits)"));
         lsrc = logits_full_;
     }
     if (out_logits)
         CK(cudaMemcpyAsync(h_logits_, lsrc, (size_t)B * cfg_.vocab * 4, cudaMemcpyDeviceToHost, stream_));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
+    if (const int st = h_out_[opt_.max_batch]) {
+        if (st == VSL_ERR_TIMEOUT && opt_.tp_size > 1) {
+            failed_ = true;
+            failed_code_ = st;
+        }
+        return status_error(st, "step_host");
+    }
     if (out_ids) memcpy(out_ids, h_out_, (size_t)B * 4);
     if (out_logits) {
         if (!nccl_) {
@@ -1112,7 +1221,7 @@ int DecodeEngine::read_tokens(int n, int B, int32_t* out) {
     if (!out || n < 0 || n > log_cap_ || B <= 0 || B > opt_.max_batch)
         return set_error(VSL_ERR_INVALID, "read_tokens: %d x %d out of range", n, B);
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     if (n) CK(cudaMemcpy(out, log_, (size_t)n * B * 4, cudaMemcpyDeviceToHost));
     return VSL_OK;
 }
@@ -1120,15 +1229,22 @@ int DecodeEngine::read_tokens(int n, int B, int32_t* out) {
 int DecodeEngine::positions(int B, int32_t* out) {
     if (!out || B <= 0 || B > opt_.max_batch) return set_error(VSL_ERR_INVALID, "positions: bad batch");
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     CK(cudaMemcpy(out, pos_, (size_t)B * 4, cudaMemcpyDeviceToHost));
     return VSL_OK;
 }
 
 int DecodeEngine::device_status(int* status) {
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     CK(cudaMemcpy(status, status_, 4, cudaMemcpyDeviceToHost));
+    return VSL_OK;
+}
+
+int DecodeEngine::inject_status(int code) {
+    CK(cudaSetDevice(opt_.device));
+    RC(sync());
+    CK(cudaMemcpy(status_, &code, 4, cudaMemcpyHostToDevice));
     return VSL_OK;
 }
 
@@ -1138,9 +1254,12 @@ int DecodeEngine::generate(const int32_t* prompt, int n_prompt, int max_new, flo
                            const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out) {
     if (!prompt || n_prompt <= 0 || max_new < 0 || !out_ids || !n_out)
         return set_error(VSL_ERR_INVALID, "generate: empty prompt or null output");
-    if (n_prompt + max_new > opt_.max_seq)
+    // the prompt takes positions 0..n_prompt-1 and every new token but the last takes one more
+    // (the last one is sampled, never fed back): like generate_batch
+    if (n_prompt + max_new - 1 > opt_.max_seq)
         return set_error(VSL_ERR_BOUNDS, "generate: prompt %d + %d new tokens exceed max_seq %d", n_prompt, max_new,
                          opt_.max_seq);
+    RC(check_usable());
     *n_out = 0;
     if (max_new == 0) return VSL_OK;
     RC(reset());
@@ -1164,6 +1283,7 @@ int DecodeEngine::generate(const int32_t* prompt, int n_prompt, int max_new, flo
         RC(run(n, 1, temperature, seed));
         log.resize(done + n);
         RC(read_tokens(done + n, 1, log.data()));
+        RC(check_device_status("generate"));
         for (int i = done; i < done + n; i++) {
             out_ids[1 + i] = log[i];
             *n_out = 2 + i;
@@ -1201,13 +1321,9 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
                    c.n_layers * (chunks(c.d_model) /*qkv*/ + 1 /*attention*/ + chunks(nh_l_ * c.head_dim) /*o*/ +
                                  chunks(c.d_model) /*gate-up*/ + chunks(ff_l_) /*down*/) +
                    chunks(c.d_model) /*lm_head*/ + 1 /*finalize*/;
-        // tensor parallel over peer memory: the argmax exchange, and the residual all-reduce
-        // kernels unless the sums ride on the projections (NCCL's kernels are not counted)
-        if (p2p_ready_) {
-            StepBufs probe{x_, q_, attn_, act_ffn_, pos_, page_table_, fd_ws_, fd_ws_bytes_, fdtc_ws_, fdtc_ws_bytes_,
-                           tc_ws_ ? &tc_route_ : nullptr, false};
-            *kernels += 1 + (fuse_allreduce(probe, B) ? 0 : 2 * c.n_layers);
-        }
+        // tensor parallel over peer memory: the residual all-reduces and the argmax exchange
+        // (NCCL's kernels are not counted)
+        if (p2p_ready_) *kernels += 1 + 2 * c.n_layers;
     }
     if (bytes) *bytes = w + kv;
     return VSL_OK;
@@ -1220,7 +1336,7 @@ int DecodeEngine::device_of_layer(int) const { return opt_.device; }
 int DecodeEngine::set_trace(bool on) {
     if (on == fs_trace_on_) return VSL_OK;
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
     graphs_.clear();
     fs_trace_on_ = on;
@@ -1232,7 +1348,7 @@ int DecodeEngine::read_trace(int cap, unsigned long long* out, int* n) {
     *n = 0;
     if (!fs_ready_) return VSL_OK;
     CK(cudaSetDevice(opt_.device));
-    CK(cudaStreamSynchronize(stream_));
+    RC(sync());
     const int m = std::min(cap, fs_n_phases_);  // start + one stamp per barrier
     CK(cudaMemcpy(out, fs_trace_, (size_t)m * 8, cudaMemcpyDeviceToHost));
     *n = m;

@@ -70,6 +70,9 @@ public:
     int generate(const int32_t* prompt, int n_prompt, int max_new, float temperature, uint64_t seed,
                  const int32_t* stop_ids, int n_stop, int32_t* out_ids, int* n_out);
     int device_status(int* status);
+    // Test hook: write `code` into the sticky status word on the engine's stream, as a kernel that
+    // gave up on a bounded wait or rejected an index would (failures are made on the host).
+    int inject_status(int code);
     int step_stats(int B, int* kernels, double* bytes);
     int set_trace(bool on);
     int read_trace(int cap, unsigned long long* out, int* n);
@@ -107,10 +110,7 @@ private:
         const TcRoute* tc;
         bool shared_pages;  // rows are consecutive positions of one sequence (prompt chunk)
     };
-    // *x_pending: the last layer's down projection left its rows in the peers' buffers (fused
-    // tensor-parallel sum); the next projection reading x must consume them
-    int enqueue_layers(const StepBufs& sb, int B, bool* x_pending = nullptr);
-    bool fuse_allreduce(const StepBufs& sb, int B) const;
+    int enqueue_layers(const StepBufs& sb, int B);
     static constexpr int PF_ROWS = 64;  // prompt rows per prefill chunk
     int alloc_prefill();
     void* pf_mem_ = nullptr;
@@ -134,6 +134,21 @@ private:
     std::vector<int32_t> pt_host_;  // host copy of the page table
     int allreduce_sum(float* buf, int count);
     int check_cuda(cudaError_t e, const char* what);
+    // Wait for the engine's stream. Without tensor parallelism this is cudaStreamSynchronize;
+    // with it, a bounded watched wait (watchdog.h) that aborts the communicator and marks the
+    // engine failed when a peer never arrives.
+    int sync();
+    // After a sync: the sticky device status word; non-zero statuses are returned as errors
+    // (a timed-out peer exchange also marks a tensor-parallel engine failed).
+    int check_device_status(const char* what);
+    // VSL_ERR_STATE once the engine has failed (a peer exchange timed out or the communicator
+    // was aborted): the ranks are out of step and the engine must be recreated.
+    int check_usable() const;
+    // ncclResult_t of an enqueue on the non-blocking communicator: waits out ncclInProgress
+    int nccl_result(int r, const char* what);
+    void abort_comm();
+    bool failed_ = false;
+    int failed_code_ = 0;
     int device_of_layer(int l) const;
 
     // weight upload helpers: a "source" is full-tensor rows in host (pinned or mapped) or
@@ -174,8 +189,7 @@ private:
     void* p2p_x_opened_[P2P_MAX_RANKS] = {};
     void* p2p_s_opened_[P2P_MAX_RANKS] = {};
     bool p2p_ready_ = false;
-    unsigned long long* ar_epochs_ = nullptr;  // device call counters of the two all-reduces
-    unsigned int* ar_done_ = nullptr;          // arrival counters of the fused exchanges (producer, consumer)
+    unsigned long long* ar_epochs_ = nullptr;  // per-chunk device call counters of the two all-reduces
     int setup_p2p();
     void* fdtc_ws_ = nullptr;  // long-context attention (tcgen05 scores) workspace; null = split-K kernel
     size_t fdtc_ws_bytes_ = 0;

@@ -41,14 +41,14 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
                            const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
                            int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                           const TcRoute* tc = nullptr, const ArFuse* ar = nullptr);
+                           const TcRoute* tc = nullptr);
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc = nullptr, const ArFuse* ar = nullptr);
+              const TcRoute* tc = nullptr);
 int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
                  float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
                  const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-                 const TcRoute* tc = nullptr, const ArFuse* ar = nullptr);
+                 const TcRoute* tc = nullptr);
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,

@@ -3,6 +3,7 @@
 // when the file has none. Host code, off the decode path: the engine consumes ids.
 #include "../../../include/vk_symbiote/Tokenizer.h"
 
+#include <algorithm>
 #include <cstring>
 #include <queue>
 #include <sstream>
@@ -271,7 +272,14 @@ std::string Tokenizer::decode_continuation(const std::vector<uint32_t>& context,
     all.insert(all.end(), tokens.begin(), tokens.end());
     const std::string head = decode(context), full = decode(all);
     if (full.size() >= head.size() && full.compare(0, head.size(), head) == 0) return full.substr(head.size());
-    return decode(tokens);  // not reached for these decoders: the context's text is always a prefix
+    // The context ends inside a character or a U+2581 space mark that arrived as byte tokens:
+    // its raw bytes are not a prefix of the full text. The continuation is the full text after
+    // the longest common byte prefix, started on a character boundary.
+    size_t n = 0;
+    const size_t m = std::min(head.size(), full.size());
+    while (n < m && head[n] == full[n]) n++;
+    while (n > 0 && n < full.size() && (static_cast<unsigned char>(full[n]) & 0xC0) == 0x80) n--;
+    return full.substr(n);
 }
 
 }  // namespace vk_symbiote

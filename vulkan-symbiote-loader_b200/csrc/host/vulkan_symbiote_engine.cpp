@@ -78,7 +78,8 @@ std::vector<uint32_t> VulkanSymbioteEngine::generate_ids(const std::vector<uint3
                                                          float temperature, const std::vector<uint32_t>& stop_ids,
                                                          uint64_t seed) {
     if (prompt.empty() || max_new_tokens == 0) return {};
-    if (prompt.size() + max_new_tokens > max_seq_)
+    // the last new token is sampled, never fed back: it takes no KV position
+    if (prompt.size() + max_new_tokens - 1 > max_seq_)
         throw std::runtime_error("generate_ids: prompt + new tokens exceed the engine's max_seq");
     std::vector<int32_t> p(prompt.begin(), prompt.end()), stops(stop_ids.begin(), stop_ids.end());
     std::vector<int32_t> out(max_new_tokens);

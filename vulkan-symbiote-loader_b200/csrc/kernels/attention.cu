@@ -463,7 +463,8 @@ void* g_fd_scratch_addr[kMaxDevices] = {};
 
 // Device address of the static scratch on the current device. In host code the array's
 // name is only a host-side stand-in, so the address is looked up once per device with that
-// device current, and cached.
+// device current, and cached for the life of the process (a cudaDeviceReset of that device
+// would leave the cached address pointing into the ended context).
 int fd_static_scratch(void** out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);

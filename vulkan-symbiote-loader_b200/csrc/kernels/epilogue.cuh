@@ -38,40 +38,7 @@ struct GemvParams {
     // once its own rows are done, filling the tail of this launch
     const void* pf_ptr;
     size_t pf_bytes;
-    // Tensor-parallel sum fused into the projections (reduce on read), over the peer-memory
-    // receive buffers of `ar`:
-    //   ar_mode 1, row-parallel producer (EK_ADD / EK_STORE): the rows this rank computes (the
-    //     residual added on rank 0) go into slot [parity][rank] of every rank's buffer instead
-    //     of y, and the launch's last CTA raises the call's epoch flag on every rank;
-    //   ar_mode 2, consumer (a projection with a fused RMSNorm): the input x is the sum of the
-    //     ranks' slots in rank order (the same bits on every rank), which CTA 0 also writes to
-    //     x_out; the launch's last CTA advances the epoch.
-    int ar_mode;
-    P2pPeers ar;
-    unsigned int* ar_done;  // [2] arrival counters of this rank: producer, consumer (zero between calls)
-    float* x_out;
 };
-
-// Wait (bounded) until every rank's flag [par][r] in this rank's buffer holds epoch e.
-__device__ __forceinline__ bool ar_flag_ready(const P2pPeers& pe, int par, int r, unsigned long long e) {
-    const unsigned long long* f =
-        reinterpret_cast<const unsigned long long*>(static_cast<const char*>(pe.base[pe.rank]) + pe.flag_off) +
-        (size_t)par * pe.n + r;
-    bool ok = ld_acquire_sys_u64(f) == e;
-    if (!ok) {
-        const unsigned long long t0 = globaltimer_ns();
-        while (!ok) {
-            for (int i = 0; i < 64 && !ok; i++) ok = ld_acquire_sys_u64(f) == e;
-            if (!ok && globaltimer_ns() - t0 > WAIT_LIMIT_NS) break;
-        }
-    }
-    return ok;
-}
-// slot [par][r] of this rank's receive buffer
-__device__ __forceinline__ const float* ar_slot(const P2pPeers& pe, int par, int r) {
-    return reinterpret_cast<const float*>(static_cast<const char*>(pe.base[pe.rank]) +
-                                          ((size_t)par * pe.n + r) * pe.slot_bytes);
-}
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }
 

@@ -28,11 +28,10 @@ namespace vsl {
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_U = 8;
 constexpr int GEMV_L2_HEAD = 96 * 1024;
-constexpr int AR_ROWS = 128;  // output rows a producer CTA stages for the peers (reduce on read)
 
 template <typename WT, int NB, int EK, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvParams p) {
-    extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations (+ [NB][AR_ROWS] producer rows)
+    extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = WTraits<WT>::VEC;
     const int K = p.K, N = p.N;
@@ -61,64 +60,9 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvPar
     pdl_wait();
     pdl_launch_dependents();
 
-    // reduce on read: the exchange's epoch; a consumer first waits for every rank's rows
-    __shared__ unsigned long long ar_e;
-    __shared__ int ar_ok;
-    if (p.ar_mode) {
-        if (threadIdx.x == 0) {
-            ar_e = *p.ar.epoch + 1;
-            ar_ok = 1;
-        }
-        __syncthreads();
-        if (p.ar_mode == 2 && threadIdx.x < p.ar.n && !ar_flag_ready(p.ar, (int)(ar_e & 1), threadIdx.x, ar_e)) {
-            ar_ok = 0;
-            set_status(p.ar.status, VSL_ERR_TIMEOUT);
-        }
-        __syncthreads();
-        if (!ar_ok) return;
-    }
-
     // ---- stage activations (RMS-normalised if requested) ----
     const int B = p.B;
-    if (p.ar_mode == 2) {
-        // x = sum of the ranks' rows in rank order (identical on every rank); CTA 0 keeps it
-        const int par = (int)(ar_e & 1);
-        float ss[NB];
-#pragma unroll
-        for (int b = 0; b < NB; b++) ss[b] = 0.0f;
-        for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float v = 0.0f;
-                if (b < B) {
-                    for (int r = 0; r < p.ar.n; r++) v += __ldcg(ar_slot(p.ar, par, r) + (size_t)b * K + k);
-                    if (blockIdx.x == 0) p.x_out[(size_t)b * K + k] = v;
-                }
-                xs[b * K + k] = v;
-                ss[b] += v * v;
-            }
-        }
-        if (NORM) {
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float t = warp_sum(ss[b]);
-                if (lane == 0) red[b][warp] = t;
-            }
-            __syncthreads();
-#pragma unroll
-            for (int b = 0; b < NB; b++) {
-                float t = 0.0f;
-#pragma unroll
-                for (int w = 0; w < NW; w++) t += red[b][w];
-                ss[b] = sqrtf(t / (float)K + p.eps);  // rms_norm.comp:32-34: x / sqrt(var) * w
-            }
-            for (int k = threadIdx.x; k < K; k += GEMV_THREADS) {
-                const float w = p.norm_w[k];
-#pragma unroll
-                for (int b = 0; b < NB; b++) xs[b * K + k] = b < B ? xs[b * K + k] / ss[b] * w : 0.0f;
-            }
-        }
-    } else if (NORM) {
+    if (NORM) {
         float ss[NB];
 #pragma unroll
         for (int b = 0; b < NB; b++) ss[b] = 0.0f;
@@ -234,47 +178,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvPar
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             if (lane != b || b >= B) continue;
-            const float s0 = acc0[b], s1 = acc1[b];
-            if (p.ar_mode == 1) {  // row-parallel producer: stage the rows for the peers
-                float* ys = xs + NB * K + b * AR_ROWS + (r0 - 2 * u_begin);
-                ys[0] = EK == EK_ADD ? __ldcg(p.y + (size_t)b * N + r0) + s0 : s0;
-                if (has1) ys[1] = EK == EK_ADD ? __ldcg(p.y + (size_t)b * N + r0 + 1) + s1 : s1;
-            } else {
-                gemv_pair_epilogue<EK>(p, b, r0, unit, has1, s0, s1, best[b], step);
-            }
-        }
-    }
-    if (p.ar_mode == 1) {
-        // push this CTA's rows [r_lo, r_hi) into slot [parity][rank] of every rank, then the
-        // launch's last CTA raises the epoch flag on every rank (stores fenced at system scope
-        // before the arrival, so a rank that sees the flag sees every CTA's rows)
-        __syncthreads();
-        const int par = (int)(ar_e & 1);
-        const int r_lo = 2 * u_begin, per = (min(N, 2 * u_end) - r_lo) / 2;  // N is even
-        for (int i = threadIdx.x; i < p.ar.n * B * per; i += GEMV_THREADS) {
-            const int r = i / (B * per), rem = i - r * (B * per), b = rem / per, j = rem - b * per;
-            const float* ys = xs + NB * K + b * AR_ROWS + 2 * j;
-            float* dst = reinterpret_cast<float*>(static_cast<char*>(p.ar.base[r]) +
-                                                  ((size_t)par * p.ar.n + p.ar.rank) * p.ar.slot_bytes) +
-                         (size_t)b * N + r_lo + 2 * j;
-            *reinterpret_cast<float2*>(dst) = make_float2(ys[0], ys[1]);
-        }
-        __threadfence_system();
-        __syncthreads();
-        if (threadIdx.x == 0 && atomicAdd(p.ar_done, 1u) == gridDim.x - 1) {
-            p.ar_done[0] = 0u;
-            __threadfence_system();
-            for (int r = 0; r < p.ar.n; r++)
-                st_release_sys_u64(reinterpret_cast<unsigned long long*>(static_cast<char*>(p.ar.base[r]) + p.ar.flag_off) +
-                                       (size_t)par * p.ar.n + p.ar.rank,
-                                   ar_e);
-        }
-    } else if (p.ar_mode == 2) {
-        // every thread of this CTA read its slots before the staging barrier: the last CTA
-        // of the launch advances the epoch
-        if (threadIdx.x == 0 && atomicAdd(p.ar_done + 1, 1u) == gridDim.x - 1) {
-            p.ar_done[1] = 0u;
-            *p.ar.epoch = ar_e;
+            gemv_pair_epilogue<EK>(p, b, r0, unit, has1, acc0[b], acc1[b], best[b], step);
         }
     }
     if (EK == EK_LMHEAD) {
@@ -572,7 +476,7 @@ static int max_rows_per_launch(int wdtype, int K) {
 template <typename WT, int NB, int EK, bool NORM>
 static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
     auto kern = vsl_gemv_kernel<WT, NB, EK, NORM>;
-    const size_t smem = (size_t)NB * (p.K + (p.ar_mode == 1 ? AR_ROWS : 0)) * sizeof(float);
+    const size_t smem = (size_t)NB * p.K * sizeof(float);
     static thread_local int configured_dev = -1;
     static thread_local size_t configured_smem = 0;
     static thread_local int occ = 1;
@@ -595,9 +499,6 @@ static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
     const int max_grid = (n_units + nw - 1) / nw;
     if (grid > max_grid) grid = max_grid;
     if (grid < 1) grid = 1;
-    if (p.ar_mode == 1 && 2 * ((n_units + grid - 1) / grid) > AR_ROWS)
-        return set_error(VSL_ERR_UNSUPPORTED, "gemv: %d rows per CTA exceed the peer staging of %d", 2 * ((n_units + grid - 1) / grid),
-                         AR_ROWS);
     return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
 }
 
@@ -680,19 +581,6 @@ static int check_common(int wdtype, const void* W, int N, int K, const float* x,
 static int run_chunks(int wdtype, int kind, GemvParams p, cudaStream_t st, int y_cols,
                       const TcRoute* tc = nullptr) {
     const int B = p.B;
-    if (p.ar_mode) {  // a fused exchange is one launch of the 16/32-bit GEMV over all rows
-        if (is_quant(wdtype) || B > max_rows_per_launch(wdtype, p.K) || (p.ar_mode == 1 && (p.N & 1)) ||
-            (p.ar_mode == 2 && !p.x_out) || p.ar.n < 2 || p.ar.n > P2P_MAX_RANKS || !p.ar_done ||
-            (size_t)B * (p.ar_mode == 1 ? p.N : p.K) * sizeof(float) > p.ar.slot_bytes)
-            return set_error(VSL_ERR_UNSUPPORTED, "gemv: fused tensor-parallel exchange not possible here");
-        switch (kind) {
-            case EK_STORE: return launch_gemv_norm<EK_STORE>(wdtype, p, st);
-            case EK_ADD: return launch_gemv_norm<EK_ADD>(wdtype, p, st);
-            case EK_SWIGLU: return launch_gemv_norm<EK_SWIGLU>(wdtype, p, st);
-            case EK_QKV: return launch_gemv_norm<EK_QKV>(wdtype, p, st);
-            default: return launch_gemv_norm<EK_LMHEAD>(wdtype, p, st);
-        }
-    }
     if (tc && tc->ws && B >= tc->min_batch && tc_supported(wdtype, p.N, p.K, B))
         return tc_project(wdtype, kind, p, tc->ws, tc->bytes, tc->status ? tc->status : p.status, st);
     // activation rows per launch: at most 4, and at most what fits beside the weight ring
@@ -765,23 +653,14 @@ extern "C" int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, in
 // Engine-internal entry points: a device status word for out-of-range positions and the
 // L2 prefetch hint for the weights of the next kernel in the decode step.
 namespace vsl {
-static void set_ar(GemvParams& p, const ArFuse* ar) {
-    if (!ar || !ar->mode) return;
-    p.ar_mode = ar->mode;
-    p.ar = *ar->peers;
-    p.ar_done = ar->done;
-    p.x_out = ar->x_out;
-}
-
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc, const ArFuse* ar) {
+              const TcRoute* tc) {
     int rc = check_common(wdtype, W, N, K, x, B);
     if (rc) return rc;
     GemvParams p = {};
     p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
-    set_ar(p, ar);
     int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
     return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N, tc);
 }
@@ -789,14 +668,13 @@ int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, fl
 int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
                  float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
                  const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-                 const TcRoute* tc, const ArFuse* ar) {
+                 const TcRoute* tc) {
     GemvParams p = {};
     p.W = W; p.N = V_local; p.K = K; p.x = x; p.B = B; p.y = logits; p.norm_w = norm_w; p.eps = eps;
     p.slots = slots; p.vocab_offset = vocab_offset;
     p.inv_temp = temperature > 0.0f ? 1.0f / temperature : 0.0f;
     p.seed = seed; p.step_counter = step_counter;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
-    set_ar(p, ar);
     return run_chunks(wdtype, EK_LMHEAD, p, stream, V_local, tc);
 }
 
@@ -805,7 +683,7 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
                            const float* rope_cos, const float* rope_sin, float* q_out, void* k_cache,
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
                            int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                           const TcRoute* tc, const ArFuse* ar) {
+                           const TcRoute* tc) {
     GemvParams p = {};
     p.W = Wqkv; p.N = (n_heads + 2 * n_kv) * head_dim; p.K = K; p.x = x; p.B = B; p.norm_w = norm_w; p.eps = eps;
     p.n_heads = n_heads; p.n_kv = n_kv; p.head_dim = head_dim; p.pos = pos;
@@ -813,7 +691,6 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
     p.kvdtype = kvdtype; p.page_table = page_table; p.max_pages = max_pages; p.page_size = page_size;
     p.status = status;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
-    set_ar(p, ar);
     return run_chunks(wdtype, EK_QKV, p, stream, 0, tc);
 }
 }  // namespace vsl

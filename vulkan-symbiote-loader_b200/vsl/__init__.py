@@ -43,7 +43,7 @@ class EngineOptions(C.Structure):
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
-                ("use_p2p", C.c_int), ("fuse_allreduce", C.c_int), ("legacy_q4", C.c_int)]
+                ("use_p2p", C.c_int), ("legacy_q4", C.c_int), ("nccl_timeout_ms", C.c_int)]
 
 
 _lib = None
@@ -112,6 +112,9 @@ def lib() -> C.CDLL:
         "vsl_engine_residency": (i32, [vp, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(u64),
                                        C.POINTER(u64)]),
         "vsl_pack_plan": (i32, [u64, C.c_uint32, u64, f64, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+        "vsl_p2p_buffer_size": (i32, [i32, sz, C.POINTER(sz)]),
+        "vsl_p2p_allreduce": (i32, [C.POINTER(vp), i32, i32, sz, vp, i32, i32, vp, vp, u64, vp]),
+        "vsl_engine_inject_status": (i32, [vp, i32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -308,6 +311,20 @@ def gguf_tensor_info(path: str, name: str):
     return t.value, [int(v) for v in ne if v], off.value
 
 
+def p2p_buffer_size(n_ranks: int, cap_bytes: int) -> int:
+    n = C.c_size_t(0)
+    check(lib().vsl_p2p_buffer_size(n_ranks, cap_bytes, C.byref(n)))
+    return n.value
+
+
+def p2p_allreduce(bases, rank: int, cap_bytes: int, data, n: int, op: int, epochs, status=None, wait_ns: int = 10**9,
+                  stream=0):
+    """One-shot peer-memory all-reduce (vsl_p2p_allreduce): bases = the ranks' receive buffers."""
+    arr = (C.c_void_p * len(bases))(*[_ptr(b) for b in bases])
+    check(lib().vsl_p2p_allreduce(arr, len(bases), rank, cap_bytes, _ptr(data), n, op, _ptr(epochs), _ptr(status),
+                                  wait_ns, _ptr(stream)))
+
+
 def pack_plan(layer_bytes: int, n_layers: int, fixed_bytes: int, budget_gb: float) -> tuple[int, int]:
     """(resident_layers, streamed_layers) the engine would choose under `budget_gb`."""
     r, st = C.c_uint32(), C.c_uint32()
@@ -494,3 +511,7 @@ class Engine:
         s = C.c_int()
         check(lib().vsl_engine_device_status(self.h, C.byref(s)))
         return s.value
+
+    def inject_status(self, code: int):
+        """Test hook: set the sticky device status word (host-made failure)."""
+        check(lib().vsl_engine_inject_status(self.h, code))
