@@ -63,6 +63,12 @@ struct DeviceOptions {
     uint32_t max_seq = 0;          // 0: min(llama.context_length, 4096)
     double vram_budget_gb = -1.0;  // < 0: ConfigManager budget if explicitly set, else no cap
     bool use_graph = true;
+    // Long-context sparse attention with the model config's window (use_sparse_attention,
+    // sparse_window_size, sparse_global_tokens, sparse_block_size; Common.h): the reference
+    // switches to it above 8192 positions (VulkanSymbioteEngine.cpp:788). Off by default here:
+    // dense attention at every length, as a standard Llama.
+    bool sparse_attention = false;
+    uint32_t sparse_min_len = 8192;
 };
 
 class VSL_CPP_API VulkanSymbioteEngine {

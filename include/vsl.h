@@ -134,6 +134,25 @@ VSL_API int vsl_flash_decode(const float* q, const void* k_cache, const void* v_
                      int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                      size_t workspace_bytes, void* stream);
 
+/* Long-context sparse mask (the reference's sparse_attention.comp:77-131, switched on when
+ * use_sparse_attention && seq_len > 8192, VulkanSymbioteEngine.cpp:788; defaults window 512,
+ * 16 global tokens, 1024-position blocks, Common.h:71-74). A query at position pos of a
+ * sequence of pos + 1 > min_len tokens attends to positions [first, pos] with, following the
+ * shader's index arithmetic,
+ *     ws = pos > window ? pos - window : 0
+ *     start = pos < global_tokens ? 0 : min(global_tokens, ws)
+ *     bs = (pos / block) * block;  clamp = bs > window ? bs - window : 0
+ *     first = max(start, clamp)
+ * (contiguous: in the shader the global tokens only enter through that min). Shorter sequences,
+ * and min_len <= 0, attend densely. The shader's 512-entry score buffer, which reads 0 for the
+ * scores beyond it, is a storage limit and not part of the mask. */
+typedef struct {
+    int min_len;
+    int window;
+    int global_tokens;
+    int block;
+} vsl_sparse_mask;
+
 /* Long-context decode attention with the score product on the tcgen05 tensor cores (same
  * semantics and cache layout as vsl_flash_decode; fp16 KV, head_dim 128, up to 8 query heads
  * per KV group, B <= 64, page_size a multiple of 64). n_pages is the size of the physical page
@@ -146,6 +165,19 @@ VSL_API int vsl_flash_decode_tc(const float* q, const void* k_cache, const void*
                                 const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                                 int n_heads, int n_kv, int head_dim, int max_len, float* out, void* workspace,
                                 size_t workspace_bytes, void* stream);
+
+/* vsl_flash_decode / vsl_flash_decode_tc with the sparse mask applied per query row (mask NULL
+ * or min_len <= 0: dense, the same as the plain entry points). Same workspaces. */
+VSL_API int vsl_flash_decode_sparse(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                    const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                                    int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out,
+                                    void* workspace, size_t workspace_bytes, const vsl_sparse_mask* mask,
+                                    void* stream);
+VSL_API int vsl_flash_decode_tc_sparse(const float* q, const void* k_cache, const void* v_cache, int n_pages,
+                                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                       int B, int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                                       void* workspace, size_t workspace_bytes, const vsl_sparse_mask* mask,
+                                       void* stream);
 
 /* Allocation-free form of vsl_flash_decode (no counterpart in the reference). For callers
  * that must not have the library allocate device memory -- hosts that own every device
@@ -243,6 +275,14 @@ typedef struct {
     int legacy_q4;     /* 1 = read GGUF Q4_0 / Q4_1 nibbles in the reference loader's order
                           (GGUFLoader.cpp:1146-1160: element 2i low, 2i+1 high nibble of
                           byte i); 0 (default) = ggml's order (element i low, i+16 high)  */
+    int sparse_min_len; /* long-context sparse attention, the reference's use_sparse_attention
+                          (VulkanSymbioteEngine.cpp:788; sparse_attention.comp:77-131): a query at
+                          position pos of a sequence longer than sparse_min_len attends to the
+                          window vsl_sparse_mask describes. 0 (default) = dense attention at every
+                          length; the reference switches at 8192                           */
+    int sparse_window;   /* window W (0 = 512)                                               */
+    int sparse_global;   /* global tokens G (0 = 16)                                         */
+    int sparse_block;    /* block BLK (0 = 1024)                                             */
     int nccl_timeout_ms; /* tensor parallel: the longest the host waits for work that involves the
                           other ranks (one call's stream work); past it, or when NCCL reports an
                           asynchronous error, the communicator is aborted, the call returns

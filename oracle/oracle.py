@@ -60,6 +60,10 @@ def lib():
         L.orc_argmax.restype = C.c_int32
         L.orc_argmax.argtypes = [vp, i32]
         L.orc_attention.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp]
+        L.orc_attention_from.argtypes = [vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp]
+        L.orc_sparse_first.argtypes = [i32, i32, i32, i32, i32]
+        L.orc_sparse_first.restype = i32
+        L.orc_model_set_sparse.argtypes = [vp, i32, i32, i32, i32]
         L.orc_model_load_gguf.argtypes = [C.c_char_p, i32, i32, i32, C.POINTER(vp)]
         L.orc_model_load_gguf_ex.argtypes = [C.c_char_p, i32, i32, i32, i32, C.POINTER(vp)]
         L.orc_dequant_blocks.argtypes = [i32, vp, C.c_size_t, i32, vp]
@@ -150,14 +154,20 @@ def argmax(v):
     return int(lib().orc_argmax(_p(v), v.size))
 
 
-def attention(q, Kc, Vc, kvdtype, n_heads, n_kv, head_dim, max_seq, length):
-    """q [n_heads*hd] fp32; Kc/Vc [n_kv][max_seq][hd] in kvdtype storage; -> o [n_heads*hd]."""
+def attention(q, Kc, Vc, kvdtype, n_heads, n_kv, head_dim, max_seq, length, first=0):
+    """q [n_heads*hd] fp32; Kc/Vc [n_kv][max_seq][hd] in kvdtype storage; positions [first, length)
+    -> o [n_heads*hd]."""
     q = np.ascontiguousarray(q, np.float32)
     o = np.empty(n_heads * head_dim, np.float32)
     scratch = np.empty(max(length, 1), np.float32)
-    lib().orc_attention(_p(q), _p(np.ascontiguousarray(Kc)), _p(np.ascontiguousarray(Vc)), kvdtype, n_heads,
-                        n_kv, head_dim, max_seq, length, _p(o), _p(scratch))
+    lib().orc_attention_from(_p(q), _p(np.ascontiguousarray(Kc)), _p(np.ascontiguousarray(Vc)), kvdtype, n_heads,
+                             n_kv, head_dim, max_seq, first, length, _p(o), _p(scratch))
     return o
+
+
+def sparse_first(min_len, window, global_tokens, block, pos):
+    """First position a query at `pos` attends to under the reference's sparse mask (0: dense)."""
+    return int(lib().orc_sparse_first(min_len, window, global_tokens, block, pos))
 
 
 class Model:
@@ -201,6 +211,11 @@ class Model:
 
     def clear_kv(self):
         lib().orc_model_clear_kv(self.h)
+
+    def set_sparse(self, min_len=8192, window=512, global_tokens=16, block=1024):
+        """Sparse long-context attention for later steps (min_len 0: dense)."""
+        if lib().orc_model_set_sparse(self.h, min_len, window, global_tokens, block) != 0:
+            raise RuntimeError("bad sparse mask")
 
     def fill_kv_synthetic(self, seed, sigma, n_pos, batch):
         rc = lib().orc_model_fill_kv_synthetic(self.h, seed, sigma, n_pos, batch)

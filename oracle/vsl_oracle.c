@@ -357,14 +357,34 @@ int32_t orc_argmax(const float* v, int n) {
     return best;
 }
 
-/* One query head against its KV group: Kg,Vg point at [max_seq][hd] of group g.
- * attention.comp:116-189: scores scaled by 1/sqrt(hd), max-subtracted softmax, then
- * normalised probabilities times V. */
+/* Long-context sparse mask of the reference (sparse_attention.comp:77-131), selected when the
+ * sequence is longer than min_len (VulkanSymbioteEngine.cpp:788: use_sparse_attention &&
+ * seq_len > 8192; window 512, 16 global tokens, blocks of 1024, Common.h:71-74). For a query at
+ * position pos of a sequence of pos + 1 tokens the shader's index arithmetic gives one
+ * contiguous range [first, pos]:
+ *   get_attention_window (:77-101): window_start = pos > W ? pos - W : 0; a query among the
+ *     first G tokens starts at 0, any other at min(G, window_start); the range ends at pos + 1;
+ *   compute_ring_attention (:105-131): block_start = (pos / BLK) * BLK; the start is raised to
+ *     block_start - W when block_start > W; the end is cut at the block's end (>= pos + 1).
+ * The shader keeps 512 scores in shared memory and reads 0 for later ones (:143-158); that
+ * buffer limit is not part of the mask and is not restated. min_len <= 0: dense (first 0). */
+int orc_sparse_first(int min_len, int window, int global, int block, int pos) {
+    if (min_len <= 0 || pos + 1 <= min_len) return 0;
+    int ws = pos > window ? pos - window : 0;
+    int start = pos < global ? 0 : (global < ws ? global : ws);
+    int bs = (pos / block) * block;
+    int clamp = bs > window ? bs - window : 0;
+    return start > clamp ? start : clamp;
+}
+
+/* One query head against its KV group: Kg,Vg point at [max_seq][hd] of group g, positions
+ * [first, len). attention.comp:116-189: scores scaled by 1/sqrt(hd), max-subtracted softmax,
+ * then normalised probabilities times V. */
 static void attn_head(const float* qh, const void* Kc, const void* Vc, int kvdtype, size_t gbase,
-                      int head_dim, int len, float* oh, float* scratch) {
+                      int head_dim, int first, int len, float* oh, float* scratch) {
     float scale = 1.0f / sqrtf((float)head_dim);
     float mx = -INFINITY;
-    for (int t = 0; t < len; t++) {
+    for (int t = first; t < len; t++) {
         size_t base = gbase + (size_t)t * head_dim;
         float s = 0.0f;
         for (int e = 0; e < head_dim; e++) s += qh[e] * load_elem(Kc, kvdtype, base + e);
@@ -373,12 +393,12 @@ static void attn_head(const float* qh, const void* Kc, const void* Vc, int kvdty
         if (s > mx) mx = s;
     }
     float sum = 0.0f;
-    for (int t = 0; t < len; t++) {
+    for (int t = first; t < len; t++) {
         scratch[t] = expf(scratch[t] - mx);
         sum += scratch[t];
     }
     for (int e = 0; e < head_dim; e++) oh[e] = 0.0f;
-    for (int t = 0; t < len; t++) {
+    for (int t = first; t < len; t++) {
         float p = scratch[t] / sum;
         size_t base = gbase + (size_t)t * head_dim;
         for (int e = 0; e < head_dim; e++) oh[e] += p * load_elem(Vc, kvdtype, base + e);
@@ -386,15 +406,19 @@ static void attn_head(const float* qh, const void* Kc, const void* Vc, int kvdty
 }
 
 /* Single-query attention for one sequence over a contiguous cache
- * K,V: [n_kv][max_seq][hd] (dtype kvdtype), attend to t in [0, len).
+ * K,V: [n_kv][max_seq][hd] (dtype kvdtype), attend to t in [first, len) (first = 0: dense).
  * Query head h reads KV group g = h*n_kv/n_heads (attention.comp:92). */
-void orc_attention(const float* q, const void* Kc, const void* Vc, int kvdtype, int n_heads,
-                   int n_kv, int head_dim, int max_seq, int len, float* o, float* scratch) {
+void orc_attention_from(const float* q, const void* Kc, const void* Vc, int kvdtype, int n_heads, int n_kv,
+                        int head_dim, int max_seq, int first, int len, float* o, float* scratch) {
     for (int h = 0; h < n_heads; h++) {
         int g = (int)((long)h * n_kv / n_heads);
         attn_head(q + (size_t)h * head_dim, Kc, Vc, kvdtype, (size_t)g * max_seq * head_dim, head_dim,
-                  len, o + (size_t)h * head_dim, scratch);
+                  first, len, o + (size_t)h * head_dim, scratch);
     }
+}
+void orc_attention(const float* q, const void* Kc, const void* Vc, int kvdtype, int n_heads,
+                   int n_kv, int head_dim, int max_seq, int len, float* o, float* scratch) {
+    orc_attention_from(q, Kc, Vc, kvdtype, n_heads, n_kv, head_dim, max_seq, 0, len, o, scratch);
 }
 
 /* ------------------------------------------------------------------------- */
@@ -440,6 +464,7 @@ typedef struct {
     float* rope_cos;
     float* rope_sin;
     int rope_len;
+    int sp_min_len, sp_window, sp_global, sp_block; /* sparse mask (sp_min_len 0: dense) */
 } orc_model;
 
 typedef struct {
@@ -707,6 +732,16 @@ static void kv_store(const orc_model* m, void* cache, size_t idx, const float* v
     else memcpy((float*)cache + idx, v, sizeof(float) * (size_t)n);
 }
 
+/* Sparse long-context attention (orc_sparse_first) for every later step; min_len 0 = dense. */
+int orc_model_set_sparse(orc_model* m, int min_len, int window, int global, int block) {
+    if (!m || min_len < 0 || window < 0 || global < 0 || (min_len > 0 && block <= 0)) return -1;
+    m->sp_min_len = min_len;
+    m->sp_window = window;
+    m->sp_global = global;
+    m->sp_block = block;
+    return 0;
+}
+
 void orc_model_clear_kv(orc_model* m) {
     orc_config* c = &m->c;
     size_t kvn = (size_t)c->n_layers * c->max_batch * c->n_kv * c->max_seq * c->head_dim;
@@ -791,8 +826,9 @@ int orc_model_step(orc_model* m, int B, const int32_t* ids, const int32_t* pos, 
                 for (int h = 0; h < c->n_heads; h++) {
                     int gi = (int)((long)h * c->n_kv / c->n_heads); /* attention.comp:92 */
                     attn_head(q + (size_t)b * qd + (size_t)h * hd, m->kcache, m->vcache, c->kvdtype,
-                              kv_index(c, l, b, gi, 0), hd, pos[b] + 1, o + (size_t)b * qd + (size_t)h * hd,
-                              scratch);
+                              kv_index(c, l, b, gi, 0), hd,
+                              orc_sparse_first(m->sp_min_len, m->sp_window, m->sp_global, m->sp_block, pos[b]),
+                              pos[b] + 1, o + (size_t)b * qd + (size_t)h * hd, scratch);
                 }
             free(scratch);
         }

@@ -40,6 +40,10 @@ extern "C" void vsl_engine_default_options(vsl_engine_options* o) {
     o->use_fused = 0;
     o->use_p2p = 1;
     o->legacy_q4 = 0;
+    o->sparse_min_len = 0;  // dense attention at every length
+    o->sparse_window = 512;
+    o->sparse_global = 16;
+    o->sparse_block = 1024;
     o->nccl_timeout_ms = 120000;
 }
 

@@ -205,6 +205,11 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     }
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);
+    if (opt.sparse_min_len < 0 || opt.sparse_window < 0 || opt.sparse_global < 0 || opt.sparse_block < 0)
+        return set_error(VSL_ERR_INVALID, "engine: negative sparse attention parameter");
+    if (opt.sparse_min_len > 0)  // zeros take the reference's values (Common.h:71-74)
+        sparse_ = SparseMask{opt.sparse_min_len, opt.sparse_window ? opt.sparse_window : 512,
+                             opt.sparse_global ? opt.sparse_global : 16, opt.sparse_block ? opt.sparse_block : 1024};
 
     CK(cudaSetDevice(opt.device));
     CK(cudaDeviceGetAttribute(&l2_bytes_, cudaDevAttrL2CacheSize, opt.device));
@@ -503,7 +508,7 @@ int DecodeEngine::build_fused_program() {
 }
 
 bool DecodeEngine::fused_supported(int B) const {
-    if (!fs_ready_ || B < 1 || B > 4 || residency_.streamed_layers) return false;
+    if (!fs_ready_ || B < 1 || B > 4 || residency_.streamed_layers || sparse_.min_len > 0) return false;
     const vsl_model_config& c = cfg_;
     if (c.head_dim != 64 && c.head_dim != 128) return false;
     if (c.head_dim == 128 && kvdtype_ != VSL_F16) return false;
@@ -902,11 +907,12 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
         if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
-                                    nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st));
+                                    nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st,
+                                    &sparse_));
         else
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
-                                 att_pf, sb.shared_pages));
+                                 att_pf, sb.shared_pages, &sparse_));
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
         RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,

@@ -149,6 +149,7 @@ private:
     void abort_comm();
     bool failed_ = false;
     int failed_code_ = 0;
+    SparseMask sparse_{};  // long-context sparse attention (min_len 0: dense)
     int device_of_layer(int l) const;
 
     // weight upload helpers: a "source" is full-tensor rows in host (pinned or mapped) or

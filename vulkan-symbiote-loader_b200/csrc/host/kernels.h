@@ -5,6 +5,7 @@
 
 #include "../kernels/p2p_allreduce.h"
 #include "../kernels/quant_layout.h"
+#include "../kernels/sparse_mask.h"
 
 namespace vsl {
 
@@ -53,13 +54,13 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                       size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                      bool shared_pages = false);
+                      bool shared_pages = false, const SparseMask* sparse = nullptr);
 size_t flash_decode_tc_workspace_bytes(int B, int n_kv);
 bool flash_decode_tc_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int B, int page_size);
 int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages,
                          const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                          int n_heads, int n_kv, int max_len, float* out, void* workspace, size_t workspace_bytes,
-                         int* status, cudaStream_t st);
+                         int* status, cudaStream_t st, const SparseMask* sparse = nullptr);
 constexpr int FDTC_MIN_SEQ = 2048;  // caches from this length on use the tensor-core attention
 int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start, uint64_t n, double sigma,
                cudaStream_t st);

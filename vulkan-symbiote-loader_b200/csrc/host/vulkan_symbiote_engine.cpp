@@ -60,6 +60,12 @@ void VulkanSymbioteEngine::open(const Path& model_path, const DeviceOptions& opt
     o.vram_budget_gb =
         opt.vram_budget_gb >= 0 ? opt.vram_budget_gb : (cm.vram_budget_explicit() ? cm.memory().vram_budget_gb : 0.0);
     o.use_graph = opt.use_graph ? 1 : 0;
+    if (opt.sparse_attention && config_.use_sparse_attention) {
+        o.sparse_min_len = (int)opt.sparse_min_len;
+        o.sparse_window = (int)config_.sparse_window_size;
+        o.sparse_global = (int)config_.sparse_global_tokens;
+        o.sparse_block = (int)config_.sparse_block_size;
+    }
     if (vsl_engine_create_gguf(model_path.c_str(), &o, &engine_) != VSL_OK) throw_vsl("VulkanSymbioteEngine");
     tokenizer_ = Tokenizer::from_gguf(model_path);
     peak_vram_gb_ = get_peak_vram_usage();

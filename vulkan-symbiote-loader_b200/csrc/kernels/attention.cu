@@ -43,6 +43,7 @@ struct FdParams {
     const void* pf_ptr;  // weights of the projection that follows (prefetched into L2)
     size_t pf_bytes;
     int wait_first;      // rows share one sequence's pages (prompt chunk): no cache read before the wait
+    SparseMask sp;       // long-context sparse mask (sp.min_len 0: dense)
 };
 
 template <typename KT> struct KvVec;
@@ -104,7 +105,11 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     // has already flagged such a position in the engine's status word).
     const int pos = p.pos[b];
     const int len = min(pos + 1, min(p.max_pages * p.page_size, p.n_splits * p.split_len));
-    const int t_begin = split * p.split_len;
+    // sparse mask: the row attends to [lo, len); splits below lo take no part, the first active
+    // split starts at lo's chunk and masks the rows below lo
+    const int lo = min(sparse_first(p.sp, pos), len - 1);
+    const int s_first = lo / p.split_len;
+    const int t_begin = split < s_first ? len : max(split * p.split_len, lo & ~(FD_CHUNK - 1));
     if (t_begin >= len) {  // empty split: not counted by the combiner; it only prefetches
         if (p.pf_ptr && tid < 32) {
             const int nblk = gridDim.x * gridDim.y * gridDim.z;
@@ -113,8 +118,8 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         }
         return;
     }
-    const int t_end = min(len, t_begin + p.split_len);
-    const int n_active = (len + p.split_len - 1) / p.split_len;
+    const int t_end = min(len, (split + 1) * p.split_len);
+    const int n_active = (len + p.split_len - 1) / p.split_len - s_first;  // splits that take part
     const int n_chunks = (t_end - t_begin + FD_CHUNK - 1) / FD_CHUNK;
     const int new_row = pos - t_begin;  // row of the freshly appended position, if in this split
     if (p.wait_first) pdl_wait();
@@ -218,11 +223,16 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
             if (lane < n) s0 = (part_s[j * FD_CHUNK + lane] + part_s[(FD_GMAX + j) * FD_CHUNK + lane]) * p.scale;
             if (lane + 32 < n)
                 s1 = (part_s[j * FD_CHUNK + lane + 32] + part_s[(FD_GMAX + j) * FD_CHUNK + lane + 32]) * p.scale;
+            if (t_begin + ci * FD_CHUNK < lo) {  // rows below the sparse window's start
+                const int t0 = t_begin + ci * FD_CHUNK;
+                if (t0 + lane < lo) s0 = -CUDART_INF_F;
+                if (t0 + lane + 32 < lo) s1 = -CUDART_INF_F;
+            }
             const float cmax = warp_max(fmaxf(s0, s1));
             const float m_old = m_s[j];
             const float m_new = fmaxf(m_old, cmax);
-            const float e0 = lane < n ? expf(s0 - m_new) : 0.0f;
-            const float e1 = lane + 32 < n ? expf(s1 - m_new) : 0.0f;
+            const float e0 = lane < n && s0 != -CUDART_INF_F ? expf(s0 - m_new) : 0.0f;
+            const float e1 = lane + 32 < n && s1 != -CUDART_INF_F ? expf(s1 - m_new) : 0.0f;
             p_s[j * FD_CHUNK + lane] = e0;
             p_s[j * FD_CHUNK + lane + 32] = e1;
             const float csum = warp_sum(e0 + e1);
@@ -302,7 +312,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     constexpr int TILE = FD_GMAX * FD_CHUNK;
     float* red = m_s;                         // FD_THREADS / 32 partial maxima (own stats are written)
     for (int j = 0; j < G; j++) {
-        const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits;
+        const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits + s_first;
         float mx = -CUDART_INF_F;
         for (int s = tid; s < n_active; s += FD_THREADS) mx = fmaxf(mx, __ldcg(p.ws_ml + (row0 + s) * 2));
         mx = warp_max(mx);
@@ -387,9 +397,12 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                       size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                      bool shared_pages) {
+                      bool shared_pages, const SparseMask* sparse) {
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
         return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
+    if (sparse && sparse->min_len > 0 && (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0))
+        return set_error(VSL_ERR_INVALID, "flash_decode: sparse mask window %d, global %d, block %d", sparse->window,
+                         sparse->global_tokens, sparse->block);
     if (B <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > FD_GMAX)
         return set_error(VSL_ERR_UNSUPPORTED, "flash_decode: heads %d / kv %d (group size <= %d)", n_heads, n_kv,
                          FD_GMAX);
@@ -414,6 +427,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
     p.pf_ptr = pf_ptr;
     p.pf_bytes = pf_bytes;
     p.wait_first = shared_pages ? 1 : 0;
+    if (sparse) p.sp = *sparse;
     if (kvdtype == VSL_F16) {
         if (head_dim == 128) return launch_fd<128, __half>(p, stream);
         if (head_dim == 64) return launch_fd<64, __half>(p, stream);
@@ -440,7 +454,19 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0, true);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr);  // the caller's rows may share pages
+}
+
+extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                       int B, int n_heads, int n_kv, int head_dim, int max_len, int split_len,
+                                       float* out, void* workspace, size_t workspace_bytes,
+                                       const vsl_sparse_mask* mask, void* stream) {
+    vsl::SparseMask m = {};
+    if (mask && mask->min_len > 0) m = vsl::SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
+    return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
+                                  n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
+                                  (cudaStream_t)stream, nullptr, 0, true, &m);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -508,5 +534,5 @@ extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, con
     if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, ws, FD_STATIC_SCRATCH_BYTES,
-                                  (cudaStream_t)stream, nullptr, 0, true);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr);  // the caller's rows may share pages
 }

@@ -62,6 +62,7 @@ struct FtArgs {
     int* status;
     uint32_t idesc;     // S MMA: K (A, K-major) . Q2 (B, K-major)
     uint32_t idesc_pv;  // PV MMA: V (A, MN-major) . P2 (B, K-major)
+    SparseMask sp;      // long-context sparse mask (sp.min_len 0: dense)
 };
 
 __device__ __forceinline__ void ft_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -106,9 +107,11 @@ __device__ __forceinline__ void ft_ld16(uint32_t taddr, uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Flattened work list: for sequence b, n_kv groups x nch[b] chunks, starting at off[b].
+// Flattened work list: for sequence b, n_kv groups x nch[b] chunks, starting at off[b]; chunk ch
+// of sequence b covers positions (c0[b] + ch) * 128 onward, of which those below lo[b] are masked
+// (the sparse mask's start; c0 = lo = 0 when dense).
 struct FtWork {
-    int nch[FT_BMAX], len[FT_BMAX];
+    int nch[FT_BMAX], len[FT_BMAX], c0[FT_BMAX], lo[FT_BMAX];
     long long off[FT_BMAX + 1];
 };
 
@@ -185,8 +188,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         for (int b = lane; b < a.B; b += 32) {
             int len = __ldcg(a.pos + b) + 1;
             len = len < 1 ? 1 : (len > a.max_len ? a.max_len : len);
+            const int lo = sparse_first(a.sp, len - 1);
             wk.len[b] = len;
-            wk.nch[b] = (len + FT_CHUNK - 1) / FT_CHUNK;
+            wk.lo[b] = lo;
+            wk.c0[b] = lo / FT_CHUNK;
+            wk.nch[b] = (len + FT_CHUNK - 1) / FT_CHUNK - lo / FT_CHUNK;
         }
         __syncwarp();
         if (lane == 0) {
@@ -226,7 +232,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 const uint32_t st = ring + s * FT_STAGE;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
-                    int p0 = cu.ch * FT_CHUNK + h * 64;
+                    int p0 = (wk.c0[cu.b] + cu.ch) * FT_CHUNK + h * 64;
                     if (p0 >= wk.len[cu.b]) p0 = 0;  // past the end: any valid page (masked later)
                     const int page = __ldg(a.page_table + (size_t)cu.b * a.max_pages + p0 / a.page_size);
                     const int row = (page * a.n_kv + cu.g) * a.page_size + (p0 % a.page_size);
@@ -416,8 +422,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             ft_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[i & 1]);
-            const int n_valid = min(FT_CHUNK, len - ch * FT_CHUNK);
-            const bool valid = t < n_valid;
+            const int base = (wk.c0[b] + ch) * FT_CHUNK;  // position of TMEM row 0
+            const int n_valid = min(FT_CHUNK, len - base);
+            const bool past_end = t >= n_valid;
+            const bool valid = !past_end && base + t >= wk.lo[b];
             float sc[FT_GMAX];
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++) {
@@ -446,7 +454,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 *reinterpret_cast<__half*>(p2p + rh * 128 + ((((pcol >> 3) ^ (rh & 7))) << 4)) = ph;
                 *reinterpret_cast<__half*>(p2p + rl * 128 + ((((pcol >> 3) ^ (rl & 7))) << 4)) = pl;
             }
-            if (n_valid < FT_CHUNK && !valid) {
+            if (n_valid < FT_CHUNK && past_end) {
                 // rows past the sequence end hold whatever the cache had (possibly NaN bit patterns):
                 // zero them so that 0 x garbage cannot reach the product
                 mbar_wait(&full[sst], fpar);  // order after the TMA's writes to this stage
@@ -613,7 +621,7 @@ bool flash_decode_tc_supported(int kvdtype, int head_dim, int n_heads, int n_kv,
 int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages,
                          const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                          int n_heads, int n_kv, int max_len, float* out, void* workspace, size_t workspace_bytes,
-                         int* status, cudaStream_t st) {
+                         int* status, cudaStream_t st, const SparseMask* sparse) {
     if (!flash_decode_tc_supported(VSL_F16, FT_HD, n_heads, n_kv, B, page_size))
         return set_error(VSL_ERR_UNSUPPORTED, "flash_decode_tc: heads %d/%d B %d page %d", n_heads, n_kv, B, page_size);
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace || max_len <= 0 ||
@@ -645,6 +653,12 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
     w += (size_t)grid * 2 * FT_GMAX * 2 * 4;
     a.counters = reinterpret_cast<int*>(w);
     a.status = status;
+    if (sparse && sparse->min_len > 0) {
+        if (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0)
+            return set_error(VSL_ERR_INVALID, "flash_decode_tc: sparse mask window %d, global %d, block %d",
+                             sparse->window, sparse->global_tokens, sparse->block);
+        a.sp = *sparse;
+    }
     // instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A/B f16 (0), both K-major,
     // N >> 3 in bits 17-22, M >> 4 in bits 24-28
     a.idesc = (1u << 4) | ((uint32_t)(FT_N >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -685,5 +699,17 @@ extern "C" int vsl_flash_decode_tc(const float* q, const void* k_cache, const vo
                                    size_t workspace_bytes, void* stream) {
     if (head_dim != FT_HD) return set_error(VSL_ERR_UNSUPPORTED, "flash_decode_tc: head_dim %d (128 only)", head_dim);
     return flash_decode_tc_impl(q, k_cache, v_cache, n_pages, page_table, max_pages, page_size, pos, B, n_heads, n_kv,
-                                max_len, out, workspace, workspace_bytes, nullptr, (cudaStream_t)stream);
+                                max_len, out, workspace, workspace_bytes, nullptr, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int vsl_flash_decode_tc_sparse(const float* q, const void* k_cache, const void* v_cache, int n_pages,
+                                          const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                          int B, int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                                          void* workspace, size_t workspace_bytes, const vsl_sparse_mask* mask,
+                                          void* stream) {
+    if (head_dim != FT_HD) return set_error(VSL_ERR_UNSUPPORTED, "flash_decode_tc: head_dim %d (128 only)", head_dim);
+    SparseMask m = {};
+    if (mask && mask->min_len > 0) m = SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
+    return flash_decode_tc_impl(q, k_cache, v_cache, n_pages, page_table, max_pages, page_size, pos, B, n_heads, n_kv,
+                                max_len, out, workspace, workspace_bytes, nullptr, (cudaStream_t)stream, &m);
 }

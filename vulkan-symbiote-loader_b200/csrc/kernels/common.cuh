@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include "../../../include/vsl.h"
+#include "sparse_mask.h"
 
 namespace vsl {
 

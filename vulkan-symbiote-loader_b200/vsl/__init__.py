@@ -38,12 +38,19 @@ class ModelConfig(C.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class SparseMask(C.Structure):
+    """vsl_sparse_mask: the reference's long-context window (min_len 0: dense)."""
+    _fields_ = [("min_len", C.c_int), ("window", C.c_int), ("global_tokens", C.c_int), ("block", C.c_int)]
+
+
 class EngineOptions(C.Structure):
     _fields_ = [("device", C.c_int), ("max_batch", C.c_int), ("max_seq", C.c_int), ("kv_dtype", C.c_int),
                 ("page_size", C.c_int), ("split_len", C.c_int), ("tp_rank", C.c_int), ("tp_size", C.c_int),
                 ("nccl_id", C.c_void_p), ("vram_budget_gb", C.c_double), ("use_graph", C.c_int),
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
-                ("use_p2p", C.c_int), ("legacy_q4", C.c_int), ("nccl_timeout_ms", C.c_int)]
+                ("use_p2p", C.c_int), ("legacy_q4", C.c_int), ("sparse_min_len", C.c_int),
+                ("sparse_window", C.c_int), ("sparse_global", C.c_int), ("sparse_block", C.c_int),
+                ("nccl_timeout_ms", C.c_int)]
 
 
 _lib = None
@@ -115,6 +122,10 @@ def lib() -> C.CDLL:
         "vsl_p2p_buffer_size": (i32, [i32, sz, C.POINTER(sz)]),
         "vsl_p2p_allreduce": (i32, [C.POINTER(vp), i32, i32, sz, vp, i32, i32, vp, vp, u64, vp]),
         "vsl_engine_inject_status": (i32, [vp, i32]),
+        "vsl_flash_decode_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, sz,
+                                          C.POINTER(SparseMask), vp]),
+        "vsl_flash_decode_tc_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp, vp, sz,
+                                             C.POINTER(SparseMask), vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -264,10 +275,17 @@ def flash_decode_workspace_size(B, n_heads, n_kv, head_dim, max_len, split_len) 
 
 
 def flash_decode(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads, n_kv, head_dim,
-                 max_len, split_len, out, workspace, workspace_bytes, stream=0):
-    check(lib().vsl_flash_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), kvdtype, _ptr(page_table), max_pages,
-                                 page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, split_len, _ptr(out),
-                                 _ptr(workspace), workspace_bytes, stream))
+                 max_len, split_len, out, workspace, workspace_bytes, stream=0, sparse=None):
+    """sparse: None (dense) or (min_len, window, global_tokens, block) -> vsl_flash_decode_sparse."""
+    if sparse is None:
+        check(lib().vsl_flash_decode(_ptr(q), _ptr(k_cache), _ptr(v_cache), kvdtype, _ptr(page_table), max_pages,
+                                     page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, split_len, _ptr(out),
+                                     _ptr(workspace), workspace_bytes, stream))
+        return
+    m = SparseMask(*sparse)
+    check(lib().vsl_flash_decode_sparse(_ptr(q), _ptr(k_cache), _ptr(v_cache), kvdtype, _ptr(page_table), max_pages,
+                                        page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, split_len, _ptr(out),
+                                        _ptr(workspace), workspace_bytes, C.byref(m), stream))
 
 
 def flash_decode_tc_workspace_size(B, n_kv) -> int:
@@ -277,10 +295,17 @@ def flash_decode_tc_workspace_size(B, n_kv) -> int:
 
 
 def flash_decode_tc(q, k_cache, v_cache, n_pages, page_table, max_pages, page_size, pos, B, n_heads, n_kv, head_dim,
-                    max_len, out, workspace, workspace_bytes, stream=0):
-    check(lib().vsl_flash_decode_tc(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table), max_pages,
-                                    page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, _ptr(out),
-                                    _ptr(workspace), workspace_bytes, stream))
+                    max_len, out, workspace, workspace_bytes, stream=0, sparse=None):
+    """sparse: None (dense) or (min_len, window, global_tokens, block) -> vsl_flash_decode_tc_sparse."""
+    if sparse is None:
+        check(lib().vsl_flash_decode_tc(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table), max_pages,
+                                        page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, _ptr(out),
+                                        _ptr(workspace), workspace_bytes, stream))
+        return
+    m = SparseMask(*sparse)
+    check(lib().vsl_flash_decode_tc_sparse(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table),
+                                           max_pages, page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len,
+                                           _ptr(out), _ptr(workspace), workspace_bytes, C.byref(m), stream))
 
 
 def lm_head_sample(wdtype, W, V_local, K, x, norm_w, eps, B, logits, slots, vocab_offset=0, temperature=0.0,
