@@ -30,6 +30,11 @@ enum class LogLevel { DEBUG = 0, INFO = 1, WARNING = 2, ERROR = 3, FATAL = 4 };
 struct MemoryConfig {
     float vram_budget_gb = 4.0f;
     float ram_budget_gb = 16.0f;
+    // Parsed and saved for compatibility; the engine does not use it. Layers over the budget
+    // stream through two HBM slots (the copy of layer l + 1 overlaps the compute of layer l),
+    // which already keeps the host link busy (0.999 of the measured pinned copy bandwidth for the
+    // 70B model under a 64 GB cap); each deeper slot would take a layer's HBM from the resident
+    // set and add that layer to the bytes streamed per token.
     uint32 prefetch_lookahead = 3;
     float eviction_aggression = 0.7f;
     bool enable_compression = true;
@@ -47,6 +52,8 @@ struct PerformanceConfig {
     uint32 workgroup_size_z = 1;
     bool use_subgroup_ops = true;
     uint32 subgroup_size = 32;
+    // Parsed and saved for compatibility; the engine does not use it: weights keep their stored
+    // type (fp16 / bf16 / fp32 / block-quantized) and every dot product accumulates in fp32.
     bool use_fp16_math = true;
     float scale_factor = 1.0f;
     uint32 thread_pool_size = 0;

@@ -174,8 +174,9 @@ def test_stop_ids_and_bounds():
         stop = full[10]
         cut = e.generate([5, 6, 7], 40, stop_ids=[stop])
         assert cut == full[:full.index(stop) + 1]
+        assert len(e.generate([5, 6, 7], 62)) == 62  # 3 + 61 positions: the last id takes none
         with pytest.raises(vsl.VslError) as err:
-            e.generate([5, 6, 7], 62)
+            e.generate([5, 6, 7], 63)
         assert err.value.code == -5
         e.reset()
         e.run(64)

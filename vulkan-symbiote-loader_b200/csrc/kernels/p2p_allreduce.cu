@@ -20,7 +20,9 @@
 // each does after finishing k on its stream), so a slot is never overwritten while still read.
 // A CTA whose wait times out still advances its epoch, so this rank's counters stay equal to
 // those of the ranks whose flags arrived; its chunk is left unreduced and the sticky status
-// reports it.
+// reports it. Once the status holds VSL_ERR_TIMEOUT (an earlier exchange of the step gave up)
+// the call only advances its epochs: the ranks are out of step, the engine reports the failure
+// after the step, and each later exchange would otherwise wait out its bound again.
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -43,9 +45,17 @@ __global__ void __launch_bounds__(AR_THREADS) vsl_p2p_allreduce_kernel(void* dat
     pdl_launch_dependents();
     const int t = threadIdx.x, c = blockIdx.x;
     const int N = peers.n, rank = peers.rank;
-    if (t == 0) s_epoch = peers.epoch[c] + 1;
+    __shared__ int s_failed;
+    if (t == 0) {
+        s_epoch = peers.epoch[c] + 1;
+        s_failed = peers.status && *(volatile int*)peers.status == VSL_ERR_TIMEOUT;
+    }
     __syncthreads();
     const unsigned long long epoch = s_epoch;
+    if (s_failed) {
+        if (t == 0) peers.epoch[c] = epoch;
+        return;
+    }
     const int par = (int)(epoch & 1);
     constexpr int ES = OP == 0 ? 4 : 8;
     const size_t bytes = (size_t)n * ES;
