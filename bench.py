@@ -69,6 +69,12 @@ def parse():
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
+    ap.add_argument("--split-len", type=int, default=0,
+                    help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
+    ap.add_argument("--timeline", action="store_true",
+                    help="per-CTA timeline of --steps decode steps of the 7B workload with the trace build "
+                         "(lib/libvsl_trace.so, `make -C vulkan-symbiote-loader_b200 trace`): one JSON line per "
+                         "rank with the time per kernel role; not a benchmark number")
     return ap.parse_args()
 
 
@@ -342,7 +348,7 @@ def run_ours(args):
     nccl_id = vdist.nccl_id(dist)
     t0 = time.perf_counter()
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=B, max_seq=max_seq,
-                               tp_rank=rank, tp_size=ws, nccl_id=nccl_id)
+                               tp_rank=rank, tp_size=ws, nccl_id=nccl_id, split_len=args.split_len)
     load_s = time.perf_counter() - t0
     if big:
         # 8192 positions of seeded N(0, 1) keys/values per sequence written straight into the
@@ -700,8 +706,130 @@ def run_profile_case(args):
     return 0
 
 
+ROLE_ORDER = ("qkv", "attention", "o", "allreduce", "gate_up", "down", "lm_head", "argmax_exchange", "other")
+
+
+def run_timeline(args):
+    """Where a decode step's time goes: every CTA of every kernel stamps %globaltimer at entry, at
+    its release from griddepcontrol.wait and at exit (trace build). Per kernel role (QKV, attention,
+    O, all-reduce, gate/up, down, lm_head) the line gives, averaged over the layers and steps:
+    span (end of the previous launch's last CTA to end of this launch's last CTA), release (end of
+    the previous launch to the first CTA's release), ramp (first to last release), tail (median
+    CTA end to last CTA end) and the median CTA duration after its release, in microseconds, plus
+    the launch's weight bytes over its span."""
+    os.environ["VSL_LIBRARY"] = "trace"
+    import numpy as np
+    import torch
+
+    import vsl
+    from vsl import dist as vdist
+    from vsl import synth
+    assert vsl.LIB_PATH.endswith("libvsl_trace.so"), vsl.LIB_PATH
+    ws, rank, local = vdist.env()
+    dist = vdist.init(ws)
+    torch.cuda.set_device(local)
+    cfg = dict(CONFIG_7B)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    max_seq = (PROMPT + args.warmup + args.steps + 8 + 63) // 64 * 64
+    nid = vdist.nccl_id(dist)
+    eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_seq=max_seq, tp_rank=rank, tp_size=ws,
+                               nccl_id=nid, split_len=args.split_len)
+    eng.prefill(synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"]))
+    eng.run(args.warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    vsl.trace_records(reset=True)
+    eng.run(args.steps)
+    torch.cuda.synchronize()
+    recs = vsl.trace_records(reset=True)
+    if eng.device_status() != 0:
+        raise SystemExit(f"device status {eng.device_status()}")
+    eng.close()
+    d, hd, F = cfg["d_model"], cfg["head_dim"], cfg["ffn"] // ws
+    nh, nkv = cfg["n_heads"] // ws, cfg["n_kv_heads"] // ws
+    wbytes = {"qkv": (nh + 2 * nkv) * hd * d * 2, "o": d * nh * hd * 2, "gate_up": 2 * F * d * 2, "down": d * F * 2,
+              "lm_head": cfg["vocab"] // ws * d * 2}
+    K = args.steps
+    launches = []  # (replay, id, role-tag, records)
+    for lid in np.unique(recs["id"]):
+        r = recs[recs["id"] == lid]
+        r = r[np.argsort(r["t0"], kind="stable")]
+        n = len(r) // K
+        if n * K != len(r):
+            continue
+        for k in range(K):
+            launches.append((k, int(lid), r[k * n:(k + 1) * n]))
+    roles = {}
+    step_us = []
+    for k in range(K):
+        seq = sorted([x for x in launches if x[0] == k], key=lambda x: int(x[2]["t1"].min()))
+        prev_end, after_attn = None, False
+        step_us.append((max(int(x[2]["t2"].max()) for x in seq) - min(int(x[2]["t0"].min()) for x in seq)) / 1e3)
+        for _, _, r in seq:
+            tag = int(r["tag"].max())
+            if 900 <= tag < 1000 and (r["tag"] != 900).any():
+                r = r[r["tag"] != 900]  # empty splits only prefetch; their stamps have no release
+            if 900 <= tag < 1000:
+                role = "attention"
+                after_attn = True
+            elif tag == 1001:
+                role = "argmax_exchange"
+            elif tag >= 1000:
+                role = "allreduce"
+            else:
+                ek, norm = tag // 100, (tag // 10) % 10
+                if ek == 3:
+                    role = "qkv"
+                elif ek == 2:
+                    role = "gate_up"
+                elif ek == 4:
+                    role = "lm_head"
+                elif ek in (0, 1) and not norm:
+                    role = "o" if after_attn else "down"
+                    after_attn = False
+                else:
+                    role = "other"
+            t2max, t1min = int(r["t2"].max()), int(r["t1"].min())
+            a = roles.setdefault(role, {"launches": 0, "span": 0.0, "release": 0.0, "ramp": 0.0, "tail": 0.0,
+                                        "cta_us": 0.0, "ctas": 0})
+            a["launches"] += 1
+            if prev_end is not None:
+                a["span"] += (t2max - prev_end) / 1e3
+                a["release"] += (t1min - prev_end) / 1e3
+            a["ramp"] += (int(r["t1"].max()) - t1min) / 1e3
+            a["tail"] += (t2max - float(np.median(r["t2"]))) / 1e3
+            a["cta_us"] += float(np.median(r["t2"] - r["t1"])) / 1e3
+            a["ctas"] += len(r)
+            prev_end = t2max
+    out = {}
+    for role in ROLE_ORDER:
+        if role not in roles:
+            continue
+        a = roles[role]
+        c = a["launches"]
+        e = {"per_step": round(c / K, 2), "span_us": round(a["span"] / c, 2), "release_us": round(a["release"] / c, 2),
+             "ramp_us": round(a["ramp"] / c, 2), "tail_us": round(a["tail"] / c, 2),
+             "cta_us_p50": round(a["cta_us"] / c, 2), "ctas": round(a["ctas"] / c, 1)}
+        if role in wbytes:
+            e["weight_gbs_over_span"] = round(wbytes[role] / (a["span"] / c * 1e-6) / 1e9, 1)
+        out[role] = e
+    line = {"timeline": "decode step, 7B fp16 bs1" + (f" ({cfg['n_layers']} layers)" if args.layers else ""),
+            "tp": ws, "rank": rank, "steps": K, "step_us_p50": round(float(np.median(step_us)), 1),
+            "step_span_note": "first CTA entry to last CTA exit of the traced kernels in one graph replay",
+            "roles": out, "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     args = parse()
+    if args.timeline:
+        return run_timeline(args)
     if args.profile_case:
         return run_profile_case(args)
     if args.sweep:

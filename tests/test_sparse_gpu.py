@@ -107,12 +107,12 @@ def test_tc_sparse_matches_oracle_past_8192():
 
 
 def test_engine_sparse_attention_teacher_forced():
-    cfg = dict(n_layers=2, d_model=1024, n_heads=16, n_kv_heads=4, head_dim=128, ffn=2816, vocab=4096,
+    cfg = dict(n_layers=2, d_model=1024, n_heads=8, n_kv_heads=2, head_dim=128, ffn=2816, vocab=4096,
                rope_theta=500000.0, rms_eps=1e-5, wdtype=vsl.BF16)
     batch, prefill, n_steps, seed = 3, 8190, 5, 13  # steps cross the switch at 8192 positions
     max_seq = 8320
     e = vsl.Engine.synthetic(cfg, seed=seed, max_batch=batch, max_seq=max_seq, sparse_min_len=8192)
-    orc = O.Model.synthetic(n_layers=2, d=1024, n_heads=16, n_kv=4, ffn=2816, vocab=4096, rope_theta=500000.0,
+    orc = O.Model.synthetic(n_layers=2, d=1024, n_heads=8, n_kv=2, ffn=2816, vocab=4096, rope_theta=500000.0,
                             wdtype=O.BF16, kvdtype=O.F16, max_seq=max_seq, max_batch=batch, seed=seed)
     orc.set_sparse(8192, 512, 16, 1024)
     e.fill_kv_synthetic(5, 1.0, prefill, batch)

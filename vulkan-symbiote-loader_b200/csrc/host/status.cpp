@@ -1,6 +1,8 @@
 #include "status.h"
 
+#include <atomic>
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 
 namespace vsl {
@@ -16,6 +18,14 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 void clear_error() { g_msg[0] = 0; }
+
+#ifdef VSL_TRACE
+// Launch ids of the trace build's per-CTA timeline (csrc/kernels/trace.cuh).
+uint32_t trace_next_id() {
+    static std::atomic<uint32_t> n{0};
+    return ++n;
+}
+#endif
 
 }  // namespace vsl
 

@@ -20,6 +20,9 @@
 
 #include "common.cuh"
 #include "launch.cuh"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(attention)
 
 namespace vsl {
 
@@ -44,6 +47,7 @@ struct FdParams {
     size_t pf_bytes;
     int wait_first;      // rows share one sequence's pages (prompt chunk): no cache read before the wait
     SparseMask sp;       // long-context sparse mask (sp.min_len 0: dense)
+    unsigned trace_id;   // launch id of the trace build (unused otherwise)
 };
 
 template <typename KT> struct KvVec;
@@ -91,6 +95,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     float* l_s = m_s + FD_GMAX;
     float* a_s = l_s + FD_GMAX;
     __shared__ int is_last;
+    VSL_TRACE_ENTRY();
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -116,13 +121,17 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
             const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
             prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
         }
+        VSL_TRACE_EXIT(p.trace_id, 900);
         return;
     }
     const int t_end = min(len, (split + 1) * p.split_len);
     const int n_active = (len + p.split_len - 1) / p.split_len - s_first;  // splits that take part
     const int n_chunks = (t_end - t_begin + FD_CHUNK - 1) / FD_CHUNK;
     const int new_row = pos - t_begin;  // row of the freshly appended position, if in this split
-    if (p.wait_first) pdl_wait();
+    if (p.wait_first) {
+        pdl_wait();
+        VSL_TRACE_RELEASED();
+    }
 
     auto chunk_ptrs = [&](int ci, const KT*& kg, const KT*& vg) {
         const int t0 = t_begin + ci * FD_CHUNK;  // t0 % 64 == 0 and page_size % 64 == 0: one page
@@ -157,6 +166,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     }
 
     pdl_wait();
+    if (!p.wait_first) VSL_TRACE_RELEASED();
     pdl_launch_dependents();
 
     // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done
@@ -292,6 +302,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
                 if (e < HD) p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = o_acc[j][i] / l_s[j];
             }
         }
+        VSL_TRACE_EXIT(p.trace_id, 901);
         return;
     }
     __threadfence();
@@ -301,7 +312,10 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         is_last = prev == n_active - 1;
     }
     __syncthreads();
-    if (!is_last) return;
+    if (!is_last) {
+        VSL_TRACE_EXIT(p.trace_id, 902);
+        return;
+    }
     __threadfence();
     // ---- combine the active splits of every head in this group ----
     // The split statistics and weights are staged in shared memory by all threads at once (one
@@ -359,6 +373,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         __syncthreads();  // red / cw reused by the next head
     }
     if (tid == 0) p.counters[(size_t)b * p.n_kv + g] = 0;
+    VSL_TRACE_EXIT(p.trace_id, 903);
 }
 
 static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
@@ -390,7 +405,9 @@ static int launch_fd(const FdParams& p, cudaStream_t st) {
         configured_dev = dev;
     }
     dim3 grid(p.n_splits, p.n_kv, p.B);
-    return launch_status(launch_k(kern, grid, dim3(FD_THREADS), smem, st, p), "flash_decode launch");
+    FdParams pt = p;
+    pt.trace_id = VSL_TRACE_ID();
+    return launch_status(launch_k(kern, grid, dim3(FD_THREADS), smem, st, pt), "flash_decode launch");
 }
 
 int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,

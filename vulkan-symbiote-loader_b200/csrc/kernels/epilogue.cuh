@@ -38,6 +38,7 @@ struct GemvParams {
     // once its own rows are done, filling the tail of this launch
     const void* pf_ptr;
     size_t pf_bytes;
+    unsigned trace_id;  // launch id of the trace build (unused otherwise)
 };
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }

@@ -22,15 +22,24 @@
 #include "quant_layout.h"
 #include "tc_gemm.h"
 #include "launch.cuh"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(gemv)
 
 namespace vsl {
 
 constexpr int GEMV_THREADS = 256;
+
+static GemvParams traced(GemvParams p) {
+    p.trace_id = VSL_TRACE_ID();
+    return p;
+}
 constexpr int GEMV_U = 8;
 constexpr int GEMV_L2_HEAD = 96 * 1024;
 
 template <typename WT, int NB, int EK, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvParams p) {
+    VSL_TRACE_ENTRY();
     extern __shared__ __align__(16) float xs[];  // [NB][K] fp32 activations
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = WTraits<WT>::VEC;
@@ -58,6 +67,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvPar
     }
 
     pdl_wait();
+    VSL_TRACE_RELEASED();
     pdl_launch_dependents();
 
     // ---- stage activations (RMS-normalised if requested) ----
@@ -187,6 +197,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_kernel(const GemvPar
             if (lane == b && b < B && best[b] != 0ull) atomicMax(p.slots + b, best[b]);
     }
     if (p.pf_ptr && lane == 0) prefetch_share(p.pf_ptr, p.pf_bytes, blockIdx.x, gridDim.x, warp, NW);
+    VSL_TRACE_EXIT(p.trace_id, (unsigned)(EK * 100 + (NORM ? 10 : 0) + NB));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -279,6 +290,7 @@ __host__ __device__ constexpr int q_stage_floats(int K) {
 
 template <int QT, int NB, int EK, bool NORM>
 __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_q_kernel(const GemvParams p) {
+    VSL_TRACE_ENTRY();
     extern __shared__ __align__(16) float xs[];  // [NB][q_stage_floats(K)]
     __shared__ float red[NB][GEMV_THREADS / 32];
     constexpr int VEC = QTraits<QT>::VEC;
@@ -306,6 +318,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_q_kernel(const GemvP
     }
 
     pdl_wait();
+    VSL_TRACE_RELEASED();
     pdl_launch_dependents();
 
     const int B = p.B;
@@ -455,6 +468,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 2) vsl_gemv_q_kernel(const GemvP
             if (lane == b && b < B && best[b] != 0ull) atomicMax(p.slots + b, best[b]);
     }
     if (p.pf_ptr && lane == 0) prefetch_share(p.pf_ptr, p.pf_bytes, blockIdx.x, gridDim.x, warp, NW);
+    VSL_TRACE_EXIT(p.trace_id, (unsigned)(EK * 100 + (NORM ? 10 : 0) + NB));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -499,7 +513,7 @@ static int launch_gemv_t(const GemvParams& p, cudaStream_t st) {
     const int max_grid = (n_units + nw - 1) / nw;
     if (grid > max_grid) grid = max_grid;
     if (grid < 1) grid = 1;
-    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
+    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, traced(p)), "gemv launch");
 }
 
 template <int QT, int NB, int EK, bool NORM>
@@ -527,7 +541,7 @@ static int launch_gemv_q_t(const GemvParams& p, cudaStream_t st) {
     const int max_grid = (n_units + nw - 1) / nw;
     if (grid > max_grid) grid = max_grid;
     if (grid < 1) grid = 1;
-    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, p), "gemv launch");
+    return launch_status(launch_k(kern, dim3(grid), dim3(GEMV_THREADS), smem, st, traced(p)), "gemv launch");
 }
 
 template <int QT, int EK, bool NORM>

@@ -28,6 +28,9 @@
 #include "common.cuh"
 #include "launch.cuh"
 #include "p2p_allreduce.h"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(p2p)
 
 namespace vsl {
 
@@ -41,7 +44,9 @@ __device__ __forceinline__ unsigned long long* ar_flag(void* base, const P2pPeer
 template <int OP>  // 0: fp32 sum, 1: u64 max
 __global__ void __launch_bounds__(AR_THREADS) vsl_p2p_allreduce_kernel(void* data, int n, const P2pPeers peers) {
     __shared__ unsigned long long s_epoch;
+    VSL_TRACE_ENTRY();
     pdl_wait();
+    VSL_TRACE_RELEASED();
     pdl_launch_dependents();
     const int t = threadIdx.x, c = blockIdx.x;
     const int N = peers.n, rank = peers.rank;
@@ -54,6 +59,7 @@ __global__ void __launch_bounds__(AR_THREADS) vsl_p2p_allreduce_kernel(void* dat
     const unsigned long long epoch = s_epoch;
     if (s_failed) {
         if (t == 0) peers.epoch[c] = epoch;
+        VSL_TRACE_EXIT(peers.trace_id, 1002);
         return;
     }
     const int par = (int)(epoch & 1);
@@ -99,6 +105,7 @@ __global__ void __launch_bounds__(AR_THREADS) vsl_p2p_allreduce_kernel(void* dat
             set_status(peers.status, VSL_ERR_TIMEOUT);
             peers.epoch[c] = epoch;
         }
+        VSL_TRACE_EXIT(peers.trace_id, 1002);
         return;
     }
     __threadfence();
@@ -133,6 +140,7 @@ __global__ void __launch_bounds__(AR_THREADS) vsl_p2p_allreduce_kernel(void* dat
         }
     }
     if (t == 0) peers.epoch[c] = epoch;
+    VSL_TRACE_EXIT(peers.trace_id, 1000 + OP);
 }
 
 int p2p_allreduce(const P2pPeers& peers, void* data, int n, int op, cudaStream_t st) {
@@ -147,10 +155,12 @@ int p2p_allreduce(const P2pPeers& peers, void* data, int n, int op, cudaStream_t
     const size_t chunks = ((size_t)n * es + peers.chunk_bytes - 1) / peers.chunk_bytes;
     if (chunks > (size_t)P2P_MAX_CHUNKS)
         return set_error(VSL_ERR_INVALID, "p2p_allreduce: %zu chunks exceed %d", chunks, P2P_MAX_CHUNKS);
+    P2pPeers pt = peers;
+    pt.trace_id = VSL_TRACE_ID();
     cudaError_t e = op == 0 ? launch_k(vsl_p2p_allreduce_kernel<0>, dim3((unsigned)chunks), dim3(AR_THREADS), 0, st,
-                                       data, n, peers)
+                                       data, n, pt)
                             : launch_k(vsl_p2p_allreduce_kernel<1>, dim3((unsigned)chunks), dim3(AR_THREADS), 0, st,
-                                       data, n, peers);
+                                       data, n, pt);
     return launch_status(e, "p2p allreduce launch");
 }
 

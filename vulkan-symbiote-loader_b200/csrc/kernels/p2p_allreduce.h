@@ -23,6 +23,7 @@ struct P2pPeers {
     unsigned long long* epoch;   // [P2P_MAX_CHUNKS] device call counters of this rank, one per chunk
     int* status;                 // VSL_ERR_TIMEOUT when a peer's message never arrives
     unsigned long long wait_ns;  // bound of the wait for the peers' flags
+    unsigned trace_id;           // launch id of the trace build (unused otherwise)
 };
 
 // op 0: in-place fp32 sum of n floats; op 1: in-place max of n u64 keys. One launch on `st`.

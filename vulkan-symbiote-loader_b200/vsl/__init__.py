@@ -13,7 +13,9 @@ import re
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
-LIB_PATH = os.path.join(PKG, "lib", "libvsl.so")
+# VSL_LIBRARY=trace selects the trace build (lib/libvsl_trace.so, `make trace`): the same kernels
+# stamping a per-CTA timeline, read with trace_records()
+LIB_PATH = os.path.join(PKG, "lib", "libvsl_trace.so" if os.environ.get("VSL_LIBRARY") == "trace" else "libvsl.so")
 HEADER = os.path.join(os.path.dirname(PKG), "include", "vsl.h")
 
 F32, F16, BF16 = 0, 1, 30
@@ -133,6 +135,30 @@ def lib() -> C.CDLL:
         fn.argtypes = args
     _lib = L
     return L
+
+
+TRACE_UNITS = ("gemv", "attention", "p2p")
+
+
+def trace_records(reset: bool = True):
+    """Per-CTA records of the trace build (id, blk, tag, smid, t0, t1, t2 ns), all units."""
+    import numpy as np
+    rec = np.dtype([("id", "<u4"), ("blk", "<u4"), ("tag", "<u4"), ("smid", "<u4"), ("t0", "<u8"), ("t1", "<u8"),
+                    ("t2", "<u8"), ("pad", "<u8")])
+    L = lib()
+    out = []
+    for unit in TRACE_UNITS:
+        fn = getattr(L, "vsl_trace_read_" + unit, None)
+        if fn is None:
+            raise VslError(-10, "trace_records needs the trace build (VSL_LIBRARY=trace, make trace)")
+        fn.restype = C.c_int
+        fn.argtypes = [C.c_void_p, C.c_uint, C.c_int]
+        buf = np.zeros(1 << 18, rec)
+        n = fn(buf.ctypes.data, buf.size, 1 if reset else 0)
+        if n < 0:
+            raise VslError(-2, f"trace read of {unit} failed ({n})")
+        out.append(buf[:n])
+    return np.concatenate(out)
 
 
 def header_functions() -> list[str]:
