@@ -71,6 +71,8 @@ def parse():
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     ap.add_argument("--split-len", type=int, default=0,
                     help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
+    ap.add_argument("--p2p-chunk", type=int, default=0,
+                    help="bytes per CTA of the peer-memory all-reduce (engine option p2p_chunk_bytes; 0 = automatic)")
     ap.add_argument("--timeline", action="store_true",
                     help="per-CTA timeline of --steps decode steps of the 7B workload with the trace build "
                          "(lib/libvsl_trace.so, `make -C vulkan-symbiote-loader_b200 trace`): one JSON line per "
@@ -348,7 +350,8 @@ def run_ours(args):
     nccl_id = vdist.nccl_id(dist)
     t0 = time.perf_counter()
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=B, max_seq=max_seq,
-                               tp_rank=rank, tp_size=ws, nccl_id=nccl_id, split_len=args.split_len)
+                               tp_rank=rank, tp_size=ws, nccl_id=nccl_id, split_len=args.split_len,
+                               p2p_chunk_bytes=args.p2p_chunk)
     load_s = time.perf_counter() - t0
     if big:
         # 8192 positions of seeded N(0, 1) keys/values per sequence written straight into the
@@ -734,7 +737,7 @@ def run_timeline(args):
     max_seq = (PROMPT + args.warmup + args.steps + 8 + 63) // 64 * 64
     nid = vdist.nccl_id(dist)
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_seq=max_seq, tp_rank=rank, tp_size=ws,
-                               nccl_id=nid, split_len=args.split_len)
+                               nccl_id=nid, split_len=args.split_len, p2p_chunk_bytes=args.p2p_chunk)
     eng.prefill(synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"]))
     eng.run(args.warmup)
     torch.cuda.synchronize()

@@ -219,17 +219,19 @@ VSL_API int vsl_synth_fill(void* dst, int dtype, uint64_t seed, uint64_t tensor_
 
 /* One-shot peer-memory all-reduce of the tensor-parallel engine (it stands where an NCCL
  * all-reduce would follow each row-parallel projection; the reference has no multi-GPU path).
- * Each rank owns a receive buffer of vsl_p2p_buffer_size(n_ranks, cap_bytes) bytes, 256-byte
- * aligned and zero-filled once; bases[r] is rank r's buffer as this rank addresses it (its own
- * buffer, or a CUDA IPC / peer mapping of another GPU's). op 0 sums n fp32 values, op 1 takes the
- * maximum of n uint64 keys, in place on `data` (16-byte aligned, n * element size <= cap_bytes).
- * The message is cut into chunks of at least 1 KB, one CTA each: a CTA stores its chunk into every
- * rank's buffer, raises a flag there, waits up to wait_ns nanoseconds for every rank's flag in its
- * own buffer and sums the chunk's slots in rank order, so all ranks get identical bits. epochs is
- * a zero-filled device array of 64 uint64 call counters (one per chunk) that every call advances,
- * also one that timed out; status (device int, may be NULL) receives VSL_ERR_TIMEOUT when a
- * peer's flag never arrived, and the data are then left partly unreduced. Every rank makes the
- * same sequence of calls with the same n; one launch on `stream`. */
+ * Each rank owns a receive buffer of vsl_p2p_buffer_size(n_ranks, cap_bytes) bytes (cap_bytes a
+ * multiple of 4), 256-byte aligned and zero-filled once; bases[r] is rank r's buffer as this rank
+ * addresses it (its own buffer, or a CUDA IPC / peer mapping of another GPU's). op 0 sums n fp32
+ * values, op 1 takes the maximum of n uint64 keys, in place on `data` (16-byte aligned, n * element
+ * size <= cap_bytes). The message travels as 8-byte words of a 32-bit piece and the call's epoch,
+ * so arrival needs no separate flag or fence. It is cut into chunks of at least 1 KB, one CTA
+ * each: a CTA stores its chunk into every rank's buffer, then waits up to wait_ns nanoseconds for
+ * every rank's words in its own buffer and sums them in rank order, so all ranks get identical
+ * bits. epochs is a zero-filled device array of 64 uint64 call counters (one per chunk) that every
+ * call advances, also one that timed out; status (device int, may be NULL) receives
+ * VSL_ERR_TIMEOUT when a peer's words never arrived, and the data are then left partly unreduced
+ * (a call that finds VSL_ERR_TIMEOUT already in status only advances its epochs). Every rank makes
+ * the same sequence of calls with the same n; one launch on `stream`. */
 VSL_API int vsl_p2p_buffer_size(int n_ranks, size_t cap_bytes, size_t* bytes);
 VSL_API int vsl_p2p_allreduce(void* const* bases, int n_ranks, int rank, size_t cap_bytes, void* data, int n, int op,
                               uint64_t* epochs, int* status, uint64_t wait_ns, void* stream);
@@ -283,6 +285,9 @@ typedef struct {
     int sparse_window;   /* window W (0 = 512)                                               */
     int sparse_global;   /* global tokens G (0 = 16)                                         */
     int sparse_block;    /* block BLK (0 = 1024)                                             */
+    int p2p_chunk_bytes; /* tensor parallel with use_p2p: bytes of the residual all-reduce's message
+                          one CTA moves (0 = automatic: 1 KB chunks, at most 64 per message);
+                          larger values mean fewer, longer CTAs. Same value on every rank.   */
     int nccl_timeout_ms; /* tensor parallel: the longest the host waits for work that involves the
                           other ranks (one call's stream work); past it, or when NCCL reports an
                           asynchronous error, the communicator is aborted, the call returns

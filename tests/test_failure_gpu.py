@@ -1,11 +1,11 @@
 """Failure handling on one GPU without faulting it.
 
 * The peer-memory all-reduce's bounded wait runs out: a 2-rank exchange whose second rank never
-  takes part (its flags are never set) returns VSL_ERR_TIMEOUT in the status word within the
-  wait bound, leaves the message unreduced and still advances every chunk's epoch; the device
-  stays usable, and a following call whose peer message and flags were placed by the host
-  (standing in for a live peer, so no kernel waits on another kernel) completes with the
-  rank-ordered sum, bit for bit.
+  takes part (none of its epoch-tagged words arrive) returns VSL_ERR_TIMEOUT in the status word
+  within the wait bound, leaves the message unreduced and still advances every chunk's epoch; the
+  device stays usable, and a following call whose peer words were placed by the host (standing in
+  for a live peer, so no kernel waits on another kernel) completes with the rank-ordered sum, bit
+  for bit.
 * The engine reports a kernel's sticky status (injected on the host) as the error of the next
   host-facing call, and generate takes exactly max_seq positions (the last sampled token never
   takes a KV position).
@@ -21,17 +21,29 @@ torch = pytest.importorskip("torch")
 import vsl  # noqa: E402
 from vsl import synth  # noqa: E402
 
-CHUNKS = 64  # flag and epoch entries per parity and rank
+CHUNKS = 64  # epoch counters per call at most
 
 
 def _layout(cap_bytes):
-    slot = (cap_bytes + 255) // 256 * 256
-    chunk = max(1024, ((slot + CHUNKS - 1) // CHUNKS + 255) // 256 * 256)
-    return slot, chunk, 2 * 2 * slot  # slot stride, chunk bytes, flag offset (2 ranks)
+    """Slot stride and chunk size (32-bit pieces) of the exchange's receive buffer."""
+    words = cap_bytes // 4
+    slot = ((words + 1) // 2 * 16 + 255) // 256 * 256
+    per = -(-((words + 1) // 2 * 2) // CHUNKS)
+    chunk = max(256, (per + 1) // 2 * 2)
+    return slot, chunk
 
 
-def _flag_index(flag_off, par, r, c):
-    return (flag_off + ((par * 2 + r) * CHUNKS + c) * 8) // 8
+def _tag(epoch):
+    return (epoch & 0x7FFFFFFF) | 0x80000000
+
+
+def _words(pieces_u32, epoch, n_words):
+    """The 8-byte words a rank writes: (piece, tag) pairs, padded to an even count."""
+    m = (n_words + 1) // 2 * 2
+    w = np.zeros(m, np.uint64)
+    w[:n_words] = pieces_u32.astype(np.uint64)
+    w |= np.uint64(_tag(epoch)) << np.uint64(32)
+    return w
 
 
 @pytest.mark.parametrize("op,n", [(0, 4096), (0, 4099), (1, 3)])
@@ -39,24 +51,25 @@ def test_p2p_wait_times_out_then_recovers(op, n):
     dev = torch.device("cuda:0")
     es = 4 if op == 0 else 8
     cap = n * es
-    slot, chunk, flag_off = _layout(cap)
-    nchunks = -(-cap // chunk)
+    slot, chunk = _layout(cap)
+    n_words = cap // 4
+    nchunks = -(-n_words // chunk)
     size = vsl.p2p_buffer_size(2, cap)
-    assert size == flag_off + 2 * 2 * CHUNKS * 8
+    assert size == 2 * 2 * slot
     bufs = [torch.zeros(size // 8, dtype=torch.int64, device=dev) for _ in range(2)]
     assert all(b.data_ptr() % 256 == 0 for b in bufs)
     epochs = torch.zeros(CHUNKS, dtype=torch.int64, device=dev)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     g = torch.Generator(device="cpu").manual_seed(5)
     if op == 0:
-        mine = torch.randn(n, generator=g).to(dev)
-        peer = torch.randn(n, generator=g).to(dev)
+        mine = torch.randn(n, generator=g)
+        peer = torch.randn(n, generator=g)
     else:
-        mine = torch.randint(0, 2**62, (n,), generator=g, dtype=torch.int64).to(dev)
-        peer = torch.randint(0, 2**62, (n,), generator=g, dtype=torch.int64).to(dev)
-    data = torch.zeros(max(n, 4) * es // 4, dtype=torch.int32, device=dev)  # 16-byte aligned storage
+        mine = torch.randint(0, 2**62, (n,), generator=g, dtype=torch.int64)
+        peer = torch.randint(0, 2**62, (n,), generator=g, dtype=torch.int64)
+    data = torch.zeros((n_words + 3) // 4 * 4, dtype=torch.int32, device=dev)  # 16-byte aligned storage
     data_view = data.view(torch.float32 if op == 0 else torch.int64)[:n]
-    data_view.copy_(mine)
+    data_view.copy_(mine.to(dev))
     torch.cuda.synchronize()
 
     # 1. rank 1 never arrives: bounded wait of 50 ms
@@ -68,26 +81,23 @@ def test_p2p_wait_times_out_then_recovers(op, n):
     assert 0.04 < elapsed < 5.0, elapsed
     ep = epochs.cpu().numpy()
     assert (ep[:nchunks] == 1).all() and (ep[nchunks:] == 0).all()
-    assert torch.equal(data_view, mine)  # left unreduced
-    # rank 0's message and flags did reach rank 1's buffer (slot [parity 1][rank 0])
-    b1 = bufs[1].view(torch.uint8)
-    got = b1[(1 * 2 + 0) * slot:(1 * 2 + 0) * slot + cap]
-    assert torch.equal(got, mine.view(torch.uint8)[:cap])
-    fl = bufs[1].cpu().numpy()
-    assert all(fl[_flag_index(flag_off, 1, 0, c)] == 1 for c in range(nchunks))
+    assert torch.equal(data_view.cpu(), mine)  # left unreduced: no word of rank 1 arrived
+    # rank 0's message reached rank 1's buffer (slot [parity 1][rank 0]) as (piece, epoch) words
+    pieces = mine.numpy().view(np.uint32)[:n_words]
+    m = (n_words + 1) // 2 * 2
+    got = bufs[1].cpu().numpy().view(np.uint64)[(1 * 2 + 0) * slot // 8:(1 * 2 + 0) * slot // 8 + m]
+    assert np.array_equal(got, _words(pieces, 1, n_words))
 
     # 2. the device is still usable; the host stands in for a live rank 1 at epoch 2 (parity 0)
     status.zero_()
-    b0 = bufs[0].view(torch.uint8)
-    b0[(0 * 2 + 1) * slot:(0 * 2 + 1) * slot + cap].copy_(peer.view(torch.uint8)[:cap])
-    for c in range(nchunks):
-        bufs[0][_flag_index(flag_off, 0, 1, c)] = 2
+    w = torch.from_numpy(_words(peer.numpy().view(np.uint32)[:n_words], 2, n_words).view(np.int64))
+    bufs[0][(0 * 2 + 1) * slot // 8:(0 * 2 + 1) * slot // 8 + m].copy_(w.to(dev))
     torch.cuda.synchronize()
     vsl.p2p_allreduce(bufs, 0, cap, data, n, op, epochs, status, wait_ns=1_000_000_000)
     torch.cuda.synchronize()
     assert status.item() == 0
     want = (mine + peer) if op == 0 else torch.maximum(mine, peer)
-    assert torch.equal(data_view, want)  # rank order: own slot first, then rank 1 (fp32 adds)
+    assert torch.equal(data_view.cpu(), want)  # rank order: own piece first, then rank 1 (fp32 adds)
     ep = epochs.cpu().numpy()
     assert (ep[:nchunks] == 2).all() and (ep[nchunks:] == 0).all()
     assert float(torch.ones(8, device=dev).sum()) == 8.0

@@ -238,6 +238,11 @@ int DecodeEngine::setup_p2p() {
                  nccl_, ar_epochs_, status_, stream_));
     RC(p2p_setup(&p2p_s_, &p2p_s_local_, p2p_s_opened_, opt_.tp_rank, opt_.tp_size, opt_.max_batch, 8, nccl_,
                  ar_epochs_ + P2P_MAX_CHUNKS, status_, stream_));
+    if (opt_.p2p_chunk_bytes > 0) {  // the same value on every rank: the layout does not depend on it
+        const int want = (opt_.p2p_chunk_bytes / 4 + 1) / 2 * 2;
+        const int whole = (int)(p2p_x_.slot_bytes / 8);
+        p2p_x_.chunk_words = std::max(p2p_x_.chunk_words, std::min(want, whole));
+    }
     p2p_ready_ = true;
     return VSL_OK;
 }

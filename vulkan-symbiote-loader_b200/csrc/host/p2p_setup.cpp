@@ -47,9 +47,8 @@ static int exchange_wait(ncclComm_t comm, ncclResult_t r, cudaStream_t st) {
 int p2p_setup(P2pPeers* out, void** local, void** opened, int rank, int n, int cap, int elem_bytes, void* comm,
               unsigned long long* epoch, int* status, cudaStream_t st) {
     if (n < 2 || n > P2P_MAX_RANKS) return set_error(VSL_ERR_UNSUPPORTED, "p2p: %d ranks", n);
-    size_t flag_off = 0;
     const size_t cap_bytes = (size_t)cap * elem_bytes;
-    const size_t bytes = p2p_buffer_bytes(n, cap_bytes, &flag_off);
+    const size_t bytes = p2p_buffer_bytes(n, cap_bytes);
     cudaError_t e = cudaMalloc(local, bytes);
     if (e != cudaSuccess) return set_error(VSL_ERR_OOM, "p2p buffer: %s", cudaGetErrorString(e));
     e = cudaMemset(*local, 0, bytes);
@@ -81,8 +80,7 @@ int p2p_setup(P2pPeers* out, void** local, void** opened, int rank, int n, int c
     p.rank = rank;
     p.cap = cap;
     p.slot_bytes = p2p_slot_bytes(cap_bytes);
-    p.chunk_bytes = p2p_chunk_bytes(cap_bytes);
-    p.flag_off = flag_off;
+    p.chunk_words = p2p_chunk_words(cap_bytes);
     p.epoch = epoch;
     p.status = status;
     p.wait_ns = 1000000000ull;  // one second

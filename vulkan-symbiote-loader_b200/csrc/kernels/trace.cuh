@@ -24,7 +24,7 @@ struct TraceRec {
     uint64_t t0, t1, t2;  // entry, release from griddepcontrol.wait, exit (ns)
     uint64_t pad;
 };
-constexpr uint32_t TRACE_CAP = 1u << 18;
+constexpr uint32_t TRACE_CAP = 1u << 20;
 
 __device__ __forceinline__ uint64_t trace_now() {
     uint64_t t;

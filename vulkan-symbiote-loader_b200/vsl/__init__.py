@@ -52,7 +52,7 @@ class EngineOptions(C.Structure):
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
                 ("use_p2p", C.c_int), ("legacy_q4", C.c_int), ("sparse_min_len", C.c_int),
                 ("sparse_window", C.c_int), ("sparse_global", C.c_int), ("sparse_block", C.c_int),
-                ("nccl_timeout_ms", C.c_int)]
+                ("p2p_chunk_bytes", C.c_int), ("nccl_timeout_ms", C.c_int)]
 
 
 _lib = None
@@ -153,7 +153,7 @@ def trace_records(reset: bool = True):
             raise VslError(-10, "trace_records needs the trace build (VSL_LIBRARY=trace, make trace)")
         fn.restype = C.c_int
         fn.argtypes = [C.c_void_p, C.c_uint, C.c_int]
-        buf = np.zeros(1 << 18, rec)
+        buf = np.zeros(1 << 20, rec)
         n = fn(buf.ctypes.data, buf.size, 1 if reset else 0)
         if n < 0:
             raise VslError(-2, f"trace read of {unit} failed ({n})")
