@@ -196,12 +196,15 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     max_pages_ = (opt.max_seq + page_size_ - 1) / page_size_;
     n_pages_ = max_pages_ * opt.max_batch;
     if (opt.split_len > 0) {
-        split_len_ = opt.split_len;
+        split_len_ = opt.split_len;  // fixed splits of split_len positions over max_seq
+        fd_splits_ = 0;
     } else {
-        // about four CTAs per SM over the whole cache at full length
+        // splits of at least 256 positions, sized from each sequence's current length, and about
+        // one CTA per SM over all (sequence, group) pairs when the cache is long: a short cache
+        // takes one split (no combine), a long one spreads over the SMs
         const int groups = opt.max_batch * nkv_l_;
-        int splits = std::max(1, (4 * 148 + groups - 1) / groups);
-        split_len_ = (int)align_up((size_t)((opt.max_seq + splits - 1) / splits), 64);
+        split_len_ = 256;
+        fd_splits_ = std::max(1, std::min((148 + groups - 1) / groups, (opt.max_seq + 255) / 256));
     }
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);
@@ -351,8 +354,7 @@ int DecodeEngine::alloc_buffers() {
     for (auto& it : items) { *it.dst = a; a += align_up(it.bytes, A); }
     status_ = reinterpret_cast<int*>(sampled_ + mb);
 
-    RC(vsl_flash_decode_workspace_size(opt_.max_batch, nh_l_, nkv_l_, c.head_dim, opt_.max_seq, split_len_,
-                                       &fd_ws_bytes_));
+    fd_ws_bytes_ = flash_decode_workspace_bytes(opt_.max_batch, nh_l_, nkv_l_, c.head_dim, fd_grid_splits());
     CK(cudaMalloc(&fd_ws_, fd_ws_bytes_));
     CK(cudaMemset(fd_ws_, 0, fd_ws_bytes_));
 
@@ -917,7 +919,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         else
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
-                                 att_pf, sb.shared_pages, &sparse_));
+                                 att_pf, sb.shared_pages, &sparse_, fd_splits_));
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
         RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
@@ -1029,7 +1031,7 @@ int DecodeEngine::alloc_prefill() {
     pf_slot_ = reinterpret_cast<unsigned long long*>(m + o_slot);
     pf_next_ = reinterpret_cast<int32_t*>(m + o_next);
     CK(cudaMallocHost((void**)&pf_h_, n_int * 4 + 64));
-    RC(vsl_flash_decode_workspace_size(PF_ROWS, nh_l_, nkv_l_, c.head_dim, opt_.max_seq, split_len_, &pf_fd_bytes_));
+    pf_fd_bytes_ = flash_decode_workspace_bytes(PF_ROWS, nh_l_, nkv_l_, c.head_dim, fd_grid_splits());
     CK(cudaMalloc(&pf_fd_ws_, pf_fd_bytes_));
     CK(cudaMemset(pf_fd_ws_, 0, pf_fd_bytes_));
     // prompt chunks: 64 rows of one sequence over the same pages, so the tcgen05-score attention

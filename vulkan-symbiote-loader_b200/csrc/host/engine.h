@@ -163,6 +163,8 @@ private:
     int nh_l_ = 0, nkv_l_ = 0, ff_l_ = 0, v_l_ = 0, v_off_ = 0;
     int kvdtype_ = VSL_F16;
     int page_size_ = 64, max_pages_ = 0, n_pages_ = 0, split_len_ = 64;
+    int fd_splits_ = 0;  // split-K attention: splits per (sequence, group); 0 = max_seq / split_len_
+    int fd_grid_splits() const { return fd_splits_ > 0 ? fd_splits_ : (opt_.max_seq + split_len_ - 1) / split_len_; }
     size_t es_ = 2;  // bytes per weight element of the 16/32-bit types (1 for block-quantized)
     // bytes of a weight row of K elements in device layout (quantized rows include their scales)
     size_t wrow(size_t K) const { return weight_row_bytes(cfg_.wdtype, K); }

@@ -6,13 +6,18 @@
 // h*n_kv/n_heads (attention.comp:92), scores are q.k / sqrt(head_dim), softmax with max
 // subtraction over positions [0, pos], output = probabilities times V.
 //
-// Design: one CTA per (split, kv group, sequence). A split covers split_len positions; a
-// CTA stages 64-position chunks of K and V (one page-contiguous block each) in padded
-// shared memory, computes the scores of all G = n_heads/n_kv query heads of its group from
-// the same staged K (so a KV page is read from HBM once per group, not once per head), and
-// keeps an online softmax (running max / sum, fp32). Splits write (max, sum, partial
-// output) to the workspace; the last CTA of a (sequence, group) to finish -- found with an
-// atomic counter that it resets to zero -- combines them, so one launch does both phases.
+// Design: one CTA per (split, kv group, sequence). A sequence's positions are cut into at most
+// n_splits splits of at least split_min positions, sized from the sequence's current length on the
+// device (a short cache takes one split and no combine; a long one spreads over the n_splits CTAs).
+// A CTA stages 64-position chunks of K and V (one page-contiguous block each) through a ring of
+// shared-memory buffers, computes the scores of all G = n_heads/n_kv query heads of its group from
+// the same staged K (so a KV page is read from HBM once per group, not once per head), and keeps
+// an online softmax (running max / sum, fp32). With 256 threads the scores split each position's
+// dot product into four partial sums and the P.V product splits the positions among two (head_dim
+// 128) or four (head_dim 64) thread groups, combined once at the end in a fixed order. Splits
+// write (max, sum, partial output) to the workspace; the last CTA of a (sequence, group) to
+// finish -- found with an atomic counter that it resets to zero -- combines them, so one launch
+// does both phases.
 #include <cuda_runtime.h>
 #include <math_constants.h>
 
@@ -26,9 +31,10 @@ VSL_TRACE_UNIT(attention)
 
 namespace vsl {
 
-constexpr int FD_THREADS = 128;
+constexpr int FD_THREADS = 256;
 constexpr int FD_CHUNK = 64;  // positions staged per iteration
 constexpr int FD_GMAX = 8;    // query heads per KV group supported
+constexpr int FD_PARTS = 4;   // partial sums per position score
 
 struct FdParams {
     const float* q;
@@ -37,7 +43,10 @@ struct FdParams {
     const int32_t* page_table;
     int max_pages, page_size;
     const int32_t* pos;
-    int B, n_heads, n_kv, split_len, n_splits;
+    int B, n_heads, n_kv;
+    int split_min;   // positions per split at least (a multiple of FD_CHUNK)
+    int n_splits;    // splits per (sequence, group) at most: the grid's x
+    int max_len;     // positions the caller's cache covers
     float scale;
     float* out;
     float* ws_o;   // [B][n_heads][n_splits][HD]
@@ -64,34 +73,49 @@ template <int HD, typename KT>
 __host__ __device__ constexpr int fd_row_elems() {
     return HD + 16 / (int)sizeof(KT);  // one 16-byte pad per row: conflict-free 16-byte reads
 }
+template <typename KT>
+__host__ __device__ constexpr int fd_stages() {
+    return sizeof(KT) == 2 ? 4 : 2;  // chunk buffers in the ring (fp32 rows are twice as large)
+}
 
 template <int HD, typename KT>
 __host__ __device__ constexpr size_t fd_smem_bytes() {
-    return (size_t)4 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunks, double-buffered
-           + (size_t)FD_GMAX * HD * sizeof(float)                      // q
-           + (size_t)2 * FD_GMAX * FD_CHUNK * sizeof(float)             // score partials
-           + (size_t)FD_GMAX * FD_CHUNK * sizeof(float)                 // probabilities
-           + (size_t)4 * FD_GMAX * sizeof(float);                       // m, l, alpha, misc
+    return (size_t)fd_stages<KT>() * 2 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunk ring
+           + (size_t)FD_GMAX * HD * sizeof(float)                                      // q
+           + (size_t)FD_PARTS * FD_GMAX * FD_CHUNK * sizeof(float)                     // score partials
+           + (size_t)FD_GMAX * FD_CHUNK * sizeof(float)                                // probabilities
+           + (size_t)(FD_THREADS / HD) * FD_GMAX * HD * sizeof(float)                  // P.V group partials
+           + (size_t)4 * FD_GMAX * sizeof(float);                                      // m, l, alpha, misc
 }
 
 __device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// wait until at most n (0..3) committed groups are still in flight
+__device__ __forceinline__ void cp_async_wait_upto(int n) {
+    if (n <= 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
+    else if (n == 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else if (n == 2) asm volatile("cp.async.wait_group 2;" ::: "memory");
+    else asm volatile("cp.async.wait_group 3;" ::: "memory");
+}
 
 template <int HD, typename KT>
 __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int STAGES = fd_stages<KT>();
     constexpr int RE = fd_row_elems<HD, KT>();
     constexpr int VEC = KvVec<KT>::VEC;
-    constexpr int VPR = HD / VEC;  // 16-byte vectors per row
-    KT* kv_s = reinterpret_cast<KT*>(smem_raw);  // [2 buffers][K, V][CHUNK][RE]
-    float* q_s = reinterpret_cast<float*>(kv_s + 4 * FD_CHUNK * RE);
-    float* part_s = q_s + FD_GMAX * HD;           // [2][GMAX][CHUNK]
-    float* p_s = part_s + 2 * FD_GMAX * FD_CHUNK;  // [GMAX][CHUNK]
-    float* m_s = p_s + FD_GMAX * FD_CHUNK;         // [GMAX]
+    constexpr int VPR = HD / VEC;             // 16-byte vectors per row
+    constexpr int NGRP = FD_THREADS / HD;     // position groups of the P.V product
+    constexpr int PDIM = HD / FD_PARTS;       // head dimensions per score partial
+    static_assert(PDIM % VEC == 0 && FD_THREADS % HD == 0, "attention tiling");
+    KT* kv_s = reinterpret_cast<KT*>(smem_raw);  // [STAGES][K, V][CHUNK][RE]
+    float* q_s = reinterpret_cast<float*>(kv_s + (size_t)STAGES * 2 * FD_CHUNK * RE);
+    float* part_s = q_s + FD_GMAX * HD;                    // [PARTS][GMAX][CHUNK]
+    float* p_s = part_s + FD_PARTS * FD_GMAX * FD_CHUNK;   // [GMAX][CHUNK]
+    float* ored = p_s + FD_GMAX * FD_CHUNK;                // [NGRP][GMAX][HD]
+    float* m_s = ored + NGRP * FD_GMAX * HD;               // [GMAX]
     float* l_s = m_s + FD_GMAX;
     float* a_s = l_s + FD_GMAX;
     __shared__ int is_last;
@@ -106,15 +130,18 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     // predecessor (the QKV projection) writes q and the key/value row at pos. When the rows are
     // consecutive positions of one sequence (a prompt chunk), the predecessor also wrote the
     // rows below pos, so the kernel waits first (wait_first).
-    // Positions past the page table or the grid's coverage are never read (the QKV kernel
-    // has already flagged such a position in the engine's status word).
+    // Positions past the page table or the caller's cache are never read (the QKV kernel has
+    // already flagged such a position in the engine's status word).
     const int pos = p.pos[b];
-    const int len = min(pos + 1, min(p.max_pages * p.page_size, p.n_splits * p.split_len));
+    const int len = min(pos + 1, min(p.max_pages * p.page_size, p.max_len));
+    // split length for this sequence's current length: at least split_min, at most n_splits splits
+    const int S = max(p.split_min, ((len + p.n_splits - 1) / p.n_splits + FD_CHUNK - 1) / FD_CHUNK * FD_CHUNK);
     // sparse mask: the row attends to [lo, len); splits below lo take no part, the first active
     // split starts at lo's chunk and masks the rows below lo
     const int lo = min(sparse_first(p.sp, pos), len - 1);
-    const int s_first = lo / p.split_len;
-    const int t_begin = split < s_first ? len : max(split * p.split_len, lo & ~(FD_CHUNK - 1));
+    const int s_first = lo / S;
+    const int n_total = (len + S - 1) / S;
+    const int t_begin = (split < s_first || split >= n_total) ? len : max(split * S, lo & ~(FD_CHUNK - 1));
     if (t_begin >= len) {  // empty split: not counted by the combiner; it only prefetches
         if (p.pf_ptr && tid < 32) {
             const int nblk = gridDim.x * gridDim.y * gridDim.z;
@@ -124,8 +151,8 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         VSL_TRACE_EXIT(p.trace_id, 900);
         return;
     }
-    const int t_end = min(len, (split + 1) * p.split_len);
-    const int n_active = (len + p.split_len - 1) / p.split_len - s_first;  // splits that take part
+    const int t_end = min(len, (split + 1) * S);
+    const int n_active = n_total - s_first;  // splits that take part
     const int n_chunks = (t_end - t_begin + FD_CHUNK - 1) / FD_CHUNK;
     const int new_row = pos - t_begin;  // row of the freshly appended position, if in this split
     if (p.wait_first) {
@@ -140,13 +167,13 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         kg = reinterpret_cast<const KT*>(p.k_cache) + base;
         vg = reinterpret_cast<const KT*>(p.v_cache) + base;
     };
-    // stage chunk ci into buffer buf with cp.async; rows equal to `skip` are left for later
-    auto issue = [&](int ci, int buf, int skip) {
+    // stage chunk ci into ring buffer ci % STAGES with cp.async; the row `skip` is left for later
+    auto issue = [&](int ci, int skip) {
         const KT* kg;
         const KT* vg;
         chunk_ptrs(ci, kg, vg);
         const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
-        KT* ks = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
+        KT* ks = kv_s + (size_t)(2 * (ci % STAGES)) * FD_CHUNK * RE;
         KT* vs = ks + FD_CHUNK * RE;
         for (int i = tid; i < n * VPR; i += FD_THREADS) {
             const int r = i / VPR, c = (i % VPR) * VEC;
@@ -157,25 +184,29 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         cp_async_commit();
     };
 
-    issue(0, 0, new_row);
-    if (n_chunks > 1) issue(1, 1, new_row);
+    // every chunk the ring holds is requested before the wait (older cache rows only)
+    const int pre = min(n_chunks, STAGES);
+    for (int ci = 0; ci < pre; ci++) issue(ci, new_row);
+    int issued = pre;
     if (p.pf_ptr && tid < 32) {
         const int nblk = gridDim.x * gridDim.y * gridDim.z;
         const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
         prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
     }
 
-    pdl_wait();
-    if (!p.wait_first) VSL_TRACE_RELEASED();
+    if (!p.wait_first) {
+        pdl_wait();
+        VSL_TRACE_RELEASED();
+    }
     pdl_launch_dependents();
 
     // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done
-    if (new_row >= 0 && new_row < min(n_chunks, 2) * FD_CHUNK) {
+    if (new_row >= 0 && new_row < pre * FD_CHUNK) {
         const int ci = new_row / FD_CHUNK, r = new_row % FD_CHUNK;
         const KT* kg;
         const KT* vg;
         chunk_ptrs(ci, kg, vg);
-        KT* ks = kv_s + (size_t)(2 * ci) * FD_CHUNK * RE;
+        KT* ks = kv_s + (size_t)(2 * (ci % STAGES)) * FD_CHUNK * RE;
         KT* vs = ks + FD_CHUNK * RE;
         for (int i = tid; i < VPR; i += FD_THREADS) {
             *reinterpret_cast<uint4*>(ks + r * RE + i * VEC) = __ldcg(reinterpret_cast<const uint4*>(kg + (size_t)r * HD + i * VEC));
@@ -186,31 +217,28 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     for (int i = tid; i < G * HD; i += FD_THREADS) q_s[i] = __ldcg(p.q + ((size_t)b * p.n_heads + h0) * HD + i);
     if (tid < FD_GMAX) { m_s[tid] = -CUDART_INF_F; l_s[tid] = 0.0f; }
 
-    constexpr int EPT = (HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
-    float o_acc[FD_GMAX][EPT];
+    const int e_own = tid % HD, grp = tid / HD;  // P.V: output element and position group
+    float o_acc[FD_GMAX];
 #pragma unroll
-    for (int j = 0; j < FD_GMAX; j++)
-#pragma unroll
-        for (int i = 0; i < EPT; i++) o_acc[j][i] = 0.0f;
+    for (int j = 0; j < FD_GMAX; j++) o_acc[j] = 0.0f;
 
     for (int ci = 0; ci < n_chunks; ci++) {
-        const int buf = ci & 1;
+        const int buf = ci % STAGES;
         const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
-        if (ci + 1 < n_chunks) cp_async_wait<1>();  // the next chunk may still be in flight
-        else cp_async_wait<0>();
+        cp_async_wait_upto(issued - ci - 1);  // later chunks may still be in flight
         __syncthreads();
         const KT* k_s = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         const KT* v_s = k_s + FD_CHUNK * RE;
-        // partial scores: thread (tt, half) covers half of the head dimension of position tt
+        // partial scores: thread (tt, part) covers a quarter of the head dimension of position tt
         {
-            const int tt = tid & (FD_CHUNK - 1), half = tid / FD_CHUNK;
+            const int tt = tid & (FD_CHUNK - 1), part = tid / FD_CHUNK;
             if (tt < n) {
                 float acc[FD_GMAX];
 #pragma unroll
                 for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
                 const KT* kr = k_s + tt * RE;
 #pragma unroll
-                for (int c = half * (HD / 2); c < (half + 1) * (HD / 2); c += VEC) {
+                for (int c = part * PDIM; c < (part + 1) * PDIM; c += VEC) {
                     float kf[VEC];
                     KvVec<KT>::widen(*reinterpret_cast<const uint4*>(kr + c), kf);
 #pragma unroll
@@ -223,26 +251,31 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
                 }
 #pragma unroll
                 for (int j = 0; j < FD_GMAX; j++)
-                    if (j < G) part_s[(half * FD_GMAX + j) * FD_CHUNK + tt] = acc[j];
+                    if (j < G) part_s[(part * FD_GMAX + j) * FD_CHUNK + tt] = acc[j];
             }
         }
         __syncthreads();
-        // online softmax per head: warp w handles heads w, w+4
+        // online softmax per head: warp j handles head j
+        const int t0 = t_begin + ci * FD_CHUNK;
         for (int j = warp; j < G; j += FD_THREADS / 32) {
             float s0 = -CUDART_INF_F, s1 = -CUDART_INF_F;
-            if (lane < n) s0 = (part_s[j * FD_CHUNK + lane] + part_s[(FD_GMAX + j) * FD_CHUNK + lane]) * p.scale;
-            if (lane + 32 < n)
-                s1 = (part_s[j * FD_CHUNK + lane + 32] + part_s[(FD_GMAX + j) * FD_CHUNK + lane + 32]) * p.scale;
-            if (t_begin + ci * FD_CHUNK < lo) {  // rows below the sparse window's start
-                const int t0 = t_begin + ci * FD_CHUNK;
-                if (t0 + lane < lo) s0 = -CUDART_INF_F;
-                if (t0 + lane + 32 < lo) s1 = -CUDART_INF_F;
+            if (lane < n && t0 + lane >= lo) {
+                float a = 0.0f;
+#pragma unroll
+                for (int q = 0; q < FD_PARTS; q++) a += part_s[(q * FD_GMAX + j) * FD_CHUNK + lane];
+                s0 = a * p.scale;
+            }
+            if (lane + 32 < n && t0 + lane + 32 >= lo) {
+                float a = 0.0f;
+#pragma unroll
+                for (int q = 0; q < FD_PARTS; q++) a += part_s[(q * FD_GMAX + j) * FD_CHUNK + lane + 32];
+                s1 = a * p.scale;
             }
             const float cmax = warp_max(fmaxf(s0, s1));
             const float m_old = m_s[j];
             const float m_new = fmaxf(m_old, cmax);
-            const float e0 = lane < n && s0 != -CUDART_INF_F ? expf(s0 - m_new) : 0.0f;
-            const float e1 = lane + 32 < n && s1 != -CUDART_INF_F ? expf(s1 - m_new) : 0.0f;
+            const float e0 = s0 != -CUDART_INF_F ? expf(s0 - m_new) : 0.0f;
+            const float e1 = s1 != -CUDART_INF_F ? expf(s1 - m_new) : 0.0f;
             p_s[j * FD_CHUNK + lane] = e0;
             p_s[j * FD_CHUNK + lane + 32] = e1;
             const float csum = warp_sum(e0 + e1);
@@ -254,56 +287,65 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
             }
         }
         __syncthreads();
-        // P V: thread owns output elements e = tid + i*128
+        // P V: thread (e_own, grp) sums the positions grp, grp + NGRP, ... of the chunk
+        {
+            float acc[FD_GMAX];
 #pragma unroll
-        for (int i = 0; i < EPT; i++) {
-            const int e = tid + i * FD_THREADS;
-            if (e < HD) {
-                float acc[FD_GMAX];
-#pragma unroll
-                for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
-                for (int tt = 0; tt < n; tt++) {
-                    const float vv = (float)v_s[tt * RE + e];
+            for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+#pragma unroll 8
+            for (int i = 0; i < FD_CHUNK / NGRP; i++) {
+                const int tt = grp + i * NGRP;
+                if (tt < n) {
+                    const float vv = (float)v_s[tt * RE + e_own];
 #pragma unroll
                     for (int j = 0; j < FD_GMAX; j++)
                         if (j < G) acc[j] = fmaf(p_s[j * FD_CHUNK + tt], vv, acc[j]);
                 }
-#pragma unroll
-                for (int j = 0; j < FD_GMAX; j++)
-                    if (j < G) o_acc[j][i] = o_acc[j][i] * a_s[j] + acc[j];
             }
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++)
+                if (j < G) o_acc[j] = o_acc[j] * a_s[j] + acc[j];
         }
         __syncthreads();  // buffer `buf` is free again
-        if (ci + 2 < n_chunks) issue(ci + 2, buf, -1);
+        if (issued < n_chunks) {
+            issue(issued, -1);
+            issued++;
+        }
     }
 
-    // ---- write this split's partial result ----
+    // ---- combine the position groups (fixed order), then write this split's result ----
+#pragma unroll
+    for (int j = 0; j < FD_GMAX; j++)
+        if (j < G) ored[(grp * FD_GMAX + j) * HD + e_own] = o_acc[j];
+    __syncthreads();
+    if (tid < HD) {
+#pragma unroll
+        for (int j = 0; j < FD_GMAX; j++) {
+            if (j >= G) continue;
+            float o = ored[j * HD + tid];
+#pragma unroll
+            for (int q = 1; q < NGRP; q++) o += ored[(q * FD_GMAX + j) * HD + tid];
+            o_acc[j] = o;
+        }
+    }
+    if (n_active == 1) {  // a single split: its partial is the answer
+        if (tid < HD) {
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++)
+                if (j < G) p.out[((size_t)b * p.n_heads + h0 + j) * HD + tid] = o_acc[j] / l_s[j];
+        }
+        VSL_TRACE_EXIT(p.trace_id, 901);
+        return;
+    }
 #pragma unroll
     for (int j = 0; j < FD_GMAX; j++) {
         if (j >= G) continue;
         const size_t row = ((size_t)b * p.n_heads + h0 + j) * p.n_splits + split;
-#pragma unroll
-        for (int i = 0; i < EPT; i++) {
-            const int e = tid + i * FD_THREADS;
-            if (e < HD) p.ws_o[row * HD + e] = o_acc[j][i];
-        }
+        if (tid < HD) p.ws_o[row * HD + tid] = o_acc[j];
         if (tid == 0) {
             p.ws_ml[row * 2 + 0] = m_s[j];
             p.ws_ml[row * 2 + 1] = l_s[j];
         }
-    }
-    if (n_active == 1) {  // a single split: its partial is the answer
-#pragma unroll
-        for (int j = 0; j < FD_GMAX; j++) {
-            if (j >= G) continue;
-#pragma unroll
-            for (int i = 0; i < EPT; i++) {
-                const int e = tid + i * FD_THREADS;
-                if (e < HD) p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = o_acc[j][i] / l_s[j];
-            }
-        }
-        VSL_TRACE_EXIT(p.trace_id, 901);
-        return;
     }
     __threadfence();
     __syncthreads();
@@ -321,10 +363,11 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     // The split statistics and weights are staged in shared memory by all threads at once (one
     // L2 round trip each), so the combine costs a few round trips rather than one per split.
     // Sums run in split order, as a sequential combine would.
+    constexpr int EPT = (HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
     float* cw = part_s;                       // exp(m_s - M) of a tile of splits
     float* cl = part_s + FD_GMAX * FD_CHUNK;  // l_s of the same tile
     constexpr int TILE = FD_GMAX * FD_CHUNK;
-    float* red = m_s;                         // FD_THREADS / 32 partial maxima (own stats are written)
+    float* red = a_s + FD_GMAX;               // FD_THREADS / 32 partial maxima
     for (int j = 0; j < G; j++) {
         const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits + s_first;
         float mx = -CUDART_INF_F;
@@ -379,6 +422,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
 static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 static int fd_splits(int max_len, int split_len) { return (max_len + split_len - 1) / split_len; }
+size_t flash_decode_workspace_bytes(int B, int n_heads, int n_kv, int head_dim, int n_splits);
 
 // Workspace: split partials from the front, split counters at the tail (+256 bytes of slack), so
 // calls with fewer rows on the same workspace (a prompt pass's last chunk) find their counters
@@ -387,6 +431,9 @@ static size_t fd_workspace(int B, int n_heads, int n_kv, int head_dim, int n_spl
     return align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float)) +
            align256((size_t)B * n_heads * n_splits * 2 * sizeof(float)) +
            align256((size_t)B * n_kv * sizeof(int)) + 256;
+}
+size_t flash_decode_workspace_bytes(int B, int n_heads, int n_kv, int head_dim, int n_splits) {
+    return fd_workspace(B, n_heads, n_kv, head_dim, n_splits);
 }
 static size_t fd_counters_offset(int B, int n_kv, size_t workspace_bytes) {
     return (workspace_bytes - (size_t)B * n_kv * sizeof(int)) & ~(size_t)255;
@@ -414,7 +461,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                       size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                      bool shared_pages, const SparseMask* sparse) {
+                      bool shared_pages, const SparseMask* sparse, int n_splits_max) {
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
         return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
     if (sparse && sparse->min_len > 0 && (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0))
@@ -428,14 +475,16 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                          page_size, split_len, FD_CHUNK);
     if (max_len <= 0 || max_len > max_pages * page_size)
         return set_error(VSL_ERR_INVALID, "flash_decode: max_len %d outside the page table", max_len);
-    const int n_splits = fd_splits(max_len, split_len);
+    // split_len is the least positions per split; the grid has n_splits_max splits per (sequence,
+    // group), or enough to cover max_len with split_len each (then every split is split_len long)
+    const int n_splits = n_splits_max > 0 ? n_splits_max : fd_splits(max_len, split_len);
     const size_t need = fd_workspace(B, n_heads, n_kv, head_dim, n_splits);
     if (workspace_bytes < need)
         return set_error(VSL_ERR_INVALID, "flash_decode: workspace %zu bytes < %zu", workspace_bytes, need);
     FdParams p = {};
     p.q = q; p.k_cache = k_cache; p.v_cache = v_cache; p.page_table = page_table; p.max_pages = max_pages;
-    p.page_size = page_size; p.pos = pos; p.B = B; p.n_heads = n_heads; p.n_kv = n_kv; p.split_len = split_len;
-    p.n_splits = n_splits; p.scale = 1.0f / sqrtf((float)head_dim); p.out = out;
+    p.page_size = page_size; p.pos = pos; p.B = B; p.n_heads = n_heads; p.n_kv = n_kv; p.split_min = split_len;
+    p.n_splits = n_splits; p.max_len = max_len; p.scale = 1.0f / sqrtf((float)head_dim); p.out = out;
     char* w = reinterpret_cast<char*>(workspace);
     p.ws_o = reinterpret_cast<float*>(w);
     w += align256((size_t)B * n_heads * n_splits * head_dim * sizeof(float));
@@ -471,7 +520,7 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0, true, nullptr);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0);  // the caller's rows may share pages
 }
 
 extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
@@ -483,7 +532,7 @@ extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, cons
     if (mask && mask->min_len > 0) m = vsl::SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0, true, &m);
+                                  (cudaStream_t)stream, nullptr, 0, true, &m, 0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -551,5 +600,5 @@ extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, con
     if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, ws, FD_STATIC_SCRATCH_BYTES,
-                                  (cudaStream_t)stream, nullptr, 0, true, nullptr);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0);  // the caller's rows may share pages
 }
