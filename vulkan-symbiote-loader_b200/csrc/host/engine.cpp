@@ -919,7 +919,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         else
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
-                                 att_pf, sb.shared_pages, &sparse_, fd_splits_));
+                                 att_pf, sb.shared_pages, &sparse_, fd_splits_, status_));
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
         RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,

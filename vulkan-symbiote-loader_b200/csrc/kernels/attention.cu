@@ -10,7 +10,9 @@
 // n_splits splits of at least split_min positions, sized from the sequence's current length on the
 // device (a short cache takes one split and no combine; a long one spreads over the n_splits CTAs).
 // A CTA stages 64-position chunks of K and V (one page-contiguous block each) through a ring of
-// shared-memory buffers, computes the scores of all G = n_heads/n_kv query heads of its group from
+// shared-memory buffers filled by bulk asynchronous copies (TMA, one per cache row, padded rows in
+// shared memory, completion on one mbarrier per buffer: a single SM pulls the whole split's cache
+// far faster than with per-thread 16-byte copies), computes the scores of all G = n_heads/n_kv query heads of its group from
 // the same staged K (so a KV page is read from HBM once per group, not once per head), and keeps
 // an online softmax (running max / sum, fp32). With 256 threads the scores split each position's
 // dot product into four partial sums and the P.V product splits the positions among two (head_dim
@@ -56,6 +58,7 @@ struct FdParams {
     size_t pf_bytes;
     int wait_first;      // rows share one sequence's pages (prompt chunk): no cache read before the wait
     SparseMask sp;       // long-context sparse mask (sp.min_len 0: dense)
+    int* status;         // VSL_ERR_TIMEOUT if a staging wait ever expires (may be null)
     unsigned trace_id;   // launch id of the trace build (unused otherwise)
 };
 
@@ -88,20 +91,8 @@ __host__ __device__ constexpr size_t fd_smem_bytes() {
            + (size_t)4 * FD_GMAX * sizeof(float);                                      // m, l, alpha, misc
 }
 
-__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-// wait until at most n (0..3) committed groups are still in flight
-__device__ __forceinline__ void cp_async_wait_upto(int n) {
-    if (n <= 0) asm volatile("cp.async.wait_group 0;" ::: "memory");
-    else if (n == 1) asm volatile("cp.async.wait_group 1;" ::: "memory");
-    else if (n == 2) asm volatile("cp.async.wait_group 2;" ::: "memory");
-    else asm volatile("cp.async.wait_group 3;" ::: "memory");
-}
-
 template <int HD, typename KT>
-__global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p) {
+__global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int STAGES = fd_stages<KT>();
     constexpr int RE = fd_row_elems<HD, KT>();
@@ -119,6 +110,7 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     float* l_s = m_s + FD_GMAX;
     float* a_s = l_s + FD_GMAX;
     __shared__ int is_last;
+    __shared__ __align__(8) uint64_t kv_bar[4];  // one per ring buffer: its chunk's copies landed
     VSL_TRACE_ENTRY();
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
@@ -167,27 +159,36 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
         kg = reinterpret_cast<const KT*>(p.k_cache) + base;
         vg = reinterpret_cast<const KT*>(p.v_cache) + base;
     };
-    // stage chunk ci into ring buffer ci % STAGES with cp.async; the row `skip` is left for later
+    // stage chunk ci into ring buffer ci % STAGES: warp 0 announces the bytes on the buffer's
+    // mbarrier and its lanes issue one bulk copy per K and V row; the row `skip` is left for later
+    constexpr uint32_t ROW_BYTES = HD * sizeof(KT);  // a multiple of 16
     auto issue = [&](int ci, int skip) {
+        if (warp != 0) return;
         const KT* kg;
         const KT* vg;
         chunk_ptrs(ci, kg, vg);
         const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
-        KT* ks = kv_s + (size_t)(2 * (ci % STAGES)) * FD_CHUNK * RE;
+        const int buf = ci % STAGES;
+        KT* ks = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         KT* vs = ks + FD_CHUNK * RE;
-        for (int i = tid; i < n * VPR; i += FD_THREADS) {
-            const int r = i / VPR, c = (i % VPR) * VEC;
+        const int skipped = skip >= ci * FD_CHUNK && skip < ci * FD_CHUNK + n ? 1 : 0;
+        if (lane == 0) mbar_arrive_expect_tx(&kv_bar[buf], (uint32_t)(n - skipped) * 2 * ROW_BYTES);
+        __syncwarp();
+        for (int r = lane; r < n; r += 32) {
             if (ci * FD_CHUNK + r == skip) continue;
-            cp_async16(ks + r * RE + c, kg + (size_t)r * HD + c);
-            cp_async16(vs + r * RE + c, vg + (size_t)r * HD + c);
+            bulk_g2s(ks + r * RE, kg + (size_t)r * HD, ROW_BYTES, &kv_bar[buf]);
+            bulk_g2s(vs + r * RE, vg + (size_t)r * HD, ROW_BYTES, &kv_bar[buf]);
         }
-        cp_async_commit();
     };
+    if (tid < STAGES) mbar_init(&kv_bar[tid], 1);
+    if (tid == 0) mbar_fence_init();
+    __syncthreads();
 
     // every chunk the ring holds is requested before the wait (older cache rows only)
     const int pre = min(n_chunks, STAGES);
     for (int ci = 0; ci < pre; ci++) issue(ci, new_row);
     int issued = pre;
+    bool staged_ok = true;
     if (p.pf_ptr && tid < 32) {
         const int nblk = gridDim.x * gridDim.y * gridDim.z;
         const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
@@ -200,7 +201,8 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     }
     pdl_launch_dependents();
 
-    // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done
+    // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done;
+    // the bulk copies never write that row
     if (new_row >= 0 && new_row < pre * FD_CHUNK) {
         const int ci = new_row / FD_CHUNK, r = new_row % FD_CHUNK;
         const KT* kg;
@@ -225,8 +227,12 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
     for (int ci = 0; ci < n_chunks; ci++) {
         const int buf = ci % STAGES;
         const int n = min(FD_CHUNK, t_end - (t_begin + ci * FD_CHUNK));
-        cp_async_wait_upto(issued - ci - 1);  // later chunks may still be in flight
-        __syncthreads();
+        // this chunk's copies (bounded wait; all threads decide together to stop)
+        const bool late = !mbar_wait(&kv_bar[buf], (uint32_t)((ci / STAGES) & 1));
+        if (__syncthreads_or(late)) {
+            staged_ok = false;
+            break;
+        }
         const KT* k_s = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         const KT* v_s = k_s + FD_CHUNK * RE;
         // partial scores: thread (tt, part) covers a quarter of the head dimension of position tt
@@ -311,6 +317,13 @@ __global__ void __launch_bounds__(FD_THREADS) vsl_flash_decode_kernel(FdParams p
             issue(issued, -1);
             issued++;
         }
+    }
+    if (!staged_ok) {
+        // a copy never landed: report it, let the copies still in flight finish (bounded), leave
+        set_status(p.status, VSL_ERR_TIMEOUT);
+        for (int ci = 0; ci < issued; ci++) mbar_wait(&kv_bar[ci % STAGES], (uint32_t)((ci / STAGES) & 1));
+        VSL_TRACE_EXIT(p.trace_id, 904);
+        return;
     }
 
     // ---- combine the position groups (fixed order), then write this split's result ----
@@ -461,7 +474,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                       const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                       int n_heads, int n_kv, int head_dim, int max_len, int split_len, float* out, void* workspace,
                       size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
-                      bool shared_pages, const SparseMask* sparse, int n_splits_max) {
+                      bool shared_pages, const SparseMask* sparse, int n_splits_max, int* status) {
     if (!q || !k_cache || !v_cache || !page_table || !pos || !out || !workspace)
         return set_error(VSL_ERR_INVALID, "flash_decode: null pointer");
     if (sparse && sparse->min_len > 0 && (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0))
@@ -493,6 +506,7 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
     p.pf_ptr = pf_ptr;
     p.pf_bytes = pf_bytes;
     p.wait_first = shared_pages ? 1 : 0;
+    p.status = status;
     if (sparse) p.sp = *sparse;
     if (kvdtype == VSL_F16) {
         if (head_dim == 128) return launch_fd<128, __half>(p, stream);
@@ -520,7 +534,7 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0, nullptr);  // the caller's rows may share pages
 }
 
 extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
@@ -532,7 +546,7 @@ extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, cons
     if (mask && mask->min_len > 0) m = vsl::SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
-                                  (cudaStream_t)stream, nullptr, 0, true, &m, 0);
+                                  (cudaStream_t)stream, nullptr, 0, true, &m, 0, nullptr);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -600,5 +614,5 @@ extern "C" int vsl_flash_decode_noalloc(const float* q, const void* k_cache, con
     if (e != cudaSuccess) return vsl::launch_status(e, "flash_decode_noalloc: clearing the split counters");
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, ws, FD_STATIC_SCRATCH_BYTES,
-                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0);  // the caller's rows may share pages
+                                  (cudaStream_t)stream, nullptr, 0, true, nullptr, 0, nullptr);  // the caller's rows may share pages
 }
