@@ -60,11 +60,16 @@ def parse():
                          "configs[4] at batch 1 after a 2048-token prompt pass, tensor-parallel over --gpus "
                          "(run it under torchrun with 8 GPUs for the TP 8 figure); 70b-stream: BASELINE configs[4] "
                          "on one GPU under a 64 GB HBM cap (layers streamed from host)")
-    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "gemv_q41", "prefill"],
+    ap.add_argument("--profile-case", choices=["tc_gemm", "attention_tc", "gemv_q8", "gemv_q4", "gemv_q41", "prefill",
+                                               "decode_layers", "p2p"],
                     help="run one kernel case 3 times (for ncu captures): tc_gemm = 32000 x 4096 fp16 at "
                          "batch 16; attention_tc = 16 x 8192-position fp16 KV, 32/8 heads; gemv_q8 / gemv_q4 / gemv_q41 = "
                          "7B gate/up (22016 x 4096, RMSNorm + SwiGLU) with Q8_0 / Q4_0 / Q4_1 weights at batch 1; prefill = "
-                         "three 128-token prompt passes on the 7B shape (--layers, default 4)")
+                         "three 128-token prompt passes on the 7B shape (--layers, default 4); decode_layers = "
+                         "three graph-replayed decode steps of the 7B shape at --layers (default 4) layers after a "
+                         "128-token prompt (every per-layer kernel in the engine's context); p2p = the peer-memory "
+                         "all-reduce of a 16 KB residual between two receive buffers on one GPU, the second rank's "
+                         "words placed by the host (two launches)")
     ap.add_argument("--profile-shape", default="32000,4096,16",
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
@@ -657,7 +662,36 @@ def run_profile_case(args):
     import torch
 
     import vsl
-    if args.profile_case == "prefill":
+    if args.profile_case == "decode_layers":
+        from vsl import synth
+        cfg = dict(CONFIG_7B)
+        cfg["n_layers"] = args.layers or 4
+        with vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, max_batch=1, max_seq=512) as e:
+            e.prefill(synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"]))
+            e.run(3)
+            if e.device_status() != 0:
+                raise SystemExit("device status")
+    elif args.profile_case == "p2p":
+        import numpy as np
+        n, cap = 4096, 4096 * 4
+        size = vsl.p2p_buffer_size(2, cap)
+        bufs = [torch.zeros(size // 8, dtype=torch.int64, device="cuda") for _ in range(2)]
+        slot = size // 4  # [2 parities][2 ranks] slots
+        epochs = torch.zeros(64, dtype=torch.int64, device="cuda")
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        data = torch.randn(n, device="cuda")
+        peer = np.random.default_rng(0).standard_normal(n).astype(np.float32).view(np.uint32)
+        for epoch in (1, 2):  # the second rank's words of both calls: (piece, epoch tag) pairs
+            w = peer.astype(np.uint64) | (np.uint64((epoch & 0x7FFFFFFF) | 0x80000000) << np.uint64(32))
+            off = ((epoch & 1) * 2 + 1) * slot // 8
+            bufs[0][off:off + n].copy_(torch.from_numpy(w.view(np.int64)).cuda())
+        torch.cuda.synchronize()
+        for _ in range(2):
+            vsl.p2p_allreduce(bufs, 0, cap, data, n, 0, epochs, status)
+        torch.cuda.synchronize()
+        if status.item() != 0:
+            raise SystemExit("p2p status")
+    elif args.profile_case == "prefill":
         from vsl import synth
         cfg = dict(CONFIG_7B)
         cfg["n_layers"] = args.layers or 4

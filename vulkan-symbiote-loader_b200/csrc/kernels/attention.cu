@@ -10,9 +10,9 @@
 // n_splits splits of at least split_min positions, sized from the sequence's current length on the
 // device (a short cache takes one split and no combine; a long one spreads over the n_splits CTAs).
 // A CTA stages 64-position chunks of K and V (one page-contiguous block each) through a ring of
-// shared-memory buffers filled by bulk asynchronous copies (TMA, one per cache row, padded rows in
-// shared memory, completion on one mbarrier per buffer: a single SM pulls the whole split's cache
-// far faster than with per-thread 16-byte copies), computes the scores of all G = n_heads/n_kv query heads of its group from
+// shared-memory buffers filled by bulk asynchronous copies (TMA: one copy per chunk of K and of V,
+// completion on one mbarrier per buffer; rows land unpadded and every thread reads its 16-byte
+// columns in an order rotated by its row, so the score reads stay free of bank conflicts), computes the scores of all G = n_heads/n_kv query heads of its group from
 // the same staged K (so a KV page is read from HBM once per group, not once per head), and keeps
 // an online softmax (running max / sum, fp32). With 256 threads the scores split each position's
 // dot product into four partial sums and the P.V product splits the positions among two (head_dim
@@ -74,7 +74,7 @@ template <> struct KvVec<__half> {
 
 template <int HD, typename KT>
 __host__ __device__ constexpr int fd_row_elems() {
-    return HD + 16 / (int)sizeof(KT);  // one 16-byte pad per row: conflict-free 16-byte reads
+    return HD;  // rows as in the cache (bulk copies of whole chunks); reads rotate their columns
 }
 template <typename KT>
 __host__ __device__ constexpr int fd_stages() {
@@ -84,7 +84,7 @@ __host__ __device__ constexpr int fd_stages() {
 template <int HD, typename KT>
 __host__ __device__ constexpr size_t fd_smem_bytes() {
     return (size_t)fd_stages<KT>() * 2 * FD_CHUNK * fd_row_elems<HD, KT>() * sizeof(KT)  // K and V chunk ring
-           + (size_t)FD_GMAX * HD * sizeof(float)                                      // q
+           + (size_t)2 * FD_GMAX * HD * sizeof(float)                                  // q (padded columns)
            + (size_t)FD_PARTS * FD_GMAX * FD_CHUNK * sizeof(float)                     // score partials
            + (size_t)FD_GMAX * FD_CHUNK * sizeof(float)                                // probabilities
            + (size_t)(FD_THREADS / HD) * FD_GMAX * HD * sizeof(float)                  // P.V group partials
@@ -103,7 +103,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
     static_assert(PDIM % VEC == 0 && FD_THREADS % HD == 0, "attention tiling");
     KT* kv_s = reinterpret_cast<KT*>(smem_raw);  // [STAGES][K, V][CHUNK][RE]
     float* q_s = reinterpret_cast<float*>(kv_s + (size_t)STAGES * 2 * FD_CHUNK * RE);
-    float* part_s = q_s + FD_GMAX * HD;                    // [PARTS][GMAX][CHUNK]
+    // q by 16-byte cache column, each column padded by one float: [GMAX][VPR][VEC + 1], so lanes
+    // reading different columns hit different banks
+    constexpr int QCOL = VEC + 1, QP = VPR * QCOL;
+    float* part_s = q_s + 2 * FD_GMAX * HD;                // [PARTS][GMAX][CHUNK]
     float* p_s = part_s + FD_PARTS * FD_GMAX * FD_CHUNK;   // [GMAX][CHUNK]
     float* ored = p_s + FD_GMAX * FD_CHUNK;                // [NGRP][GMAX][HD]
     float* m_s = ored + NGRP * FD_GMAX * HD;               // [GMAX]
@@ -159,11 +162,12 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
         kg = reinterpret_cast<const KT*>(p.k_cache) + base;
         vg = reinterpret_cast<const KT*>(p.v_cache) + base;
     };
-    // stage chunk ci into ring buffer ci % STAGES: warp 0 announces the bytes on the buffer's
-    // mbarrier and its lanes issue one bulk copy per K and V row; the row `skip` is left for later
+    // stage chunk ci into ring buffer ci % STAGES: one thread announces the bytes on the buffer's
+    // mbarrier and copies the chunk's K and V rows in one bulk copy each (two when the row `skip`,
+    // left for later, sits inside the chunk)
     constexpr uint32_t ROW_BYTES = HD * sizeof(KT);  // a multiple of 16
     auto issue = [&](int ci, int skip) {
-        if (warp != 0) return;
+        if (tid != 0) return;
         const KT* kg;
         const KT* vg;
         chunk_ptrs(ci, kg, vg);
@@ -171,13 +175,18 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
         const int buf = ci % STAGES;
         KT* ks = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         KT* vs = ks + FD_CHUNK * RE;
-        const int skipped = skip >= ci * FD_CHUNK && skip < ci * FD_CHUNK + n ? 1 : 0;
-        if (lane == 0) mbar_arrive_expect_tx(&kv_bar[buf], (uint32_t)(n - skipped) * 2 * ROW_BYTES);
-        __syncwarp();
-        for (int r = lane; r < n; r += 32) {
-            if (ci * FD_CHUNK + r == skip) continue;
-            bulk_g2s(ks + r * RE, kg + (size_t)r * HD, ROW_BYTES, &kv_bar[buf]);
-            bulk_g2s(vs + r * RE, vg + (size_t)r * HD, ROW_BYTES, &kv_bar[buf]);
+        const int r = skip - ci * FD_CHUNK;  // row left out, if in [0, n)
+        const bool cut = r >= 0 && r < n;
+        mbar_arrive_expect_tx(&kv_bar[buf], (uint32_t)(n - (cut ? 1 : 0)) * 2 * ROW_BYTES);
+        const int r0 = cut ? r : n;          // rows [0, r0) and [r1, n)
+        const int r1 = cut ? r + 1 : n;
+        if (r0 > 0) {
+            bulk_g2s(ks, kg, (uint32_t)r0 * ROW_BYTES, &kv_bar[buf]);
+            bulk_g2s(vs, vg, (uint32_t)r0 * ROW_BYTES, &kv_bar[buf]);
+        }
+        if (n > r1) {
+            bulk_g2s(ks + (size_t)r1 * HD, kg + (size_t)r1 * HD, (uint32_t)(n - r1) * ROW_BYTES, &kv_bar[buf]);
+            bulk_g2s(vs + (size_t)r1 * HD, vg + (size_t)r1 * HD, (uint32_t)(n - r1) * ROW_BYTES, &kv_bar[buf]);
         }
     };
     if (tid < STAGES) mbar_init(&kv_bar[tid], 1);
@@ -216,7 +225,10 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
         }
     }
     const int h0 = g * G;
-    for (int i = tid; i < G * HD; i += FD_THREADS) q_s[i] = __ldcg(p.q + ((size_t)b * p.n_heads + h0) * HD + i);
+    for (int i = tid; i < G * HD; i += FD_THREADS) {
+        const int j = i / HD, d = i - j * HD;
+        q_s[j * QP + (d / VEC) * QCOL + d % VEC] = __ldcg(p.q + ((size_t)b * p.n_heads + h0) * HD + i);
+    }
     if (tid < FD_GMAX) { m_s[tid] = -CUDART_INF_F; l_s[tid] = 0.0f; }
 
     const int e_own = tid % HD, grp = tid / HD;  // P.V: output element and position group
@@ -235,7 +247,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
         }
         const KT* k_s = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         const KT* v_s = k_s + FD_CHUNK * RE;
-        // partial scores: thread (tt, part) covers a quarter of the head dimension of position tt
+        // partial scores: thread (tt, part) covers a quarter of the head dimension of position tt,
+        // the 16-byte columns c = (tt + part + 4k) mod NCOL: the 8 lanes of a shared-memory phase
+        // read 8 different bank groups of their (unpadded) rows
         {
             const int tt = tid & (FD_CHUNK - 1), part = tid / FD_CHUNK;
             if (tt < n) {
@@ -244,14 +258,15 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
                 for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
                 const KT* kr = k_s + tt * RE;
 #pragma unroll
-                for (int c = part * PDIM; c < (part + 1) * PDIM; c += VEC) {
+                for (int k = 0; k < PDIM / VEC; k++) {
+                    const int c = ((tt + part + FD_PARTS * k) % VPR) * VEC;
                     float kf[VEC];
                     KvVec<KT>::widen(*reinterpret_cast<const uint4*>(kr + c), kf);
 #pragma unroll
                     for (int j = 0; j < FD_GMAX; j++) {
                         if (j < G) {
 #pragma unroll
-                            for (int e = 0; e < VEC; e++) acc[j] = fmaf(q_s[j * HD + c + e], kf[e], acc[j]);
+                            for (int e = 0; e < VEC; e++) acc[j] = fmaf(q_s[j * QP + (c / VEC) * QCOL + e], kf[e], acc[j]);
                         }
                     }
                 }
