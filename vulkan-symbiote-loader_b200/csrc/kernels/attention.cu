@@ -198,17 +198,11 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
     for (int ci = 0; ci < pre; ci++) issue(ci, new_row);
     int issued = pre;
     bool staged_ok = true;
-    if (p.pf_ptr && tid < 32) {
-        const int nblk = gridDim.x * gridDim.y * gridDim.z;
-        const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
-        prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
-    }
 
     if (!p.wait_first) {
         pdl_wait();
         VSL_TRACE_RELEASED();
     }
-    pdl_launch_dependents();
 
     // the new row (if it sits in an already-issued chunk) and q, now that the QKV kernel is done;
     // the bulk copies never write that row
@@ -333,6 +327,15 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
             issued++;
         }
     }
+    // The next projection's weights are requested into L2, and its CTAs allowed to start (they
+    // request their own heads), only now that this split's cache has landed: issued earlier, those
+    // tens of megabytes of prefetches queue in HBM ahead of the few cache chunks attention waits for.
+    if (p.pf_ptr && tid < 32) {
+        const int nblk = gridDim.x * gridDim.y * gridDim.z;
+        const int me = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        prefetch_share(p.pf_ptr, p.pf_bytes, me, nblk, tid, 32);
+    }
+    pdl_launch_dependents();
     if (!staged_ok) {
         // a copy never landed: report it, let the copies still in flight finish (bounded), leave
         set_status(p.status, VSL_ERR_TIMEOUT);
