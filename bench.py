@@ -76,6 +76,10 @@ def parse():
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
     ap.add_argument("--split-len", type=int, default=0,
                     help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
+    ap.add_argument("--attn-route", type=int, default=0, choices=[0, 1, 2],
+                    help="decode attention kernel (engine option attn_route): 0 automatic, 1 split-K, 2 tcgen05")
+    ap.add_argument("--attn-prefetch", type=int, default=1, choices=[0, 1],
+                    help="split-K attention requests the output projection into L2 (engine option attn_prefetch)")
     ap.add_argument("--p2p-chunk", type=int, default=0,
                     help="bytes per CTA of the peer-memory all-reduce (engine option p2p_chunk_bytes; 0 = automatic)")
     ap.add_argument("--timeline", action="store_true",
@@ -356,7 +360,8 @@ def run_ours(args):
     t0 = time.perf_counter()
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_batch=B, max_seq=max_seq,
                                tp_rank=rank, tp_size=ws, nccl_id=nccl_id, split_len=args.split_len,
-                               p2p_chunk_bytes=args.p2p_chunk)
+                               p2p_chunk_bytes=args.p2p_chunk, attn_route=args.attn_route,
+                               attn_prefetch=args.attn_prefetch)
     load_s = time.perf_counter() - t0
     if big:
         # 8192 positions of seeded N(0, 1) keys/values per sequence written straight into the
@@ -771,7 +776,8 @@ def run_timeline(args):
     max_seq = (PROMPT + args.warmup + args.steps + 8 + 63) // 64 * 64
     nid = vdist.nccl_id(dist)
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_seq=max_seq, tp_rank=rank, tp_size=ws,
-                               nccl_id=nid, split_len=args.split_len, p2p_chunk_bytes=args.p2p_chunk)
+                               nccl_id=nid, split_len=args.split_len, p2p_chunk_bytes=args.p2p_chunk,
+                               attn_route=args.attn_route, attn_prefetch=args.attn_prefetch)
     eng.prefill(synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"]))
     eng.run(args.warmup)
     torch.cuda.synchronize()

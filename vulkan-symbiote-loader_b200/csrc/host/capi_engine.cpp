@@ -44,6 +44,8 @@ extern "C" void vsl_engine_default_options(vsl_engine_options* o) {
     o->sparse_window = 512;
     o->sparse_global = 16;
     o->sparse_block = 1024;
+    o->attn_route = 0;
+    o->attn_prefetch = 1;
     o->p2p_chunk_bytes = 0;
     o->nccl_timeout_ms = 120000;
 }

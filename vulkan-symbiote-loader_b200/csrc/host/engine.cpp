@@ -208,6 +208,7 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     }
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);
+    if (opt.attn_route < 0 || opt.attn_route > 2) return set_error(VSL_ERR_INVALID, "engine: attn_route %d", opt.attn_route);
     if (opt.sparse_min_len < 0 || opt.sparse_window < 0 || opt.sparse_global < 0 || opt.sparse_block < 0)
         return set_error(VSL_ERR_INVALID, "engine: negative sparse attention parameter");
     if (opt.sparse_min_len > 0)  // zeros take the reference's values (Common.h:71-74)
@@ -359,7 +360,8 @@ int DecodeEngine::alloc_buffers() {
     CK(cudaMemset(fd_ws_, 0, fd_ws_bytes_));
 
     // long caches: attention with tcgen05 scores and an even split of the KV over the SMs
-    if (opt_.max_seq >= FDTC_MIN_SEQ &&
+    const bool want_tc = opt_.attn_route == 2 || (opt_.attn_route == 0 && opt_.max_seq >= FDTC_MIN_SEQ);
+    if (want_tc &&
         flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, opt_.max_batch, page_size_)) {
         fdtc_ws_bytes_ = flash_decode_tc_workspace_bytes(opt_.max_batch, nkv_l_);
         CK(cudaMalloc(&fdtc_ws_, fdtc_ws_bytes_));
@@ -891,7 +893,7 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
     const size_t wgu_b = 2 * (size_t)ff_l_ * wrow(d), wd_b = (size_t)d * wrow(ff_l_);
     const size_t head = 16ull << 20;
     auto H = [&](size_t bytes) { return std::min(bytes, head); };
-    const size_t att_pf = std::min(wo_b, (size_t)l2_bytes_ / 2);
+    const size_t att_pf = opt_.attn_prefetch ? std::min(wo_b, (size_t)l2_bytes_ / 2) : 0;
     const bool streamed = residency_.streamed_layers > 0;
     if (streamed) {  // bring the copy stream into this step (and into a graph being captured)
         CK(cudaEventRecord(ev_fork_, st));

@@ -52,7 +52,8 @@ class EngineOptions(C.Structure):
                 ("use_pdl", C.c_int), ("use_fused", C.c_int),
                 ("use_p2p", C.c_int), ("legacy_q4", C.c_int), ("sparse_min_len", C.c_int),
                 ("sparse_window", C.c_int), ("sparse_global", C.c_int), ("sparse_block", C.c_int),
-                ("p2p_chunk_bytes", C.c_int), ("nccl_timeout_ms", C.c_int)]
+                ("attn_route", C.c_int), ("attn_prefetch", C.c_int), ("p2p_chunk_bytes", C.c_int),
+                ("nccl_timeout_ms", C.c_int)]
 
 
 _lib = None
