@@ -195,16 +195,18 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     if (page_size_ % 64) return set_error(VSL_ERR_INVALID, "engine: page_size %d must be a multiple of 64", page_size_);
     max_pages_ = (opt.max_seq + page_size_ - 1) / page_size_;
     n_pages_ = max_pages_ * opt.max_batch;
+    fd_splits_ = 0;  // fixed splits of split_len_ positions over max_seq
     if (opt.split_len > 0) {
-        split_len_ = opt.split_len;  // fixed splits of split_len positions over max_seq
-        fd_splits_ = 0;
+        split_len_ = opt.split_len;
     } else {
-        // splits of at least 256 positions, sized from each sequence's current length, and about
-        // one CTA per SM over all (sequence, group) pairs when the cache is long: a short cache
-        // takes one split (no combine), a long one spreads over the SMs
+        // about four CTAs per SM over the whole cache at full length. Many short splits beat fewer
+        // long ones at every length measured: a CTA's chunks run one after another through a chain
+        // of dependent shared-memory steps, while the splits run on separate SMs (7B batch 1 at
+        // ~150 positions: 96 CTAs of one chunk each, 11 us per layer including the combine, against
+        // 19 us for 32 CTAs of three chunks)
         const int groups = opt.max_batch * nkv_l_;
-        split_len_ = 256;
-        fd_splits_ = std::max(1, std::min((148 + groups - 1) / groups, (opt.max_seq + 255) / 256));
+        int splits = std::max(1, (4 * 148 + groups - 1) / groups);
+        split_len_ = (int)align_up((size_t)((opt.max_seq + splits - 1) / splits), 64);
     }
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);

@@ -14,12 +14,6 @@ int sm_count();
 bool pdl_enabled();
 void set_pdl_enabled(bool on);
 
-// Every kernel of the library runs with the largest shared-memory carve-out of the L1/shared
-// array, set once per kernel and device: consecutive kernels then never need different SM
-// configurations, so a kernel's CTAs can become resident next to the draining CTAs of its
-// predecessor instead of waiting for the SM to empty and be reconfigured.
-void prefer_max_shared(const void* kernel);
-
 // Launch `kernel` on `stream` with the programmatic-stream-serialization attribute, so the
 // kernel may begin while its predecessor on the stream drains (it calls pdl_wait() before
 // touching the predecessor's outputs).
@@ -36,7 +30,6 @@ cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    prefer_max_shared(reinterpret_cast<const void*>(kernel));
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

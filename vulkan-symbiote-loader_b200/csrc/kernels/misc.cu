@@ -1,9 +1,6 @@
 // Small decode kernels: embedding gather, standalone RMSNorm, argmax, the seeded synthetic
 // initialiser, and the end-of-step token bookkeeping.
 #include <atomic>
-#include <mutex>
-#include <set>
-#include <utility>
 #include <type_traits>
 #include <cuda_runtime.h>
 #include <math_constants.h>
@@ -20,17 +17,6 @@ namespace vsl {
 static std::atomic<bool> g_pdl{true};
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 void set_pdl_enabled(bool on) { g_pdl.store(on, std::memory_order_relaxed); }
-
-void prefer_max_shared(const void* kernel) {
-    static std::mutex mu;
-    static std::set<std::pair<int, const void*>> done;
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return;
-    std::lock_guard<std::mutex> lock(mu);
-    if (!done.insert({dev, kernel}).second) return;
-    // a preference: a failure leaves the driver's default and is not an error of the launch
-    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
-}
 
 int sm_count() {
     static thread_local int cached_dev = -1, cached = 148;
