@@ -15,8 +15,9 @@
 // columns in an order rotated by its row, so the score reads stay free of bank conflicts), computes the scores of all G = n_heads/n_kv query heads of its group from
 // the same staged K (so a KV page is read from HBM once per group, not once per head), and keeps
 // an online softmax (running max / sum, fp32). With 256 threads the scores split each position's
-// dot product into four partial sums and the P.V product splits the positions among two (head_dim
-// 128) or four (head_dim 64) thread groups, combined once at the end in a fixed order. Splits
+// dot product into two partial sums and the P.V product gives every thread one output element
+// (head_dim 128; with head_dim 64 two position groups share the output, combined once at the end
+// in a fixed order). Splits
 // write (max, sum, partial output) to the workspace; the last CTA of a (sequence, group) to
 // finish -- found with an atomic counter that it resets to zero -- combines them, so one launch
 // does both phases.
@@ -33,10 +34,15 @@ VSL_TRACE_UNIT(attention)
 
 namespace vsl {
 
-constexpr int FD_THREADS = 256;
+// 128 threads and at most 64 registers per thread: a CTA (8 K registers) fits on an SM beside the
+// two CTAs of the projection that precedes it (2 x 28 K of the 64 K registers), so with
+// programmatic dependent launch the attention CTAs become resident and start staging the cache
+// while that projection still streams its weights
+constexpr int FD_THREADS = 128;
+constexpr int FD_MIN_CTAS = 8;  // register cap 64 (launch bounds)
 constexpr int FD_CHUNK = 64;  // positions staged per iteration
 constexpr int FD_GMAX = 8;    // query heads per KV group supported
-constexpr int FD_PARTS = 4;   // partial sums per position score
+constexpr int FD_PARTS = FD_THREADS / FD_CHUNK;  // partial sums per position score
 
 struct FdParams {
     const float* q;
@@ -92,7 +98,7 @@ __host__ __device__ constexpr size_t fd_smem_bytes() {
 }
 
 template <int HD, typename KT>
-__global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParams p) {
+__global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int STAGES = fd_stages<KT>();
     constexpr int RE = fd_row_elems<HD, KT>();
@@ -100,7 +106,7 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
     constexpr int VPR = HD / VEC;             // 16-byte vectors per row
     constexpr int NGRP = FD_THREADS / HD;     // position groups of the P.V product
     constexpr int PDIM = HD / FD_PARTS;       // head dimensions per score partial
-    static_assert(PDIM % VEC == 0 && FD_THREADS % HD == 0, "attention tiling");
+    static_assert(PDIM % VEC == 0 && FD_THREADS % HD == 0 && (VPR % FD_PARTS) == 0, "attention tiling");
     KT* kv_s = reinterpret_cast<KT*>(smem_raw);  // [STAGES][K, V][CHUNK][RE]
     float* q_s = reinterpret_cast<float*>(kv_s + (size_t)STAGES * 2 * FD_CHUNK * RE);
     // q by 16-byte cache column, each column padded by one float: [GMAX][VPR][VEC + 1], so lanes
@@ -241,9 +247,9 @@ __global__ void __launch_bounds__(FD_THREADS, 1) vsl_flash_decode_kernel(FdParam
         }
         const KT* k_s = kv_s + (size_t)(2 * buf) * FD_CHUNK * RE;
         const KT* v_s = k_s + FD_CHUNK * RE;
-        // partial scores: thread (tt, part) covers a quarter of the head dimension of position tt,
-        // the 16-byte columns c = (tt + part + 4k) mod NCOL: the 8 lanes of a shared-memory phase
-        // read 8 different bank groups of their (unpadded) rows
+        // partial scores: thread (tt, part) covers 1/FD_PARTS of the head dimension of position tt,
+        // the 16-byte columns c = (tt + part + FD_PARTS k) mod NCOL: the 8 lanes of a shared-memory
+        // phase read 8 different bank groups of their (unpadded) rows
         {
             const int tt = tid & (FD_CHUNK - 1), part = tid / FD_CHUNK;
             if (tt < n) {
