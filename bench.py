@@ -78,7 +78,7 @@ def parse():
                     help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
     ap.add_argument("--attn-route", type=int, default=0, choices=[0, 1, 2],
                     help="decode attention kernel (engine option attn_route): 0 automatic, 1 split-K, 2 tcgen05")
-    ap.add_argument("--attn-prefetch", type=int, default=1, choices=[0, 1],
+    ap.add_argument("--attn-prefetch", type=int, default=0, choices=[0, 1],
                     help="split-K attention requests the output projection into L2 (engine option attn_prefetch)")
     ap.add_argument("--p2p-chunk", type=int, default=0,
                     help="bytes per CTA of the peer-memory all-reduce (engine option p2p_chunk_bytes; 0 = automatic)")

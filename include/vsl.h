@@ -288,8 +288,8 @@ typedef struct {
     int attn_route;      /* decode attention: 0 (default) = tcgen05-score attention when max_seq >= 2048,
                           split-K kernel below; 1 = split-K kernel always; 2 = tcgen05 attention
                           always (fp16 KV, head_dim 128)                                    */
-    int attn_prefetch;   /* 1 (default) = the split-K attention kernel requests the output projection's
-                          weights into L2 while it runs; 0 = it does not                     */
+    int attn_prefetch;   /* 1 = the split-K attention kernel requests the output projection's weights
+                          into L2 while it runs; 0 (default) = it does not (measured faster)  */
     int p2p_chunk_bytes; /* tensor parallel with use_p2p: bytes of the residual all-reduce's message
                           one CTA moves (0 = automatic: 1 KB chunks, at most 64 per message);
                           larger values mean fewer, longer CTAs. Same value on every rank.   */
