@@ -29,6 +29,9 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+# The decode path's tensor-parallel sums are the engine's own peer-memory exchange; NCCL only carries
+# set-up and prompt-pass sums, so its NVLink multicast (NVLS) buffers are not needed.
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 sys.path.insert(0, os.path.join(ROOT, "vulkan-symbiote-loader_b200"))
 
 CONFIG_7B = dict(n_layers=32, d_model=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000,
