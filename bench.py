@@ -77,6 +77,9 @@ def parse():
                     help="N,K,B of the tc_gemm profile case (weights N x K, batch B)")
     ap.add_argument("--sweep", action="store_true",
                     help="projection sweep (BASELINE configs[2]): one JSON line per shape and batch")
+    ap.add_argument("--sweep-shapes", default="",
+                    help="projection shapes NxK,NxK,... for --sweep (default: the 7B decode shapes and lm_head)")
+    ap.add_argument("--sweep-batches", default="1,4,16,64", help="activation rows for --sweep")
     ap.add_argument("--split-len", type=int, default=0,
                     help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
     ap.add_argument("--attn-route", type=int, default=0, choices=[0, 1, 2],
@@ -612,12 +615,15 @@ def run_sweep(args):
 
     import vsl
     hbm_peak, peak_kind = peaks()
-    for N, K in SWEEP_SHAPES:
+    shapes = [tuple(int(v) for v in t.split("x")) for t in args.sweep_shapes.split(",")] if args.sweep_shapes \
+        else SWEEP_SHAPES
+    batches = [int(v) for v in args.sweep_batches.split(",")]
+    for N, K in shapes:
         copies = max(2, -(-400_000_000 // (N * K * 2)))
         W = torch.empty((copies, N, K), dtype=torch.float16, device="cuda")
         for c in range(copies):
             vsl.synth_fill(W[c], vsl.F16, 1, 5000 + c, 0, N * K, 0.02)
-        for B in (1, 4, 16, 64):
+        for B in batches:
             x = torch.randn((B, K), device="cuda").half().float()
             y = torch.empty((B, N), device="cuda")
             tc = B >= 5  # the engine's route: GEMV up to 4 rows, tcgen05 tensor cores above

@@ -179,6 +179,19 @@ VSL_API int vsl_flash_decode_tc_sparse(const float* q, const void* k_cache, cons
                                        void* workspace, size_t workspace_bytes, const vsl_sparse_mask* mask,
                                        void* stream);
 
+/* Prompt attention (the reference runs attention.comp once per prompt token during its prompt
+ * pass, VulkanSymbioteEngine.cpp:678-765): n_rows query rows of ONE sequence, row r at position
+ * pos[r] and attending to positions [first, pos[r]] of the cache (first from the sparse mask,
+ * 0 when mask is NULL or dense), with the rows' own K and V already in the cache. page_row is
+ * that sequence's page-table row (max_pages entries); q and out are [n_rows][n_heads][128]
+ * fp32. fp16 KV, head_dim 128, page_size a multiple of 64; query blocks of 128 rows on the
+ * tcgen05 tensor cores, one CTA per (head, block). status (nullable device int) receives
+ * VSL_ERR_TIMEOUT if a bounded wait expires. No workspace. */
+VSL_API int vsl_flash_prefill(const float* q, const void* k_cache, const void* v_cache, int n_pages,
+                              const int32_t* page_row, int max_pages, int page_size, const int32_t* pos, int n_rows,
+                              int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                              const vsl_sparse_mask* mask, int* status, void* stream);
+
 /* Allocation-free form of vsl_flash_decode (no counterpart in the reference). For callers
  * that must not have the library allocate device memory -- hosts that own every device
  * byte through their own pool or budget, or loops that cannot take an allocation's implicit

@@ -63,12 +63,13 @@ def test_tiny_fp32_prefill_logits_match_oracle(golden, fixture_gguf):
 
 
 @pytest.mark.parametrize("wdtype,n_prompt,max_seq,hd", [(vsl.F16, 100, 256, 128), (vsl.BF16, 64, 256, 128),
-                                                        (vsl.BF16, 200, 2048, 128), (vsl.BF16, 90, 256, 64),
-                                                        (vsl.F16, 150, 256, 64)])
+                                                        (vsl.BF16, 200, 2048, 128), (vsl.F16, 300, 512, 128),
+                                                        (vsl.BF16, 90, 256, 64), (vsl.F16, 150, 256, 64)])
 def test_half_prefill_chunks_match_oracle(wdtype, n_prompt, max_seq, hd):
-    """100 tokens = chunks of 64 + 36 rows (tcgen05 projections); head_dim 128 takes the
-    tcgen05-score attention, head_dim 64 the split-K kernel, whose split counters must stay
-    valid when the last chunk has fewer rows than the first. Then 6 teacher-forced decode steps."""
+    """Prompts in chunks of up to 128 rows (300 tokens = 128 + 128 + 44) on the tcgen05
+    projections; head_dim 128 takes the tensor-core prompt attention (one query block per head),
+    head_dim 64 the split-K kernel, whose split counters must stay valid when the last chunk has
+    fewer rows than the first. Then 6 teacher-forced decode steps."""
     cfg = dict(n_layers=2, d_model=1024, n_heads=1024 // hd, n_kv_heads=256 // hd, head_dim=hd, ffn=2816,
                vocab=6000, rope_theta=10000.0, rms_eps=1e-5, wdtype=wdtype)
     seed = 41

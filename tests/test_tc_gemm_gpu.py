@@ -81,7 +81,7 @@ def run(dtype, N, K, B, epi, norm=False, seed=0):
 
 @pytest.mark.parametrize("dtype", [vsl.F16, vsl.BF16])
 @pytest.mark.parametrize("N,K", [(128, 64), (4096, 4096), (11008, 4096), (4096, 11008), (333, 1376)])
-@pytest.mark.parametrize("B", [5, 8, 16, 64])
+@pytest.mark.parametrize("B", [5, 8, 16, 64, 100, 128])
 def test_tc_store(dtype, N, K, B):
     run(dtype, N, K, B, vsl.EPI_STORE)
 
@@ -141,7 +141,7 @@ def test_tc_rejects_bad_shapes():
     X = torch.zeros(8 * 4096, device="cuda")
     Y = torch.zeros(8 * 4096, device="cuda")
     with pytest.raises(vsl.VslError):
-        vsl.skinny_gemm_tc(vsl.F16, W, 4096, 4096, X, 65, Y, vsl.EPI_STORE, None, 0.0, ws, nbytes)
+        vsl.skinny_gemm_tc(vsl.F16, W, 4096, 4096, X, 129, Y, vsl.EPI_STORE, None, 0.0, ws, nbytes)
     with pytest.raises(vsl.VslError):
         vsl.skinny_gemm_tc(vsl.F32, W, 4096, 4096, X, 8, Y, vsl.EPI_STORE, None, 0.0, ws, nbytes)
     with pytest.raises(vsl.VslError):

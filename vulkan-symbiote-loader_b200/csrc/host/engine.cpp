@@ -281,7 +281,6 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(tc_ws_);
     cudaFree(pf_mem_);
     cudaFree(pf_fd_ws_);
-    cudaFree(pf_fdtc_ws_);
     cudaFree(pf_tc_ws_);
     if (pf_h_) cudaFreeHost(pf_h_);
     cudaFree(fdtc_ws_);
@@ -372,7 +371,7 @@ int DecodeEngine::alloc_buffers() {
     // batched projections (5..64 rows, 16-bit weights) run on the tensor cores: one workspace
     // sized for the largest projection of the model
     if (es_ == 2 && !is_quant(c.wdtype) && opt_.max_batch >= TC_MIN_BATCH) {
-        const int tb = std::min(opt_.max_batch, 64);
+        const int tb = std::min(opt_.max_batch, TC_MAX_BATCH);
         const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
         const int k_max = std::max({c.d_model, nh_l_ * c.head_dim, ff_l_});
         tc_ws_bytes_ = tc_workspace_bytes(n_max, k_max, tb) + 1024;
@@ -811,7 +810,6 @@ int DecodeEngine::reset() {
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
     if (pf_tc_ws_) CK(cudaMemsetAsync(pf_tc_route_.ws, 0, pf_tc_route_.bytes, stream_));
-    if (pf_fdtc_ws_) CK(cudaMemsetAsync(pf_fdtc_ws_, 0, pf_fdtc_bytes_, stream_));
     RC(sync());
     std::fill(pos_host_.begin(), pos_host_.end(), 0);
     steps_host_ = 0;
@@ -916,7 +914,10 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, sb.x, L.attn_norm, c.rms_eps, B, sb.pos,
                                   rope_cos_, rope_sin_, sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_,
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
-        if (sb.fdtc_ws)
+        if (sb.shared_pages && pf_attn_tc_)
+            RC(flash_prefill_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
+                                  nh_l_, nkv_l_, opt_.max_seq, sb.attn, status_, st, &sparse_));
+        else if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                     nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st,
                                     &sparse_));
@@ -1035,15 +1036,13 @@ int DecodeEngine::alloc_prefill() {
     pf_slot_ = reinterpret_cast<unsigned long long*>(m + o_slot);
     pf_next_ = reinterpret_cast<int32_t*>(m + o_next);
     CK(cudaMallocHost((void**)&pf_h_, n_int * 4 + 64));
-    pf_fd_bytes_ = flash_decode_workspace_bytes(PF_ROWS, nh_l_, nkv_l_, c.head_dim, fd_grid_splits());
-    CK(cudaMalloc(&pf_fd_ws_, pf_fd_bytes_));
-    CK(cudaMemset(pf_fd_ws_, 0, pf_fd_bytes_));
-    // prompt chunks: 64 rows of one sequence over the same pages, so the tcgen05-score attention
-    // (one KV pass per row and KV head on the tensor cores) at every cache length
-    if (flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, PF_ROWS, page_size_)) {
-        pf_fdtc_bytes_ = flash_decode_tc_workspace_bytes(PF_ROWS, nkv_l_);
-        CK(cudaMalloc(&pf_fdtc_ws_, pf_fdtc_bytes_));
-        CK(cudaMemset(pf_fdtc_ws_, 0, pf_fdtc_bytes_));
+    // prompt chunks: up to 128 rows of one sequence over the same pages, one query block of the
+    // tensor-core prompt attention per head (fp16 KV, head_dim 128); otherwise the split-K kernel
+    pf_attn_tc_ = flash_prefill_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, page_size_);
+    if (!pf_attn_tc_) {
+        pf_fd_bytes_ = flash_decode_workspace_bytes(PF_ROWS, nh_l_, nkv_l_, c.head_dim, fd_grid_splits());
+        CK(cudaMalloc(&pf_fd_ws_, pf_fd_bytes_));
+        CK(cudaMemset(pf_fd_ws_, 0, pf_fd_bytes_));
     }
     if (es_ == 2 && !is_quant(c.wdtype)) {
         const int n_max = std::max({(nh_l_ + 2 * nkv_l_) * c.head_dim, c.d_model, 2 * ff_l_, v_l_});
@@ -1083,8 +1082,8 @@ int DecodeEngine::prefill(const int32_t* ids, int n, int seq, int32_t* next_id, 
         CK(cudaMemcpyAsync(pf_ids_, pf_h_, (2 * (size_t)P + (size_t)P * max_pages_) * 4, cudaMemcpyHostToDevice,
                            stream_));
         RC(embed_impl(c.wdtype, tok_embd_, c.vocab, d, pf_ids_, nc, pf_x_, nullptr, stream_));
-        StepBufs sb{pf_x_, pf_q_, pf_attn_, pf_act_, pf_pos_, pf_pages_, pf_fd_ws_, pf_fd_bytes_, pf_fdtc_ws_,
-                    pf_fdtc_bytes_, pf_tc_ws_ ? &pf_tc_route_ : nullptr, true};
+        StepBufs sb{pf_x_, pf_q_, pf_attn_, pf_act_, pf_pos_, pf_pages_, pf_fd_ws_, pf_fd_bytes_, nullptr, 0,
+                    pf_tc_ws_ ? &pf_tc_route_ : nullptr, true};
         RC(enqueue_layers(sb, nc));
         if (c0 + nc == n) {  // the last prompt token: logits, greedy next token
             CK(cudaMemsetAsync(pf_slot_, 0, 16, stream_));

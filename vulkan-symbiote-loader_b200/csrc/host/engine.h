@@ -111,7 +111,7 @@ private:
         bool shared_pages;  // rows are consecutive positions of one sequence (prompt chunk)
     };
     int enqueue_layers(const StepBufs& sb, int B);
-    static constexpr int PF_ROWS = 64;  // prompt rows per prefill chunk
+    static constexpr int PF_ROWS = 128;  // prompt rows per prefill chunk (one query block)
     int alloc_prefill();
     void* pf_mem_ = nullptr;
     int32_t* pf_ids_ = nullptr;   // [PF] ids, then [PF] positions, then [PF][max_pages] page rows
@@ -127,8 +127,7 @@ private:
     int32_t* pf_h_ = nullptr;     // pinned staging of ids / positions / page rows
     void* pf_fd_ws_ = nullptr;
     size_t pf_fd_bytes_ = 0;
-    void* pf_fdtc_ws_ = nullptr;
-    size_t pf_fdtc_bytes_ = 0;
+    bool pf_attn_tc_ = false;  // prompt chunks take the tensor-core prompt attention
     void* pf_tc_ws_ = nullptr;
     TcRoute pf_tc_route_ = {};
     std::vector<int32_t> pt_host_;  // host copy of the page table

@@ -34,6 +34,7 @@ struct TcRoute {
 };
 size_t tc_workspace_bytes(int N, int K, int B);
 constexpr int TC_MIN_BATCH = 5;  // below this the GEMV streams the weights once per launch anyway
+constexpr int TC_MAX_BATCH = 128;  // activation rows per launch (MMA N = 2 x padded rows <= 256)
 
 int embed_impl(int dtype, const void* table, int V, int d, const int32_t* ids, int B, float* x,
                unsigned long long* slots, cudaStream_t st);
@@ -64,6 +65,12 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
                          const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
                          int n_heads, int n_kv, int max_len, float* out, void* workspace, size_t workspace_bytes,
                          int* status, cudaStream_t st, const SparseMask* sparse = nullptr);
+// Prompt attention: up to 128 rows per query block of one sequence (one page-table row), fp16
+// KV, head_dim 128; grid = heads x query blocks (attention_prefill.cu).
+bool flash_prefill_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int page_size);
+int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages, const int32_t* page_row,
+                       int max_pages, int page_size, const int32_t* pos, int P, int n_heads, int n_kv, int max_len,
+                       float* out, int* status, cudaStream_t st, const SparseMask* sparse = nullptr);
 constexpr int FDTC_MIN_SEQ = 2048;  // caches from this length on use the tensor-core attention
 int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start, uint64_t n, double sigma,
                cudaStream_t st);

@@ -1,0 +1,502 @@
+// Prompt attention on tcgen05 tensor cores: one query block per CTA.
+//
+// A prompt chunk is up to 128 consecutive positions of one sequence whose K and V rows the
+// chunk's QKV projection has just appended to the paged cache. Row r (position pos[r]) attends
+// causally to positions [first(r), pos[r]] of the cache (first = 0 unless the long-context
+// sparse mask applies), with the semantics of the decode kernels (attention.cu, attention_tc.cu;
+// reference attention.comp:84-189 run once per prompt token): scores q.k / sqrt(head_dim),
+// max-subtracted softmax, probabilities times V. One CTA takes one query head and a block of
+// 128 rows, so the K and V of each 128-position chunk are read once for the whole block rather
+// than once per row:
+//   * S[128 rows][128 positions] = Q2 . K^T (tcgen05.mma kind::f16, M = N = 128, fp32 in TMEM),
+//     with the fp32 query split into fp16 hi and lo tiles that accumulate into the same scores
+//     (about 22 bits of the query survive);
+//   * online softmax (fp32) by 4 warps, one query row per thread (its TMEM lane), over two reads
+//     of the row's scores (maximum, then probabilities), written back to shared memory as fp16
+//     hi/lo tiles P2;
+//   * PV[128 rows][128 dims] = P2 . V (V as the MN-major B operand, in place as it lands from
+//     TMA) into TMEM; each thread folds its row into fp32 registers with the softmax rescale.
+// K and V of a chunk arrive by tensor TMA (two 64-position pages x two 64-column 128-byte-swizzle
+// atoms each) into single K and V tiles with their own barriers, so the next chunk's K loads
+// while this chunk's softmax runs. The next chunk's scores are issued before this chunk's
+// product. Rows past the cache end are zeroed in the V tile before the product (0 x garbage);
+// rows of K past the end give scores that the mask drops.
+// Roles: warps 0-3 softmax and accumulation (TMEM lane quarter = warp), warp 4 TMA producer,
+// warp 5 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second)
+// and records VSL_ERR_TIMEOUT; the kernel then drains its copies and MMAs and frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include <climits>
+
+#include "common.cuh"
+#include "kv_map.h"
+#include "launch.cuh"
+
+namespace vsl {
+
+constexpr int FP_THREADS = 192;        // 4 softmax warps, TMA producer, MMA issuer
+constexpr int FP_ROWS = 128;           // query rows per CTA (MMA M)
+constexpr int FP_CHUNK = 128;          // positions per chunk
+constexpr int FP_HD = 128;
+constexpr int FP_ATOM = 128 * 64 * 2;  // one 64-column swizzle atom of a 128-row tile (16 KB)
+constexpr int FP_TILE = 2 * FP_ATOM;   // a 128 x 128 16-bit tile
+// shared memory: Q hi, Q lo, K, V, P hi, P lo
+constexpr size_t FP_SMEM = 1024 + 6 * (size_t)FP_TILE;
+constexpr uint32_t FP_TMEM_COLS = 512;  // S[2] at columns 0 and 128, PV at 256
+
+struct FpArgs {
+    const float* q;             // [P][n_heads][128]
+    const int32_t* pos;         // [P] positions of the rows
+    const int32_t* page_row;    // the sequence's page-table row
+    int P, n_heads, n_kv, G, max_len, max_pages, page_size;
+    float scale;
+    float* out;                 // [P][n_heads][128]
+    int* status;
+    uint32_t idesc_s;           // Q2 (A, K-major) . K (B, K-major)
+    uint32_t idesc_pv;          // P2 (A, K-major) . V (B, MN-major)
+    SparseMask sp;
+};
+
+__device__ __forceinline__ void fp_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fp_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fp_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// K-major 128-byte-swizzle operand (8-row x 128-byte atoms, 1024 bytes apart)
+__device__ __forceinline__ uint64_t fp_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// MN-major 128-byte-swizzle operand: the V tile as TMA lands it (rows = positions = K, 64 head
+// dims = N per 128-byte row); the next 64 dims sit one 16 KB atom further (leading byte offset),
+// the next 8 positions 1024 bytes further (stride byte offset)
+__device__ __forceinline__ uint64_t fp_desc_mn(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)(FP_ATOM >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void fp_mma(uint32_t d, uint64_t ad, uint64_t bd, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void fp_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void fp_ld16(uint32_t taddr, float* v) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ int fp_abort(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+// byte offset of 16-bit column `col` (0..127) of row `r` in a 128 x 128 K-major swizzled tile
+__device__ __forceinline__ uint32_t fp_off(int r, int col) {
+    return (uint32_t)((col >> 6) * FP_ATOM + (r >> 3) * 1024 + (r & 7) * 128 + ((((col & 63) >> 3) ^ (r & 7)) << 4) +
+                      (col & 7) * 2);
+}
+
+__global__ void __launch_bounds__(FP_THREADS, 1)
+    vsl_prefill_attention_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
+                                 const __grid_constant__ FpArgs a) {
+    extern __shared__ unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t k_full, k_empty, v_full, v_empty, s_full[2], s_free[2], q_ready, p_ready, o_full,
+        o_free;
+    __shared__ uint32_t tmem_s;
+    __shared__ int abort_s, len_s, lo_s;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+    const uint32_t qt = base, kt = base + 2 * FP_TILE, vt = base + 3 * FP_TILE, pt = base + 4 * FP_TILE;
+    unsigned char* smem_g = smem_raw - smem_u32(smem_raw);  // generic pointer of shared address 0
+    const int h = blockIdx.x, g = h / a.G;
+    const int r0 = blockIdx.y * FP_ROWS;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&k_full, 1);
+        mbar_init(&k_empty, 1);
+        mbar_init(&v_full, 1);
+        mbar_init(&v_empty, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+        }
+        mbar_init(&q_ready, 4);
+        mbar_init(&p_ready, 4);
+        mbar_init(&o_full, 1);
+        mbar_init(&o_free, 4);
+        mbar_fence_init();
+        abort_s = 0;
+        len_s = 0;
+        lo_s = INT_MAX;
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
+    }
+    if (warp == 5) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_s)),
+                     "r"(FP_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // q, K and V of this chunk are written by the preceding projection
+    pdl_wait();
+    __syncthreads();
+    // this thread's query row: position, first attended position; the block's cache length and
+    // lowest first position
+    int pr = -1, first = INT_MAX;
+    if (threadIdx.x < FP_ROWS && r0 + (int)threadIdx.x < a.P) {
+        pr = __ldg(a.pos + r0 + threadIdx.x);
+        pr = pr < 0 ? 0 : (pr >= a.max_len ? a.max_len - 1 : pr);
+        first = sparse_first(a.sp, pr);
+        atomicMax(&len_s, pr + 1);
+        atomicMin(&lo_s, first);
+    }
+    fp_fence_before();
+    __syncthreads();
+    fp_fence_after();
+    pdl_launch_dependents();
+    const uint32_t tmem = tmem_s;
+    const int len = len_s;                          // >= 1: row 0 of the block exists
+    const int c0 = (lo_s == INT_MAX ? 0 : lo_s) / FP_CHUNK;
+    const int n = (len + FP_CHUNK - 1) / FP_CHUNK - c0;  // chunks of the block
+
+    if (warp == 4) {
+        // ================= TMA producer: K(i) and V(i) into single tiles =================
+        if (lane == 0) {
+            int issued_k = 0, issued_v = 0;
+            bool ok = true;
+            for (int i = 0; i < n && ok; i++) {
+                for (int kv = 0; kv < 2 && ok; kv++) {
+                    uint64_t* full = kv ? &v_full : &k_full;
+                    uint64_t* empty = kv ? &v_empty : &k_empty;
+                    if (i > 0 && !mbar_wait(empty, (uint32_t)((i - 1) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    if (fp_abort(&abort_s)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full, FP_TILE);
+                    const uint32_t dst = kv ? vt : kt;
+#pragma unroll
+                    for (int hh = 0; hh < 2; hh++) {
+                        int p0 = (c0 + i) * FP_CHUNK + hh * 64;
+                        if (p0 >= len) p0 = 0;  // past the end: any valid page (masked or zeroed later)
+                        const int page = __ldg(a.page_row + p0 / a.page_size);
+                        const int row = (page * a.n_kv + g) * a.page_size + (p0 % a.page_size);
+#pragma unroll
+                        for (int at = 0; at < 2; at++)
+                            fp_tma(dst + at * FP_ATOM + hh * (FP_ATOM / 2), kv ? &map_v : &map_k, at * 64, row, full);
+                    }
+                    if (kv) issued_v++;
+                    else issued_k++;
+                }
+            }
+            if (!ok) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+            }
+            // no copy may still be landing when the CTA leaves
+            if (issued_k > 0) mbar_wait(&k_full, (uint32_t)((issued_k - 1) & 1));
+            if (issued_v > 0) mbar_wait(&v_full, (uint32_t)((issued_v - 1) & 1));
+        }
+    } else if (warp == 5) {
+        // ================= MMA issue =================
+        if (lane == 0) {
+            bool ok = mbar_wait(&q_ready, 0u);
+            int s_issued = 0, pv_issued = 0;
+            auto issue_s = [&](int i) -> bool {
+                if (!mbar_wait(&k_full, (uint32_t)(i & 1))) return false;
+                if (i >= 2 && !mbar_wait(&s_free[i & 1], (uint32_t)(((i >> 1) - 1) & 1))) return false;
+                fp_fence_after();
+#pragma unroll
+                for (int hl = 0; hl < 2; hl++)
+#pragma unroll
+                    for (int at = 0; at < 2; at++) {
+                        const uint64_t ad = fp_desc(qt + hl * FP_TILE + at * FP_ATOM), bd = fp_desc(kt + at * FP_ATOM);
+#pragma unroll
+                        for (int k = 0; k < 4; k++)
+                            fp_mma(tmem + (uint32_t)((i & 1) * FP_CHUNK), ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k),
+                                   a.idesc_s, (hl | at | k) ? 1u : 0u);
+                    }
+                fp_commit(&s_full[i & 1]);
+                fp_commit(&k_empty);  // K(i) is no longer read
+                s_issued++;
+                return true;
+            };
+            auto issue_pv = [&](int i) -> bool {
+                if (!mbar_wait(&p_ready, (uint32_t)(i & 1))) return false;
+                if (!mbar_wait(&v_full, (uint32_t)(i & 1))) return false;
+                if (i >= 1 && !mbar_wait(&o_free, (uint32_t)((i - 1) & 1))) return false;
+                fp_fence_after();
+#pragma unroll
+                for (int hl = 0; hl < 2; hl++)
+#pragma unroll
+                    for (int k = 0; k < FP_CHUNK / 16; k++) {
+                        const uint64_t ad =
+                            fp_desc(pt + hl * FP_TILE + (uint32_t)((k >> 2) * FP_ATOM)) + (uint64_t)(2 * (k & 3));
+                        const uint64_t bd = fp_desc_mn(vt + (uint32_t)(k * 2048));
+                        fp_mma(tmem + 2 * FP_CHUNK, ad, bd, a.idesc_pv, (hl | k) ? 1u : 0u);
+                    }
+                fp_commit(&o_full);
+                fp_commit(&v_empty);  // V(i) and P2(i) are no longer read
+                pv_issued++;
+                return true;
+            };
+            if (ok && n > 0) ok = issue_s(0);
+            for (int i = 0; i < n && ok; i++) {
+                if (fp_abort(&abort_s)) {
+                    ok = false;
+                    break;
+                }
+                if (i + 1 < n) {
+                    ok = issue_s(i + 1);
+                    if (!ok) break;
+                }
+                ok = issue_pv(i);
+            }
+            if (!ok) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+            }
+            // the accumulators must not be freed under a running MMA
+            if (s_issued > 0) mbar_wait(&s_full[(s_issued - 1) & 1], (uint32_t)(((s_issued - 1) >> 1) & 1));
+            if (pv_issued > 0) mbar_wait(&o_full, (uint32_t)((pv_issued - 1) & 1));
+        }
+        __syncwarp();
+    } else {
+        // ================= softmax + accumulation (warps 0-3; thread t = query row t) =================
+        const int t = threadIdx.x;
+        // ---- stage Q2: rows of this head as fp16 hi / lo, 128-byte swizzle ----
+        {
+            const size_t qs = (size_t)a.n_heads * FP_HD;
+            const int col = 4 * lane;
+#pragma unroll 4
+            for (int k = 0; k < FP_ROWS / 4; k++) {
+                const int r = warp + 4 * k;
+                float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (r0 + r < a.P)
+                    x = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(r0 + r) * qs + (size_t)h * FP_HD + col));
+                const float xs[4] = {x.x, x.y, x.z, x.w};
+                __half hh[4], ll[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    hh[e] = __float2half_rn(xs[e]);
+                    ll[e] = __float2half_rn(xs[e] - __half2float(hh[e]));
+                }
+                const uint32_t o = fp_off(r, col);
+                *reinterpret_cast<uint2*>(smem_g + qt + o) = *reinterpret_cast<const uint2*>(hh);
+                *reinterpret_cast<uint2*>(smem_g + qt + FP_TILE + o) = *reinterpret_cast<const uint2*>(ll);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_ready);
+        }
+        float o[FP_HD];
+#pragma unroll
+        for (int j = 0; j < FP_HD; j++) o[j] = 0.0f;
+        float m = -CUDART_INF_F, l = 0.0f;
+        bool failed = false;
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        for (int i = 0; i < n; i++) {
+            {
+                const bool bad = !mbar_wait(&s_full[i & 1], (uint32_t)((i >> 1) & 1)) || fp_abort(&abort_s);
+                if (named_barrier_or(1, 128, bad)) {  // the four warps leave together
+                    failed = true;
+                    break;
+                }
+            }
+            fp_fence_after();
+            const int cb = (c0 + i) * FP_CHUNK;  // position of score column 0
+            const int jlo = first - cb, jhi = pr - cb;  // valid columns: jlo <= j <= jhi
+            const uint32_t ts = tmem + lane_base + (uint32_t)((i & 1) * FP_CHUNK);
+            // pass 1: the row's maximum over its valid columns
+            float cm = -CUDART_INF_F;
+#pragma unroll
+            for (int c16 = 0; c16 < FP_CHUNK / 16; c16++) {
+                float v[16];
+                fp_ld16(ts + (uint32_t)(c16 * 16), v);
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const int j = c16 * 16 + e;
+                    if (j >= jlo && j <= jhi) cm = fmaxf(cm, v[e] * a.scale);
+                }
+            }
+            const float mn = fmaxf(m, cm);
+            const float alpha = mn == -CUDART_INF_F ? 1.0f : expf(m - mn);
+            // pass 2: probabilities, as fp16 hi / lo rows of P2 (P2 of the previous chunk has been
+            // read: its product completed before that chunk's fold below)
+            float ls = 0.0f;
+#pragma unroll
+            for (int c16 = 0; c16 < FP_CHUNK / 16; c16++) {
+                float v[16];
+                fp_ld16(ts + (uint32_t)(c16 * 16), v);
+                __half ph[16], pl[16];
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const int j = c16 * 16 + e;
+                    const float p = (j >= jlo && j <= jhi) ? expf(v[e] * a.scale - mn) : 0.0f;
+                    ls += p;
+                    ph[e] = __float2half_rn(p);
+                    pl[e] = __float2half_rn(p - __half2float(ph[e]));
+                }
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const uint32_t off = fp_off(t, c16 * 16 + hf * 8);
+                    *reinterpret_cast<uint4*>(smem_g + pt + off) = *reinterpret_cast<const uint4*>(ph + hf * 8);
+                    *reinterpret_cast<uint4*>(smem_g + pt + FP_TILE + off) = *reinterpret_cast<const uint4*>(pl + hf * 8);
+                }
+            }
+            fp_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[i & 1]);
+            m = mn;
+            l = l * alpha + ls;
+            if (cb + FP_CHUNK > len) {
+                // V rows past the cache end hold whatever the pool had (possibly NaN bit
+                // patterns): zero them so that 0 x garbage cannot reach the product
+                const bool bad = !mbar_wait(&v_full, (uint32_t)(i & 1));
+                if (named_barrier_or(1, 128, bad)) {
+                    failed = true;
+                    break;
+                }
+                if (cb + t >= len) {
+#pragma unroll
+                    for (int at = 0; at < 2; at++)
+#pragma unroll
+                        for (int c = 0; c < 8; c++)
+                            *reinterpret_cast<uint4*>(smem_g + vt + at * FP_ATOM + (t >> 3) * 1024 + (t & 7) * 128 +
+                                                      c * 16) = make_uint4(0, 0, 0, 0);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_ready);
+            // ---- fold PV(i) into the row's accumulators ----
+            {
+                const bool bad = !mbar_wait(&o_full, (uint32_t)(i & 1)) || fp_abort(&abort_s);
+                if (named_barrier_or(1, 128, bad)) {
+                    failed = true;
+                    break;
+                }
+            }
+            fp_fence_after();
+#pragma unroll
+            for (int c16 = 0; c16 < FP_HD / 16; c16++) {
+                float v[16];
+                fp_ld16(tmem + lane_base + (uint32_t)(2 * FP_CHUNK + c16 * 16), v);
+#pragma unroll
+                for (int e = 0; e < 16; e++) o[c16 * 16 + e] = o[c16 * 16 + e] * alpha + v[e];
+            }
+            fp_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free);
+        }
+        if (failed) {
+            set_status(a.status, VSL_ERR_TIMEOUT);
+            atomicExch(&abort_s, 1);
+        } else if (pr >= 0) {
+            const float inv = 1.0f / l;  // l > 0: position pr is always attended
+            float* dst = a.out + ((size_t)(r0 + t) * a.n_heads + h) * FP_HD;
+#pragma unroll
+            for (int j = 0; j < FP_HD; j += 4)
+                *reinterpret_cast<float4*>(dst + j) = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+        }
+    }
+
+    fp_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        fp_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FP_TMEM_COLS) : "memory");
+    }
+}
+
+bool flash_prefill_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int page_size) {
+    return kvdtype == VSL_F16 && head_dim == FP_HD && n_kv > 0 && n_heads % n_kv == 0 && page_size > 0 &&
+           page_size % 64 == 0;
+}
+
+int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages, const int32_t* page_row,
+                       int max_pages, int page_size, const int32_t* pos, int P, int n_heads, int n_kv, int max_len,
+                       float* out, int* status, cudaStream_t st, const SparseMask* sparse) {
+    if (!flash_prefill_supported(VSL_F16, FP_HD, n_heads, n_kv, page_size))
+        return set_error(VSL_ERR_UNSUPPORTED, "flash_prefill: heads %d/%d page %d", n_heads, n_kv, page_size);
+    if (!q || !k_cache || !v_cache || !page_row || !pos || !out || P <= 0 || max_len <= 0 ||
+        max_len > max_pages * page_size || n_pages <= 0)
+        return set_error(VSL_ERR_INVALID, "flash_prefill: null pointer, no rows or max_len outside the page table");
+    if (((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15) || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
+        return set_error(VSL_ERR_INVALID, "flash_prefill: caches, q and out must be 16-byte aligned");
+    FpArgs a = {};
+    a.q = q;
+    a.pos = pos;
+    a.page_row = page_row;
+    a.P = P;
+    a.n_heads = n_heads;
+    a.n_kv = n_kv;
+    a.G = n_heads / n_kv;
+    a.max_len = max_len;
+    a.max_pages = max_pages;
+    a.page_size = page_size;
+    a.scale = 1.0f / sqrtf((float)FP_HD);
+    a.out = out;
+    a.status = status;
+    if (sparse && sparse->min_len > 0) {
+        if (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0)
+            return set_error(VSL_ERR_INVALID, "flash_prefill: sparse mask window %d, global %d, block %d",
+                             sparse->window, sparse->global_tokens, sparse->block);
+        a.sp = *sparse;
+    }
+    // instruction descriptor (kind::f16): D f32 (bits 4-5 = 1), A/B f16 (0), N >> 3 in bits
+    // 17-22, M >> 4 in bits 24-28; bit 16 marks B as MN-major (V in the product)
+    a.idesc_s = (1u << 4) | ((uint32_t)(FP_CHUNK >> 3) << 17) | ((uint32_t)(FP_ROWS >> 4) << 24);
+    a.idesc_pv = (1u << 4) | ((uint32_t)(FP_HD >> 3) << 17) | ((uint32_t)(FP_ROWS >> 4) << 24) | (1u << 16);
+    const long long rows = (long long)n_pages * n_kv * page_size;
+    CUtensorMap mk, mv;
+    int rc = kv_tensor_map(&mk, k_cache, rows);
+    if (rc) return rc;
+    rc = kv_tensor_map(&mv, v_cache, rows);
+    if (rc) return rc;
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(vsl_prefill_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)FP_SMEM);
+        if (e != cudaSuccess) return launch_status(e, "flash_prefill smem attribute");
+        configured_dev = dev;
+    }
+    const dim3 grid((unsigned)n_heads, (unsigned)((P + FP_ROWS - 1) / FP_ROWS));
+    return launch_status(launch_k(vsl_prefill_attention_kernel, grid, dim3(FP_THREADS), FP_SMEM, st, mk, mv, a),
+                         "flash_prefill launch");
+}
+
+}  // namespace vsl
+
+using namespace vsl;
+
+extern "C" int vsl_flash_prefill(const float* q, const void* k_cache, const void* v_cache, int n_pages,
+                                 const int32_t* page_row, int max_pages, int page_size, const int32_t* pos, int n_rows,
+                                 int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                                 const vsl_sparse_mask* mask, int* status, void* stream) {
+    if (head_dim != FP_HD) return set_error(VSL_ERR_UNSUPPORTED, "flash_prefill: head_dim %d (128 only)", head_dim);
+    SparseMask m = {};
+    if (mask && mask->min_len > 0) m = SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
+    return flash_prefill_impl(q, k_cache, v_cache, n_pages, page_row, max_pages, page_size, pos, n_rows, n_heads, n_kv,
+                              max_len, out, status, (cudaStream_t)stream, &m);
+}

@@ -32,6 +32,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kv_map.h"
 #include "launch.cuh"
 
 namespace vsl {
@@ -593,8 +594,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 ft_encode_fn() {
     return fn;
 }
 
-// KV cache [rows = n_pages * n_kv * page_size][128] fp16 as 64-row x 64-column boxes, 128-byte swizzle
-static int ft_map(CUtensorMap* m, const void* base, long long rows) {
+int kv_tensor_map(CUtensorMap* m, const void* base, long long rows) {
     auto fn = ft_encode_fn();
     if (!fn) return set_error(VSL_ERR_CUDA, "tensor-map encoder unavailable from the driver");
     const cuuint64_t dims[2] = {(cuuint64_t)FT_HD, (cuuint64_t)rows};
@@ -665,9 +665,9 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
     a.idesc_pv = a.idesc | (1u << 15);  // A (V) MN-major
     const long long rows = (long long)n_pages * n_kv * page_size;
     CUtensorMap mk, mv;
-    int rc = ft_map(&mk, k_cache, rows);
+    int rc = kv_tensor_map(&mk, k_cache, rows);
     if (rc) return rc;
-    rc = ft_map(&mv, v_cache, rows);
+    rc = kv_tensor_map(&mv, v_cache, rows);
     if (rc) return rc;
     static thread_local int configured_dev = -1;
     int dev = 0;

@@ -48,7 +48,10 @@ namespace vsl {
 constexpr int TC_THREADS = 192;
 constexpr int TC_BM = 128;            // rows of W per tile (MMA M)
 constexpr int TC_ATOM = 64;           // k per 128-byte swizzle atom of 16-bit values
-constexpr int TC_KA = 2;              // atoms per stage
+#ifndef VSL_TC_KA
+#define VSL_TC_KA 2
+#endif
+constexpr int TC_KA = VSL_TC_KA;      // atoms per stage (build-time tuning: 1 or 2)
 constexpr int TC_BK = TC_ATOM * TC_KA;           // k per stage (one k-block)
 constexpr int TC_A_ATOM = TC_BM * TC_ATOM * 2;   // 16 KB
 constexpr int TC_A_BYTES = TC_A_ATOM * TC_KA;    // 32 KB of weights per stage

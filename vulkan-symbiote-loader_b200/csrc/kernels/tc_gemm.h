@@ -8,8 +8,6 @@
 
 namespace vsl {
 
-constexpr int TC_MAX_BATCH = 64;  // activation rows per launch (MMA N = 2 x padded batch <= 128)
-
 // Device workspace one projection needs: split activations [2*Bp][K] (16-bit), per-CTA
 // partials of split row tiles, and one arrival counter per row tile (zero before first use;
 // the kernel leaves them zero).

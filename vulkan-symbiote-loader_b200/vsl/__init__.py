@@ -127,6 +127,8 @@ def lib() -> C.CDLL:
         "vsl_engine_inject_status": (i32, [vp, i32]),
         "vsl_flash_decode_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, sz,
                                           C.POINTER(SparseMask), vp]),
+        "vsl_flash_prefill": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp,
+                                    C.POINTER(SparseMask), vp, vp]),
         "vsl_flash_decode_tc_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp, vp, sz,
                                              C.POINTER(SparseMask), vp]),
     }
@@ -333,6 +335,16 @@ def flash_decode_tc(q, k_cache, v_cache, n_pages, page_table, max_pages, page_si
     check(lib().vsl_flash_decode_tc_sparse(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table),
                                            max_pages, page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len,
                                            _ptr(out), _ptr(workspace), workspace_bytes, C.byref(m), stream))
+
+
+def flash_prefill(q, k_cache, v_cache, n_pages, page_row, max_pages, page_size, pos, n_rows, n_heads, n_kv, head_dim,
+                  max_len, out, sparse=None, status=None, stream=0):
+    """Prompt attention of n_rows rows of one sequence (page_row: its page-table row).
+    sparse: None (dense) or (min_len, window, global_tokens, block)."""
+    m = C.byref(SparseMask(*sparse)) if sparse is not None else None
+    check(lib().vsl_flash_prefill(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_row), max_pages,
+                                  page_size, _ptr(pos), n_rows, n_heads, n_kv, head_dim, max_len, _ptr(out), m,
+                                  _ptr(status), stream))
 
 
 def lm_head_sample(wdtype, W, V_local, K, x, norm_w, eps, B, logits, slots, vocab_offset=0, temperature=0.0,
