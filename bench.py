@@ -88,6 +88,9 @@ def parse():
                     help="split-K attention requests the output projection into L2 (engine option attn_prefetch)")
     ap.add_argument("--p2p-chunk", type=int, default=0,
                     help="bytes per CTA of the peer-memory all-reduce (engine option p2p_chunk_bytes; 0 = automatic)")
+    ap.add_argument("--timeline-prefill", action="store_true",
+                    help="per-CTA timeline of one 128-token prompt pass of the 7B workload (trace build): time per "
+                         "kernel role; not a benchmark number")
     ap.add_argument("--timeline", action="store_true",
                     help="per-CTA timeline of --steps decode steps of the 7B workload with the trace build "
                          "(lib/libvsl_trace.so, `make -C vulkan-symbiote-loader_b200 trace`): one JSON line per "
@@ -760,6 +763,66 @@ def run_profile_case(args):
 ROLE_ORDER = ("qkv", "attention", "o", "allreduce", "gate_up", "down", "lm_head", "argmax_exchange", "other")
 
 
+def run_timeline_prefill(args):
+    """Where a prompt pass's time goes (trace build, one GPU): every CTA of the traced kernels
+    stamps %globaltimer at entry, release from griddepcontrol.wait and exit. Per kernel role
+    (activation split, QKV, attention, O, gate/up, down, lm_head) the line gives the launches per
+    pass and, averaged over them, the span (end of the previous launch's last CTA to end of this
+    launch's last CTA) and the median CTA duration after release, in microseconds."""
+    os.environ["VSL_LIBRARY"] = "trace"
+    import numpy as np
+    import torch
+
+    import vsl
+    from vsl import synth
+    assert vsl.LIB_PATH.endswith("libvsl_trace.so"), vsl.LIB_PATH
+    cfg = dict(CONFIG_7B)
+    if args.layers:
+        cfg["n_layers"] = args.layers
+    prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
+    with vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, max_seq=512) as eng:
+        for _ in range(3):
+            eng.reset()
+            eng.prefill(prompt)
+        eng.reset()
+        torch.cuda.synchronize()
+        vsl.trace_records(reset=True)
+        t0 = time.perf_counter()
+        eng.prefill(prompt)
+        host_ms = (time.perf_counter() - t0) * 1e3
+        recs = vsl.trace_records(reset=True)
+        if eng.device_status() != 0:
+            raise SystemExit(f"device status {eng.device_status()}")
+    launches = sorted((recs[recs["id"] == lid] for lid in np.unique(recs["id"])), key=lambda r: int(r["t1"].min()))
+    roles, prev_end, after_attn = {}, None, False
+    for r in launches:
+        tag = int(r["tag"].max())
+        if tag == 2100:
+            role = "split"
+        elif tag == 2200 or 900 <= tag < 1000:
+            role, after_attn = "attention", True
+        else:
+            ek = (tag - 2000) // 10 if tag >= 2000 else tag // 100
+            role = {3: "qkv", 2: "gate_up", 4: "lm_head"}.get(ek)
+            if role is None:
+                role = "o" if after_attn else "down"
+                after_attn = False
+        a = roles.setdefault(role, {"launches": 0, "span": 0.0, "cta_us": 0.0})
+        a["launches"] += 1
+        t2max = int(r["t2"].max())
+        if prev_end is not None:
+            a["span"] += (t2max - prev_end) / 1e3
+        a["cta_us"] += float(np.median(r["t2"] - r["t1"])) / 1e3
+        prev_end = t2max
+    span_us = (max(int(r["t2"].max()) for r in launches) - min(int(r["t0"].min()) for r in launches)) / 1e3
+    out = {k: {"launches": v["launches"], "span_us": round(v["span"] / v["launches"], 2),
+               "cta_us_p50": round(v["cta_us"] / v["launches"], 2)} for k, v in roles.items()}
+    print(json.dumps({"timeline": f"prompt pass, 7B fp16, {PROMPT} tokens", "layers": cfg["n_layers"],
+                      "traced_span_us": round(span_us, 1), "host_ms": round(host_ms, 3), "roles": out,
+                      "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}))
+    return 0
+
+
 def run_timeline(args):
     """Where a decode step's time goes: every CTA of every kernel stamps %globaltimer at entry, at
     its release from griddepcontrol.wait and at exit (trace build). Per kernel role (QKV, attention,
@@ -880,6 +943,8 @@ def run_timeline(args):
 
 def main():
     args = parse()
+    if args.timeline_prefill:
+        return run_timeline_prefill(args)
     if args.timeline:
         return run_timeline(args)
     if args.profile_case:

@@ -34,6 +34,9 @@
 #include "common.cuh"
 #include "kv_map.h"
 #include "launch.cuh"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(prefill)
 
 namespace vsl {
 
@@ -58,6 +61,7 @@ struct FpArgs {
     uint32_t idesc_s;           // Q2 (A, K-major) . K (B, K-major)
     uint32_t idesc_pv;          // P2 (A, K-major) . V (B, MN-major)
     SparseMask sp;
+    unsigned trace_id;          // launch id of the trace build (unused otherwise)
 };
 
 __device__ __forceinline__ void fp_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -113,6 +117,7 @@ __device__ __forceinline__ uint32_t fp_off(int r, int col) {
 __global__ void __launch_bounds__(FP_THREADS, 1)
     vsl_prefill_attention_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                                  const __grid_constant__ FpArgs a) {
+    VSL_TRACE_ENTRY();
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t k_full, k_empty, v_full, v_empty, s_full[2], s_free[2], q_ready, p_ready, o_full,
         o_free;
@@ -154,6 +159,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     }
     // q, K and V of this chunk are written by the preceding projection
     pdl_wait();
+    VSL_TRACE_RELEASED();
     __syncthreads();
     // this thread's query row: position, first attended position; the block's cache length and
     // lowest first position
@@ -286,7 +292,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         {
             const size_t qs = (size_t)a.n_heads * FP_HD;
             const int col = 4 * lane;
-#pragma unroll 4
+#pragma unroll 8
             for (int k = 0; k < FP_ROWS / 4; k++) {
                 const int r = warp + 4 * k;
                 float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -425,6 +431,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         fp_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FP_TMEM_COLS) : "memory");
     }
+    VSL_TRACE_EXIT(a.trace_id, 2200u);
 }
 
 bool flash_prefill_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int page_size) {
@@ -456,6 +463,7 @@ int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache,
     a.scale = 1.0f / sqrtf((float)FP_HD);
     a.out = out;
     a.status = status;
+    a.trace_id = VSL_TRACE_ID();
     if (sparse && sparse->min_len > 0) {
         if (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0)
             return set_error(VSL_ERR_INVALID, "flash_prefill: sparse mask window %d, global %d, block %d",

@@ -42,19 +42,29 @@
 #include "epilogue.cuh"
 #include "launch.cuh"
 #include "tc_gemm.h"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(tc)
 
 namespace vsl {
 
 constexpr int TC_THREADS = 192;
 constexpr int TC_BM = 128;            // rows of W per tile (MMA M)
 constexpr int TC_ATOM = 64;           // k per 128-byte swizzle atom of 16-bit values
-#ifndef VSL_TC_KA
-#define VSL_TC_KA 2
+constexpr int TC_A_ATOM = TC_BM * TC_ATOM * 2;   // 16 KB of weights per atom
+// A stage (one k-block) holds KA atoms of W and of X2: two (128 k) for up to TC_KA1_ROWS - 1
+// padded activation rows, one (64 k) from there on, where the X2 tile (2 x 64 B per k) is large
+// enough that finer, deeper stages overlap copies and MMAs better.
+#ifndef VSL_TC_KA1_ROWS
+#define VSL_TC_KA1_ROWS 96
 #endif
-constexpr int TC_KA = VSL_TC_KA;      // atoms per stage (build-time tuning: 1 or 2)
-constexpr int TC_BK = TC_ATOM * TC_KA;           // k per stage (one k-block)
-constexpr int TC_A_ATOM = TC_BM * TC_ATOM * 2;   // 16 KB
-constexpr int TC_A_BYTES = TC_A_ATOM * TC_KA;    // 32 KB of weights per stage
+constexpr int TC_KA1_ROWS = VSL_TC_KA1_ROWS;
+// From this many activation rows on, the grid is always one CTA per SM (stream-K), since the
+// MMA work of a whole row tile per CTA would outlast its weight stream.
+#ifndef VSL_TC_SK_ROWS
+#define VSL_TC_SK_ROWS 1024
+#endif
+constexpr int TC_SK_ROWS = VSL_TC_SK_ROWS;
 constexpr int TC_MAX_STAGES = 12;
 constexpr int TC_SMEM_BUDGET = 200 * 1024;     // ring bytes (+1 KB alignment slack)
 
@@ -154,10 +164,12 @@ __device__ __forceinline__ bool next_segment(const TcArgs& a, long long& f, long
 // ---------------------------------------------------------------------------------------
 template <typename WT>
 __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict__ x, int K, const float* __restrict__ nw,
-                                                     float eps, int Bp, WT* __restrict__ x2) {
+                                                     float eps, int Bp, WT* __restrict__ x2, unsigned trace_id) {
     __shared__ float red[8];
     const int b = blockIdx.x;
+    VSL_TRACE_ENTRY();
     pdl_wait();
+    VSL_TRACE_RELEASED();
     pdl_launch_dependents();
     const float* xr = x + (size_t)b * K;
     float den = 1.0f;
@@ -187,6 +199,7 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
         hi[k] = h;
         lo[k] = l;
     }
+    VSL_TRACE_EXIT(trace_id, 2100u);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -194,52 +207,69 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
 // ---------------------------------------------------------------------------------------
 // Epilogue of up to TC_EB activation rows b0.. for this thread's weight row: v[j] is the
 // finished sum for row `row`, sequence b0 + j. Rows pair up within a warp (lane parity = row
-// parity) and the even lane runs the pair. All global inputs of the chunk (residuals, positions,
-// RoPE terms) are requested before any is used, so the chunk costs one memory round trip.
+// parity) and both lanes of a pair work on the pair: the even lane on the chunk's first TC_EB/2
+// sequences, the odd lane on the rest, each given its partner's sums by one shuffle per
+// sequence. The positions and KV pages of the sequences (EK_QKV) come from shared memory, staged
+// once per CTA; the remaining global inputs of the half-chunk (residuals, RoPE terms) are
+// requested before any is used, so a half-chunk costs one memory round trip.
 constexpr int TC_EB = 16;
+constexpr int TC_EH = TC_EB / 2;
 
 template <int EK>
-__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int b_end, int row, const float* v,
-                                                  int step) {
+__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_pos, const int* s_page, int b0,
+                                                  int b_end, int row, const float* v, int step) {
     const int lane = threadIdx.x & 31;
-    float v1[TC_EB];
+    const bool odd = lane & 1;
+    const int r0 = row & ~1;  // the pair's first row
+    // own[i] / mate[i]: this lane's and its partner's sums for sequence b0 + jb + i
+    float own[TC_EH], mate[TC_EH];
 #pragma unroll
-    for (int j = 0; j < TC_EB; j++) v1[j] = __shfl_down_sync(0xffffffffu, v[j], 1);
-    const bool act = !(lane & 1) && row < a.N;
-    const bool has1 = row + 1 < a.N;
+    for (int i = 0; i < TC_EH; i++) {
+        own[i] = odd ? v[TC_EH + i] : v[i];
+        mate[i] = __shfl_xor_sync(0xffffffffu, odd ? v[i] : v[TC_EH + i], 1);
+    }
+    const int jb = odd ? TC_EH : 0;
+    const bool act = r0 < a.N;
+    const bool has1 = r0 + 1 < a.N;
     const int nb = b_end - b0 < TC_EB ? b_end - b0 : TC_EB;
-    unsigned long long best[EK == EK_LMHEAD ? TC_EB : 1];
+    unsigned long long best[EK == EK_LMHEAD ? TC_EH : 1];
 #pragma unroll
-    for (int j = 0; j < (EK == EK_LMHEAD ? TC_EB : 1); j++) best[j] = 0ull;
+    for (int i = 0; i < (EK == EK_LMHEAD ? TC_EH : 1); i++) best[i] = 0ull;
     if (act) {
-        EpiPre pre[TC_EB];
+        EpiPre pre[TC_EH];
 #pragma unroll
-        for (int j = 0; j < TC_EB; j++) {
-            if (j < nb) {
+        for (int i = 0; i < TC_EH; i++) {
+            if (jb + i < nb) {
+                const int b = b0 + jb + i;
                 int pos = 0, page = 0;
-                if (EK == EK_QKV) epi_pos_page(a.ep, b0 + j, pos, page);
-                pre[j] = epi_fetch<EK>(a.ep, b0 + j, row, has1, pos, page);
+                if (EK == EK_QKV) {
+                    pos = s_pos[b];
+                    page = s_page[b];
+                }
+                pre[i] = epi_fetch<EK>(a.ep, b, r0, has1, pos, page);
             }
         }
 #pragma unroll
-        for (int j = 0; j < TC_EB; j++) {
-            if (j < nb) {
+        for (int i = 0; i < TC_EH; i++) {
+            if (jb + i < nb) {
                 unsigned long long bb = 0ull;
-                epi_apply<EK>(a.ep, pre[j], b0 + j, row, row >> 1, has1, v[j], v1[j], bb, step);
-                if (EK == EK_LMHEAD) best[EK == EK_LMHEAD ? j : 0] = bb;
+                const float s0 = odd ? mate[i] : own[i], s1 = odd ? own[i] : mate[i];
+                epi_apply<EK>(a.ep, pre[i], b0 + jb + i, r0, r0 >> 1, has1, s0, s1, bb, step);
+                if (EK == EK_LMHEAD) best[EK == EK_LMHEAD ? i : 0] = bb;
             }
         }
     }
     if (EK == EK_LMHEAD) {
+        // sequence b0 + jb + i: the maximum over the lanes of this parity
 #pragma unroll
-        for (int j = 0; j < TC_EB; j++) {
-            unsigned long long bb = best[EK == EK_LMHEAD ? j : 0];
+        for (int i = 0; i < TC_EH; i++) {
+            unsigned long long bb = best[EK == EK_LMHEAD ? i : 0];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
+            for (int o = 16; o > 1; o >>= 1) {
                 const unsigned long long t = __shfl_xor_sync(0xffffffffu, bb, o);
                 bb = t > bb ? t : bb;
             }
-            if (lane == 0 && bb && j < nb) atomicMax(a.ep.slots + b0 + j, bb);
+            if (lane < 2 && bb && jb + i < nb) atomicMax(a.ep.slots + b0 + jb + i, bb);
         }
     }
 }
@@ -247,8 +277,8 @@ __device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, int b0, int b
 // Sum of the partials of split row tile rt from CTAs first..lastc (in CTA order: the result
 // does not depend on arrival order) for activation rows [bs0, bs1), then the epilogue.
 template <int EK>
-__device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, int G, int rt, int first, int lastc, int bs0, int bs1,
-                                              int row, int rloc, int step) {
+__device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos, const int* s_page, int G, int rt,
+                                              int first, int lastc, int bs0, int bs1, int row, int rloc, int step) {
     for (int b0 = bs0; b0 < bs1; b0 += TC_EB) {
         // TC_EB rows x 4 CTAs of loads are in flight at a time
         float v[TC_EB];
@@ -272,11 +302,11 @@ __device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, int G, int rt, in
 #pragma unroll
                     for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
         }
-        tc_epilogue_chunk<EK>(a, b0, bs1, row, v, step);
+        tc_epilogue_chunk<EK>(a, s_pos, s_page, b0, bs1, row, v, step);
     }
 }
 
-template <int EK>
+template <int EK, int KA>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     vsl_tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ TcArgs a) {
@@ -286,7 +316,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
     __shared__ int last_s;
+    __shared__ int s_pos[EK == EK_QKV ? TC_MAX_BATCH : 1], s_page[EK == EK_QKV ? TC_MAX_BATCH : 1];
 
+    VSL_TRACE_ENTRY();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ring = (smem_u32(smem_raw) + 1023u) & ~1023u;
     const int G = gridDim.x, c = blockIdx.x;
@@ -321,7 +353,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         // ================= producer =================
         if (lane == 0) {
-            const uint32_t tx = (uint32_t)(TC_A_BYTES + a.b_bytes);
+            const uint32_t tx = (uint32_t)(TC_A_ATOM * KA + a.b_bytes);
             long long it = 0;
             // weights do not depend on the previous kernel: the first stages' W tiles are
             // requested before griddepcontrol.wait, their X2 tiles after it
@@ -335,12 +367,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int kb = s2.kb0; kb < s2.kb1 && pre < S; kb++, pre++) {
                         mbar_arrive_expect_tx(&full[pre], tx);
 #pragma unroll
-                        for (int at = 0; at < TC_KA; at++)
-                            tma_load_2d(ring + pre * a.stage_bytes + at * TC_A_ATOM, &map_w, kb * TC_BK + at * TC_ATOM,
+                        for (int at = 0; at < KA; at++)
+                            tma_load_2d(ring + pre * a.stage_bytes + at * TC_A_ATOM, &map_w, (kb * KA + at) * TC_ATOM,
                                         s2.rt * TC_BM, &full[pre]);
                     }
             }
             pdl_wait();
+            VSL_TRACE_RELEASED();
             pdl_launch_dependents();
             bool ok = true;
             // stage index and the parity of its empty-barrier phase advance incrementally (a
@@ -356,14 +389,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         }
                         mbar_arrive_expect_tx(&full[s], tx);
 #pragma unroll
-                        for (int at = 0; at < TC_KA; at++)
-                            tma_load_2d(ring + s * a.stage_bytes + at * TC_A_ATOM, &map_w, kb * TC_BK + at * TC_ATOM,
+                        for (int at = 0; at < KA; at++)
+                            tma_load_2d(ring + s * a.stage_bytes + at * TC_A_ATOM, &map_w, (kb * KA + at) * TC_ATOM,
                                         sg.rt * TC_BM, &full[s]);
                     }
 #pragma unroll
-                    for (int at = 0; at < TC_KA; at++)
-                        tma_load_2d(ring + s * a.stage_bytes + TC_A_BYTES + at * a.b_atom, &map_x,
-                                    kb * TC_BK + at * TC_ATOM, 0, &full[s]);
+                    for (int at = 0; at < KA; at++)
+                        tma_load_2d(ring + s * a.stage_bytes + TC_A_ATOM * KA + at * a.b_atom, &map_x,
+                                    (kb * KA + at) * TC_ATOM, 0, &full[s]);
                     if (++s == S) {
                         s = 0;
                         epar ^= 1u;
@@ -404,9 +437,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = ring + s * a.stage_bytes, sb = sa + TC_A_BYTES;
+                    const uint32_t sa = ring + s * a.stage_bytes, sb = sa + TC_A_ATOM * KA;
 #pragma unroll
-                    for (int at = 0; at < TC_KA; at++) {
+                    for (int at = 0; at < KA; at++) {
                         const uint64_t ad = sw128_desc(sa + at * TC_A_ATOM), bd = sw128_desc(sb + at * a.b_atom);
 #pragma unroll
                         for (int k = 0; k < TC_ATOM / 16; k++)  // +32 bytes per 16 values inside the atom
@@ -441,6 +474,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int et = threadIdx.x - 64;  // 0..127
         int step = 0;
         if (EK == EK_LMHEAD && a.ep.inv_temp > 0.0f) step = *a.ep.step_counter;
+        if (EK == EK_QKV) {  // positions and KV pages of the sequences, once per CTA
+            for (int b = et; b < a.B; b += 128) {
+                int pos, page;
+                epi_pos_page(a.ep, b, pos, page);
+                s_pos[b] = pos;
+                s_page[b] = page;
+            }
+            named_barrier_sync(1, 128);
+        }
         long long f = f0;
         int si = 0;
         Segment sg;
@@ -469,7 +511,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
                 for (int i = 0; i < TC_EB; i++) hi[i] += lo[i];
                 if (sg.full) {
-                    tc_epilogue_chunk<EK>(a, b0, a.B, row, hi, step);
+                    tc_epilogue_chunk<EK>(a, s_pos, s_page, b0, a.B, row, hi, step);
                 } else {
 #pragma unroll
                     for (int i = 0; i < TC_EB; i++)
@@ -495,7 +537,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     named_barrier_sync(1, 128);
                     if (last_s) {
                         __threadfence();
-                        tc_fixup_rows<EK>(a, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
+                        tc_fixup_rows<EK>(a, s_pos, s_page, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
                         if (et == 0) a.counters[sg.rt] = 0;
                     }
                 }
@@ -526,7 +568,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             __threadfence();
-            tc_fixup_rows<EK>(a, G, rt, first, lastc, (int)((long long)a.B * k / ns),
+            tc_fixup_rows<EK>(a, s_pos, s_page, G, rt, first, lastc, (int)((long long)a.B * k / ns),
                               (int)((long long)a.B * (k + 1) / ns), rt * TC_BM + rloc, rloc, step);
             // the last contributor through here clears the tile's counters for the next launch
             // (every contributor has seen all arrivals by now)
@@ -548,6 +590,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * a.tmem_cols)
                      : "memory");
     }
+    VSL_TRACE_EXIT(a.ep.trace_id, (unsigned)(2000 + EK * 10 + KA));
 }
 
 // ---------------------------------------------------------------------------------------
@@ -602,10 +645,10 @@ bool tc_supported(int wdtype, int N, int K, int B) {
            (K % 8) == 0;
 }
 
-template <int EK>
+template <int EK, int KA>
 static int launch_tc(const TcArgs& a, const CUtensorMap& mw, const CUtensorMap& mx, int grid, size_t smem,
                      cudaStream_t st) {
-    auto kern = vsl_tc_gemm_kernel<EK>;
+    auto kern = vsl_tc_gemm_kernel<EK, KA>;
     static thread_local int configured_dev = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -634,12 +677,13 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     a.B = p.B;
     a.Bp = pad_batch(p.B);
     a.n_rt = (p.N + TC_BM - 1) / TC_BM;
-    a.nkb = (p.K + TC_BK - 1) / TC_BK;
+    const int ka = a.Bp >= TC_KA1_ROWS ? 1 : 2;
+    a.nkb = (p.K + TC_ATOM * ka - 1) / (TC_ATOM * ka);
     a.T = (long long)a.n_rt * a.nkb;
     const int n = 2 * a.Bp;  // MMA N (multiple of 16)
     a.b_atom = n * TC_ATOM * 2;  // n % 16 == 0: a multiple of 2 KB, so every atom stays 1 KB aligned
-    a.b_bytes = a.b_atom * TC_KA;
-    a.stage_bytes = TC_A_BYTES + a.b_bytes;
+    a.b_bytes = a.b_atom * ka;
+    a.stage_bytes = TC_A_ATOM * ka + a.b_bytes;
     a.stages = TC_SMEM_BUDGET / a.stage_bytes;
     if (a.stages > TC_MAX_STAGES) a.stages = TC_MAX_STAGES;
     a.tmem_cols = 32;
@@ -663,13 +707,14 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     a.status = status;
     a.ep = p;
     a.ep.status = status;
+    a.ep.trace_id = VSL_TRACE_ID();
 
     // With at most one row tile per SM, the grid is a multiple of the tile count: every tile is
     // split into the same number of k ranges and no CTA straddles two tiles (fewer partial
     // segments and fixups; 12288 x 4096 at 64 rows: 28.6 us on 96 CTAs against 40.2 us on 148).
     // Otherwise stream-K spreads the k-blocks evenly over every SM.
     int grid = G0;
-    if (a.n_rt <= G0) grid = a.n_rt * (G0 / a.n_rt);
+    if (a.n_rt <= G0 && a.Bp < TC_SK_ROWS) grid = a.n_rt * (G0 / a.n_rt);
     if ((long long)grid > a.T) grid = (int)a.T;
     // many contributors per split tile (at least two CTAs per row tile) and a long sum
     a.dist_fixup = a.B >= 32 && 2 * a.n_rt <= grid ? 1 : 0;
@@ -684,20 +729,30 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     cudaError_t e;
     if (wdtype == VSL_BF16)
         e = launch_k(vsl_xsplit_kernel<__nv_bfloat16>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
-                     static_cast<__nv_bfloat16*>(x2));
+                     static_cast<__nv_bfloat16*>(x2), (unsigned)VSL_TRACE_ID());
     else
         e = launch_k(vsl_xsplit_kernel<__half>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
-                     static_cast<__half*>(x2));
+                     static_cast<__half*>(x2), (unsigned)VSL_TRACE_ID());
     rc = launch_status(e, "tc activation split");
     if (rc) return rc;
 
     const size_t smem = (size_t)a.stages * a.stage_bytes + 1024;
     switch (kind) {
-        case EK_STORE: return launch_tc<EK_STORE>(a, mw, mx, grid, smem, st);
-        case EK_ADD: return launch_tc<EK_ADD>(a, mw, mx, grid, smem, st);
-        case EK_SWIGLU: return launch_tc<EK_SWIGLU>(a, mw, mx, grid, smem, st);
-        case EK_QKV: return launch_tc<EK_QKV>(a, mw, mx, grid, smem, st);
-        default: return launch_tc<EK_LMHEAD>(a, mw, mx, grid, smem, st);
+        case EK_STORE:
+            return ka == 1 ? launch_tc<EK_STORE, 1>(a, mw, mx, grid, smem, st)
+                           : launch_tc<EK_STORE, 2>(a, mw, mx, grid, smem, st);
+        case EK_ADD:
+            return ka == 1 ? launch_tc<EK_ADD, 1>(a, mw, mx, grid, smem, st)
+                           : launch_tc<EK_ADD, 2>(a, mw, mx, grid, smem, st);
+        case EK_SWIGLU:
+            return ka == 1 ? launch_tc<EK_SWIGLU, 1>(a, mw, mx, grid, smem, st)
+                           : launch_tc<EK_SWIGLU, 2>(a, mw, mx, grid, smem, st);
+        case EK_QKV:
+            return ka == 1 ? launch_tc<EK_QKV, 1>(a, mw, mx, grid, smem, st)
+                           : launch_tc<EK_QKV, 2>(a, mw, mx, grid, smem, st);
+        default:
+            return ka == 1 ? launch_tc<EK_LMHEAD, 1>(a, mw, mx, grid, smem, st)
+                           : launch_tc<EK_LMHEAD, 2>(a, mw, mx, grid, smem, st);
     }
 }
 

@@ -140,7 +140,7 @@ def lib() -> C.CDLL:
     return L
 
 
-TRACE_UNITS = ("gemv", "attention", "p2p")
+TRACE_UNITS = ("gemv", "attention", "p2p", "tc", "prefill")
 
 
 def trace_records(reset: bool = True):
