@@ -279,7 +279,7 @@ def run_reference(args):
 
 def profiled_traffic():
     """DRAM read+write bytes per launch of the dominant kernel from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "gemv_gateup_7b_fp16_bs1.md")
+    path = os.path.join(ROOT, "profiles", "gemv_decode_7b_fp16_bs1.md")
     try:
         with open(path) as f:
             for line in f:
@@ -336,7 +336,7 @@ def dominant_kernel_roofline(torch, vsl, cfg, tp, hbm_peak, peak_kind):
             "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
             "peak_kind": peak_kind, "bytes_per_launch": bytes_per_launch, "us_per_launch": round(ms * 1e3, 3),
             "traffic": profiled_traffic() if tp == 1 else None,
-            "traffic_source": "profiles/gemv_gateup_7b_fp16_bs1.md (ncu, engine launch: includes the 16.8 MB "
+            "traffic_source": "profiles/gemv_decode_7b_fp16_bs1.md (ncu, engine launch: includes the 16.8 MB "
                               "L2 prefetch of the next projection)"}
 
 
@@ -380,15 +380,18 @@ def run_ours(args):
         eng.run(1, batch=B)
     elif w70:
         # the 2048-token prompt through the prompt pass once (time to first token, host call to
-        # sampled id, max over ranks)
+        # sampled id, max over ranks), after an untimed short prompt that allocates the pass's
+        # buffers
         prompt = synth.synth_ids(SEED, 0, PREFILL_70B, cfg["vocab"])
+        eng.prefill(prompt[:128])
+        eng.reset()
         if dist:
             dist.barrier()
         t_p = time.perf_counter()
         eng.prefill(prompt)
         ttft_s = vdist.max_over_ranks(dist, time.perf_counter() - t_p)
     else:
-        # prompt positions 0..127 through the prompt pass (two chunks of 64 rows); time to first
+        # prompt positions 0..127 through the prompt pass (one chunk of 128 rows); time to first
         # token through the host API (ids in, first sampled id out), the median of 3 after one
         # untimed call, each from an empty cache
         prompt = synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"])
@@ -793,6 +796,19 @@ def run_timeline_prefill(args):
         recs = vsl.trace_records(reset=True)
         if eng.device_status() != 0:
             raise SystemExit(f"device status {eng.device_status()}")
+    # phase stamps of the prompt attention (tags 2201-2206): [t0, t1] of a phase per CTA
+    ph = recs[(recs["tag"] > 2200) & (recs["tag"] < 2300)]
+    recs = recs[(recs["tag"] <= 2200) | (recs["tag"] >= 2300)]
+    main = {(int(r["id"]), int(r["blk"])): int(r["t1"]) for r in recs[recs["tag"] == 2200]}
+    phase_names = {2201: "stage_q", 2202: "scores_to_p_ready", 2203: "p_ready_to_pv_done", 2204: "softmax_warps_total",
+                   2205: "mma_waits_q", 2206: "mma_waits_k_issues_s", 2207: "scores_load_and_row_max"}
+    phases = {}
+    for tag, name in phase_names.items():
+        r = ph[ph["tag"] == tag]
+        if len(r):
+            rel = [int(x["t0"]) - main.get((int(x["id"]), int(x["blk"])), int(x["t0"])) for x in r]
+            phases[name] = {"us_p50": round(float(np.median((r["t1"] - r["t0"]).astype(np.int64))) / 1e3, 2),
+                            "starts_after_release_us_p50": round(float(np.median(rel)) / 1e3, 2)}
     launches = sorted((recs[recs["id"] == lid] for lid in np.unique(recs["id"])), key=lambda r: int(r["t1"].min()))
     roles, prev_end, after_attn = {}, None, False
     for r in launches:
@@ -819,6 +835,7 @@ def run_timeline_prefill(args):
                "cta_us_p50": round(v["cta_us"] / v["launches"], 2)} for k, v in roles.items()}
     print(json.dumps({"timeline": f"prompt pass, 7B fp16, {PROMPT} tokens", "layers": cfg["n_layers"],
                       "traced_span_us": round(span_us, 1), "host_ms": round(host_ms, 3), "roles": out,
+                      "attention_phases": phases,
                       "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}))
     return 0
 

@@ -11,18 +11,20 @@
 //   * S[128 rows][128 positions] = Q2 . K^T (tcgen05.mma kind::f16, M = N = 128, fp32 in TMEM),
 //     with the fp32 query split into fp16 hi and lo tiles that accumulate into the same scores
 //     (about 22 bits of the query survive);
-//   * online softmax (fp32) by 4 warps, one query row per thread (its TMEM lane), over two reads
-//     of the row's scores (maximum, then probabilities), written back to shared memory as fp16
-//     hi/lo tiles P2;
+//   * online softmax (fp32) by 8 warps, two per TMEM lane quarter: a thread takes one query row
+//     (its TMEM lane) and half of the chunk's 128 score columns, read with one 64-column TMEM
+//     load (the row maximum is combined with the partner warp through shared memory), and
+//     writes its half of the row back as fp16 hi/lo tiles P2;
 //   * PV[128 rows][128 dims] = P2 . V (V as the MN-major B operand, in place as it lands from
-//     TMA) into TMEM; each thread folds its row into fp32 registers with the softmax rescale.
+//     TMA) into TMEM; each thread folds its half of the row's dims into fp32 registers with the
+//     softmax rescale.
 // K and V of a chunk arrive by tensor TMA (two 64-position pages x two 64-column 128-byte-swizzle
 // atoms each) into single K and V tiles with their own barriers, so the next chunk's K loads
 // while this chunk's softmax runs. The next chunk's scores are issued before this chunk's
 // product. Rows past the cache end are zeroed in the V tile before the product (0 x garbage);
 // rows of K past the end give scores that the mask drops.
-// Roles: warps 0-3 softmax and accumulation (TMEM lane quarter = warp), warp 4 TMA producer,
-// warp 5 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second)
+// Roles: warps 0-7 softmax and accumulation (TMEM lane quarter = warp % 4, column half =
+// warp / 4), warp 8 TMA producer, warp 9 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second)
 // and records VSL_ERR_TIMEOUT; the kernel then drains its copies and MMAs and frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -38,9 +40,20 @@
 
 VSL_TRACE_UNIT(prefill)
 
+// Phase stamps of the trace build: one extra record per CTA and phase, [t0, t1] of the phase
+#ifdef VSL_TRACE
+#define FP_STAMP(var) const uint64_t var = vsl::trace_now()
+#define FP_PHASE(tag, ta, tb) vsl_trace_record(a.trace_id, (tag), (ta), (tb))
+#else
+#define FP_STAMP(var)
+#define FP_PHASE(tag, ta, tb)
+#endif
+
 namespace vsl {
 
-constexpr int FP_THREADS = 192;        // 4 softmax warps, TMA producer, MMA issuer
+constexpr int FP_SM_WARPS = 8;         // softmax warps
+constexpr int FP_THREADS = 32 * FP_SM_WARPS + 64;  // + TMA producer, MMA issuer
+constexpr int FP_SM_THREADS = 32 * FP_SM_WARPS;
 constexpr int FP_ROWS = 128;           // query rows per CTA (MMA M)
 constexpr int FP_CHUNK = 128;          // positions per chunk
 constexpr int FP_HD = 128;
@@ -96,16 +109,24 @@ __device__ __forceinline__ void fp_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void fp_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+// 64 consecutive fp32 columns of this warp's 32 TMEM lanes, one load and one wait
+__device__ __forceinline__ void fp_ld64(uint32_t taddr, float* v) {
+    uint32_t r[64];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+          "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+          "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+          "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+          "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ int fp_abort(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 // byte offset of 16-bit column `col` (0..127) of row `r` in a 128 x 128 K-major swizzled tile
@@ -123,6 +144,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         o_free;
     __shared__ uint32_t tmem_s;
     __shared__ int abort_s, len_s, lo_s;
+    __shared__ float red_m[2][2][FP_ROWS], red_l[2][FP_ROWS];  // row maxima (by chunk parity) and sums per half
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -138,12 +160,12 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         mbar_init(&v_empty, 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+            mbar_init(&s_free[i], FP_SM_WARPS);
         }
-        mbar_init(&q_ready, 4);
-        mbar_init(&p_ready, 4);
+        mbar_init(&q_ready, FP_SM_WARPS);
+        mbar_init(&p_ready, FP_SM_WARPS);
         mbar_init(&o_full, 1);
-        mbar_init(&o_free, 4);
+        mbar_init(&o_free, FP_SM_WARPS);
         mbar_fence_init();
         abort_s = 0;
         len_s = 0;
@@ -151,7 +173,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_k)) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_v)) : "memory");
     }
-    if (warp == 5) {
+    if (warp == FP_SM_WARPS + 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_s)),
                      "r"(FP_TMEM_COLS)
                      : "memory");
@@ -164,12 +186,15 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     // this thread's query row: position, first attended position; the block's cache length and
     // lowest first position
     int pr = -1, first = INT_MAX;
-    if (threadIdx.x < FP_ROWS && r0 + (int)threadIdx.x < a.P) {
-        pr = __ldg(a.pos + r0 + threadIdx.x);
+    const int row = threadIdx.x & (FP_ROWS - 1);
+    if (threadIdx.x < FP_SM_THREADS && r0 + row < a.P) {
+        pr = __ldg(a.pos + r0 + row);
         pr = pr < 0 ? 0 : (pr >= a.max_len ? a.max_len - 1 : pr);
         first = sparse_first(a.sp, pr);
-        atomicMax(&len_s, pr + 1);
-        atomicMin(&lo_s, first);
+        if (threadIdx.x < FP_ROWS) {
+            atomicMax(&len_s, pr + 1);
+            atomicMin(&lo_s, first);
+        }
     }
     fp_fence_before();
     __syncthreads();
@@ -180,7 +205,7 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     const int c0 = (lo_s == INT_MAX ? 0 : lo_s) / FP_CHUNK;
     const int n = (len + FP_CHUNK - 1) / FP_CHUNK - c0;  // chunks of the block
 
-    if (warp == 4) {
+    if (warp == FP_SM_WARPS) {
         // ================= TMA producer: K(i) and V(i) into single tiles =================
         if (lane == 0) {
             int issued_k = 0, issued_v = 0;
@@ -221,10 +246,13 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             if (issued_k > 0) mbar_wait(&k_full, (uint32_t)((issued_k - 1) & 1));
             if (issued_v > 0) mbar_wait(&v_full, (uint32_t)((issued_v - 1) & 1));
         }
-    } else if (warp == 5) {
+    } else if (warp == FP_SM_WARPS + 1) {
         // ================= MMA issue =================
         if (lane == 0) {
+            FP_STAMP(tm0);
             bool ok = mbar_wait(&q_ready, 0u);
+            FP_STAMP(tm_q);
+            FP_PHASE(2205u, tm0, tm_q);
             int s_issued = 0, pv_issued = 0;
             auto issue_s = [&](int i) -> bool {
                 if (!mbar_wait(&k_full, (uint32_t)(i & 1))) return false;
@@ -265,6 +293,8 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
                 return true;
             };
             if (ok && n > 0) ok = issue_s(0);
+            FP_STAMP(tm_s);
+            FP_PHASE(2206u, tm_q, tm_s);  // waits for K(0), then issues S(0)
             for (int i = 0; i < n && ok; i++) {
                 if (fp_abort(&abort_s)) {
                     ok = false;
@@ -286,15 +316,18 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         }
         __syncwarp();
     } else {
-        // ================= softmax + accumulation (warps 0-3; thread t = query row t) =================
-        const int t = threadIdx.x;
+        // ===== softmax + accumulation (warps 0-7; row = TMEM lane, hc = half of the columns) =====
+        const int t = row;            // query row = TMEM lane
+        const int hc = warp >> 2;     // score columns / head dims [64 hc, 64 hc + 64)
+        const int th = threadIdx.x;   // 0..255
+        FP_STAMP(ts_setup);
         // ---- stage Q2: rows of this head as fp16 hi / lo, 128-byte swizzle ----
         {
             const size_t qs = (size_t)a.n_heads * FP_HD;
             const int col = 4 * lane;
 #pragma unroll 8
-            for (int k = 0; k < FP_ROWS / 4; k++) {
-                const int r = warp + 4 * k;
+            for (int k = 0; k < FP_ROWS / FP_SM_WARPS; k++) {
+                const int r = warp + FP_SM_WARPS * k;
                 float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
                 if (r0 + r < a.P)
                     x = __ldcg(reinterpret_cast<const float4*>(a.q + (size_t)(r0 + r) * qs + (size_t)h * FP_HD + col));
@@ -313,57 +346,59 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&q_ready);
         }
-        float o[FP_HD];
+        FP_STAMP(ts_q);
+        if (th == 0) FP_PHASE(2201u, ts_setup, ts_q);
+        constexpr int HALF = FP_CHUNK / 2;  // == FP_HD / 2
+        float o[HALF];
 #pragma unroll
-        for (int j = 0; j < FP_HD; j++) o[j] = 0.0f;
-        float m = -CUDART_INF_F, l = 0.0f;
+        for (int j = 0; j < HALF; j++) o[j] = 0.0f;
+        float m = -CUDART_INF_F, l = 0.0f;  // l: this half's share of the row sum
         bool failed = false;
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const uint32_t lane_base = ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(hc * HALF);
         for (int i = 0; i < n; i++) {
             {
                 const bool bad = !mbar_wait(&s_full[i & 1], (uint32_t)((i >> 1) & 1)) || fp_abort(&abort_s);
-                if (named_barrier_or(1, 128, bad)) {  // the four warps leave together
+                if (named_barrier_or(1, FP_SM_THREADS, bad)) {  // the softmax warps leave together
                     failed = true;
                     break;
                 }
             }
             fp_fence_after();
-            const int cb = (c0 + i) * FP_CHUNK;  // position of score column 0
-            const int jlo = first - cb, jhi = pr - cb;  // valid columns: jlo <= j <= jhi
+            FP_STAMP(ts_s);
+            const int cb = (c0 + i) * FP_CHUNK + hc * HALF;  // position of this half's score column 0
+            const int jlo = first - cb, jhi = pr - cb;       // valid columns: jlo <= j <= jhi
             const uint32_t ts = tmem + lane_base + (uint32_t)((i & 1) * FP_CHUNK);
-            // pass 1: the row's maximum over its valid columns
+            // the row's maximum over its valid columns (both halves)
+            float sv[HALF];  // this half's scores, read once
+            fp_ld64(ts, sv);
             float cm = -CUDART_INF_F;
 #pragma unroll
-            for (int c16 = 0; c16 < FP_CHUNK / 16; c16++) {
-                float v[16];
-                fp_ld16(ts + (uint32_t)(c16 * 16), v);
-#pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    const int j = c16 * 16 + e;
-                    if (j >= jlo && j <= jhi) cm = fmaxf(cm, v[e] * a.scale);
-                }
-            }
+            for (int j = 0; j < HALF; j++)
+                if (j >= jlo && j <= jhi) cm = fmaxf(cm, sv[j] * a.scale);
+            red_m[i & 1][hc][t] = cm;
+            named_barrier_sync(1, FP_SM_THREADS);
+            cm = fmaxf(cm, red_m[i & 1][hc ^ 1][t]);
+            FP_STAMP(ts_m);
+            if (th == 0 && i == 0) FP_PHASE(2207u, ts_s, ts_m);
             const float mn = fmaxf(m, cm);
             const float alpha = mn == -CUDART_INF_F ? 1.0f : expf(m - mn);
-            // pass 2: probabilities, as fp16 hi / lo rows of P2 (P2 of the previous chunk has been
-            // read: its product completed before that chunk's fold below)
+            // probabilities, as fp16 hi / lo halves of the row of P2 (P2 of the previous chunk has
+            // been read: its product completed before that chunk's fold below)
             float ls = 0.0f;
 #pragma unroll
-            for (int c16 = 0; c16 < FP_CHUNK / 16; c16++) {
-                float v[16];
-                fp_ld16(ts + (uint32_t)(c16 * 16), v);
+            for (int c16 = 0; c16 < HALF / 16; c16++) {
                 __half ph[16], pl[16];
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
                     const int j = c16 * 16 + e;
-                    const float p = (j >= jlo && j <= jhi) ? expf(v[e] * a.scale - mn) : 0.0f;
+                    const float p = (j >= jlo && j <= jhi) ? expf(sv[j] * a.scale - mn) : 0.0f;
                     ls += p;
                     ph[e] = __float2half_rn(p);
                     pl[e] = __float2half_rn(p - __half2float(ph[e]));
                 }
 #pragma unroll
                 for (int hf = 0; hf < 2; hf++) {
-                    const uint32_t off = fp_off(t, c16 * 16 + hf * 8);
+                    const uint32_t off = fp_off(t, hc * HALF + c16 * 16 + hf * 8);
                     *reinterpret_cast<uint4*>(smem_g + pt + off) = *reinterpret_cast<const uint4*>(ph + hf * 8);
                     *reinterpret_cast<uint4*>(smem_g + pt + FP_TILE + off) = *reinterpret_cast<const uint4*>(pl + hf * 8);
                 }
@@ -373,41 +408,45 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             if (lane == 0) mbar_arrive(&s_free[i & 1]);
             m = mn;
             l = l * alpha + ls;
-            if (cb + FP_CHUNK > len) {
+            const int ccb = (c0 + i) * FP_CHUNK;  // position of V row 0
+            if (ccb + FP_CHUNK > len) {
                 // V rows past the cache end hold whatever the pool had (possibly NaN bit
-                // patterns): zero them so that 0 x garbage cannot reach the product
+                // patterns): zero them so that 0 x garbage cannot reach the product (thread th
+                // clears half `th / 128` of V row `th % 128`)
                 const bool bad = !mbar_wait(&v_full, (uint32_t)(i & 1));
-                if (named_barrier_or(1, 128, bad)) {
+                if (named_barrier_or(1, FP_SM_THREADS, bad)) {
                     failed = true;
                     break;
                 }
-                if (cb + t >= len) {
+                const int vr = th & (FP_CHUNK - 1), at = th >> 7;
+                if (ccb + vr >= len) {
 #pragma unroll
-                    for (int at = 0; at < 2; at++)
-#pragma unroll
-                        for (int c = 0; c < 8; c++)
-                            *reinterpret_cast<uint4*>(smem_g + vt + at * FP_ATOM + (t >> 3) * 1024 + (t & 7) * 128 +
-                                                      c * 16) = make_uint4(0, 0, 0, 0);
+                    for (int c = 0; c < 8; c++)
+                        *reinterpret_cast<uint4*>(smem_g + vt + at * FP_ATOM + (vr >> 3) * 1024 + (vr & 7) * 128 +
+                                                  c * 16) = make_uint4(0, 0, 0, 0);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_ready);
-            // ---- fold PV(i) into the row's accumulators ----
+            FP_STAMP(ts_p);
+            if (th == 0 && i == 0) FP_PHASE(2202u, ts_s, ts_p);
+            // ---- fold PV(i) into this half of the row's accumulators ----
             {
                 const bool bad = !mbar_wait(&o_full, (uint32_t)(i & 1)) || fp_abort(&abort_s);
-                if (named_barrier_or(1, 128, bad)) {
+                if (named_barrier_or(1, FP_SM_THREADS, bad)) {
                     failed = true;
                     break;
                 }
             }
             fp_fence_after();
+            FP_STAMP(ts_o);
+            if (th == 0 && i == 0) FP_PHASE(2203u, ts_p, ts_o);
+            {
+                float v[HALF];
+                fp_ld64(tmem + lane_base + (uint32_t)(2 * FP_CHUNK), v);
 #pragma unroll
-            for (int c16 = 0; c16 < FP_HD / 16; c16++) {
-                float v[16];
-                fp_ld16(tmem + lane_base + (uint32_t)(2 * FP_CHUNK + c16 * 16), v);
-#pragma unroll
-                for (int e = 0; e < 16; e++) o[c16 * 16 + e] = o[c16 * 16 + e] * alpha + v[e];
+                for (int j = 0; j < HALF; j++) o[j] = o[j] * alpha + v[j];
             }
             fp_fence_before();
             __syncwarp();
@@ -416,18 +455,25 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         if (failed) {
             set_status(a.status, VSL_ERR_TIMEOUT);
             atomicExch(&abort_s, 1);
-        } else if (pr >= 0) {
-            const float inv = 1.0f / l;  // l > 0: position pr is always attended
-            float* dst = a.out + ((size_t)(r0 + t) * a.n_heads + h) * FP_HD;
+        } else {
+            red_l[hc][t] = l;
+            named_barrier_sync(1, FP_SM_THREADS);
+            if (pr >= 0) {
+                const float inv = 1.0f / (red_l[0][t] + red_l[1][t]);  // > 0: position pr is always attended
+                float* dst = a.out + ((size_t)(r0 + t) * a.n_heads + h) * FP_HD + hc * HALF;
 #pragma unroll
-            for (int j = 0; j < FP_HD; j += 4)
-                *reinterpret_cast<float4*>(dst + j) = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+                for (int j = 0; j < HALF; j += 4)
+                    *reinterpret_cast<float4*>(dst + j) =
+                        make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+            }
+            FP_STAMP(ts_end);
+            if (th == 0) FP_PHASE(2204u, ts_setup, ts_end);
         }
     }
 
     fp_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == FP_SM_WARPS + 1) {
         fp_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(FP_TMEM_COLS) : "memory");
     }

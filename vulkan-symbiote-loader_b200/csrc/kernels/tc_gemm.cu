@@ -121,17 +121,26 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-// 16 consecutive fp32 columns of this warp's 32 TMEM lanes
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-    uint32_t r[16];
+
+// two 16-column pieces of this warp's 32 TMEM lanes (the hi and lo accumulator columns of
+// the same rows), one wait for both
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, uint32_t tb, float* va, float* vb) {
+    uint32_t r[32];
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(ta), "r"(tb)
+        : "memory");
 #pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+    for (int i = 0; i < 16; i++) {
+        va[i] = __uint_as_float(r[i]);
+        vb[i] = __uint_as_float(r[16 + i]);
+    }
 }
 
 // ---------------------------------------------------------------------------------------
@@ -161,7 +170,42 @@ __device__ __forceinline__ bool next_segment(const TcArgs& a, long long& f, long
 
 // ---------------------------------------------------------------------------------------
 // activation split: X2[b] = rn(xn), X2[Bp + b] = rn(xn - X2[b]), xn = RMSNorm(x[b]) or x[b]
+// One CTA per row. A row of up to XS_VEC x 1024 values is read once, as float4 per thread and
+// step, and kept in registers for both the sum of squares and the split; longer rows are read
+// twice. K % 8 == 0 (tc_supported), so rows and their halves stay 16- and 8-byte aligned.
 // ---------------------------------------------------------------------------------------
+constexpr int XS_VEC = 12;
+
+template <typename WT>
+__device__ __forceinline__ void xs_emit(WT* hi, WT* lo, int j, float4 t, const float* nw, bool nw4, float den) {
+    float e[4] = {t.x, t.y, t.z, t.w};
+    if (nw) {
+        float w[4];
+        if (nw4) {
+            const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw) + j);
+            w[0] = w4.x, w[1] = w4.y, w[2] = w4.z, w[3] = w4.w;
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++) w[q] = __ldg(nw + 4 * j + q);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) e[q] = e[q] / den * w[q];  // rms_norm.comp:32-34: x / sqrt(var) * w
+    }
+    WT h[4], l[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        if constexpr (std::is_same<WT, __half>::value) {
+            h[q] = __float2half_rn(e[q]);
+            l[q] = __float2half_rn(e[q] - __half2float(h[q]));
+        } else {
+            h[q] = __float2bfloat16_rn(e[q]);
+            l[q] = __float2bfloat16_rn(e[q] - __bfloat162float(h[q]));
+        }
+    }
+    *reinterpret_cast<uint2*>(hi + 4 * (size_t)j) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(lo + 4 * (size_t)j) = *reinterpret_cast<const uint2*>(l);
+}
+
 template <typename WT>
 __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict__ x, int K, const float* __restrict__ nw,
                                                      float eps, int Bp, WT* __restrict__ x2, unsigned trace_id) {
@@ -171,33 +215,48 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
     pdl_wait();
     VSL_TRACE_RELEASED();
     pdl_launch_dependents();
-    const float* xr = x + (size_t)b * K;
+    const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
+    const int n4 = K / 4;
+    const bool in_regs = n4 <= XS_VEC * 256;
+    const bool nw4 = ((uintptr_t)nw & 15) == 0;
+    float4 v[XS_VEC];
+    float ss = 0.0f;
+    if (in_regs) {
+#pragma unroll
+        for (int i = 0; i < XS_VEC; i++) {
+            const int j = threadIdx.x + i * 256;
+            v[i] = j < n4 ? __ldcg(xr + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+        if (nw) {
+#pragma unroll
+            for (int i = 0; i < XS_VEC; i++) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+        }
+    } else if (nw) {
+        for (int j = threadIdx.x; j < n4; j += 256) {
+            const float4 t = __ldcg(xr + j);
+            ss += t.x * t.x + t.y * t.y + t.z * t.z + t.w * t.w;
+        }
+    }
     float den = 1.0f;
     if (nw) {
-        float ss = 0.0f;
-        for (int k = threadIdx.x; k < K; k += 256) ss += xr[k] * xr[k];
         ss = warp_sum(ss);
         if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
         __syncthreads();
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < 8; w++) s += red[w];
-        den = sqrtf(s / (float)K + eps);  // rms_norm.comp:32-34: x / sqrt(var) * w
+        den = sqrtf(s / (float)K + eps);
     }
     WT* hi = x2 + (size_t)b * K;
     WT* lo = x2 + (size_t)(Bp + b) * K;
-    for (int k = threadIdx.x; k < K; k += 256) {
-        const float v = nw ? xr[k] / den * nw[k] : xr[k];
-        WT h, l;
-        if constexpr (std::is_same<WT, __half>::value) {
-            h = __float2half_rn(v);
-            l = __float2half_rn(v - __half2float(h));
-        } else {
-            h = __float2bfloat16_rn(v);
-            l = __float2bfloat16_rn(v - __bfloat162float(h));
+    if (in_regs) {
+#pragma unroll
+        for (int i = 0; i < XS_VEC; i++) {
+            const int j = threadIdx.x + i * 256;
+            if (j < n4) xs_emit(hi, lo, j, v[i], nw, nw4, den);
         }
-        hi[k] = h;
-        lo[k] = l;
+    } else {
+        for (int j = threadIdx.x; j < n4; j += 256) xs_emit(hi, lo, j, __ldcg(xr + j), nw, nw4, den);
     }
     VSL_TRACE_EXIT(trace_id, 2100u);
 }
@@ -215,12 +274,58 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
 constexpr int TC_EB = 16;
 constexpr int TC_EH = TC_EB / 2;
 
+// Global inputs of a chunk's epilogue for this lane's half of the sequences (residual pair or
+// RoPE terms; positions and pages stay in shared memory until the epilogue applies).
+struct TcPre {
+    float a0, a1;
+};
 template <int EK>
-__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_pos, const int* s_page, int b0,
-                                                  int b_end, int row, const float* v, int step) {
+__device__ __forceinline__ void tc_epi_fetch(const TcArgs& a, const int* s_pos, const int* s_page, int b0, int b_end,
+                                             int row, TcPre* pre) {
+    const int lane = threadIdx.x & 31;
+    const int r0 = row & ~1;  // the pair's first row
+    const int jb = (lane & 1) ? TC_EH : 0;
+    const int nb = b_end - b0 < TC_EB ? b_end - b0 : TC_EB;
+    const bool has1 = r0 + 1 < a.N;
+    if (r0 >= a.N) return;
+    if constexpr (EK == EK_QKV) {
+        // RoPE terms of the pair at each sequence's position (q and k rows only); the table row
+        // of a position comes staged from shared memory
+        const int hd = a.ep.head_dim;
+        if (r0 >= (a.ep.n_heads + a.ep.n_kv) * hd) return;
+        const int rc = (r0 % hd) >> 1;
+#pragma unroll
+        for (int i = 0; i < TC_EH; i++) {
+            const int b = b0 + jb + i;
+            if (jb + i < nb && s_page[b] >= 0) {
+                const size_t t = (size_t)s_pos[b] + rc;  // s_pos holds pos * head_dim / 2 here
+                pre[i] = TcPre{__ldg(a.ep.rope_cos + t), __ldg(a.ep.rope_sin + t)};
+            }
+        }
+        return;
+    }
+#pragma unroll
+    for (int i = 0; i < TC_EH; i++) {
+        if (jb + i < nb) {
+            const int b = b0 + jb + i;
+            int pos = 0, page = 0;
+            if (EK == EK_QKV) {
+                pos = s_pos[b];
+                page = s_page[b];
+            }
+            const EpiPre e = epi_fetch<EK>(a.ep, b, r0, has1, pos, page);
+            pre[i] = TcPre{e.a0, e.a1};
+        }
+    }
+}
+
+// The epilogue of a chunk given its fetched inputs.
+template <int EK>
+__device__ __forceinline__ void tc_epi_apply(const TcArgs& a, const int* s_pos, const int* s_page, const int* s_kvrow,
+                                             int b0, int b_end, int row, const float* v, const TcPre* pre, int step) {
     const int lane = threadIdx.x & 31;
     const bool odd = lane & 1;
-    const int r0 = row & ~1;  // the pair's first row
+    const int r0 = row & ~1;
     // own[i] / mate[i]: this lane's and its partner's sums for sequence b0 + jb + i
     float own[TC_EH], mate[TC_EH];
 #pragma unroll
@@ -232,29 +337,58 @@ __device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_
     const bool act = r0 < a.N;
     const bool has1 = r0 + 1 < a.N;
     const int nb = b_end - b0 < TC_EB ? b_end - b0 : TC_EB;
+    if constexpr (EK == EK_QKV) {
+        // q rows: rotated pair into q_out; k rows: rotated pair, v rows: as is, into the
+        // sequence's KV page (s_page: page, -1 outside the cache; s_kvrow: the row of KV group 0
+        // for the position)
+        if (!act) return;
+        const GemvParams& p = a.ep;
+        const int hd = p.head_dim, qd = p.n_heads * hd, kvd = p.n_kv * hd;
+        const int el = r0 % hd;
+        const bool is_q = r0 < qd, is_v = r0 >= qd + kvd;
+        const int g = is_q ? 0 : (is_v ? r0 - qd - kvd : r0 - qd) / hd;
+        void* cache = is_v ? p.v_cache : p.k_cache;
+#pragma unroll
+        for (int i = 0; i < TC_EH; i++) {
+            if (jb + i >= nb) continue;
+            const int b = b0 + jb + i;
+            if (s_page[b] < 0) {
+                if (p.status) atomicCAS(p.status, 0, VSL_ERR_BOUNDS);
+                continue;
+            }
+            const float s0 = odd ? mate[i] : own[i], s1 = odd ? own[i] : mate[i];
+            float o0 = s0, o1 = s1;
+            if (!is_v) {  // rotate q and k: adjacent pair (el, el + 1)
+                o0 = __fsub_rn(__fmul_rn(s0, pre[i].a0), __fmul_rn(s1, pre[i].a1));
+                o1 = __fadd_rn(__fmul_rn(s0, pre[i].a1), __fmul_rn(s1, pre[i].a0));
+            }
+            if (is_q) {
+                *reinterpret_cast<float2*>(p.q_out + (size_t)b * qd + r0) = make_float2(o0, o1);
+            } else {
+                const size_t idx = ((size_t)s_kvrow[b] + (size_t)g * p.page_size) * hd + el;
+                if (p.kvdtype == VSL_F16)
+                    *reinterpret_cast<__half2*>(static_cast<__half*>(cache) + idx) = __floats2half2_rn(o0, o1);
+                else if (p.kvdtype == VSL_BF16)
+                    *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(cache) + idx) =
+                        __floats2bfloat162_rn(o0, o1);
+                else
+                    *reinterpret_cast<float2*>(static_cast<float*>(cache) + idx) = make_float2(o0, o1);
+            }
+        }
+        return;
+    }
     unsigned long long best[EK == EK_LMHEAD ? TC_EH : 1];
 #pragma unroll
     for (int i = 0; i < (EK == EK_LMHEAD ? TC_EH : 1); i++) best[i] = 0ull;
     if (act) {
-        EpiPre pre[TC_EH];
-#pragma unroll
-        for (int i = 0; i < TC_EH; i++) {
-            if (jb + i < nb) {
-                const int b = b0 + jb + i;
-                int pos = 0, page = 0;
-                if (EK == EK_QKV) {
-                    pos = s_pos[b];
-                    page = s_page[b];
-                }
-                pre[i] = epi_fetch<EK>(a.ep, b, r0, has1, pos, page);
-            }
-        }
 #pragma unroll
         for (int i = 0; i < TC_EH; i++) {
             if (jb + i < nb) {
                 unsigned long long bb = 0ull;
                 const float s0 = odd ? mate[i] : own[i], s1 = odd ? own[i] : mate[i];
-                epi_apply<EK>(a.ep, pre[i], b0 + jb + i, r0, r0 >> 1, has1, s0, s1, bb, step);
+                const int b = b0 + jb + i;
+                const EpiPre e = {pre[i].a0, pre[i].a1, EK == EK_QKV ? s_pos[b] : 0, EK == EK_QKV ? s_page[b] : 0};
+                epi_apply<EK>(a.ep, e, b, r0, r0 >> 1, has1, s0, s1, bb, step);
                 if (EK == EK_LMHEAD) best[EK == EK_LMHEAD ? i : 0] = bb;
             }
         }
@@ -274,11 +408,21 @@ __device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_
     }
 }
 
+template <int EK>
+__device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_pos, const int* s_page,
+                                                  const int* s_kvrow, int b0, int b_end, int row, const float* v,
+                                                  int step) {
+    TcPre pre[TC_EH];
+    tc_epi_fetch<EK>(a, s_pos, s_page, b0, b_end, row, pre);
+    tc_epi_apply<EK>(a, s_pos, s_page, s_kvrow, b0, b_end, row, v, pre, step);
+}
+
 // Sum of the partials of split row tile rt from CTAs first..lastc (in CTA order: the result
 // does not depend on arrival order) for activation rows [bs0, bs1), then the epilogue.
 template <int EK>
-__device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos, const int* s_page, int G, int rt,
-                                              int first, int lastc, int bs0, int bs1, int row, int rloc, int step) {
+__device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos, const int* s_page, const int* s_kvrow,
+                                              int G, int rt, int first, int lastc, int bs0, int bs1, int row, int rloc,
+                                              int step) {
     for (int b0 = bs0; b0 < bs1; b0 += TC_EB) {
         // TC_EB rows x 4 CTAs of loads are in flight at a time
         float v[TC_EB];
@@ -302,7 +446,7 @@ __device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos,
 #pragma unroll
                     for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
         }
-        tc_epilogue_chunk<EK>(a, s_pos, s_page, b0, bs1, row, v, step);
+        tc_epilogue_chunk<EK>(a, s_pos, s_page, s_kvrow, b0, bs1, row, v, step);
     }
 }
 
@@ -316,7 +460,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ uint32_t tmem_base_s;
     __shared__ int abort_s;
     __shared__ int last_s;
-    __shared__ int s_pos[EK == EK_QKV ? TC_MAX_BATCH : 1], s_page[EK == EK_QKV ? TC_MAX_BATCH : 1];
+    // EK_QKV, per sequence: RoPE table row (pos * head_dim / 2), KV page (-1: outside the cache)
+    // and the cache row of KV group 0 at the position
+    __shared__ int s_pos[EK == EK_QKV ? TC_MAX_BATCH : 1], s_page[EK == EK_QKV ? TC_MAX_BATCH : 1],
+        s_kvrow[EK == EK_QKV ? TC_MAX_BATCH : 1];
 
     VSL_TRACE_ENTRY();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -478,8 +625,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int b = et; b < a.B; b += 128) {
                 int pos, page;
                 epi_pos_page(a.ep, b, pos, page);
-                s_pos[b] = pos;
+                s_pos[b] = pos * (a.ep.head_dim >> 1);
                 s_page[b] = page;
+                s_kvrow[b] = page < 0 ? 0 : page * a.ep.n_kv * a.ep.page_size + pos % a.ep.page_size;
             }
             named_barrier_sync(1, 128);
         }
@@ -504,14 +652,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int row = sg.rt * TC_BM + rloc;
             float* wsp = a.ws + ((size_t)c * 2 + sg.slot) * a.Bp * TC_BM;
             const uint32_t tl = tmem + (uint32_t)(buf * a.tmem_cols) + ((uint32_t)(q * 32) << 16);
+            // a full segment's epilogue requests the next chunk's global inputs before it
+            // applies this chunk, so their latency overlaps the work
+            TcPre pre[TC_EH], pre_next[TC_EH];
+            if (sg.full) tc_epi_fetch<EK>(a, s_pos, s_page, 0, a.B, row, pre);
             for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
                 float hi[TC_EB], lo[TC_EB];
-                tmem_ld16(tl + (uint32_t)b0, hi);
-                tmem_ld16(tl + (uint32_t)(a.Bp + b0), lo);
+                tmem_ld16x2(tl + (uint32_t)b0, tl + (uint32_t)(a.Bp + b0), hi, lo);
 #pragma unroll
                 for (int i = 0; i < TC_EB; i++) hi[i] += lo[i];
                 if (sg.full) {
-                    tc_epilogue_chunk<EK>(a, s_pos, s_page, b0, a.B, row, hi, step);
+                    if (b0 + TC_EB < a.B) tc_epi_fetch<EK>(a, s_pos, s_page, b0 + TC_EB, a.B, row, pre_next);
+                    tc_epi_apply<EK>(a, s_pos, s_page, s_kvrow, b0, a.B, row, hi, pre, step);
+#pragma unroll
+                    for (int i = 0; i < TC_EH; i++) pre[i] = pre_next[i];
                 } else {
 #pragma unroll
                     for (int i = 0; i < TC_EB; i++)
@@ -537,7 +691,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     named_barrier_sync(1, 128);
                     if (last_s) {
                         __threadfence();
-                        tc_fixup_rows<EK>(a, s_pos, s_page, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
+                        tc_fixup_rows<EK>(a, s_pos, s_page, s_kvrow, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
                         if (et == 0) a.counters[sg.rt] = 0;
                     }
                 }
@@ -568,7 +722,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             __threadfence();
-            tc_fixup_rows<EK>(a, s_pos, s_page, G, rt, first, lastc, (int)((long long)a.B * k / ns),
+            tc_fixup_rows<EK>(a, s_pos, s_page, s_kvrow, G, rt, first, lastc, (int)((long long)a.B * k / ns),
                               (int)((long long)a.B * (k + 1) / ns), rt * TC_BM + rloc, rloc, step);
             // the last contributor through here clears the tile's counters for the next launch
             // (every contributor has seen all arrivals by now)
