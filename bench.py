@@ -798,7 +798,8 @@ def run_timeline_prefill(args):
             raise SystemExit(f"device status {eng.device_status()}")
     # phase stamps of the prompt attention (tags 2201-2206): [t0, t1] of a phase per CTA
     ph = recs[(recs["tag"] > 2200) & (recs["tag"] < 2300)]
-    recs = recs[(recs["tag"] <= 2200) | (recs["tag"] >= 2300)]
+    epi = recs[(recs["tag"] >= 2090) & (recs["tag"] < 2100)]  # GEMM epilogue of a CTA's first segment
+    recs = recs[((recs["tag"] <= 2200) | (recs["tag"] >= 2300)) & ((recs["tag"] < 2090) | (recs["tag"] >= 2100))]
     main = {(int(r["id"]), int(r["blk"])): int(r["t1"]) for r in recs[recs["tag"] == 2200]}
     phase_names = {2201: "stage_q", 2202: "scores_to_p_ready", 2203: "p_ready_to_pv_done", 2204: "softmax_warps_total",
                    2205: "mma_waits_q", 2206: "mma_waits_k_issues_s", 2207: "scores_load_and_row_max"}
@@ -809,6 +810,11 @@ def run_timeline_prefill(args):
             rel = [int(x["t0"]) - main.get((int(x["id"]), int(x["blk"])), int(x["t0"])) for x in r]
             phases[name] = {"us_p50": round(float(np.median((r["t1"] - r["t0"]).astype(np.int64))) / 1e3, 2),
                             "starts_after_release_us_p50": round(float(np.median(rel)) / 1e3, 2)}
+    epilogue = {}
+    for ek, name in ((3, "qkv"), (2, "gate_up"), (1, "o_or_down")):
+        r = epi[epi["tag"] == 2090 + ek]
+        if len(r):
+            epilogue[name] = round(float(np.median((r["t1"] - r["t0"]).astype(np.int64))) / 1e3, 2)
     launches = sorted((recs[recs["id"] == lid] for lid in np.unique(recs["id"])), key=lambda r: int(r["t1"].min()))
     roles, prev_end, after_attn = {}, None, False
     for r in launches:
@@ -835,7 +841,7 @@ def run_timeline_prefill(args):
                "cta_us_p50": round(v["cta_us"] / v["launches"], 2)} for k, v in roles.items()}
     print(json.dumps({"timeline": f"prompt pass, 7B fp16, {PROMPT} tokens", "layers": cfg["n_layers"],
                       "traced_span_us": round(span_us, 1), "host_ms": round(host_ms, 3), "roles": out,
-                      "attention_phases": phases,
+                      "attention_phases": phases, "gemm_epilogue_us_p50": epilogue,
                       "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}))
     return 0
 

@@ -914,9 +914,14 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         RC(qkv_rope_append_status(c.wdtype, L.wqkv, nh_l_, nkv_l_, hd, d, sb.x, L.attn_norm, c.rms_eps, B, sb.pos,
                                   rope_cos_, rope_sin_, sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_,
                                   page_size_, status_, st, L.wo, H(wo_b), tcr));
+        // a prompt chunk's attention writes the output projection's split activations straight
+        // into the tensor-core workspace when that projection takes the tensor-core route
+        const bool presplit = sb.shared_pages && pf_attn_tc_ && tc_route_taken(tcr, c.wdtype, d, nh_l_ * hd, B);
         if (sb.shared_pages && pf_attn_tc_)
             RC(flash_prefill_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
-                                  nh_l_, nkv_l_, opt_.max_seq, sb.attn, status_, st, &sparse_));
+                                  nh_l_, nkv_l_, opt_.max_seq, presplit ? nullptr : sb.attn, status_, st, &sparse_,
+                                  presplit ? tcr->ws : nullptr, c.wdtype == VSL_BF16 ? 1 : 0,
+                                  (int)tc_split_rows(B)));
         else if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                     nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st,
@@ -925,7 +930,8 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
             RC(flash_decode_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                  nh_l_, nkv_l_, hd, opt_.max_seq, split_len_, sb.attn, sb.fd_ws, sb.fd_bytes, st, L.wo,
                                  att_pf, sb.shared_pages, &sparse_, fd_splits_, status_));
-        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr));
+        RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr,
+                     presplit));
         RC(allreduce_sum(sb.x, B * d));
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
                      H(wd_b), st, tcr));

@@ -46,7 +46,10 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
                            const TcRoute* tc = nullptr);
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc = nullptr);
+              const TcRoute* tc = nullptr, bool x_presplit = false);
+// Whether gemv_hint takes the tensor-core route for this projection (then x_presplit may be used).
+bool tc_route_taken(const TcRoute* tc, int wdtype, int N, int K, int B);
+size_t tc_split_rows(int B);  // padded activation rows of the split tile (hi rows, then lo rows)
 int lm_head_hint(int wdtype, const void* W, int V_local, int K, const float* x, const float* norm_w, float eps, int B,
                  float* logits, unsigned long long* slots, int vocab_offset, float temperature, uint64_t seed,
                  const int32_t* step_counter, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
@@ -68,9 +71,13 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
 // Prompt attention: up to 128 rows per query block of one sequence (one page-table row), fp16
 // KV, head_dim 128; grid = heads x query blocks (attention_prefill.cu).
 bool flash_prefill_supported(int kvdtype, int head_dim, int n_heads, int n_kv, int page_size);
+// x2 (optional): instead of out, write the rows as the split activations of the following
+// tensor-core projection: hi rows [0, P), lo rows [x2_rows, x2_rows + P), n_heads * 128 columns,
+// bf16 when x2_bf16 else fp16.
 int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages, const int32_t* page_row,
                        int max_pages, int page_size, const int32_t* pos, int P, int n_heads, int n_kv, int max_len,
-                       float* out, int* status, cudaStream_t st, const SparseMask* sparse = nullptr);
+                       float* out, int* status, cudaStream_t st, const SparseMask* sparse = nullptr,
+                       void* x2 = nullptr, int x2_bf16 = 0, int x2_rows = 0);
 constexpr int FDTC_MIN_SEQ = 2048;  // caches from this length on use the tensor-core attention
 int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start, uint64_t n, double sigma,
                cudaStream_t st);

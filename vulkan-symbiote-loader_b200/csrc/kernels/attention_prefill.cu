@@ -32,6 +32,7 @@
 #include <math_constants.h>
 
 #include <climits>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kv_map.h"
@@ -75,7 +76,35 @@ struct FpArgs {
     uint32_t idesc_pv;          // P2 (A, K-major) . V (B, MN-major)
     SparseMask sp;
     unsigned trace_id;          // launch id of the trace build (unused otherwise)
+    void* x2;                   // non-null: write the split activations of the next projection instead of out
+    int x2_bf16, x2_rows;       // their type; row of the first lo row
 };
+
+// Row `rb` of the next projection's split activations (hi row rb, lo row x2_rows + rb) at
+// columns [k0, k0 + 64): 64 values v * inv as 16-bit hi and residual lo.
+template <typename T>
+__device__ __forceinline__ void fp_store_split(const FpArgs& a, size_t rb, size_t k0, const float* o, float inv) {
+    const size_t K = (size_t)a.n_heads * FP_HD;
+    T* hi = static_cast<T*>(a.x2) + rb * K + k0;
+    T* lo = static_cast<T*>(a.x2) + ((size_t)a.x2_rows + rb) * K + k0;
+#pragma unroll
+    for (int j = 0; j < 64; j += 8) {
+        T h[8], l[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float v = o[j + e] * inv;
+            if constexpr (std::is_same<T, __half>::value) {
+                h[e] = __float2half_rn(v);
+                l[e] = __float2half_rn(v - __half2float(h[e]));
+            } else {
+                h[e] = __float2bfloat16_rn(v);
+                l[e] = __float2bfloat16_rn(v - __bfloat162float(h[e]));
+            }
+        }
+        *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<const uint4*>(h);
+        *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<const uint4*>(l);
+    }
+}
 
 __device__ __forceinline__ void fp_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -127,6 +156,18 @@ __device__ __forceinline__ void fp_ld64(uint32_t taddr, float* v) {
         : "memory");
 #pragma unroll
     for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+// 8 consecutive fp32 columns of this warp's 32 TMEM lanes
+__device__ __forceinline__ void fp_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
 }
 __device__ __forceinline__ int fp_abort(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 // byte offset of 16-bit column `col` (0..127) of row `r` in a 128 x 128 K-major swizzled tile
@@ -384,24 +425,25 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             const float alpha = mn == -CUDART_INF_F ? 1.0f : expf(m - mn);
             // probabilities, as fp16 hi / lo halves of the row of P2 (P2 of the previous chunk has
             // been read: its product completed before that chunk's fold below)
+            // (a rolled loop over 8-column groups, re-reading the scores from TMEM: the code runs
+            // once per chunk, so a compact body avoids instruction-fetch stalls)
             float ls = 0.0f;
+#pragma unroll 1
+            for (int c8 = 0; c8 < HALF / 8; c8++) {
+                float v[8];
+                fp_ld8(ts + (uint32_t)(c8 * 8), v);
+                __half ph[8], pl[8];
 #pragma unroll
-            for (int c16 = 0; c16 < HALF / 16; c16++) {
-                __half ph[16], pl[16];
-#pragma unroll
-                for (int e = 0; e < 16; e++) {
-                    const int j = c16 * 16 + e;
-                    const float p = (j >= jlo && j <= jhi) ? expf(sv[j] * a.scale - mn) : 0.0f;
+                for (int e = 0; e < 8; e++) {
+                    const int j = c8 * 8 + e;
+                    const float p = (j >= jlo && j <= jhi) ? expf(v[e] * a.scale - mn) : 0.0f;
                     ls += p;
                     ph[e] = __float2half_rn(p);
                     pl[e] = __float2half_rn(p - __half2float(ph[e]));
                 }
-#pragma unroll
-                for (int hf = 0; hf < 2; hf++) {
-                    const uint32_t off = fp_off(t, hc * HALF + c16 * 16 + hf * 8);
-                    *reinterpret_cast<uint4*>(smem_g + pt + off) = *reinterpret_cast<const uint4*>(ph + hf * 8);
-                    *reinterpret_cast<uint4*>(smem_g + pt + FP_TILE + off) = *reinterpret_cast<const uint4*>(pl + hf * 8);
-                }
+                const uint32_t off = fp_off(t, hc * HALF + c8 * 8);
+                *reinterpret_cast<uint4*>(smem_g + pt + off) = *reinterpret_cast<const uint4*>(ph);
+                *reinterpret_cast<uint4*>(smem_g + pt + FP_TILE + off) = *reinterpret_cast<const uint4*>(pl);
             }
             fp_fence_before();
             __syncwarp();
@@ -458,7 +500,13 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         } else {
             red_l[hc][t] = l;
             named_barrier_sync(1, FP_SM_THREADS);
-            if (pr >= 0) {
+            if (pr >= 0 && a.x2) {
+                const float inv = 1.0f / (red_l[0][t] + red_l[1][t]);
+                if (a.x2_bf16)
+                    fp_store_split<__nv_bfloat16>(a, (size_t)(r0 + t), (size_t)h * FP_HD + hc * HALF, o, inv);
+                else
+                    fp_store_split<__half>(a, (size_t)(r0 + t), (size_t)h * FP_HD + hc * HALF, o, inv);
+            } else if (pr >= 0) {
                 const float inv = 1.0f / (red_l[0][t] + red_l[1][t]);  // > 0: position pr is always attended
                 float* dst = a.out + ((size_t)(r0 + t) * a.n_heads + h) * FP_HD + hc * HALF;
 #pragma unroll
@@ -487,14 +535,17 @@ bool flash_prefill_supported(int kvdtype, int head_dim, int n_heads, int n_kv, i
 
 int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache, int n_pages, const int32_t* page_row,
                        int max_pages, int page_size, const int32_t* pos, int P, int n_heads, int n_kv, int max_len,
-                       float* out, int* status, cudaStream_t st, const SparseMask* sparse) {
+                       float* out, int* status, cudaStream_t st, const SparseMask* sparse, void* x2, int x2_bf16,
+                       int x2_rows) {
     if (!flash_prefill_supported(VSL_F16, FP_HD, n_heads, n_kv, page_size))
         return set_error(VSL_ERR_UNSUPPORTED, "flash_prefill: heads %d/%d page %d", n_heads, n_kv, page_size);
-    if (!q || !k_cache || !v_cache || !page_row || !pos || !out || P <= 0 || max_len <= 0 ||
+    if (!q || !k_cache || !v_cache || !page_row || !pos || (!out && !x2) || P <= 0 || max_len <= 0 ||
         max_len > max_pages * page_size || n_pages <= 0)
         return set_error(VSL_ERR_INVALID, "flash_prefill: null pointer, no rows or max_len outside the page table");
-    if (((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15) || ((uintptr_t)q & 15) || ((uintptr_t)out & 15))
+    if (((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15) || ((uintptr_t)q & 15) || ((uintptr_t)out & 15) ||
+        ((uintptr_t)x2 & 15))
         return set_error(VSL_ERR_INVALID, "flash_prefill: caches, q and out must be 16-byte aligned");
+    if (x2 && x2_rows < P) return set_error(VSL_ERR_INVALID, "flash_prefill: split tile of %d rows for %d", x2_rows, P);
     FpArgs a = {};
     a.q = q;
     a.pos = pos;
@@ -510,6 +561,9 @@ int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache,
     a.out = out;
     a.status = status;
     a.trace_id = VSL_TRACE_ID();
+    a.x2 = x2;
+    a.x2_bf16 = x2_bf16;
+    a.x2_rows = x2_rows;
     if (sparse && sparse->min_len > 0) {
         if (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0)
             return set_error(VSL_ERR_INVALID, "flash_prefill: sparse mask window %d, global %d, block %d",
@@ -552,5 +606,5 @@ extern "C" int vsl_flash_prefill(const float* q, const void* k_cache, const void
     SparseMask m = {};
     if (mask && mask->min_len > 0) m = SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
     return flash_prefill_impl(q, k_cache, v_cache, n_pages, page_row, max_pages, page_size, pos, n_rows, n_heads, n_kv,
-                              max_len, out, status, (cudaStream_t)stream, &m);
+                              max_len, out, status, (cudaStream_t)stream, &m, nullptr, 0, 0);
 }

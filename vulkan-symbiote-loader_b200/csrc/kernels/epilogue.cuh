@@ -39,6 +39,9 @@ struct GemvParams {
     const void* pf_ptr;
     size_t pf_bytes;
     unsigned trace_id;  // launch id of the trace build (unused otherwise)
+    // tensor-core route only: the split activations are already in the workspace (written by
+    // the producing kernel), so no activation-split launch precedes the GEMM
+    int x_presplit;
 };
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }

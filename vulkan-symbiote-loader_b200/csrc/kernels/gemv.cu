@@ -667,14 +667,21 @@ extern "C" int vsl_qkv_rope_append(int wdtype, const void* Wqkv, int n_heads, in
 // Engine-internal entry points: a device status word for out-of-range positions and the
 // L2 prefetch hint for the weights of the next kernel in the decode step.
 namespace vsl {
+bool tc_route_taken(const TcRoute* tc, int wdtype, int N, int K, int B) {
+    return tc && tc->ws && B >= tc->min_batch && tc_supported(wdtype, N, K, B) && tc->bytes >= tc_workspace_bytes(N, K, B);
+}
+
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc) {
+              const TcRoute* tc, bool x_presplit) {
     int rc = check_common(wdtype, W, N, K, x, B);
     if (rc) return rc;
+    if (x_presplit && (norm_w || !tc_route_taken(tc, wdtype, N, K, B)))
+        return set_error(VSL_ERR_INVALID, "gemv: pre-split activations need the tensor-core route and no norm");
     GemvParams p = {};
     p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
+    p.x_presplit = x_presplit ? 1 : 0;
     int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
     return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N, tc);
 }

@@ -17,7 +17,8 @@
 //              MMAs of one segment overlap the epilogue of the previous one) and one lane
 //              issues tcgen05.mma (M=128, N=2Bp, K=16; 8 per k-block), committing each stage
 //              back to the producer and each finished segment to the epilogue;
-//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (= rows), hi + lo, then either the
+//   warps 2-9  epilogue, two warps per TMEM lane quarter on alternate 16-column chunks of the
+//              batch: tcgen05.ld of their 32 TMEM lanes (= rows), hi + lo, then either the
 //              projection epilogue directly (a segment that covers all of K) or a partial to
 //              the workspace plus an arrival on the row tile's counter.
 // Split row tiles: at 32 or more activation rows, when each row tile is shared by two or
@@ -48,7 +49,9 @@ VSL_TRACE_UNIT(tc)
 
 namespace vsl {
 
-constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARPS = 8;  // two per TMEM lane quarter, each on alternate 16-row chunks of the batch
+constexpr int TC_EPI_THREADS = 32 * TC_EPI_WARPS;
+constexpr int TC_THREADS = 64 + TC_EPI_THREADS;
 constexpr int TC_BM = 128;            // rows of W per tile (MMA M)
 constexpr int TC_ATOM = 64;           // k per 128-byte swizzle atom of 16-bit values
 constexpr int TC_A_ATOM = TC_BM * TC_ATOM * 2;   // 16 KB of weights per atom
@@ -176,18 +179,17 @@ __device__ __forceinline__ bool next_segment(const TcArgs& a, long long& f, long
 // ---------------------------------------------------------------------------------------
 constexpr int XS_VEC = 12;
 
+// norm weights of 4-value group j (any alignment)
+__device__ __forceinline__ float4 xs_w4(const float* nw, bool nw4, int j) {
+    if (nw4) return __ldg(reinterpret_cast<const float4*>(nw) + j);
+    return make_float4(__ldg(nw + 4 * j), __ldg(nw + 4 * j + 1), __ldg(nw + 4 * j + 2), __ldg(nw + 4 * j + 3));
+}
+
 template <typename WT>
-__device__ __forceinline__ void xs_emit(WT* hi, WT* lo, int j, float4 t, const float* nw, bool nw4, float den) {
+__device__ __forceinline__ void xs_emit(WT* hi, WT* lo, int j, float4 t, bool norm, float4 w4, float den) {
     float e[4] = {t.x, t.y, t.z, t.w};
-    if (nw) {
-        float w[4];
-        if (nw4) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(nw) + j);
-            w[0] = w4.x, w[1] = w4.y, w[2] = w4.z, w[3] = w4.w;
-        } else {
-#pragma unroll
-            for (int q = 0; q < 4; q++) w[q] = __ldg(nw + 4 * j + q);
-        }
+    if (norm) {
+        const float w[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
         for (int q = 0; q < 4; q++) e[q] = e[q] / den * w[q];  // rms_norm.comp:32-34: x / sqrt(var) * w
     }
@@ -212,13 +214,22 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
     __shared__ float red[8];
     const int b = blockIdx.x;
     VSL_TRACE_ENTRY();
+    const int n4 = K / 4;
+    const bool in_regs = n4 <= XS_VEC * 256;
+    const bool nw4 = ((uintptr_t)nw & 15) == 0;
+    // the norm weights are not written by the previous kernel: requested before its end
+    float4 w[XS_VEC];
+    if (in_regs && nw) {
+#pragma unroll
+        for (int i = 0; i < XS_VEC; i++) {
+            const int j = threadIdx.x + i * 256;
+            if (j < n4) w[i] = xs_w4(nw, nw4, j);
+        }
+    }
     pdl_wait();
     VSL_TRACE_RELEASED();
     pdl_launch_dependents();
     const float4* xr = reinterpret_cast<const float4*>(x + (size_t)b * K);
-    const int n4 = K / 4;
-    const bool in_regs = n4 <= XS_VEC * 256;
-    const bool nw4 = ((uintptr_t)nw & 15) == 0;
     float4 v[XS_VEC];
     float ss = 0.0f;
     if (in_regs) {
@@ -249,14 +260,16 @@ __global__ void __launch_bounds__(256) vsl_xsplit_kernel(const float* __restrict
     }
     WT* hi = x2 + (size_t)b * K;
     WT* lo = x2 + (size_t)(Bp + b) * K;
+    const float4 one = make_float4(1.0f, 1.0f, 1.0f, 1.0f);
     if (in_regs) {
 #pragma unroll
         for (int i = 0; i < XS_VEC; i++) {
             const int j = threadIdx.x + i * 256;
-            if (j < n4) xs_emit(hi, lo, j, v[i], nw, nw4, den);
+            if (j < n4) xs_emit(hi, lo, j, v[i], nw != nullptr, nw ? w[i] : one, den);
         }
     } else {
-        for (int j = threadIdx.x; j < n4; j += 256) xs_emit(hi, lo, j, __ldcg(xr + j), nw, nw4, den);
+        for (int j = threadIdx.x; j < n4; j += 256)
+            xs_emit(hi, lo, j, __ldcg(xr + j), nw != nullptr, nw ? xs_w4(nw, nw4, j) : one, den);
     }
     VSL_TRACE_EXIT(trace_id, 2100u);
 }
@@ -422,16 +435,16 @@ __device__ __forceinline__ void tc_epilogue_chunk(const TcArgs& a, const int* s_
 template <int EK>
 __device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos, const int* s_page, const int* s_kvrow,
                                               int G, int rt, int first, int lastc, int bs0, int bs1, int row, int rloc,
-                                              int step) {
-    for (int b0 = bs0; b0 < bs1; b0 += TC_EB) {
-        // TC_EB rows x 4 CTAs of loads are in flight at a time
+                                              int step, int hb) {
+    for (int b0 = bs0 + hb * TC_EB; b0 < bs1; b0 += 2 * TC_EB) {
+        // TC_EB rows x 2 CTAs of loads are in flight per thread (two warps share each row)
         float v[TC_EB];
 #pragma unroll
         for (int j = 0; j < TC_EB; j++) v[j] = 0.0f;
-        for (int c0 = first; c0 <= lastc; c0 += 4) {
-            float t[4][TC_EB];
+        for (int c0 = first; c0 <= lastc; c0 += 2) {
+            float t[2][TC_EB];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < 2; u++) {
                 const int cc = c0 + u;
                 if (cc <= lastc) {
                     const int slot = sk_lo(a.T, G, cc) >= (long long)rt * a.nkb ? 0 : 1;
@@ -441,7 +454,7 @@ __device__ __forceinline__ void tc_fixup_rows(const TcArgs& a, const int* s_pos,
                 }
             }
 #pragma unroll
-            for (int u = 0; u < 4; u++)
+            for (int u = 0; u < 2; u++)
                 if (c0 + u <= lastc)
 #pragma unroll
                     for (int j = 0; j < TC_EB; j++) v[j] += t[u][j];
@@ -479,7 +492,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&tmem_full[i], 1);
-            mbar_init(&tmem_empty[i], 4);
+            mbar_init(&tmem_empty[i], TC_EPI_WARPS);
         }
         mbar_fence_init();
         abort_s = 0;
@@ -616,20 +629,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ================= epilogue warps =================
         pdl_wait();
         pdl_launch_dependents();
-        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const int q = warp & 3;          // TMEM lane quarter this warp may access
+        const int hb = (warp - 2) >> 2;  // chunks b0 = 16 (2 j + hb) of the batch
         const int rloc = q * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..127
+        const int et = threadIdx.x - 64;  // 0..TC_EPI_THREADS - 1
         int step = 0;
         if (EK == EK_LMHEAD && a.ep.inv_temp > 0.0f) step = *a.ep.step_counter;
         if (EK == EK_QKV) {  // positions and KV pages of the sequences, once per CTA
-            for (int b = et; b < a.B; b += 128) {
+            for (int b = et; b < a.B; b += TC_EPI_THREADS) {
                 int pos, page;
                 epi_pos_page(a.ep, b, pos, page);
                 s_pos[b] = pos * (a.ep.head_dim >> 1);
                 s_page[b] = page;
                 s_kvrow[b] = page < 0 ? 0 : page * a.ep.n_kv * a.ep.page_size + pos % a.ep.page_size;
             }
-            named_barrier_sync(1, 128);
+            named_barrier_sync(1, TC_EPI_THREADS);
         }
         long long f = f0;
         int si = 0;
@@ -639,9 +653,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         while (next_segment(a, f, f1, f0, sg)) {
             const int buf = si & 1;
             {
-                // the four epilogue warps leave together (they meet at named barriers below)
+                // the epilogue warps leave together (they meet at named barriers below)
                 const bool bad = !mbar_wait(&tmem_full[buf], (uint32_t)((si >> 1) & 1)) || ld_abort(&abort_s);
-                if (named_barrier_or(1, 128, bad)) {
+                if (named_barrier_or(1, TC_EPI_THREADS, bad)) {
                     set_status(a.status, VSL_ERR_TIMEOUT);
                     atomicExch(&abort_s, 1);
                     aborted = true;
@@ -649,23 +663,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
             }
             tc_fence_after();
+#ifdef VSL_TRACE
+            const uint64_t te0 = vsl::trace_now();
+#endif
             const int row = sg.rt * TC_BM + rloc;
             float* wsp = a.ws + ((size_t)c * 2 + sg.slot) * a.Bp * TC_BM;
             const uint32_t tl = tmem + (uint32_t)(buf * a.tmem_cols) + ((uint32_t)(q * 32) << 16);
-            // a full segment's epilogue requests the next chunk's global inputs before it
-            // applies this chunk, so their latency overlaps the work
-            TcPre pre[TC_EH], pre_next[TC_EH];
-            if (sg.full) tc_epi_fetch<EK>(a, s_pos, s_page, 0, a.B, row, pre);
-            for (int b0 = 0; b0 < a.B; b0 += TC_EB) {
+            for (int b0 = hb * TC_EB; b0 < a.B; b0 += 2 * TC_EB) {
                 float hi[TC_EB], lo[TC_EB];
                 tmem_ld16x2(tl + (uint32_t)b0, tl + (uint32_t)(a.Bp + b0), hi, lo);
 #pragma unroll
                 for (int i = 0; i < TC_EB; i++) hi[i] += lo[i];
                 if (sg.full) {
-                    if (b0 + TC_EB < a.B) tc_epi_fetch<EK>(a, s_pos, s_page, b0 + TC_EB, a.B, row, pre_next);
-                    tc_epi_apply<EK>(a, s_pos, s_page, s_kvrow, b0, a.B, row, hi, pre, step);
-#pragma unroll
-                    for (int i = 0; i < TC_EH; i++) pre[i] = pre_next[i];
+                    tc_epilogue_chunk<EK>(a, s_pos, s_page, s_kvrow, b0, a.B, row, hi, step);
                 } else {
 #pragma unroll
                     for (int i = 0; i < TC_EB; i++)
@@ -676,11 +686,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tmem_empty[buf]);
+#ifdef VSL_TRACE
+            if (et == 0 && si == 0) vsl_trace_record(a.ep.trace_id, 2090u + EK, te0, vsl::trace_now());
+#endif
             si++;
             if (!sg.full) {
                 // partial written: arrive on the row tile (release after the CTA's stores)
                 __threadfence();
-                named_barrier_sync(1, 128);
+                named_barrier_sync(1, TC_EPI_THREADS);
                 if (a.dist_fixup) {
                     if (et == 0) atomicAdd(a.counters + sg.rt, 1);
                     split_rt[n_split++] = sg.rt;
@@ -688,10 +701,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     const int first = sk_owner(a.T, G, (long long)sg.rt * a.nkb);
                     const int lastc = sk_owner(a.T, G, (long long)sg.rt * a.nkb + a.nkb - 1);
                     if (et == 0) last_s = atomicAdd(a.counters + sg.rt, 1) == lastc - first ? 1 : 0;
-                    named_barrier_sync(1, 128);
+                    named_barrier_sync(1, TC_EPI_THREADS);
                     if (last_s) {
                         __threadfence();
-                        tc_fixup_rows<EK>(a, s_pos, s_page, s_kvrow, G, sg.rt, first, lastc, 0, a.B, row, rloc, step);
+                        tc_fixup_rows<EK>(a, s_pos, s_page, s_kvrow, G, sg.rt, first, lastc, 0, a.B, row, rloc, step, hb);
                         if (et == 0) a.counters[sg.rt] = 0;
                     }
                 }
@@ -716,14 +729,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 }
                 bad = !ok;
             }
-            if (named_barrier_or(1, 128, bad)) {
+            if (named_barrier_or(1, TC_EPI_THREADS, bad)) {
                 set_status(a.status, VSL_ERR_TIMEOUT);
                 atomicExch(&abort_s, 1);
                 break;
             }
             __threadfence();
             tc_fixup_rows<EK>(a, s_pos, s_page, s_kvrow, G, rt, first, lastc, (int)((long long)a.B * k / ns),
-                              (int)((long long)a.B * (k + 1) / ns), rt * TC_BM + rloc, rloc, step);
+                              (int)((long long)a.B * (k + 1) / ns), rt * TC_BM + rloc, rloc, step, hb);
             // the last contributor through here clears the tile's counters for the next launch
             // (every contributor has seen all arrivals by now)
             if (et == 0) {
@@ -781,6 +794,7 @@ static int make_map(CUtensorMap* m, const void* base, int wdtype, int rows, int 
 }
 
 static int pad_batch(int B) { return (B + 7) / 8 * 8; }
+size_t tc_split_rows(int B) { return (size_t)pad_batch(B); }
 
 size_t tc_workspace_bytes(int N, int K, int B) {
     const int Bp = pad_batch(B);
@@ -879,9 +893,11 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
     rc = make_map(&mx, x2, wdtype, n, p.K, n);
     if (rc) return rc;
 
-    // activation split (+ RMSNorm)
-    cudaError_t e;
-    if (wdtype == VSL_BF16)
+    // activation split (+ RMSNorm), unless the producing kernel wrote the split tile already
+    cudaError_t e = cudaSuccess;
+    if (p.x_presplit)
+        ;
+    else if (wdtype == VSL_BF16)
         e = launch_k(vsl_xsplit_kernel<__nv_bfloat16>, dim3(p.B), dim3(256), 0, st, p.x, p.K, p.norm_w, p.eps, a.Bp,
                      static_cast<__nv_bfloat16*>(x2), (unsigned)VSL_TRACE_ID());
     else
