@@ -82,7 +82,7 @@ def parse():
     ap.add_argument("--sweep-batches", default="1,4,16,64", help="activation rows for --sweep")
     ap.add_argument("--split-len", type=int, default=0,
                     help="split-K attention positions per CTA (engine option split_len; 0 = automatic)")
-    ap.add_argument("--attn-route", type=int, default=0, choices=[0, 1, 2],
+    ap.add_argument("--attn-route", type=int, default=0, choices=[0, 1, 2, 3],
                     help="decode attention kernel (engine option attn_route): 0 automatic, 1 split-K, 2 tcgen05")
     ap.add_argument("--attn-prefetch", type=int, default=0, choices=[0, 1],
                     help="split-K attention requests the output projection into L2 (engine option attn_prefetch)")

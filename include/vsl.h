@@ -92,7 +92,7 @@ VSL_API int vsl_rmsnorm(const float* x, const float* w, int B, int d, float eps,
 VSL_API int vsl_gemv(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
              const float* norm_w, float eps, void* stream);
 
-/* Batched projection on the tcgen05 tensor cores for 1 <= B <= 64 activation rows (the
+/* Batched projection on the tcgen05 tensor cores for 1 <= B <= 128 activation rows (the
  * skinny-GEMM form of vsl_gemv for batched decode: every weight tile is read from HBM once
  * for all B rows; same projection sites as vsl_gemv). W is fp16 or bf16 with N >= 128,
  * K >= 64 and K % 8 == 0; x, y, norm_w, eps and epilogue mean what they mean for vsl_gemv.
@@ -178,6 +178,16 @@ VSL_API int vsl_flash_decode_tc_sparse(const float* q, const void* k_cache, cons
                                        int B, int n_heads, int n_kv, int head_dim, int max_len, float* out,
                                        void* workspace, size_t workspace_bytes, const vsl_sparse_mask* mask,
                                        void* stream);
+
+/* Decode attention for short caches (same semantics and cache layout as vsl_flash_decode_sparse;
+ * fp16 or fp32 KV, head_dim 64 or 128, up to 8 query heads per KV group, page_size a multiple of
+ * 64): one CTA per (sequence, KV group) processes 256 positions (128 with fp32 KV) at a time and
+ * needs no workspace. status (nullable device int) receives VSL_ERR_TIMEOUT if a bounded wait
+ * expires. Meant for caches of up to about a thousand positions. */
+VSL_API int vsl_flash_decode_short(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                   const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                                   int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                                   const vsl_sparse_mask* mask, int* status, void* stream);
 
 /* Prompt attention (the reference runs attention.comp once per prompt token during its prompt
  * pass, VulkanSymbioteEngine.cpp:678-765): n_rows query rows of ONE sequence, row r at position
@@ -299,8 +309,10 @@ typedef struct {
     int sparse_global;   /* global tokens G (0 = 16)                                         */
     int sparse_block;    /* block BLK (0 = 1024)                                             */
     int attn_route;      /* decode attention: 0 (default) = tcgen05-score attention when max_seq >= 2048,
-                          split-K kernel below; 1 = split-K kernel always; 2 = tcgen05 attention
-                          always (fp16 KV, head_dim 128)                                    */
+                          the short-cache kernel (one CTA per sequence and KV group, 256-position
+                          rounds) when max_seq <= 1024, the split-K kernel between; 1 = split-K
+                          always; 2 = tcgen05 attention always (fp16 KV, head_dim 128); 3 = the
+                          short-cache kernel always                                          */
     int attn_prefetch;   /* 1 = the split-K attention kernel requests the output projection's weights
                           into L2 while it runs; 0 (default) = it does not (measured faster)  */
     int p2p_chunk_bytes; /* tensor parallel with use_p2p: bytes of the residual all-reduce's message

@@ -210,7 +210,7 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     }
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);
-    if (opt.attn_route < 0 || opt.attn_route > 2) return set_error(VSL_ERR_INVALID, "engine: attn_route %d", opt.attn_route);
+    if (opt.attn_route < 0 || opt.attn_route > 3) return set_error(VSL_ERR_INVALID, "engine: attn_route %d", opt.attn_route);
     if (opt.sparse_min_len < 0 || opt.sparse_window < 0 || opt.sparse_global < 0 || opt.sparse_block < 0)
         return set_error(VSL_ERR_INVALID, "engine: negative sparse attention parameter");
     if (opt.sparse_min_len > 0)  // zeros take the reference's values (Common.h:71-74)
@@ -360,6 +360,8 @@ int DecodeEngine::alloc_buffers() {
     CK(cudaMalloc(&fd_ws_, fd_ws_bytes_));
     CK(cudaMemset(fd_ws_, 0, fd_ws_bytes_));
 
+    // short caches: one CTA per (sequence, KV group), no split combine
+    short_attn_ = opt_.attn_route == 3 || (opt_.attn_route == 0 && opt_.max_seq <= FS_MAX_LEN);
     // long caches: attention with tcgen05 scores and an even split of the KV over the SMs
     const bool want_tc = opt_.attn_route == 2 || (opt_.attn_route == 0 && opt_.max_seq >= FDTC_MIN_SEQ);
     if (want_tc &&
@@ -922,6 +924,10 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
                                   nh_l_, nkv_l_, opt_.max_seq, presplit ? nullptr : sb.attn, status_, st, &sparse_,
                                   presplit ? tcr->ws : nullptr, c.wdtype == VSL_BF16 ? 1 : 0,
                                   (int)tc_split_rows(B)));
+        else if (short_attn_ && !sb.shared_pages)
+            RC(flash_decode_short_impl(sb.q, L.k_cache, L.v_cache, kvdtype_, sb.pages, max_pages_, page_size_, sb.pos,
+                                       B, nh_l_, nkv_l_, hd, opt_.max_seq, sb.attn, st, L.wo, att_pf, &sparse_,
+                                       status_));
         else if (sb.fdtc_ws)
             RC(flash_decode_tc_impl(sb.q, L.k_cache, L.v_cache, n_pages_, sb.pages, max_pages_, page_size_, sb.pos, B,
                                     nh_l_, nkv_l_, opt_.max_seq, sb.attn, sb.fdtc_ws, sb.fdtc_bytes, status_, st,

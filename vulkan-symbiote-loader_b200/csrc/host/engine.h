@@ -128,6 +128,7 @@ private:
     void* pf_fd_ws_ = nullptr;
     size_t pf_fd_bytes_ = 0;
     bool pf_attn_tc_ = false;  // prompt chunks take the tensor-core prompt attention
+    bool short_attn_ = false;  // decode steps take the short-cache attention kernel
     void* pf_tc_ws_ = nullptr;
     TcRoute pf_tc_route_ = {};
     std::vector<int32_t> pt_host_;  // host copy of the page table

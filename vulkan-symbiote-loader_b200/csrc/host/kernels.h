@@ -60,6 +60,12 @@ int flash_decode_impl(const float* q, const void* k_cache, const void* v_cache, 
                       size_t workspace_bytes, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
                       bool shared_pages = false, const SparseMask* sparse = nullptr, int n_splits_max = 0,
                       int* status = nullptr);
+// Short caches: one CTA per (sequence, KV group), 256-position rounds, no workspace (attention.cu).
+constexpr int FS_MAX_LEN = 1024;  // the engine's automatic route takes it up to this max_seq
+int flash_decode_short_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                            const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                            int n_heads, int n_kv, int head_dim, int max_len, float* out, cudaStream_t stream,
+                            const void* pf_ptr, size_t pf_bytes, const SparseMask* sparse, int* status);
 // workspace of flash_decode_impl with n_splits splits per (sequence, group)
 size_t flash_decode_workspace_bytes(int B, int n_heads, int n_kv, int head_dim, int n_splits);
 size_t flash_decode_tc_workspace_bytes(int B, int n_kv);

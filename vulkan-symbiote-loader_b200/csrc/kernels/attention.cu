@@ -454,6 +454,325 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
     VSL_TRACE_EXIT(p.trace_id, 903);
 }
 
+// ---------------------------------------------------------------------------------------
+// Short caches: one CTA per (sequence, KV group), no split combine.
+//
+// At a few hundred positions the split-K kernel's cost is its dependent chain (a chunk per CTA,
+// then partials through global memory and a last-CTA combine), not bytes. This form stages a
+// whole round of positions (256 with fp16 KV, 128 with fp32: four or two 64-position chunks,
+// each on its own mbarrier) and processes it at once with 512 threads: every position's score
+// in parallel (PARTS threads per position, joined by shuffles), one block-wide maximum and sum,
+// then P.V over NG position groups per head dimension, reduced once at the end. Longer caches
+// take further rounds with the online softmax; the engine uses this kernel only while the cache
+// is at most FS_MAX_LEN positions. Older rows are requested before griddepcontrol.wait, the row
+// at pos (written by the predecessor) after it.
+// ---------------------------------------------------------------------------------------
+constexpr int FS_THREADS = 512;
+constexpr int FS_WARPS = FS_THREADS / 32;
+template <typename KT>
+__host__ __device__ constexpr int fs_chunks() {
+    return sizeof(KT) == 2 ? 4 : 2;  // 64-position chunks per round
+}
+template <int HD, typename KT>
+__host__ __device__ constexpr size_t fs_smem_bytes() {
+    constexpr int R = fs_chunks<KT>() * FD_CHUNK;
+    return (size_t)2 * R * HD * sizeof(KT)                         // K and V of a round
+           + (size_t)FD_GMAX * (HD / KvVec<KT>::VEC) * (KvVec<KT>::VEC + 1) * sizeof(float)  // q, padded columns
+           + (size_t)FD_GMAX * R * sizeof(float)                    // scores / probabilities
+           + (size_t)(FS_THREADS / HD) * FD_GMAX * HD * sizeof(float)  // P.V group partials
+           + (size_t)2 * FS_WARPS * FD_GMAX * sizeof(float)          // warp maxima / sums
+           + (size_t)4 * FD_GMAX * sizeof(float);                    // m, l, alpha
+}
+
+template <int HD, typename KT>
+__global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(FdParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    constexpr int NCH = fs_chunks<KT>();
+    constexpr int R = NCH * FD_CHUNK;             // positions per round
+    constexpr int PARTS = FS_THREADS / R;         // threads per position score
+    constexpr int VEC = KvVec<KT>::VEC;
+    constexpr int VPR = HD / VEC;                 // 16-byte vectors per row
+    constexpr int NG = FS_THREADS / HD;           // position groups of P.V
+    constexpr int QCOL = VEC + 1, QP = VPR * QCOL;
+    static_assert(VPR % PARTS == 0 && R % NG == 0, "short attention tiling");
+    KT* k_s = reinterpret_cast<KT*>(smem_raw);    // [R][HD]
+    KT* v_s = k_s + (size_t)R * HD;               // [R][HD]
+    float* q_s = reinterpret_cast<float*>(v_s + (size_t)R * HD);  // [GMAX][VPR][VEC + 1]
+    float* s_s = q_s + FD_GMAX * QP;              // [GMAX][R]
+    float* ored = s_s + FD_GMAX * R;              // [NG][GMAX][HD]
+    float* red = ored + NG * FD_GMAX * HD;        // [2][WARPS][GMAX]
+    float* m_s = red + 2 * FS_WARPS * FD_GMAX;    // [GMAX]
+    float* l_s = m_s + FD_GMAX;
+    float* a_s = l_s + FD_GMAX;
+    __shared__ __align__(8) uint64_t bar[4];      // one per chunk of the round
+    VSL_TRACE_ENTRY();
+
+    const int g = blockIdx.x, b = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int G = p.n_heads / p.n_kv;
+    const int pos = p.pos[b];
+    const int len = min(pos + 1, min(p.max_pages * p.page_size, p.max_len));
+    const int lo = min(sparse_first(p.sp, pos), len - 1);
+    const int t_begin = lo & ~(FD_CHUNK - 1);
+    const int n_rounds = (len - t_begin + R - 1) / R;
+    const int new_row = pos - t_begin;  // position of the freshly appended row, relative to t_begin
+    constexpr uint32_t ROW_BYTES = HD * sizeof(KT);
+
+    auto chunk_ptrs = [&](int t0, const KT*& kg, const KT*& vg) {
+        const int page = p.page_table[(size_t)b * p.max_pages + t0 / p.page_size];
+        const size_t base = (((size_t)page * p.n_kv + g) * p.page_size + (t0 % p.page_size)) * HD;
+        kg = reinterpret_cast<const KT*>(p.k_cache) + base;
+        vg = reinterpret_cast<const KT*>(p.v_cache) + base;
+    };
+    // round r: chunk c (rows rb .. rb + n) into slot c; `skip` (relative to t_begin) is left out
+    auto issue_round = [&](int r, int skip) {
+        if (tid != 0) return;
+        for (int c = 0; c < NCH; c++) {
+            const int t0 = t_begin + r * R + c * FD_CHUNK;
+            if (t0 >= len) break;
+            const int n = min(FD_CHUNK, len - t0);
+            const KT* kg;
+            const KT* vg;
+            chunk_ptrs(t0, kg, vg);
+            KT* ks = k_s + (size_t)c * FD_CHUNK * HD;
+            KT* vs = v_s + (size_t)c * FD_CHUNK * HD;
+            const int rr = skip - (t0 - t_begin);
+            const bool cut = rr >= 0 && rr < n;
+            mbar_arrive_expect_tx(&bar[c], (uint32_t)(n - (cut ? 1 : 0)) * 2 * ROW_BYTES);
+            const int r0 = cut ? rr : n, r1 = cut ? rr + 1 : n;
+            if (r0 > 0) {
+                bulk_g2s(ks, kg, (uint32_t)r0 * ROW_BYTES, &bar[c]);
+                bulk_g2s(vs, vg, (uint32_t)r0 * ROW_BYTES, &bar[c]);
+            }
+            if (n > r1) {
+                bulk_g2s(ks + (size_t)r1 * HD, kg + (size_t)r1 * HD, (uint32_t)(n - r1) * ROW_BYTES, &bar[c]);
+                bulk_g2s(vs + (size_t)r1 * HD, vg + (size_t)r1 * HD, (uint32_t)(n - r1) * ROW_BYTES, &bar[c]);
+            }
+        }
+    };
+    if (tid < NCH) mbar_init(&bar[tid], 1);
+    if (tid == 0) mbar_fence_init();
+    __syncthreads();
+    // round 0's older rows do not depend on the predecessor
+    issue_round(0, new_row);
+    pdl_wait();
+    VSL_TRACE_RELEASED();
+    // q and the new row, written by the QKV projection (a position past the cache is never read:
+    // the QKV kernel has flagged it in the status word)
+    if (pos < len && new_row < R) {
+        const int c = new_row / FD_CHUNK, rr = new_row % FD_CHUNK;
+        const KT* kg;
+        const KT* vg;
+        chunk_ptrs(t_begin + c * FD_CHUNK, kg, vg);
+        for (int i = tid; i < VPR; i += FS_THREADS) {
+            *reinterpret_cast<uint4*>(k_s + ((size_t)c * FD_CHUNK + rr) * HD + i * VEC) =
+                __ldcg(reinterpret_cast<const uint4*>(kg + (size_t)rr * HD + i * VEC));
+            *reinterpret_cast<uint4*>(v_s + ((size_t)c * FD_CHUNK + rr) * HD + i * VEC) =
+                __ldcg(reinterpret_cast<const uint4*>(vg + (size_t)rr * HD + i * VEC));
+        }
+    }
+    const int h0 = g * G;
+    for (int i = tid; i < G * HD; i += FS_THREADS) {
+        const int j = i / HD, d = i - j * HD;
+        q_s[j * QP + (d / VEC) * QCOL + d % VEC] = __ldcg(p.q + ((size_t)b * p.n_heads + h0) * HD + i);
+    }
+    if (tid < FD_GMAX) {
+        m_s[tid] = -CUDART_INF_F;
+        l_s[tid] = 0.0f;
+    }
+    const int d_own = tid % HD, grp = tid / HD;  // P.V: head dimension and position group
+    float o_acc[FD_GMAX];
+#pragma unroll
+    for (int j = 0; j < FD_GMAX; j++) o_acc[j] = 0.0f;
+    bool staged_ok = true;
+    int issued_rounds = 1;
+    for (int r = 0; r < n_rounds; r++) {
+        const int rb = t_begin + r * R;
+        const int n = min(R, len - rb);
+        const int nch = (n + FD_CHUNK - 1) / FD_CHUNK;
+        bool late = false;
+        for (int c = 0; c < nch; c++) late |= !mbar_wait(&bar[c], (uint32_t)(r & 1));
+        if (__syncthreads_or(late)) {
+            staged_ok = false;
+            break;
+        }
+        // scores: PARTS adjacent threads per position, each over VPR / PARTS 16-byte columns in an
+        // order rotated by the position (conflict-free reads of the unpadded rows)
+        {
+            const int tt = tid / PARTS, part = tid % PARTS;
+            float acc[FD_GMAX];
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+            if (tt < n) {
+                const KT* kr = k_s + (size_t)tt * HD;
+#pragma unroll
+                for (int k = 0; k < VPR / PARTS; k++) {
+                    const int cv = (part + PARTS * k + tt) % VPR;
+                    float kf[VEC];
+                    KvVec<KT>::widen(*reinterpret_cast<const uint4*>(kr + cv * VEC), kf);
+#pragma unroll
+                    for (int j = 0; j < FD_GMAX; j++) {
+                        if (j < G) {
+#pragma unroll
+                            for (int e = 0; e < VEC; e++) acc[j] = fmaf(q_s[j * QP + cv * QCOL + e], kf[e], acc[j]);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++) {
+                if (j >= G) break;
+#pragma unroll
+                for (int o = 1; o < PARTS; o <<= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+            }
+            if (part == 0) {
+                const bool valid = tt < n && rb + tt >= lo;
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++)
+                    if (j < G) s_s[j * R + tt] = valid ? acc[j] * p.scale : -CUDART_INF_F;
+            }
+        }
+        __syncthreads();
+        // maximum per head over the round
+        for (int j = 0; j < G; j++) {
+            const float v = tid < R ? s_s[j * R + tid] : -CUDART_INF_F;
+            const float mx = warp_max(v);
+            if (lane == 0) red[warp * FD_GMAX + j] = mx;
+        }
+        __syncthreads();
+        for (int j = 0; j < G; j++) {
+            float cm = -CUDART_INF_F;
+#pragma unroll
+            for (int w = 0; w < R / 32; w++) cm = fmaxf(cm, red[w * FD_GMAX + j]);
+            const float mo = m_s[j];
+            const float mn = fmaxf(mo, cm);
+            // probabilities in place, their sum per warp
+            float e = 0.0f;
+            if (tid < R) {
+                const float sv = s_s[j * R + tid];
+                e = sv != -CUDART_INF_F ? expf(sv - mn) : 0.0f;
+                s_s[j * R + tid] = e;
+            }
+            const float sm = warp_sum(e);
+            if (lane == 0) red[(FS_WARPS + warp) * FD_GMAX + j] = sm;
+            if (tid == 0) a_s[j] = mo == -CUDART_INF_F ? 0.0f : expf(mo - mn);
+        }
+        __syncthreads();
+        if (tid < G) {
+            float sm = 0.0f;
+#pragma unroll
+            for (int w = 0; w < R / 32; w++) sm += red[(FS_WARPS + w) * FD_GMAX + tid];
+            const float mo = m_s[tid];
+            float cm = -CUDART_INF_F;
+#pragma unroll
+            for (int w = 0; w < R / 32; w++) cm = fmaxf(cm, red[w * FD_GMAX + tid]);
+            m_s[tid] = fmaxf(mo, cm);
+            l_s[tid] = l_s[tid] * a_s[tid] + sm;
+        }
+        // P.V: thread (d_own, grp) sums positions grp, grp + NG, ... of the round
+        {
+            float acc[FD_GMAX];
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+#pragma unroll 4
+            for (int i = grp; i < n; i += NG) {
+                const float vv = (float)v_s[(size_t)i * HD + d_own];
+#pragma unroll
+                for (int j = 0; j < FD_GMAX; j++)
+                    if (j < G) acc[j] = fmaf(s_s[j * R + i], vv, acc[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < FD_GMAX; j++)
+                if (j < G) o_acc[j] = o_acc[j] * a_s[j] + acc[j];
+        }
+        __syncthreads();  // the round's buffers, scores and statistics are consumed
+        if (r + 1 < n_rounds) {
+            issue_round(r + 1, -1);  // rows after the wait: the new row is already in the cache
+            issued_rounds++;
+        }
+    }
+    if (p.pf_ptr && tid < 32) prefetch_share(p.pf_ptr, p.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x,
+                                             gridDim.x * gridDim.y, tid, 32);
+    pdl_launch_dependents();
+    if (!staged_ok) {
+        set_status(p.status, VSL_ERR_TIMEOUT);
+        // let the copies still in flight land (bounded) before the CTA leaves
+        if (tid == 0) {
+            const int r = issued_rounds - 1;
+            for (int c = 0; c < NCH; c++)
+                if (t_begin + r * R + c * FD_CHUNK < len) mbar_wait(&bar[c], (uint32_t)(r & 1));
+        }
+        __syncthreads();
+        VSL_TRACE_EXIT(p.trace_id, 906);
+        return;
+    }
+    // the position groups, in a fixed order
+#pragma unroll
+    for (int j = 0; j < FD_GMAX; j++)
+        if (j < G) ored[(grp * FD_GMAX + j) * HD + d_own] = o_acc[j];
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += FS_THREADS) {
+        const int j = i / HD, d = i - j * HD;
+        float o = ored[j * HD + d];
+#pragma unroll
+        for (int q = 1; q < NG; q++) o += ored[(q * FD_GMAX + j) * HD + d];
+        p.out[((size_t)b * p.n_heads + h0 + j) * HD + d] = o / l_s[j];
+    }
+    VSL_TRACE_EXIT(p.trace_id, 905);
+}
+
+template <int HD, typename KT>
+static int launch_fs(const FdParams& p, cudaStream_t st) {
+    auto kern = vsl_flash_decode_short_kernel<HD, KT>;
+    constexpr size_t smem = fs_smem_bytes<HD, KT>();
+    static thread_local int configured_dev = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_dev != dev) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return launch_status(e, "flash_decode_short smem attribute");
+        configured_dev = dev;
+    }
+    FdParams pt = p;
+    pt.trace_id = VSL_TRACE_ID();
+    return launch_status(launch_k(kern, dim3(p.n_kv, p.B), dim3(FS_THREADS), smem, st, pt), "flash_decode_short launch");
+}
+
+int flash_decode_short_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                            const int32_t* page_table, int max_pages, int page_size, const int32_t* pos, int B,
+                            int n_heads, int n_kv, int head_dim, int max_len, float* out, cudaStream_t stream,
+                            const void* pf_ptr, size_t pf_bytes, const SparseMask* sparse, int* status) {
+    if (!q || !k_cache || !v_cache || !page_table || !pos || !out)
+        return set_error(VSL_ERR_INVALID, "flash_decode_short: null pointer");
+    if (sparse && sparse->min_len > 0 && (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0))
+        return set_error(VSL_ERR_INVALID, "flash_decode_short: sparse mask window %d, global %d, block %d",
+                         sparse->window, sparse->global_tokens, sparse->block);
+    if (B <= 0 || n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > FD_GMAX)
+        return set_error(VSL_ERR_UNSUPPORTED, "flash_decode_short: heads %d / kv %d (group size <= %d)", n_heads,
+                         n_kv, FD_GMAX);
+    if (page_size <= 0 || page_size % FD_CHUNK)
+        return set_error(VSL_ERR_INVALID, "flash_decode_short: page_size %d must be a multiple of %d", page_size,
+                         FD_CHUNK);
+    if (max_len <= 0 || max_len > max_pages * page_size)
+        return set_error(VSL_ERR_INVALID, "flash_decode_short: max_len %d outside the page table", max_len);
+    FdParams p = {};
+    p.q = q; p.k_cache = k_cache; p.v_cache = v_cache; p.page_table = page_table; p.max_pages = max_pages;
+    p.page_size = page_size; p.pos = pos; p.B = B; p.n_heads = n_heads; p.n_kv = n_kv;
+    p.max_len = max_len; p.scale = 1.0f / sqrtf((float)head_dim); p.out = out;
+    p.pf_ptr = pf_ptr;
+    p.pf_bytes = pf_bytes;
+    p.status = status;
+    if (sparse) p.sp = *sparse;
+    if (kvdtype == VSL_F16) {
+        if (head_dim == 128) return launch_fs<128, __half>(p, stream);
+        if (head_dim == 64) return launch_fs<64, __half>(p, stream);
+    } else if (kvdtype == VSL_F32) {
+        if (head_dim == 128) return launch_fs<128, float>(p, stream);
+        if (head_dim == 64) return launch_fs<64, float>(p, stream);
+    }
+    return set_error(VSL_ERR_UNSUPPORTED, "flash_decode_short: head_dim %d / kv dtype %d", head_dim, kvdtype);
+}
+
 static size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
 
 static int fd_splits(int max_len, int split_len) { return (max_len + split_len - 1) / split_len; }
@@ -557,6 +876,17 @@ extern "C" int vsl_flash_decode(const float* q, const void* k_cache, const void*
     return vsl::flash_decode_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads,
                                   n_kv, head_dim, max_len, split_len, out, workspace, workspace_bytes,
                                   (cudaStream_t)stream, nullptr, 0, true, nullptr, 0, nullptr);  // the caller's rows may share pages
+}
+
+extern "C" int vsl_flash_decode_short(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
+                                      const int32_t* page_table, int max_pages, int page_size, const int32_t* pos,
+                                      int B, int n_heads, int n_kv, int head_dim, int max_len, float* out,
+                                      const vsl_sparse_mask* mask, int* status, void* stream) {
+    vsl::SparseMask m = {};
+    if (mask && mask->min_len > 0) m = vsl::SparseMask{mask->min_len, mask->window, mask->global_tokens, mask->block};
+    return vsl::flash_decode_short_impl(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B,
+                                        n_heads, n_kv, head_dim, max_len, out, (cudaStream_t)stream, nullptr, 0, &m,
+                                        status);
 }
 
 extern "C" int vsl_flash_decode_sparse(const float* q, const void* k_cache, const void* v_cache, int kvdtype,

@@ -127,6 +127,8 @@ def lib() -> C.CDLL:
         "vsl_engine_inject_status": (i32, [vp, i32]),
         "vsl_flash_decode_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, i32, vp, vp, sz,
                                           C.POINTER(SparseMask), vp]),
+        "vsl_flash_decode_short": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp,
+                                         C.POINTER(SparseMask), vp, vp]),
         "vsl_flash_prefill": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp,
                                     C.POINTER(SparseMask), vp, vp]),
         "vsl_flash_decode_tc_sparse": (i32, [vp, vp, vp, i32, vp, i32, i32, vp, i32, i32, i32, i32, i32, vp, vp, sz,
@@ -335,6 +337,16 @@ def flash_decode_tc(q, k_cache, v_cache, n_pages, page_table, max_pages, page_si
     check(lib().vsl_flash_decode_tc_sparse(_ptr(q), _ptr(k_cache), _ptr(v_cache), n_pages, _ptr(page_table),
                                            max_pages, page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len,
                                            _ptr(out), _ptr(workspace), workspace_bytes, C.byref(m), stream))
+
+
+def flash_decode_short(q, k_cache, v_cache, kvdtype, page_table, max_pages, page_size, pos, B, n_heads, n_kv,
+                       head_dim, max_len, out, sparse=None, status=None, stream=0):
+    """Short-cache decode attention (one CTA per sequence and KV group; no workspace).
+    sparse: None (dense) or (min_len, window, global_tokens, block)."""
+    m = C.byref(SparseMask(*sparse)) if sparse is not None else None
+    check(lib().vsl_flash_decode_short(_ptr(q), _ptr(k_cache), _ptr(v_cache), kvdtype, _ptr(page_table), max_pages,
+                                       page_size, _ptr(pos), B, n_heads, n_kv, head_dim, max_len, _ptr(out), m,
+                                       _ptr(status), stream))
 
 
 def flash_prefill(q, k_cache, v_cache, n_pages, page_row, max_pages, page_size, pos, n_rows, n_heads, n_kv, head_dim,
