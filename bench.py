@@ -890,6 +890,14 @@ def run_timeline(args):
     wbytes = {"qkv": (nh + 2 * nkv) * hd * d * 2, "o": d * nh * hd * 2, "gate_up": 2 * F * d * 2, "down": d * F * 2,
               "lm_head": cfg["vocab"] // ws * d * 2}
     K = args.steps
+    # phase stamps of the short-cache attention (tags 2301-2304, first round of each CTA)
+    ph = recs[(recs["tag"] > 2300) & (recs["tag"] < 2400)]
+    recs = recs[(recs["tag"] <= 2300) | (recs["tag"] >= 2400)]
+    att_phases = {}
+    for tag, name in ((2301, "release_to_staged"), (2302, "scores"), (2303, "softmax"), (2304, "p_v")):
+        r = ph[ph["tag"] == tag]
+        if len(r):
+            att_phases[name] = round(float(np.median((r["t1"] - r["t0"]).astype(np.int64))) / 1e3, 2)
     launches = []  # (replay, id, role-tag, records)
     for lid in np.unique(recs["id"]):
         r = recs[recs["id"] == lid]
@@ -957,6 +965,8 @@ def run_timeline(args):
             "tp": ws, "rank": rank, "steps": K, "step_us_p50": round(float(np.median(step_us)), 1),
             "step_span_note": "first CTA entry to last CTA exit of the traced kernels in one graph replay",
             "roles": out, "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}
+    if att_phases:
+        line["attention_phases_us_p50"] = att_phases
     print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

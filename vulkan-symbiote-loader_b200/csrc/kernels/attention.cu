@@ -467,6 +467,15 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
 // is at most FS_MAX_LEN positions. Older rows are requested before griddepcontrol.wait, the row
 // at pos (written by the predecessor) after it.
 // ---------------------------------------------------------------------------------------
+// Phase stamps of the trace build (thread 0, first round): [t0, t1] of a phase per CTA
+#ifdef VSL_TRACE
+#define FS_STAMP(var) const uint64_t var = vsl::trace_now()
+#define FS_PHASE(tag, ta, tb) \
+    if (tid == 0 && r == 0) vsl_trace_record(p.trace_id, (tag), (ta), (tb))
+#else
+#define FS_STAMP(var)
+#define FS_PHASE(tag, ta, tb)
+#endif
 constexpr int FS_THREADS = 512;
 constexpr int FS_WARPS = FS_THREADS / 32;
 template <typename KT>
@@ -484,7 +493,7 @@ __host__ __device__ constexpr size_t fs_smem_bytes() {
            + (size_t)4 * FD_GMAX * sizeof(float);                    // m, l, alpha
 }
 
-template <int HD, typename KT>
+template <int HD, typename KT, int GT>  // GT: query heads per KV group, rounded up to 1, 2, 4 or 8
 __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(FdParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int NCH = fs_chunks<KT>();
@@ -557,6 +566,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
     issue_round(0, new_row);
     pdl_wait();
     VSL_TRACE_RELEASED();
+    FS_STAMP(ts_rel);
     // q and the new row, written by the QKV projection (a position past the cache is never read:
     // the QKV kernel has flagged it in the status word)
     if (pos < len && new_row < R) {
@@ -581,9 +591,9 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
         l_s[tid] = 0.0f;
     }
     const int d_own = tid % HD, grp = tid / HD;  // P.V: head dimension and position group
-    float o_acc[FD_GMAX];
+    float o_acc[GT];
 #pragma unroll
-    for (int j = 0; j < FD_GMAX; j++) o_acc[j] = 0.0f;
+    for (int j = 0; j < GT; j++) o_acc[j] = 0.0f;
     bool staged_ok = true;
     int issued_rounds = 1;
     for (int r = 0; r < n_rounds; r++) {
@@ -596,13 +606,15 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
             staged_ok = false;
             break;
         }
+        FS_STAMP(ts_staged);
+        FS_PHASE(2301u, ts_rel, ts_staged);
         // scores: PARTS adjacent threads per position, each over VPR / PARTS 16-byte columns in an
         // order rotated by the position (conflict-free reads of the unpadded rows)
         {
             const int tt = tid / PARTS, part = tid % PARTS;
-            float acc[FD_GMAX];
+            float acc[GT];
 #pragma unroll
-            for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+            for (int j = 0; j < GT; j++) acc[j] = 0.0f;
             if (tt < n) {
                 const KT* kr = k_s + (size_t)tt * HD;
 #pragma unroll
@@ -611,7 +623,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
                     float kf[VEC];
                     KvVec<KT>::widen(*reinterpret_cast<const uint4*>(kr + cv * VEC), kf);
 #pragma unroll
-                    for (int j = 0; j < FD_GMAX; j++) {
+                    for (int j = 0; j < GT; j++) {
                         if (j < G) {
 #pragma unroll
                             for (int e = 0; e < VEC; e++) acc[j] = fmaf(q_s[j * QP + cv * QCOL + e], kf[e], acc[j]);
@@ -620,7 +632,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
                 }
             }
 #pragma unroll
-            for (int j = 0; j < FD_GMAX; j++) {
+            for (int j = 0; j < GT; j++) {
                 if (j >= G) break;
 #pragma unroll
                 for (int o = 1; o < PARTS; o <<= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
@@ -628,11 +640,13 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
             if (part == 0) {
                 const bool valid = tt < n && rb + tt >= lo;
 #pragma unroll
-                for (int j = 0; j < FD_GMAX; j++)
+                for (int j = 0; j < GT; j++)
                     if (j < G) s_s[j * R + tt] = valid ? acc[j] * p.scale : -CUDART_INF_F;
             }
         }
         __syncthreads();
+        FS_STAMP(ts_scores);
+        FS_PHASE(2302u, ts_staged, ts_scores);
         // maximum per head over the round
         for (int j = 0; j < G; j++) {
             const float v = tid < R ? s_s[j * R + tid] : -CUDART_INF_F;
@@ -669,23 +683,27 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
             m_s[tid] = fmaxf(mo, cm);
             l_s[tid] = l_s[tid] * a_s[tid] + sm;
         }
+        FS_STAMP(ts_soft);
+        FS_PHASE(2303u, ts_scores, ts_soft);
         // P.V: thread (d_own, grp) sums positions grp, grp + NG, ... of the round
         {
-            float acc[FD_GMAX];
+            float acc[GT];
 #pragma unroll
-            for (int j = 0; j < FD_GMAX; j++) acc[j] = 0.0f;
+            for (int j = 0; j < GT; j++) acc[j] = 0.0f;
 #pragma unroll 4
             for (int i = grp; i < n; i += NG) {
                 const float vv = (float)v_s[(size_t)i * HD + d_own];
 #pragma unroll
-                for (int j = 0; j < FD_GMAX; j++)
+                for (int j = 0; j < GT; j++)
                     if (j < G) acc[j] = fmaf(s_s[j * R + i], vv, acc[j]);
             }
 #pragma unroll
-            for (int j = 0; j < FD_GMAX; j++)
+            for (int j = 0; j < GT; j++)
                 if (j < G) o_acc[j] = o_acc[j] * a_s[j] + acc[j];
         }
         __syncthreads();  // the round's buffers, scores and statistics are consumed
+        FS_STAMP(ts_pv);
+        FS_PHASE(2304u, ts_soft, ts_pv);
         if (r + 1 < n_rounds) {
             issue_round(r + 1, -1);  // rows after the wait: the new row is already in the cache
             issued_rounds++;
@@ -708,7 +726,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
     }
     // the position groups, in a fixed order
 #pragma unroll
-    for (int j = 0; j < FD_GMAX; j++)
+    for (int j = 0; j < GT; j++)
         if (j < G) ored[(grp * FD_GMAX + j) * HD + d_own] = o_acc[j];
     __syncthreads();
     for (int i = tid; i < G * HD; i += FS_THREADS) {
@@ -721,9 +739,9 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
     VSL_TRACE_EXIT(p.trace_id, 905);
 }
 
-template <int HD, typename KT>
-static int launch_fs(const FdParams& p, cudaStream_t st) {
-    auto kern = vsl_flash_decode_short_kernel<HD, KT>;
+template <int HD, typename KT, int GT>
+static int launch_fs_g(const FdParams& p, cudaStream_t st) {
+    auto kern = vsl_flash_decode_short_kernel<HD, KT, GT>;
     constexpr size_t smem = fs_smem_bytes<HD, KT>();
     static thread_local int configured_dev = -1;
     int dev = 0;
@@ -736,6 +754,14 @@ static int launch_fs(const FdParams& p, cudaStream_t st) {
     FdParams pt = p;
     pt.trace_id = VSL_TRACE_ID();
     return launch_status(launch_k(kern, dim3(p.n_kv, p.B), dim3(FS_THREADS), smem, st, pt), "flash_decode_short launch");
+}
+template <int HD, typename KT>
+static int launch_fs(const FdParams& p, cudaStream_t st) {
+    const int G = p.n_heads / p.n_kv;
+    if (G <= 1) return launch_fs_g<HD, KT, 1>(p, st);
+    if (G <= 2) return launch_fs_g<HD, KT, 2>(p, st);
+    if (G <= 4) return launch_fs_g<HD, KT, 4>(p, st);
+    return launch_fs_g<HD, KT, 8>(p, st);
 }
 
 int flash_decode_short_impl(const float* q, const void* k_cache, const void* v_cache, int kvdtype,
