@@ -75,6 +75,7 @@ struct FpArgs {
     uint32_t idesc_s;           // Q2 (A, K-major) . K (B, K-major)
     uint32_t idesc_pv;          // P2 (A, K-major) . V (B, MN-major)
     SparseMask sp;
+    long long kv_rows;          // rows of the pool's tensor map (n_pages * n_kv * page_size)
     unsigned trace_id;          // launch id of the trace build (unused otherwise)
     void* x2;                   // non-null: write the split activations of the next projection instead of out
     int x2_bf16, x2_rows;       // their type; row of the first lo row
@@ -224,6 +225,28 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     pdl_wait();
     VSL_TRACE_RELEASED();
     __syncthreads();
+    // dense mask: chunk 0 starts at position 0 whatever the rows' positions, so the producer
+    // requests its K and V now, before the block's length is known (pages of positions past the
+    // cache end give rows that are masked (K) or zeroed (V) later; entries outside the page
+    // table's row or the pool fall back to row 0 of the pool)
+    const bool early = a.sp.min_len <= 0;
+    if (early && warp == FP_SM_WARPS && lane == 0) {
+        for (int kv = 0; kv < 2; kv++) {
+            uint64_t* full = kv ? &v_full : &k_full;
+            mbar_arrive_expect_tx(full, FP_TILE);
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                const int pi = (hh * 64) / a.page_size;
+                const int page = pi < a.max_pages ? __ldg(a.page_row + pi) : 0;
+                long long row = ((long long)page * a.n_kv + g) * a.page_size + (hh * 64) % a.page_size;
+                if (row < 0 || row + 64 > a.kv_rows) row = 0;
+#pragma unroll
+                for (int at = 0; at < 2; at++)
+                    fp_tma((kv ? vt : kt) + at * FP_ATOM + hh * (FP_ATOM / 2), kv ? &map_v : &map_k, at * 64, (int)row,
+                           full);
+            }
+        }
+    }
     // this thread's query row: position, first attended position; the block's cache length and
     // lowest first position
     int pr = -1, first = INT_MAX;
@@ -240,7 +263,6 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     fp_fence_before();
     __syncthreads();
     fp_fence_after();
-    pdl_launch_dependents();
     const uint32_t tmem = tmem_s;
     const int len = len_s;                          // >= 1: row 0 of the block exists
     const int c0 = (lo_s == INT_MAX ? 0 : lo_s) / FP_CHUNK;
@@ -249,9 +271,9 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
     if (warp == FP_SM_WARPS) {
         // ================= TMA producer: K(i) and V(i) into single tiles =================
         if (lane == 0) {
-            int issued_k = 0, issued_v = 0;
+            int issued_k = early ? 1 : 0, issued_v = early ? 1 : 0;  // chunk 0 already requested
             bool ok = true;
-            for (int i = 0; i < n && ok; i++) {
+            for (int i = early ? 1 : 0; i < n && ok; i++) {
                 for (int kv = 0; kv < 2 && ok; kv++) {
                     uint64_t* full = kv ? &v_full : &k_full;
                     uint64_t* empty = kv ? &v_empty : &k_empty;
@@ -426,7 +448,8 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             // probabilities, as fp16 hi / lo halves of the row of P2 (P2 of the previous chunk has
             // been read: its product completed before that chunk's fold below)
             // (a rolled loop over 8-column groups, re-reading the scores from TMEM: the code runs
-            // once per chunk, so a compact body avoids instruction-fetch stalls)
+            // once per chunk, and a compact body measured faster than the fully unrolled form
+            // working from registers, 6.2 against 9.9 us)
             float ls = 0.0f;
 #pragma unroll 1
             for (int c8 = 0; c8 < HALF / 8; c8++) {
@@ -471,6 +494,9 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_ready);
+            // the next projection's CTAs may start once the first chunk's probabilities are out
+            // (earlier, their weight requests delayed this kernel's K and V: 24.7 against 22.1 us)
+            if (i == 0) pdl_launch_dependents();
             FP_STAMP(ts_p);
             if (th == 0 && i == 0) FP_PHASE(2202u, ts_s, ts_p);
             // ---- fold PV(i) into this half of the row's accumulators ----
@@ -575,6 +601,7 @@ int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache,
     a.idesc_s = (1u << 4) | ((uint32_t)(FP_CHUNK >> 3) << 17) | ((uint32_t)(FP_ROWS >> 4) << 24);
     a.idesc_pv = (1u << 4) | ((uint32_t)(FP_HD >> 3) << 17) | ((uint32_t)(FP_ROWS >> 4) << 24) | (1u << 16);
     const long long rows = (long long)n_pages * n_kv * page_size;
+    a.kv_rows = rows;
     CUtensorMap mk, mv;
     int rc = kv_tensor_map(&mk, k_cache, rows);
     if (rc) return rc;
