@@ -292,9 +292,10 @@ typedef struct {
     double vram_budget_gb; /* 0 = no cap; above the cap layers stream from pinned host */
     int use_graph;     /* capture the decode step in a CUDA graph (default 1)          */
     int use_pdl;       /* programmatic dependent launch between kernels (default 1)    */
-    int use_fused;     /* 1 = run each decode step as one persistent cooperative kernel
-                          when the shape allows it; 0 (default) = one kernel per operation,
-                          replayed as a CUDA graph with programmatic dependent launch  */
+    int use_fused;     /* must be 0 (the default): decode steps run one kernel per operation,
+                          replayed as a CUDA graph with programmatic dependent launch; the
+                          persistent single-kernel step this field selected measured slower
+                          and was removed (1 is refused with VSL_ERR_UNSUPPORTED)          */
     int use_p2p;       /* tensor parallel: 1 (default) = one-shot NVLink peer-memory all-reduces
                           (CUDA IPC buffers, one kernel per reduction); 0 = NCCL            */
     int legacy_q4;     /* 1 = read GGUF Q4_0 / Q4_1 nibbles in the reference loader's order
@@ -464,13 +465,6 @@ VSL_API int vsl_engine_residency(vsl_engine* e, uint32_t* resident_layers, uint3
  * VSL_ERR_OOM when the budget cannot hold the fixed part plus two layer slots. */
 VSL_API int vsl_pack_plan(uint64_t layer_bytes, uint32_t n_layers, uint64_t fixed_bytes, double budget_gb,
                           uint32_t* resident_layers, uint32_t* streamed_layers);
-
-/* Per-phase trace of the fused decode step (one persistent kernel per token): when on, CTA 0
- * records %globaltimer (ns) at kernel start and after each phase barrier of every step;
- * vsl_engine_read_trace copies the last step's stamps (embedding, then per layer QKV,
- * attention, combine, O, gate/up, down, then lm_head). */
-VSL_API int vsl_engine_set_trace(vsl_engine* e, int enable);
-VSL_API int vsl_engine_read_trace(vsl_engine* e, int cap, uint64_t* out_ns, int* n_out);
 
 /* Sticky device status word of the engine (0 = OK; VSL_ERR_TIMEOUT / VSL_ERR_BOUNDS set by
  * kernels that gave up on a bounded wait or rejected an index). */

@@ -38,8 +38,6 @@ CHILD = textwrap.dedent("""
         "vsl_engine_generate_batch": (N, i32, i32, 1, 2, C.c_float(0.0), C.c_uint64(0), i32, 1, i32, i32),
         "vsl_engine_reset_seq": (N, 0),
         "vsl_engine_residency": (N, C.byref(u32), C.byref(u32), C.byref(u64), C.byref(u64)),
-        "vsl_engine_set_trace": (N, 1),
-        "vsl_engine_read_trace": (N, 1, (C.c_uint64 * 4)(), C.byref(i)),
         "vsl_engine_device_status": (N, C.byref(i)),
         "vsl_tokenizer_info": (N, C.byref(i), C.byref(i), i32, i32),
         "vsl_tokenize": (N, b"ab", 2, i32, 8, C.byref(i)),

@@ -183,49 +183,3 @@ def test_stop_ids_and_bounds():
         with pytest.raises(vsl.VslError):
             e.run(1)
         assert e.device_status() == 0
-
-
-@pytest.mark.parametrize("name,max_seq", [("tiny_fp32", 128), ("gqa_fp16", 64)])
-def test_fused_step_golden_ids(golden, fixture_gguf, name, max_seq):
-    """The persistent fused decode step reproduces the golden greedy ids on its own."""
-    g = golden(name)
-    with vsl.Engine.from_gguf(fixture_gguf(name), max_seq=max_seq, use_fused=1) as e:
-        kernels, _ = e.step_stats(1)
-        assert kernels == 1
-        assert e.generate(g["prompt"], g["n_new"]) == g["ids"]
-        assert e.device_status() == 0
-
-
-@pytest.mark.parametrize("wdtype,hd,nkv", [(vsl.F16, 128, 4), (vsl.BF16, 64, 2), (vsl.F32, 64, 8)])
-def test_fused_step_matches_per_op_kernels(wdtype, hd, nkv):
-    """The persistent fused decode step against the per-operation kernels on one model."""
-    nh = 8
-    cfg = dict(n_layers=3, d_model=nh * hd, n_heads=nh, n_kv_heads=nkv, head_dim=hd, ffn=1408, vocab=5000,
-               rope_theta=10000.0, rms_eps=1e-5, wdtype=wdtype)
-    ids = synth.synth_ids(12, 2, 90, cfg["vocab"])
-    runs = []
-    for fused in (1, 0):
-        with vsl.Engine.synthetic(cfg, seed=12, max_seq=160, use_fused=fused) as e:
-            kernels, _ = e.step_stats(1)
-            assert (kernels == 1) == bool(fused)
-            lg = [e.step_host([t], want_logits=True)[1][0] for t in ids[:70]]
-            gen = e.generate(ids[:9], 60)
-            assert e.device_status() == 0
-            runs.append((np.stack(lg), gen))
-    tol = 1e-4 if wdtype == vsl.F32 else 2e-3
-    assert np.abs(runs[0][0] - runs[1][0]).max() < tol
-    assert runs[0][1] == runs[1][1]
-
-
-def test_fused_step_batch_and_long_prefill():
-    """Batch 4 with a 700-position prefilled cache (several attention chunks per sequence)."""
-    cfg = dict(n_layers=2, d_model=1024, n_heads=8, n_kv_heads=2, head_dim=128, ffn=2048, vocab=4000,
-               rope_theta=500000.0, rms_eps=1e-5, wdtype=vsl.BF16)
-    res = {}
-    for fused in (1, 0):
-        with vsl.Engine.synthetic(cfg, seed=3, max_batch=4, max_seq=800, use_fused=fused) as e:
-            e.fill_kv_synthetic(9, 1.0, 700, 4)
-            ids = synth.synth_ids(3, 4, 4 * 6, cfg["vocab"]).reshape(6, 4)
-            res[fused] = np.stack([e.step_host(ids[s], want_logits=True)[1] for s in range(6)])
-            assert e.device_status() == 0
-    assert np.abs(res[1] - res[0]).max() < 2e-3

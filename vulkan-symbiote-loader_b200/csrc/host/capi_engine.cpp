@@ -293,16 +293,3 @@ extern "C" int vsl_pack_plan(uint64_t layer_bytes, uint32_t n_layers, uint64_t f
     return VSL_OK;
 }
 
-extern "C" int vsl_engine_set_trace(vsl_engine* e, int enable) {
-    GUARD_BEGIN
-    if (int rc = check_engine(e)) return rc;
-    return e->impl->set_trace(enable != 0);
-    GUARD_END
-}
-
-extern "C" int vsl_engine_read_trace(vsl_engine* e, int cap, uint64_t* out_ns, int* n_out) {
-    GUARD_BEGIN
-    if (int rc = check_engine(e)) return rc;
-    return e->impl->read_trace(cap, reinterpret_cast<unsigned long long*>(out_ns), n_out);
-    GUARD_END
-}

@@ -211,6 +211,8 @@ int DecodeEngine::init(const vsl_model_config& cfg, const vsl_engine_options& op
     if (split_len_ % 64) return set_error(VSL_ERR_INVALID, "engine: split_len %d must be a multiple of 64", split_len_);
     set_pdl_enabled(opt.use_pdl != 0);
     if (opt.attn_route < 0 || opt.attn_route > 3) return set_error(VSL_ERR_INVALID, "engine: attn_route %d", opt.attn_route);
+    if (opt.use_fused)
+        return set_error(VSL_ERR_UNSUPPORTED, "engine: use_fused (the persistent single-kernel step was removed)");
     if (opt.sparse_min_len < 0 || opt.sparse_window < 0 || opt.sparse_global < 0 || opt.sparse_block < 0)
         return set_error(VSL_ERR_INVALID, "engine: negative sparse attention parameter");
     if (opt.sparse_min_len > 0)  // zeros take the reference's values (Common.h:71-74)
@@ -340,12 +342,6 @@ int DecodeEngine::alloc_buffers() {
         {(void**)&rope_sin_, (size_t)opt_.max_seq * half * 4},
         {(void**)&page_table_, mb * (size_t)max_pages_ * 4},
         {(void**)&ar_epochs_, 2 * P2P_MAX_CHUNKS * 8},
-        {(void**)&fs_bar_, 16},
-        {(void**)&fs_abort_, 4},
-        {(void**)&fs_att_ws_, mb * (size_t)nh_l_ * (size_t)((opt_.max_seq + 63) / 64) * (hd + 2) * 4},
-        {(void**)&fs_phases_, (size_t)(3 + 6 * c.n_layers) * sizeof(FsPhase)},
-        {(void**)&fs_kv_, (size_t)c.n_layers * sizeof(FsKV)},
-        {(void**)&fs_trace_, (size_t)(4 + 6 * c.n_layers) * 8},
     };
     size_t total = 0;
     for (auto& it : items) total += align_up(it.bytes, A);
@@ -462,125 +458,9 @@ int DecodeEngine::alloc_buffers() {
     CK(cudaMemcpy(page_table_, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
     pt_host_ = pt;
     pos_host_.assign(mb, 0);
-    return build_fused_program();
-}
-
-// Phase list of the fused decode step (one persistent kernel per token): embedding, then per
-// layer QKV (+RoPE, KV append) -> attention chunks -> combine -> O (+residual) ->
-// gate/up (+SwiGLU) -> down (+residual), then lm_head (+argmax) and the token bookkeeping.
-int DecodeEngine::build_fused_program() {
-    fs_ready_ = false;
-    if (!opt_.use_fused || opt_.tp_size != 1 || residency_.streamed_layers || is_quant(cfg_.wdtype)) return VSL_OK;
-    const vsl_model_config& c = cfg_;
-    const int hd = c.head_dim, d = c.d_model;
-    const int vec = (int)(16 / es_);
-    std::vector<FsPhase> ph;
-    auto gemv = [&](int epi, int layer, int N, int K, const void* W, const float* x, float* y, const float* nw) {
-        FsPhase f = {};
-        f.kind = FS_GEMV;
-        f.epi = epi;
-        f.layer = layer;
-        f.N = N;
-        f.K = K;
-        f.W = W;
-        f.x = x;
-        f.y = y;
-        f.norm_w = nw;
-        fs_geometry(K, (int)es_, vec, &f.R, &f.kc, &f.n_kc, &f.cg);
-        ph.push_back(f);
-    };
-    auto simple = [&](int kind, int layer) {
-        FsPhase f = {};
-        f.kind = kind;
-        f.layer = layer;
-        ph.push_back(f);
-    };
-    // EK_* values of the shared epilogues (kernels/epilogue.cuh)
-    enum { E_STORE = 0, E_ADD = 1, E_SWIGLU = 2, E_QKV = 3, E_LMHEAD = 4 };
-    simple(FS_EMBED, 0);
-    for (int l = 0; l < c.n_layers; l++) {
-        const LayerPtrs& L = layers_[l];
-        gemv(E_QKV, l, (nh_l_ + 2 * nkv_l_) * hd, d, L.wqkv, x_, nullptr, L.attn_norm);
-        simple(FS_ATTN, l);
-        simple(FS_ATTN_COMBINE, l);
-        gemv(E_ADD, l, d, nh_l_ * hd, L.wo, attn_, x_, nullptr);
-        gemv(E_SWIGLU, l, 2 * ff_l_, d, L.wgu, x_, act_ffn_, L.ffn_norm);
-        gemv(E_ADD, l, d, ff_l_, L.wd, act_ffn_, x_, nullptr);
-    }
-    gemv(E_LMHEAD, 0, v_l_, d, lm_head_, x_, logits_, out_norm_);
-    simple(FS_FINAL, 0);
-    fs_n_phases_ = (int)ph.size();
-    fs_max_chunks_ = (opt_.max_seq + 63) / 64;
-    std::vector<FsKV> kv(c.n_layers);
-    for (int l = 0; l < c.n_layers; l++) kv[l] = FsKV{layers_[l].k_cache, layers_[l].v_cache};
-    CK(cudaMemcpy(fs_phases_, ph.data(), ph.size() * sizeof(FsPhase), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(fs_kv_, kv.data(), kv.size() * sizeof(FsKV), cudaMemcpyHostToDevice));
-    fs_ready_ = true;
     return VSL_OK;
 }
 
-bool DecodeEngine::fused_supported(int B) const {
-    if (!fs_ready_ || B < 1 || B > 4 || residency_.streamed_layers || sparse_.min_len > 0) return false;
-    const vsl_model_config& c = cfg_;
-    if (c.head_dim != 64 && c.head_dim != 128) return false;
-    if (c.head_dim == 128 && kvdtype_ != VSL_F16) return false;
-    if (nh_l_ / nkv_l_ > 8) return false;
-    const size_t work = FS_WORK;
-    const int vec = (int)(16 / es_);
-    for (int K : {c.d_model, nh_l_ * c.head_dim, ff_l_})
-        if ((size_t)B * K * 4 > work || K % vec != 0) return false;
-    return true;
-}
-
-int DecodeEngine::enqueue_fused_step(int B, float temperature, uint64_t seed) {
-    const vsl_model_config& c = cfg_;
-    FsProgram P = {};
-    P.phases = fs_phases_;
-    P.n_phases = fs_n_phases_;
-    P.n_barriers = fs_n_phases_ - 1;
-    P.kv = fs_kv_;
-    P.B = B;
-    P.d = c.d_model;
-    P.nh = nh_l_;
-    P.nkv = nkv_l_;
-    P.hd = c.head_dim;
-    P.wdtype = c.wdtype;
-    P.kvdtype = kvdtype_;
-    P.eps = c.rms_eps;
-    P.tok_embd = tok_embd_;
-    P.V = c.vocab;
-    P.page_table = page_table_;
-    P.max_pages = max_pages_;
-    P.page_size = page_size_;
-    P.max_seq = opt_.max_seq;
-    P.rope_cos = rope_cos_;
-    P.rope_sin = rope_sin_;
-    P.x = x_;
-    P.q = q_;
-    P.attn = attn_;
-    P.att_ws = fs_att_ws_;
-    P.max_chunks = fs_max_chunks_;
-    P.logits = logits_;
-    P.V_local = v_l_;
-    P.vocab_offset = v_off_;
-    P.inv_temp = temperature > 0.0f ? 1.0f / temperature : 0.0f;
-    P.seed = seed;
-    P.slots = slots_;
-    P.ids = ids_;
-    P.pos = pos_;
-    P.step = step_;
-    P.forced = forced_;
-    P.n_forced = n_forced_;
-    P.log = log_;
-    P.log_cap = log_cap_;
-    P.sampled = sampled_;
-    P.status = status_;
-    P.bar_counter = fs_bar_;
-    P.bar_epoch = fs_bar_ + 1;
-    P.abort_flag = fs_abort_;
-    P.trace = fs_trace_on_ ? fs_trace_ : nullptr;
-    return fused_step_launch(P, sm_count(), stream_);
-}
 
 // ---------------------------------------------------------------------------------------
 // weight upload
@@ -807,8 +687,6 @@ int DecodeEngine::reset() {
     CK(cudaMemsetAsync(step_, 0, 4, stream_));
     CK(cudaMemsetAsync(n_forced_, 0, 4, stream_));
     CK(cudaMemsetAsync(status_, 0, 4, stream_));
-    CK(cudaMemsetAsync(fs_bar_, 0, 16, stream_));
-    CK(cudaMemsetAsync(fs_abort_, 0, 4, stream_));
     if (tc_ws_) CK(cudaMemsetAsync(tc_ws_, 0, tc_ws_bytes_, stream_));  // arrival counters
     if (fdtc_ws_) CK(cudaMemsetAsync(fdtc_ws_, 0, fdtc_ws_bytes_, stream_));
     if (pf_tc_ws_) CK(cudaMemsetAsync(pf_tc_route_.ws, 0, pf_tc_route_.bytes, stream_));
@@ -950,7 +828,6 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
 }
 
 int DecodeEngine::enqueue_step(int B, float temperature, uint64_t seed) {
-    if (fused_supported(B)) return enqueue_fused_step(B, temperature, seed);
     const vsl_model_config& c = cfg_;
     const int d = c.d_model, hd = c.head_dim;
     cudaStream_t st = stream_;
@@ -1334,12 +1211,10 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
     double kv = 0;
     const double kv_es = (double)dtype_bytes(kvdtype_);
     for (int b = 0; b < B; b++) kv += 2.0 * c.n_layers * nkv_l_ * hd * kv_es * (pos_host_[b] + 1);
-    if (kernels && fused_supported(B)) {
-        *kernels = 1;
-    } else if (kernels) {
+    if (kernels) {
         // GEMV launches cover at most 4 activation rows (fewer when K is large), see gemv.cu;
         // batches on the tensor-core route take two launches per projection (split + GEMM)
-        const bool tc = tc_ws_ && B >= TC_MIN_BATCH && B <= 64;
+        const bool tc = tc_ws_ && B >= TC_MIN_BATCH && B <= TC_MAX_BATCH;
         auto chunks = [&](int K) {
             if (tc) return 2;
             int cmax = (int)std::min<size_t>(4, (200 * 1024) / ((size_t)K * 4));
@@ -1359,28 +1234,5 @@ int DecodeEngine::step_stats(int B, int* kernels, double* bytes) {
 
 int DecodeEngine::device_of_layer(int) const { return opt_.device; }
 
-// Per-phase timing of the fused step: the graph bakes the trace pointer in, so switching
-// tracing drops the captured graphs.
-int DecodeEngine::set_trace(bool on) {
-    if (on == fs_trace_on_) return VSL_OK;
-    CK(cudaSetDevice(opt_.device));
-    RC(sync());
-    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
-    graphs_.clear();
-    fs_trace_on_ = on;
-    return VSL_OK;
-}
-
-int DecodeEngine::read_trace(int cap, unsigned long long* out, int* n) {
-    if (!out || !n) return set_error(VSL_ERR_INVALID, "read_trace: null output");
-    *n = 0;
-    if (!fs_ready_) return VSL_OK;
-    CK(cudaSetDevice(opt_.device));
-    RC(sync());
-    const int m = std::min(cap, fs_n_phases_);  // start + one stamp per barrier
-    CK(cudaMemcpy(out, fs_trace_, (size_t)m * 8, cudaMemcpyDeviceToHost));
-    *n = m;
-    return VSL_OK;
-}
 
 }  // namespace vsl

@@ -21,7 +21,6 @@
 #include "kernels.h"
 #include "../kernels/p2p_allreduce.h"
 #include "../../../include/vsl.h"
-#include "../kernels/fused_step.h"
 
 namespace vsl {
 
@@ -74,8 +73,6 @@ public:
     // gave up on a bounded wait or rejected an index would (failures are made on the host).
     int inject_status(int code);
     int step_stats(int B, int* kernels, double* bytes);
-    int set_trace(bool on);
-    int read_trace(int cap, unsigned long long* out, int* n);
 
     const vsl_model_config& config() const { return cfg_; }
     cudaStream_t stream() const { return stream_; }
@@ -91,9 +88,6 @@ private:
     int init(const vsl_model_config& cfg, const vsl_engine_options& opt);
     int alloc_buffers();
     int enqueue_step(int B, float temperature, uint64_t seed);
-    int build_fused_program();
-    bool fused_supported(int B) const;
-    int enqueue_fused_step(int B, float temperature, uint64_t seed);
     int get_graph(int B, float temperature, uint64_t seed, cudaGraphExec_t* exec);
     // buffers of one pass over the decoder layers (decode step or prefill chunk)
     struct StepBufs {
@@ -250,17 +244,6 @@ private:
     };
     std::map<GraphKey, cudaGraphExec_t> graphs_;
 
-    // fused decode step
-    FsPhase* fs_phases_ = nullptr;  // device
-    FsKV* fs_kv_ = nullptr;         // device
-    int fs_n_phases_ = 0;
-    int fs_max_chunks_ = 0;
-    float* fs_att_ws_ = nullptr;
-    unsigned long long* fs_bar_ = nullptr;  // [counter, epoch]
-    int* fs_abort_ = nullptr;
-    unsigned long long* fs_trace_ = nullptr;
-    bool fs_trace_on_ = false;
-    bool fs_ready_ = false;
 
     void* nccl_ = nullptr;  // ncclComm_t
     vk_symbiote::PackResidency residency_{};

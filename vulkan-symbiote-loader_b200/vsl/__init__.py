@@ -113,8 +113,6 @@ def lib() -> C.CDLL:
         "vsl_engine_stream": (vp, [vp]),
         "vsl_engine_step_stats": (i32, [vp, i32, C.POINTER(i32), C.POINTER(f64)]),
         "vsl_engine_device_status": (i32, [vp, C.POINTER(i32)]),
-        "vsl_engine_set_trace": (i32, [vp, i32]),
-        "vsl_engine_read_trace": (i32, [vp, i32, C.POINTER(C.c_uint64), C.POINTER(i32)]),
         "vsl_engine_memory_stats": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
         "vsl_engine_prefill": (i32, [vp, vp, i32, i32, C.POINTER(i32), vp]),
         "vsl_engine_reset_seq": (i32, [vp, i32]),
@@ -532,17 +530,6 @@ class Engine:
         b = C.c_double()
         check(lib().vsl_engine_step_stats(self.h, batch, C.byref(k), C.byref(b)))
         return k.value, b.value
-
-    def set_trace(self, on: bool = True):
-        check(lib().vsl_engine_set_trace(self.h, 1 if on else 0))
-
-    def read_trace(self):
-        """Nanosecond stamps of the last fused step: start, then one per phase barrier."""
-        cap = 4096
-        buf = (C.c_uint64 * cap)()
-        n = C.c_int()
-        check(lib().vsl_engine_read_trace(self.h, cap, buf, C.byref(n)))
-        return [int(buf[i]) for i in range(n.value)]
 
     def memory_stats(self):
         w, kv, o = C.c_size_t(), C.c_size_t(), C.c_size_t()
