@@ -865,15 +865,17 @@ def run_timeline(args):
     ws, rank, local = vdist.env()
     dist = vdist.init(ws)
     torch.cuda.set_device(local)
-    cfg = dict(CONFIG_7B)
+    w70 = args.workload == "70b"  # the 70B shape after a 2048-token prompt (--layers for a reduced depth)
+    cfg = dict(CONFIG_70B if w70 else CONFIG_7B)
     if args.layers:
         cfg["n_layers"] = args.layers
-    max_seq = (PROMPT + args.warmup + args.steps + 8 + 63) // 64 * 64
+    prompt_len = PREFILL_70B if w70 else PROMPT
+    max_seq = (prompt_len + args.warmup + args.steps + 8 + 63) // 64 * 64
     nid = vdist.nccl_id(dist)
     eng = vsl.Engine.synthetic(cfg, seed=SEED, sigma=SIGMA, device=local, max_seq=max_seq, tp_rank=rank, tp_size=ws,
                                nccl_id=nid, split_len=args.split_len, p2p_chunk_bytes=args.p2p_chunk,
                                attn_route=args.attn_route, attn_prefetch=args.attn_prefetch)
-    eng.prefill(synth.synth_ids(SEED, 0, PROMPT, cfg["vocab"]))
+    eng.prefill(synth.synth_ids(SEED, 0, prompt_len, cfg["vocab"]))
     eng.run(args.warmup)
     torch.cuda.synchronize()
     if dist:
@@ -961,7 +963,8 @@ def run_timeline(args):
         if role in wbytes:
             e["weight_gbs_over_span"] = round(wbytes[role] / (a["span"] / c * 1e-6) / 1e9, 1)
         out[role] = e
-    line = {"timeline": "decode step, 7B fp16 bs1" + (f" ({cfg['n_layers']} layers)" if args.layers else ""),
+    line = {"timeline": ("decode step, 70B fp16 bs1 after 2048 positions" if w70 else "decode step, 7B fp16 bs1") +
+                        (f" ({cfg['n_layers']} layers)" if args.layers else ""),
             "tp": ws, "rank": rank, "steps": K, "step_us_p50": round(float(np.median(step_us)), 1),
             "step_span_note": "first CTA entry to last CTA exit of the traced kernels in one graph replay",
             "roles": out, "library": "lib/libvsl_trace.so (trace build; timings perturbed slightly by the stamps)"}

@@ -34,6 +34,9 @@
 #include "common.cuh"
 #include "kv_map.h"
 #include "launch.cuh"
+#include "trace.cuh"
+
+VSL_TRACE_UNIT(attention_tc)
 
 namespace vsl {
 
@@ -64,6 +67,7 @@ struct FtArgs {
     uint32_t idesc;     // S MMA: K (A, K-major) . Q2 (B, K-major)
     uint32_t idesc_pv;  // PV MMA: V (A, MN-major) . P2 (B, K-major)
     SparseMask sp;      // long-context sparse mask (sp.min_len 0: dense)
+    unsigned trace_id;  // launch id of the trace build (unused otherwise)
 };
 
 __device__ __forceinline__ void ft_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -145,6 +149,7 @@ __device__ __forceinline__ void ft_next(const FtWork& w, int n_kv, FtCur& c) {
 __global__ void __launch_bounds__(FT_THREADS, 1)
     vsl_flash_decode_tc_kernel(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                            const __grid_constant__ FtArgs a) {
+    VSL_TRACE_ENTRY();
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t full[FT_STAGES], empty[FT_STAGES], s_full[2], s_free[2], q_ready;
     __shared__ __align__(8) uint64_t p_ready[2], o_full[2], o_free[2];
@@ -184,6 +189,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     pdl_wait();
+    VSL_TRACE_RELEASED();
     pdl_launch_dependents();
     if (warp == 0) {  // work list from the current positions
         for (int b = lane; b < a.B; b += 32) {
@@ -576,6 +582,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         ft_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(64) : "memory");
     }
+    VSL_TRACE_EXIT(a.trace_id, 907u);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -653,6 +660,7 @@ int flash_decode_tc_impl(const float* q, const void* k_cache, const void* v_cach
     w += (size_t)grid * 2 * FT_GMAX * 2 * 4;
     a.counters = reinterpret_cast<int*>(w);
     a.status = status;
+    a.trace_id = VSL_TRACE_ID();
     if (sparse && sparse->min_len > 0) {
         if (sparse->window < 0 || sparse->global_tokens < 0 || sparse->block <= 0)
             return set_error(VSL_ERR_INVALID, "flash_decode_tc: sparse mask window %d, global %d, block %d",

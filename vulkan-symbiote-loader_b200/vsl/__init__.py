@@ -140,7 +140,7 @@ def lib() -> C.CDLL:
     return L
 
 
-TRACE_UNITS = ("gemv", "attention", "p2p", "tc", "prefill")
+TRACE_UNITS = ("gemv", "attention", "p2p", "tc", "prefill", "attention_tc")
 
 
 def trace_records(reset: bool = True):
