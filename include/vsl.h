@@ -309,11 +309,11 @@ typedef struct {
     int sparse_window;   /* window W (0 = 512)                                               */
     int sparse_global;   /* global tokens G (0 = 16)                                         */
     int sparse_block;    /* block BLK (0 = 1024)                                             */
-    int attn_route;      /* decode attention: 0 (default) = tcgen05-score attention when max_seq >= 2048,
-                          the short-cache kernel (one CTA per sequence and KV group, 256-position
-                          rounds) when max_seq <= 1024, the split-K kernel between; 1 = split-K
-                          always; 2 = tcgen05 attention always (fp16 KV, head_dim 128); 3 = the
-                          short-cache kernel always                                          */
+    int attn_route;      /* decode attention: 0 (default) = tcgen05-score attention when max_seq >= 2048
+                          and max_batch >= 8, the short-cache kernel (one CTA per sequence and KV
+                          group, 256-position rounds) when max_seq <= 1024, the split-K kernel
+                          otherwise; 1 = split-K always; 2 = tcgen05 attention always (fp16 KV,
+                          head_dim 128); 3 = the short-cache kernel always                  */
     int attn_prefetch;   /* 1 = the split-K attention kernel requests the output projection's weights
                           into L2 while it runs; 0 (default) = it does not (measured faster)  */
     int p2p_chunk_bytes; /* tensor parallel with use_p2p: bytes of the residual all-reduce's message

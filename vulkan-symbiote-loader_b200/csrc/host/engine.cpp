@@ -358,8 +358,11 @@ int DecodeEngine::alloc_buffers() {
 
     // short caches: one CTA per (sequence, KV group), no split combine
     short_attn_ = opt_.attn_route == 3 || (opt_.attn_route == 0 && opt_.max_seq <= FS_MAX_LEN);
-    // long caches: attention with tcgen05 scores and an even split of the KV over the SMs
-    const bool want_tc = opt_.attn_route == 2 || (opt_.attn_route == 0 && opt_.max_seq >= FDTC_MIN_SEQ);
+    // long caches of several sequences: attention with tcgen05 scores and an even split of the
+    // KV over the SMs (with one or a few sequences its merge of many splits is the tail: at 70B
+    // batch 1 over 2048 positions 114 us per layer against 38.5 us for the split-K kernel)
+    const bool want_tc = opt_.attn_route == 2 ||
+                         (opt_.attn_route == 0 && opt_.max_seq >= FDTC_MIN_SEQ && opt_.max_batch >= FDTC_MIN_BATCH);
     if (want_tc &&
         flash_decode_tc_supported(kvdtype_, c.head_dim, nh_l_, nkv_l_, opt_.max_batch, page_size_)) {
         fdtc_ws_bytes_ = flash_decode_tc_workspace_bytes(opt_.max_batch, nkv_l_);

@@ -84,7 +84,8 @@ int flash_prefill_impl(const float* q, const void* k_cache, const void* v_cache,
                        int max_pages, int page_size, const int32_t* pos, int P, int n_heads, int n_kv, int max_len,
                        float* out, int* status, cudaStream_t st, const SparseMask* sparse = nullptr,
                        void* x2 = nullptr, int x2_bf16 = 0, int x2_rows = 0);
-constexpr int FDTC_MIN_SEQ = 2048;  // caches from this length on use the tensor-core attention
+constexpr int FDTC_MIN_SEQ = 2048;   // caches from this length on use the tensor-core attention ...
+constexpr int FDTC_MIN_BATCH = 8;    // ... when the engine serves at least this many sequences
 int synth_impl(void* dst, int dtype, uint64_t seed, uint64_t tid, uint64_t start, uint64_t n, double sigma,
                cudaStream_t st);
 int finalize_impl(const unsigned long long* slots, int B, int32_t* ids, int32_t* pos, int32_t* step_counter,

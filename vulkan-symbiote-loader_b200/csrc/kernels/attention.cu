@@ -395,60 +395,83 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
     }
     __threadfence();
     // ---- combine the active splits of every head in this group ----
-    // The split statistics and weights are staged in shared memory by all threads at once (one
-    // L2 round trip each), so the combine costs a few round trips rather than one per split.
-    // Sums run in split order, as a sequential combine would.
-    constexpr int EPT = (HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
-    float* cw = part_s;                       // exp(m_s - M) of a tile of splits
-    float* cl = part_s + FD_GMAX * FD_CHUNK;  // l_s of the same tile
-    constexpr int TILE = FD_GMAX * FD_CHUNK;
-    float* red = a_s + FD_GMAX;               // FD_THREADS / 32 partial maxima
-    for (int j = 0; j < G; j++) {
-        const size_t row0 = ((size_t)b * p.n_heads + h0 + j) * p.n_splits + s_first;
-        float mx = -CUDART_INF_F;
-        for (int s = tid; s < n_active; s += FD_THREADS) mx = fmaxf(mx, __ldcg(p.ws_ml + (row0 + s) * 2));
-        mx = warp_max(mx);
-        if (lane == 0) red[warp] = mx;
+    // All G heads at once: the split statistics of a tile of splits are staged in shared memory
+    // by all threads (one L2 round trip), then each thread sums its (head, dimension) elements
+    // over the tile with eight loads in flight, so the combine costs a few round trips rather
+    // than a few per head. Sums run in split order, as a sequential combine would.
+    constexpr int EPT = (FD_GMAX * HD + FD_THREADS - 1) / FD_THREADS;  // output elements per thread
+    constexpr int TS = (FD_PARTS * FD_GMAX * FD_CHUNK) / FD_GMAX;       // splits per staged tile
+    float* cw = part_s;          // [TS][GMAX] exp(m_s - M_j)
+    float* cl = ored;            // [TS][GMAX] l_s
+    float* mx_s = p_s;           // [GMAX] per-head maxima
+    float* l_tot = p_s + FD_GMAX;  // [GMAX] per-head sums
+    float* redw = p_s + 2 * FD_GMAX;  // [warps][GMAX]
+    const size_t hrow0 = ((size_t)b * p.n_heads + h0) * p.n_splits + s_first;  // head h0 + j: + j * n_splits
+    {
+        float mx[FD_GMAX];
+#pragma unroll
+        for (int j = 0; j < FD_GMAX; j++) {
+            mx[j] = -CUDART_INF_F;
+            if (j < G)
+                for (int sp = tid; sp < n_active; sp += FD_THREADS)
+                    mx[j] = fmaxf(mx[j], __ldcg(p.ws_ml + (hrow0 + (size_t)j * p.n_splits + sp) * 2));
+        }
+#pragma unroll
+        for (int j = 0; j < FD_GMAX; j++) {
+            if (j >= G) break;
+            const float m = warp_max(mx[j]);
+            if (lane == 0) redw[warp * FD_GMAX + j] = m;
+        }
         __syncthreads();
-        float M = red[0];
+        if (tid < G) {
+            float M = redw[tid];
+            for (int w = 1; w < FD_THREADS / 32; w++) M = fmaxf(M, redw[w * FD_GMAX + tid]);
+            mx_s[tid] = M;
+            l_tot[tid] = 0.0f;
+        }
+    }
+    float acc[EPT];
 #pragma unroll
-        for (int w = 1; w < FD_THREADS / 32; w++) M = fmaxf(M, red[w]);
-        float L = 0.0f;
-        float acc[EPT];
+    for (int i = 0; i < EPT; i++) acc[i] = 0.0f;
+    for (int t0 = 0; t0 < n_active; t0 += TS) {
+        const int nt = min(TS, n_active - t0);
+        __syncthreads();  // maxima written; the previous tile consumed
 #pragma unroll
-        for (int i = 0; i < EPT; i++) acc[i] = 0.0f;
-        for (int t0 = 0; t0 < n_active; t0 += TILE) {
-            const int nt = min(TILE, n_active - t0);
-            __syncthreads();  // previous tile (and red) consumed
-            for (int s = tid; s < nt; s += FD_THREADS) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (row0 + t0 + s) * 2));
-                cw[s] = expf(ml.x - M);
-                cl[s] = ml.y;
-            }
-            __syncthreads();
-            for (int s = 0; s < nt; s++) L += cl[s] * cw[s];
-#pragma unroll
-            for (int i = 0; i < EPT; i++) {
-                const int e = tid + i * FD_THREADS;
-                if (e >= HD) continue;
-                const float* src = p.ws_o + (row0 + t0) * HD + e;
-                int s = 0;
-                for (; s + 8 <= nt; s += 8) {  // eight independent loads in flight
-                    float o[8];
-#pragma unroll
-                    for (int u = 0; u < 8; u++) o[u] = __ldcg(src + (size_t)(s + u) * HD);
-#pragma unroll
-                    for (int u = 0; u < 8; u++) acc[i] += o[u] * cw[s + u];
-                }
-                for (; s < nt; s++) acc[i] += __ldcg(src + (size_t)s * HD) * cw[s];
+        for (int j = 0; j < FD_GMAX; j++) {
+            if (j >= G) break;
+            for (int sp = tid; sp < nt; sp += FD_THREADS) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.ws_ml + (hrow0 + (size_t)j * p.n_splits + t0 + sp) * 2));
+                cw[sp * FD_GMAX + j] = expf(ml.x - mx_s[j]);
+                cl[sp * FD_GMAX + j] = ml.y;
             }
         }
+        __syncthreads();
+        if (tid < G)
+            for (int sp = 0; sp < nt; sp++) l_tot[tid] += cl[sp * FD_GMAX + tid] * cw[sp * FD_GMAX + tid];
 #pragma unroll
         for (int i = 0; i < EPT; i++) {
             const int e = tid + i * FD_THREADS;
-            if (e < HD) p.out[((size_t)b * p.n_heads + h0 + j) * HD + e] = acc[i] / L;
+            if (e >= G * HD) continue;
+            const int j = e / HD, d = e - j * HD;
+            const float* src = p.ws_o + (hrow0 + (size_t)j * p.n_splits + t0) * HD + d;
+            int sp = 0;
+            for (; sp + 8 <= nt; sp += 8) {  // eight independent loads in flight
+                float o[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) o[u] = __ldcg(src + (size_t)(sp + u) * HD);
+#pragma unroll
+                for (int u = 0; u < 8; u++) acc[i] += o[u] * cw[(sp + u) * FD_GMAX + j];
+            }
+            for (; sp < nt; sp++) acc[i] += __ldcg(src + (size_t)sp * HD) * cw[sp * FD_GMAX + j];
         }
-        __syncthreads();  // red / cw reused by the next head
+    }
+    __syncthreads();  // the last tile's sums are in l_tot
+#pragma unroll
+    for (int i = 0; i < EPT; i++) {
+        const int e = tid + i * FD_THREADS;
+        if (e >= G * HD) continue;
+        const int j = e / HD, d = e - j * HD;
+        p.out[((size_t)b * p.n_heads + h0 + j) * HD + d] = acc[i] / l_tot[j];
     }
     if (tid == 0) p.counters[(size_t)b * p.n_kv + g] = 0;
     VSL_TRACE_EXIT(p.trace_id, 903);
