@@ -448,22 +448,30 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
         __syncthreads();
         if (tid < G)
             for (int sp = 0; sp < nt; sp++) l_tot[tid] += cl[sp * FD_GMAX + tid] * cw[sp * FD_GMAX + tid];
+        // the thread's elements advance together, eight splits at a time: EPT x 8 loads in flight
+        const float* src[EPT];
+        int jj[EPT];
 #pragma unroll
         for (int i = 0; i < EPT; i++) {
-            const int e = tid + i * FD_THREADS;
-            if (e >= G * HD) continue;
-            const int j = e / HD, d = e - j * HD;
-            const float* src = p.ws_o + (hrow0 + (size_t)j * p.n_splits + t0) * HD + d;
-            int sp = 0;
-            for (; sp + 8 <= nt; sp += 8) {  // eight independent loads in flight
-                float o[8];
-#pragma unroll
-                for (int u = 0; u < 8; u++) o[u] = __ldcg(src + (size_t)(sp + u) * HD);
-#pragma unroll
-                for (int u = 0; u < 8; u++) acc[i] += o[u] * cw[(sp + u) * FD_GMAX + j];
-            }
-            for (; sp < nt; sp++) acc[i] += __ldcg(src + (size_t)sp * HD) * cw[sp * FD_GMAX + j];
+            const int e = min(tid + i * FD_THREADS, G * HD - 1);  // past G * HD: a duplicate, not stored
+            jj[i] = e / HD;
+            src[i] = p.ws_o + (hrow0 + (size_t)jj[i] * p.n_splits + t0) * HD + (e - jj[i] * HD);
         }
+        int sp = 0;
+        for (; sp + 8 <= nt; sp += 8) {
+            float o[EPT][8];
+#pragma unroll
+            for (int i = 0; i < EPT; i++)
+#pragma unroll
+                for (int u = 0; u < 8; u++) o[i][u] = __ldcg(src[i] + (size_t)(sp + u) * HD);
+#pragma unroll
+            for (int i = 0; i < EPT; i++)
+#pragma unroll
+                for (int u = 0; u < 8; u++) acc[i] += o[i][u] * cw[(sp + u) * FD_GMAX + jj[i]];
+        }
+        for (; sp < nt; sp++)
+#pragma unroll
+            for (int i = 0; i < EPT; i++) acc[i] += __ldcg(src[i] + (size_t)sp * HD) * cw[sp * FD_GMAX + jj[i]];
     }
     __syncthreads();  // the last tile's sums are in l_tot
 #pragma unroll
