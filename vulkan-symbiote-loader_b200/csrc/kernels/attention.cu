@@ -37,7 +37,7 @@ namespace vsl {
 // registers, small enough to become resident beside the preceding projection's CTAs, measured
 // slower: 16 us per layer against 11-12 us at 7B batch 1.)
 constexpr int FD_THREADS = 256;
-constexpr int FD_MIN_CTAS = 1;
+constexpr int FD_MIN_CTAS = 2;  // two CTAs per SM: a long cache's splits fit in one wave
 constexpr int FD_CHUNK = 64;  // positions staged per iteration
 constexpr int FD_GMAX = 8;    // query heads per KV group supported
 constexpr int FD_PARTS = FD_THREADS / FD_CHUNK;  // partial sums per position score
