@@ -281,9 +281,11 @@ DecodeEngine::~DecodeEngine() {
     cudaFree(act_);
     cudaFree(fd_ws_);
     cudaFree(tc_ws_);
+    cudaFree(x2n_);
     cudaFree(pf_mem_);
     cudaFree(pf_fd_ws_);
     cudaFree(pf_tc_ws_);
+    cudaFree(pf_x2n_);
     if (pf_h_) cudaFreeHost(pf_h_);
     cudaFree(fdtc_ws_);
     if (host_layers_) cudaFreeHost(host_layers_);
@@ -380,6 +382,11 @@ int DecodeEngine::alloc_buffers() {
         CK(cudaMemset(tc_ws_, 0, tc_ws_bytes_));
         char* base = reinterpret_cast<char*>(((uintptr_t)tc_ws_ + 1023) & ~(uintptr_t)1023);
         tc_route_ = TcRoute{base, tc_ws_bytes_ - 1024, TC_MIN_BATCH, status_};
+        // the gate/up projection writes the down projection's split activations here
+        const size_t x2n = 2 * tc_split_rows(tb) * (size_t)ff_l_ * 2;
+        CK(cudaMalloc(&x2n_, x2n));
+        tc_route_.x2_next = x2n_;
+        tc_route_.x2_next_bytes = x2n;
     }
 
 
@@ -820,10 +827,17 @@ int DecodeEngine::enqueue_layers(const StepBufs& sb, int B) {
         RC(gemv_hint(c.wdtype, L.wo, d, nh_l_ * hd, sb.attn, B, sb.x, res_epi, nullptr, 0.0f, L.wgu, H(wgu_b), st, tcr,
                      presplit));
         RC(allreduce_sum(sb.x, B * d));
+        // when both take the tensor-core route, gate/up writes the down projection's split
+        // activations itself (no split launch before down)
+        void* x2n = tcr && tcr->x2_next && tcr->x2_next_bytes >= 2 * tc_split_rows(B) * (size_t)ff_l_ * 2 &&
+                            tc_route_taken(tcr, c.wdtype, 2 * ff_l_, d, B) && tc_route_taken(tcr, c.wdtype, d, ff_l_, B)
+                        ? tcr->x2_next
+                        : nullptr;
         RC(gemv_hint(c.wdtype, L.wgu, 2 * ff_l_, d, sb.x, B, sb.act, VSL_EPI_SWIGLU, L.ffn_norm, c.rms_eps, L.wd,
-                     H(wd_b), st, tcr));
+                     H(wd_b), st, tcr, false, nullptr, x2n));
         RC(gemv_hint(c.wdtype, L.wd, d, ff_l_, sb.act, B, sb.x, res_epi, nullptr, 0.0f,
-                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr));
+                     last ? lm_head_ : layers_[l + 1].wqkv, last ? H((size_t)v_l_ * wrow(d)) : H(qkv_b), st, tcr,
+                     x2n != nullptr, x2n));
         RC(allreduce_sum(sb.x, B * d));
         if (L.slot >= 0) CK(cudaEventRecord(ev_done_[L.slot], st));
     }
@@ -944,6 +958,10 @@ int DecodeEngine::alloc_prefill() {
         CK(cudaMemset(pf_tc_ws_, 0, bytes));
         char* base = reinterpret_cast<char*>(((uintptr_t)pf_tc_ws_ + 1023) & ~(uintptr_t)1023);
         pf_tc_route_ = TcRoute{base, bytes - 1024, TC_MIN_BATCH, status_};
+        const size_t x2n = 2 * tc_split_rows(PF_ROWS) * (size_t)ff_l_ * 2;
+        CK(cudaMalloc(&pf_x2n_, x2n));
+        pf_tc_route_.x2_next = pf_x2n_;
+        pf_tc_route_.x2_next_bytes = x2n;
     }
     return VSL_OK;
 }

@@ -124,6 +124,7 @@ private:
     bool pf_attn_tc_ = false;  // prompt chunks take the tensor-core prompt attention
     bool short_attn_ = false;  // decode steps take the short-cache attention kernel
     void* pf_tc_ws_ = nullptr;
+    void* pf_x2n_ = nullptr;  // gate/up -> down split activations of the prompt pass
     TcRoute pf_tc_route_ = {};
     std::vector<int32_t> pt_host_;  // host copy of the page table
     int allreduce_sum(float* buf, int count);
@@ -191,6 +192,7 @@ private:
     void* fdtc_ws_ = nullptr;  // long-context attention (tcgen05 scores) workspace; null = split-K kernel
     size_t fdtc_ws_bytes_ = 0;
     void* tc_ws_ = nullptr;  // tensor-core route of batched projections (batch >= 5, 16-bit weights)
+    void* x2n_ = nullptr;    // gate/up -> down split activations of the decode step
     size_t tc_ws_bytes_ = 0;
     TcRoute tc_route_ = {};
 

@@ -31,6 +31,8 @@ struct TcRoute {
     size_t bytes;
     int min_batch;  // projections with at least this many activation rows use the tensor cores
     int* status;    // device status word for expired waits
+    void* x2_next = nullptr;  // split activations of the down projection, written by gate/up
+    size_t x2_next_bytes = 0;
 };
 size_t tc_workspace_bytes(int N, int K, int B);
 constexpr int TC_MIN_BATCH = 5;  // below this the GEMV streams the weights once per launch anyway
@@ -44,9 +46,13 @@ int qkv_rope_append_status(int wdtype, const void* Wqkv, int n_heads, int n_kv, 
                            void* v_cache, int kvdtype, const int32_t* page_table, int max_pages, int page_size,
                            int* status, cudaStream_t stream, const void* pf_ptr, size_t pf_bytes,
                            const TcRoute* tc = nullptr);
+// x_presplit: the tensor-core route reads split activations already in place (x2_in, or the
+// workspace start when null); x2_out (SwiGLU on the tensor-core route): write the output as the
+// next projection's split activations (hi rows, lo rows from tc_split_rows(B)) instead of y.
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc = nullptr, bool x_presplit = false);
+              const TcRoute* tc = nullptr, bool x_presplit = false, const void* x2_in = nullptr,
+              void* x2_out = nullptr);
 // Whether gemv_hint takes the tensor-core route for this projection (then x_presplit may be used).
 bool tc_route_taken(const TcRoute* tc, int wdtype, int N, int K, int B);
 size_t tc_split_rows(int B);  // padded activation rows of the split tile (hi rows, then lo rows)

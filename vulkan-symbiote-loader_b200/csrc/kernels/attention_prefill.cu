@@ -63,6 +63,8 @@ constexpr int FP_TILE = 2 * FP_ATOM;   // a 128 x 128 16-bit tile
 // shared memory: Q hi, Q lo, K, V, P hi, P lo
 constexpr size_t FP_SMEM = 1024 + 6 * (size_t)FP_TILE;
 constexpr uint32_t FP_TMEM_COLS = 512;  // S[2] at columns 0 and 128, PV at 256
+constexpr int FP_OST = FP_HD + 4;       // fp32 row stride of the staged output (padded, 16-byte aligned)
+static_assert((size_t)FP_ROWS * FP_OST * 4 <= 3 * (size_t)FP_TILE, "staged output fits the Q and K tiles");
 
 struct FpArgs {
     const float* q;             // [P][n_heads][128]
@@ -81,30 +83,27 @@ struct FpArgs {
     int x2_bf16, x2_rows;       // their type; row of the first lo row
 };
 
-// Row `rb` of the next projection's split activations (hi row rb, lo row x2_rows + rb) at
-// columns [k0, k0 + 64): 64 values v * inv as 16-bit hi and residual lo.
+// Eight values of row `rb` of the next projection's split activations (hi row rb, lo row
+// x2_rows + rb) at columns [k0, k0 + 8), from shared memory, as 16-bit hi and residual lo.
 template <typename T>
-__device__ __forceinline__ void fp_store_split(const FpArgs& a, size_t rb, size_t k0, const float* o, float inv) {
+__device__ __forceinline__ void fp_store_split8(const FpArgs& a, size_t rb, size_t k0, const float* v) {
     const size_t K = (size_t)a.n_heads * FP_HD;
-    T* hi = static_cast<T*>(a.x2) + rb * K + k0;
-    T* lo = static_cast<T*>(a.x2) + ((size_t)a.x2_rows + rb) * K + k0;
+    const float4 v0 = *reinterpret_cast<const float4*>(v), v1 = *reinterpret_cast<const float4*>(v + 4);
+    const float x[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    T h[8], l[8];
 #pragma unroll
-    for (int j = 0; j < 64; j += 8) {
-        T h[8], l[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const float v = o[j + e] * inv;
-            if constexpr (std::is_same<T, __half>::value) {
-                h[e] = __float2half_rn(v);
-                l[e] = __float2half_rn(v - __half2float(h[e]));
-            } else {
-                h[e] = __float2bfloat16_rn(v);
-                l[e] = __float2bfloat16_rn(v - __bfloat162float(h[e]));
-            }
+    for (int e = 0; e < 8; e++) {
+        if constexpr (std::is_same<T, __half>::value) {
+            h[e] = __float2half_rn(x[e]);
+            l[e] = __float2half_rn(x[e] - __half2float(h[e]));
+        } else {
+            h[e] = __float2bfloat16_rn(x[e]);
+            l[e] = __float2bfloat16_rn(x[e] - __bfloat162float(h[e]));
         }
-        *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<const uint4*>(h);
-        *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<const uint4*>(l);
     }
+    *reinterpret_cast<uint4*>(static_cast<T*>(a.x2) + rb * K + k0) = *reinterpret_cast<const uint4*>(h);
+    *reinterpret_cast<uint4*>(static_cast<T*>(a.x2) + ((size_t)a.x2_rows + rb) * K + k0) =
+        *reinterpret_cast<const uint4*>(l);
 }
 
 __device__ __forceinline__ void fp_tma(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -526,19 +525,33 @@ __global__ void __launch_bounds__(FP_THREADS, 1)
         } else {
             red_l[hc][t] = l;
             named_barrier_sync(1, FP_SM_THREADS);
-            if (pr >= 0 && a.x2) {
-                const float inv = 1.0f / (red_l[0][t] + red_l[1][t]);
-                if (a.x2_bf16)
-                    fp_store_split<__nv_bfloat16>(a, (size_t)(r0 + t), (size_t)h * FP_HD + hc * HALF, o, inv);
-                else
-                    fp_store_split<__half>(a, (size_t)(r0 + t), (size_t)h * FP_HD + hc * HALF, o, inv);
-            } else if (pr >= 0) {
-                const float inv = 1.0f / (red_l[0][t] + red_l[1][t]);  // > 0: position pr is always attended
-                float* dst = a.out + ((size_t)(r0 + t) * a.n_heads + h) * FP_HD + hc * HALF;
+            // the normalised rows go through shared memory (the Q and K tiles are free: the last
+            // scores and product are done) and out with coalesced stores by all 256 threads, in
+            // a rolled loop (straight-line stores from each thread's registers measured slower)
+            float* ost = reinterpret_cast<float*>(smem_g + qt);  // [128][FP_OST] fp32
+            const float inv = pr >= 0 ? 1.0f / (red_l[0][t] + red_l[1][t]) : 0.0f;  // > 0: pr is attended
+            float* orow = ost + t * FP_OST + hc * HALF;
 #pragma unroll
-                for (int j = 0; j < HALF; j += 4)
-                    *reinterpret_cast<float4*>(dst + j) =
-                        make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+            for (int j = 0; j < HALF; j += 4)
+                *reinterpret_cast<float4*>(orow + j) = make_float4(o[j] * inv, o[j + 1] * inv, o[j + 2] * inv, o[j + 3] * inv);
+            named_barrier_sync(1, FP_SM_THREADS);
+            const int nrows = min(FP_ROWS, a.P - r0);
+            if (a.x2) {
+#pragma unroll 1
+                for (int it = th; it < nrows * 16; it += FP_SM_THREADS) {  // 16 threads per row, 8 columns each
+                    const int r = it >> 4, c8 = (it & 15) * 8;
+                    if (a.x2_bf16)
+                        fp_store_split8<__nv_bfloat16>(a, (size_t)(r0 + r), (size_t)h * FP_HD + c8, ost + r * FP_OST + c8);
+                    else
+                        fp_store_split8<__half>(a, (size_t)(r0 + r), (size_t)h * FP_HD + c8, ost + r * FP_OST + c8);
+                }
+            } else {
+#pragma unroll 1
+                for (int it = th; it < nrows * 32; it += FP_SM_THREADS) {  // 32 threads per row, 4 columns each
+                    const int r = it >> 5, c4 = (it & 31) * 4;
+                    *reinterpret_cast<float4*>(a.out + ((size_t)(r0 + r) * a.n_heads + h) * FP_HD + c4) =
+                        *reinterpret_cast<const float4*>(ost + r * FP_OST + c4);
+                }
             }
             FP_STAMP(ts_end);
             if (th == 0) FP_PHASE(2204u, ts_setup, ts_end);

@@ -39,9 +39,15 @@ struct GemvParams {
     const void* pf_ptr;
     size_t pf_bytes;
     unsigned trace_id;  // launch id of the trace build (unused otherwise)
-    // tensor-core route only: the split activations are already in the workspace (written by
-    // the producing kernel), so no activation-split launch precedes the GEMM
+    // tensor-core route only: the split activations are already there (written by the producing
+    // kernel: at x2_in, or at the workspace start when x2_in is null), so no activation-split
+    // launch precedes the GEMM
     int x_presplit;
+    const void* x2_in;
+    // EK_SWIGLU on the tensor-core route: write the output as the next projection's split
+    // activations instead of y (hi rows from 0, lo rows from x2_out_rows; N / 2 columns)
+    void* x2_out;
+    int x2_out_rows, x2_out_bf16;
 };
 
 __device__ __forceinline__ float silu_f(float z) { return z / (1.0f + expf(-z)); }
@@ -110,7 +116,22 @@ __device__ __forceinline__ void epi_apply(const GemvParams& p, const EpiPre& e, 
         *y0 = e.a0 + s0;
         if (has1) y0[1] = e.a1 + s1;
     } else if (EK == EK_SWIGLU) {
-        p.y[(size_t)b * (N >> 1) + unit] = silu_f(s0) * s1;
+        const float v = silu_f(s0) * s1;
+        if (p.x2_out) {  // as hi / lo 16-bit halves of the next projection's split tile
+            const size_t K2 = (size_t)(N >> 1);
+            const size_t ih = (size_t)b * K2 + unit, il = ((size_t)p.x2_out_rows + b) * K2 + unit;
+            if (p.x2_out_bf16) {
+                const __nv_bfloat16 h = __float2bfloat16_rn(v);
+                static_cast<__nv_bfloat16*>(p.x2_out)[ih] = h;
+                static_cast<__nv_bfloat16*>(p.x2_out)[il] = __float2bfloat16_rn(v - __bfloat162float(h));
+            } else {
+                const __half h = __float2half_rn(v);
+                static_cast<__half*>(p.x2_out)[ih] = h;
+                static_cast<__half*>(p.x2_out)[il] = __float2half_rn(v - __half2float(h));
+            }
+        } else {
+            p.y[(size_t)b * (N >> 1) + unit] = v;
+        }
     } else if (EK == EK_QKV) {
         const int hd = p.head_dim;
         const int qd = p.n_heads * hd, kvd = p.n_kv * hd;

@@ -673,15 +673,21 @@ bool tc_route_taken(const TcRoute* tc, int wdtype, int N, int K, int B) {
 
 int gemv_hint(int wdtype, const void* W, int N, int K, const float* x, int B, float* y, int epilogue,
               const float* norm_w, float eps, const void* pf_ptr, size_t pf_bytes, cudaStream_t stream,
-              const TcRoute* tc, bool x_presplit) {
+              const TcRoute* tc, bool x_presplit, const void* x2_in, void* x2_out) {
     int rc = check_common(wdtype, W, N, K, x, B);
     if (rc) return rc;
     if (x_presplit && (norm_w || !tc_route_taken(tc, wdtype, N, K, B)))
         return set_error(VSL_ERR_INVALID, "gemv: pre-split activations need the tensor-core route and no norm");
+    if (x2_out && (epilogue != VSL_EPI_SWIGLU || !tc_route_taken(tc, wdtype, N, K, B)))
+        return set_error(VSL_ERR_INVALID, "gemv: a split output needs the SwiGLU epilogue on the tensor-core route");
     GemvParams p = {};
     p.W = W; p.N = N; p.K = K; p.x = x; p.B = B; p.y = y; p.norm_w = norm_w; p.eps = eps;
     p.pf_ptr = pf_ptr; p.pf_bytes = pf_bytes;
     p.x_presplit = x_presplit ? 1 : 0;
+    p.x2_in = x2_in;
+    p.x2_out = x2_out;
+    p.x2_out_rows = x2_out ? (int)tc_split_rows(B) : 0;
+    p.x2_out_bf16 = wdtype == VSL_BF16 ? 1 : 0;
     int kind = epilogue == VSL_EPI_ADD ? EK_ADD : epilogue == VSL_EPI_SWIGLU ? EK_SWIGLU : EK_STORE;
     return run_chunks(wdtype, kind, p, stream, epilogue == VSL_EPI_SWIGLU ? N / 2 : N, tc);
 }

@@ -863,7 +863,9 @@ int tc_project(int wdtype, int kind, const GemvParams& p, void* workspace, size_
 
     unsigned char* w8 = static_cast<unsigned char*>(workspace);
     auto up = [](size_t v) { return (v + 1023) / 1024 * 1024; };
-    void* x2 = w8;
+    void* x2 = p.x_presplit && p.x2_in ? const_cast<void*>(p.x2_in) : static_cast<void*>(w8);
+    if (((uintptr_t)x2 & 15) || (p.x2_out && (kind != EK_SWIGLU || ((uintptr_t)p.x2_out & 15))))
+        return set_error(VSL_ERR_INVALID, "tc gemm: split activations must be 16-byte aligned (output: SwiGLU only)");
     const size_t x2b = up((size_t)2 * a.Bp * p.K * 2);
     const int G0 = sm_count();
     a.ws = reinterpret_cast<float*>(w8 + x2b);
