@@ -362,7 +362,7 @@ def run_ours(args):
         cfg["n_layers"] = args.layers
     B = BATCH_8B if big else 1
     start = PREFILL_8B if big else PREFILL_70B if w70 else PROMPT
-    max_seq = start + args.warmup + 2 * args.steps + 8
+    max_seq = start + args.warmup + 3 * args.steps + 8
     max_seq = (max_seq + 63) // 64 * 64
     parity = tp_parity(np, vsl, vdist, dist, rank, ws, local) if not (big or w70 or qname) else None
     nccl_id = vdist.nccl_id(dist)
@@ -422,10 +422,23 @@ def run_ours(args):
         dist.barrier()
     ms = e0.elapsed_time(e1)
     ms = vdist.max_over_ranks(dist, ms)
+    # per-step device times of the same graph replays, one event pair per step (the median is
+    # insensitive to the ranks' launch skew at the first exchange of the window above)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev[0].record(s)
+    for i in range(args.steps):
+        eng.run(1, batch=B)
+        ev[i + 1].record(s)
+    torch.cuda.synchronize()
+    step_ms = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps))
+    step_ms_p50 = vdist.max_over_ranks(dist, step_ms[len(step_ms) // 2])
     _, bytes_end = eng.step_stats(B)
     status = eng.device_status()
     # end to end through the host API: pinned host ids in, sampled ids back, every step
-    n_log = (1 if big else 0) + args.warmup + args.steps
+    n_log = (1 if big else 0) + args.warmup + 2 * args.steps
     nxt = np.asarray(eng.read_tokens(n_log, batch=B)[-1], np.int32).reshape(B)
     for _ in range(2):
         nxt, _ = eng.step_host(nxt)
@@ -456,7 +469,7 @@ def run_ours(args):
         line = {
             "metric": "decode tok/s (8B bf16 GQA, bs16, 8192-position KV)", "value": round(tok_s, 3),
             "unit": "tok/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "ms_per_step": round(ms / args.steps, 4), "step_ms_p50": round(step_ms_p50, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random-init weights and KV in HBM)",
             "config": {"workload": "8B Llama-3 shape bf16 (BASELINE configs[3]), 16 sequences x 8192 prefilled "
                                    "fp16 KV positions, greedy decode",
@@ -475,7 +488,7 @@ def run_ours(args):
     elif rank == 0 and w70:
         line = {
             "metric": "decode tok/s (70B fp16, bs1)", "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "step_ms_p50": round(step_ms_p50, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded random-init weights filled in HBM)",
             "config": {"workload": "70B Llama shape fp16 (BASELINE configs[4]), batch 1, 2048-token prompt (prefill), "
@@ -500,7 +513,7 @@ def run_ours(args):
     elif rank == 0:
         line = {
             "metric": f"decode tok/s (7B {qname or 'fp16'}, bs1)", "value": round(tok_s, 3), "unit": "tok/s",
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "step_ms_p50": round(step_ms_p50, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": qname.lower() + " weights, f32 math" if qname else "f16",
             "data": "synthetic (seeded random-init weights filled in HBM)",
