@@ -371,7 +371,7 @@ int DecodeEngine::alloc_buffers() {
         CK(cudaMalloc(&fdtc_ws_, fdtc_ws_bytes_));
         CK(cudaMemset(fdtc_ws_, 0, fdtc_ws_bytes_));
     }
-    // batched projections (5..64 rows, 16-bit weights) run on the tensor cores: one workspace
+    // batched projections (5..128 rows, 16-bit weights) run on the tensor cores: one workspace
     // sized for the largest projection of the model
     if (es_ == 2 && !is_quant(c.wdtype) && opt_.max_batch >= TC_MIN_BATCH) {
         const int tb = std::min(opt_.max_batch, TC_MAX_BATCH);
@@ -1189,7 +1189,7 @@ int DecodeEngine::generate(const int32_t* prompt, int n_prompt, int max_new, flo
     *n_out = 0;
     if (max_new == 0) return VSL_OK;
     RC(reset());
-    // the prompt in one prompt pass (chunks of 64 rows), which also samples the first new
+    // the prompt in one prompt pass (chunks of 128 rows), which also samples the first new
     // token; then one graph-launched decode step per token, in chunks of 16 when stop ids can
     // end the loop early
     auto is_stop = [&](int32_t t) {

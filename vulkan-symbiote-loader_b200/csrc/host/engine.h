@@ -52,7 +52,7 @@ public:
     int set_forced(const int32_t* ids, int n_steps, int B);
     int run(int n_steps, int B, float temperature, uint64_t seed);
     int step_host(const int32_t* ids, int B, int32_t* out_ids, float* out_logits);
-    // Prompt pass: positions pos..pos+n-1 of sequence `seq` run as up to 64 rows at a time
+    // Prompt pass: positions pos..pos+n-1 of sequence `seq` run as up to 128 rows at a time
     // (tensor-core projections, causal attention through per-row positions over the sequence's
     // pages); writes their KV and leaves `seq` ready to decode the token sampled greedily from
     // the last prompt token's logits.
