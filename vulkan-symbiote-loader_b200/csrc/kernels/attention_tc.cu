@@ -15,13 +15,15 @@
 //     folds O into its accumulators one chunk later, so the next chunk's scores and softmax
 //     overlap this product.
 //   * K and V chunks (two 64-position pages each, 2 x 64-column 128-byte-swizzle atoms) arrive by
-//     tensor TMA into a 3-stage mbarrier ring (192 KB in flight per SM); rows past the end of a
-//     sequence are zeroed in shared memory before the product reads them (0 x garbage).
+//     tensor TMA into a 3-stage ring (192 KB per SM) with separate barriers for the K and the V
+//     half of a stage, each filled by its own producer thread: a K half is refilled as soon as its
+//     scores are computed, before the softmax and the product of its chunk; rows past the end of
+//     a sequence are zeroed in shared memory before the product reads them (0 x garbage).
 //   * work split (stream-K): the flattened list of (sequence, KV group, 128-position chunk) is cut
 //     into equal ranges over persistent CTAs, whatever the per-sequence lengths; a (sequence,
 //     group) shared by several CTAs is merged by the last to finish, in CTA order
 //     (deterministic), with an atomic counter it resets to zero.
-// Roles: warps 0-3 softmax and accumulation (TMEM lane quarter = warp), warp 4 TMA producer,
+// Roles: warps 0-3 softmax and accumulation (TMEM lane quarter = warp), warp 4 TMA producers,
 // warp 5 TMEM allocation and the single-thread MMA issue. Every wait is bounded (one second) and
 // records VSL_ERR_TIMEOUT; the kernel then drains its copies and MMAs and frees its TMEM.
 #include <cuda.h>
@@ -151,11 +153,14 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                            const __grid_constant__ FtArgs a) {
     VSL_TRACE_ENTRY();
     extern __shared__ unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t full[FT_STAGES], empty[FT_STAGES], s_full[2], s_free[2], q_ready;
+    // K and V halves of a stage have their own barriers: the K half is refilled once the chunk's
+    // scores are computed, the V half once its product is
+    __shared__ __align__(8) uint64_t full_k[FT_STAGES], full_v[FT_STAGES], empty_k[FT_STAGES], empty_v[FT_STAGES];
+    __shared__ __align__(8) uint64_t s_full[2], s_free[2], q_ready;
     __shared__ __align__(8) uint64_t p_ready[2], o_full[2], o_free[2];
     __shared__ uint32_t tmem_s;
     __shared__ int abort_s, last_s;
-    __shared__ float red_max[4][FT_GMAX], red_sum[4][FT_GMAX];
+    __shared__ float red_max[2][4][FT_GMAX], red_sum[4][FT_GMAX];
     __shared__ FtWork wk;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -167,8 +172,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < FT_STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);  // tcgen05.commit after the chunk's P.V
+            mbar_init(&full_k[s], 1);
+            mbar_init(&full_v[s], 1);
+            mbar_init(&empty_k[s], 1);  // tcgen05.commit after the chunk's scores
+            mbar_init(&empty_v[s], 1);  // tcgen05.commit after the chunk's P.V
         }
         for (int i = 0; i < 2; i++) {
             mbar_init(&s_full[i], 1);
@@ -222,8 +229,13 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     const long long f0 = c < Gc ? ft_lo(T, Gc, c) : 0, f1 = c < Gc ? ft_lo(T, Gc, c + 1) : 0;
 
     if (warp == 4) {
-        // ================= TMA producer =================
-        if (lane == 0) {
+        // ================= TMA producers: lane 0 the K halves, lane 1 the V halves =================
+        if (lane < 2) {
+            const bool kside = lane == 0;
+            uint64_t* fullx = kside ? full_k : full_v;
+            uint64_t* emptyx = kside ? empty_k : empty_v;
+            const CUtensorMap* map = kside ? &map_k : &map_v;
+            const uint32_t half = kside ? 0u : (uint32_t)(2 * FT_ATOM);
             FtCur cu;
             if (f0 < f1) ft_seek(wk, a.B, a.n_kv, f0, cu);
             int s = 0;
@@ -231,12 +243,12 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             long long it = 0;
             bool ok = true;
             for (long long f = f0; f < f1 && ok; f++, it++) {
-                if (it >= FT_STAGES && !mbar_wait(&empty[s], epar)) {
+                if (it >= FT_STAGES && !mbar_wait(&emptyx[s], epar)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&full[s], FT_STAGE);
-                const uint32_t st = ring + s * FT_STAGE;
+                mbar_arrive_expect_tx(&fullx[s], FT_STAGE / 2);
+                const uint32_t st = ring + s * FT_STAGE + half;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
                     int p0 = (wk.c0[cu.b] + cu.ch) * FT_CHUNK + h * 64;
@@ -244,10 +256,8 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     const int page = __ldg(a.page_table + (size_t)cu.b * a.max_pages + p0 / a.page_size);
                     const int row = (page * a.n_kv + cu.g) * a.page_size + (p0 % a.page_size);
 #pragma unroll
-                    for (int at = 0; at < 2; at++) {
-                        ft_tma(st + at * FT_ATOM + h * (FT_ATOM / 2), &map_k, at * 64, row, &full[s]);
-                        ft_tma(st + (2 + at) * FT_ATOM + h * (FT_ATOM / 2), &map_v, at * 64, row, &full[s]);
-                    }
+                    for (int at = 0; at < 2; at++)
+                        ft_tma(st + at * FT_ATOM + h * (FT_ATOM / 2), map, at * 64, row, &fullx[s]);
                 }
                 ft_next(wk, a.n_kv, cu);
                 if (++s == FT_STAGES) {
@@ -261,7 +271,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             }
             const long long issued = it;
             for (long long u = issued > FT_STAGES ? issued - FT_STAGES : 0; u < issued; u++)
-                mbar_wait(&full[u % FT_STAGES], (uint32_t)((u / FT_STAGES) & 1));
+                mbar_wait(&fullx[u % FT_STAGES], (uint32_t)((u / FT_STAGES) & 1));
         }
     } else if (warp == 5) {
         // ================= MMA issue =================
@@ -279,6 +289,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             bool ok = true;
             long long s_issued = 0;
             int st_of[2] = {0, 0};      // stage of chunk i (kept for PV(i) and the stage release)
+            uint32_t par_of[2] = {0u, 0u};  // and the parity of that use of the stage
             int segpos[2] = {0, 0};     // (b * n_kv + g) of chunk i
             auto issue_s = [&](long long i) -> bool {
                 const int key = cs.b * a.n_kv + cs.g;
@@ -288,7 +299,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     pb = cs.b;
                     pg = cs.g;
                 }
-                if (!mbar_wait(&full[ss], fpar)) return false;
+                if (!mbar_wait(&full_k[ss], fpar)) return false;
                 if (i >= 2 && !mbar_wait(&s_free[i & 1], (uint32_t)(((i >> 1) - 1) & 1))) return false;
                 ft_fence_after();
                 const uint32_t st = ring + ss * FT_STAGE;
@@ -301,7 +312,9 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                                a.idesc, (at > 0 || k > 0) ? 1u : 0u);
                 }
                 ft_commit(&s_full[i & 1]);
+                ft_commit(&empty_k[ss]);  // the K half of this stage is no longer read
                 st_of[i & 1] = ss;
+                par_of[i & 1] = fpar;
                 segpos[i & 1] = key;
                 if (++ss == FT_STAGES) {
                     ss = 0;
@@ -313,6 +326,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             auto issue_pv = [&](long long i) -> bool {
                 if (!mbar_wait(&p_ready[i & 1], (uint32_t)((i >> 1) & 1))) return false;
                 if (i >= 2 && !mbar_wait(&o_free[i & 1], (uint32_t)(((i >> 1) - 1) & 1))) return false;
+                if (!mbar_wait(&full_v[st_of[i & 1]], par_of[i & 1])) return false;
                 ft_fence_after();
                 const uint32_t vt = ring + st_of[i & 1] * FT_STAGE + 2 * FT_ATOM;
                 const uint32_t pt = p2 + (uint32_t)(i & 1) * FT_P2;
@@ -324,7 +338,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                     ft_mma(tmem + (uint32_t)(2 * FT_N + (i & 1) * FT_N), ad, bd, a.idesc_pv, k > 0 ? 1u : 0u);
                 }
                 ft_commit(&o_full[i & 1]);
-                ft_commit(&empty[st_of[i & 1]]);  // K and V of this chunk are no longer read
+                ft_commit(&empty_v[st_of[i & 1]]);  // the V half of this stage is no longer read
                 return true;
             };
             if (n > 0) ok = issue_s(0);
@@ -376,6 +390,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
         int pb = -1, pg = -1;
         int sst = 0;
         uint32_t fpar = 0u;
+        // A failed wait (or another role's abort) is carried to the next barrier, a bar.red.or that
+        // all four warps take, so they leave the loop together with one barrier per chunk; what
+        // runs in between on a failed wait reads stale shared or tensor memory and is discarded.
+        bool bad = false;
         for (long long f = f0; f < f1; f++, i++) {
             const int b = cu.b, g = cu.g, ch = cu.ch;
             const int len = wk.len[b];
@@ -415,14 +433,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 pg = g;
             }
             // ---- scores of chunk i (TMEM row t) ----
-            {
-                const bool bad = !mbar_wait(&s_full[i & 1], (uint32_t)((i >> 1) & 1)) || ft_abort(&abort_s);
-                if (named_barrier_or(1, 128, bad)) {  // the four warps leave together
-                    set_status(a.status, VSL_ERR_TIMEOUT);
-                    atomicExch(&abort_s, 1);
-                    break;
-                }
-            }
+            bad = bad || !mbar_wait(&s_full[i & 1], (uint32_t)((i >> 1) & 1)) || ft_abort(&abort_s);
             ft_fence_after();
             uint32_t r[16];
             ft_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)((i & 1) * FT_N), r);
@@ -438,21 +449,27 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             for (int j = 0; j < FT_GMAX; j++) {
                 sc[j] = (j < G && valid) ? (__uint_as_float(r[j]) + __uint_as_float(r[8 + j])) * a.scale : -CUDART_INF_F;
                 if (j < G) {
-                    const float mx = warp_max(sc[j]);
-                    if (lane == 0) red_max[warp][j] = mx;
+                    const float mx = warp_max_redux(sc[j]);
+                    if (lane == 0) red_max[i & 1][warp][j] = mx;  // two buffers: a warp may be a chunk ahead
                 }
             }
-            named_barrier_sync(1, 128);
+            if (named_barrier_or(1, 128, bad)) {  // the four warps leave together
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+                break;
+            }
             float alpha[FT_GMAX];
             const int pc = t >> 6, pcol = t & 63;  // P2 atom and column of position t
             unsigned char* p2p = smem_g + p2 + (uint32_t)(i & 1) * FT_P2 + pc * (FT_P2 / 2) + ((pcol & 7) << 1);
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++) {
                 if (j >= G) break;
-                const float cm = fmaxf(fmaxf(red_max[0][j], red_max[1][j]), fmaxf(red_max[2][j], red_max[3][j]));
+                const float(&rm)[4][FT_GMAX] = red_max[i & 1];
+                const float cm = fmaxf(fmaxf(rm[0][j], rm[1][j]), fmaxf(rm[2][j], rm[3][j]));
                 const float mn = fmaxf(m[j], cm);
-                alpha[j] = expf(m[j] - mn);
-                const float pj = valid ? expf(sc[j] - mn) : 0.0f;
+                // __expf: arguments are <= 0 here, where its error stays a few ulp of the fp32 result
+                alpha[j] = __expf(m[j] - mn);
+                const float pj = valid ? __expf(sc[j] - mn) : 0.0f;
                 m[j] = mn;
                 lt[j] = lt[j] * alpha[j] + pj;
                 const __half ph = __float2half_rn(pj);
@@ -464,7 +481,7 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             if (n_valid < FT_CHUNK && past_end) {
                 // rows past the sequence end hold whatever the cache had (possibly NaN bit patterns):
                 // zero them so that 0 x garbage cannot reach the product
-                mbar_wait(&full[sst], fpar);  // order after the TMA's writes to this stage
+                mbar_wait(&full_v[sst], fpar);  // order after the TMA's writes to this stage
                 unsigned char* vrow = smem_g + ring + sst * FT_STAGE + 2 * FT_ATOM + t * 128;
 #pragma unroll
                 for (int at2 = 0; at2 < 2; at2++)
@@ -482,9 +499,8 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
             // ---- fold PV(i-1) into the output (lagged one chunk: PV(i) overlaps the next softmax) ----
             ft_next(wk, a.n_kv, cu);
             const bool seg_end = f + 1 == f1 || cu.b != b || cu.g != g;
-            auto fold = [&](long long k, const float* al) -> bool {
-                const bool bad = !mbar_wait(&o_full[k & 1], (uint32_t)((k >> 1) & 1)) || ft_abort(&abort_s);
-                if (named_barrier_or(1, 128, bad)) return false;
+            auto fold = [&](long long k, const float* al) {
+                bad = bad || !mbar_wait(&o_full[k & 1], (uint32_t)((k >> 1) & 1)) || ft_abort(&abort_s);
                 ft_fence_after();
                 uint32_t ov[16];
                 ft_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(2 * FT_N + (k & 1) * FT_N), ov);
@@ -494,16 +510,9 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < FT_GMAX; j++)
                     if (j < G) o[j] = o[j] * al[j] + (__uint_as_float(ov[j]) + __uint_as_float(ov[8 + j]));
-                return true;
             };
-            bool fold_ok = true;
-            if (!seg_start) fold_ok = fold(i - 1, alpha_prev);
-            if (fold_ok && seg_end) fold_ok = fold(i, alpha);
-            if (!fold_ok) {
-                set_status(a.status, VSL_ERR_TIMEOUT);
-                atomicExch(&abort_s, 1);
-                break;
-            }
+            if (!seg_start) fold(i - 1, alpha_prev);
+            if (seg_end) fold(i, alpha);
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++) alpha_prev[j] = alpha[j];
             if (!seg_end) continue;
@@ -514,7 +523,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
                 const float sm = warp_sum(lt[j]);
                 if (lane == 0) red_sum[warp][j] = sm;
             }
-            named_barrier_sync(1, 128);
+            if (named_barrier_or(1, 128, bad)) {
+                set_status(a.status, VSL_ERR_TIMEOUT);
+                atomicExch(&abort_s, 1);
+                break;
+            }
             float l[FT_GMAX];
 #pragma unroll
             for (int j = 0; j < FT_GMAX; j++)
