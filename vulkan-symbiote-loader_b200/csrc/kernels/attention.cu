@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
                 for (int q = 0; q < FD_PARTS; q++) a += part_s[(q * FD_GMAX + j) * FD_CHUNK + lane + 32];
                 s1 = a * p.scale;
             }
-            const float cmax = warp_max(fmaxf(s0, s1));
+            const float cmax = warp_max_redux(fmaxf(s0, s1));
             const float m_old = m_s[j];
             const float m_new = fmaxf(m_old, cmax);
             const float e0 = s0 != -CUDART_INF_F ? expf(s0 - m_new) : 0.0f;
@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(FD_THREADS, FD_MIN_CTAS) vsl_flash_decode_kern
 #pragma unroll
         for (int j = 0; j < FD_GMAX; j++) {
             if (j >= G) break;
-            const float m = warp_max(mx[j]);
+            const float m = warp_max_redux(mx[j]);
             if (lane == 0) redw[warp * FD_GMAX + j] = m;
         }
         __syncthreads();
@@ -681,7 +681,7 @@ __global__ void __launch_bounds__(FS_THREADS, 1) vsl_flash_decode_short_kernel(F
         // maximum per head over the round
         for (int j = 0; j < G; j++) {
             const float v = tid < R ? s_s[j * R + tid] : -CUDART_INF_F;
-            const float mx = warp_max(v);
+            const float mx = warp_max_redux(v);
             if (lane == 0) red[warp * FD_GMAX + j] = mx;
         }
         __syncthreads();
