@@ -149,13 +149,8 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-// The same maximum in one instruction (sm_100a's redux.sync on f32; like fmaxf, a NaN lane does
-// not win over a number).
+// Maximum over the 32 lanes of a warp in one instruction (sm_100a's redux.sync on f32; like
+// fmaxf, a NaN lane does not win over a number).
 __device__ __forceinline__ float warp_max_redux(float v) {
     float r;
     asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
